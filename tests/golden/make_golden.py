@@ -1,0 +1,153 @@
+"""Generate golden fixtures by running the reference's own CPU code.
+
+Run from the repository root where the reference checkout is readable:
+
+    RAON_REFERENCE=/path/to/raon-npu python tests/golden/make_golden.py
+
+It imports the reference's ``quant.q4nx``, ``host.backend.NumpyBackend``,
+``host.raon.RaonModel._route_token`` and ``kernels.moe_grouped.planner`` and
+records their outputs on seeded inputs into ``tests/golden/*.npz``.  The tests
+regenerate the same inputs from the seeds recorded here and check the oracle
+(and through it the CUDA path) against these outputs.  The reference is never
+needed at test time.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REF = os.environ.get("RAON_REFERENCE", "")
+if not REF or not Path(REF).is_dir():
+    raise SystemExit("set RAON_REFERENCE to the reference checkout")
+sys.path.insert(0, REF)
+
+from quant import q4nx as rq  # noqa: E402
+from host.backend import NumpyBackend  # noqa: E402
+from host.weights import Weights  # noqa: E402
+from host.raon import RaonModel  # noqa: E402
+from kernels.moe_grouped.planner import build_plan, scatter_b2  # noqa: E402
+
+sys.path.insert(0, str(HERE.parent.parent))
+from tests.golden.cases import (  # noqa: E402
+    QUANT_CASES, LINEAR_CASES, MOE_CASE, ROUTER_CASE, COMBINE_CASE,
+    quant_input, linear_inputs, moe_inputs, router_inputs, combine_inputs,
+)
+
+
+class _Tensors(Weights):
+    """In-memory weight store (the reference's own test double pattern)."""
+
+    def __init__(self, tensors):
+        self.tensors = dict(tensors)
+        self.selected_layers = None
+        self.load_global = True
+        self.skip_moe_experts = False
+
+
+def sha(b: bytes) -> str:
+    return hashlib.sha256(b).hexdigest()
+
+
+def make_quant():
+    out = {}
+    for name, (n, k, seed, kind) in QUANT_CASES.items():
+        w = quant_input(n, k, seed, kind)
+        c, s, m = rq.quantize(w)
+        packed = rq.pack_gemv(c, s, m)
+        deq = rq.dequantize_simple(*rq.parse_gemv(packed, K=k, M=n))
+        out[f"{name}/codes_sha"] = np.array(sha(c.tobytes()))
+        out[f"{name}/scales"] = s
+        out[f"{name}/mins"] = m
+        out[f"{name}/packed_sha"] = np.array(sha(packed))
+        out[f"{name}/deq_sha"] = np.array(sha(deq.astype(np.float32).tobytes()))
+    np.savez_compressed(HERE / "quant.npz", **out)
+
+
+def make_linear():
+    out = {}
+    for name, case in LINEAR_CASES.items():
+        w_f32, x, bias = linear_inputs(**case, q=rq)
+        tensors = {"w.weight": w_f32}
+        if bias is not None:
+            tensors["w.bias"] = bias
+        y = NumpyBackend(_Tensors(tensors)).linear("w.weight", x)
+        out[f"{name}/y"] = y
+    np.savez_compressed(HERE / "linear.npz", **out)
+
+
+def make_moe():
+    d = moe_inputs(**MOE_CASE, q=rq)
+    tensors = {}
+    for e, (wg, wu, wd) in d["experts"].items():
+        tensors[f"model.layers.0.moe.experts.{e}.gate_proj.weight"] = wg
+        tensors[f"model.layers.0.moe.experts.{e}.up_proj.weight"] = wu
+        tensors[f"model.layers.0.moe.experts.{e}.down_proj.weight"] = wd
+    be = NumpyBackend(_Tensors(tensors))
+    out = {}
+    for t in range(d["x"].shape[0]):
+        out[f"tok{t}/default"] = be.moe_experts(0, d["x"][t], d["top_ids"][t], d["top_w"][t])
+        out[f"tok{t}/betas"] = be.moe_experts(0, d["x"][t], d["top_ids"][t], d["top_w"][t],
+                                              gate_beta=2.0, value_beta=10.0)
+    np.savez_compressed(HERE / "moe.npz", **out)
+
+
+class _FakeModel:
+    """Just enough of RaonModel for ``_route_token``."""
+
+    class _Cfg:
+        pass
+
+    def __init__(self, router_w, bias, k, scaling):
+        self._c = {"router_weight": router_w, "router_bias": bias}
+        self.config = self._Cfg()
+        self.config.num_experts_per_token = k
+        self.config.moe_renormalize = True
+        self.config.routed_scaling_factor = scaling
+
+    def _layer_constants(self, layer_idx):
+        return self._c
+
+
+def make_router():
+    d = router_inputs(**ROUTER_CASE)
+    fake = _FakeModel(d["router_w_f32"], d["bias"], d["k"], d["scaling"])
+    out = {}
+    for t in range(d["x"].shape[0]):
+        top, w, logits = RaonModel._route_token(fake, 0, d["x"][t])
+        out[f"tok{t}/top"] = np.asarray(top)
+        out[f"tok{t}/w"] = np.asarray(w, np.float32)
+        out[f"tok{t}/logits"] = np.asarray(logits, np.float32)
+    np.savez_compressed(HERE / "router.npz", **out)
+
+
+def make_combine():
+    d = combine_inputs(**COMBINE_CASE)
+    plan = build_plan(d["top_ids"], include_shared=True)
+    # Lay the per-(token, route) rows out in the planner's call/slot/row order.
+    outputs = []
+    for call in plan.calls:
+        arr = np.zeros((8, 8, d["rows"].shape[-1]), np.uint16)
+        for slot, job in enumerate(call.jobs):
+            if job is None:
+                continue
+            for r, item in enumerate(job.assignments):
+                arr[slot, r] = d["shared"][item.token] if job.shared else d["rows"][item.token, item.route]
+        outputs.append(arr)
+    routed, shared = scatter_b2(plan, outputs, d["top_ids"], d["top_w"])
+    np.savez_compressed(HERE / "combine.npz", routed=routed, shared=shared)
+
+
+if __name__ == "__main__":
+    make_quant()
+    make_linear()
+    make_moe()
+    make_router()
+    make_combine()
+    for p in sorted(HERE.glob("*.npz")):
+        print(p.name, p.stat().st_size)
