@@ -1,0 +1,123 @@
+/*
+ * raon_cuda.h -- C ABI of the B200 (sm_100a) q4nx GEMV / MoE backend.
+ *
+ * This is the drop-in boundary for the GEMV and MoE entry points of the
+ * reference's execution backend (raon-npu ``host/backend.py:65-204``, the
+ * ``Backend`` ABC, implemented on the NPU by ``npu/backend.py``).  Every
+ * function takes plain pointers and sizes, returns an ``int`` status
+ * (RC_OK == 0) and leaves a thread-local message for ``rc_last_error``.
+ *
+ * Conventions (reference ``host/backend.py:9-14``): bf16 values travel as
+ * uint16 bit patterns; an f32 activation gives an f32 result.  Device
+ * pointers are CUDA device addresses on the context's device; ``stream``
+ * arguments are ``cudaStream_t`` values (NULL = the context's own stream).
+ */
+#ifndef RAON_CUDA_H
+#define RAON_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RC_OK 0
+#define RC_ERR_INVALID 1   /* bad shape / dtype / id: the reference raises ValueError */
+#define RC_ERR_NOT_FOUND 2 /* unknown weight handle: the reference raises KeyError   */
+#define RC_ERR_CUDA 3      /* CUDA runtime failure: RuntimeError                      */
+#define RC_ERR_TIMEOUT 4   /* a bounded device-side wait ran out: RuntimeError        */
+
+#define RC_DTYPE_BF16 0
+#define RC_DTYPE_F32 1
+
+#define RC_ACT_SWIGLU 0 /* g*sigmoid(g)*u        (kernels/moe/reference.py:160-170) */
+#define RC_ACT_SITU 1   /* SiTU-GLU with betas   (host/backend.py:47-62)            */
+
+#define RC_ROUTER_SOFTMAX 0      /* softmax(x.Wr) -> top-k -> renormalise                  */
+#define RC_ROUTER_SIGMOID_BIAS 1 /* sigmoid, top-k of score+bias (host/raon.py:1224-1247) */
+
+/* Upload flags. */
+#define RC_UPLOAD_SRC_DEVICE 1u /* ``packed`` is a device pointer, not host memory        */
+#define RC_UPLOAD_GATE_UP 2u    /* rows are [gate; up] halves (kernels/moe/pack.py:136-172):
+                                   store them interleaved so the GEMV epilogue can apply
+                                   the GLU activation in registers                        */
+
+typedef struct rc_ctx rc_ctx;
+typedef struct rc_weight rc_weight;
+
+/* Thread-local text of the last failure on this thread (never NULL). */
+const char *rc_last_error(void);
+
+/* ABI version; bumps on any signature change. */
+int rc_abi_version(void);
+
+/* Create a context on ``device``: one CUDA stream, scratch memory, SM count.
+ * Replaces the device/runner set-up of ``NpuBackend.__init__``
+ * (npu/backend.py:2404-2485). */
+int rc_init(int device, rc_ctx **out);
+int rc_destroy(rc_ctx *ctx);
+
+/* The context's stream as a ``cudaStream_t`` (for callers that order work on it). */
+int rc_stream(rc_ctx *ctx, void **stream_out);
+
+/* Block until all work on the context's device is done (its own stream and
+ * any caller streams), then report any error word a kernel left
+ * (RC_ERR_TIMEOUT for a bounded wait that gave up). */
+int rc_sync(rc_ctx *ctx);
+
+/* Number of SMs of the context's device (the persistent grids are sized by it). */
+int rc_sm_count(rc_ctx *ctx, int *out);
+
+/* Upload one q4nx matrix given as ``pack_gemv`` bytes (quant/q4nx.py:335-393,
+ * rows=4: N % 128 == 0, K % 256 == 0, nbytes == N*K*5/8) and repack it once,
+ * on the device, into the GEMV tile layout.  Replaces the bundle upload of
+ * ``NpuBackend._get_weight_tensor`` (npu/backend.py:3127-3148), which hands the
+ * same bytes to the NPU unchanged. */
+int rc_upload_q4nx(rc_ctx *ctx, const uint8_t *packed, size_t nbytes, int n, int k,
+                   unsigned flags, rc_weight **out);
+/* Quantise an f32 [N, K] device matrix to q4nx and write its ``pack_gemv``
+ * bytes (N*K*5/8, device memory), bit-identical to the reference's offline
+ * converter ``quantize`` + ``pack_gemv`` (quant/q4nx.py:127-200,335-393).
+ * Synchronous; RC_ERR_INVALID for non-finite input, as the reference. */
+int rc_quantize_q4nx(rc_ctx *ctx, const float *w_dev, int n, int k, uint8_t *packed_dev, void *stream);
+
+int rc_weight_free(rc_weight *w);
+int rc_weight_info(const rc_weight *w, int *n, int *k, size_t *device_bytes, unsigned *flags);
+
+/* Attach an f32 bias [N] (host memory) to a matrix; ``rc_weight_bias`` returns
+ * its device address for the ``bias_dev`` argument of rc_gemv.  The reference
+ * adds ``<name>.bias`` in f32 before rounding (host/backend.py:410-413). */
+int rc_weight_set_bias(rc_weight *w, const float *bias_host);
+int rc_weight_bias(const rc_weight *w, const float **bias_dev);
+
+/* Dequantise an uploaded matrix to f32 [N, K] (row-major, device memory):
+ * ``f32(f64(min) + f64(scale) * code)``, bit-identical to the reference's
+ * ``parse_gemv`` + ``dequantize_simple`` (quant/q4nx.py:203-223,396-438).
+ * For an RC_UPLOAD_GATE_UP matrix the rows come back in the original
+ * [gate; up] order. */
+int rc_dequant_q4nx(rc_ctx *ctx, const rc_weight *w, float *out_dev, void *stream);
+
+/* y[t, r] = x[t, :] . W[row0 + r, :] (+ bias[row0 + r]) for t < T, r < nrows.
+ * Replaces ``Backend.linear`` / ``linear_batch`` (host/backend.py:71-83,
+ * numpy oracle host/backend.py:402-417; NPU npu/backend.py:3569-3721).
+ *   x_dtype RC_DTYPE_BF16, y_dtype RC_DTYPE_BF16: bf16 bits in, RTNE bf16 out
+ *                                                 (the reference's contract);
+ *   x_dtype RC_DTYPE_BF16, y_dtype RC_DTYPE_F32:  the same f32 sums, unrounded
+ *                                                 (e.g. f32 logits);
+ *   x_dtype RC_DTYPE_F32,  y_dtype RC_DTYPE_F32:  f32 in, f32 out.
+ * row0 and nrows must be multiples of 16 (use a wider range and slice for
+ * others).  ``bias`` is f32 [N] or NULL.  Any T >= 1; a row's result does
+ * not depend on T or on the other rows (linear_batch == stacked linear). */
+int rc_gemv(rc_ctx *ctx, const rc_weight *w, const void *x_dev, int x_dtype, int ldx, int T,
+            void *y_dev, int y_dtype, int ldy, int row0, int nrows, const float *bias_dev,
+            void *stream);
+
+/* Same as rc_gemv on host buffers: copies x in, runs, copies y out, waits. */
+int rc_gemv_host(rc_ctx *ctx, const rc_weight *w, const void *x_host, int x_dtype, int T,
+                 void *y_host, const float *bias_dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RAON_CUDA_H */

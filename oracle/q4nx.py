@@ -247,6 +247,29 @@ def quantize_pack(w: np.ndarray):
     return pack_gemv(codes, scales, mins), codes, scales, mins
 
 
+def normal_weight_q4nx(n: int, k: int, seed: int, std: float = 0.02, chunk_rows: int = 8192):
+    """Seeded ``N(0, std)`` f32 [n, k] weights, quantised and packed in row chunks.
+
+    Draws the same numbers as one ``default_rng(seed).standard_normal((n, k))``
+    call (the generator is consumed sequentially) but bounds host memory; since
+    ``pack_gemv`` orders blocks slice-major, packing 128-row-aligned chunks and
+    concatenating equals packing the whole matrix.  Returns
+    (packed bytes, codes, scales, mins).
+    """
+    assert chunk_rows % 128 == 0
+    rng = np.random.default_rng(seed)
+    parts, cs, ss, ms = [], [], [], []
+    for r0 in range(0, n, chunk_rows):
+        rows = min(chunk_rows, n - r0)
+        w = (rng.standard_normal((rows, k)) * std).astype(np.float32)
+        c, s, m = quantize(w)
+        parts.append(pack_gemv(c, s, m))
+        cs.append(c)
+        ss.append(s)
+        ms.append(m)
+    return b"".join(parts), np.concatenate(cs), np.concatenate(ss), np.concatenate(ms)
+
+
 def dequantize_packed(buf, n: int, k: int) -> np.ndarray:
     """parse_gemv + dequantize_simple: the f32 weights the CPU path multiplies by."""
     return dequantize_simple(*parse_gemv(buf, K=k, M=n))

@@ -1,0 +1,652 @@
+// q4nx weight-dequant-fused GEMV for T = 1..16 token rows (decode).
+//
+// Arithmetic.  For output row n and 32-column group g,
+//     y[t,n] = sum_g scale[n,g] * D[t,n,g] + min[n,g] * S[t,g]
+// with D = sum code*x over the group and S = sum x over the group -- the same
+// factorisation the reference's NPU kernel uses (kernels/gemv/q4nx_gemv.cc:88-124),
+// but with every product and partial sum kept in f32 (the reference's CPU
+// oracle, host/backend.py:402-417, multiplies the f32-dequantised weights).
+// D comes from the tensor cores: codes enter as exact bf16 values 128+code
+// (one LOP3 per two weights), so the mma yields D' = D + 128*S and the group
+// update is  acc += scale*D' + (min - 128*scale)*S  in f32.
+//
+// Streaming.  A persistent grid (one CTA per SM, 8 warps) splits the matrix's
+// units (16 rows x 256 columns, 2560 B) into equal contiguous ranges, one per
+// warp ("stream-K").  Each warp owns a 3-deep ring in shared memory fed by
+// 1-D bulk copies (cp.async.bulk + mbarrier, L2 evict-first), so every byte
+// of the matrix is requested up front.  A row tile whose K range is split
+// between warps is reduced deterministically: each warp stores its partial,
+// and the last to arrive (per-tile counter) sums the partials in warp order,
+// applies bias/rounding and resets the counter.  The partition depends only on
+// (N, K, SM count), never on T, so a row's result is independent of the batch.
+//
+// Activations.  Each CTA stages the T x K activations once in shared memory,
+// already permuted into mma B-fragment order, together with the 32-column
+// group sums S; the unit loop then reads them with 16-byte shared loads.
+// (For K too large to stage, a small prep kernel writes the same layout to
+// global scratch and the unit loop reads it through the read-only path.)
+//
+// Launch chaining.  The kernel uses programmatic dependent launch: it issues
+// its first weight copies while the previous kernel in the stream is still
+// running and only waits (griddepcontrol.wait) before it reads activations or
+// touches scratch, so back-to-back GEMVs overlap their HBM traffic.
+#include <string.h>
+
+#include "rc_device.cuh"
+#include "rc_internal.cuh"
+
+namespace rc {
+
+enum GemvEpilogue : int {
+  kEpiBf16 = 0,   // y[t][n] = bf16_rne(acc + bias)
+  kEpiF32 = 1,    // token slots (2t, 2t+1) carry the hi/lo bf16 split of an f32 row
+  kEpiGlu = 2,    // unit rows (g, g+8) are (gate, up): y[t][8*tile+g] = bf16(act(bf16 g, bf16 u))
+  kEpiF32Raw = 3, // bf16 activations, unrounded f32 output
+};
+
+struct GemvParams {
+  const uint8_t *tiles;    // first unit of the row range, t16 layout
+  int n_tiles;             // row tiles (16 rows) in the range
+  int kb;                  // K / 256
+  int active_warps;        // warps that own units (<= units)
+  int stages;              // weight ring depth per warp
+  int slots;               // token slots holding data (bf16: T, f32: 2T); others are never read back
+  // activations: raw (staged path) ...
+  const void *x;
+  int x_dtype;
+  int ldx;
+  int tokens;              // real token rows (bf16/glu: <= 16, f32: <= 8)
+  int x_vec;               // x rows 16-byte aligned: vector loads allowed
+  // ... or pre-permuted in global scratch (large-K path)
+  const uint32_t *xfrag;
+  const float *gsum;
+  void *y;
+  int ldy;
+  const float *bias;       // f32 per row of the range, or null
+  float *partials;
+  int *counters;
+  int *err;
+  int act;
+  float gate_beta, value_beta;
+};
+
+// Activation layout (shared or global):
+// xfrag: for token block tb (8 token slots) and k16-step s, lane l = 4g+q holds
+//   word0 = {x[slot g][16s+2q], x[g][16s+2q+1]}, word1 = {x[g][16s+2q+8], ..+9}
+// (the mma B fragment); stored so a lane reads 4 steps as two 16-byte loads:
+//   word index ((tb*(K/64) + s/4)*32 + l)*8 + (s%4)*2 + {0,1}.
+// gsum: for tb, group grp = 8*kbi + gi and quad lane q, float2 {S[2q], S[2q+1]}
+//   at float index ((((tb*KB + kbi)*4 + q)*8 + gi)*2.
+// Token slots: bf16 input -> slot = token; f32 input -> slots 2t / 2t+1 hold
+// the bf16 hi / lo parts of token t (x = hi + lo to 2^-17 relative).
+__host__ __device__ constexpr size_t xfrag_bytes(int ntb, int k) { return (size_t)ntb * 16 * k; }
+__host__ __device__ constexpr size_t gsum_bytes(int ntb, int k) { return (size_t)ntb * k; }
+
+// Eight consecutive activations x[slot][k..k+8) as bf16 pairs.
+__device__ __forceinline__ void load8(const GemvParams &p, int slot, int k, uint32_t (&w)[4]) {
+  w[0] = w[1] = w[2] = w[3] = 0u;
+  if (p.x_dtype == RC_DTYPE_BF16) {
+    if (slot >= p.tokens) return;
+    const uint16_t *row = static_cast<const uint16_t *>(p.x) + (size_t)slot * p.ldx + k;
+    if (p.x_vec) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(row);
+      w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = (uint32_t)row[2 * i] | ((uint32_t)row[2 * i + 1] << 16);
+    }
+    return;
+  }
+  const int t = slot >> 1;
+  if (t >= p.tokens) return;
+  const float *row = static_cast<const float *>(p.x) + (size_t)t * p.ldx + k;
+  float v[8];
+  if (p.x_vec) {
+    const float4 a = *reinterpret_cast<const float4 *>(row), b = *reinterpret_cast<const float4 *>(row + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = row[i];
+  }
+  uint32_t h[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint16_t hi = f32_to_bf16_rne(v[i]);
+    h[i] = (slot & 1) ? f32_to_bf16_rne(v[i] - bf16_to_f32(hi)) : hi;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = h[2 * i] | (h[2 * i + 1] << 16);
+}
+
+// Build the fragment-ordered activations and group sums for all token slots
+// of NTB blocks.  Called by every thread of the CTA (or grid); ``stride``
+// threads cooperate.  Each group of 32 columns is summed as four sequential
+// 8-element partials combined pairwise, a fixed order.
+template <bool SHARED>
+__device__ __forceinline__ void build_activations(const GemvParams &p, int ntb, uint32_t *xf, float *gs,
+                                                  long long first, long long stride) {
+  const int k = p.kb * kUnitK, k64 = k / 64, c8n = k / 8;
+  // Only the slots that hold data are built: the B columns of empty slots feed
+  // mma output columns that are never stored, so their contents do not matter.
+  const long long total = (long long)p.slots * c8n;   // multiple of 32: whole warps iterate together
+  for (long long idx = first; idx < total; idx += stride) {
+    const int slot = (int)(idx / c8n), c8 = (int)(idx - (long long)slot * c8n);
+    const int kk = c8 * 8;
+    uint32_t w[4];
+    load8(p, slot, kk, w);
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      part += bf16_to_f32(w[i] & 0xFFFFu);
+      part += bf16_to_f32(w[i] >> 16);
+    }
+    const int s = kk >> 4, j = (kk >> 3) & 1, tb = slot >> 3, g = slot & 7;
+    const size_t base = ((size_t)tb * k64 + (s >> 2)) * 32 * 8 + (s & 3) * 2 + j;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) xf[base + (size_t)(g * 4 + q) * 8] = w[q];
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    if ((c8 & 3) == 0) {
+      const int grp = c8 >> 2, kbi = grp >> 3, gi = grp & 7;
+      gs[((((size_t)tb * p.kb + kbi) * 4 + (g >> 1)) * 8 + gi) * 2 + (g & 1)] = part;
+    }
+  }
+}
+
+// Large-K path: the activations go to global scratch in the same layout.
+__global__ void gemv_prep_kernel(GemvParams p, int ntb, uint32_t *xfrag, float *gsum) {
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  build_activations<false>(p, ntb, xfrag, gsum, blockIdx.x * (long long)blockDim.x + threadIdx.x,
+                           (long long)gridDim.x * blockDim.x);
+}
+
+// --------------------------------------------------------- main kernel --
+template <int NTB>
+struct Acc {
+  float v[NTB][4];
+};
+
+__device__ __forceinline__ long long range_start(long long w, long long units, long long warps) {
+  return w * units / warps;
+}
+// Warp whose range contains unit u (ranges are floor(w*U/W), all non-empty).
+__device__ __forceinline__ long long warp_of_unit(long long u, long long units, long long warps) {
+  return ((u + 1) * warps + units - 1) / units - 1;
+}
+
+template <int NTB, bool STAGED>
+__device__ __forceinline__ void compute_unit(const uint8_t *unit, const uint32_t *xf, const float *gs,
+                                             const GemvParams &p, int kbi, int lane, Acc<NTB> &acc) {
+  const int g = lane >> 2, q = lane & 3;
+  const uint4 *codes = reinterpret_cast<const uint4 *>(unit) + lane;
+  const uint4 *params = reinterpret_cast<const uint4 *>(unit + kUnitCodeBytes + g * 64);
+  const int k64 = p.kb * 4;
+#pragma unroll
+  for (int s4 = 0; s4 < 4; ++s4) {
+    const uint4 cw = codes[s4 * 32];
+    const uint4 sm = params[s4];
+    uint4 xa[NTB], xb[NTB];
+    float4 gsv[NTB];
+#pragma unroll
+    for (int tb = 0; tb < NTB; ++tb) {
+      const uint4 *xv = reinterpret_cast<const uint4 *>(xf + (((size_t)tb * k64 + kbi * 4 + s4) * 32 + lane) * 8);
+      const float4 *gp = reinterpret_cast<const float4 *>(gs + ((((size_t)tb * p.kb + kbi) * 4 + q) * 8 + 2 * s4) * 2);
+      if (STAGED) {
+        xa[tb] = xv[0];
+        xb[tb] = xv[1];
+        gsv[tb] = gp[0];
+      } else {
+        xa[tb] = __ldg(xv);
+        xb[tb] = __ldg(xv + 1);
+        gsv[tb] = __ldg(gp);
+      }
+    }
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t wa = half ? cw.z : cw.x;
+      const uint32_t wb = half ? cw.w : cw.y;
+      float d[NTB][4];
+#pragma unroll
+      for (int tb = 0; tb < NTB; ++tb) d[tb][0] = d[tb][1] = d[tb][2] = d[tb][3] = 0.f;
+      {
+        const uint32_t a0 = codes_to_bf16x2<0>(wa), a1 = codes_to_bf16x2<1>(wa);
+        const uint32_t a2 = codes_to_bf16x2<2>(wa), a3 = codes_to_bf16x2<3>(wa);
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb)
+          mma_bf16_16816(d[tb], a0, a1, a2, a3, half ? xb[tb].x : xa[tb].x, half ? xb[tb].y : xa[tb].y);
+      }
+      {
+        const uint32_t a0 = codes_to_bf16x2<0>(wb), a1 = codes_to_bf16x2<1>(wb);
+        const uint32_t a2 = codes_to_bf16x2<2>(wb), a3 = codes_to_bf16x2<3>(wb);
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb)
+          mma_bf16_16816(d[tb], a0, a1, a2, a3, half ? xb[tb].z : xa[tb].z, half ? xb[tb].w : xa[tb].w);
+      }
+      const uint32_t lo = half ? sm.z : sm.x;   // {scale[g], min[g]}
+      const uint32_t hi = half ? sm.w : sm.y;   // {scale[g+8], min[g+8]}
+      const float sc0 = bf16_to_f32(lo & 0xFFFFu), mn0 = bf16_to_f32(lo >> 16);
+      const float sc1 = bf16_to_f32(hi & 0xFFFFu), mn1 = bf16_to_f32(hi >> 16);
+      const float mp0 = fmaf(-128.f, sc0, mn0), mp1 = fmaf(-128.f, sc1, mn1);
+#pragma unroll
+      for (int tb = 0; tb < NTB; ++tb) {
+        const float S0 = half ? gsv[tb].z : gsv[tb].x;
+        const float S1 = half ? gsv[tb].w : gsv[tb].y;
+        acc.v[tb][0] = fmaf(sc0, d[tb][0], fmaf(mp0, S0, acc.v[tb][0]));
+        acc.v[tb][1] = fmaf(sc0, d[tb][1], fmaf(mp0, S1, acc.v[tb][1]));
+        acc.v[tb][2] = fmaf(sc1, d[tb][2], fmaf(mp1, S0, acc.v[tb][2]));
+        acc.v[tb][3] = fmaf(sc1, d[tb][3], fmaf(mp1, S1, acc.v[tb][3]));
+      }
+    }
+  }
+}
+
+template <int NTB, int EPI>
+__device__ __forceinline__ void finalize_tile(const GemvParams &p, long long tile, int lane, const Acc<NTB> &a) {
+  const int g = lane >> 2, q = lane & 3;
+  const int r0 = (int)tile * kUnitRows + g, r1 = r0 + 8;
+#pragma unroll
+  for (int tb = 0; tb < NTB; ++tb) {
+    const int t0 = tb * 8 + 2 * q;
+    // The bias is added only when present (no +0.0 that would turn -0.0 into +0.0).
+    if (EPI == kEpiBf16 || EPI == kEpiF32Raw) {
+      float v00 = a.v[tb][0], v01 = a.v[tb][1], v10 = a.v[tb][2], v11 = a.v[tb][3];
+      if (p.bias) {
+        const float b0 = p.bias[r0], b1 = p.bias[r1];
+        v00 += b0;
+        v01 += b0;
+        v10 += b1;
+        v11 += b1;
+      }
+      if (EPI == kEpiBf16) {
+        uint16_t *y = static_cast<uint16_t *>(p.y);
+        if (t0 < p.tokens) {
+          y[(size_t)t0 * p.ldy + r0] = f32_to_bf16_rne(v00);
+          y[(size_t)t0 * p.ldy + r1] = f32_to_bf16_rne(v10);
+        }
+        if (t0 + 1 < p.tokens) {
+          y[(size_t)(t0 + 1) * p.ldy + r0] = f32_to_bf16_rne(v01);
+          y[(size_t)(t0 + 1) * p.ldy + r1] = f32_to_bf16_rne(v11);
+        }
+      } else {
+        float *y = static_cast<float *>(p.y);
+        if (t0 < p.tokens) {
+          y[(size_t)t0 * p.ldy + r0] = v00;
+          y[(size_t)t0 * p.ldy + r1] = v10;
+        }
+        if (t0 + 1 < p.tokens) {
+          y[(size_t)(t0 + 1) * p.ldy + r0] = v01;
+          y[(size_t)(t0 + 1) * p.ldy + r1] = v11;
+        }
+      }
+    } else if (EPI == kEpiF32) {
+      float *y = static_cast<float *>(p.y);
+      const int t = tb * 4 + q;
+      if (t < p.tokens) {
+        float v0 = a.v[tb][0] + a.v[tb][1], v1 = a.v[tb][2] + a.v[tb][3];
+        if (p.bias) {
+          v0 += p.bias[r0];
+          v1 += p.bias[r1];
+        }
+        y[(size_t)t * p.ldy + r0] = v0;
+        y[(size_t)t * p.ldy + r1] = v1;
+      }
+    } else {
+      uint16_t *y = static_cast<uint16_t *>(p.y);
+      const int col = (int)tile * 8 + g;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = t0 + e;
+        if (t < p.tokens) {
+          const float gate = bf16_round(a.v[tb][e]);
+          const float up = bf16_round(a.v[tb][2 + e]);
+          const float v = p.act == RC_ACT_SITU ? act_situ(gate, up, p.gate_beta, p.value_beta) : act_swiglu(gate, up);
+          y[(size_t)t * p.ldy + col] = f32_to_bf16_rne(v);
+        }
+      }
+    }
+  }
+}
+
+template <int NTB, int EPI>
+__device__ void flush_tile(const GemvParams &p, long long tile, long long ub, long long ue, long long gw,
+                           long long units, int lane, const Acc<NTB> &acc) {
+  const long long first = tile * p.kb, last = first + p.kb - 1;
+  if (first >= ub && last < ue) {
+    finalize_tile<NTB, EPI>(p, tile, lane, acc);
+    return;
+  }
+  const long long W = p.active_warps;
+  const int slot = (tile == ub / p.kb) ? 0 : 1;
+  float4 *part = reinterpret_cast<float4 *>(p.partials);
+#pragma unroll
+  for (int tb = 0; tb < NTB; ++tb)
+    part[((gw * 2 + slot) * 2 + tb) * 32 + lane] = make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3]);
+  __threadfence();
+  __syncwarp();
+  const long long w_first = warp_of_unit(first, units, W), w_last = warp_of_unit(last, units, W);
+  int is_last = 0;
+  if (lane == 0) {
+    const int pieces = (int)(w_last - w_first + 1);
+    const int old = atomicAdd(p.counters + tile, 1);
+    is_last = (old == pieces - 1);
+    if (is_last) atomicExch(p.counters + tile, 0);
+  }
+  is_last = __shfl_sync(0xffffffffu, is_last, 0);
+  if (!is_last) return;
+  __threadfence();
+  Acc<NTB> sum;
+#pragma unroll
+  for (int tb = 0; tb < NTB; ++tb) sum.v[tb][0] = sum.v[tb][1] = sum.v[tb][2] = sum.v[tb][3] = 0.f;
+  // Issue up to 8 pieces' loads before summing them (one L2 round trip per
+  // batch), then add in warp order -- the same order for every launch.
+  constexpr int kBatch = 8;
+  for (long long w0 = w_first; w0 <= w_last; w0 += kBatch) {
+    float4 v[kBatch][NTB];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const long long w2 = w0 + i;
+      if (w2 > w_last) break;
+      const int s2 = (tile == range_start(w2, units, W) / p.kb) ? 0 : 1;
+#pragma unroll
+      for (int tb = 0; tb < NTB; ++tb)
+        v[i][tb] = w2 == gw ? make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3])
+                            : __ldcg(part + ((w2 * 2 + s2) * 2 + tb) * 32 + lane);
+    }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      if (w0 + i > w_last) break;
+#pragma unroll
+      for (int tb = 0; tb < NTB; ++tb) {
+        sum.v[tb][0] += v[i][tb].x;
+        sum.v[tb][1] += v[i][tb].y;
+        sum.v[tb][2] += v[i][tb].z;
+        sum.v[tb][3] += v[i][tb].w;
+      }
+    }
+  }
+  finalize_tile<NTB, EPI>(p, tile, lane, sum);
+}
+
+template <int NTB>
+constexpr int gemv_min_blocks() { return NTB == 1 ? 2 : 1; }
+
+template <int NTB, int EPI, bool STAGED>
+__global__ void __launch_bounds__(kGemvThreads, gemv_min_blocks<NTB>()) gemv_kernel(GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long gw = (long long)blockIdx.x * kGemvWarps + warp;
+  const bool active = gw < p.active_warps;
+  const long long units = (long long)p.n_tiles * p.kb;
+  const long long W = p.active_warps;
+  const long long ub = active ? range_start(gw, units, W) : 0;
+  const long long ue = active ? range_start(gw + 1, units, W) : 0;
+  const int n = (int)(ue - ub);
+  const int k = p.kb * kUnitK;
+
+  const int S = p.stages;
+  uint8_t *ring = smem + warp * S * kUnitBytes;
+  const uint32_t ring_s = smem_addr(ring);
+  uint8_t *after_ring = smem + kGemvWarps * S * kUnitBytes;
+  uint32_t *xs = reinterpret_cast<uint32_t *>(after_ring);
+  float *gs = reinterpret_cast<float *>(after_ring + (STAGED ? xfrag_bytes(NTB, k) : 0));
+  uint8_t *bars = after_ring + (STAGED ? xfrag_bytes(NTB, k) + gsum_bytes(NTB, k) : 0);
+  const uint32_t bar0 = smem_addr(bars) + warp * S * 8;
+  const uint64_t pol = policy_evict_first();
+  if (lane == 0 && n > 0) {
+    for (int s = 0; s < S; ++s) mbar_init(bar0 + 8 * s, 1);
+    mbar_fence_init();
+    for (int j = 0; j < n && j < S; ++j) {
+      mbar_arrive_expect_tx(bar0 + 8 * j, kUnitBytes);
+      bulk_copy_g2s(ring_s + j * kUnitBytes, p.tiles + (size_t)(ub + j) * kUnitBytes, kUnitBytes, bar0 + 8 * j, pol);
+    }
+  }
+  pdl_launch_dependents();
+  // Weights are in flight; now wait for the producer of x (and for any earlier
+  // launch that shares the scratch) before touching anything it wrote.
+  pdl_wait_prior();
+  if (STAGED) {
+    build_activations<true>(p, NTB, xs, gs, threadIdx.x, blockDim.x);
+    __syncthreads();
+  }
+  if (n == 0) return;
+  const uint32_t *xf = STAGED ? xs : p.xfrag;
+  const float *gsp = STAGED ? gs : p.gsum;
+
+  Acc<NTB> acc;
+#pragma unroll
+  for (int tb = 0; tb < NTB; ++tb) acc.v[tb][0] = acc.v[tb][1] = acc.v[tb][2] = acc.v[tb][3] = 0.f;
+  long long cur = ub / p.kb;
+  for (int j = 0; j < n; ++j) {
+    const long long u = ub + j;
+    const long long tile = u / p.kb;
+    const int kbi = (int)(u - tile * p.kb);
+    if (tile != cur) {
+      flush_tile<NTB, EPI>(p, cur, ub, ue, gw, units, lane, acc);
+#pragma unroll
+      for (int tb = 0; tb < NTB; ++tb) acc.v[tb][0] = acc.v[tb][1] = acc.v[tb][2] = acc.v[tb][3] = 0.f;
+      cur = tile;
+    }
+    const int slot = j % S;
+    if (!mbar_wait_bounded(bar0 + 8 * slot, (uint32_t)((j / S) & 1))) {
+      if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+      // Let the copies already issued land before the CTA's shared memory goes away.
+      for (int j2 = j + 1; j2 < n && j2 < j + S; ++j2)
+        mbar_wait_bounded(bar0 + 8 * (j2 % S), (uint32_t)((j2 / S) & 1));
+      return;
+    }
+    compute_unit<NTB, STAGED>(ring + slot * kUnitBytes, xf, gsp, p, kbi, lane, acc);
+    __syncwarp();
+    if (lane == 0 && j + S < n) {
+      mbar_arrive_expect_tx(bar0 + 8 * slot, kUnitBytes);
+      bulk_copy_g2s(ring_s + slot * kUnitBytes, p.tiles + (size_t)(u + S) * kUnitBytes, kUnitBytes,
+                    bar0 + 8 * slot, pol);
+    }
+  }
+  flush_tile<NTB, EPI>(p, cur, ub, ue, gw, units, lane, acc);
+}
+
+// ------------------------------------------------------------------ host --
+static size_t gemv_smem_bytes(int ntb, int k, bool staged, int stages) {
+  size_t b = (size_t)kGemvWarps * stages * (kUnitBytes + 8);
+  if (staged) b += xfrag_bytes(ntb, k) + gsum_bytes(ntb, k);
+  return b;
+}
+
+// Ring depth: deep enough to cover a warp's whole range for small matrices
+// (everything requested at once), bounded by shared memory for large ones.
+// Small rings keep the footprint low so consecutive launches can co-reside
+// on an SM under programmatic dependent launch.
+static int gemv_stages(int ntb, int k, bool staged, long long units_per_warp) {
+  int s = (int)(units_per_warp < 2 ? 2 : (units_per_warp > kGemvMaxStages ? kGemvMaxStages : units_per_warp));
+  while (s > 2 && gemv_smem_bytes(ntb, k, staged, s) > (size_t)kGemvSmemLimit) --s;
+  return s;
+}
+
+static cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s, cudaLaunchAttribute *attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+template <int NTB, int EPI, bool STAGED>
+static cudaError_t launch_main(const GemvParams &p, int grid, cudaStream_t s) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(gemv_kernel<NTB, EPI, STAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kGemvSmemLimit);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kGemvThreads),
+                                      gemv_smem_bytes(NTB, p.kb * kUnitK, STAGED, p.stages),
+                                      s, attr);
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<NTB, EPI, STAGED>, p);
+}
+
+template <int NTB, bool STAGED>
+static cudaError_t launch_epi(const GemvParams &p, int epi, int grid, cudaStream_t s) {
+  switch (epi) {
+    case kEpiBf16: return launch_main<NTB, kEpiBf16, STAGED>(p, grid, s);
+    case kEpiF32: return launch_main<NTB, kEpiF32, STAGED>(p, grid, s);
+    case kEpiF32Raw: return launch_main<NTB, kEpiF32Raw, STAGED>(p, grid, s);
+    default: return launch_main<NTB, kEpiGlu, STAGED>(p, grid, s);
+  }
+}
+
+// Grid of the persistent kernel for a given unit count: a function of the
+// matrix shape and SM count only (never of T), so results are batch-invariant.
+void gemv_geometry(const rc_ctx *ctx, long long units, int *grid, int *active_warps) {
+  long long g = (units + kGemvWarps - 1) / kGemvWarps;
+  if (g > ctx->sm_count) g = ctx->sm_count;
+  if (g < 1) g = 1;
+  long long w = g * kGemvWarps;
+  if (w > units) w = units;
+  *grid = (int)g;
+  *active_warps = (int)w;
+}
+
+// Token slots one launch can stage for K columns (16 when they fit in shared memory).
+bool gemv_can_stage(int ntb, int k) { return gemv_smem_bytes(ntb, k, true, 2) <= (size_t)kGemvSmemLimit; }
+
+// One launch over <= 16 bf16 token rows (<= 8 f32 rows).
+int gemv_launch(rc_ctx *ctx, const uint8_t *tiles, int n_tiles, int k, const void *x, int x_dtype, int ldx,
+                int tokens, void *y, int ldy, const float *bias, int epi, int act, float gb, float vb,
+                cudaStream_t s) {
+  const int slots = x_dtype == RC_DTYPE_F32 ? 2 * tokens : tokens;
+  const int ntb = slots > 8 ? 2 : 1;
+  const bool staged = gemv_can_stage(ntb, k);
+  int rc = ensure_gemv_scratch(ctx, staged ? 0 : k, n_tiles);
+  if (rc) return rc;
+  GemvParams p{};
+  p.tiles = tiles;
+  p.n_tiles = n_tiles;
+  p.kb = k / kUnitK;
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.ldx = ldx;
+  p.tokens = tokens;
+  p.slots = slots;
+  const size_t esz = x_dtype == RC_DTYPE_F32 ? 4 : 2;
+  p.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && ((size_t)ldx * esz) % 16 == 0) ? 1 : 0;
+  p.y = y;
+  p.ldy = ldy;
+  p.bias = bias;
+  p.partials = ctx->partials;
+  p.counters = ctx->counters;
+  p.err = ctx->err;
+  p.act = act;
+  p.gate_beta = gb;
+  p.value_beta = vb;
+  cudaError_t e;
+  if (!staged) {
+    const unsigned xs = ctx->launch_seq++ % kXSlots;
+    p.xfrag = ctx->xfrag + xs * xfrag_slot_words(ctx->xfrag_k);
+    p.gsum = ctx->gsum + xs * gsum_slot_floats(ctx->xfrag_k);
+    const long long work = (long long)p.slots * (k / 8);
+    long long pg = (work + 255) / 256;
+    if (pg > ctx->sm_count) pg = ctx->sm_count;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)pg), dim3(256), 0, s, attr);
+    e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel, p, ntb, const_cast<uint32_t *>(p.xfrag),
+                           const_cast<float *>(p.gsum));
+    if (e != cudaSuccess) {
+      set_error("gemv prep launch: %s", cudaGetErrorString(e));
+      return RC_ERR_CUDA;
+    }
+  }
+  int grid = 0;
+  gemv_geometry(ctx, (long long)n_tiles * p.kb, &grid, &p.active_warps);
+  const long long units = (long long)n_tiles * p.kb;
+  p.stages = gemv_stages(ntb, k, staged, (units + p.active_warps - 1) / p.active_warps);
+  if (staged)
+    e = ntb == 2 ? launch_epi<2, true>(p, epi, grid, s) : launch_epi<1, true>(p, epi, grid, s);
+  else
+    e = ntb == 2 ? launch_epi<2, false>(p, epi, grid, s) : launch_epi<1, false>(p, epi, grid, s);
+  if (e != cudaSuccess) {
+    set_error("gemv launch: %s", cudaGetErrorString(e));
+    return RC_ERR_CUDA;
+  }
+  return RC_OK;
+}
+
+}  // namespace rc
+
+using namespace rc;
+
+extern "C" {
+
+int rc_gemv(rc_ctx *ctx, const rc_weight *w, const void *x_dev, int x_dtype, int ldx, int T, void *y_dev,
+            int y_dtype, int ldy, int row0, int nrows, const float *bias_dev, void *stream) {
+  RC_CHECK_ARG(ctx && x_dev && y_dev, "rc_gemv: NULL argument");
+  if (!w) {
+    set_error("rc_gemv: unknown weight handle");
+    return RC_ERR_NOT_FOUND;
+  }
+  RC_CHECK_ARG(!(w->flags & RC_UPLOAD_GATE_UP), "rc_gemv: a gate/up-interleaved matrix is only usable by the MoE path");
+  RC_CHECK_ARG(x_dtype == RC_DTYPE_BF16 || x_dtype == RC_DTYPE_F32, "rc_gemv: x_dtype must be BF16 or F32");
+  RC_CHECK_ARG(y_dtype == RC_DTYPE_F32 || (y_dtype == RC_DTYPE_BF16 && x_dtype == RC_DTYPE_BF16),
+               "rc_gemv: y_dtype must be F32, or BF16 with BF16 activations");
+  RC_CHECK_ARG(T >= 1, "rc_gemv: T must be >= 1 (got %d)", T);
+  RC_CHECK_ARG(row0 >= 0 && nrows > 0 && row0 % kUnitRows == 0 && nrows % kUnitRows == 0 && row0 + nrows <= w->n,
+               "rc_gemv: rows [%d, %d) must be 16-aligned inside [0, %d)", row0, row0 + nrows, w->n);
+  RC_CHECK_ARG(ldx >= w->k, "rc_gemv: ldx (%d) < K (%d)", ldx, w->k);
+  RC_CHECK_ARG(ldy >= nrows, "rc_gemv: ldy (%d) < nrows (%d)", ldy, nrows);
+  RC_CUDA_TRY(cudaSetDevice(ctx->device));
+  const cudaStream_t s = pick_stream(ctx, stream);
+  const int per = x_dtype == RC_DTYPE_F32 ? kMaxTokensPerLaunch / 2 : kMaxTokensPerLaunch;
+  const size_t xe = x_dtype == RC_DTYPE_F32 ? 4 : 2;
+  const size_t ye = y_dtype == RC_DTYPE_F32 ? 4 : 2;
+  const int epi = x_dtype == RC_DTYPE_F32 ? kEpiF32 : (y_dtype == RC_DTYPE_F32 ? kEpiF32Raw : kEpiBf16);
+  const uint8_t *tiles = w->tiles + (size_t)(row0 / kUnitRows) * (w->k / kUnitK) * kUnitBytes;
+  const float *bias = bias_dev ? bias_dev + row0 : nullptr;
+  for (int t0 = 0; t0 < T; t0 += per) {
+    const int tc = T - t0 < per ? T - t0 : per;
+    const void *xc = static_cast<const uint8_t *>(x_dev) + (size_t)t0 * ldx * xe;
+    void *yc = static_cast<uint8_t *>(y_dev) + (size_t)t0 * ldy * ye;
+    int rc = gemv_launch(ctx, tiles, nrows / kUnitRows, w->k, xc, x_dtype, ldx, tc, yc, ldy, bias, epi, 0, 0.f,
+                         0.f, s);
+    if (rc) return rc;
+  }
+  return RC_OK;
+}
+
+int rc_gemv_host(rc_ctx *ctx, const rc_weight *w, const void *x_host, int x_dtype, int T, void *y_host,
+                 const float *bias_dev) {
+  RC_CHECK_ARG(ctx && x_host && y_host, "rc_gemv_host: NULL argument");
+  if (!w) {
+    set_error("rc_gemv_host: unknown weight handle");
+    return RC_ERR_NOT_FOUND;
+  }
+  RC_CHECK_ARG(T >= 1, "rc_gemv_host: T must be >= 1 (got %d)", T);
+  RC_CHECK_ARG(x_dtype == RC_DTYPE_BF16 || x_dtype == RC_DTYPE_F32, "rc_gemv_host: x_dtype must be BF16 or F32");
+  RC_CUDA_TRY(cudaSetDevice(ctx->device));
+  const size_t xe = x_dtype == RC_DTYPE_F32 ? 4 : 2;
+  const size_t xb = (size_t)T * w->k * xe, yb = (size_t)T * w->n * xe;
+  int rc = ensure_host_staging(ctx, xb, yb);
+  if (rc) return rc;
+  memcpy(ctx->pin_x, x_host, xb);
+  RC_CUDA_TRY(cudaMemcpyAsync(ctx->dev_x, ctx->pin_x, xb, cudaMemcpyHostToDevice, ctx->stream));
+  rc = rc_gemv(ctx, w, ctx->dev_x, x_dtype, w->k, T, ctx->dev_y, x_dtype, w->n, 0, w->n, bias_dev, nullptr);
+  if (rc) return rc;
+  RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, yb, cudaMemcpyDeviceToHost, ctx->stream));
+  RC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  rc = check_error_word(ctx);
+  if (rc) return rc;
+  memcpy(y_host, ctx->pin_y, yb);
+  return RC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,130 @@
+// Device-side helpers: bf16 bit arithmetic, mbarrier / bulk-copy PTX wrappers,
+// programmatic dependent launch controls, and the legacy-register bf16 mma.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rc {
+
+// f32 -> bf16 bits, round to nearest even; every NaN becomes 0x7FC0 (the
+// reference's converter, quant/q4nx.py:32-44, host/weights.py:104-115).
+__device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
+  return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+__device__ __forceinline__ float bf16_to_f32(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+
+__device__ __forceinline__ float bf16_round(float f) { return bf16_to_f32(f32_to_bf16_rne(f)); }
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------- mbarrier --
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase ``parity`` of a barrier, giving up after ``limit_ns`` of
+// global time.  Returns false on timeout; callers record an error word and
+// unwind instead of hanging the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  uint64_t limit_ns = 1000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// ---------------------------------------------------------- bulk copies --
+// L2 policy for data that is streamed exactly once (weights).
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing on ``bar``.
+// Both addresses 16-byte aligned, ``bytes`` a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// ------------------------------------------- programmatic dependent launch --
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// --------------------------------------------------------------------- mma --
+// D(16x8 f32) += A(16x16 bf16, row) * B(16x8 bf16, col), register operands.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two 4-bit codes at bits [j*4, j*4+4) and [16+j*4, 16+j*4+4) -> bf16x2 {128+lo, 128+hi}.
+template <int J>
+__device__ __forceinline__ uint32_t codes_to_bf16x2(uint32_t w) {
+  return ((w >> (4 * J)) & 0x000F000Fu) | 0x43004300u;
+}
+
+// --------------------------------------------------------------- GLU acts --
+// SiLU-GLU with the overflow-free sigmoid (kernels/moe/reference.py:160-170).
+__device__ __forceinline__ float act_swiglu(float g, float u) {
+  const float e = expf(-fabsf(g));
+  const float sig = g >= 0.f ? 1.f / (1.f + e) : e / (1.f + e);
+  return (g * sig) * u;
+}
+
+// SiTU-GLU: gb*tanh(g/gb)*sigmoid(g) * vb*tanh(v/vb) (host/backend.py:47-62).
+__device__ __forceinline__ float act_situ(float g, float v, float gb, float vb) {
+  const float sig = 1.f / (1.f + expf(-g));
+  const float t1 = (gb * tanhf(g / gb)) * sig;
+  const float t2 = vb * tanhf(v / vb);
+  return t1 * t2;
+}
+
+}  // namespace rc

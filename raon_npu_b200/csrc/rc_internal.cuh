@@ -1,0 +1,115 @@
+// Internal definitions shared by the raon_cuda translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string>
+
+#include "../../include/raon_cuda.h"
+
+namespace rc {
+
+// ----------------------------------------------------------- tile layout --
+// GPU tile layout of a q4nx matrix ("t16"): the matrix is cut into units of
+// 16 output rows x 256 input columns, stored unit after unit in
+// (row-tile, k-block) order, 2560 bytes each (= 16*256*5/8, the same bits per
+// weight as the reference's pack_gemv blocks):
+//   bytes [0, 2048):   4-bit codes in mma.sync A-fragment order.  For k16-step
+//                      s (0..15) and lane l (g = l/4, q = l%4) the 32-bit word at
+//                      byte ((s/4)*32 + l)*16 + (s%4)*4 holds
+//                        bits  0..3 / 16..19: code[g  ][16s+2q] / [16s+2q+1]
+//                        bits  4..7 / 20..23: code[g+8][16s+2q] / [16s+2q+1]
+//                        bits  8..11/ 24..27: code[g  ][16s+2q+8] / [16s+2q+9]
+//                        bits 12..15/ 28..31: code[g+8][16s+2q+8] / [16s+2q+9]
+//                      so ((w >> 4j) & 0x000F000F) | 0x43004300 is A register j
+//                      as bf16x2 (128 + code), one 16-byte load per lane per
+//                      4 k16-steps, 512 contiguous bytes per warp load.
+//   bytes [2048,2560): per (g = 0..7, group 0..7) 8 bytes at 2048 + (g*8+group)*8:
+//                      bf16 {scale[g], min[g], scale[g+8], min[g+8]}.
+constexpr int kUnitRows = 16;
+constexpr int kUnitK = 256;
+constexpr int kUnitBytes = 2560;
+constexpr int kUnitCodeBytes = 2048;
+constexpr int kGroupsPerUnit = 8;
+
+// Reference pack_gemv block (quant/q4nx.py:335-393).
+constexpr int kRefBlockRows = 32;
+constexpr int kRefBlockBytes = 5120;
+constexpr int kRefParamBytes = 1024;
+
+// GEMV persistent kernel geometry.
+constexpr int kGemvWarps = 8;         // consumer warps per CTA, each with a private ring
+constexpr int kGemvMaxStages = 12;    // ring depth (units in flight) per warp; chosen per launch
+constexpr int kGemvThreads = kGemvWarps * 32;
+constexpr int kGemvSmemLimit = 227 * 1024;   // opt-in dynamic shared memory per CTA on sm_100
+constexpr int kMaxTokensPerLaunch = 16;   // two 8-token mma column blocks
+// Activation scratch rotates over this many slots: consecutive launches chained
+// by programmatic dependent launch may be resident together, and a launch must
+// never read a slot that a still-running neighbour has cached.
+constexpr int kXSlots = 4;
+
+// Device error words (ctx->err): first failure wins.
+constexpr int kErrWaitTimeout = 1;
+
+void set_error(const char *fmt, ...);
+
+#define RC_CUDA_TRY(expr)                                                              \
+  do {                                                                                 \
+    cudaError_t _e = (expr);                                                           \
+    if (_e != cudaSuccess) {                                                           \
+      ::rc::set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__, \
+                      __LINE__);                                                       \
+      return RC_ERR_CUDA;                                                              \
+    }                                                                                  \
+  } while (0)
+
+#define RC_CHECK_ARG(cond, ...)        \
+  do {                                 \
+    if (!(cond)) {                     \
+      ::rc::set_error(__VA_ARGS__);    \
+      return RC_ERR_INVALID;           \
+    }                                  \
+  } while (0)
+
+}  // namespace rc
+
+struct rc_weight {
+  rc_ctx *ctx;
+  int n, k;            // logical rows (N) and columns (K)
+  unsigned flags;      // RC_UPLOAD_* flags it was uploaded with
+  uint8_t *tiles;      // t16 layout, n/16 * k/256 units
+  size_t bytes;
+  float *bias;         // optional f32 [n] on the device
+};
+
+struct rc_ctx {
+  int device;
+  int sm_count;
+  cudaStream_t stream;
+  // GEMV scratch: fragment-ordered x, group sums, split-K partials, tile counters.
+  uint32_t *xfrag;      // kXSlots x [2 token blocks][K/64][32 lanes][8 words]
+  size_t xfrag_k;       // K capacity of one xfrag / gsum slot
+  float *gsum;          // kXSlots x [2][K/256][4][8][2]
+  unsigned launch_seq;  // picks the activation slot of the next launch
+  float *partials;      // [warps][2][2 token blocks][32 lanes][4]
+  int *counters;        // [tiles], all zero between launches
+  size_t counters_cap;
+  int *err;             // device error word
+  int *qflag;           // quantiser status word (non-finite input / overflow)
+  // Host staging for rc_gemv_host.
+  void *pin_x, *pin_y;
+  size_t pin_x_cap, pin_y_cap;
+  void *dev_x, *dev_y;
+  size_t dev_x_cap, dev_y_cap;
+};
+
+namespace rc {
+int ensure_gemv_scratch(rc_ctx *ctx, int k, int n_tiles);
+int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb);
+int check_error_word(rc_ctx *ctx);
+// Words of one xfrag slot / floats of one gsum slot for K columns.
+inline size_t xfrag_slot_words(size_t k) { return 2 * k * 4; }
+inline size_t gsum_slot_floats(size_t k) { return k / 2; }
+cudaStream_t pick_stream(rc_ctx *ctx, void *stream);
+}  // namespace rc

@@ -1,0 +1,166 @@
+"""Thin object layer over the C ABI: a device context and uploaded q4nx weights.
+
+Device buffers may be torch tensors (any object with ``data_ptr()``) or raw
+integer addresses; torch is used only as plumbing (allocation, streams).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import check
+
+
+def _ptr(t) -> int:
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    return int(t.data_ptr())
+
+
+def _stream_for(stream, *tensors) -> int:
+    """The stream to launch on: an explicit one, else the current torch stream of
+    the first torch tensor argument (so launches are ordered after the torch
+    copies/allocations that produced the buffers), else 0 = the context stream."""
+    if stream is not None:
+        return int(stream)
+    for t in tensors:
+        if t is not None and hasattr(t, "device") and getattr(t, "is_cuda", False):
+            import torch
+            h = int(torch.cuda.current_stream(t.device).cuda_stream)
+            # torch reports the legacy default stream as 0, which the C ABI
+            # reads as "the context's own stream": pass cudaStreamLegacy instead.
+            return h if h != 0 else CUDA_STREAM_LEGACY
+    return 0
+
+
+CUDA_STREAM_LEGACY = 1   # cudaStreamLegacy
+
+
+class Context:
+    """One CUDA context slot of the library: a stream, SM count and scratch."""
+
+    def __init__(self, device: int = 0):
+        self.lib = _lib.load()
+        h = ctypes.c_void_p()
+        check(self.lib.rc_init(int(device), ctypes.byref(h)), "rc_init")
+        self.handle = h
+        self.device = int(device)
+        s = ctypes.c_void_p()
+        check(self.lib.rc_stream(h, ctypes.byref(s)))
+        self.stream = s.value or 0
+        n = ctypes.c_int()
+        check(self.lib.rc_sm_count(h, ctypes.byref(n)))
+        self.sm_count = n.value
+
+    def sync(self) -> None:
+        check(self.lib.rc_sync(self.handle), "rc_sync")
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.rc_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def upload_q4nx(self, packed, n: int, k: int, gate_up: bool = False) -> "Q4nxWeight":
+        return Q4nxWeight(self, packed, n, k, gate_up=gate_up)
+
+    def quantize_q4nx(self, w_dev, packed_dev, n: int, k: int, stream: int | None = None) -> None:
+        """f32 [n, k] device weights -> pack_gemv bytes on the device (synchronous)."""
+        check(self.lib.rc_quantize_q4nx(self.handle, ctypes.c_void_p(_ptr(w_dev)), int(n), int(k),
+                                        ctypes.c_void_p(_ptr(packed_dev)),
+                                        ctypes.c_void_p(_stream_for(stream, w_dev, packed_dev))),
+              "rc_quantize_q4nx")
+
+
+class Q4nxWeight:
+    """A q4nx matrix resident in HBM in the GEMV tile layout."""
+
+    def __init__(self, ctx: Context, packed, n: int, k: int, gate_up: bool = False):
+        self.ctx = ctx
+        flags = _lib.RC_UPLOAD_GATE_UP if gate_up else 0
+        if isinstance(packed, (bytes, bytearray, memoryview, np.ndarray)):
+            buf = np.frombuffer(packed, dtype=np.uint8) if not isinstance(packed, np.ndarray) else \
+                np.ascontiguousarray(packed, dtype=np.uint8)
+            src, nbytes = buf.ctypes.data, buf.nbytes
+            keep = buf
+        else:  # device tensor: the upload runs on the context stream, so let its producer finish
+            flags |= _lib.RC_UPLOAD_SRC_DEVICE
+            src, nbytes = _ptr(packed), int(packed.numel() * packed.element_size())
+            keep = packed
+            if getattr(packed, "is_cuda", False):
+                import torch
+                torch.cuda.current_stream(packed.device).synchronize()
+        h = ctypes.c_void_p()
+        check(ctx.lib.rc_upload_q4nx(ctx.handle, ctypes.c_void_p(src), nbytes, int(n), int(k), flags,
+                                     ctypes.byref(h)), "rc_upload_q4nx")
+        del keep
+        self.handle = h
+        self.n, self.k, self.gate_up = int(n), int(k), bool(gate_up)
+        self.device_bytes = n * k * 5 // 8
+
+    def set_bias(self, bias: np.ndarray) -> int:
+        """Attach an f32 [n] bias; returns its device address."""
+        b = np.ascontiguousarray(bias, dtype=np.float32)
+        if b.shape != (self.n,):
+            raise ValueError(f"bias must be [{self.n}] float32")
+        check(self.ctx.lib.rc_weight_set_bias(self.handle, ctypes.c_void_p(b.ctypes.data)), "rc_weight_set_bias")
+        p = ctypes.c_void_p()
+        check(self.ctx.lib.rc_weight_bias(self.handle, ctypes.byref(p)))
+        return p.value or 0
+
+    def free(self) -> None:
+        if self.handle:
+            self.ctx.lib.rc_weight_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def dequant_into(self, out_dev, stream: int | None = None) -> None:
+        """Write f32 [n, k] weights into a device buffer (bit-exact dequantisation)."""
+        check(self.ctx.lib.rc_dequant_q4nx(self.ctx.handle, self.handle, ctypes.c_void_p(_ptr(out_dev)),
+                                           ctypes.c_void_p(_stream_for(stream, out_dev))), "rc_dequant_q4nx")
+
+    def gemv_into(self, x_dev, y_dev, tokens: int, x_dtype: int = _lib.RC_DTYPE_BF16, ldx: int | None = None,
+                  ldy: int | None = None, row0: int = 0, nrows: int | None = None, bias_dev=None,
+                  stream: int | None = None, y_dtype: int | None = None) -> None:
+        """Launch ``y = x . W[row0:row0+nrows].T (+bias)`` on device buffers (asynchronous).
+
+        ``y_dtype`` defaults to the activation dtype (the reference contract);
+        f32 output with bf16 activations returns the unrounded sums."""
+        nrows = self.n - row0 if nrows is None else nrows
+        y_dtype = x_dtype if y_dtype is None else y_dtype
+        check(self.ctx.lib.rc_gemv(
+            self.ctx.handle, self.handle, ctypes.c_void_p(_ptr(x_dev)), int(x_dtype),
+            int(self.k if ldx is None else ldx), int(tokens), ctypes.c_void_p(_ptr(y_dev)), int(y_dtype),
+            int(nrows if ldy is None else ldy), int(row0), int(nrows), ctypes.c_void_p(_ptr(bias_dev)),
+            ctypes.c_void_p(_stream_for(stream, x_dev, y_dev))), "rc_gemv")
+
+    def gemv_host(self, x: np.ndarray, bias_dev=None) -> np.ndarray:
+        """Host-buffer GEMV through ``rc_gemv_host`` (copies in, runs, copies out, waits)."""
+        if x.dtype == np.uint16:
+            dt, out = _lib.RC_DTYPE_BF16, np.empty((x.shape[0], self.n), np.uint16)
+        elif x.dtype == np.float32:
+            dt, out = _lib.RC_DTYPE_F32, np.empty((x.shape[0], self.n), np.float32)
+        else:
+            raise ValueError(f"x must be uint16 (bf16 bits) or float32, got {x.dtype}")
+        if x.ndim != 2 or x.shape[1] != self.k:
+            raise ValueError(f"x must be [T, {self.k}], got {x.shape}")
+        xc = np.ascontiguousarray(x)
+        check(self.ctx.lib.rc_gemv_host(self.ctx.handle, self.handle, ctypes.c_void_p(xc.ctypes.data), dt,
+                                        int(x.shape[0]), ctypes.c_void_p(out.ctypes.data),
+                                        ctypes.c_void_p(_ptr(bias_dev))), "rc_gemv_host")
+        return out

@@ -1,0 +1,52 @@
+"""The C-ABI library loads and exports every function ``include/raon_cuda.h``
+declares (CPU only: no function that needs a GPU is called)."""
+
+import ctypes
+import subprocess
+
+import pytest
+
+from raon_npu_b200 import _lib
+from raon_npu_b200.build import LIB, build
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.load()
+
+
+def test_header_declares_what_the_binding_declares():
+    assert _lib.header_functions() == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in _lib.header_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB)], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    missing = [n for n in _lib.header_functions() if n not in exported]
+    assert not missing, missing
+
+
+def test_library_has_no_torch_dependency():
+    out = subprocess.run(["ldd", str(LIB)], capture_output=True, text=True).stdout
+    assert "torch" not in out and "c10" not in out
+
+
+def test_abi_version_and_error_text(lib):
+    assert lib.rc_abi_version() == 1
+    assert isinstance(lib.rc_last_error(), bytes)
+
+
+def test_argument_errors_raise_value_error_without_a_gpu(lib):
+    # NULL out pointer is rejected before any CUDA call.
+    assert lib.rc_init(0, None) == _lib.RC_ERR_INVALID
+    with pytest.raises(ValueError):
+        _lib.check(lib.rc_init(0, None))
+
+
+def test_unknown_weight_handle_is_key_error(lib):
+    n = ctypes.c_int()
+    with pytest.raises(KeyError):
+        _lib.check(lib.rc_weight_info(None, ctypes.byref(n), None, None, None))
