@@ -10,15 +10,18 @@
 // (one LOP3 per two weights), so the mma yields D' = D + 128*S and the group
 // update is  acc += scale*D' + (min - 128*scale)*S  in f32.
 //
-// Streaming.  A persistent grid (one CTA per SM, 8 warps) splits the matrix's
-// units (16 rows x 256 columns, 2560 B) into equal contiguous ranges, one per
-// warp ("stream-K").  Each warp owns a 3-deep ring in shared memory fed by
-// 1-D bulk copies (cp.async.bulk + mbarrier, L2 evict-first), so every byte
-// of the matrix is requested up front.  A row tile whose K range is split
-// between warps is reduced deterministically: each warp stores its partial,
-// and the last to arrive (per-tile counter) sums the partials in warp order,
-// applies bias/rounding and resets the counter.  The partition depends only on
-// (N, K, SM count), never on T, so a row's result is independent of the batch.
+// Streaming.  A grid of at most one CTA per SM (8 warps each) splits the
+// matrix's units (16 rows x 256 columns, 2560 B) into contiguous ranges, one
+// per warp: either each CTA owns whole row tiles and its warps split them
+// (split tiles reduced in shared memory), or -- for a few tall tiles -- all
+// units are split evenly over the grid (split tiles reduced through global
+// partials: the last warp to arrive, by a per-tile counter, sums them and
+// resets the counter).  Either way the pieces of a tile are summed in warp
+// order.  Each warp owns a ring of 2..12 units in shared memory fed by 1-D
+// bulk copies (cp.async.bulk + mbarrier, L2 evict-first); for small matrices
+// the ring holds the warp's whole range, so every byte is requested up front.
+// The partition depends only on (N, K, SM count), never on T, so a row's
+// result is independent of the batch.
 //
 // Activations.  Each CTA stages the T x K activations once in shared memory,
 // already permuted into mma B-fragment order, together with the 32-column
@@ -48,7 +51,9 @@ struct GemvParams {
   const uint8_t *tiles;    // first unit of the row range, t16 layout
   int n_tiles;             // row tiles (16 rows) in the range
   int kb;                  // K / 256
-  int active_warps;        // warps that own units (<= units)
+  int active_warps;        // stream-K partition: warps that own units (<= units)
+  int mode;                // GemvPartition
+  int warps;               // warps per CTA (8 or 16)
   int stages;              // weight ring depth per warp
   int slots;               // token slots holding data (bf16: T, f32: 2T); others are never read back
   // activations: raw (staged path) ...
@@ -129,26 +134,41 @@ __device__ __forceinline__ void build_activations(const GemvParams &p, int ntb, 
   // Only the slots that hold data are built: the B columns of empty slots feed
   // mma output columns that are never stored, so their contents do not matter.
   const long long total = (long long)p.slots * c8n;   // multiple of 32: whole warps iterate together
-  for (long long idx = first; idx < total; idx += stride) {
-    const int slot = (int)(idx / c8n), c8 = (int)(idx - (long long)slot * c8n);
-    const int kk = c8 * 8;
-    uint32_t w[4];
-    load8(p, slot, kk, w);
-    float part = 0.f;
+  // Four chunks' loads are issued before any is used, so a thread pays one
+  // memory round trip per four chunks instead of one per chunk.
+  constexpr int kBatch = 4;
+  for (long long base0 = first; base0 < total; base0 += stride * kBatch) {
+    uint32_t w[kBatch][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      part += bf16_to_f32(w[i] & 0xFFFFu);
-      part += bf16_to_f32(w[i] >> 16);
+    for (int b = 0; b < kBatch; ++b) {
+      const long long idx = base0 + b * stride;
+      if (idx < total) {
+        const int slot = (int)(idx / c8n), c8 = (int)(idx - (long long)slot * c8n);
+        load8(p, slot, c8 * 8, w[b]);
+      }
     }
-    const int s = kk >> 4, j = (kk >> 3) & 1, tb = slot >> 3, g = slot & 7;
-    const size_t base = ((size_t)tb * k64 + (s >> 2)) * 32 * 8 + (s & 3) * 2 + j;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) xf[base + (size_t)(g * 4 + q) * 8] = w[q];
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    if ((c8 & 3) == 0) {
-      const int grp = c8 >> 2, kbi = grp >> 3, gi = grp & 7;
-      gs[((((size_t)tb * p.kb + kbi) * 4 + (g >> 1)) * 8 + gi) * 2 + (g & 1)] = part;
+    for (int b = 0; b < kBatch; ++b) {
+      const long long idx = base0 + b * stride;
+      if (idx >= total) break;
+      const int slot = (int)(idx / c8n), c8 = (int)(idx - (long long)slot * c8n);
+      const int kk = c8 * 8;
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        part += bf16_to_f32(w[b][i] & 0xFFFFu);
+        part += bf16_to_f32(w[b][i] >> 16);
+      }
+      const int s = kk >> 4, j = (kk >> 3) & 1, tb = slot >> 3, g = slot & 7;
+      const size_t base = ((size_t)tb * k64 + (s >> 2)) * 32 * 8 + (s & 3) * 2 + j;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xf[base + (size_t)(g * 4 + q) * 8] = w[b][q];
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      if ((c8 & 3) == 0) {
+        const int grp = c8 >> 2, kbi = grp >> 3, gi = grp & 7;
+        gs[((((size_t)tb * p.kb + kbi) * 4 + (g >> 1)) * 8 + gi) * 2 + (g & 1)] = part;
+      }
     }
   }
 }
@@ -167,12 +187,20 @@ struct Acc {
   float v[NTB][4];
 };
 
-__device__ __forceinline__ long long range_start(long long w, long long units, long long warps) {
-  return w * units / warps;
+template <int NTB>
+__device__ __forceinline__ void acc_zero(Acc<NTB> &a) {
+#pragma unroll
+  for (int tb = 0; tb < NTB; ++tb) a.v[tb][0] = a.v[tb][1] = a.v[tb][2] = a.v[tb][3] = 0.f;
 }
-// Warp whose range contains unit u (ranges are floor(w*U/W), all non-empty).
-__device__ __forceinline__ long long warp_of_unit(long long u, long long units, long long warps) {
-  return ((u + 1) * warps + units - 1) / units - 1;
+
+// Balanced split of ``units`` over ``parts``: part i owns [i*U/P, (i+1)*U/P).
+// 32-bit arithmetic; the host guarantees units * parts < 2^32.
+__device__ __forceinline__ uint32_t split_start(uint32_t i, uint32_t units, uint32_t parts) {
+  return i * units / parts;
+}
+// The part whose range contains unit u (all ranges non-empty: parts <= units).
+__device__ __forceinline__ uint32_t split_owner(uint32_t u, uint32_t units, uint32_t parts) {
+  return ((u + 1) * parts + units - 1) / units - 1;
 }
 
 template <int NTB, bool STAGED>
@@ -190,8 +218,8 @@ __device__ __forceinline__ void compute_unit(const uint8_t *unit, const uint32_t
     float4 gsv[NTB];
 #pragma unroll
     for (int tb = 0; tb < NTB; ++tb) {
-      const uint4 *xv = reinterpret_cast<const uint4 *>(xf + (((size_t)tb * k64 + kbi * 4 + s4) * 32 + lane) * 8);
-      const float4 *gp = reinterpret_cast<const float4 *>(gs + ((((size_t)tb * p.kb + kbi) * 4 + q) * 8 + 2 * s4) * 2);
+      const uint4 *xv = reinterpret_cast<const uint4 *>(xf + ((tb * k64 + kbi * 4 + s4) * 32 + lane) * 8);
+      const float4 *gp = reinterpret_cast<const float4 *>(gs + (((tb * p.kb + kbi) * 4 + q) * 8 + 2 * s4) * 2);
       if (STAGED) {
         xa[tb] = xv[0];
         xb[tb] = xv[1];
@@ -242,7 +270,7 @@ __device__ __forceinline__ void compute_unit(const uint8_t *unit, const uint32_t
 }
 
 template <int NTB, int EPI>
-__device__ __forceinline__ void finalize_tile(const GemvParams &p, long long tile, int lane, const Acc<NTB> &a) {
+__device__ __forceinline__ void finalize_tile(const GemvParams &p, uint32_t tile, int lane, const Acc<NTB> &a) {
   const int g = lane >> 2, q = lane & 3;
   const int r0 = (int)tile * kUnitRows + g, r1 = r0 + 8;
 #pragma unroll
@@ -308,46 +336,51 @@ __device__ __forceinline__ void finalize_tile(const GemvParams &p, long long til
   }
 }
 
-template <int NTB, int EPI>
-__device__ void flush_tile(const GemvParams &p, long long tile, long long ub, long long ue, long long gw,
-                           long long units, int lane, const Acc<NTB> &acc) {
-  const long long first = tile * p.kb, last = first + p.kb - 1;
-  if (first >= ub && last < ue) {
-    finalize_tile<NTB, EPI>(p, tile, lane, acc);
-    return;
+template <int NTB>
+__device__ __forceinline__ void acc_add(Acc<NTB> &s, const float4 (&v)[NTB]) {
+#pragma unroll
+  for (int tb = 0; tb < NTB; ++tb) {
+    s.v[tb][0] += v[tb].x;
+    s.v[tb][1] += v[tb].y;
+    s.v[tb][2] += v[tb].z;
+    s.v[tb][3] += v[tb].w;
   }
-  const long long W = p.active_warps;
-  const int slot = (tile == ub / p.kb) ? 0 : 1;
+}
+
+// Global stream-K split tile: store this warp's partial; the last of the
+// tile's warps to arrive (per-tile counter) sums all partials in warp order.
+template <int NTB, int EPI>
+__device__ void flush_split_global(const GemvParams &p, uint32_t tile, int slot, uint32_t gw, uint32_t units,
+                                   int lane, const Acc<NTB> &acc) {
+  const uint32_t W = (uint32_t)p.active_warps;
   float4 *part = reinterpret_cast<float4 *>(p.partials);
 #pragma unroll
   for (int tb = 0; tb < NTB; ++tb)
     part[((gw * 2 + slot) * 2 + tb) * 32 + lane] = make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3]);
   __threadfence();
   __syncwarp();
-  const long long w_first = warp_of_unit(first, units, W), w_last = warp_of_unit(last, units, W);
+  const uint32_t first = tile * p.kb, last = first + p.kb - 1;
+  const uint32_t w_first = split_owner(first, units, W), w_last = split_owner(last, units, W);
   int is_last = 0;
   if (lane == 0) {
-    const int pieces = (int)(w_last - w_first + 1);
     const int old = atomicAdd(p.counters + tile, 1);
-    is_last = (old == pieces - 1);
+    is_last = (old == (int)(w_last - w_first));
     if (is_last) atomicExch(p.counters + tile, 0);
   }
   is_last = __shfl_sync(0xffffffffu, is_last, 0);
   if (!is_last) return;
   __threadfence();
   Acc<NTB> sum;
-#pragma unroll
-  for (int tb = 0; tb < NTB; ++tb) sum.v[tb][0] = sum.v[tb][1] = sum.v[tb][2] = sum.v[tb][3] = 0.f;
-  // Issue up to 8 pieces' loads before summing them (one L2 round trip per
-  // batch), then add in warp order -- the same order for every launch.
-  constexpr int kBatch = 8;
-  for (long long w0 = w_first; w0 <= w_last; w0 += kBatch) {
+  acc_zero(sum);
+  // Up to 8/NTB pieces' loads in flight before they are added, in warp order.
+  constexpr int kBatch = 8 / NTB;
+  for (uint32_t w0 = w_first; w0 <= w_last; w0 += kBatch) {
     float4 v[kBatch][NTB];
 #pragma unroll
     for (int i = 0; i < kBatch; ++i) {
-      const long long w2 = w0 + i;
+      const uint32_t w2 = w0 + i;
       if (w2 > w_last) break;
-      const int s2 = (tile == range_start(w2, units, W) / p.kb) ? 0 : 1;
+      const int s2 = (tile == split_start(w2, units, W) / p.kb) ? 0 : 1;
 #pragma unroll
       for (int tb = 0; tb < NTB; ++tb)
         v[i][tb] = w2 == gw ? make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3])
@@ -356,42 +389,62 @@ __device__ void flush_tile(const GemvParams &p, long long tile, long long ub, lo
 #pragma unroll
     for (int i = 0; i < kBatch; ++i) {
       if (w0 + i > w_last) break;
-#pragma unroll
-      for (int tb = 0; tb < NTB; ++tb) {
-        sum.v[tb][0] += v[i][tb].x;
-        sum.v[tb][1] += v[i][tb].y;
-        sum.v[tb][2] += v[i][tb].z;
-        sum.v[tb][3] += v[i][tb].w;
-      }
+      acc_add(sum, v[i]);
     }
   }
   finalize_tile<NTB, EPI>(p, tile, lane, sum);
 }
 
-template <int NTB>
-constexpr int gemv_min_blocks() { return NTB == 1 ? 2 : 1; }
+
+// Partitions (chosen on the host from the shape and SM count only):
+//   kPartTiles:   CTA c owns whole row tiles [c*NT/G, (c+1)*NT/G); its warps
+//                 split that unit range evenly; a tile shared by several warps
+//                 is reduced in shared memory after a CTA barrier.
+//   kPartStreamK: warps split all units evenly across the grid; tiles shared
+//                 by several warps are reduced through global partials.
+enum GemvPartition : int { kPartTiles = 0, kPartStreamK = 1 };
 
 template <int NTB, int EPI, bool STAGED>
-__global__ void __launch_bounds__(kGemvThreads, gemv_min_blocks<NTB>()) gemv_kernel(GemvParams p) {
+__global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long gw = (long long)blockIdx.x * kGemvWarps + warp;
-  const bool active = gw < p.active_warps;
-  const long long units = (long long)p.n_tiles * p.kb;
-  const long long W = p.active_warps;
-  const long long ub = active ? range_start(gw, units, W) : 0;
-  const long long ue = active ? range_start(gw + 1, units, W) : 0;
-  const int n = (int)(ue - ub);
+  const uint32_t kb = (uint32_t)p.kb;
   const int k = p.kb * kUnitK;
 
+  // ---- this warp's unit range
+  uint32_t ub = 0, ue = 0, cta_u0 = 0, cta_units = 0, cta_warps = 0;
+  const uint32_t units = (uint32_t)p.n_tiles * kb;
+  const int nw = blockDim.x >> 5;              // 8 or 16 warps
+  const uint32_t gw = blockIdx.x * nw + warp;
+  if (p.mode == kPartTiles) {
+    const uint32_t t0 = blockIdx.x * (uint32_t)p.n_tiles / gridDim.x;
+    const uint32_t t1 = (blockIdx.x + 1) * (uint32_t)p.n_tiles / gridDim.x;
+    cta_u0 = t0 * kb;
+    cta_units = (t1 - t0) * kb;
+    cta_warps = cta_units < (uint32_t)nw ? cta_units : (uint32_t)nw;
+    if ((uint32_t)warp < cta_warps) {
+      ub = cta_u0 + split_start(warp, cta_units, cta_warps);
+      ue = cta_u0 + split_start(warp + 1, cta_units, cta_warps);
+    }
+  } else if (gw < (uint32_t)p.active_warps) {
+    ub = split_start(gw, units, p.active_warps);
+    ue = split_start(gw + 1, units, p.active_warps);
+  }
+  const int n = (int)(ue - ub);
+
+  // ---- shared memory: weight rings | activations | group sums | tile partials | barriers
   const int S = p.stages;
   uint8_t *ring = smem + warp * S * kUnitBytes;
   const uint32_t ring_s = smem_addr(ring);
-  uint8_t *after_ring = smem + kGemvWarps * S * kUnitBytes;
-  uint32_t *xs = reinterpret_cast<uint32_t *>(after_ring);
-  float *gs = reinterpret_cast<float *>(after_ring + (STAGED ? xfrag_bytes(NTB, k) : 0));
-  uint8_t *bars = after_ring + (STAGED ? xfrag_bytes(NTB, k) + gsum_bytes(NTB, k) : 0);
-  const uint32_t bar0 = smem_addr(bars) + warp * S * 8;
+  uint8_t *cur_p = smem + nw * S * kUnitBytes;
+  uint32_t *xs = reinterpret_cast<uint32_t *>(cur_p);
+  if (STAGED) cur_p += xfrag_bytes(NTB, k);
+  float *gs = reinterpret_cast<float *>(cur_p);
+  if (STAGED) cur_p += gsum_bytes(NTB, k);
+  float4 *tile_part = reinterpret_cast<float4 *>(cur_p);   // [warp][slot][tb][lane]
+  cur_p += (size_t)nw * 2 * 2 * 32 * sizeof(float4);
+  const uint32_t bar0 = smem_addr(cur_p) + warp * S * 8;
+
   const uint64_t pol = policy_evict_first();
   if (lane == 0 && n > 0) {
     for (int s = 0; s < S; ++s) mbar_init(bar0 + 8 * s, 1);
@@ -409,46 +462,80 @@ __global__ void __launch_bounds__(kGemvThreads, gemv_min_blocks<NTB>()) gemv_ker
     build_activations<true>(p, NTB, xs, gs, threadIdx.x, blockDim.x);
     __syncthreads();
   }
-  if (n == 0) return;
   const uint32_t *xf = STAGED ? xs : p.xfrag;
   const float *gsp = STAGED ? gs : p.gsum;
 
-  Acc<NTB> acc;
+  bool timed_out = false;
+  if (n > 0) {
+    Acc<NTB> acc;
+    acc_zero(acc);
+    uint32_t tile = ub / kb, kbi = ub - tile * kb;
+    uint32_t seg_k0 = kbi;     // first k-block of the current tile segment
+    int seg = 0;               // 0 = the warp's first tile segment
+    for (int j = 0; j < n; ++j) {
+      const int slot = j % S;
+      if (!mbar_wait_bounded(bar0 + 8 * slot, (uint32_t)((j / S) & 1))) {
+        if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+        // Let the copies already issued land before the CTA's shared memory goes away.
+        for (int j2 = j + 1; j2 < n && j2 < j + S; ++j2)
+          mbar_wait_bounded(bar0 + 8 * (j2 % S), (uint32_t)((j2 / S) & 1));
+        timed_out = true;
+        break;
+      }
+      compute_unit<NTB, STAGED>(ring + slot * kUnitBytes, xf, gsp, p, (int)kbi, lane, acc);
+      __syncwarp();
+      if (lane == 0 && j + S < n) {
+        mbar_arrive_expect_tx(bar0 + 8 * slot, kUnitBytes);
+        bulk_copy_g2s(ring_s + slot * kUnitBytes, p.tiles + (size_t)(ub + j + S) * kUnitBytes, kUnitBytes,
+                      bar0 + 8 * slot, pol);
+      }
+      const bool tile_end = kbi + 1 == kb;
+      if (tile_end || j + 1 == n) {
+        if (seg_k0 == 0 && tile_end) {
+          finalize_tile<NTB, EPI>(p, tile, lane, acc);
+        } else if (p.mode == kPartTiles) {
 #pragma unroll
-  for (int tb = 0; tb < NTB; ++tb) acc.v[tb][0] = acc.v[tb][1] = acc.v[tb][2] = acc.v[tb][3] = 0.f;
-  long long cur = ub / p.kb;
-  for (int j = 0; j < n; ++j) {
-    const long long u = ub + j;
-    const long long tile = u / p.kb;
-    const int kbi = (int)(u - tile * p.kb);
-    if (tile != cur) {
-      flush_tile<NTB, EPI>(p, cur, ub, ue, gw, units, lane, acc);
-#pragma unroll
-      for (int tb = 0; tb < NTB; ++tb) acc.v[tb][0] = acc.v[tb][1] = acc.v[tb][2] = acc.v[tb][3] = 0.f;
-      cur = tile;
-    }
-    const int slot = j % S;
-    if (!mbar_wait_bounded(bar0 + 8 * slot, (uint32_t)((j / S) & 1))) {
-      if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
-      // Let the copies already issued land before the CTA's shared memory goes away.
-      for (int j2 = j + 1; j2 < n && j2 < j + S; ++j2)
-        mbar_wait_bounded(bar0 + 8 * (j2 % S), (uint32_t)((j2 / S) & 1));
-      return;
-    }
-    compute_unit<NTB, STAGED>(ring + slot * kUnitBytes, xf, gsp, p, kbi, lane, acc);
-    __syncwarp();
-    if (lane == 0 && j + S < n) {
-      mbar_arrive_expect_tx(bar0 + 8 * slot, kUnitBytes);
-      bulk_copy_g2s(ring_s + slot * kUnitBytes, p.tiles + (size_t)(u + S) * kUnitBytes, kUnitBytes,
-                    bar0 + 8 * slot, pol);
+          for (int tb = 0; tb < NTB; ++tb)
+            tile_part[((warp * 2 + (seg ? 1 : 0)) * 2 + tb) * 32 + lane] =
+                make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3]);
+        } else {
+          flush_split_global<NTB, EPI>(p, tile, seg ? 1 : 0, gw, units, lane, acc);
+        }
+        acc_zero(acc);
+        ++tile;
+        kbi = 0;
+        seg_k0 = 0;
+        seg = 1;
+      } else {
+        ++kbi;
+      }
     }
   }
-  flush_tile<NTB, EPI>(p, cur, ub, ue, gw, units, lane, acc);
+  if (p.mode != kPartTiles) return;
+  // Tiles shared by warps of this CTA: the warp holding a tile's first unit
+  // sums the pieces in warp order once every warp has stored its partial.
+  __syncthreads();
+  if (n == 0 || timed_out) return;
+  const uint32_t tl = (ue - 1) / kb;                  // the warp's last tile
+  const uint32_t tl_first = tl * kb, tl_last = tl_first + kb - 1;
+  if (tl_first < ub || tl_last < ue) return;          // not the tile's first owner, or not split
+  const uint32_t w_last = split_owner(tl_last - cta_u0, cta_units, cta_warps);
+  Acc<NTB> sum;
+  acc_zero(sum);
+  for (uint32_t w2 = (uint32_t)warp; w2 <= w_last; ++w2) {
+    const int s2 = (w2 == (uint32_t)warp && tl != ub / kb) ? 1 : 0;
+    float4 v[NTB];
+#pragma unroll
+    for (int tb = 0; tb < NTB; ++tb) v[tb] = tile_part[((w2 * 2 + s2) * 2 + tb) * 32 + lane];
+    acc_add(sum, v);
+  }
+  finalize_tile<NTB, EPI>(p, tl, lane, sum);
 }
 
 // ------------------------------------------------------------------ host --
-static size_t gemv_smem_bytes(int ntb, int k, bool staged, int stages) {
-  size_t b = (size_t)kGemvWarps * stages * (kUnitBytes + 8);
+static size_t gemv_smem_bytes(int ntb, int k, bool staged, int stages, int nw) {
+  size_t b = (size_t)nw * stages * (kUnitBytes + 8);
+  b += (size_t)nw * 2 * 2 * 32 * 16;   // per-warp tile partials (CTA-tile partition)
   if (staged) b += xfrag_bytes(ntb, k) + gsum_bytes(ntb, k);
   return b;
 }
@@ -457,9 +544,9 @@ static size_t gemv_smem_bytes(int ntb, int k, bool staged, int stages) {
 // (everything requested at once), bounded by shared memory for large ones.
 // Small rings keep the footprint low so consecutive launches can co-reside
 // on an SM under programmatic dependent launch.
-static int gemv_stages(int ntb, int k, bool staged, long long units_per_warp) {
+static int gemv_stages(int ntb, int k, bool staged, long long units_per_warp, int nw) {
   int s = (int)(units_per_warp < 2 ? 2 : (units_per_warp > kGemvMaxStages ? kGemvMaxStages : units_per_warp));
-  while (s > 2 && gemv_smem_bytes(ntb, k, staged, s) > (size_t)kGemvSmemLimit) --s;
+  while (s > 2 && gemv_smem_bytes(ntb, k, staged, s, nw) > (size_t)kGemvSmemLimit) --s;
   return s;
 }
 
@@ -490,8 +577,8 @@ static cudaError_t launch_main(const GemvParams &p, int grid, cudaStream_t s) {
     configured[dev] = true;
   }
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kGemvThreads),
-                                      gemv_smem_bytes(NTB, p.kb * kUnitK, STAGED, p.stages),
+  cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(p.warps * 32),
+                                      gemv_smem_bytes(NTB, p.kb * kUnitK, STAGED, p.stages, p.warps),
                                       s, attr);
   return cudaLaunchKernelEx(&cfg, gemv_kernel<NTB, EPI, STAGED>, p);
 }
@@ -508,18 +595,52 @@ static cudaError_t launch_epi(const GemvParams &p, int epi, int grid, cudaStream
 
 // Grid of the persistent kernel for a given unit count: a function of the
 // matrix shape and SM count only (never of T), so results are batch-invariant.
-void gemv_geometry(const rc_ctx *ctx, long long units, int *grid, int *active_warps) {
-  long long g = (units + kGemvWarps - 1) / kGemvWarps;
-  if (g > ctx->sm_count) g = ctx->sm_count;
-  if (g < 1) g = 1;
-  long long w = g * kGemvWarps;
-  if (w > units) w = units;
-  *grid = (int)g;
-  *active_warps = (int)w;
+//
+// Whole-tile CTA ranges are used when they balance the SMs within 25% (their
+// split tiles reduce in shared memory); otherwise -- few tall tiles -- all
+// units are split evenly over the grid's warps (global stream-K).
+struct GemvGeometry {
+  int mode, grid, warps, active_warps;
+  long long units_per_warp;
+};
+
+// Large matrices (>= 16 units per warp at 8 warps per SM) run one CTA of 16
+// warps per SM, sharing one copy of the staged activations: latency hiding
+// limits their stream.  Smaller ones run 8-warp CTAs, which leaves room for
+// the next launch's CTA to co-reside under programmatic dependent launch.
+GemvGeometry gemv_geometry(const rc_ctx *ctx, int n_tiles, int kb, int max_warps) {
+  GemvGeometry g{};
+  const long long units = (long long)n_tiles * kb;
+  const long long sm = ctx->sm_count;
+  const int nw = (units >= 16ll * kGemvWarps * sm && max_warps >= kGemvMaxWarps) ? kGemvMaxWarps : kGemvWarps;
+  g.warps = nw;
+  const long long gt = n_tiles < sm ? n_tiles : sm;
+  const long long tiles_per_cta = (n_tiles + gt - 1) / gt;
+  const bool balanced = tiles_per_cta * gt * 4 <= (long long)n_tiles * 5;
+  const bool fits32 = units * (long long)(sm * nw) < (1ll << 32);
+  if (balanced || !fits32) {
+    g.mode = kPartTiles;
+    g.grid = (int)gt;
+    g.active_warps = (int)(gt * nw);
+    const long long cta_units = tiles_per_cta * kb;
+    g.units_per_warp = (cta_units + nw - 1) / nw;
+  } else {
+    long long gr = (units + nw - 1) / nw;
+    if (gr > sm) gr = sm;
+    long long w = gr * nw;
+    if (w > units) w = units;
+    g.mode = kPartStreamK;
+    g.grid = (int)gr;
+    g.active_warps = (int)w;
+    g.units_per_warp = (units + w - 1) / w;
+  }
+  return g;
 }
 
-// Token slots one launch can stage for K columns (16 when they fit in shared memory).
-bool gemv_can_stage(int ntb, int k) { return gemv_smem_bytes(ntb, k, true, 2) <= (size_t)kGemvSmemLimit; }
+// Whether ntb token blocks of K columns fit in shared memory next to the rings of nw warps.
+static bool gemv_can_stage(int ntb, int k, int nw) {
+  return gemv_smem_bytes(ntb, k, true, 2, nw) <= (size_t)kGemvSmemLimit;
+}
 
 // One launch over <= 16 bf16 token rows (<= 8 f32 rows).
 int gemv_launch(rc_ctx *ctx, const uint8_t *tiles, int n_tiles, int k, const void *x, int x_dtype, int ldx,
@@ -527,7 +648,12 @@ int gemv_launch(rc_ctx *ctx, const uint8_t *tiles, int n_tiles, int k, const voi
                 cudaStream_t s) {
   const int slots = x_dtype == RC_DTYPE_F32 ? 2 * tokens : tokens;
   const int ntb = slots > 8 ? 2 : 1;
-  const bool staged = gemv_can_stage(ntb, k);
+  // The geometry must not depend on T (batch invariance): 16-warp CTAs only
+  // where even two token blocks can be staged next to their rings.  Staging
+  // itself may still fall back to global scratch; that changes no arithmetic.
+  const GemvGeometry geo =
+      gemv_geometry(ctx, n_tiles, k / kUnitK, gemv_can_stage(2, k, kGemvMaxWarps) ? kGemvMaxWarps : kGemvWarps);
+  const bool staged = gemv_can_stage(ntb, k, geo.warps);
   int rc = ensure_gemv_scratch(ctx, staged ? 0 : k, n_tiles);
   if (rc) return rc;
   GemvParams p{};
@@ -567,10 +693,11 @@ int gemv_launch(rc_ctx *ctx, const uint8_t *tiles, int n_tiles, int k, const voi
       return RC_ERR_CUDA;
     }
   }
-  int grid = 0;
-  gemv_geometry(ctx, (long long)n_tiles * p.kb, &grid, &p.active_warps);
-  const long long units = (long long)n_tiles * p.kb;
-  p.stages = gemv_stages(ntb, k, staged, (units + p.active_warps - 1) / p.active_warps);
+  const int grid = geo.grid;
+  p.mode = geo.mode;
+  p.warps = geo.warps;
+  p.active_warps = geo.active_warps;
+  p.stages = gemv_stages(ntb, k, staged, geo.units_per_warp, geo.warps);
   if (staged)
     e = ntb == 2 ? launch_epi<2, true>(p, epi, grid, s) : launch_epi<1, true>(p, epi, grid, s);
   else

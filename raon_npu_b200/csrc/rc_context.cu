@@ -130,7 +130,7 @@ int rc_init(int device, rc_ctx **out) {
   if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&ctx->qflag, sizeof(int));
   if (e == cudaSuccess) {
-    size_t warps = (size_t)ctx->sm_count * kGemvWarps;
+    size_t warps = (size_t)ctx->sm_count * kGemvMaxWarps;   // stream-K partials: one slot pair per warp
     e = cudaMalloc(&ctx->partials, warps * 2 * 2 * 32 * 4 * sizeof(float));
   }
   if (e != cudaSuccess) {

@@ -39,9 +39,9 @@ constexpr int kRefBlockBytes = 5120;
 constexpr int kRefParamBytes = 1024;
 
 // GEMV persistent kernel geometry.
-constexpr int kGemvWarps = 8;         // consumer warps per CTA, each with a private ring
+constexpr int kGemvWarps = 8;         // warps per CTA for small matrices (each with a private ring)
+constexpr int kGemvMaxWarps = 16;     // warps per CTA for large matrices (one CTA per SM)
 constexpr int kGemvMaxStages = 12;    // ring depth (units in flight) per warp; chosen per launch
-constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kGemvSmemLimit = 227 * 1024;   // opt-in dynamic shared memory per CTA on sm_100
 constexpr int kMaxTokensPerLaunch = 16;   // two 8-token mma column blocks
 // Activation scratch rotates over this many slots: consecutive launches chained
