@@ -253,8 +253,8 @@ __device__ __forceinline__ void compute_unit(const uint8_t *unit, const uint32_t
       }
       const uint32_t lo = half ? sm.z : sm.x;   // {scale[g], min[g]}
       const uint32_t hi = half ? sm.w : sm.y;   // {scale[g+8], min[g+8]}
-      const float sc0 = bf16_to_f32(lo & 0xFFFFu), mn0 = bf16_to_f32(lo >> 16);
-      const float sc1 = bf16_to_f32(hi & 0xFFFFu), mn1 = bf16_to_f32(hi >> 16);
+      const float sc0 = bf16_lo_f32(lo), mn0 = bf16_hi_f32(lo);
+      const float sc1 = bf16_lo_f32(hi), mn1 = bf16_hi_f32(hi);
       const float mp0 = fmaf(-128.f, sc0, mn0), mp1 = fmaf(-128.f, sc1, mn1);
 #pragma unroll
       for (int tb = 0; tb < NTB; ++tb) {
@@ -472,13 +472,18 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(GemvParams 
     uint32_t tile = ub / kb, kbi = ub - tile * kb;
     uint32_t seg_k0 = kbi;     // first k-block of the current tile segment
     int seg = 0;               // 0 = the warp's first tile segment
+    int slot = 0;
+    uint32_t phase = 0;        // parity of the ring slot's current fill
     for (int j = 0; j < n; ++j) {
-      const int slot = j % S;
-      if (!mbar_wait_bounded(bar0 + 8 * slot, (uint32_t)((j / S) & 1))) {
+      if (!mbar_wait_bounded(bar0 + 8 * slot, phase)) {
         if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
         // Let the copies already issued land before the CTA's shared memory goes away.
-        for (int j2 = j + 1; j2 < n && j2 < j + S; ++j2)
-          mbar_wait_bounded(bar0 + 8 * (j2 % S), (uint32_t)((j2 / S) & 1));
+        int s2 = slot;
+        uint32_t ph2 = phase;
+        for (int j2 = j + 1; j2 < n && j2 < j + S; ++j2) {
+          if (++s2 == S) s2 = 0, ph2 ^= 1u;
+          mbar_wait_bounded(bar0 + 8 * s2, ph2);
+        }
         timed_out = true;
         break;
       }
@@ -489,6 +494,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(GemvParams 
         bulk_copy_g2s(ring_s + slot * kUnitBytes, p.tiles + (size_t)(ub + j + S) * kUnitBytes, kUnitBytes,
                       bar0 + 8 * slot, pol);
       }
+      if (++slot == S) slot = 0, phase ^= 1u;
       const bool tile_end = kbi + 1 == kb;
       if (tile_end || j + 1 == n) {
         if (seg_k0 == 0 && tile_end) {

@@ -111,6 +111,10 @@ __device__ __forceinline__ uint32_t codes_to_bf16x2(uint32_t w) {
   return ((w >> (4 * J)) & 0x000F000Fu) | 0x43004300u;
 }
 
+// {lo16, hi16} bf16 pair -> f32 values.
+__device__ __forceinline__ float bf16_lo_f32(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi_f32(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
 // --------------------------------------------------------------- GLU acts --
 // SiLU-GLU with the overflow-free sigmoid (kernels/moe/reference.py:160-170).
 __device__ __forceinline__ float act_swiglu(float g, float u) {
