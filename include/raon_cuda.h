@@ -117,6 +117,34 @@ int rc_gemv(rc_ctx *ctx, const rc_weight *w, const void *x_dev, int x_dtype, int
 int rc_gemv_host(rc_ctx *ctx, const rc_weight *w, const void *x_host, int x_dtype, int T,
                  void *y_host, const float *bias_dev);
 
+/* rc_gemv without any device allocation (this entry point has no counterpart
+ * in the reference).  Arguments and results are those of rc_gemv; the context
+ * is the one the weight was uploaded with.
+ *
+ * Who needs it: callers that must not allocate device memory while they run
+ * a GEMV -- a latency-critical serving thread that cannot afford the implicit
+ * device-wide synchronisation cudaMalloc/cudaFree may perform, or a host that
+ * reserves a fixed device-memory budget at start-up (weights, caches) and
+ * forbids allocations afterwards.  rc_gemv may grow its scratch with
+ * cudaMalloc on first use of a larger shape; this function never calls
+ * cudaMalloc, cudaFree or anything that allocates.
+ *
+ * How: the split-K scratch (per-tile counters, per-warp partial sums) lives in
+ * one static device array of 5,308,416 bytes that every GPU which loads this
+ * library keeps until the process exits.  The first call on a device looks up
+ * that array's device address (cudaGetSymbolAddress) with the device current;
+ * make this first call before any stream capture.  Every call shares the
+ * array, which keeps the last call's contents: each call clears the counters
+ * it uses, and calls that overlap on the GPU (different streams or threads)
+ * race -- keep them ordered on one stream.
+ *
+ * Limits (RC_ERR_INVALID beyond them): nrows <= 262,144; the activations of
+ * one launch must fit in shared memory -- K <= 5,120 for up to 16 bf16 rows
+ * per call (8 f32 rows), K <= 10,240 for up to 8 bf16 rows per call. */
+int rc_gemv_noalloc(const rc_weight *w, const void *x_dev, int x_dtype, int ldx, int T,
+                    void *y_dev, int y_dtype, int ldy, int row0, int nrows,
+                    const float *bias_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,7 @@ SIGNATURES = {
     "rc_dequant_q4nx": (_I, [_P, _P, _P, _P]),
     "rc_gemv": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _I, _I, _I, _P, _P]),
     "rc_gemv_host": (_I, [_P, _P, _P, _I, _I, _P, _P]),
+    "rc_gemv_noalloc": (_I, [_P, _P, _I, _I, _I, _P, _I, _I, _I, _I, _P, _P]),
 }
 
 _lib = None

@@ -35,6 +35,8 @@
 // touches scratch, so back-to-back GEMVs overlap their HBM traffic.
 #include <string.h>
 
+#include <mutex>
+
 #include "rc_device.cuh"
 #include "rc_internal.cuh"
 
@@ -715,6 +717,88 @@ int gemv_launch(rc_ctx *ctx, const uint8_t *tiles, int n_tiles, int k, const voi
   return RC_OK;
 }
 
+// ------------------------------------------------- allocation-free variant --
+// Scratch of rc_gemv_noalloc: the per-tile arrival counters and the per-warp
+// split-K partials of the stream-K partition, in one statically sized device
+// array that every GPU loading this library holds until the process exits.
+constexpr int kNoAllocMaxTiles = 16384;               // 262,144 output rows
+constexpr int kNoAllocMaxWarps = 160 * kGemvMaxWarps; // 160 SMs x 16 warps
+constexpr size_t kNoAllocCounterBytes = (size_t)kNoAllocMaxTiles * sizeof(int);
+constexpr size_t kNoAllocPartialBytes = (size_t)kNoAllocMaxWarps * 2 * 2 * 32 * 4 * sizeof(float);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocCounterBytes + kNoAllocPartialBytes];
+
+// Device address of g_noalloc_scratch per device.  In host code the array's
+// name is only a host-side stand-in, so the address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+static std::mutex g_noalloc_mu;
+static void *g_noalloc_addr[64];
+
+static int noalloc_scratch(int device, unsigned char **out) {
+  RC_CHECK_ARG(device >= 0 && device < 64, "rc_gemv_noalloc: device %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[device]) {
+    void *ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr) {
+      set_error("rc_gemv_noalloc: cudaGetSymbolAddress of the static scratch failed on device %d: %s", device,
+                cudaGetErrorString(e));
+      return RC_ERR_CUDA;
+    }
+    g_noalloc_addr[device] = ptr;
+  }
+  *out = static_cast<unsigned char *>(g_noalloc_addr[device]);
+  return RC_OK;
+}
+
+// One launch of the GEMV kernel with its scratch in the static array: the same
+// geometry and kernel as gemv_launch, restricted to shapes whose activations
+// stage in shared memory (so no global activation scratch is needed).
+static int gemv_launch_noalloc(rc_ctx *ctx, unsigned char *scratch, const uint8_t *tiles, int n_tiles, int k,
+                               const void *x, int x_dtype, int ldx, int tokens, void *y, int ldy, const float *bias,
+                               int epi, cudaStream_t s) {
+  const int slots = x_dtype == RC_DTYPE_F32 ? 2 * tokens : tokens;
+  const int ntb = slots > 8 ? 2 : 1;
+  const GemvGeometry geo =
+      gemv_geometry(ctx, n_tiles, k / kUnitK, gemv_can_stage(2, k, kGemvMaxWarps) ? kGemvMaxWarps : kGemvWarps);
+  RC_CHECK_ARG(gemv_can_stage(ntb, k, geo.warps),
+               "rc_gemv_noalloc: K=%d with %d token rows per launch does not fit in shared memory "
+               "(use fewer rows per call, or rc_gemv)", k, tokens);
+  RC_CHECK_ARG(geo.mode == kPartTiles || geo.active_warps <= kNoAllocMaxWarps,
+               "rc_gemv_noalloc: %d warps exceed the static scratch (%d)", geo.active_warps, kNoAllocMaxWarps);
+  int *counters = reinterpret_cast<int *>(scratch);
+  // Every call shares the array and it keeps the last call's contents; the
+  // counters must start at zero (a call that gave up a wait can leave them set).
+  RC_CUDA_TRY(cudaMemsetAsync(counters, 0, (size_t)n_tiles * sizeof(int), s));
+  GemvParams p{};
+  p.tiles = tiles;
+  p.n_tiles = n_tiles;
+  p.kb = k / kUnitK;
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.ldx = ldx;
+  p.tokens = tokens;
+  p.slots = slots;
+  const size_t esz = x_dtype == RC_DTYPE_F32 ? 4 : 2;
+  p.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && ((size_t)ldx * esz) % 16 == 0) ? 1 : 0;
+  p.y = y;
+  p.ldy = ldy;
+  p.bias = bias;
+  p.partials = reinterpret_cast<float *>(scratch + kNoAllocCounterBytes);
+  p.counters = counters;
+  p.err = ctx->err;
+  p.mode = geo.mode;
+  p.warps = geo.warps;
+  p.active_warps = geo.active_warps;
+  p.stages = gemv_stages(ntb, k, true, geo.units_per_warp, geo.warps);
+  const cudaError_t e =
+      ntb == 2 ? launch_epi<2, true>(p, epi, geo.grid, s) : launch_epi<1, true>(p, epi, geo.grid, s);
+  if (e != cudaSuccess) {
+    set_error("rc_gemv_noalloc launch: %s", cudaGetErrorString(e));
+    return RC_ERR_CUDA;
+  }
+  return RC_OK;
+}
+
 }  // namespace rc
 
 using namespace rc;
@@ -779,6 +863,47 @@ int rc_gemv_host(rc_ctx *ctx, const rc_weight *w, const void *x_host, int x_dtyp
   rc = check_error_word(ctx);
   if (rc) return rc;
   memcpy(y_host, ctx->pin_y, yb);
+  return RC_OK;
+}
+
+int rc_gemv_noalloc(const rc_weight *w, const void *x_dev, int x_dtype, int ldx, int T, void *y_dev, int y_dtype,
+                    int ldy, int row0, int nrows, const float *bias_dev, void *stream) {
+  RC_CHECK_ARG(x_dev && y_dev, "rc_gemv_noalloc: NULL argument");
+  if (!w) {
+    set_error("rc_gemv_noalloc: unknown weight handle");
+    return RC_ERR_NOT_FOUND;
+  }
+  rc_ctx *ctx = w->ctx;
+  RC_CHECK_ARG(!(w->flags & RC_UPLOAD_GATE_UP), "rc_gemv_noalloc: a gate/up-interleaved matrix is only usable by the MoE path");
+  RC_CHECK_ARG(x_dtype == RC_DTYPE_BF16 || x_dtype == RC_DTYPE_F32, "rc_gemv_noalloc: x_dtype must be BF16 or F32");
+  RC_CHECK_ARG(y_dtype == RC_DTYPE_F32 || (y_dtype == RC_DTYPE_BF16 && x_dtype == RC_DTYPE_BF16),
+               "rc_gemv_noalloc: y_dtype must be F32, or BF16 with BF16 activations");
+  RC_CHECK_ARG(T >= 1, "rc_gemv_noalloc: T must be >= 1 (got %d)", T);
+  RC_CHECK_ARG(row0 >= 0 && nrows > 0 && row0 % kUnitRows == 0 && nrows % kUnitRows == 0 && row0 + nrows <= w->n,
+               "rc_gemv_noalloc: rows [%d, %d) must be 16-aligned inside [0, %d)", row0, row0 + nrows, w->n);
+  RC_CHECK_ARG(nrows / kUnitRows <= kNoAllocMaxTiles,
+               "rc_gemv_noalloc: %d rows exceed the static scratch limit of %d rows", nrows,
+               kNoAllocMaxTiles * kUnitRows);
+  RC_CHECK_ARG(ldx >= w->k, "rc_gemv_noalloc: ldx (%d) < K (%d)", ldx, w->k);
+  RC_CHECK_ARG(ldy >= nrows, "rc_gemv_noalloc: ldy (%d) < nrows (%d)", ldy, nrows);
+  RC_CUDA_TRY(cudaSetDevice(ctx->device));
+  unsigned char *scratch = nullptr;
+  int rc = noalloc_scratch(ctx->device, &scratch);
+  if (rc) return rc;
+  const cudaStream_t s = pick_stream(ctx, stream);
+  const int per = x_dtype == RC_DTYPE_F32 ? kMaxTokensPerLaunch / 2 : kMaxTokensPerLaunch;
+  const size_t xe = x_dtype == RC_DTYPE_F32 ? 4 : 2;
+  const size_t ye = y_dtype == RC_DTYPE_F32 ? 4 : 2;
+  const int epi = x_dtype == RC_DTYPE_F32 ? kEpiF32 : (y_dtype == RC_DTYPE_F32 ? kEpiF32Raw : kEpiBf16);
+  const uint8_t *tiles = w->tiles + (size_t)(row0 / kUnitRows) * (w->k / kUnitK) * kUnitBytes;
+  const float *bias = bias_dev ? bias_dev + row0 : nullptr;
+  for (int t0 = 0; t0 < T; t0 += per) {
+    const int tc = T - t0 < per ? T - t0 : per;
+    const void *xc = static_cast<const uint8_t *>(x_dev) + (size_t)t0 * ldx * xe;
+    void *yc = static_cast<uint8_t *>(y_dev) + (size_t)t0 * ldy * ye;
+    rc = gemv_launch_noalloc(ctx, scratch, tiles, nrows / kUnitRows, w->k, xc, x_dtype, ldx, tc, yc, ldy, bias, epi, s);
+    if (rc) return rc;
+  }
   return RC_OK;
 }
 

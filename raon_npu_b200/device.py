@@ -149,6 +149,21 @@ class Q4nxWeight:
             int(nrows if ldy is None else ldy), int(row0), int(nrows), ctypes.c_void_p(_ptr(bias_dev)),
             ctypes.c_void_p(_stream_for(stream, x_dev, y_dev))), "rc_gemv")
 
+    def gemv_noalloc_into(self, x_dev, y_dev, tokens: int, x_dtype: int = _lib.RC_DTYPE_BF16,
+                          ldx: int | None = None, ldy: int | None = None, row0: int = 0,
+                          nrows: int | None = None, bias_dev=None, stream: int | None = None,
+                          y_dtype: int | None = None) -> None:
+        """``gemv_into`` through ``rc_gemv_noalloc``: the same result, computed with
+        the library's static scratch instead of context-allocated scratch, for
+        callers that must not allocate device memory during the call."""
+        nrows = self.n - row0 if nrows is None else nrows
+        y_dtype = x_dtype if y_dtype is None else y_dtype
+        check(self.ctx.lib.rc_gemv_noalloc(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), int(x_dtype), int(self.k if ldx is None else ldx),
+            int(tokens), ctypes.c_void_p(_ptr(y_dev)), int(y_dtype), int(nrows if ldy is None else ldy),
+            int(row0), int(nrows), ctypes.c_void_p(_ptr(bias_dev)),
+            ctypes.c_void_p(_stream_for(stream, x_dev, y_dev))), "rc_gemv_noalloc")
+
     def gemv_host(self, x: np.ndarray, bias_dev=None) -> np.ndarray:
         """Host-buffer GEMV through ``rc_gemv_host`` (copies in, runs, copies out, waits)."""
         if x.dtype == np.uint16:
