@@ -117,6 +117,67 @@ int rc_gemv(rc_ctx *ctx, const rc_weight *w, const void *x_dev, int x_dtype, int
 int rc_gemv_host(rc_ctx *ctx, const rc_weight *w, const void *x_host, int x_dtype, int T,
                  void *y_host, const float *bias_dev);
 
+/* ------------------------------------------------------------------ MoE ---
+ * One MoE layer: n_experts routed experts (+ an optional shared expert, id
+ * n_experts), each a q4nx [gate; up] matrix [2*inter, hidden] and a down
+ * matrix [hidden, inter_pad] (inter zero-padded to a multiple of 256), both
+ * as pack_gemv bytes -- the reference's expert packers
+ * (kernels/moe/pack.py:136-224).  Expert parallelism: load only the experts a
+ * rank owns; the others are skipped and their slot outputs are zero. */
+typedef struct rc_moe rc_moe;
+
+int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_shared, rc_moe **out);
+int rc_moe_destroy(rc_moe *m);
+
+/* Upload expert ``expert`` (0..n_experts-1, or n_experts for the shared one). */
+int rc_moe_set_expert(rc_moe *m, int expert, const uint8_t *gate_up, size_t gate_up_bytes,
+                      const uint8_t *down, size_t down_bytes, unsigned flags);
+
+/* Router weights bf16 [n_experts][hidden] (host) and, for the sigmoid+bias
+ * router, the per-expert correction bias f32 [n_experts] (or NULL). */
+int rc_moe_set_router(rc_moe *m, const uint16_t *router_w, const float *bias);
+
+/* Router for T <= 16 tokens x [T][hidden] (device): top-k ids (best first,
+ * lower index wins ties) and weights, optional f32 logits [T][n_experts].
+ * Replaces the host router ``RaonModel._route_token`` (host/raon.py:1224-1247)
+ * and the softmax top-k of the north-star configs. */
+int rc_moe_route(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize,
+                 float scaling, int32_t *ids_dev, float *w_dev, float *logits_dev, void *stream);
+
+/* Routed experts of one token for caller-supplied top-k ids / weights
+ * (device arrays, any order): ``Backend.moe_experts`` (host/backend.py:98-117,
+ * numpy host/backend.py:466-510; NPU npu/backend.py:5029-5322).  Experts are
+ * summed in ascending ID in f32, then RTNE.  with_shared != 0 also adds the
+ * shared expert as ``_moe_token`` does (host/raon.py:1310-1327). */
+int rc_moe_experts(rc_moe *m, const uint16_t *x_dev, const int32_t *ids_dev, const float *w_dev, int k,
+                   int act, float gate_beta, float value_beta, int with_shared, uint16_t *out_dev,
+                   void *stream);
+
+/* rc_moe_experts on host buffers (x [hidden] bf16, ids [k] int32, w [k] f32,
+ * out [hidden] bf16): copies in, runs, copies out, waits.  Validates the ids
+ * (range, loaded) as the reference's ValueError checks do. */
+int rc_moe_experts_host(rc_moe *m, const uint16_t *x_host, const int32_t *ids_host, const float *w_host,
+                        int k, int act, float gate_beta, float value_beta, int with_shared,
+                        uint16_t *out_host);
+
+/* The whole decode layer for one token: router, routed + shared experts,
+ * combine; optional copies of the selected ids / weights. */
+int rc_moe_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int renormalize, float scaling,
+                  int act, float gate_beta, float value_beta, uint16_t *out_dev, int32_t *ids_dev,
+                  float *w_dev, void *stream);
+
+/* Expert-parallel halves of rc_moe_decode.  decode_local routes, runs the
+ * experts this rank holds and writes every slot's down output
+ * slot_out[k (+1 shared)][hidden] (zeros for experts held elsewhere) and the
+ * slot weights (ascending-ID order); after the ranks exchange their slot rows
+ * (each slot is non-zero on exactly one rank), rc_moe_combine produces the
+ * same bytes as rc_moe_decode on one GPU. */
+int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int k, int router, int renormalize, float scaling,
+                        int act, float gate_beta, float value_beta, uint16_t *slot_out_dev,
+                        float *slot_w_dev, void *stream);
+int rc_moe_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int k, int with_shared,
+                   uint16_t *out_dev, void *stream);
+
 /* rc_gemv without any device allocation (this entry point has no counterpart
  * in the reference).  Arguments and results are those of rc_gemv; the context
  * is the one the weight was uploaded with.

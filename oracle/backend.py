@@ -82,6 +82,23 @@ def moe_experts(experts, x, top_ids, top_weights, act="situ", gate_beta=4.0, val
     return f32_to_bf16(acc)
 
 
+def moe_term_magnitude(experts, x, top_ids, top_weights, act="situ", gate_beta=4.0, value_beta=25.0,
+                       shared_down_u16=None) -> np.ndarray:
+    """Per output h: sum_e |w_e * down_e[h]| (+ |shared[h]|), the magnitude of the
+    terms the f32 combine accumulates.  Each expert output is a bf16 value
+    whose last rounding step may fall either way between two implementations
+    summing in different orders, so an implementation-independent bound on an
+    MoE output is one bf16 step (2^-8 relative) of this magnitude."""
+    mag = None
+    for eid, wt in zip(top_ids, top_weights):
+        wg, wu, wd = experts[int(eid)]
+        t = np.abs(bf16_to_f32(expert_forward(wg, wu, wd, x, act, gate_beta, value_beta)).astype(np.float64) * wt)
+        mag = t if mag is None else mag + t
+    if shared_down_u16 is not None:
+        mag = mag + np.abs(bf16_to_f32(shared_down_u16).astype(np.float64))
+    return mag
+
+
 def moe_token_with_shared(routed_u16, shared_down_u16) -> np.ndarray:
     """``bf16(f32(routed) + f32(shared))`` (``host/raon.py:1321-1327``)."""
     return f32_to_bf16(bf16_to_f32(routed_u16) + bf16_to_f32(shared_down_u16))

@@ -7,6 +7,7 @@ integer addresses; torch is used only as plumbing (allocation, streams).
 from __future__ import annotations
 
 import ctypes
+import weakref
 
 import numpy as np
 
@@ -56,12 +57,19 @@ class Context:
         n = ctypes.c_int()
         check(self.lib.rc_sm_count(h, ctypes.byref(n)))
         self.sm_count = n.value
+        # Objects created on this context; they are released before it is.
+        self._children = weakref.WeakSet()
+
+    def _adopt(self, obj) -> None:
+        self._children.add(obj)
 
     def sync(self) -> None:
         check(self.lib.rc_sync(self.handle), "rc_sync")
 
     def close(self) -> None:
         if self.handle:
+            for child in list(self._children):
+                child.release()
             self.lib.rc_destroy(self.handle)
             self.handle = None
 
@@ -107,6 +115,7 @@ class Q4nxWeight:
         self.handle = h
         self.n, self.k, self.gate_up = int(n), int(k), bool(gate_up)
         self.device_bytes = n * k * 5 // 8
+        ctx._adopt(self)
 
     def set_bias(self, bias: np.ndarray) -> int:
         """Attach an f32 [n] bias; returns its device address."""
@@ -119,9 +128,11 @@ class Q4nxWeight:
         return p.value or 0
 
     def free(self) -> None:
-        if self.handle:
+        if self.handle and self.ctx.handle:
             self.ctx.lib.rc_weight_free(self.handle)
-            self.handle = None
+        self.handle = None
+
+    release = free
 
     def __del__(self):
         try:
@@ -179,3 +190,125 @@ class Q4nxWeight:
                                         int(x.shape[0]), ctypes.c_void_p(out.ctypes.data),
                                         ctypes.c_void_p(_ptr(bias_dev))), "rc_gemv_host")
         return out
+
+
+ACT_CODES = {"swiglu": _lib.RC_ACT_SWIGLU, "situ": _lib.RC_ACT_SITU}
+ROUTER_CODES = {"softmax": _lib.RC_ROUTER_SOFTMAX, "sigmoid_bias": _lib.RC_ROUTER_SIGMOID_BIAS}
+
+
+def _buf(packed):
+    """(pointer, nbytes, flags, keepalive) for host bytes/ndarray or a device tensor."""
+    if isinstance(packed, (bytes, bytearray, memoryview, np.ndarray)):
+        b = np.frombuffer(packed, np.uint8) if not isinstance(packed, np.ndarray) else \
+            np.ascontiguousarray(packed, dtype=np.uint8)
+        return b.ctypes.data, b.nbytes, 0, b
+    if getattr(packed, "is_cuda", False):
+        import torch
+        torch.cuda.current_stream(packed.device).synchronize()
+    return _ptr(packed), int(packed.numel() * packed.element_size()), _lib.RC_UPLOAD_SRC_DEVICE, packed
+
+
+class MoeLayer:
+    """One MoE layer on the device: experts (q4nx [gate; up] + down), router.
+
+    ``set_expert`` takes the reference's expert packing (pack_gemv bytes of the
+    stacked [gate; up] matrix and of the K-padded down matrix).  For expert
+    parallelism, load only the experts a rank owns.
+    """
+
+    def __init__(self, ctx: Context, hidden: int, inter: int, n_experts: int, has_shared: bool = True):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        check(ctx.lib.rc_moe_create(ctx.handle, int(hidden), int(inter), int(n_experts), int(bool(has_shared)),
+                                    ctypes.byref(h)), "rc_moe_create")
+        self.handle = h
+        self.hidden, self.inter, self.n_experts, self.has_shared = int(hidden), int(inter), int(n_experts), \
+            bool(has_shared)
+        self.inter_pad = (self.inter + 255) // 256 * 256
+        self.loaded: set[int] = set()
+        ctx._adopt(self)
+
+    def close(self) -> None:
+        if self.handle and self.ctx.handle:
+            self.ctx.lib.rc_moe_destroy(self.handle)
+        self.handle = None
+
+    release = close
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_expert(self, expert: int, gate_up_packed, down_packed) -> None:
+        gp, gn, gf, gk = _buf(gate_up_packed)
+        dp, dn, df, dk = _buf(down_packed)
+        if gf != df:
+            raise ValueError("gate_up and down must both be host or both be device buffers")
+        check(self.ctx.lib.rc_moe_set_expert(self.handle, int(expert), ctypes.c_void_p(gp), gn, ctypes.c_void_p(dp),
+                                             dn, gf), "rc_moe_set_expert")
+        del gk, dk
+        self.loaded.add(int(expert))
+
+    def set_router(self, router_w_bits: np.ndarray, bias: np.ndarray | None = None) -> None:
+        wr = np.ascontiguousarray(router_w_bits, dtype=np.uint16)
+        if wr.shape != (self.n_experts, self.hidden):
+            raise ValueError(f"router weights must be [{self.n_experts}, {self.hidden}] bf16 bits")
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        if b is not None and b.shape != (self.n_experts,):
+            raise ValueError(f"router bias must be [{self.n_experts}] f32")
+        check(self.ctx.lib.rc_moe_set_router(self.handle, ctypes.c_void_p(wr.ctypes.data),
+                                             ctypes.c_void_p(None if b is None else b.ctypes.data)),
+              "rc_moe_set_router")
+
+    def route(self, x_dev, tokens: int, k: int, ids_dev, w_dev, logits_dev=None, router: str = "softmax",
+              renormalize: bool = True, scaling: float = 1.0, stream: int | None = None) -> None:
+        check(self.ctx.lib.rc_moe_route(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), int(tokens), int(k), ROUTER_CODES[router],
+            int(bool(renormalize)), float(scaling), ctypes.c_void_p(_ptr(ids_dev)), ctypes.c_void_p(_ptr(w_dev)),
+            ctypes.c_void_p(_ptr(logits_dev)), ctypes.c_void_p(_stream_for(stream, x_dev, ids_dev))), "rc_moe_route")
+
+    def experts(self, x_dev, ids_dev, w_dev, k: int, out_dev, act: str = "situ", gate_beta: float = 4.0,
+                value_beta: float = 25.0, with_shared: bool = False, stream: int | None = None) -> None:
+        check(self.ctx.lib.rc_moe_experts(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), ctypes.c_void_p(_ptr(ids_dev)), ctypes.c_void_p(_ptr(w_dev)),
+            int(k), ACT_CODES[act], float(gate_beta), float(value_beta), int(bool(with_shared)),
+            ctypes.c_void_p(_ptr(out_dev)), ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_experts")
+
+    def experts_host(self, x: np.ndarray, ids: np.ndarray, w: np.ndarray, act: str = "situ", gate_beta: float = 4.0,
+                     value_beta: float = 25.0, with_shared: bool = False) -> np.ndarray:
+        xh = np.ascontiguousarray(x, dtype=np.uint16)
+        ih = np.ascontiguousarray(ids, dtype=np.int32)
+        wh = np.ascontiguousarray(w, dtype=np.float32)
+        out = np.empty(self.hidden, np.uint16)
+        check(self.ctx.lib.rc_moe_experts_host(
+            self.handle, ctypes.c_void_p(xh.ctypes.data), ctypes.c_void_p(ih.ctypes.data),
+            ctypes.c_void_p(wh.ctypes.data), int(ih.size), ACT_CODES[act], float(gate_beta), float(value_beta),
+            int(bool(with_shared)), ctypes.c_void_p(out.ctypes.data)), "rc_moe_experts_host")
+        return out
+
+    def decode(self, x_dev, k: int, out_dev, ids_dev=None, w_dev=None, router: str = "softmax",
+               renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
+               value_beta: float = 25.0, stream: int | None = None) -> None:
+        check(self.ctx.lib.rc_moe_decode(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), int(k), ROUTER_CODES[router], int(bool(renormalize)),
+            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(_ptr(out_dev)),
+            ctypes.c_void_p(_ptr(ids_dev)), ctypes.c_void_p(_ptr(w_dev)),
+            ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_decode")
+
+    def decode_local(self, x_dev, k: int, slot_out_dev, slot_w_dev, router: str = "softmax",
+                     renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
+                     value_beta: float = 25.0, stream: int | None = None) -> None:
+        check(self.ctx.lib.rc_moe_decode_local(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), int(k), ROUTER_CODES[router], int(bool(renormalize)),
+            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(_ptr(slot_out_dev)),
+            ctypes.c_void_p(_ptr(slot_w_dev)), ctypes.c_void_p(_stream_for(stream, x_dev, slot_out_dev))),
+            "rc_moe_decode_local")
+
+    def combine(self, slot_out_dev, slot_w_dev, k: int, out_dev, with_shared: bool = True,
+                stream: int | None = None) -> None:
+        check(self.ctx.lib.rc_moe_combine(
+            self.handle, ctypes.c_void_p(_ptr(slot_out_dev)), ctypes.c_void_p(_ptr(slot_w_dev)), int(k),
+            int(bool(with_shared)), ctypes.c_void_p(_ptr(out_dev)),
+            ctypes.c_void_p(_stream_for(stream, slot_out_dev, out_dev))), "rc_moe_combine")

@@ -1,0 +1,332 @@
+"""GPU parity of the MoE decode path (router, grouped expert GEMVs, combine)
+against the CPU oracle and the reference's own outputs.
+
+Bars: top-k expert ids bit-exact (lower index wins ties) and router logits
+equal to the oracle's f64-accumulated logits.  Outputs (bf16) against the
+oracle's bf16 outputs: RMS relative error <= 2e-3 (the north star's
+tolerance), and per element |y - y_ref| <= 2^-8 * m[h] + ulp(y_ref[h]) with
+m[h] = sum_e |w_e down_e[h]| (+ |shared[h]|) (``oracle.backend.
+moe_term_magnitude``): one bf16 rounding step per accumulated term plus the
+final rounding.  Why not "bit-exact but for rare flips": both sides stage the
+reference's bf16 roundings (gate, up, act, down) but sum in different orders
+and use different exp/tanh; a 1-ulp flip of one gate/up output flips an
+activation element, which moves every down-projection output a little, so
+per-expert outputs differ by one bf16 step on many elements, and the weighted
+sum over the experts can cancel to a result smaller than its terms.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import backend as ob
+from oracle import q4nx as q
+from tests.golden import cases
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as _t
+    return _t
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    from raon_npu_b200.build import build
+    build()
+    from raon_npu_b200.device import Context
+    c = Context(0)
+    yield c
+    c.close()
+
+
+def ulp_diff(a, b):
+    def key(u):
+        u = np.asarray(u).astype(np.int32)
+        return np.where(u & 0x8000, -(u & 0x7FFF), u & 0x7FFF)
+    return np.abs(key(a) - key(b))
+
+
+def bf16_ulp_at(u16):
+    """Spacing of bf16 values at each element (one step of the last place)."""
+    f = np.abs(q.bf16_to_f32(u16).astype(np.float64))
+    e = np.floor(np.log2(np.maximum(f, 2.0 ** -126)))
+    return 2.0 ** (e - 7)
+
+
+def rms_rel(got, ref):
+    rf = q.bf16_to_f32(np.asarray(ref, np.uint16)).astype(np.float64)
+    gf = q.bf16_to_f32(np.asarray(got, np.uint16)).astype(np.float64)
+    return float(np.sqrt(np.mean((gf - rf) ** 2)) / max(np.sqrt(np.mean(rf ** 2)), 1e-30))
+
+
+def assert_bf16_outputs_close(got, ref, magnitude=None, tol=2e-3):
+    got = np.asarray(got, np.uint16)
+    ref = np.asarray(ref, np.uint16)
+    rf = q.bf16_to_f32(ref).astype(np.float64)
+    gf = q.bf16_to_f32(got).astype(np.float64)
+    err = np.abs(gf - rf)
+    if magnitude is not None:
+        bound = 2.0 ** -8 * magnitude + bf16_ulp_at(ref)
+        bad = err > bound
+        assert not bad.any(), (np.nonzero(bad)[0][:8], err[bad][:8], bound[bad][:8])
+    else:
+        assert ulp_diff(got, ref).max() <= 1
+    rms = np.sqrt(np.mean(err ** 2)) / max(np.sqrt(np.mean(rf ** 2)), 1e-30)
+    assert rms <= tol, rms
+
+
+def make_layer(ctx, d, has_shared=False, shared=None):
+    from raon_npu_b200.device import MoeLayer
+    e0 = next(iter(d["packed"]))
+    hidden = d["experts"][e0][2].shape[0]
+    inter = d["experts"][e0][0].shape[0]
+    layer = MoeLayer(ctx, hidden, inter, len(d["packed"]), has_shared=has_shared)
+    for e, (pgu, pdn) in d["packed"].items():
+        layer.set_expert(e, pgu, pdn)
+    if shared is not None:
+        layer.set_expert(len(d["packed"]), *shared)
+    return layer
+
+
+# ---------------------------------------------------------------- experts --
+def test_moe_experts_matches_reference_fixture(ctx):
+    """NumpyBackend.moe_experts outputs recorded from the reference (SiTU, two beta pairs)."""
+    g = np.load(cases.__file__.replace("cases.py", "moe.npz"))
+    d = cases.moe_inputs(**cases.MOE_CASE)
+    layer = make_layer(ctx, d)
+    for t in range(d["x"].shape[0]):
+        for tag, kw in (("default", {}), ("betas", dict(gate_beta=2.0, value_beta=10.0))):
+            out = layer.experts_host(d["x"][t], d["top_ids"][t], d["top_w"][t], act="situ", **kw)
+            mag = ob.moe_term_magnitude(d["experts"], d["x"][t], d["top_ids"][t], d["top_w"][t], "situ", **kw)
+            assert_bf16_outputs_close(out, g[f"tok{t}/{tag}"], mag)
+    layer.close()
+
+
+@pytest.mark.parametrize("act", ["swiglu", "situ"])
+def test_moe_experts_matches_oracle_config3_shapes(ctx, act):
+    """hidden 2048, intermediate 768, 8 of 16 experts (the config-3 expert shapes)."""
+    d = cases.moe_inputs(hidden=2048, inter=768, experts=16, k=8, tokens=2, seed=61)
+    layer = make_layer(ctx, d)
+    for t in range(2):
+        out = layer.experts_host(d["x"][t], d["top_ids"][t], d["top_w"][t], act=act)
+        ref = ob.moe_experts(d["experts"], d["x"][t], d["top_ids"][t], d["top_w"][t], act=act)
+        mag = ob.moe_term_magnitude(d["experts"], d["x"][t], d["top_ids"][t], d["top_w"][t], act)
+        assert_bf16_outputs_close(out, ref, mag)
+    layer.close()
+
+
+def test_moe_experts_padded_intermediate(ctx):
+    """Real-Raon-like intermediate 1088 (down K zero-padded to 1280, kernels/moe/pack.py:190-224)."""
+    rng = np.random.default_rng(71)
+    hidden, inter, E = 256, 1088, 4
+    experts, packed = {}, {}
+    for e in range(E):
+        gu = (rng.standard_normal((2 * inter, hidden)) * 0.02).astype(np.float32)
+        dn = (rng.standard_normal((hidden, inter)) * 0.02).astype(np.float32)
+        dnp, _ = q.pad_gemv(dn, m_align=128, k_align=256)
+        pgu, fgu = cases.q4nx_weight(gu, q)
+        pdn, fdn = cases.q4nx_weight(dnp, q)
+        experts[e] = (fgu[:inter], fgu[inter:], fdn[:, :inter])
+        packed[e] = (pgu, pdn)
+    from raon_npu_b200.device import MoeLayer
+    layer = MoeLayer(ctx, hidden, inter, E, has_shared=False)
+    for e, (a, b) in packed.items():
+        layer.set_expert(e, a, b)
+    x = q.f32_to_bf16(rng.standard_normal(hidden).astype(np.float32))
+    ids = np.array([3, 0, 2])
+    w = np.array([0.5, 0.3, 0.2], np.float32)
+    out = layer.experts_host(x, ids, w, act="situ")
+    assert_bf16_outputs_close(out, ob.moe_experts(experts, x, ids, w, act="situ"),
+                              ob.moe_term_magnitude(experts, x, ids, w, "situ"))
+    layer.close()
+
+
+def test_moe_experts_rejects_unknown_expert(ctx):
+    d = cases.moe_inputs(**cases.MOE_CASE)
+    layer = make_layer(ctx, d)
+    with pytest.raises(ValueError):
+        layer.experts_host(d["x"][0], np.array([0, 99, 1]), d["top_w"][0])
+    layer.close()
+
+
+# ----------------------------------------------------------------- router --
+def _router_layer(ctx, hidden, E, seed, dup=None):
+    from raon_npu_b200.device import MoeLayer
+    rng = np.random.default_rng(seed)
+    wr = q.f32_to_bf16((rng.standard_normal((E, hidden)) * 0.02).astype(np.float32))
+    if dup:
+        for a, b in dup:
+            wr[b] = wr[a]
+    layer = MoeLayer(ctx, hidden, 64, E, has_shared=False)
+    layer.set_router(wr)
+    return layer, wr, rng
+
+
+def test_softmax_router_matches_oracle(torch, ctx):
+    layer, wr, rng = _router_layer(ctx, 2048, 128, seed=81)
+    T, k = 16, 8
+    x = q.f32_to_bf16(rng.standard_normal((T, 2048)).astype(np.float32))
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    lg = torch.empty((T, 128), dtype=torch.float32, device="cuda")
+    layer.route(xd, T, k, ids, w, lg)
+    torch.cuda.synchronize()
+    ctx.sync()
+    for t in range(T):
+        r_ids, r_w, r_lg = ob.route_softmax(x[t], wr, k)
+        np.testing.assert_array_equal(lg[t].cpu().numpy(), r_lg)
+        np.testing.assert_array_equal(ids[t].cpu().numpy(), r_ids)
+        np.testing.assert_allclose(w[t].cpu().numpy(), r_w, rtol=2e-6)
+        # selection logic on the device's own logits is exact by construction
+        np.testing.assert_array_equal(ids[t].cpu().numpy(), ob.topk_lower_index_wins(lg[t].cpu().numpy(), k))
+    layer.close()
+
+
+def test_router_ties_lower_index_wins(torch, ctx):
+    # experts 9 and 40 duplicate expert 3 (identical logits); 77 duplicates 12
+    layer, wr, rng = _router_layer(ctx, 256, 128, seed=82, dup=[(3, 9), (3, 40), (12, 77)])
+    x = q.f32_to_bf16(rng.standard_normal((4, 256)).astype(np.float32))
+    x[3] = 0                                    # every logit 0: all 128 experts tie
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    ids = torch.empty((4, 8), dtype=torch.int32, device="cuda")
+    w = torch.empty((4, 8), dtype=torch.float32, device="cuda")
+    lg = torch.empty((4, 128), dtype=torch.float32, device="cuda")
+    layer.route(xd, 4, 8, ids, w, lg)
+    torch.cuda.synchronize()
+    for t in range(4):
+        np.testing.assert_array_equal(ids[t].cpu().numpy(), ob.topk_lower_index_wins(ob.router_logits(x[t], wr), 8))
+    np.testing.assert_array_equal(ids[3].cpu().numpy(), np.arange(8))
+    np.testing.assert_allclose(w[3].cpu().numpy(), np.full(8, 0.125, np.float32), rtol=1e-6)
+    layer.close()
+
+
+def test_sigmoid_bias_router_matches_reference_fixture(torch, ctx):
+    from raon_npu_b200.device import MoeLayer
+    g = np.load(cases.__file__.replace("cases.py", "router.npz"))
+    d = cases.router_inputs(**cases.ROUTER_CASE)
+    E, H = d["router_w_bits"].shape
+    layer = MoeLayer(ctx, H, 64, E, has_shared=False)
+    layer.set_router(d["router_w_bits"], d["bias"])
+    T, k = d["x"].shape[0], d["k"]
+    xd = torch.from_numpy(d["x"].view(np.int16)).cuda()
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    layer.route(xd, T, k, ids, w, router="sigmoid_bias", scaling=d["scaling"])
+    torch.cuda.synchronize()
+    for t in range(T):
+        np.testing.assert_array_equal(ids[t].cpu().numpy(), g[f"tok{t}/top"])
+        np.testing.assert_allclose(w[t].cpu().numpy(), g[f"tok{t}/w"], rtol=1e-5)
+    layer.close()
+
+
+# ------------------------------------------------------- decode layer (cfg 3) --
+def _config3_layer(torch, ctx, n_experts=128, hidden=2048, inter=768, seed=91, owned=None, has_shared=True):
+    """Experts generated on the GPU (seeded), quantised by rc_quantize_q4nx.
+    Returns (layer, router bits, host packed bytes of every expert)."""
+    from raon_npu_b200.device import MoeLayer
+    gen = torch.Generator(device="cuda")
+    layer = MoeLayer(ctx, hidden, inter, n_experts, has_shared=has_shared)
+    packed = {}
+    ids = list(range(n_experts)) + ([n_experts] if has_shared else [])
+    for e in ids:
+        gen.manual_seed(seed * 1000 + e)
+        gu = torch.randn((2 * inter, hidden), generator=gen, device="cuda") * 0.02
+        dn = torch.randn((hidden, inter), generator=gen, device="cuda") * 0.02
+        pgu = torch.empty(2 * inter * hidden * 5 // 8, dtype=torch.uint8, device="cuda")
+        pdn = torch.empty(hidden * inter * 5 // 8, dtype=torch.uint8, device="cuda")
+        ctx.quantize_q4nx(gu, pgu, 2 * inter, hidden)
+        ctx.quantize_q4nx(dn, pdn, hidden, inter)
+        packed[e] = (pgu, pdn)
+        if owned is None or e in owned:
+            layer.set_expert(e, pgu, pdn)
+    rng = np.random.default_rng(seed)
+    wr = q.f32_to_bf16((rng.standard_normal((n_experts, hidden)) * 0.02).astype(np.float32))
+    layer.set_router(wr)
+    return layer, wr, packed
+
+
+def _oracle_expert(packed, e, hidden, inter):
+    pgu, pdn = (t.cpu().numpy() for t in packed[e])
+    fgu = q.dequantize_packed(pgu, 2 * inter, hidden)
+    return fgu[:inter], fgu[inter:], q.dequantize_packed(pdn, hidden, inter)
+
+
+def test_moe_decode_layer_config3(torch, ctx):
+    """hidden 2048, 128 experts + shared, I=768, softmax top-8, SwiGLU."""
+    layer, wr, packed = _config3_layer(torch, ctx)
+    rng = np.random.default_rng(5)
+    for trial in range(3):
+        x = q.f32_to_bf16(rng.standard_normal(2048).astype(np.float32))
+        xd = torch.from_numpy(x.view(np.int16)).cuda()
+        out = torch.empty(2048, dtype=torch.int16, device="cuda")
+        ids = torch.empty(8, dtype=torch.int32, device="cuda")
+        w = torch.empty(8, dtype=torch.float32, device="cuda")
+        layer.decode(xd, 8, out, ids, w, act="swiglu")
+        torch.cuda.synchronize()
+        ctx.sync()
+        r_ids, r_w, _ = ob.route_softmax(x, wr, 8)
+        np.testing.assert_array_equal(ids.cpu().numpy(), r_ids)
+        experts = {int(e): _oracle_expert(packed, int(e), 2048, 768) for e in r_ids}
+        routed = ob.moe_experts(experts, x, r_ids, r_w, act="swiglu")
+        sh = ob.expert_forward(*_oracle_expert(packed, 128, 2048, 768), x, "swiglu")
+        ref = ob.moe_token_with_shared(routed, sh)
+        mag = ob.moe_term_magnitude(experts, x, r_ids, r_w, "swiglu", shared_down_u16=sh)
+        got = out.cpu().numpy().view(np.uint16)
+        assert_bf16_outputs_close(got, ref, mag)
+
+        # Stage by stage: every expert's bf16 output row (8 routed slots in
+        # ascending expert ID, then the shared expert) against the oracle's,
+        # and the combine of the GPU's own rows, restated by the oracle, bit-exact.
+        slots = torch.empty((9, 2048), dtype=torch.int16, device="cuda")
+        sw = torch.empty(8, dtype=torch.float32, device="cuda")
+        layer.decode_local(xd, 8, slots, sw, act="swiglu")
+        torch.cuda.synchronize()
+        rows = slots.cpu().numpy().view(np.uint16)
+        order = np.argsort(r_ids, kind="stable")
+        np.testing.assert_array_equal(sw.cpu().numpy(), w.cpu().numpy()[order])
+        for s, e in enumerate(list(r_ids[order]) + [128]):
+            e_ref = sh if e == 128 else ob.expert_forward(*experts[int(e)], x, "swiglu")
+            # one expert row: a flipped activation element moves ~20% of the
+            # down outputs by one bf16 step, so the bar is one step (2^-8) RMS
+            assert rms_rel(rows[s], e_ref) <= 2.0 ** -8, (s, int(e), rms_rel(rows[s], e_ref))
+        routed_gpu = ob.combine_ascending(rows[None, :8], r_ids[order][None], w.cpu().numpy()[order][None])[0]
+        np.testing.assert_array_equal(ob.moe_token_with_shared(routed_gpu, rows[8]), got)
+    layer.close()
+
+
+def test_expert_parallel_halves_reproduce_single_gpu_bytes(torch, ctx):
+    """Two 'ranks' on one GPU, each holding half of the experts (rank 0 also the
+    shared one): exchanging the slot rows and combining gives exactly the bytes
+    of the single-layer decode."""
+    full, wr, _ = _config3_layer(torch, ctx, n_experts=32, seed=92)
+    r0, _, _ = _config3_layer(torch, ctx, n_experts=32, seed=92, owned=set(range(16)) | {32})
+    r1, _, _ = _config3_layer(torch, ctx, n_experts=32, seed=92, owned=set(range(16, 32)))
+    rng = np.random.default_rng(6)
+    for _ in range(4):
+        x = q.f32_to_bf16(rng.standard_normal(2048).astype(np.float32))
+        xd = torch.from_numpy(x.view(np.int16)).cuda()
+        ref = torch.empty(2048, dtype=torch.int16, device="cuda")
+        full.decode(xd, 8, ref, act="swiglu")
+        slots = [torch.empty((9, 2048), dtype=torch.int16, device="cuda") for _ in range(2)]
+        sw = [torch.empty(8, dtype=torch.float32, device="cuda") for _ in range(2)]
+        r0.decode_local(xd, 8, slots[0], sw[0], act="swiglu")
+        r1.decode_local(xd, 8, slots[1], sw[1], act="swiglu")
+        torch.cuda.synchronize()
+        # each slot row is produced by exactly one rank; the other rank's row is zero
+        a = slots[0].view(torch.int16)
+        b = slots[1].view(torch.int16)
+        assert bool(((a == 0) | (b == 0)).all())
+        merged = torch.where(a != 0, a, b)
+        assert torch.equal(sw[0], sw[1])
+        out = torch.empty(2048, dtype=torch.int16, device="cuda")
+        r0.combine(merged, sw[0], 8, out, with_shared=True)
+        torch.cuda.synchronize()
+        ctx.sync()
+        assert torch.equal(out, ref)
+    for layer in (full, r0, r1):
+        layer.close()
