@@ -122,8 +122,8 @@ int rc_gemv_host(rc_ctx *ctx, const rc_weight *w, const void *x_host, int x_dtyp
  * n_experts), each a q4nx [gate; up] matrix [2*inter, hidden] and a down
  * matrix [hidden, inter_pad] (inter zero-padded to a multiple of 256), both
  * as pack_gemv bytes -- the reference's expert packers
- * (kernels/moe/pack.py:136-224).  Expert parallelism: load only the experts a
- * rank owns; the others are skipped and their slot outputs are zero. */
+ * (kernels/moe/pack.py:136-224).  Expert parallelism: a rank loads the
+ * experts it computes (rc_moe_decode_local). */
 typedef struct rc_moe rc_moe;
 
 int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_shared, rc_moe **out);
@@ -144,39 +144,54 @@ int rc_moe_set_router(rc_moe *m, const uint16_t *router_w, const float *bias);
 int rc_moe_route(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize,
                  float scaling, int32_t *ids_dev, float *w_dev, float *logits_dev, void *stream);
 
-/* Routed experts of one token for caller-supplied top-k ids / weights
- * (device arrays, any order): ``Backend.moe_experts`` (host/backend.py:98-117,
- * numpy host/backend.py:466-510; NPU npu/backend.py:5029-5322).  Experts are
- * summed in ascending ID in f32, then RTNE.  with_shared != 0 also adds the
- * shared expert as ``_moe_token`` does (host/raon.py:1310-1327). */
-int rc_moe_experts(rc_moe *m, const uint16_t *x_dev, const int32_t *ids_dev, const float *w_dev, int k,
-                   int act, float gate_beta, float value_beta, int with_shared, uint16_t *out_dev,
+/* Routed experts of T <= 16 tokens for caller-supplied top-k ids / weights
+ * [T][k] (device arrays, any order within a token, distinct ids):
+ * ``Backend.moe_experts`` (host/backend.py:98-117, numpy
+ * host/backend.py:466-510; NPU npu/backend.py:5029-5322) for T = 1.  Experts
+ * are summed in ascending ID in f32, then RTNE.  with_shared != 0 also adds
+ * the shared expert as ``_moe_token`` does (host/raon.py:1310-1327).
+ * x [T][hidden] bf16, out [T][hidden] bf16. */
+int rc_moe_experts(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev, const float *w_dev,
+                   int k, int act, float gate_beta, float value_beta, int with_shared, uint16_t *out_dev,
                    void *stream);
 
-/* rc_moe_experts on host buffers (x [hidden] bf16, ids [k] int32, w [k] f32,
- * out [hidden] bf16): copies in, runs, copies out, waits.  Validates the ids
- * (range, loaded) as the reference's ValueError checks do. */
-int rc_moe_experts_host(rc_moe *m, const uint16_t *x_host, const int32_t *ids_host, const float *w_host,
-                        int k, int act, float gate_beta, float value_beta, int with_shared,
-                        uint16_t *out_host);
+/* rc_moe_experts on host buffers: copies in, runs, copies out, waits.
+ * Validates the ids (range, loaded, distinct per token) as the reference's
+ * ValueError checks do. */
+int rc_moe_experts_host(rc_moe *m, const uint16_t *x_host, int T, const int32_t *ids_host,
+                        const float *w_host, int k, int act, float gate_beta, float value_beta,
+                        int with_shared, uint16_t *out_host);
 
-/* The whole decode layer for one token: router, routed + shared experts,
- * combine; optional copies of the selected ids / weights. */
-int rc_moe_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int renormalize, float scaling,
-                  int act, float gate_beta, float value_beta, uint16_t *out_dev, int32_t *ids_dev,
-                  float *w_dev, void *stream);
+/* ``moe_experts_grouped`` (npu/backend.py:4845-4979): routed sums
+ * routed_out [T][hidden] and, when shared_gu [T][2*inter] (the shared
+ * expert's gate | up rows, computed by the caller) is given, the shared
+ * expert's down rows shared_out [T][hidden] = linear(shared_down,
+ * RTNE(act(gate, up))). */
+int rc_moe_experts_grouped(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev,
+                           const float *w_dev, int k, const uint16_t *shared_gu_dev, int act,
+                           float gate_beta, float value_beta, uint16_t *routed_out_dev,
+                           uint16_t *shared_out_dev, void *stream);
 
-/* Expert-parallel halves of rc_moe_decode.  decode_local routes, runs the
- * experts this rank holds and writes every slot's down output
- * slot_out[k (+1 shared)][hidden] (zeros for experts held elsewhere) and the
- * slot weights (ascending-ID order); after the ranks exchange their slot rows
- * (each slot is non-zero on exactly one rank), rc_moe_combine produces the
- * same bytes as rc_moe_decode on one GPU. */
-int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int k, int router, int renormalize, float scaling,
-                        int act, float gate_beta, float value_beta, uint16_t *slot_out_dev,
+/* The whole decode layer for T <= 16 tokens: router, routed + shared experts,
+ * combine; optional copies of the selected ids / weights [T][k]. */
+int rc_moe_decode(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize,
+                  float scaling, int act, float gate_beta, float value_beta, uint16_t *out_dev,
+                  int32_t *ids_dev, float *w_dev, void *stream);
+
+/* Expert-parallel halves of rc_moe_decode.  decode_local routes all T tokens,
+ * runs the routed experts [expert_lo, expert_hi) for every token and the
+ * shared expert for tokens [shared_t0, shared_t0 + shared_tn), and writes the
+ * slot rows slot_out [T][k+1][hidden] (slot r < k: the r-th selected expert in
+ * ascending ID; slot k: the shared expert; zeros where another rank computes
+ * the slot) and the slot weights slot_w [T][k].  Once the ranks' slot rows
+ * are summed (each row is non-zero on at most one rank, so the sum is exact),
+ * rc_moe_combine produces the same bytes as rc_moe_decode on one GPU. */
+int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize,
+                        float scaling, int act, float gate_beta, float value_beta, int expert_lo,
+                        int expert_hi, int shared_t0, int shared_tn, uint16_t *slot_out_dev,
                         float *slot_w_dev, void *stream);
-int rc_moe_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int k, int with_shared,
-                   uint16_t *out_dev, void *stream);
+int rc_moe_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int T, int k,
+                   int with_shared, uint16_t *out_dev, void *stream);
 
 /* rc_gemv without any device allocation (this entry point has no counterpart
  * in the reference).  Arguments and results are those of rc_gemv; the context

@@ -88,7 +88,7 @@ def moe_term_magnitude(experts, x, top_ids, top_weights, act="situ", gate_beta=4
     terms the f32 combine accumulates.  Each expert output is a bf16 value
     whose last rounding step may fall either way between two implementations
     summing in different orders, so an implementation-independent bound on an
-    MoE output is one bf16 step (2^-8 relative) of this magnitude."""
+    MoE output is one bf16 step (at most 2^-7 relative) of this magnitude."""
     mag = None
     for eid, wt in zip(top_ids, top_weights):
         wg, wu, wd = experts[int(eid)]

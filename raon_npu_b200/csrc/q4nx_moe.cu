@@ -1,8 +1,8 @@
-// MoE decode on the q4nx experts: router top-k, grouped expert GEMVs with the
-// GLU activation fused into the gate/up epilogue, and the ascending-expert-ID
-// combine.  Everything stays on the device, so a layer is a fixed chain of
-// launches (graph-capturable) with no host round trip between router and
-// experts.
+// MoE decode on the q4nx experts: router top-k, token grouping by expert,
+// grouped expert GEMVs with the GLU activation fused into the gate/up
+// epilogue, and the ascending-expert-ID combine.  Everything stays on the
+// device, so a layer is a fixed chain of launches (graph-capturable) with no
+// host round trip between router and experts.
 //
 // Reference semantics (raon-npu):
 //   router      host/raon.py:1224-1247 (sigmoid + bias) and the softmax top-k
@@ -11,11 +11,27 @@
 //               act -> RTNE, down linear (bf16); f32 weighted sum over the
 //               experts in ascending ID, then RTNE.
 //   shared      host/raon.py:1310-1327: out = RTNE(f32(routed) + f32(shared)).
+//   grouped     npu/backend.py:4845-4979: T tokens, routed sums plus the shared
+//               expert's down rows from caller-supplied shared gate/up rows.
 //
-// Grouped GEMV partition: every warp owns whole row tiles (tiles w, w+W, ...
-// of the slot-major tile list), so no tile is split and an expert's output is
-// bit-identical whichever slots or ranks take part -- expert-parallel results
-// equal single-GPU results byte for byte.
+// Work layout for T <= 16 tokens (one or two 8-column mma blocks):
+//   groups      one per active expert, ascending ID, the shared expert last;
+//               group g carries a token mask and, per token, the destination
+//               slot row t*(k+1) + (position of the expert in the token's
+//               ascending list; k for the shared expert).
+//   gate/up     every warp takes whole row tiles of the group-major tile list
+//               (tiles w, w+W, ...); all T tokens are staged once per CTA and
+//               every tile computes all T columns, so an expert's weights are
+//               read once however many tokens chose it; the epilogue keeps the
+//               columns of the group's tokens:  act[g][t][col].
+//   down        CTA c takes a contiguous range of the tile list, stages the
+//               activation rows of the (at most 4) groups the range touches
+//               and scatters row results to down_out[t*(k+1)+pos][row].
+//   combine     per token, ascending ID, f32 multiply then add (no FMA), RTNE.
+// No tile is split across warps and mma output columns do not interact, so an
+// expert's output for a token is bit-identical whichever tokens, groups or
+// ranks share the launch -- expert-parallel results equal single-GPU results
+// byte for byte.
 #include <string.h>
 
 #include "q4nx_core.cuh"
@@ -24,11 +40,78 @@
 
 namespace rc {
 
-constexpr int kMoeMaxK = 16;          // routed experts per token
+constexpr int kMoeMaxK = 16;               // routed experts per token
+constexpr int kMoeMaxTokens = 16;          // tokens per call: two 8-column mma blocks
+constexpr int kMoeMaxExperts = 256;
 constexpr int kMoeWarps = 8;
 constexpr int kMoeMaxStages = 8;
+constexpr int kMoeMaxGroupsPerCta = 4;     // down kernel: groups one CTA's tile range may touch
 
-struct rc_moe_impl;
+// Per-call device scratch of a layer.
+struct MoeScratch {
+  float *logits;           // [T][E]
+  int *counter;            // [T + 1] arrival counters (per token, then "all tokens"), zero between calls
+  int32_t *ids;            // [T][k] rank order (best first)
+  float *weights;          // [T][k]
+  int32_t *slot_expert;    // [T][k+1] ascending ID, then the shared expert (or -1)
+  float *slot_w;           // [T][k]   weights in slot order
+  int *n_groups;           // [1]
+  int32_t *group_expert;   // [E+1]
+  uint32_t *group_mask;    // [E+1] tokens of each group
+  int32_t *group_dst;      // [E+1][16] slot row of (group, token)
+};
+
+// What one rank computes: routed experts [lo, hi) for every token, the shared
+// expert (id E) for the tokens in shared_mask.
+struct MoeOwned {
+  int lo, hi;
+  uint32_t shared_mask;
+};
+
+// ------------------------------------------------------------ grouping --
+// One warp.  Reads the slot lists of T tokens (written by other threads or
+// CTAs: the caller fences), builds the ascending-ID group table.  Scratch
+// smem_mask / smem_gidx hold E+1 entries.
+__device__ void build_groups(const int32_t *slot_expert, int T, int k, int n_experts, MoeOwned own,
+                             const MoeScratch &s, uint32_t *smem_mask, int *smem_gidx, int lane) {
+  const int ne = n_experts + 1;
+  for (int e = lane; e < ne; e += 32) smem_mask[e] = 0u;
+  __syncwarp();
+  for (int pr = lane; pr < T * k; pr += 32) {
+    const int t = pr / k, r = pr - t * k;
+    const int e = __ldcg(slot_expert + t * (k + 1) + r);
+    if (e >= own.lo && e < own.hi) atomicOr(smem_mask + e, 1u << t);
+  }
+  __syncwarp();
+  if (lane == 0) smem_mask[n_experts] = own.shared_mask;
+  __syncwarp();
+  int base = 0;
+  for (int c = 0; c < ne; c += 32) {
+    const int e = c + lane;
+    const uint32_t m = e < ne ? smem_mask[e] : 0u;
+    const uint32_t b = __ballot_sync(0xffffffffu, m != 0u);
+    if (m) {
+      const int gi = base + __popc(b & ((1u << lane) - 1u));
+      s.group_expert[gi] = e;
+      s.group_mask[gi] = m;
+      smem_gidx[e] = gi;
+    }
+    base += __popc(b);
+  }
+  if (lane == 0) *s.n_groups = base;
+  __syncwarp();
+  for (int pr = lane; pr < T * (k + 1); pr += 32) {
+    const int t = pr / (k + 1), r = pr - t * (k + 1);
+    const int e = __ldcg(slot_expert + pr);
+    bool mine;
+    if (r < k) {
+      mine = e >= own.lo && e < own.hi;
+    } else {
+      mine = e >= 0 && ((own.shared_mask >> t) & 1u);
+    }
+    if (mine) s.group_dst[smem_gidx[e] * kMoeMaxTokens + t] = pr;
+  }
+}
 
 // ----------------------------------------------------------------- router --
 struct RouteParams {
@@ -37,13 +120,9 @@ struct RouteParams {
   float scaling;
   const uint16_t *wr;      // [E][hidden] bf16
   const float *bias;       // [E] (sigmoid mode)
-  float *logits;           // [T][E] f32 scratch (always written)
-  int *counter;            // [T] arrival counters, zero between launches
-  int32_t *ids;            // [T][k]   rank order (best first)
-  float *weights;          // [T][k]
-  int32_t *slot_expert;    // [T][k+1] ascending ID, then the shared expert (or -1)
-  float *slot_w;           // [T][k]   weights in slot order
+  MoeScratch s;
   int shared_id;           // expert id of the shared expert, -1 if none
+  MoeOwned own;
 };
 
 constexpr int kRouteThreads = 256;
@@ -52,8 +131,12 @@ constexpr int kRouteExpertsPerCta = 8;   // one warp per expert
 // Phase 1 (every CTA): logits of 8 experts for one token, f64 accumulation of
 // exact bf16 x bf16 products, rounded once to f32.  Phase 2 (the last CTA of
 // the token, by an arrival counter): top-k with "lower index wins" ties, the
-// routing weights and the ascending-ID slot list.
+// routing weights and the ascending-ID slot list.  Phase 3 (the last token to
+// finish): the group table.
 __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p) {
+  __shared__ uint32_t smask[kMoeMaxExperts + 1];
+  __shared__ int sgidx[kMoeMaxExperts + 1];
+  __shared__ int is_last;
   pdl_launch_dependents();
   pdl_wait_prior();
   const int t = blockIdx.y;
@@ -71,23 +154,22 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) p.logits[(size_t)t * p.n_experts + e] = __double2float_rn(acc);
+    if (lane == 0) p.s.logits[(size_t)t * p.n_experts + e] = __double2float_rn(acc);
   }
   __threadfence();
   __syncthreads();
-  __shared__ int is_last;
   if (threadIdx.x == 0) {
-    const int old = atomicAdd(p.counter + t, 1);
+    const int old = atomicAdd(p.s.counter + t, 1);
     is_last = old == (int)gridDim.x - 1;
-    if (is_last) atomicExch(p.counter + t, 0);
+    if (is_last) atomicExch(p.s.counter + t, 0);
   }
   __syncthreads();
   if (!is_last || warp != 0) return;
   __threadfence();
 
   // ---- selection (one warp): value per expert, then k rounds of warp argmax
-  const float *lg = p.logits + (size_t)t * p.n_experts;
-  constexpr int kPer = 8;   // experts per lane (n_experts <= 256)
+  const float *lg = p.s.logits + (size_t)t * p.n_experts;
+  constexpr int kPer = kMoeMaxExperts / 32;
   float val[kPer], score[kPer];
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
@@ -129,133 +211,171 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
       if (lane + 32 * i == bi) sc = score[i], val[i] = -INFINITY;
     sel_score[r] = __shfl_sync(0xffffffffu, sc, bi & 31);
   }
-  if (lane != 0) return;
-  // ---- routing weights
-  float w[kMoeMaxK];
-  if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
-    float sum = 0.f;
-    for (int r = 0; r < p.k; ++r) sum += sel_score[r];
+  if (lane == 0) {
+    // ---- routing weights
+    float w[kMoeMaxK];
+    if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
+      float sum = 0.f;
+      for (int r = 0; r < p.k; ++r) sum += sel_score[r];
+      for (int r = 0; r < p.k; ++r) {
+        float c = sel_score[r];
+        if (p.renorm) c = c / (sum + 1e-20f);
+        w[r] = c * p.scaling;
+      }
+    } else {
+      // softmax over all experts then renormalised over the top-k equals the
+      // softmax of the selected logits (the full denominator cancels).
+      const float mx = sel_score[0];
+      float sum = 0.f;
+      for (int r = 0; r < p.k; ++r) sum += expf(sel_score[r] - mx);
+      for (int r = 0; r < p.k; ++r) w[r] = expf(sel_score[r] - mx) / sum;
+    }
     for (int r = 0; r < p.k; ++r) {
-      float c = sel_score[r];
-      if (p.renorm) c = c / (sum + 1e-20f);
-      w[r] = c * p.scaling;
+      p.s.ids[(size_t)t * p.k + r] = sel[r];
+      p.s.weights[(size_t)t * p.k + r] = w[r];
     }
-  } else {
-    // softmax over all experts then renormalised over the top-k equals the
-    // softmax of the selected logits (the full denominator cancels).
-    const float mx = sel_score[0];
-    float sum = 0.f;
-    for (int r = 0; r < p.k; ++r) sum += expf(sel_score[r] - mx);
-    for (int r = 0; r < p.k; ++r) w[r] = expf(sel_score[r] - mx) / sum;
-  }
-  for (int r = 0; r < p.k; ++r) {
-    p.ids[(size_t)t * p.k + r] = sel[r];
-    p.weights[(size_t)t * p.k + r] = w[r];
-  }
-  // ---- ascending-ID slot list (insertion sort of k <= 16 entries)
-  int order[kMoeMaxK];
-  for (int r = 0; r < p.k; ++r) order[r] = r;
-  for (int a = 1; a < p.k; ++a) {
-    const int v = order[a];
-    int b = a - 1;
-    while (b >= 0 && sel[order[b]] > sel[v]) {
-      order[b + 1] = order[b];
-      --b;
+    // ---- ascending-ID slot list (insertion sort of k <= 16 entries)
+    int order[kMoeMaxK];
+    for (int r = 0; r < p.k; ++r) order[r] = r;
+    for (int a = 1; a < p.k; ++a) {
+      const int v = order[a];
+      int b = a - 1;
+      while (b >= 0 && sel[order[b]] > sel[v]) {
+        order[b + 1] = order[b];
+        --b;
+      }
+      order[b + 1] = v;
     }
-    order[b + 1] = v;
+    int32_t *se = p.s.slot_expert + (size_t)t * (p.k + 1);
+    float *sw = p.s.slot_w + (size_t)t * p.k;
+    for (int r = 0; r < p.k; ++r) {
+      se[r] = sel[order[r]];
+      sw[r] = w[order[r]];
+    }
+    se[p.k] = p.shared_id;
+    __threadfence();
+    const int old = atomicAdd(p.s.counter + p.tokens, 1);
+    is_last = old == p.tokens - 1;
+    if (is_last) atomicExch(p.s.counter + p.tokens, 0);
   }
-  int32_t *se = p.slot_expert + (size_t)t * (p.k + 1);
-  float *sw = p.slot_w + (size_t)t * p.k;
-  for (int r = 0; r < p.k; ++r) {
-    se[r] = sel[order[r]];
-    sw[r] = w[order[r]];
-  }
-  se[p.k] = p.shared_id;
+  __syncwarp();
+  if (!__shfl_sync(0xffffffffu, is_last, 0)) return;
+  __threadfence();
+  build_groups(p.s.slot_expert, p.tokens, p.k, p.n_experts, p.own, p.s, smask, sgidx, lane);
 }
 
-// Slot list from caller-supplied top ids / weights (the Backend.moe_experts
-// boundary): sort ascending by ID, append the shared expert.
-__global__ void moe_slots_kernel(const int32_t *ids, const float *w, int k, int shared_id, int32_t *slot_expert,
-                                 float *slot_w) {
+// Slot lists from caller-supplied top ids / weights [T][k] (the
+// Backend.moe_experts boundary): per token sort ascending by ID, append the
+// shared expert; then the group table.  One warp.
+__global__ void moe_slots_kernel(const int32_t *ids, const float *w, int T, int k, int n_experts, int shared_id,
+                                 MoeOwned own, MoeScratch s) {
+  __shared__ uint32_t smask[kMoeMaxExperts + 1];
+  __shared__ int sgidx[kMoeMaxExperts + 1];
   pdl_launch_dependents();
   pdl_wait_prior();
-  if (threadIdx.x != 0) return;
-  int order[kMoeMaxK];
-  for (int r = 0; r < k; ++r) order[r] = r;
-  for (int a = 1; a < k; ++a) {
-    const int v = order[a];
-    int b = a - 1;
-    while (b >= 0 && ids[order[b]] > ids[v]) {
-      order[b + 1] = order[b];
-      --b;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x >= 32) return;
+  for (int t = lane; t < T; t += 32) {
+    const int32_t *id = ids + (size_t)t * k;
+    const float *wt = w + (size_t)t * k;
+    int order[kMoeMaxK];
+    for (int r = 0; r < k; ++r) order[r] = r;
+    for (int a = 1; a < k; ++a) {
+      const int v = order[a];
+      int b = a - 1;
+      while (b >= 0 && id[order[b]] > id[v]) {
+        order[b + 1] = order[b];
+        --b;
+      }
+      order[b + 1] = v;
     }
-    order[b + 1] = v;
+    for (int r = 0; r < k; ++r) {
+      s.slot_expert[(size_t)t * (k + 1) + r] = id[order[r]];
+      s.slot_w[(size_t)t * k + r] = wt[order[r]];
+    }
+    s.slot_expert[(size_t)t * (k + 1) + k] = shared_id;
   }
-  for (int r = 0; r < k; ++r) {
-    slot_expert[r] = ids[order[r]];
-    slot_w[r] = w[order[r]];
-  }
-  slot_expert[k] = shared_id;
+  __threadfence_block();
+  __syncwarp();
+  build_groups(s.slot_expert, T, k, n_experts, own, s, smask, sgidx, lane);
 }
 
 // ------------------------------------------------------ grouped expert GEMV --
 enum MoeEpi : int { kMoeEpiGlu = 0, kMoeEpiDown = 1 };
 
 struct MoeGemvParams {
-  const uint8_t *const *expert_tiles;  // per expert: t16 tiles, or null (not on this rank)
-  const int32_t *slot_expert;          // [n_slots]: expert of each slot (-1: none)
-  int n_slots;
-  int slot_tiles;                      // row tiles per expert matrix
+  const uint8_t *const *expert_tiles;  // [E+1]: t16 tiles of each expert matrix (null: not loaded)
+  const int *n_groups;
+  const int32_t *group_expert;
+  const uint32_t *group_mask;
+  const int32_t *group_dst;
+  int skip_last_group;                 // gate/up: the shared group's activations come from elsewhere
+  int group_tiles;                     // row tiles per expert matrix
   int kb;                              // K / 256
   int stages;
+  int T;                               // tokens of the call
   // activations (fields read by the shared staging code)
   const void *x;
   int x_dtype, ldx, tokens, slots, x_vec;
   // output
   uint16_t *y;
-  long long y_slot_stride;             // elements between slots
-  int ldy;                             // elements between token rows within a slot (glu)
+  int ldy;
   int act;
   float gate_beta, value_beta;
   int *err;
 };
 
-__device__ __forceinline__ const uint8_t *slot_base(const MoeGemvParams &p, int slot) {
-  const int e = p.slot_expert[slot];
-  return e < 0 ? nullptr : p.expert_tiles[e];
-}
-
-// EPI == kMoeEpiGlu: x = the token rows (shared by all slots); tile rows are
-//   interleaved (gate g, up g) pairs; y[slot][t][8*tile + g] = bf16(act(gate, up)).
-// EPI == kMoeEpiDown: x row s feeds slot s only (token block s/8, column s%8);
-//   y[slot][row] = bf16(sum).
-template <int EPI>
+// EPI == kMoeEpiGlu: x = the T token rows; tile rows are interleaved
+//   (gate g, up g) pairs; y = act rows, act[g][t][8*tile + g'] for the tokens of
+//   group g (8*NTB rows per group).
+// EPI == kMoeEpiDown: x = act; y = down_out rows, [t*(k+1)+pos][hidden].
+template <int EPI, int NTB>
 __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb = p.kb, k = kb * kUnitK, S = p.stages;
-  const int ntb = (p.slots + 7) >> 3;
   uint8_t *ring = smem + warp * S * kUnitBytes;
   const uint32_t ring_s = smem_addr(ring);
+  constexpr int kStageBlocks = EPI == kMoeEpiGlu ? NTB : NTB * kMoeMaxGroupsPerCta;
   uint8_t *cur = smem + kMoeWarps * S * kUnitBytes;
   uint32_t *xs = reinterpret_cast<uint32_t *>(cur);
-  cur += xfrag_bytes(ntb, k);
+  cur += xfrag_bytes(kStageBlocks, k);
   float *gs = reinterpret_cast<float *>(cur);
-  cur += gsum_bytes(ntb, k);
+  cur += gsum_bytes(kStageBlocks, k);
   const uint32_t bar0 = smem_addr(cur) + warp * S * 8;
 
-  const int W = gridDim.x * kMoeWarps;
-  const int w = blockIdx.x * kMoeWarps + warp;
-  const int total_tiles = p.n_slots * p.slot_tiles;
-  const int my_tiles = w < total_tiles ? (total_tiles - 1 - w) / W + 1 : 0;
+  pdl_launch_dependents();
+  // The group table is written by the previous launch: wait before reading it.
+  pdl_wait_prior();
+  const int ng = *p.n_groups - (p.skip_last_group ? 1 : 0);
+  const int total = ng * p.group_tiles;
+  int t_begin, t_step, t_end, g_lo = 0;
+  MoeGemvParams q = p;
+  if (EPI == kMoeEpiDown) {
+    const int per = (total + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int c0 = blockIdx.x * per;
+    const int c1 = c0 + per < total ? c0 + per : total;
+    t_begin = c0 + warp;
+    t_step = kMoeWarps;
+    t_end = c1;
+    g_lo = c0 / p.group_tiles;
+    const int g_hi = c1 > c0 ? (c1 - 1) / p.group_tiles : g_lo - 1;
+    // stage the activation rows of groups g_lo..g_hi (8*NTB rows each)
+    q.x = static_cast<const uint16_t *>(p.x) + (size_t)g_lo * 8 * NTB * p.ldx;
+    q.tokens = q.slots = (g_hi - g_lo + 1) * 8 * NTB;
+  } else {
+    t_begin = blockIdx.x * kMoeWarps + warp;
+    t_step = gridDim.x * kMoeWarps;
+    t_end = total;
+  }
+  const int my_tiles = t_begin < t_end ? (t_end - 1 - t_begin) / t_step + 1 : 0;
   const int n = my_tiles * kb;
 
-  // unit j of this warp -> (slot, tile, kbi) and its source (null: skipped slot)
   auto unit_src = [&](int j) -> const uint8_t * {
     const int i = j / kb, kbi = j - i * kb;
-    const int tg = w + i * W;
-    const int slot = tg / p.slot_tiles, tile = tg - slot * p.slot_tiles;
-    const uint8_t *b = slot_base(p, slot);
+    const int tg = t_begin + i * t_step;
+    const int grp = tg / p.group_tiles, tile = tg - grp * p.group_tiles;
+    const uint8_t *b = p.expert_tiles[p.group_expert[grp]];
     return b ? b + ((size_t)tile * kb + kbi) * kUnitBytes : nullptr;
   };
   const uint64_t pol = policy_evict_first();
@@ -268,28 +388,25 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
       mbar_arrive_expect_tx(bar0 + 8 * sl, 0);   // nothing to fetch: complete the phase at once
     }
   };
-  pdl_launch_dependents();
-  // The slot list is written by the previous launch (router / slot kernel):
-  // wait before reading it.
-  pdl_wait_prior();
   if (lane == 0 && n > 0) {
     for (int s = 0; s < S; ++s) mbar_init(bar0 + 8 * s, 1);
     mbar_fence_init();
     for (int j = 0; j < n && j < S; ++j) issue(j, j);
   }
-  build_activations<true>(p, ntb, xs, gs, threadIdx.x, blockDim.x);
+  build_activations<true>(q, kStageBlocks, xs, gs, threadIdx.x, blockDim.x);
   __syncthreads();
   if (n == 0) return;
 
-  Acc<1> acc;
+  Acc<NTB> acc;
   acc_zero(acc);
   int slot_ring = 0;
   uint32_t phase = 0;
+  const int g = lane >> 2, qd = lane & 3;
   for (int j = 0; j < n; ++j) {
     const int i = j / kb, kbi = j - i * kb;
-    const int tg = w + i * W;
-    const int slot = tg / p.slot_tiles, tile = tg - slot * p.slot_tiles;
-    const bool live = slot_base(p, slot) != nullptr;
+    const int tg = t_begin + i * t_step;
+    const int grp = tg / p.group_tiles, tile = tg - grp * p.group_tiles;
+    const bool live = p.expert_tiles[p.group_expert[grp]] != nullptr;
     if (!mbar_wait_bounded(bar0 + 8 * slot_ring, phase)) {
       if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
       int s2 = slot_ring;
@@ -301,42 +418,35 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
       return;
     }
     if (live) {
-      if (EPI == kMoeEpiGlu) {
-        compute_unit<1, true>(ring + slot_ring * kUnitBytes, xs, gs, p, kbi, lane, acc);
-      } else {
-        const int tb = slot >> 3;   // token block holding this slot's activation row
-        compute_unit<1, true>(ring + slot_ring * kUnitBytes, xs + (size_t)tb * (k / 64) * 256,
-                              gs + (size_t)tb * kb * 64, p, kbi, lane, acc);
-      }
+      const int blk = EPI == kMoeEpiGlu ? 0 : (grp - g_lo) * NTB;
+      compute_unit<NTB, true>(ring + slot_ring * kUnitBytes, xs + (size_t)blk * (k / 64) * 256,
+                              gs + (size_t)blk * kb * 64, p, kbi, lane, acc);
     }
     __syncwarp();
     if (lane == 0 && j + S < n) issue(j + S, slot_ring);
     if (++slot_ring == S) slot_ring = 0, phase ^= 1u;
     if (kbi + 1 == kb) {
-      // whole tile done: epilogue (skipped slots write zeros)
-      const int g = lane >> 2, q = lane & 3;
-      uint16_t *y = p.y + (size_t)slot * p.y_slot_stride;
-      if (EPI == kMoeEpiGlu) {
-        const int col = tile * 8 + g;
+      // whole tile done: epilogue for the tokens of this group
+      const uint32_t mask = p.group_mask[grp];
+#pragma unroll
+      for (int tb = 0; tb < NTB; ++tb) {
 #pragma unroll
         for (int e2 = 0; e2 < 2; ++e2) {
-          const int t = 2 * q + e2;
-          if (t < p.tokens) {
+          const int t = tb * 8 + 2 * qd + e2;
+          if (t >= p.T || !((mask >> t) & 1u)) continue;
+          if (EPI == kMoeEpiGlu) {
             float v = 0.f;
             if (live) {
-              const float gate = bf16_round(acc.v[0][e2]);
-              const float up = bf16_round(acc.v[0][2 + e2]);
+              const float gate = bf16_round(acc.v[tb][e2]);
+              const float up = bf16_round(acc.v[tb][2 + e2]);
               v = p.act == RC_ACT_SITU ? act_situ(gate, up, p.gate_beta, p.value_beta) : act_swiglu(gate, up);
             }
-            y[(size_t)t * p.ldy + col] = f32_to_bf16_rne(v);
+            p.y[((size_t)grp * 8 * NTB + t) * p.ldy + tile * 8 + g] = f32_to_bf16_rne(v);
+          } else {
+            uint16_t *y = p.y + (size_t)p.group_dst[grp * kMoeMaxTokens + t] * p.ldy + tile * kUnitRows + g;
+            y[0] = live ? f32_to_bf16_rne(acc.v[tb][e2]) : (uint16_t)0;
+            y[8] = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : (uint16_t)0;
           }
-        }
-      } else {
-        const int c = slot & 7;
-        if (q == (c >> 1)) {
-          const int r0 = tile * kUnitRows + g;
-          y[r0] = f32_to_bf16_rne(acc.v[0][c & 1]);
-          y[r0 + 8] = f32_to_bf16_rne(acc.v[0][2 + (c & 1)]);
         }
       }
       acc_zero(acc);
@@ -344,24 +454,45 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
   }
 }
 
-// ---------------------------------------------------------------- combine --
-// out = RTNE(sum_{slots in ascending ID} f32(down[s]) * w[s]); with a shared
-// expert (slot k) out = RTNE(f32(out) + f32(down[k])).  routed_out (optional)
-// receives the routed sum alone (the Backend.moe_experts contract).
-__global__ void moe_combine_kernel(const uint16_t *down, long long slot_stride, const float *slot_w, int k,
-                                   int with_shared, int hidden, uint16_t *out, uint16_t *routed_out) {
+// Shared-expert activations from caller-supplied gate|up rows [T][2*inter]
+// (the grouped boundary): act[g_shared][t][c] = RTNE(act(gu[t][c], gu[t][inter + c]))
+// for c < inter; the pad columns of act stay zero.
+__global__ void moe_shared_act_kernel(const uint16_t *gu, int T, int inter, int inter_pad, const int *n_groups,
+                                      int rows_per_group, int act, float gb, float vb, uint16_t *act_out) {
   pdl_launch_dependents();
   pdl_wait_prior();
+  const int t = blockIdx.y;
+  uint16_t *dst = act_out + ((size_t)(*n_groups - 1) * rows_per_group + t) * inter_pad;
+  const uint16_t *src = gu + (size_t)t * 2 * inter;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < inter; c += gridDim.x * blockDim.x) {
+    const float gate = bf16_to_f32(src[c]), up = bf16_to_f32(src[inter + c]);
+    dst[c] = f32_to_bf16_rne(act == RC_ACT_SITU ? act_situ(gate, up, gb, vb) : act_swiglu(gate, up));
+  }
+}
+
+// ---------------------------------------------------------------- combine --
+// Per token t: routed = RTNE(sum_{slots in ascending ID} f32(down[t][s]) * w[t][s]);
+// out = routed, or RTNE(f32(routed) + f32(down[t][k])) with the shared expert.
+// routed_out / shared_out (optional) receive the routed sum and the shared
+// expert's row (the grouped boundary returns them apart).
+__global__ void moe_combine_kernel(const uint16_t *down, const float *slot_w, int k, int with_shared, int hidden,
+                                   uint16_t *out, uint16_t *routed_out, uint16_t *shared_out) {
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  const int t = blockIdx.y;
+  const uint16_t *rows = down + (size_t)t * (k + 1) * hidden;
+  const float *w = slot_w + (size_t)t * k;
   for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < hidden; h += gridDim.x * blockDim.x) {
     float acc = 0.f;
     // product rounded, then sum rounded -- as the reference's f32 numpy update
     // (no fused multiply-add contraction)
-    for (int s = 0; s < k; ++s)
-      acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(down[(size_t)s * slot_stride + h]), slot_w[s]));
+    for (int s = 0; s < k; ++s) acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(rows[(size_t)s * hidden + h]), w[s]));
     const uint16_t routed = f32_to_bf16_rne(acc);
-    if (routed_out) routed_out[h] = routed;
+    const size_t o = (size_t)t * hidden + h;
+    if (routed_out) routed_out[o] = routed;
+    if (shared_out) shared_out[o] = rows[(size_t)k * hidden + h];
     if (out) {
-      out[h] = with_shared ? f32_to_bf16_rne(bf16_to_f32(routed) + bf16_to_f32(down[(size_t)k * slot_stride + h]))
+      out[o] = with_shared ? f32_to_bf16_rne(bf16_to_f32(routed) + bf16_to_f32(rows[(size_t)k * hidden + h]))
                            : routed;
     }
   }
@@ -381,47 +512,51 @@ struct rc_moe {
   const uint8_t **dn_tiles;
   uint16_t *router_w;         // [E][hidden] bf16
   float *router_bias;         // [E]
-  // per-call scratch
-  float *logits;              // [16][E]
-  int *route_counter;         // [16]
-  int32_t *ids, *slot_expert; // [16][kMax], [16][kMax+1]
-  float *weights, *slot_w;
-  uint16_t *act;              // [kMax+1][inter_pad]  (pad columns stay zero)
-  uint16_t *down_out;         // [kMax+1][hidden]
+  MoeScratch s;
+  uint16_t *act;              // [E+1][16][inter_pad]  (pad columns stay zero)
+  uint16_t *down_out;         // [16][kMax+1][hidden]
 };
 
 namespace rc {
 
-static int moe_stages(int ntb, int k, int units_per_warp) {
+static size_t moe_smem_bytes(int stage_blocks, int k, int stages) {
+  return (size_t)kMoeWarps * stages * (kUnitBytes + 8) + xfrag_bytes(stage_blocks, k) + gsum_bytes(stage_blocks, k);
+}
+
+static int moe_stages(int stage_blocks, int k, int units_per_warp) {
   int s = units_per_warp < 2 ? 2 : (units_per_warp > kMoeMaxStages ? kMoeMaxStages : units_per_warp);
-  auto bytes = [&](int st) {
-    return (size_t)kMoeWarps * st * (kUnitBytes + 8) + xfrag_bytes(ntb, k) + gsum_bytes(ntb, k);
-  };
-  while (s > 2 && bytes(s) > (size_t)kGemvSmemLimit) --s;
+  while (s > 2 && moe_smem_bytes(stage_blocks, k, s) > (size_t)kGemvSmemLimit) --s;
   return s;
 }
 
-template <int EPI>
-static cudaError_t launch_moe_gemv(const rc_ctx *ctx, MoeGemvParams p, cudaStream_t s) {
+template <int EPI, int NTB>
+static cudaError_t launch_moe_gemv_t(const rc_ctx *ctx, MoeGemvParams p, int max_groups, cudaStream_t s) {
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (!configured[dev]) {
-    e = cudaFuncSetAttribute(moe_gemv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemLimit);
+  if (dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(moe_gemv_kernel<EPI, NTB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kGemvSmemLimit);
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    if (dev < 64) configured[dev] = true;
   }
-  const int total_tiles = p.n_slots * p.slot_tiles;
-  int grid = (total_tiles + kMoeWarps - 1) / kMoeWarps;
+  const int max_tiles = max_groups * p.group_tiles;
+  int grid = (max_tiles + kMoeWarps - 1) / kMoeWarps;
   if (grid > ctx->sm_count) grid = ctx->sm_count;
+  if (grid < 1) grid = 1;
+  if (EPI == kMoeEpiDown) {
+    // a CTA's contiguous range of `per` tiles touches at most
+    // kMoeMaxGroupsPerCta groups when per - 1 <= (kMoeMaxGroupsPerCta - 1) * group_tiles
+    while ((max_tiles + grid - 1) / grid - 1 > (kMoeMaxGroupsPerCta - 1) * p.group_tiles) grid *= 2;
+  }
   const int W = grid * kMoeWarps;
-  const int tiles_per_warp = (total_tiles + W - 1) / W;
-  const int ntb = (p.slots + 7) / 8;
+  const int tiles_per_warp = (max_tiles + W - 1) / W;
+  const int stage_blocks = EPI == kMoeEpiGlu ? NTB : NTB * kMoeMaxGroupsPerCta;
   const int k = p.kb * kUnitK;
-  p.stages = moe_stages(ntb, k, tiles_per_warp * p.kb);
-  const size_t smem =
-      (size_t)kMoeWarps * p.stages * (kUnitBytes + 8) + xfrag_bytes(ntb, k) + gsum_bytes(ntb, k);
+  p.stages = moe_stages(stage_blocks, k, tiles_per_warp * p.kb);
+  const size_t smem = moe_smem_bytes(stage_blocks, k, p.stages);
+  if (smem > (size_t)kGemvSmemLimit) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kMoeWarps * 32);
@@ -432,7 +567,13 @@ static cudaError_t launch_moe_gemv(const rc_ctx *ctx, MoeGemvParams p, cudaStrea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, moe_gemv_kernel<EPI>, p);
+  return cudaLaunchKernelEx(&cfg, moe_gemv_kernel<EPI, NTB>, p);
+}
+
+template <int EPI>
+static cudaError_t launch_moe_gemv(const rc_ctx *ctx, const MoeGemvParams &p, int max_groups, cudaStream_t s) {
+  return p.T <= 8 ? launch_moe_gemv_t<EPI, 1>(ctx, p, max_groups, s)
+                  : launch_moe_gemv_t<EPI, 2>(ctx, p, max_groups, s);
 }
 
 static cudaLaunchConfig_t small_cfg(dim3 grid, dim3 block, cudaStream_t s, cudaLaunchAttribute *attr) {
@@ -447,47 +588,71 @@ static cudaLaunchConfig_t small_cfg(dim3 grid, dim3 block, cudaStream_t s, cudaL
   return cfg;
 }
 
-// Experts of one token for an already prepared slot list (slot_expert / slot_w
-// on the device): gate/up GEMV with the GLU epilogue, then the down GEMV into
-// down_out[slot].  n_slots = k (+1 with the shared expert).
-static int moe_run_experts(rc_moe *m, const uint16_t *x, int n_slots, int act, float gb, float vb, cudaStream_t s) {
+// Upper bound of the group count, for launch sizing only (the kernels read the
+// real count from the device).
+static int max_groups(int T, int k, const MoeOwned &own) {
+  const int owned = own.hi - own.lo;
+  const int routed = T * k < owned ? T * k : owned;
+  return routed + (own.shared_mask ? 1 : 0);
+}
+
+// gate/up with the GLU epilogue (the shared group's activations come from
+// shared_gu instead when it is given), then the down GEMV into down_out
+// [T][k+1][hidden].
+static int moe_run_experts(rc_moe *m, const uint16_t *x, int T, int k, const MoeOwned &own, int act, float gb,
+                           float vb, const uint16_t *shared_gu, uint16_t *down_out, cudaStream_t s) {
+  const int ntb = T <= 8 ? 1 : 2;
+  const int mg = max_groups(T, k, own);
+  if (mg == 0) return RC_OK;
   MoeGemvParams g{};
   g.expert_tiles = m->gu_tiles;
-  g.slot_expert = m->slot_expert;
-  g.n_slots = n_slots;
-  g.slot_tiles = m->inter / 8;              // interleaved gate/up: 8 intermediate columns per tile
+  g.n_groups = m->s.n_groups;
+  g.group_expert = m->s.group_expert;
+  g.group_mask = m->s.group_mask;
+  g.group_dst = m->s.group_dst;
+  g.skip_last_group = shared_gu && own.shared_mask ? 1 : 0;
+  g.group_tiles = m->inter / 8;              // interleaved gate/up: 8 intermediate columns per tile
   g.kb = m->hidden / kUnitK;
+  g.T = T;
   g.x = x;
   g.x_dtype = RC_DTYPE_BF16;
   g.ldx = m->hidden;
-  g.tokens = 1;
-  g.slots = 1;
+  g.tokens = T;
+  g.slots = T;
   g.x_vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (m->hidden * 2) % 16 == 0;
   g.y = m->act;
-  g.y_slot_stride = m->inter_pad;
   g.ldy = m->inter_pad;
   g.act = act;
   g.gate_beta = gb;
   g.value_beta = vb;
   g.err = m->ctx->err;
-  cudaError_t e = launch_moe_gemv<kMoeEpiGlu>(m->ctx, g, s);
+  cudaError_t e = cudaSuccess;
+  if (mg - g.skip_last_group > 0) e = launch_moe_gemv<kMoeEpiGlu>(m->ctx, g, mg - g.skip_last_group, s);
   if (e != cudaSuccess) {
     set_error("moe gate/up launch: %s", cudaGetErrorString(e));
     return RC_ERR_CUDA;
   }
+  if (g.skip_last_group) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = small_cfg(dim3((m->inter + 255) / 256, T), dim3(256), s, attr);
+    e = cudaLaunchKernelEx(&cfg, moe_shared_act_kernel, shared_gu, T, m->inter, m->inter_pad,
+                           (const int *)m->s.n_groups, 8 * ntb, act, gb, vb, m->act);
+    if (e != cudaSuccess) {
+      set_error("moe shared activation launch: %s", cudaGetErrorString(e));
+      return RC_ERR_CUDA;
+    }
+  }
   MoeGemvParams d = g;
   d.expert_tiles = m->dn_tiles;
-  d.slot_tiles = m->hidden / kUnitRows;
+  d.skip_last_group = 0;
+  d.group_tiles = m->hidden / kUnitRows;
   d.kb = m->inter_pad / kUnitK;
   d.x = m->act;
   d.ldx = m->inter_pad;
-  d.tokens = n_slots;
-  d.slots = n_slots;
   d.x_vec = 1;
-  d.y = m->down_out;
-  d.y_slot_stride = m->hidden;
+  d.y = down_out;
   d.ldy = m->hidden;
-  e = launch_moe_gemv<kMoeEpiDown>(m->ctx, d, s);
+  e = launch_moe_gemv<kMoeEpiDown>(m->ctx, d, mg, s);
   if (e != cudaSuccess) {
     set_error("moe down launch: %s", cudaGetErrorString(e));
     return RC_ERR_CUDA;
@@ -495,12 +660,12 @@ static int moe_run_experts(rc_moe *m, const uint16_t *x, int n_slots, int act, f
   return RC_OK;
 }
 
-static int moe_combine(rc_moe *m, const uint16_t *down, const float *slot_w, int k, int with_shared, uint16_t *out,
-                       uint16_t *routed_out, cudaStream_t s) {
+static int moe_combine(rc_moe *m, const uint16_t *down, const float *slot_w, int T, int k, int with_shared,
+                       uint16_t *out, uint16_t *routed_out, uint16_t *shared_out, cudaStream_t s) {
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = small_cfg(dim3((m->hidden + 255) / 256), dim3(256), s, attr);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_combine_kernel, down, (long long)m->hidden, slot_w, k,
-                                           with_shared, m->hidden, out, routed_out);
+  cudaLaunchConfig_t cfg = small_cfg(dim3((m->hidden + 255) / 256, T), dim3(256), s, attr);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_combine_kernel, down, slot_w, k, with_shared, m->hidden, out,
+                                           routed_out, shared_out);
   if (e != cudaSuccess) {
     set_error("moe combine launch: %s", cudaGetErrorString(e));
     return RC_ERR_CUDA;
@@ -509,7 +674,7 @@ static int moe_combine(rc_moe *m, const uint16_t *down, const float *slot_w, int
 }
 
 static int moe_route(rc_moe *m, const uint16_t *x, int T, int k, int mode, int renorm, float scaling,
-                     cudaStream_t s) {
+                     const MoeOwned &own, cudaStream_t s) {
   RouteParams r{};
   r.x = x;
   r.ldx = m->hidden;
@@ -522,13 +687,9 @@ static int moe_route(rc_moe *m, const uint16_t *x, int T, int k, int mode, int r
   r.scaling = scaling;
   r.wr = m->router_w;
   r.bias = m->router_bias;
-  r.logits = m->logits;
-  r.counter = m->route_counter;
-  r.ids = m->ids;
-  r.weights = m->weights;
-  r.slot_expert = m->slot_expert;
-  r.slot_w = m->slot_w;
+  r.s = m->s;
   r.shared_id = m->has_shared ? m->n_experts : -1;
+  r.own = own;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = small_cfg(
       dim3((m->n_experts + kRouteExpertsPerCta - 1) / kRouteExpertsPerCta, T), dim3(kRouteThreads), s, attr);
@@ -540,6 +701,40 @@ static int moe_route(rc_moe *m, const uint16_t *x, int T, int k, int mode, int r
   return RC_OK;
 }
 
+static int moe_slots(rc_moe *m, const int32_t *ids, const float *w, int T, int k, const MoeOwned &own,
+                     cudaStream_t s) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = small_cfg(dim3(1), dim3(32), s, attr);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_slots_kernel, ids, w, T, k, m->n_experts,
+                                           m->has_shared ? m->n_experts : -1, own, m->s);
+  if (e != cudaSuccess) {
+    set_error("moe slot list launch: %s", cudaGetErrorString(e));
+    return RC_ERR_CUDA;
+  }
+  return RC_OK;
+}
+
+static uint32_t token_mask(int t0, int tn) {
+  uint32_t m = 0;
+  for (int t = t0; t < t0 + tn; ++t) m |= 1u << t;
+  return m;
+}
+
+static int check_loaded(const rc_moe *m, const MoeOwned &own) {
+  for (int e = own.lo; e < own.hi; ++e)
+    RC_CHECK_ARG(m->gate_up[e] != nullptr, "expert %d is in the computed range but not loaded", e);
+  RC_CHECK_ARG(!own.shared_mask || m->gate_up[m->n_experts] != nullptr, "the shared expert is not loaded");
+  return RC_OK;
+}
+
+static MoeOwned all_owned(const rc_moe *m, int T, int with_shared) {
+  MoeOwned o;
+  o.lo = 0;
+  o.hi = m->n_experts;
+  o.shared_mask = with_shared ? token_mask(0, T) : 0u;
+  return o;
+}
+
 }  // namespace rc
 
 extern "C" {
@@ -549,7 +744,8 @@ int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_sha
   *out = nullptr;
   RC_CHECK_ARG(hidden > 0 && hidden % 256 == 0, "hidden (%d) must be a multiple of 256", hidden);
   RC_CHECK_ARG(inter > 0 && inter % 64 == 0, "intermediate size (%d) must be a multiple of 64", inter);
-  RC_CHECK_ARG(n_experts > 0 && n_experts <= 256, "n_experts (%d) must be in 1..256", n_experts);
+  RC_CHECK_ARG(n_experts > 0 && n_experts <= kMoeMaxExperts, "n_experts (%d) must be in 1..%d", n_experts,
+               kMoeMaxExperts);
   RC_CUDA_TRY(cudaSetDevice(ctx->device));
   rc_moe *m = new rc_moe();
   m->ctx = ctx;
@@ -561,6 +757,7 @@ int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_sha
   const int ne = n_experts + 1;
   m->gate_up = new rc_weight *[ne]();
   m->down = new rc_weight *[ne]();
+  const int T = kMoeMaxTokens, K = kMoeMaxK;
   cudaError_t e = cudaMalloc(&m->gu_tiles, ne * sizeof(void *));
   if (e == cudaSuccess) e = cudaMalloc(&m->dn_tiles, ne * sizeof(void *));
   if (e == cudaSuccess) e = cudaMemset(m->gu_tiles, 0, ne * sizeof(void *));
@@ -568,16 +765,21 @@ int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_sha
   if (e == cudaSuccess) e = cudaMalloc(&m->router_w, (size_t)n_experts * hidden * 2);
   if (e == cudaSuccess) e = cudaMalloc(&m->router_bias, (size_t)n_experts * 4);
   if (e == cudaSuccess) e = cudaMemset(m->router_bias, 0, (size_t)n_experts * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&m->logits, (size_t)kMoeMaxK * n_experts * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&m->route_counter, kMoeMaxK * 4);
-  if (e == cudaSuccess) e = cudaMemset(m->route_counter, 0, kMoeMaxK * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&m->ids, kMoeMaxK * kMoeMaxK * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&m->weights, kMoeMaxK * kMoeMaxK * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&m->slot_expert, kMoeMaxK * (kMoeMaxK + 1) * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&m->slot_w, kMoeMaxK * kMoeMaxK * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&m->act, (size_t)(kMoeMaxK + 1) * m->inter_pad * 2);
-  if (e == cudaSuccess) e = cudaMemset(m->act, 0, (size_t)(kMoeMaxK + 1) * m->inter_pad * 2);
-  if (e == cudaSuccess) e = cudaMalloc(&m->down_out, (size_t)(kMoeMaxK + 1) * hidden * 2);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.logits, (size_t)T * n_experts * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.counter, (T + 1) * 4);
+  if (e == cudaSuccess) e = cudaMemset(m->s.counter, 0, (T + 1) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.ids, T * K * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.weights, T * K * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.slot_expert, T * (K + 1) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.slot_w, T * K * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.n_groups, 4);
+  if (e == cudaSuccess) e = cudaMemset(m->s.n_groups, 0, 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.group_expert, ne * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.group_mask, ne * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->s.group_dst, (size_t)ne * kMoeMaxTokens * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->act, (size_t)ne * T * m->inter_pad * 2);
+  if (e == cudaSuccess) e = cudaMemset(m->act, 0, (size_t)ne * T * m->inter_pad * 2);
+  if (e == cudaSuccess) e = cudaMalloc(&m->down_out, (size_t)T * (K + 1) * hidden * 2);
   if (e != cudaSuccess) {
     set_error("rc_moe_create: %s", cudaGetErrorString(e));
     rc_moe_destroy(m);
@@ -601,12 +803,16 @@ int rc_moe_destroy(rc_moe *m) {
   cudaFree(m->dn_tiles);
   cudaFree(m->router_w);
   cudaFree(m->router_bias);
-  cudaFree(m->logits);
-  cudaFree(m->route_counter);
-  cudaFree(m->ids);
-  cudaFree(m->weights);
-  cudaFree(m->slot_expert);
-  cudaFree(m->slot_w);
+  cudaFree(m->s.logits);
+  cudaFree(m->s.counter);
+  cudaFree(m->s.ids);
+  cudaFree(m->s.weights);
+  cudaFree(m->s.slot_expert);
+  cudaFree(m->s.slot_w);
+  cudaFree(m->s.n_groups);
+  cudaFree(m->s.group_expert);
+  cudaFree(m->s.group_mask);
+  cudaFree(m->s.group_dst);
   cudaFree(m->act);
   cudaFree(m->down_out);
   delete m;
@@ -644,64 +850,73 @@ int rc_moe_set_router(rc_moe *m, const uint16_t *router_w, const float *bias) {
   return RC_OK;
 }
 
+#define RC_MOE_CHECK_TK(fn)                                                                              \
+  RC_CHECK_ARG(T >= 1 && T <= kMoeMaxTokens, fn ": T must be 1..%d", kMoeMaxTokens);                    \
+  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK && k <= m->n_experts, fn ": k must be 1..%d and <= n_experts", \
+               kMoeMaxK)
+
 int rc_moe_route(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
                  int32_t *ids_dev, float *w_dev, float *logits_dev, void *stream) {
   RC_CHECK_ARG(m && x_dev, "rc_moe_route: NULL argument");
-  RC_CHECK_ARG(T >= 1 && T <= kMoeMaxK, "rc_moe_route: T must be 1..%d", kMoeMaxK);
-  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK && k <= m->n_experts, "rc_moe_route: k must be 1..%d", kMoeMaxK);
+  RC_MOE_CHECK_TK("rc_moe_route");
   RC_CHECK_ARG(router == RC_ROUTER_SOFTMAX || router == RC_ROUTER_SIGMOID_BIAS, "unknown router %d", router);
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   const cudaStream_t s = pick_stream(m->ctx, stream);
-  int rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, s);
+  int rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, all_owned(m, T, m->has_shared), s);
   if (rc) return rc;
-  if (ids_dev) RC_CUDA_TRY(cudaMemcpyAsync(ids_dev, m->ids, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
-  if (w_dev) RC_CUDA_TRY(cudaMemcpyAsync(w_dev, m->weights, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
+  if (ids_dev) RC_CUDA_TRY(cudaMemcpyAsync(ids_dev, m->s.ids, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
+  if (w_dev) RC_CUDA_TRY(cudaMemcpyAsync(w_dev, m->s.weights, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
   if (logits_dev)
-    RC_CUDA_TRY(cudaMemcpyAsync(logits_dev, m->logits, (size_t)T * m->n_experts * 4, cudaMemcpyDeviceToDevice, s));
+    RC_CUDA_TRY(cudaMemcpyAsync(logits_dev, m->s.logits, (size_t)T * m->n_experts * 4, cudaMemcpyDeviceToDevice, s));
   return RC_OK;
 }
 
-int rc_moe_experts(rc_moe *m, const uint16_t *x_dev, const int32_t *ids_dev, const float *w_dev, int k, int act,
-                   float gate_beta, float value_beta, int with_shared, uint16_t *out_dev, void *stream) {
+int rc_moe_experts(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev, const float *w_dev, int k,
+                   int act, float gate_beta, float value_beta, int with_shared, uint16_t *out_dev, void *stream) {
   RC_CHECK_ARG(m && x_dev && ids_dev && w_dev && out_dev, "rc_moe_experts: NULL argument");
-  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK, "rc_moe_experts: k must be 1..%d", kMoeMaxK);
+  RC_MOE_CHECK_TK("rc_moe_experts");
   RC_CHECK_ARG(act == RC_ACT_SWIGLU || act == RC_ACT_SITU, "unknown activation %d", act);
   RC_CHECK_ARG(!with_shared || m->has_shared, "this MoE layer has no shared expert");
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   const cudaStream_t s = pick_stream(m->ctx, stream);
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = small_cfg(dim3(1), dim3(32), s, attr);
-  RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_slots_kernel, ids_dev, w_dev, k, with_shared ? m->n_experts : -1,
-                                 m->slot_expert, m->slot_w));
-  int rc = moe_run_experts(m, x_dev, k + (with_shared ? 1 : 0), act, gate_beta, value_beta, s);
+  const MoeOwned own = all_owned(m, T, with_shared);
+  int rc = moe_slots(m, ids_dev, w_dev, T, k, own, s);
   if (rc) return rc;
-  return moe_combine(m, m->down_out, m->slot_w, k, with_shared, out_dev, nullptr, s);
+  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, m->down_out, s);
+  if (rc) return rc;
+  return moe_combine(m, m->down_out, m->s.slot_w, T, k, with_shared, out_dev, nullptr, nullptr, s);
 }
 
-int rc_moe_experts_host(rc_moe *m, const uint16_t *x_host, const int32_t *ids_host, const float *w_host, int k,
-                        int act, float gate_beta, float value_beta, int with_shared, uint16_t *out_host) {
+int rc_moe_experts_host(rc_moe *m, const uint16_t *x_host, int T, const int32_t *ids_host, const float *w_host,
+                        int k, int act, float gate_beta, float value_beta, int with_shared, uint16_t *out_host) {
   RC_CHECK_ARG(m && x_host && ids_host && w_host && out_host, "rc_moe_experts_host: NULL argument");
-  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK, "rc_moe_experts_host: k must be 1..%d", kMoeMaxK);
-  for (int r = 0; r < k; ++r) {
-    RC_CHECK_ARG(ids_host[r] >= 0 && ids_host[r] < m->n_experts, "expert id %d out of range 0..%d", ids_host[r],
-                 m->n_experts - 1);
-    RC_CHECK_ARG(m->gate_up[ids_host[r]] != nullptr, "expert %d is not loaded", ids_host[r]);
+  RC_MOE_CHECK_TK("rc_moe_experts_host");
+  for (int t = 0; t < T; ++t) {
+    for (int r = 0; r < k; ++r) {
+      const int e = ids_host[t * k + r];
+      RC_CHECK_ARG(e >= 0 && e < m->n_experts, "expert id %d out of range 0..%d", e, m->n_experts - 1);
+      RC_CHECK_ARG(m->gate_up[e] != nullptr, "expert %d is not loaded", e);
+      for (int r2 = 0; r2 < r; ++r2)
+        RC_CHECK_ARG(ids_host[t * k + r2] != e, "token %d routes to expert %d twice", t, e);
+    }
   }
+  RC_CHECK_ARG(!with_shared || (m->has_shared && m->gate_up[m->n_experts]), "the shared expert is not loaded");
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   rc_ctx *ctx = m->ctx;
-  const size_t xb = (size_t)m->hidden * 2 + kMoeMaxK * 8, yb = (size_t)m->hidden * 2;
+  const size_t x_bytes = (size_t)T * m->hidden * 2, id_bytes = (size_t)T * k * 4;
+  const size_t off_ids = (x_bytes + 15) / 16 * 16, off_w = off_ids + (id_bytes + 15) / 16 * 16;
+  const size_t xb = off_w + id_bytes, yb = (size_t)T * m->hidden * 2;
   int rc = ensure_host_staging(ctx, xb, yb);
   if (rc) return rc;
   uint8_t *px = static_cast<uint8_t *>(ctx->pin_x);
-  memcpy(px, x_host, (size_t)m->hidden * 2);
-  memcpy(px + (size_t)m->hidden * 2, ids_host, (size_t)k * 4);
-  memcpy(px + (size_t)m->hidden * 2 + kMoeMaxK * 4, w_host, (size_t)k * 4);
+  memcpy(px, x_host, x_bytes);
+  memcpy(px + off_ids, ids_host, id_bytes);
+  memcpy(px + off_w, w_host, id_bytes);
   uint8_t *dx = static_cast<uint8_t *>(ctx->dev_x);
   RC_CUDA_TRY(cudaMemcpyAsync(dx, px, xb, cudaMemcpyHostToDevice, ctx->stream));
-  rc = rc_moe_experts(m, reinterpret_cast<const uint16_t *>(dx),
-                      reinterpret_cast<const int32_t *>(dx + (size_t)m->hidden * 2),
-                      reinterpret_cast<const float *>(dx + (size_t)m->hidden * 2 + kMoeMaxK * 4), k, act, gate_beta,
-                      value_beta, with_shared, static_cast<uint16_t *>(ctx->dev_y), nullptr);
+  rc = rc_moe_experts(m, reinterpret_cast<const uint16_t *>(dx), T, reinterpret_cast<const int32_t *>(dx + off_ids),
+                      reinterpret_cast<const float *>(dx + off_w), k, act, gate_beta, value_beta, with_shared,
+                      static_cast<uint16_t *>(ctx->dev_y), nullptr);
   if (rc) return rc;
   RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, yb, cudaMemcpyDeviceToHost, ctx->stream));
   RC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
@@ -711,50 +926,86 @@ int rc_moe_experts_host(rc_moe *m, const uint16_t *x_host, const int32_t *ids_ho
   return RC_OK;
 }
 
-int rc_moe_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int renormalize, float scaling, int act,
-                  float gate_beta, float value_beta, uint16_t *out_dev, int32_t *ids_dev, float *w_dev,
+int rc_moe_experts_grouped(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev, const float *w_dev,
+                           int k, const uint16_t *shared_gu_dev, int act, float gate_beta, float value_beta,
+                           uint16_t *routed_out_dev, uint16_t *shared_out_dev, void *stream) {
+  RC_CHECK_ARG(m && x_dev && ids_dev && w_dev && routed_out_dev, "rc_moe_experts_grouped: NULL argument");
+  RC_MOE_CHECK_TK("rc_moe_experts_grouped");
+  RC_CHECK_ARG(act == RC_ACT_SWIGLU || act == RC_ACT_SITU, "unknown activation %d", act);
+  RC_CHECK_ARG(!shared_gu_dev || (shared_out_dev && m->has_shared && m->down[m->n_experts]),
+               "shared_gu needs shared_out and a loaded shared expert");
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  const cudaStream_t s = pick_stream(m->ctx, stream);
+  const MoeOwned own = all_owned(m, T, shared_gu_dev != nullptr);
+  int rc = moe_slots(m, ids_dev, w_dev, T, k, own, s);
+  if (rc) return rc;
+  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, shared_gu_dev, m->down_out, s);
+  if (rc) return rc;
+  return moe_combine(m, m->down_out, m->s.slot_w, T, k, 0, nullptr, routed_out_dev,
+                     shared_gu_dev ? shared_out_dev : nullptr, s);
+}
+
+int rc_moe_decode(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
+                  int act, float gate_beta, float value_beta, uint16_t *out_dev, int32_t *ids_dev, float *w_dev,
                   void *stream) {
   RC_CHECK_ARG(m && x_dev && out_dev, "rc_moe_decode: NULL argument");
-  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK && k <= m->n_experts, "rc_moe_decode: k must be 1..%d", kMoeMaxK);
+  RC_MOE_CHECK_TK("rc_moe_decode");
   RC_CHECK_ARG(act == RC_ACT_SWIGLU || act == RC_ACT_SITU, "unknown activation %d", act);
   RC_CHECK_ARG(router == RC_ROUTER_SOFTMAX || router == RC_ROUTER_SIGMOID_BIAS, "unknown router %d", router);
+  const MoeOwned own = all_owned(m, T, m->has_shared);
+  int rc = check_loaded(m, own);
+  if (rc) return rc;
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   const cudaStream_t s = pick_stream(m->ctx, stream);
-  int rc = moe_route(m, x_dev, 1, k, router, renormalize, scaling, s);
+  rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, own, s);
   if (rc) return rc;
-  rc = moe_run_experts(m, x_dev, k + m->has_shared, act, gate_beta, value_beta, s);
+  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, m->down_out, s);
   if (rc) return rc;
-  rc = moe_combine(m, m->down_out, m->slot_w, k, m->has_shared, out_dev, nullptr, s);
+  rc = moe_combine(m, m->down_out, m->s.slot_w, T, k, m->has_shared, out_dev, nullptr, nullptr, s);
   if (rc) return rc;
-  if (ids_dev) RC_CUDA_TRY(cudaMemcpyAsync(ids_dev, m->ids, (size_t)k * 4, cudaMemcpyDeviceToDevice, s));
-  if (w_dev) RC_CUDA_TRY(cudaMemcpyAsync(w_dev, m->weights, (size_t)k * 4, cudaMemcpyDeviceToDevice, s));
+  if (ids_dev) RC_CUDA_TRY(cudaMemcpyAsync(ids_dev, m->s.ids, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
+  if (w_dev) RC_CUDA_TRY(cudaMemcpyAsync(w_dev, m->s.weights, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
   return RC_OK;
 }
 
-int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int k, int router, int renormalize, float scaling, int act,
-                        float gate_beta, float value_beta, uint16_t *slot_out_dev, float *slot_w_dev,
-                        void *stream) {
+int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
+                        int act, float gate_beta, float value_beta, int expert_lo, int expert_hi, int shared_t0,
+                        int shared_tn, uint16_t *slot_out_dev, float *slot_w_dev, void *stream) {
   RC_CHECK_ARG(m && x_dev && slot_out_dev && slot_w_dev, "rc_moe_decode_local: NULL argument");
-  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK && k <= m->n_experts, "rc_moe_decode_local: k must be 1..%d", kMoeMaxK);
+  RC_MOE_CHECK_TK("rc_moe_decode_local");
+  RC_CHECK_ARG(act == RC_ACT_SWIGLU || act == RC_ACT_SITU, "unknown activation %d", act);
+  RC_CHECK_ARG(router == RC_ROUTER_SOFTMAX || router == RC_ROUTER_SIGMOID_BIAS, "unknown router %d", router);
+  RC_CHECK_ARG(0 <= expert_lo && expert_lo <= expert_hi && expert_hi <= m->n_experts,
+               "expert range [%d, %d) outside 0..%d", expert_lo, expert_hi, m->n_experts);
+  RC_CHECK_ARG(shared_tn == 0 || (m->has_shared && shared_t0 >= 0 && shared_tn > 0 && shared_t0 + shared_tn <= T),
+               "shared token range [%d, +%d) invalid for T=%d", shared_t0, shared_tn, T);
+  MoeOwned own;
+  own.lo = expert_lo;
+  own.hi = expert_hi;
+  own.shared_mask = shared_tn ? token_mask(shared_t0, shared_tn) : 0u;
+  int rc = check_loaded(m, own);
+  if (rc) return rc;
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   const cudaStream_t s = pick_stream(m->ctx, stream);
-  int rc = moe_route(m, x_dev, 1, k, router, renormalize, scaling, s);
+  // slot rows of experts computed elsewhere stay zero, so the ranks' slot rows
+  // can be summed in the exchange (x + 0 = x exactly)
+  RC_CUDA_TRY(cudaMemsetAsync(slot_out_dev, 0, (size_t)T * (k + 1) * m->hidden * 2, s));
+  rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, own, s);
   if (rc) return rc;
-  rc = moe_run_experts(m, x_dev, k + m->has_shared, act, gate_beta, value_beta, s);
+  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, slot_out_dev, s);
   if (rc) return rc;
-  const int slots = k + m->has_shared;
-  RC_CUDA_TRY(cudaMemcpyAsync(slot_out_dev, m->down_out, (size_t)slots * m->hidden * 2, cudaMemcpyDeviceToDevice, s));
-  RC_CUDA_TRY(cudaMemcpyAsync(slot_w_dev, m->slot_w, (size_t)k * 4, cudaMemcpyDeviceToDevice, s));
+  RC_CUDA_TRY(cudaMemcpyAsync(slot_w_dev, m->s.slot_w, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
   return RC_OK;
 }
 
-int rc_moe_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int k, int with_shared,
+int rc_moe_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int T, int k, int with_shared,
                    uint16_t *out_dev, void *stream) {
   RC_CHECK_ARG(m && slot_out_dev && slot_w_dev && out_dev, "rc_moe_combine: NULL argument");
-  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK, "rc_moe_combine: k must be 1..%d", kMoeMaxK);
+  RC_MOE_CHECK_TK("rc_moe_combine");
   RC_CHECK_ARG(!with_shared || m->has_shared, "this MoE layer has no shared expert");
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
-  return moe_combine(m, slot_out_dev, slot_w_dev, k, with_shared, out_dev, nullptr, pick_stream(m->ctx, stream));
+  return moe_combine(m, slot_out_dev, slot_w_dev, T, k, with_shared, out_dev, nullptr, nullptr,
+                     pick_stream(m->ctx, stream));
 }
 
 }  // extern "C"

@@ -208,6 +208,17 @@ def _buf(packed):
     return _ptr(packed), int(packed.numel() * packed.element_size()), _lib.RC_UPLOAD_SRC_DEVICE, packed
 
 
+def _tokens(x, hidden: int) -> int:
+    """Token count of an activation tensor [T, hidden] or [hidden]."""
+    if x.dim() == 1:
+        if x.shape[0] != hidden:
+            raise ValueError(f"x must be [hidden={hidden}] or [T, hidden]")
+        return 1
+    if x.dim() != 2 or x.shape[1] != hidden or not x.is_contiguous():
+        raise ValueError(f"x must be a contiguous [T, hidden={hidden}] tensor")
+    return int(x.shape[0])
+
+
 class MoeLayer:
     """One MoE layer on the device: experts (q4nx [gate; up] + down), router.
 
@@ -271,44 +282,74 @@ class MoeLayer:
 
     def experts(self, x_dev, ids_dev, w_dev, k: int, out_dev, act: str = "situ", gate_beta: float = 4.0,
                 value_beta: float = 25.0, with_shared: bool = False, stream: int | None = None) -> None:
+        """x [T, hidden] (or [hidden]) bf16, ids / w [T, k] -> out [T, hidden]."""
         check(self.ctx.lib.rc_moe_experts(
-            self.handle, ctypes.c_void_p(_ptr(x_dev)), ctypes.c_void_p(_ptr(ids_dev)), ctypes.c_void_p(_ptr(w_dev)),
-            int(k), ACT_CODES[act], float(gate_beta), float(value_beta), int(bool(with_shared)),
-            ctypes.c_void_p(_ptr(out_dev)), ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_experts")
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), _tokens(x_dev, self.hidden), ctypes.c_void_p(_ptr(ids_dev)),
+            ctypes.c_void_p(_ptr(w_dev)), int(k), ACT_CODES[act], float(gate_beta), float(value_beta),
+            int(bool(with_shared)), ctypes.c_void_p(_ptr(out_dev)),
+            ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_experts")
 
     def experts_host(self, x: np.ndarray, ids: np.ndarray, w: np.ndarray, act: str = "situ", gate_beta: float = 4.0,
                      value_beta: float = 25.0, with_shared: bool = False) -> np.ndarray:
+        """Host arrays: x [hidden] or [T, hidden] bf16 bits, ids / w [k] or [T, k]."""
         xh = np.ascontiguousarray(x, dtype=np.uint16)
         ih = np.ascontiguousarray(ids, dtype=np.int32)
         wh = np.ascontiguousarray(w, dtype=np.float32)
-        out = np.empty(self.hidden, np.uint16)
+        T = 1 if xh.ndim == 1 else xh.shape[0]
+        k = ih.shape[-1]
+        if xh.shape[-1] != self.hidden or ih.size != T * k or wh.shape != ih.shape:
+            raise ValueError("x must be [T, hidden]; ids and weights [T, k]")
+        out = np.empty(xh.shape, np.uint16)
         check(self.ctx.lib.rc_moe_experts_host(
-            self.handle, ctypes.c_void_p(xh.ctypes.data), ctypes.c_void_p(ih.ctypes.data),
-            ctypes.c_void_p(wh.ctypes.data), int(ih.size), ACT_CODES[act], float(gate_beta), float(value_beta),
+            self.handle, ctypes.c_void_p(xh.ctypes.data), T, ctypes.c_void_p(ih.ctypes.data),
+            ctypes.c_void_p(wh.ctypes.data), int(k), ACT_CODES[act], float(gate_beta), float(value_beta),
             int(bool(with_shared)), ctypes.c_void_p(out.ctypes.data)), "rc_moe_experts_host")
         return out
+
+    def experts_grouped(self, x_dev, ids_dev, w_dev, k: int, routed_out_dev, shared_gu_dev=None,
+                        shared_out_dev=None, act: str = "situ", gate_beta: float = 4.0, value_beta: float = 25.0,
+                        stream: int | None = None) -> None:
+        """``moe_experts_grouped``: routed sums [T, hidden] and, from the shared
+        expert's gate|up rows [T, 2*inter], its down rows [T, hidden]."""
+        check(self.ctx.lib.rc_moe_experts_grouped(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), _tokens(x_dev, self.hidden), ctypes.c_void_p(_ptr(ids_dev)),
+            ctypes.c_void_p(_ptr(w_dev)), int(k), ctypes.c_void_p(_ptr(shared_gu_dev)), ACT_CODES[act],
+            float(gate_beta), float(value_beta), ctypes.c_void_p(_ptr(routed_out_dev)),
+            ctypes.c_void_p(_ptr(shared_out_dev)), ctypes.c_void_p(_stream_for(stream, x_dev, routed_out_dev))),
+            "rc_moe_experts_grouped")
 
     def decode(self, x_dev, k: int, out_dev, ids_dev=None, w_dev=None, router: str = "softmax",
                renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
                value_beta: float = 25.0, stream: int | None = None) -> None:
+        """x [T, hidden] (or [hidden]) -> out of the same shape; optional ids / w [T, k]."""
         check(self.ctx.lib.rc_moe_decode(
-            self.handle, ctypes.c_void_p(_ptr(x_dev)), int(k), ROUTER_CODES[router], int(bool(renormalize)),
-            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(_ptr(out_dev)),
-            ctypes.c_void_p(_ptr(ids_dev)), ctypes.c_void_p(_ptr(w_dev)),
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), _tokens(x_dev, self.hidden), int(k), ROUTER_CODES[router],
+            int(bool(renormalize)), float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta),
+            ctypes.c_void_p(_ptr(out_dev)), ctypes.c_void_p(_ptr(ids_dev)), ctypes.c_void_p(_ptr(w_dev)),
             ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_decode")
 
-    def decode_local(self, x_dev, k: int, slot_out_dev, slot_w_dev, router: str = "softmax",
+    def decode_local(self, x_dev, k: int, slot_out_dev, slot_w_dev, experts: tuple[int, int] | None = None,
+                     shared_tokens: tuple[int, int] | None = None, router: str = "softmax",
                      renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
                      value_beta: float = 25.0, stream: int | None = None) -> None:
+        """Expert-parallel half: slot rows [T, k+1, hidden] of the routed experts
+        in ``experts`` = [lo, hi) and of the shared expert for tokens
+        ``shared_tokens`` = (t0, count); zeros elsewhere.  Defaults: every
+        routed expert, and the shared expert (if any) for every token."""
+        T = _tokens(x_dev, self.hidden)
+        lo, hi = (0, self.n_experts) if experts is None else (int(experts[0]), int(experts[1]))
+        if shared_tokens is None:
+            shared_tokens = (0, T) if self.has_shared else (0, 0)
         check(self.ctx.lib.rc_moe_decode_local(
-            self.handle, ctypes.c_void_p(_ptr(x_dev)), int(k), ROUTER_CODES[router], int(bool(renormalize)),
-            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(_ptr(slot_out_dev)),
-            ctypes.c_void_p(_ptr(slot_w_dev)), ctypes.c_void_p(_stream_for(stream, x_dev, slot_out_dev))),
-            "rc_moe_decode_local")
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), T, int(k), ROUTER_CODES[router], int(bool(renormalize)),
+            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), lo, hi, int(shared_tokens[0]),
+            int(shared_tokens[1]), ctypes.c_void_p(_ptr(slot_out_dev)), ctypes.c_void_p(_ptr(slot_w_dev)),
+            ctypes.c_void_p(_stream_for(stream, x_dev, slot_out_dev))), "rc_moe_decode_local")
 
-    def combine(self, slot_out_dev, slot_w_dev, k: int, out_dev, with_shared: bool = True,
+    def combine(self, slot_out_dev, slot_w_dev, k: int, out_dev, tokens: int = 1, with_shared: bool = True,
                 stream: int | None = None) -> None:
+        """slot rows [T, k+1, hidden] and slot weights [T, k] -> out [T, hidden]."""
         check(self.ctx.lib.rc_moe_combine(
-            self.handle, ctypes.c_void_p(_ptr(slot_out_dev)), ctypes.c_void_p(_ptr(slot_w_dev)), int(k),
+            self.handle, ctypes.c_void_p(_ptr(slot_out_dev)), ctypes.c_void_p(_ptr(slot_w_dev)), int(tokens), int(k),
             int(bool(with_shared)), ctypes.c_void_p(_ptr(out_dev)),
             ctypes.c_void_p(_stream_for(stream, slot_out_dev, out_dev))), "rc_moe_combine")

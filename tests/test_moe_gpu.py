@@ -4,15 +4,20 @@ against the CPU oracle and the reference's own outputs.
 Bars: top-k expert ids bit-exact (lower index wins ties) and router logits
 equal to the oracle's f64-accumulated logits.  Outputs (bf16) against the
 oracle's bf16 outputs: RMS relative error <= 2e-3 (the north star's
-tolerance), and per element |y - y_ref| <= 2^-8 * m[h] + ulp(y_ref[h]) with
+tolerance), and per element |y - y_ref| <= 2^-7 * m[h] + ulp(y_ref[h]) with
 m[h] = sum_e |w_e down_e[h]| (+ |shared[h]|) (``oracle.backend.
-moe_term_magnitude``): one bf16 rounding step per accumulated term plus the
-final rounding.  Why not "bit-exact but for rare flips": both sides stage the
-reference's bf16 roundings (gate, up, act, down) but sum in different orders
-and use different exp/tanh; a 1-ulp flip of one gate/up output flips an
-activation element, which moves every down-projection output a little, so
-per-expert outputs differ by one bf16 step on many elements, and the weighted
-sum over the experts can cancel to a result smaller than its terms.
+moe_term_magnitude``): one bf16 step of every accumulated term (a step is at
+most 2^-7 of the value) plus the final rounding.
+
+Why not "bit-exact but for rare flips": both sides stage the reference's bf16
+roundings (gate, up, act, down) but sum in different orders and use different
+exp/tanh; a 1-ulp flip of one gate/up output flips an activation element,
+which moves every down-projection output a little, so per-expert outputs
+differ by one bf16 step on many elements, and the weighted sum over the
+experts can cancel to a result smaller than its terms.  What is bit-exact:
+the routing, the combine (restated by the oracle on the GPU's own expert
+rows), batch invariance (a token's bytes do not depend on the other tokens of
+the call) and expert parallelism (ranks reproduce the single-GPU bytes).
 """
 
 from __future__ import annotations
@@ -70,7 +75,7 @@ def assert_bf16_outputs_close(got, ref, magnitude=None, tol=2e-3):
     gf = q.bf16_to_f32(got).astype(np.float64)
     err = np.abs(gf - rf)
     if magnitude is not None:
-        bound = 2.0 ** -8 * magnitude + bf16_ulp_at(ref)
+        bound = 2.0 ** -7 * magnitude + bf16_ulp_at(ref)
         bad = err > bound
         assert not bad.any(), (np.nonzero(bad)[0][:8], err[bad][:8], bound[bad][:8])
     else:
@@ -301,7 +306,7 @@ def test_moe_decode_layer_config3(torch, ctx):
 
 def test_expert_parallel_halves_reproduce_single_gpu_bytes(torch, ctx):
     """Two 'ranks' on one GPU, each holding half of the experts (rank 0 also the
-    shared one): exchanging the slot rows and combining gives exactly the bytes
+    shared one): summing the slot rows and combining gives exactly the bytes
     of the single-layer decode."""
     full, wr, _ = _config3_layer(torch, ctx, n_experts=32, seed=92)
     r0, _, _ = _config3_layer(torch, ctx, n_experts=32, seed=92, owned=set(range(16)) | {32})
@@ -314,8 +319,8 @@ def test_expert_parallel_halves_reproduce_single_gpu_bytes(torch, ctx):
         full.decode(xd, 8, ref, act="swiglu")
         slots = [torch.empty((9, 2048), dtype=torch.int16, device="cuda") for _ in range(2)]
         sw = [torch.empty(8, dtype=torch.float32, device="cuda") for _ in range(2)]
-        r0.decode_local(xd, 8, slots[0], sw[0], act="swiglu")
-        r1.decode_local(xd, 8, slots[1], sw[1], act="swiglu")
+        r0.decode_local(xd, 8, slots[0], sw[0], experts=(0, 16), shared_tokens=(0, 1), act="swiglu")
+        r1.decode_local(xd, 8, slots[1], sw[1], experts=(16, 32), shared_tokens=(0, 0), act="swiglu")
         torch.cuda.synchronize()
         # each slot row is produced by exactly one rank; the other rank's row is zero
         a = slots[0].view(torch.int16)
@@ -330,3 +335,139 @@ def test_expert_parallel_halves_reproduce_single_gpu_bytes(torch, ctx):
         assert torch.equal(out, ref)
     for layer in (full, r0, r1):
         layer.close()
+
+
+def test_decode_refuses_missing_experts(torch, ctx):
+    layer, _, _ = _config3_layer(torch, ctx, n_experts=16, seed=93, owned=set(range(8)) | {16})
+    xd = torch.zeros(2048, dtype=torch.int16, device="cuda")
+    out = torch.empty(2048, dtype=torch.int16, device="cuda")
+    with pytest.raises(ValueError):
+        layer.decode(xd, 8, out, act="swiglu")
+    slots = torch.empty((9, 2048), dtype=torch.int16, device="cuda")
+    sw = torch.empty(8, dtype=torch.float32, device="cuda")
+    with pytest.raises(ValueError):
+        layer.decode_local(xd, 8, slots, sw, experts=(4, 12), act="swiglu")
+    layer.close()
+
+
+# --------------------------------------------------------- multi-token --
+@pytest.mark.parametrize("T", [2, 5, 8, 9, 16])
+def test_decode_tokens_are_batch_invariant_and_match_oracle(torch, ctx, T):
+    """T tokens in one call: every token's output and routing equal the bytes of
+    a one-token call (columns of the grouped GEMV do not interact), and match
+    the oracle within the MoE bar."""
+    layer, wr, packed = _config3_layer(torch, ctx, n_experts=32, seed=94)
+    rng = np.random.default_rng(100 + T)
+    x = q.f32_to_bf16(rng.standard_normal((T, 2048)).astype(np.float32))
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    out = torch.empty((T, 2048), dtype=torch.int16, device="cuda")
+    ids = torch.empty((T, 8), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, 8), dtype=torch.float32, device="cuda")
+    layer.decode(xd, 8, out, ids, w, act="swiglu")
+    one = torch.empty(2048, dtype=torch.int16, device="cuda")
+    for t in range(T):
+        layer.decode(xd[t], 8, one, act="swiglu")
+        torch.cuda.synchronize()
+        assert torch.equal(one, out[t]), t
+    ctx.sync()
+    got = out.cpu().numpy().view(np.uint16)
+    for t in range(min(T, 3)):
+        r_ids, r_w, _ = ob.route_softmax(x[t], wr, 8)
+        np.testing.assert_array_equal(ids[t].cpu().numpy(), r_ids)
+        experts = {int(e): _oracle_expert(packed, int(e), 2048, 768) for e in r_ids}
+        sh = ob.expert_forward(*_oracle_expert(packed, 32, 2048, 768), x[t], "swiglu")
+        ref = ob.moe_token_with_shared(ob.moe_experts(experts, x[t], r_ids, r_w, act="swiglu"), sh)
+        mag = ob.moe_term_magnitude(experts, x[t], r_ids, r_w, "swiglu", shared_down_u16=sh)
+        assert_bf16_outputs_close(got[t], ref, mag)
+    layer.close()
+
+
+@pytest.mark.parametrize("ranks,M", [(4, 1), (4, 4), (8, 2)])
+def test_expert_parallel_ranks_reproduce_single_gpu_bytes(torch, ctx, ranks, M):
+    """Expert parallelism as the multi-GPU path runs it, emulated on one GPU:
+    every rank holds experts [r*E/N, (r+1)*E/N) and the shared expert, routes
+    all N*M gathered tokens, computes its experts for all of them and the
+    shared expert for its own M tokens; the slot rows summed over ranks (the
+    reduce-scatter) and combined per rank give exactly the single-GPU bytes."""
+    E = 32
+    T = ranks * M
+    full, wr, _ = _config3_layer(torch, ctx, n_experts=E, seed=95)
+    per = E // ranks
+    layers = [_config3_layer(torch, ctx, n_experts=E, seed=95, owned=set(range(r * per, (r + 1) * per)) | {E})[0]
+              for r in range(ranks)]
+    rng = np.random.default_rng(7)
+    x = q.f32_to_bf16(rng.standard_normal((T, 2048)).astype(np.float32))
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    ref = torch.empty((T, 2048), dtype=torch.int16, device="cuda")
+    full.decode(xd, 8, ref, act="swiglu")
+    total = torch.zeros((T, 9, 2048), dtype=torch.float32, device="cuda")
+    sws = []
+    for r, layer in enumerate(layers):
+        slots = torch.empty((T, 9, 2048), dtype=torch.int16, device="cuda")
+        sw = torch.empty((T, 8), dtype=torch.float32, device="cuda")
+        layer.decode_local(xd, 8, slots, sw, experts=(r * per, (r + 1) * per), shared_tokens=(r * M, M),
+                           act="swiglu")
+        total += slots.view(torch.bfloat16).float()
+        sws.append(sw)
+    torch.cuda.synchronize()
+    summed = total.to(torch.bfloat16).view(torch.int16)
+    for r, layer in enumerate(layers):
+        assert torch.equal(sws[r], sws[0])
+        out = torch.empty((M, 2048), dtype=torch.int16, device="cuda")
+        layer.combine(summed[r * M:(r + 1) * M].contiguous(), sws[r][r * M:(r + 1) * M].contiguous(), 8, out,
+                      tokens=M, with_shared=True)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref[r * M:(r + 1) * M]), r
+    ctx.sync()
+    for layer in [full] + layers:
+        layer.close()
+
+
+def test_experts_multi_token_matches_oracle(torch, ctx):
+    """rc_moe_experts with caller ids for T = 6 tokens, overlapping expert choices."""
+    d = cases.moe_inputs(hidden=2048, inter=768, experts=16, k=8, tokens=6, seed=62)
+    layer = make_layer(ctx, d)
+    out = layer.experts_host(d["x"], d["top_ids"], d["top_w"], act="swiglu")
+    for t in range(6):
+        ref = ob.moe_experts(d["experts"], d["x"][t], d["top_ids"][t], d["top_w"][t], act="swiglu")
+        mag = ob.moe_term_magnitude(d["experts"], d["x"][t], d["top_ids"][t], d["top_w"][t], "swiglu")
+        assert_bf16_outputs_close(out[t], ref, mag)
+        one = layer.experts_host(d["x"][t], d["top_ids"][t], d["top_w"][t], act="swiglu")
+        np.testing.assert_array_equal(one, out[t])
+    with pytest.raises(ValueError):
+        bad = d["top_ids"].copy()
+        bad[2, 1] = bad[2, 0]
+        layer.experts_host(d["x"], bad, d["top_w"], act="swiglu")
+    layer.close()
+
+
+def test_experts_grouped_matches_oracle(torch, ctx):
+    """``moe_experts_grouped``: routed sums and the shared expert's down rows from
+    caller-supplied shared gate|up rows (SiTU), T = 4."""
+    d = cases.moe_inputs(hidden=2048, inter=768, experts=16, k=8, tokens=4, seed=63)
+    rng = np.random.default_rng(64)
+    dn = (rng.standard_normal((2048, 768)) * 0.02).astype(np.float32)
+    gu_dummy = (rng.standard_normal((2 * 768, 2048)) * 0.02).astype(np.float32)
+    p_dn, f_dn = cases.q4nx_weight(dn, q)
+    p_gu, _ = cases.q4nx_weight(gu_dummy, q)
+    layer = make_layer(ctx, d, has_shared=True, shared=(p_gu, p_dn))
+    shared_gu = q.f32_to_bf16((rng.standard_normal((4, 2 * 768)) * 2).astype(np.float32))
+    dev = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).view(dt)).cuda()
+    xd = dev(d["x"], np.int16)
+    ids = dev(d["top_ids"].astype(np.int32), np.int32)
+    w = dev(d["top_w"].astype(np.float32), np.float32)
+    sgu = dev(shared_gu, np.int16)
+    routed = torch.empty((4, 2048), dtype=torch.int16, device="cuda")
+    shared = torch.empty((4, 2048), dtype=torch.int16, device="cuda")
+    layer.experts_grouped(xd, ids, w, 8, routed, sgu, shared, act="situ")
+    torch.cuda.synchronize()
+    ctx.sync()
+    r_ref, s_ref = ob.moe_experts_grouped(d["experts"], f_dn, d["x"], d["top_ids"], d["top_w"], shared_gu,
+                                          act="situ")
+    got_r = routed.cpu().numpy().view(np.uint16)
+    got_s = shared.cpu().numpy().view(np.uint16)
+    for t in range(4):
+        mag = ob.moe_term_magnitude(d["experts"], d["x"][t], d["top_ids"][t], d["top_w"][t], "situ")
+        assert_bf16_outputs_close(got_r[t], r_ref[t], mag)
+        assert rms_rel(got_s[t], s_ref[t]) <= 2.0 ** -8
+    layer.close()
