@@ -14,6 +14,15 @@ Metric: q4nx GEMV HBM GB/s = algorithmic bytes (N*K*5/8 packed weights +
 step reads a different copy of its matrix and a step streams ~1 GB, far more
 than the 126 MB L2, so no timed GEMV is served from L2.
 
+The line also carries ``moe``: the config-3 MoE decode layer (BASELINE
+configs[2]; hidden 2048, 128 experts + 1 shared, top-8 softmax router, SwiGLU
+2048->768->2048 in q4nx), one token per rank per step, the routed experts
+sharded expert-parallel over the N ranks (all-gather of the token rows,
+local grouped expert GEMVs, reduce-scatter of the slot rows over NCCL): total
+tokens/s over the slowest rank's device time, with each rank's HBM roofline
+(packed bytes of the distinct experts it streams per step).  Steps rotate
+over distinct layers so no step finds its experts in L2.
+
 ``--impl reference`` times the reference's own CPU arithmetic for this path
 (the numpy restatement in ``oracle/``: f32-dequantised weights, f32 dot,
 bf16 RTNE -- ``host/backend.py:402-417``) on the host cores, rank 0 only.
@@ -185,8 +194,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     barrier()
     step = step_graph.replay
 
-    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[local_rank])
-                          if "CUDA_VISIBLE_DEVICES" in os.environ else local_rank)
+    clocks = ClockSampler(_gpu_index(local_rank))
     clocks.start()
     time.sleep(0.3)
     torch.cuda.synchronize()
@@ -244,6 +252,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(ctx, torch, dev, weights, host_x, budget_s=args.cpu_seconds)
+    for ws in weights.values():
+        for w in ws:
+            w.free()
+    weights.clear()
+
+    moe = None if args.no_moe else run_moe(args, ctx, torch, dev, rank, world, local_rank, barrier)
 
     if rank == 0:
         line = {
@@ -265,11 +279,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "clocks": clk,
             "per_shape": per_shape,
             "cpu_baseline": cpu,
+            "moe": moe,
         }
         print(json.dumps(line), flush=True)
-    for ws in weights.values():
-        for w in ws:
-            w.free()
     ctx.close()
 
 
@@ -320,6 +332,240 @@ def measure_per_shape(ctx, torch, dev, gen, stream, weights):
                 w.free()
     ctx.sync()
     return out
+
+
+# ---------------------------------------------------- MoE decode layer --
+# hidden 2048, 128 routed experts + 1 shared, SwiGLU
+# gate/up 2048->768 and down 768->2048 in q4nx, softmax router top-8, one
+# token per rank per step, experts sharded expert-parallel over the ranks.
+MOE = dict(hidden=2048, inter=768, experts=128, k=8, tokens_per_rank=1)
+
+
+def moe_expert_bytes(hidden: int, inter: int) -> int:
+    inter_pad = (inter + 255) // 256 * 256
+    return 2 * inter * hidden * 5 // 8 + hidden * inter_pad * 5 // 8
+
+
+def _moe_seed(layer: int, expert: int) -> int:
+    return 7_000_000 + 1000 * layer + expert
+
+
+def build_moe_layers(ctx, torch, dev, n_layers: int):
+    """n_layers distinct config-3 layers; this rank loads its own experts and
+    the shared one (weights seeded per (layer, expert), so every rank agrees)."""
+    from raon_npu_b200.device import MoeLayer
+    from raon_npu_b200.expert_parallel import ExpertParallelMoe
+    H, I, E, k = MOE["hidden"], MOE["inter"], MOE["experts"], MOE["k"]
+    gen = torch.Generator(device=dev)
+    eps = []
+    for li in range(n_layers):
+        layer = MoeLayer(ctx, H, I, E, has_shared=True)
+        ep = ExpertParallelMoe(layer, k, act="swiglu", router="softmax")
+        for e in range(E + 1):
+            if not ep.owns(e):
+                continue
+            gen.manual_seed(_moe_seed(li, e))
+            gu = torch.randn((2 * I, H), generator=gen, device=dev) * 0.02
+            dn = torch.randn((H, I), generator=gen, device=dev) * 0.02
+            pgu = torch.empty(2 * I * H * 5 // 8, dtype=torch.uint8, device=dev)
+            pdn = torch.empty(H * I * 5 // 8, dtype=torch.uint8, device=dev)
+            ctx.quantize_q4nx(gu, pgu, 2 * I, H)
+            ctx.quantize_q4nx(dn, pdn, H, I)
+            layer.set_expert(e, pgu, pdn)
+        gen.manual_seed(_moe_seed(li, 999))
+        wr = (torch.randn((E, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        layer.set_router(wr.view(torch.int16).cpu().numpy().view(np.uint16))
+        eps.append(ep)
+    torch.cuda.synchronize()
+    return eps
+
+
+def moe_cpu_sample(n_tokens: int, budget_s: float):
+    """The reference's CPU arithmetic for one config-3 decode layer (oracle port:
+    router, routed experts in ascending ID, shared expert), timed per token
+    over f32-dequantised weights cached.  To bound the setup, 16 distinct
+    expert weight sets are generated and expert e uses set e % 16 (every
+    expert has the same shape, so the timed arithmetic is unchanged).
+    Returns (tokens, seconds)."""
+    from oracle import backend as ob
+    from oracle import q4nx as q
+    H, I, E, k = MOE["hidden"], MOE["inter"], MOE["experts"], MOE["k"]
+    rng = np.random.default_rng(77)
+    wr = q.f32_to_bf16((rng.standard_normal((E, H)) * 0.02).astype(np.float32))
+    cache = {}
+
+    def expert(e):
+        if e not in cache:
+            _, c, s_, m = q.normal_weight_q4nx(2 * I, H, seed=_moe_seed(0, e))
+            gu = q.dequantize_simple(c, s_, m)
+            _, c, s_, m = q.normal_weight_q4nx(H, I, seed=_moe_seed(0, e) + 500)
+            cache[e] = (gu[:I], gu[I:], q.dequantize_simple(c, s_, m))
+        return cache[e]
+    done, secs = 0, 0.0
+    shared = expert(E)
+    while done < n_tokens and (secs < budget_s or done == 0):
+        x = q.f32_to_bf16(rng.standard_normal(H).astype(np.float32))
+        ids, _, _ = ob.route_softmax(x, wr, k)
+        experts = {int(e): expert(int(e) % 16) for e in ids}
+        t0 = time.perf_counter()
+        ob.moe_decode_layer(experts, shared, wr, x, k, act="swiglu")
+        secs += time.perf_counter() - t0
+        done += 1
+    return done, secs
+
+
+def _gather_tokens(torch, dist, world, x):
+    if world == 1:
+        return x
+    g = torch.empty((world * x.shape[0], x.shape[1]), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(g.view(torch.bfloat16), x.view(torch.bfloat16))
+    return g
+
+
+def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barrier):
+    """Config-3 MoE decode layer, expert-parallel over the ranks: tokens/s of
+    all ranks, per-rank HBM roofline of the experts each rank streams."""
+    import torch.distributed as dist
+    H, E, k, M = MOE["hidden"], MOE["experts"], MOE["k"], MOE["tokens_per_rank"]
+    eb = moe_expert_bytes(H, MOE["inter"])
+    per_rank_layer = (E // world + 1) * eb
+    # rotate over distinct layers so a step never finds its experts in L2
+    n_layers = min(16, max(2, -(-3 * 126_000_000 // per_rank_layer)))
+    eps = build_moe_layers(ctx, torch, dev, n_layers)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242 + rank)
+    xs = [torch.randn((M, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16).contiguous()
+          for _ in range(n_layers)]
+    outs = [torch.empty((M, H), dtype=torch.int16, device=dev) for _ in range(n_layers)]
+
+    # eager warm-up; it also creates the NCCL communicators before any capture
+    for _ in range(args.warmup):
+        for li in range(n_layers):
+            eps[li].decode(xs[li], outs[li])
+    torch.cuda.synchronize()
+    ctx.sync()
+    graphs, graph_err = [], None
+    try:
+        for li in range(n_layers):
+            graphs.append(capture_graph(torch, lambda li=li: eps[li].decode(xs[li], outs[li])))
+    except Exception as e:                  # noqa: BLE001 - reported in the JSON line
+        graphs, graph_err = [], f"{type(e).__name__}: {e}"[:200]
+    ok = torch.tensor([1 if graphs else 0], dtype=torch.int32, device=dev)
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if not int(ok.item()):
+        graphs = []
+
+    def step(s):
+        li = s % n_layers
+        if graphs:
+            graphs[li].replay()
+        else:
+            eps[li].decode(xs[li], outs[li])
+    for s in range(args.warmup * n_layers):
+        step(s)
+    torch.cuda.synchronize()
+    ctx.sync()
+    barrier()
+    clocks = ClockSampler(_gpu_index(local_rank))
+    clocks.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.steps):
+        step(s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = ms
+    if world > 1:
+        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_max = float(tt.item())
+    del graphs
+    ctx.sync()
+
+    # Algorithmic bytes of each step on this rank: the packed weights of the
+    # distinct experts it owns that the gathered tokens chose, the shared
+    # expert, the router weights and the token rows.
+    lo, hi = eps[0].experts
+    T = world * M
+    layer_bytes = []
+    for li in range(n_layers):
+        xg = _gather_tokens(torch, dist, world, xs[li])
+        ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+        w = torch.empty((T, k), dtype=torch.float32, device=dev)
+        eps[li].layer.route(xg, T, k, ids, w)
+        torch.cuda.synchronize()
+        active = {int(e) for e in ids.cpu().numpy().ravel() if lo <= int(e) < hi}
+        layer_bytes.append((len(active) + 1) * eb + E * H * 2 + 4 * T * H)
+    rank_bytes = sum(layer_bytes[s % n_layers] for s in range(args.steps)) / args.steps
+    rb = torch.tensor([rank_bytes], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(rb)
+    avg_rank_bytes = float(rb.item()) / world
+    peak, peak_kind = peaks()
+    achieved = avg_rank_bytes / (ms_max * 1e-3) / 1e9
+
+    # End to end through the host entry point: pinned host token rows -> device,
+    # expert-parallel decode (collectives included), rows back to the host.
+    host_x = [x.cpu().numpy().view(np.uint16) for x in xs]
+    e2e_n = max(2 * n_layers, min(args.steps, 64))
+    for li in range(n_layers):
+        eps[li].decode_host(host_x[li])
+    barrier()
+    t0 = time.perf_counter()
+    for s in range(e2e_n):
+        eps[s % n_layers].decode_host(host_x[s % n_layers])
+    e2e_s = (time.perf_counter() - t0) / e2e_n
+    if world > 1:
+        tt = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n_tok, secs = moe_cpu_sample(64, args.cpu_seconds)
+        cpu = {"value": round(n_tok / secs, 2), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{n_tok} decode tokens through the oracle's numpy MoE layer (router, 8 routed + "
+                         f"shared SwiGLU experts, ascending-ID combine; host/backend.py:466-510, "
+                         f"host/raon.py:1224-1327 restated), f32 weights cached (16 weight sets, id mod 16)"}
+    for ep in eps:
+        ep.layer.close()
+    res = {
+        "metric": "MoE decode layer tokens/s", "value": round(world * M / (ms_max * 1e-3), 1), "unit": "tokens/s",
+        "ms_per_step": round(ms_max, 5), "steps": args.steps, "scaling": "weak",
+        "config": {"workload": "MoE decode layer (BASELINE configs[2])", "hidden": H, "intermediate": MOE["inter"],
+                   "experts": E, "shared_experts": 1, "top_k": k, "router": "softmax, renormalised top-k",
+                   "act": "swiglu", "tokens_per_rank": M, "parallelism": f"ep{world}",
+                   "experts_per_rank": E // world, "layers_rotated": n_layers,
+                   "l2": "each step uses the next of %d distinct layers (%.0f MB of packed experts per rank)"
+                         % (n_layers, n_layers * per_rank_layer / 1e6),
+                   "cuda_graph": bool(int(ok.item())), "graph_error": graph_err},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": None,
+                     "per_rank_bytes_per_step": round(avg_rank_bytes),
+                     "kernel": "MoE layer step per rank (router+grouping, grouped gate/up GEMV, grouped down "
+                               "GEMV, combine; NCCL all-gather + reduce-scatter at N>1)"},
+        "e2e": {"value": round(world * M / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * M * H,
+                "d2h_bytes_per_step": 2 * M * H, "api": "ExpertParallelMoe.decode_host (synchronous)"},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clk,
+        "cpu_baseline": cpu,
+    }
+    return res
+
+
+def _gpu_index(local_rank: int) -> int:
+    if "CUDA_VISIBLE_DEVICES" in os.environ:
+        return int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank])
+    return local_rank
 
 
 # ----------------------------------------------------------- CPU legs --
@@ -390,6 +636,14 @@ def run_reference(args, rank: int):
                              "sample": "one full sweep per step through the numpy restatement of "
                                        "NumpyBackend.linear (host/backend.py:402-417), f32 weights cached"},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_moe:
+        n_tok, msecs = moe_cpu_sample(64, args.cpu_seconds)
+        line["moe"] = {"metric": "MoE decode layer tokens/s", "value": round(n_tok / msecs, 2), "unit": "tokens/s",
+                       "config": {"workload": "MoE decode layer (BASELINE configs[2])", "parallelism": "1 host"},
+                       "cpu_baseline": {"value": round(n_tok / msecs, 2), "unit": "tokens/s",
+                                        "cores": os.cpu_count(), "kind": "port",
+                                        "sample": f"{n_tok} decode tokens, oracle numpy MoE layer, f32 weights "
+                                                  f"cached (16 weight sets, id mod 16)"}}
     print(json.dumps(line), flush=True)
 
 
@@ -417,6 +671,29 @@ def run_profile_case(args):
     print(json.dumps({"profile": args.profile, "tokens": args.tokens, "launches": args.launches, "copies": copies}))
 
 
+def run_profile_moe(args):
+    """A few plain config-3 MoE decode steps on one GPU (no timing) for an ncu
+    capture: ``python bench.py --profile moe --launches 6``."""
+    import torch
+    from raon_npu_b200.device import Context
+    dev = torch.device("cuda", 0)
+    ctx = Context(0)
+    eps = build_moe_layers(ctx, torch, dev, 2)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242)
+    xs = [torch.randn((args.tokens, MOE["hidden"]), generator=gen, device=dev).to(torch.bfloat16)
+          .view(torch.int16).contiguous() for _ in range(2)]
+    out = torch.empty((args.tokens, MOE["hidden"]), dtype=torch.int16, device=dev)
+    for i in range(args.launches):
+        eps[i % 2].decode(xs[i % 2], out)
+    torch.cuda.synchronize()
+    ctx.sync()
+    for ep in eps:
+        ep.layer.close()
+    ctx.close()
+    print(json.dumps({"profile": "moe", "tokens": args.tokens, "steps": args.launches}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -426,10 +703,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-shape", action="store_true", help="skip the per-shape launch table")
-    ap.add_argument("--profile", default=None, help="NxK: run a few plain GEMV launches for ncu and exit")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode layer (configs[2])")
+    ap.add_argument("--profile", default=None, help="NxK: run a few plain GEMV launches for ncu and exit; "
+                    "'moe': a few config-3 MoE decode steps")
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--launches", type=int, default=4)
     args = ap.parse_args()
+    if args.profile == "moe":
+        run_profile_moe(args)
+        return
     if args.profile:
         run_profile_case(args)
         return

@@ -78,7 +78,8 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on ``bar``.
-// Both addresses 16-byte aligned, ``bytes`` a multiple of 16.  No multicast.
+// Both addresses 16-byte aligned, ``bytes`` a multiple of 16.  The copy
+// lands in the issuing CTA's own shared memory only.
 __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
                                               uint64_t policy) {
   asm volatile(

@@ -1,0 +1,124 @@
+"""Expert-parallel MoE decode over ``torch.distributed`` (NCCL on B200s).
+
+The reference runs the MoE layer of a decode token on one device
+(``host/raon.py:1290-1327``: router, routed experts, shared expert, combine).
+Here the routed experts of a layer are split over the ranks of a process
+group -- rank r holds experts [r*E/N, (r+1)*E/N) plus a replica of the shared
+expert (dense weights stay replicated) -- and each rank decodes its own M
+tokens:
+
+1. ``all_gather`` the ranks' token rows -> x [N*M, hidden] on every rank;
+2. ``decode_local``: every rank routes all N*M tokens (identical router
+   weights and inputs give identical routes everywhere), runs its own experts
+   for every token that chose them and the shared expert for its own tokens,
+   and writes slot rows [N*M, k+1, hidden] -- zeros where another rank owns
+   the slot;
+3. ``reduce_scatter`` (sum) of the slot rows: rank r receives the rows of its
+   own M tokens.  Every row is non-zero on at most one rank and x + 0 = x in
+   bf16, so the sum is exact;
+4. ``combine`` (ascending expert ID, f32, then the shared expert) of the own
+   tokens.
+
+The result of every token is byte-identical to the single-GPU decode
+(``MoeLayer.decode``): each expert's rows come out of whole-tile GEMVs whose
+columns do not interact, the exchange is exact and the combine is the same
+kernel.  Two collectives per layer, each a few KB per token.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def _bf16(t):
+    import torch
+    return t.view(torch.bfloat16)
+
+
+class ExpertParallelMoe:
+    """One MoE layer sharded expert-parallel over ``group``.
+
+    ``layer`` is a :class:`raon_npu_b200.device.MoeLayer` (or an object with
+    the same ``decode_local`` / ``combine`` interface and ``n_experts``,
+    ``hidden``, ``has_shared`` attributes).  Only the experts this rank owns
+    (``owns``) need to be loaded into it.
+    """
+
+    def __init__(self, layer, k: int, group=None, act: str = "swiglu", router: str = "softmax",
+                 renormalize: bool = True, scaling: float = 1.0, gate_beta: float = 4.0, value_beta: float = 25.0):
+        import torch.distributed as dist
+        self.layer = layer
+        self.k = int(k)
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        E = layer.n_experts
+        if E % self.world:
+            raise ValueError(f"{E} experts do not split evenly over {self.world} ranks")
+        per = E // self.world
+        self.experts = (self.rank * per, (self.rank + 1) * per)
+        self.kw = dict(router=router, renormalize=renormalize, scaling=scaling, act=act, gate_beta=gate_beta,
+                       value_beta=value_beta)
+        self._bufs: dict = {}
+
+    def owns(self, expert: int) -> bool:
+        """Experts this rank loads: its routed range and the shared expert (id E)."""
+        lo, hi = self.experts
+        return lo <= expert < hi or (self.layer.has_shared and expert == self.layer.n_experts)
+
+    def _buf(self, name, shape, dtype, device):
+        import torch
+        b = self._bufs.get(name)
+        if b is None or tuple(b.shape) != tuple(shape) or b.device != device:
+            b = torch.empty(shape, dtype=dtype, device=device)
+            self._bufs[name] = b
+        return b
+
+    def decode(self, x, out) -> None:
+        """x [M, hidden] bf16 bits (int16) of this rank's tokens -> out [M, hidden]."""
+        import torch
+        import torch.distributed as dist
+        M, H = x.shape
+        N, k = self.world, self.k
+        T = N * M
+        dev = x.device
+        if N > 1:
+            xg = self._buf("xg", (T, H), torch.int16, dev)
+            dist.all_gather_into_tensor(_bf16(xg), _bf16(x), group=self.group)
+        else:
+            xg = x
+        slots = self._buf("slots", (T, k + 1, H), torch.int16, dev)
+        sw = self._buf("sw", (T, k), torch.float32, dev)
+        shared = (self.rank * M, M) if self.layer.has_shared else (0, 0)
+        self.layer.decode_local(xg, k, slots, sw, experts=self.experts, shared_tokens=shared, **self.kw)
+        if N > 1:
+            mine = self._buf("mine", (M, k + 1, H), torch.int16, dev)
+            dist.reduce_scatter_tensor(_bf16(mine), _bf16(slots), op=dist.ReduceOp.SUM, group=self.group)
+        else:
+            mine = slots
+        self.layer.combine(mine, sw[self.rank * M:(self.rank + 1) * M], k, out, tokens=M,
+                           with_shared=self.layer.has_shared)
+
+    def decode_host(self, x: np.ndarray) -> np.ndarray:
+        """Host entry point: x [M, hidden] bf16 bits -> out [M, hidden] (copies in
+        from pinned memory, decodes, copies out, waits)."""
+        import torch
+        xs = np.ascontiguousarray(x, dtype=np.uint16)
+        M, H = xs.shape
+        dev = torch.device("cuda", torch.cuda.current_device())
+        pin_in = self._buf("pin_in", (M, H), torch.int16, torch.device("cpu"))
+        if not pin_in.is_pinned():
+            pin_in = pin_in.pin_memory()
+            self._bufs["pin_in"] = pin_in
+        pin_out = self._buf("pin_out", (M, H), torch.int16, torch.device("cpu"))
+        if not pin_out.is_pinned():
+            pin_out = pin_out.pin_memory()
+            self._bufs["pin_out"] = pin_out
+        pin_in.numpy()[:] = xs.view(np.int16)
+        xd = self._buf("x_dev", (M, H), torch.int16, dev)
+        od = self._buf("out_dev", (M, H), torch.int16, dev)
+        xd.copy_(pin_in, non_blocking=True)
+        self.decode(xd, od)
+        pin_out.copy_(od, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return pin_out.numpy().copy().view(np.uint16)

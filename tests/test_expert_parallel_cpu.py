@@ -1,0 +1,137 @@
+"""Host logic of the expert-parallel MoE decode on CPU (gloo, world size 2).
+
+``raon_npu_b200.expert_parallel.ExpertParallelMoe`` drives an MoE layer
+through all-gather -> local experts -> reduce-scatter -> combine.  Here the
+layer is a stand-in built on the oracle (the same ``decode_local`` /
+``combine`` contract as ``MoeLayer``, computed in numpy), so the test checks
+the partition of experts and shared-expert tokens over the ranks, the token
+order of the gather, the exactness of the summed exchange and the slicing of
+the combine: every rank's outputs must equal the single-process oracle decode
+of its tokens byte for byte.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+HIDDEN, INTER, E, K, M = 256, 256, 8, 3, 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _model(seed=11):
+    """Experts (dequantised f32 gate, up, down; id E = shared) and router bits."""
+    from oracle import q4nx as q
+    from tests.golden import cases
+    rng = np.random.default_rng(seed)
+    experts = {}
+    for e in range(E + 1):
+        gu = (rng.standard_normal((2 * INTER, HIDDEN)) * 0.02).astype(np.float32)
+        dn = (rng.standard_normal((HIDDEN, INTER)) * 0.02).astype(np.float32)
+        _, fgu = cases.q4nx_weight(gu, q)
+        _, fdn = cases.q4nx_weight(dn, q)
+        experts[e] = (fgu[:INTER], fgu[INTER:], fdn)
+    wr = q.f32_to_bf16((rng.standard_normal((E, HIDDEN)) * 0.02).astype(np.float32))
+    return experts, wr
+
+
+class OracleLayer:
+    """CPU stand-in for ``MoeLayer`` (test infrastructure: numpy oracle)."""
+
+    def __init__(self, experts, wr, owned):
+        self.experts = {e: w for e, w in experts.items() if e in owned}
+        self.wr = wr
+        self.n_experts, self.hidden, self.has_shared = E, HIDDEN, True
+
+    def decode_local(self, x, k, slots, sw, experts, shared_tokens, act, **_):
+        import torch
+        from oracle import backend as ob
+        xs = x.numpy().view(np.uint16)
+        lo, hi = experts
+        t0, tn = shared_tokens
+        rows = np.zeros((xs.shape[0], k + 1, self.hidden), np.uint16)
+        wts = np.zeros((xs.shape[0], k), np.float32)
+        for t in range(xs.shape[0]):
+            ids, w, _ = ob.route_softmax(xs[t], self.wr, k)
+            order = np.argsort(ids, kind="stable")
+            for pos, r in enumerate(order):
+                e = int(ids[r])
+                wts[t, pos] = w[r]
+                if lo <= e < hi:
+                    rows[t, pos] = ob.expert_forward(*self.experts[e], xs[t], act)
+            if t0 <= t < t0 + tn:
+                rows[t, k] = ob.expert_forward(*self.experts[E], xs[t], act)
+        slots.copy_(torch.from_numpy(rows.view(np.int16)))
+        sw.copy_(torch.from_numpy(wts))
+
+    def combine(self, slots, sw, k, out, tokens, with_shared):
+        import torch
+        from oracle import backend as ob
+        rows = slots.numpy().view(np.uint16)
+        w = sw.numpy()
+        # slot rows are already in ascending-ID order: combine with ids 0..k-1
+        routed = ob.combine_ascending(rows[:, :k], np.tile(np.arange(k), (tokens, 1)), w)
+        res = np.stack([ob.moe_token_with_shared(routed[t], rows[t, k]) for t in range(tokens)])
+        out.copy_(torch.from_numpy(res.view(np.int16)))
+
+
+def _worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+    from raon_npu_b200.expert_parallel import ExpertParallelMoe
+    from oracle import q4nx as q
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        experts, wr = _model()
+        per = E // world
+        owned = set(range(rank * per, (rank + 1) * per)) | {E}
+        ep = ExpertParallelMoe(OracleLayer(experts, wr, owned), K, act="swiglu")
+        assert ep.experts == (rank * per, (rank + 1) * per)
+        assert all(ep.owns(e) for e in owned) and not any(ep.owns(e) for e in set(range(E)) - owned)
+        rng = np.random.default_rng(100 + rank)
+        x = q.f32_to_bf16(rng.standard_normal((M, HIDDEN)).astype(np.float32))
+        out = torch.empty((M, HIDDEN), dtype=torch.int16)
+        ep.decode(torch.from_numpy(x.view(np.int16)), out)
+        np.save(os.path.join(result_dir, f"x{rank}.npy"), x)
+        np.save(os.path.join(result_dir, f"out{rank}.npy"), out.numpy().view(np.uint16))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_expert_parallel_two_ranks_match_single_process(tmp_path):
+    import torch.multiprocessing as mp
+    from oracle import backend as ob
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    experts, wr = _model()
+    for rank in range(world):
+        x = np.load(tmp_path / f"x{rank}.npy")
+        out = np.load(tmp_path / f"out{rank}.npy")
+        for t in range(M):
+            ref, _, _, _ = ob.moe_decode_layer({e: experts[e] for e in range(E)}, experts[E], wr, x[t], K,
+                                               act="swiglu")
+            np.testing.assert_array_equal(out[t], ref)
+
+
+def test_single_process_owns_every_expert():
+    from raon_npu_b200.expert_parallel import ExpertParallelMoe
+    import torch.distributed as dist
+
+    class L:
+        n_experts, hidden, has_shared = 6, 256, True
+    if dist.is_initialized():
+        pytest.skip("needs a process without a default group")
+    ep = ExpertParallelMoe(L(), 2)
+    assert ep.world == 1 and ep.experts == (0, 6)
+    assert all(ep.owns(e) for e in range(7))

@@ -1,0 +1,98 @@
+"""Expert-parallel MoE decode over NCCL on 2+ GPUs of one box.
+
+Each rank (one process per GPU) holds E/N routed experts and the shared
+expert and decodes its own tokens through ``ExpertParallelMoe`` (NCCL
+all-gather, grouped expert GEMVs, NCCL reduce-scatter, combine).  Every
+rank's output must equal, byte for byte, the single-GPU ``MoeLayer.decode``
+of the same tokens with all experts loaded.  Skipped with fewer than 2 GPUs.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+E, H, I, K, M = 32, 2048, 768, 8, 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _layer(torch, ctx, owned):
+    from raon_npu_b200.device import MoeLayer
+    layer = MoeLayer(ctx, H, I, E, has_shared=True)
+    gen = torch.Generator(device="cuda")
+    for e in sorted(owned):
+        gen.manual_seed(31_000 + e)
+        gu = torch.randn((2 * I, H), generator=gen, device="cuda") * 0.02
+        dn = torch.randn((H, I), generator=gen, device="cuda") * 0.02
+        pgu = torch.empty(2 * I * H * 5 // 8, dtype=torch.uint8, device="cuda")
+        pdn = torch.empty(H * I * 5 // 8, dtype=torch.uint8, device="cuda")
+        ctx.quantize_q4nx(gu, pgu, 2 * I, H)
+        ctx.quantize_q4nx(dn, pdn, H, I)
+        layer.set_expert(e, pgu, pdn)
+    rng = np.random.default_rng(5)
+    wr = ((rng.standard_normal((E, H)) * 0.02).astype(np.float32).view(np.uint32) + 0x8000) >> 16
+    layer.set_router(wr.astype(np.uint16))
+    return layer
+
+
+def _worker(rank, world, port, out_dir):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from raon_npu_b200.build import build
+        from raon_npu_b200.device import Context
+        from raon_npu_b200.expert_parallel import ExpertParallelMoe
+        build()
+        ctx = Context(rank)
+        per = E // world
+        layer = _layer(torch, ctx, set(range(rank * per, (rank + 1) * per)) | {E})
+        ep = ExpertParallelMoe(layer, K, act="swiglu")
+        full = _layer(torch, ctx, set(range(E + 1)))
+        gen = torch.Generator(device="cuda")
+        res = []
+        for trial in range(3):
+            gen.manual_seed(100 * trial + rank)
+            x = torch.randn((M, H), generator=gen, device="cuda").to(torch.bfloat16).view(torch.int16).contiguous()
+            out = torch.empty((M, H), dtype=torch.int16, device="cuda")
+            ep.decode(x, out)
+            ref = torch.empty((M, H), dtype=torch.int16, device="cuda")
+            full.decode(x, K, ref, act="swiglu")
+            torch.cuda.synchronize()
+            res.append(bool(torch.equal(out, ref)))
+        host = ep.decode_host(x.cpu().numpy().view(np.uint16))
+        res.append(bool(np.array_equal(host, ref.cpu().numpy().view(np.uint16))))
+        ctx.sync()
+        np.save(os.path.join(out_dir, f"ok{rank}.npy"), np.array(res))
+        layer.close()
+        full.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(600)
+def test_expert_parallel_nccl_matches_single_gpu_bytes(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    for r in range(world):
+        ok = np.load(tmp_path / f"ok{r}.npy")
+        assert ok.all(), (r, ok)
