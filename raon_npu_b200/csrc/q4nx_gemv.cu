@@ -292,14 +292,15 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(GemvParams 
     int slot = 0;
     uint32_t phase = 0;        // parity of the ring slot's current fill
     for (int j = 0; j < n; ++j) {
-      if (!mbar_wait_bounded(bar0 + 8 * slot, phase)) {
+      if (!mbar_wait_bounded_warp(bar0 + 8 * slot, phase)) {
         if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
-        // Let the copies already issued land before the CTA's shared memory goes away.
+        // Let the copies already issued (this unit's included) land before the
+        // CTA's shared memory goes away.
         int s2 = slot;
         uint32_t ph2 = phase;
-        for (int j2 = j + 1; j2 < n && j2 < j + S; ++j2) {
-          if (++s2 == S) s2 = 0, ph2 ^= 1u;
+        for (int j2 = j; j2 < n && j2 < j + S; ++j2) {
           mbar_wait_bounded(bar0 + 8 * s2, ph2);
+          if (++s2 == S) s2 = 0, ph2 ^= 1u;
         }
         timed_out = true;
         break;

@@ -43,7 +43,8 @@ namespace rc {
 constexpr int kMoeMaxK = 16;               // routed experts per token
 constexpr int kMoeMaxTokens = 16;          // tokens per call: two 8-column mma blocks
 constexpr int kMoeMaxExperts = 256;
-constexpr int kMoeWarps = 8;
+constexpr int kMoeWarps = 16;
+constexpr int kMoePartialBytes = 32 * 1024;   // per-CTA unit partials of one round
 constexpr int kMoeMaxStages = 8;
 constexpr int kMoeMaxGroupsPerCta = 4;     // down kernel: groups one CTA's tile range may touch
 
@@ -127,141 +128,172 @@ struct RouteParams {
 
 constexpr int kRouteThreads = 256;
 constexpr int kRouteExpertsPerCta = 8;   // one warp per expert
+constexpr int kRouteChunk = 2048;        // columns per pass: 8 x 16-byte loads per lane
 
-// Phase 1 (every CTA): logits of 8 experts for one token, f64 accumulation of
-// exact bf16 x bf16 products, rounded once to f32.  Phase 2 (the last CTA of
-// the token, by an arrival counter): top-k with "lower index wins" ties, the
-// routing weights and the ascending-ID slot list.  Phase 3 (the last token to
-// finish): the group table.
+// Phase 1 (every CTA, one warp per expert, all T tokens): logits as f64 sums
+// of exact bf16 x bf16 products, rounded once to f32.  The expert's router row
+// is fetched before waiting on the previous launch (it does not depend on
+// it); token rows are staged in shared memory 2048 columns at a time, so
+// every global fetch is one round trip for all lanes.  Phase 2 (the last CTA
+// to arrive): one warp per token selects the top k; then warp 0 builds the
+// group table.
 __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p) {
+  extern __shared__ __align__(16) uint8_t route_smem[];   // x chunk [T][kRouteChunk] bf16
   __shared__ uint32_t smask[kMoeMaxExperts + 1];
   __shared__ int sgidx[kMoeMaxExperts + 1];
   __shared__ int is_last;
   pdl_launch_dependents();
-  pdl_wait_prior();
-  const int t = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * kRouteExpertsPerCta + warp;
-  const uint16_t *xr = p.x + (size_t)t * p.ldx;
-  if (e < p.n_experts) {
-    const uint16_t *wr = p.wr + (size_t)e * p.hidden;
-    double acc = 0.0;
-    for (int h = lane * 2; h < p.hidden; h += 64) {
-      const uint32_t xv = *reinterpret_cast<const uint32_t *>(xr + h);
-      const uint32_t wv = *reinterpret_cast<const uint32_t *>(wr + h);
-      acc = fma((double)bf16_to_f32(xv & 0xFFFFu), (double)bf16_to_f32(wv & 0xFFFFu), acc);
-      acc = fma((double)bf16_to_f32(xv >> 16), (double)bf16_to_f32(wv >> 16), acc);
-    }
+  const int T = p.tokens;
+  uint4 *xs = reinterpret_cast<uint4 *>(route_smem);
+  // row stride of the staged chunk, in 16-byte vectors: the launch allocates
+  // T * min(hidden, kRouteChunk) bf16
+  const int vs = (p.hidden < kRouteChunk ? p.hidden : kRouteChunk) / 8;
+  double acc[kMoeMaxTokens];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) p.s.logits[(size_t)t * p.n_experts + e] = __double2float_rn(acc);
+  for (int t = 0; t < kMoeMaxTokens; ++t) acc[t] = 0.0;
+  for (int c0 = 0; c0 < p.hidden; c0 += kRouteChunk) {
+    const int cols = p.hidden - c0 < kRouteChunk ? p.hidden - c0 : kRouteChunk;
+    const int v8 = cols / 8;                       // 16-byte vectors per row in this chunk
+    uint4 wv[kRouteChunk / 256];
+#pragma unroll
+    for (int i = 0; i < kRouteChunk / 256; ++i) {
+      const int v = i * 32 + lane;
+      wv[i] = make_uint4(0, 0, 0, 0);
+      if (e < p.n_experts && v < v8)
+        wv[i] = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + c0) + v);
+    }
+    if (c0 == 0) pdl_wait_prior();                 // token rows come from the previous launch
+    __syncthreads();                               // previous chunk fully consumed
+    for (int i = threadIdx.x; i < T * v8; i += blockDim.x) {
+      const int t = i / v8, v = i - t * v8;
+      xs[t * vs + v] = *(reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.ldx + c0) + v);
+    }
+    __syncthreads();
+    if (e < p.n_experts) {
+#pragma unroll
+      for (int t = 0; t < kMoeMaxTokens; ++t) {
+        if (t < T) {
+#pragma unroll
+          for (int i = 0; i < kRouteChunk / 256; ++i) {
+            const int v = i * 32 + lane;
+            if (v < v8) {
+              const uint4 xv = xs[t * vs + v];
+              const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+              const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                acc[t] = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), (double)bf16_to_f32(ww[j] & 0xFFFFu), acc[t]);
+                acc[t] = fma((double)bf16_to_f32(xw[j] >> 16), (double)bf16_to_f32(ww[j] >> 16), acc[t]);
+              }
+            }
+          }
+        }
+      }
+    }
   }
-  __threadfence();
+  if (e < p.n_experts) {
+#pragma unroll
+    for (int t = 0; t < kMoeMaxTokens; ++t) {
+      if (t < T) {
+        double a = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) p.s.logits[(size_t)t * p.n_experts + e] = __double2float_rn(a);
+      }
+    }
+  }
+  // one release per CTA: the barrier orders the warps' logit stores before
+  // thread 0's (cumulative) fence and arrival
   __syncthreads();
   if (threadIdx.x == 0) {
-    const int old = atomicAdd(p.s.counter + t, 1);
+    __threadfence();
+    const int old = atomicAdd(p.s.counter, 1);
     is_last = old == (int)gridDim.x - 1;
-    if (is_last) atomicExch(p.s.counter + t, 0);
+    if (is_last) {
+      atomicExch(p.s.counter, 0);
+      __threadfence();
+    }
   }
   __syncthreads();
-  if (!is_last || warp != 0) return;
-  __threadfence();
+  if (!is_last) return;
 
-  // ---- selection (one warp): value per expert, then k rounds of warp argmax
-  const float *lg = p.s.logits + (size_t)t * p.n_experts;
-  constexpr int kPer = kMoeMaxExperts / 32;
-  float val[kPer], score[kPer];
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int ei = lane + 32 * i;
-    val[i] = -INFINITY;
-    score[i] = 0.f;
-    if (ei < p.n_experts) {
-      const float l = __ldcg(lg + ei);
-      if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
-        score[i] = __double2float_rn(1.0 / (1.0 + exp(-(double)l)));
-        val[i] = score[i] + p.bias[ei];
-      } else {
-        score[i] = l;
-        val[i] = l;
-      }
+  // ---- phase 2 (last CTA, all threads): top-k of every token by counting,
+  // for each expert, the experts ahead of it (larger value, or equal value and
+  // lower index); rank < k selects.
+  const int E = p.n_experts, k = p.k;
+  float *val = reinterpret_cast<float *>(route_smem);      // [T][E]
+  float *score = val + T * E;                               // [T][E]
+  int *rank = reinterpret_cast<int *>(score + T * E);       // [T][E]
+  int *sel = rank + T * E;                                  // [T][k] expert of each rank
+  float *selw = reinterpret_cast<float *>(sel + T * k);     // [T][k] weight of each rank
+  for (int i = threadIdx.x; i < T * E; i += blockDim.x) {
+    const float l = __ldcg(p.s.logits + i);
+    float sc = l, v = l;
+    if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
+      sc = __double2float_rn(1.0 / (1.0 + exp(-(double)l)));
+      v = sc + p.bias[i % E];
     }
+    score[i] = sc;
+    val[i] = v;
   }
-  int sel[kMoeMaxK];
-  float sel_score[kMoeMaxK];
-  for (int r = 0; r < p.k; ++r) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int ei = lane + 32 * i;
-      if (ei < p.n_experts && (val[i] > bv || (val[i] == bv && ei < bi))) bv = val[i], bi = ei;
+  __syncthreads();
+  for (int i = threadIdx.x; i < T * E; i += blockDim.x) {
+    const int t = i / E, e0 = i - t * E;
+    const float v = val[i];
+    const float *row = val + t * E;
+    int ahead = 0;
+    for (int e2 = 0; e2 < E; ++e2) {
+      const float v2 = row[e2];
+      ahead += (v2 > v || (v2 == v && e2 < e0)) ? 1 : 0;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
-    }
-    sel[r] = bi;
-    // the owner lane retires the winner and publishes its score
-    float sc = 0.f;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i)
-      if (lane + 32 * i == bi) sc = score[i], val[i] = -INFINITY;
-    sel_score[r] = __shfl_sync(0xffffffffu, sc, bi & 31);
+    rank[i] = ahead;
+    if (ahead < k) sel[t * k + ahead] = e0;
   }
-  if (lane == 0) {
-    // ---- routing weights
-    float w[kMoeMaxK];
+  __syncthreads();
+  for (int i = threadIdx.x; i < T * k; i += blockDim.x) {
+    const int t = i / k, r = i - t * k;
+    const float *sc = score + t * E;
+    const int *st = sel + t * k;
+    float w;
     if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
       float sum = 0.f;
-      for (int r = 0; r < p.k; ++r) sum += sel_score[r];
-      for (int r = 0; r < p.k; ++r) {
-        float c = sel_score[r];
-        if (p.renorm) c = c / (sum + 1e-20f);
-        w[r] = c * p.scaling;
-      }
+      for (int r2 = 0; r2 < k; ++r2) sum += sc[st[r2]];
+      w = sc[st[r]];
+      if (p.renorm) w = w / (sum + 1e-20f);
+      w = w * p.scaling;
     } else {
       // softmax over all experts then renormalised over the top-k equals the
-      // softmax of the selected logits (the full denominator cancels).
-      const float mx = sel_score[0];
+      // softmax of the selected logits (the full denominator cancels)
+      const float mx = sc[st[0]];
       float sum = 0.f;
-      for (int r = 0; r < p.k; ++r) sum += expf(sel_score[r] - mx);
-      for (int r = 0; r < p.k; ++r) w[r] = expf(sel_score[r] - mx) / sum;
+      for (int r2 = 0; r2 < k; ++r2) sum += expf(sc[st[r2]] - mx);
+      w = expf(sc[st[r]] - mx) / sum;
     }
-    for (int r = 0; r < p.k; ++r) {
-      p.s.ids[(size_t)t * p.k + r] = sel[r];
-      p.s.weights[(size_t)t * p.k + r] = w[r];
-    }
-    // ---- ascending-ID slot list (insertion sort of k <= 16 entries)
-    int order[kMoeMaxK];
-    for (int r = 0; r < p.k; ++r) order[r] = r;
-    for (int a = 1; a < p.k; ++a) {
-      const int v = order[a];
-      int b = a - 1;
-      while (b >= 0 && sel[order[b]] > sel[v]) {
-        order[b + 1] = order[b];
-        --b;
-      }
-      order[b + 1] = v;
-    }
-    int32_t *se = p.s.slot_expert + (size_t)t * (p.k + 1);
-    float *sw = p.s.slot_w + (size_t)t * p.k;
-    for (int r = 0; r < p.k; ++r) {
-      se[r] = sel[order[r]];
-      sw[r] = w[order[r]];
-    }
-    se[p.k] = p.shared_id;
-    __threadfence();
-    const int old = atomicAdd(p.s.counter + p.tokens, 1);
-    is_last = old == p.tokens - 1;
-    if (is_last) atomicExch(p.s.counter + p.tokens, 0);
+    selw[i] = w;
+    p.s.ids[i] = st[r];
+    p.s.weights[i] = w;
   }
-  __syncwarp();
-  if (!__shfl_sync(0xffffffffu, is_last, 0)) return;
-  __threadfence();
-  build_groups(p.s.slot_expert, p.tokens, p.k, p.n_experts, p.own, p.s, smask, sgidx, lane);
+  __syncthreads();
+  // ascending-ID slot lists: one warp per token, ballots over the experts
+  for (int t = warp; t < T; t += kRouteThreads / 32) {
+    int base = 0;
+    for (int c = 0; c < E; c += 32) {
+      const int e1 = c + lane;
+      const int rk = e1 < E ? rank[t * E + e1] : k;
+      const uint32_t b = __ballot_sync(0xffffffffu, rk < k);
+      if (rk < k) {
+        const int pos = base + __popc(b & ((1u << lane) - 1u));
+        p.s.slot_expert[t * (k + 1) + pos] = e1;
+        p.s.slot_w[t * k + pos] = selw[t * k + rk];
+      }
+      base += __popc(b);
+    }
+    if (lane == 0) p.s.slot_expert[t * (k + 1) + k] = p.shared_id;
+  }
+  __syncthreads();
+  if (warp == 0) build_groups(p.s.slot_expert, T, k, E, p.own, p.s, smask, sgidx, lane);
 }
 
 // Slot lists from caller-supplied top ids / weights [T][k] (the
@@ -313,6 +345,7 @@ struct MoeGemvParams {
   int group_tiles;                     // row tiles per expert matrix
   int kb;                              // K / 256
   int stages;
+  int round_tiles;                     // tiles per reduction round of a CTA
   int T;                               // tokens of the call
   // activations (fields read by the shared staging code)
   const void *x;
@@ -323,17 +356,31 @@ struct MoeGemvParams {
   int act;
   float gate_beta, value_beta;
   int *err;
+  // gate/up launch of an expert-parallel call: zero the slot rows another rank
+  // computes (zero_rows [T*(k+1)][hidden], null otherwise)
+  uint16_t *zero_rows;
+  const int32_t *slot_expert;
+  int k, hidden;
+  MoeOwned own;
 };
 
 // EPI == kMoeEpiGlu: x = the T token rows; tile rows are interleaved
 //   (gate g, up g) pairs; y = act rows, act[g][t][8*tile + g'] for the tokens of
 //   group g (8*NTB rows per group).
 // EPI == kMoeEpiDown: x = act; y = down_out rows, [t*(k+1)+pos][hidden].
+//
+// Partition: CTA c owns the contiguous tiles [c0, c1) of the group-major tile
+// list; its units (tile, k-block) are dealt to the warps round-robin (unit u
+// to warp u % 16) in rounds of p.round_tiles whole tiles.  Each unit's
+// contribution goes to its own shared-memory partial; after a round's barrier
+// one warp per tile sums the tile's partials in k-block order and runs the
+// epilogue.  A tile's result therefore depends on the tile alone, never on
+// the partition, the grid or the other groups of the launch.
 template <int EPI, int NTB>
 __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kb = p.kb, k = kb * kUnitK, S = p.stages;
+  const int kb = p.kb, k = kb * kUnitK, S = p.stages, R = p.round_tiles;
   uint8_t *ring = smem + warp * S * kUnitBytes;
   const uint32_t ring_s = smem_addr(ring);
   constexpr int kStageBlocks = EPI == kMoeEpiGlu ? NTB : NTB * kMoeMaxGroupsPerCta;
@@ -342,38 +389,47 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
   cur += xfrag_bytes(kStageBlocks, k);
   float *gs = reinterpret_cast<float *>(cur);
   cur += gsum_bytes(kStageBlocks, k);
+  float4 *part = reinterpret_cast<float4 *>(cur);          // [R*kb][NTB][32 lanes]
+  cur += (size_t)R * kb * NTB * 32 * sizeof(float4);
   const uint32_t bar0 = smem_addr(cur) + warp * S * 8;
 
   pdl_launch_dependents();
   // The group table is written by the previous launch: wait before reading it.
   pdl_wait_prior();
+  if (EPI == kMoeEpiGlu && p.zero_rows) {
+    const int rows = p.T * (p.k + 1);
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+      const int t = r / (p.k + 1), pos = r - t * (p.k + 1);
+      const int e = p.slot_expert[r];
+      const bool mine = pos < p.k ? (e >= p.own.lo && e < p.own.hi) : (e >= 0 && ((p.own.shared_mask >> t) & 1u));
+      if (mine) continue;
+      uint4 *dst = reinterpret_cast<uint4 *>(p.zero_rows + (size_t)r * p.hidden);
+      for (int i = threadIdx.x; i < p.hidden / 8; i += blockDim.x) dst[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
   const int ng = *p.n_groups - (p.skip_last_group ? 1 : 0);
   const int total = ng * p.group_tiles;
-  int t_begin, t_step, t_end, g_lo = 0;
+  const int per = (total + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int c0 = blockIdx.x * per;
+  const int c1 = c0 + per < total ? c0 + per : total;
+  const int n_tiles = c1 > c0 ? c1 - c0 : 0;
+  const int n_units = n_tiles * kb;
+  int g_lo = 0;
   MoeGemvParams q = p;
   if (EPI == kMoeEpiDown) {
-    const int per = (total + (int)gridDim.x - 1) / (int)gridDim.x;
-    const int c0 = blockIdx.x * per;
-    const int c1 = c0 + per < total ? c0 + per : total;
-    t_begin = c0 + warp;
-    t_step = kMoeWarps;
-    t_end = c1;
+    // stage the activation rows of the groups the range touches (8*NTB rows each)
     g_lo = c0 / p.group_tiles;
-    const int g_hi = c1 > c0 ? (c1 - 1) / p.group_tiles : g_lo - 1;
-    // stage the activation rows of groups g_lo..g_hi (8*NTB rows each)
+    const int g_hi = n_tiles ? (c1 - 1) / p.group_tiles : g_lo - 1;
     q.x = static_cast<const uint16_t *>(p.x) + (size_t)g_lo * 8 * NTB * p.ldx;
     q.tokens = q.slots = (g_hi - g_lo + 1) * 8 * NTB;
-  } else {
-    t_begin = blockIdx.x * kMoeWarps + warp;
-    t_step = gridDim.x * kMoeWarps;
-    t_end = total;
   }
-  const int my_tiles = t_begin < t_end ? (t_end - 1 - t_begin) / t_step + 1 : 0;
-  const int n = my_tiles * kb;
+  // this warp's units: u = warp + kMoeWarps * j
+  const int n = warp < n_units ? (n_units - 1 - warp) / kMoeWarps + 1 : 0;
 
   auto unit_src = [&](int j) -> const uint8_t * {
-    const int i = j / kb, kbi = j - i * kb;
-    const int tg = t_begin + i * t_step;
+    const int u = warp + kMoeWarps * j;
+    const int ti = u / kb, kbi = u - ti * kb;
+    const int tg = c0 + ti;
     const int grp = tg / p.group_tiles, tile = tg - grp * p.group_tiles;
     const uint8_t *b = p.expert_tiles[p.group_expert[grp]];
     return b ? b + ((size_t)tile * kb + kbi) * kUnitBytes : nullptr;
@@ -389,44 +445,67 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
     }
   };
   if (lane == 0 && n > 0) {
-    for (int s = 0; s < S; ++s) mbar_init(bar0 + 8 * s, 1);
+    for (int sl = 0; sl < S; ++sl) mbar_init(bar0 + 8 * sl, 1);
     mbar_fence_init();
     for (int j = 0; j < n && j < S; ++j) issue(j, j);
   }
   build_activations<true>(q, kStageBlocks, xs, gs, threadIdx.x, blockDim.x);
   __syncthreads();
-  if (n == 0) return;
 
-  Acc<NTB> acc;
-  acc_zero(acc);
-  int slot_ring = 0;
+  const int U = R * kb;                                    // units per round
+  const int n_rounds = (n_units + U - 1) / U;
+  int j = 0, slot_ring = 0;
   uint32_t phase = 0;
+  int issued = n < S ? n : S;                              // copies issued so far (lane 0)
+  bool failed = false;
+  int j_fail = 0;
   const int g = lane >> 2, qd = lane & 3;
-  for (int j = 0; j < n; ++j) {
-    const int i = j / kb, kbi = j - i * kb;
-    const int tg = t_begin + i * t_step;
-    const int grp = tg / p.group_tiles, tile = tg - grp * p.group_tiles;
-    const bool live = p.expert_tiles[p.group_expert[grp]] != nullptr;
-    if (!mbar_wait_bounded(bar0 + 8 * slot_ring, phase)) {
-      if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
-      int s2 = slot_ring;
-      uint32_t ph2 = phase;
-      for (int j2 = j + 1; j2 < n && j2 < j + S; ++j2) {
-        if (++s2 == S) s2 = 0, ph2 ^= 1u;
-        mbar_wait_bounded(bar0 + 8 * s2, ph2);
+  for (int r = 0; r < n_rounds; ++r) {
+    const int u_end = (r + 1) * U < n_units ? (r + 1) * U : n_units;
+    for (; j < n && warp + kMoeWarps * j < u_end; ++j) {
+      const int u = warp + kMoeWarps * j;
+      const int ti = u / kb, kbi = u - ti * kb;
+      const int tg = c0 + ti;
+      const int grp = tg / p.group_tiles;
+      if (!failed && !mbar_wait_bounded_warp(bar0 + 8 * slot_ring, phase)) {
+        if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+        failed = true;
+        j_fail = j;
       }
-      return;
+      if (!failed && p.expert_tiles[p.group_expert[grp]] != nullptr) {
+        Acc<NTB> acc;
+        acc_zero(acc);
+        const int blk = EPI == kMoeEpiGlu ? 0 : (grp - g_lo) * NTB;
+        compute_unit<NTB, true>(ring + slot_ring * kUnitBytes, xs + (size_t)blk * (k / 64) * 256,
+                                gs + (size_t)blk * kb * 64, p, kbi, lane, acc);
+        float4 *dst = part + (size_t)(u - r * U) * NTB * 32 + lane;
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb)
+          dst[tb * 32] = make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3]);
+      }
+      __syncwarp();
+      if (!failed && lane == 0 && j + S < n) {
+        issue(j + S, slot_ring);
+        ++issued;
+      }
+      if (++slot_ring == S) slot_ring = 0, phase ^= 1u;
     }
-    if (live) {
-      const int blk = EPI == kMoeEpiGlu ? 0 : (grp - g_lo) * NTB;
-      compute_unit<NTB, true>(ring + slot_ring * kUnitBytes, xs + (size_t)blk * (k / 64) * 256,
-                              gs + (size_t)blk * kb * 64, p, kbi, lane, acc);
-    }
-    __syncwarp();
-    if (lane == 0 && j + S < n) issue(j + S, slot_ring);
-    if (++slot_ring == S) slot_ring = 0, phase ^= 1u;
-    if (kbi + 1 == kb) {
-      // whole tile done: epilogue for the tokens of this group
+    __syncthreads();
+    // one warp per tile of this round: ordered sum of its units, epilogue
+    const int t_lo = r * R, t_hi = t_lo + R < n_tiles ? t_lo + R : n_tiles;
+    for (int ti = t_lo + warp; ti < t_hi; ti += kMoeWarps) {
+      const int tg = c0 + ti;
+      const int grp = tg / p.group_tiles, tile = tg - grp * p.group_tiles;
+      const bool live = p.expert_tiles[p.group_expert[grp]] != nullptr;
+      Acc<NTB> acc;
+      acc_zero(acc);
+      const float4 *src = part + (size_t)(ti - t_lo) * kb * NTB * 32 + lane;
+      for (int kbi = 0; kbi < kb; ++kbi) {
+        float4 v[NTB];
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb) v[tb] = src[(kbi * NTB + tb) * 32];
+        acc_add(acc, v);
+      }
       const uint32_t mask = p.group_mask[grp];
 #pragma unroll
       for (int tb = 0; tb < NTB; ++tb) {
@@ -449,8 +528,13 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
           }
         }
       }
-      acc_zero(acc);
     }
+    __syncthreads();
+  }
+  // after a timeout, wait (bounded) for the copies still in flight before the
+  // CTA's shared memory is released
+  if (failed && lane == 0) {
+    for (int jj = j_fail; jj < issued; ++jj) mbar_wait_bounded(bar0 + 8 * (jj % S), (uint32_t)(jj / S) & 1u);
   }
 }
 
@@ -474,28 +558,68 @@ __global__ void moe_shared_act_kernel(const uint16_t *gu, int T, int inter, int 
 // Per token t: routed = RTNE(sum_{slots in ascending ID} f32(down[t][s]) * w[t][s]);
 // out = routed, or RTNE(f32(routed) + f32(down[t][k])) with the shared expert.
 // routed_out / shared_out (optional) receive the routed sum and the shared
-// expert's row (the grouped boundary returns them apart).
-__global__ void moe_combine_kernel(const uint16_t *down, const float *slot_w, int k, int with_shared, int hidden,
-                                   uint16_t *out, uint16_t *routed_out, uint16_t *shared_out) {
+// expert's row (the grouped boundary returns them apart).  A thread owns 8
+// columns and fetches all k+1 rows before summing (one memory round trip).
+constexpr int kCombineThreads = 128;
+
+__global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(const uint16_t *down, const float *slot_w,
+                                                                        int k, int with_shared, int hidden,
+                                                                        uint16_t *out, uint16_t *routed_out,
+                                                                        uint16_t *shared_out) {
   pdl_launch_dependents();
   pdl_wait_prior();
   const int t = blockIdx.y;
-  const uint16_t *rows = down + (size_t)t * (k + 1) * hidden;
-  const float *w = slot_w + (size_t)t * k;
-  for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < hidden; h += gridDim.x * blockDim.x) {
-    float acc = 0.f;
-    // product rounded, then sum rounded -- as the reference's f32 numpy update
-    // (no fused multiply-add contraction)
-    for (int s = 0; s < k; ++s) acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(rows[(size_t)s * hidden + h]), w[s]));
-    const uint16_t routed = f32_to_bf16_rne(acc);
-    const size_t o = (size_t)t * hidden + h;
-    if (routed_out) routed_out[o] = routed;
-    if (shared_out) shared_out[o] = rows[(size_t)k * hidden + h];
-    if (out) {
-      out[o] = with_shared ? f32_to_bf16_rne(bf16_to_f32(routed) + bf16_to_f32(rows[(size_t)k * hidden + h]))
-                           : routed;
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;   // 8-column vector
+  if (v * 8 >= hidden) return;
+  const uint16_t *rows = down + (size_t)t * (k + 1) * hidden + (size_t)v * 8;
+  const bool need_shared = with_shared || shared_out;
+  uint4 r[kMoeMaxK];
+  float w[kMoeMaxK];
+#pragma unroll
+  for (int s = 0; s < kMoeMaxK; ++s) {
+    r[s] = make_uint4(0, 0, 0, 0);
+    if (s < k) r[s] = __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)s * hidden));
+  }
+  // the shared row by its own load: selecting r[k] would index the array at
+  // run time and move it to local memory
+  const uint4 sh = need_shared ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)k * hidden))
+                               : make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int s = 0; s < kMoeMaxK; ++s) w[s] = s < k ? __ldcg(slot_w + (size_t)t * k + s) : 0.f;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  // product rounded, then sum rounded -- as the reference's f32 numpy update
+  // (no fused multiply-add contraction)
+#pragma unroll
+  for (int s = 0; s < kMoeMaxK; ++s) {
+    if (s < k) {
+      const uint32_t q[4] = {r[s].x, r[s].y, r[s].z, r[s].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(bf16_to_f32(q[j] & 0xFFFFu), w[s]));
+        acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(bf16_to_f32(q[j] >> 16), w[s]));
+      }
     }
   }
+  const uint32_t shw[4] = {sh.x, sh.y, sh.z, sh.w};
+  uint32_t ro[4], oo[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t lo = f32_to_bf16_rne(acc[2 * j]), hi = f32_to_bf16_rne(acc[2 * j + 1]);
+    ro[j] = lo | (hi << 16);
+    if (with_shared) {
+      const uint32_t olo = f32_to_bf16_rne(bf16_to_f32(lo) + bf16_to_f32(shw[j] & 0xFFFFu));
+      const uint32_t ohi = f32_to_bf16_rne(bf16_to_f32(hi) + bf16_to_f32(shw[j] >> 16));
+      oo[j] = olo | (ohi << 16);
+    } else {
+      oo[j] = ro[j];
+    }
+  }
+  const size_t o = (size_t)t * hidden + (size_t)v * 8;
+  if (routed_out) *reinterpret_cast<uint4 *>(routed_out + o) = make_uint4(ro[0], ro[1], ro[2], ro[3]);
+  if (shared_out) *reinterpret_cast<uint4 *>(shared_out + o) = sh;
+  if (out) *reinterpret_cast<uint4 *>(out + o) = make_uint4(oo[0], oo[1], oo[2], oo[3]);
 }
 
 }  // namespace rc
@@ -519,14 +643,9 @@ struct rc_moe {
 
 namespace rc {
 
-static size_t moe_smem_bytes(int stage_blocks, int k, int stages) {
-  return (size_t)kMoeWarps * stages * (kUnitBytes + 8) + xfrag_bytes(stage_blocks, k) + gsum_bytes(stage_blocks, k);
-}
-
-static int moe_stages(int stage_blocks, int k, int units_per_warp) {
-  int s = units_per_warp < 2 ? 2 : (units_per_warp > kMoeMaxStages ? kMoeMaxStages : units_per_warp);
-  while (s > 2 && moe_smem_bytes(stage_blocks, k, s) > (size_t)kGemvSmemLimit) --s;
-  return s;
+static size_t moe_smem_bytes(int stage_blocks, int k, int stages, int partial_bytes) {
+  return (size_t)kMoeWarps * stages * (kUnitBytes + 8) + xfrag_bytes(stage_blocks, k) + gsum_bytes(stage_blocks, k) +
+         partial_bytes;
 }
 
 template <int EPI, int NTB>
@@ -542,21 +661,27 @@ static cudaError_t launch_moe_gemv_t(const rc_ctx *ctx, MoeGemvParams p, int max
     if (dev < 64) configured[dev] = true;
   }
   const int max_tiles = max_groups * p.group_tiles;
-  int grid = (max_tiles + kMoeWarps - 1) / kMoeWarps;
-  if (grid > ctx->sm_count) grid = ctx->sm_count;
-  if (grid < 1) grid = 1;
+  int grid = ctx->sm_count;
   if (EPI == kMoeEpiDown) {
     // a CTA's contiguous range of `per` tiles touches at most
     // kMoeMaxGroupsPerCta groups when per - 1 <= (kMoeMaxGroupsPerCta - 1) * group_tiles
     while ((max_tiles + grid - 1) / grid - 1 > (kMoeMaxGroupsPerCta - 1) * p.group_tiles) grid *= 2;
   }
-  const int W = grid * kMoeWarps;
-  const int tiles_per_warp = (max_tiles + W - 1) / W;
+  const int per = (max_tiles + grid - 1) / grid;
   const int stage_blocks = EPI == kMoeEpiGlu ? NTB : NTB * kMoeMaxGroupsPerCta;
   const int k = p.kb * kUnitK;
-  p.stages = moe_stages(stage_blocks, k, tiles_per_warp * p.kb);
-  const size_t smem = moe_smem_bytes(stage_blocks, k, p.stages);
+  const int unit_partial = NTB * 32 * 16;                  // bytes per unit partial
+  int R = kMoePartialBytes / (p.kb * unit_partial);
+  if (R < 1) R = 1;
+  if (R > per) R = per;
+  const int units_per_warp = (per * p.kb + kMoeWarps - 1) / kMoeWarps;
+  int S = units_per_warp < 2 ? 2 : (units_per_warp > kMoeMaxStages ? kMoeMaxStages : units_per_warp);
+  while (S > 2 && moe_smem_bytes(stage_blocks, k, S, R * p.kb * unit_partial) > (size_t)kGemvSmemLimit) --S;
+  while (R > 1 && moe_smem_bytes(stage_blocks, k, S, R * p.kb * unit_partial) > (size_t)kGemvSmemLimit) --R;
+  const size_t smem = moe_smem_bytes(stage_blocks, k, S, R * p.kb * unit_partial);
   if (smem > (size_t)kGemvSmemLimit) return cudaErrorInvalidConfiguration;
+  p.stages = S;
+  p.round_tiles = R;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kMoeWarps * 32);
@@ -600,9 +725,13 @@ static int max_groups(int T, int k, const MoeOwned &own) {
 // shared_gu instead when it is given), then the down GEMV into down_out
 // [T][k+1][hidden].
 static int moe_run_experts(rc_moe *m, const uint16_t *x, int T, int k, const MoeOwned &own, int act, float gb,
-                           float vb, const uint16_t *shared_gu, uint16_t *down_out, cudaStream_t s) {
+                           float vb, const uint16_t *shared_gu, uint16_t *down_out, bool zero_foreign,
+                           cudaStream_t s) {
   const int ntb = T <= 8 ? 1 : 2;
   const int mg = max_groups(T, k, own);
+  const bool glu_launch = mg - (shared_gu && own.shared_mask ? 1 : 0) > 0;
+  if (zero_foreign && !glu_launch)
+    RC_CUDA_TRY(cudaMemsetAsync(down_out, 0, (size_t)T * (k + 1) * m->hidden * 2, s));
   if (mg == 0) return RC_OK;
   MoeGemvParams g{};
   g.expert_tiles = m->gu_tiles;
@@ -626,6 +755,11 @@ static int moe_run_experts(rc_moe *m, const uint16_t *x, int T, int k, const Moe
   g.gate_beta = gb;
   g.value_beta = vb;
   g.err = m->ctx->err;
+  g.zero_rows = zero_foreign ? down_out : nullptr;
+  g.slot_expert = m->s.slot_expert;
+  g.k = k;
+  g.hidden = m->hidden;
+  g.own = own;
   cudaError_t e = cudaSuccess;
   if (mg - g.skip_last_group > 0) e = launch_moe_gemv<kMoeEpiGlu>(m->ctx, g, mg - g.skip_last_group, s);
   if (e != cudaSuccess) {
@@ -645,6 +779,7 @@ static int moe_run_experts(rc_moe *m, const uint16_t *x, int T, int k, const Moe
   MoeGemvParams d = g;
   d.expert_tiles = m->dn_tiles;
   d.skip_last_group = 0;
+  d.zero_rows = nullptr;
   d.group_tiles = m->hidden / kUnitRows;
   d.kb = m->inter_pad / kUnitK;
   d.x = m->act;
@@ -662,8 +797,12 @@ static int moe_run_experts(rc_moe *m, const uint16_t *x, int T, int k, const Moe
 
 static int moe_combine(rc_moe *m, const uint16_t *down, const float *slot_w, int T, int k, int with_shared,
                        uint16_t *out, uint16_t *routed_out, uint16_t *shared_out, cudaStream_t s) {
+  auto mis = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
+  RC_CHECK_ARG(!mis(down) && !mis(out) && !mis(routed_out) && !mis(shared_out),
+               "MoE slot and output rows must be 16-byte aligned");
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = small_cfg(dim3((m->hidden + 255) / 256, T), dim3(256), s, attr);
+  cudaLaunchConfig_t cfg = small_cfg(dim3((m->hidden / 8 + kCombineThreads - 1) / kCombineThreads, T),
+                                     dim3(kCombineThreads), s, attr);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_combine_kernel, down, slot_w, k, with_shared, m->hidden, out,
                                            routed_out, shared_out);
   if (e != cudaSuccess) {
@@ -674,7 +813,8 @@ static int moe_combine(rc_moe *m, const uint16_t *down, const float *slot_w, int
 }
 
 static int moe_route(rc_moe *m, const uint16_t *x, int T, int k, int mode, int renorm, float scaling,
-                     const MoeOwned &own, cudaStream_t s) {
+                     const MoeOwned &own, cudaStream_t s, const MoeScratch *scratch = nullptr) {
+  RC_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0, "token rows must be 16-byte aligned");
   RouteParams r{};
   r.x = x;
   r.ldx = m->hidden;
@@ -687,13 +827,32 @@ static int moe_route(rc_moe *m, const uint16_t *x, int T, int k, int mode, int r
   r.scaling = scaling;
   r.wr = m->router_w;
   r.bias = m->router_bias;
-  r.s = m->s;
+  r.s = scratch ? *scratch : m->s;
   r.shared_id = m->has_shared ? m->n_experts : -1;
   r.own = own;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess && (dev >= 64 || !configured[dev])) {
+    constexpr int kPhase1Max = kMoeMaxTokens * kRouteChunk * 2;
+    constexpr int kPhase2Max = kMoeMaxTokens * kMoeMaxExperts * 12 + kMoeMaxTokens * kMoeMaxK * 8;
+    e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kPhase1Max > kPhase2Max ? kPhase1Max : kPhase2Max);
+    if (e == cudaSuccess && dev < 64) configured[dev] = true;
+  }
+  if (e != cudaSuccess) {
+    set_error("moe router setup: %s", cudaGetErrorString(e));
+    return RC_ERR_CUDA;
+  }
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = small_cfg(
-      dim3((m->n_experts + kRouteExpertsPerCta - 1) / kRouteExpertsPerCta, T), dim3(kRouteThreads), s, attr);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_route_kernel, r);
+  cudaLaunchConfig_t cfg = small_cfg(dim3((m->n_experts + kRouteExpertsPerCta - 1) / kRouteExpertsPerCta),
+                                     dim3(kRouteThreads), s, attr);
+  const int chunk = m->hidden < kRouteChunk ? m->hidden : kRouteChunk;
+  const size_t phase1 = (size_t)T * chunk * 2;
+  const size_t phase2 = (size_t)T * m->n_experts * 12 + (size_t)T * k * 8;
+  const size_t need = phase1 > phase2 ? phase1 : phase2;
+  cfg.dynamicSmemBytes = (need + 15) / 16 * 16;
+  e = cudaLaunchKernelEx(&cfg, moe_route_kernel, r);
   if (e != cudaSuccess) {
     set_error("moe router launch: %s", cudaGetErrorString(e));
     return RC_ERR_CUDA;
@@ -882,7 +1041,7 @@ int rc_moe_experts(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_d
   const MoeOwned own = all_owned(m, T, with_shared);
   int rc = moe_slots(m, ids_dev, w_dev, T, k, own, s);
   if (rc) return rc;
-  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, m->down_out, s);
+  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, m->down_out, false, s);
   if (rc) return rc;
   return moe_combine(m, m->down_out, m->s.slot_w, T, k, with_shared, out_dev, nullptr, nullptr, s);
 }
@@ -939,7 +1098,7 @@ int rc_moe_experts_grouped(rc_moe *m, const uint16_t *x_dev, int T, const int32_
   const MoeOwned own = all_owned(m, T, shared_gu_dev != nullptr);
   int rc = moe_slots(m, ids_dev, w_dev, T, k, own, s);
   if (rc) return rc;
-  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, shared_gu_dev, m->down_out, s);
+  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, shared_gu_dev, m->down_out, false, s);
   if (rc) return rc;
   return moe_combine(m, m->down_out, m->s.slot_w, T, k, 0, nullptr, routed_out_dev,
                      shared_gu_dev ? shared_out_dev : nullptr, s);
@@ -959,7 +1118,7 @@ int rc_moe_decode(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, in
   const cudaStream_t s = pick_stream(m->ctx, stream);
   rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, own, s);
   if (rc) return rc;
-  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, m->down_out, s);
+  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, m->down_out, false, s);
   if (rc) return rc;
   rc = moe_combine(m, m->down_out, m->s.slot_w, T, k, m->has_shared, out_dev, nullptr, nullptr, s);
   if (rc) return rc;
@@ -987,15 +1146,15 @@ int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int rout
   if (rc) return rc;
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   const cudaStream_t s = pick_stream(m->ctx, stream);
-  // slot rows of experts computed elsewhere stay zero, so the ranks' slot rows
-  // can be summed in the exchange (x + 0 = x exactly)
-  RC_CUDA_TRY(cudaMemsetAsync(slot_out_dev, 0, (size_t)T * (k + 1) * m->hidden * 2, s));
-  rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, own, s);
+  // The router writes the slot weights straight into slot_w_dev; slot rows of
+  // experts computed elsewhere are zeroed by the gate/up launch, so the
+  // ranks' slot rows can be summed in the exchange (x + 0 = x exactly).
+  RC_CHECK_ARG((reinterpret_cast<uintptr_t>(slot_out_dev) & 15) == 0, "slot_out must be 16-byte aligned");
+  MoeScratch sc = m->s;
+  sc.slot_w = slot_w_dev;
+  rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, own, s, &sc);
   if (rc) return rc;
-  rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, slot_out_dev, s);
-  if (rc) return rc;
-  RC_CUDA_TRY(cudaMemcpyAsync(slot_w_dev, m->s.slot_w, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
-  return RC_OK;
+  return moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, slot_out_dev, true, s);
 }
 
 int rc_moe_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int T, int k, int with_shared,

@@ -69,6 +69,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// mbar_wait_bounded for a whole warp (every lane calls it): one verdict for
+// all lanes, so a timeout never splits the warp before warp-wide instructions.
+__device__ __forceinline__ bool mbar_wait_bounded_warp(uint32_t bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
+}
+
 // ---------------------------------------------------------- bulk copies --
 // L2 policy for data that is streamed exactly once (weights).
 __device__ __forceinline__ uint64_t policy_evict_first() {
