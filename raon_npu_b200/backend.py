@@ -21,7 +21,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from .device import Context, Q4nxWeight
+from .device import Context, MoeLayer, Q4nxWeight
 
 
 class Backend(ABC):
@@ -43,6 +43,12 @@ class Backend(ABC):
                     gate_beta: float = 4.0, value_beta: float = 25.0,
                     shared_gu: np.ndarray | None = None) -> np.ndarray:
         """Weighted sum of routed experts for one token (host/backend.py:98-117)."""
+
+    def moe_experts_grouped(self, layer: int, x: np.ndarray, top_ids: np.ndarray, top_weights: np.ndarray,
+                            shared_gu: np.ndarray, gate_beta: float = 4.0,
+                            value_beta: float = 25.0) -> tuple[np.ndarray, np.ndarray]:
+        """Routed sums and shared down rows for T tokens (npu/backend.py:4845-4979)."""
+        raise NotImplementedError
 
     def moe_prestart_shared(self, layer: int, x: np.ndarray) -> None:
         """Overlap hook; results never depend on it (host/backend.py:119-125)."""
@@ -74,8 +80,46 @@ class _Slice:
     row_end: int
 
 
+def _bf16_input(x, hidden: int, what: str) -> np.ndarray:
+    """bf16 bits of one token row; f32 rows are rounded (RTNE, NaN -> 0x7FC0)."""
+    x = np.asarray(x)
+    if x.shape != (hidden,):
+        raise ValueError(f"{what} must have shape [{hidden}], got {x.shape}")
+    if x.dtype == np.uint16:
+        return x
+    if x.dtype == np.float32:
+        u = x.view(np.uint32).astype(np.uint64)
+        r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+        r[np.isnan(x)] = 0x7FC0
+        return r
+    raise ValueError(f"{what} must be uint16 (bf16 bits) or float32, got {x.dtype}")
+
+
+def check_moe_routes(top_ids, top_weights, n_experts: int, k: int, tokens: int | None = None):
+    """The reference's route validation (npu/backend.py:4866-4900, 5047-5056):
+    integer ids in range and distinct per token, f32 weights of the same shape.
+    Returns (ids int32 [T, k], weights f32 [T, k])."""
+    ids = np.asarray(top_ids)
+    w = np.asarray(top_weights)
+    T = ids.shape[0] if ids.ndim == 2 else -1
+    if ids.ndim != 2 or not np.issubdtype(ids.dtype, np.integer) or (tokens is not None and T != tokens) \
+            or not 1 <= k <= min(16, n_experts) or ids.shape[1] != k:
+        raise ValueError(f"top_ids must be an integer ndarray with shape [T, k], k in 1..{min(16, n_experts)}")
+    if np.any(ids < 0) or np.any(ids >= n_experts):
+        raise ValueError(f"top_ids values must be in 0..{n_experts - 1}")
+    srt = np.sort(ids, axis=1)
+    if np.any(srt[:, 1:] == srt[:, :-1]):
+        raise ValueError(f"each token must route to {k} distinct experts")
+    if w.shape != ids.shape or w.dtype != np.float32:
+        raise ValueError(f"top_weights must be a float32 ndarray with shape {ids.shape}")
+    return ids.astype(np.int32), w
+
+
 class CudaBackend(Backend):
     """GEMV / MoE on a B200 through ``libraon_cuda.so``.
+
+    MoE layers: ``register_moe_layer`` + ``register_moe_expert`` per expert;
+    ``moe_experts`` / ``moe_experts_grouped`` then run on the device.
 
     ``register_bundle(bundle, packed, n, k)`` uploads one ``pack_gemv`` matrix;
     ``map_name(name, bundle, row_start, row_end)`` exposes a row slice of it
@@ -85,6 +129,8 @@ class CudaBackend(Backend):
     unpadded activation (the reference's ``padded_k`` handling).
     """
 
+    prefill_grouped_moe = True
+
     def __init__(self, device: int = 0):
         self.ctx = Context(device)
         self._bundles: dict[str, Q4nxWeight] = {}
@@ -92,6 +138,7 @@ class CudaBackend(Backend):
         self._orig_k: dict[str, int] = {}
         self._bias: dict[str, int] = {}                   # name -> device address of its bundle's bias
         self._bundle_bias_host: dict[str, np.ndarray] = {}
+        self._moe: dict[int, tuple[MoeLayer, str]] = {}   # layer -> (experts on the device, activation)
 
     # ------------------------------------------------------------ weights --
     def register_bundle(self, bundle: str, packed, n: int, k: int) -> Q4nxWeight:
@@ -171,8 +218,89 @@ class CudaBackend(Backend):
     def mla_attend_chunk(self, *a, **k):
         raise NotImplementedError("mla_attend_chunk is outside the GEMV/MoE path of this backend")
 
+    # ---------------------------------------------------------------- MoE --
+    def register_moe_layer(self, layer: int, hidden: int, inter: int, n_experts: int, act: str = "situ",
+                           has_shared: bool = False) -> MoeLayer:
+        """Create MoE layer ``layer`` (experts registered with ``register_moe_expert``).
+        ``act`` is the GLU of the experts: "situ" (the reference model's) or "swiglu"."""
+        if act not in ("situ", "swiglu"):
+            raise ValueError(f"unknown activation {act!r}")
+        old = self._moe.pop(int(layer), None)
+        if old is not None:
+            old[0].close()
+        m = MoeLayer(self.ctx, hidden, inter, n_experts, has_shared=has_shared)
+        self._moe[int(layer)] = (m, act)
+        return m
+
+    def register_moe_expert(self, layer: int, expert: int, gate_up_packed, down_packed) -> None:
+        """Expert ``expert`` of ``layer`` (``n_experts`` = the shared expert): the
+        reference's expert packing (kernels/moe/pack.py:136-224), pack_gemv bytes of
+        the stacked [gate; up] matrix and of the K-padded down matrix."""
+        self._moe_layer(layer)[0].set_expert(int(expert), gate_up_packed, down_packed)
+
+    def _moe_layer(self, layer):
+        if not isinstance(layer, (int, np.integer)):
+            raise ValueError("layer must be an integer")
+        entry = self._moe.get(int(layer))
+        if entry is None:
+            raise ValueError(f"layer {layer} is not a registered MoE layer")
+        return entry
+
     def moe_experts(self, layer, x, top_ids, top_weights, gate_beta=4.0, value_beta=25.0, shared_gu=None):
-        raise NotImplementedError("register an MoE layer first")
+        """Routed experts of one token: ascending-ID f32 sum of w_e * down_e, RTNE
+        (host/backend.py:466-510).  f32 ``x`` is rounded to bf16 first, as the
+        device backend does (npu/backend.py:5059).  ``shared_gu`` is accepted and
+        not used: the shared expert stays with the caller (host/raon.py:1308-1327)."""
+        m, act = self._moe_layer(layer)
+        x_u16 = _bf16_input(x, m.hidden, "x")
+        ids, w = check_moe_routes(np.asarray(top_ids)[None], np.asarray(top_weights)[None], m.n_experts,
+                                  np.asarray(top_ids).shape[-1] if np.ndim(top_ids) else 0)
+        return m.experts_host(x_u16, ids[0], w[0], act=act, gate_beta=gate_beta, value_beta=value_beta)
+
+    def moe_experts_grouped(self, layer, x, top_ids, top_weights, shared_gu, gate_beta=4.0, value_beta=25.0):
+        """T tokens at once (npu/backend.py:4845-4979): returns (routed [T, C],
+        shared_down [T, C]), shared_down = down(RTNE(act(shared_gu))) of the
+        layer's shared expert.  Token rows are independent, so any T is
+        processed in device calls of up to 16 tokens with identical bytes."""
+        import torch
+        m, act = self._moe_layer(layer)
+        if not isinstance(x, np.ndarray) or x.dtype != np.uint16 or x.ndim != 2 or x.shape[1] != m.hidden \
+                or x.shape[0] < 1:
+            raise ValueError(f"x must be a [T, {m.hidden}] uint16 ndarray with T >= 1")
+        T = x.shape[0]
+        k = np.asarray(top_ids).shape[-1] if np.ndim(top_ids) == 2 else 0
+        ids, w = check_moe_routes(top_ids, top_weights, m.n_experts, k, tokens=T)
+        if not m.has_shared:
+            raise ValueError(f"layer {layer} has no shared expert")
+        if not isinstance(shared_gu, np.ndarray) or shared_gu.dtype != np.uint16 \
+                or shared_gu.shape != (T, 2 * m.inter):
+            raise ValueError(f"shared_gu must be a [T, {2 * m.inter}] uint16 ndarray")
+        dev = torch.device("cuda", self.ctx.device)
+        routed = np.empty((T, m.hidden), np.uint16)
+        shared = np.empty((T, m.hidden), np.uint16)
+        for t0 in range(0, T, 16):
+            t1 = min(T, t0 + 16)
+            xd = torch.from_numpy(np.ascontiguousarray(x[t0:t1]).view(np.int16)).to(dev)
+            idd = torch.from_numpy(np.ascontiguousarray(ids[t0:t1])).to(dev)
+            wd = torch.from_numpy(np.ascontiguousarray(w[t0:t1])).to(dev)
+            gd = torch.from_numpy(np.ascontiguousarray(shared_gu[t0:t1]).view(np.int16)).to(dev)
+            ro = torch.empty((t1 - t0, m.hidden), dtype=torch.int16, device=dev)
+            so = torch.empty((t1 - t0, m.hidden), dtype=torch.int16, device=dev)
+            m.experts_grouped(xd, idd, wd, k, ro, gd, so, act=act, gate_beta=gate_beta, value_beta=value_beta)
+            routed[t0:t1] = ro.cpu().numpy().view(np.uint16)
+            shared[t0:t1] = so.cpu().numpy().view(np.uint16)
+        self.ctx.sync()
+        return routed, shared
 
     def reset(self) -> None:
         return None
+
+    def close(self) -> None:
+        """Release every device resource of this backend."""
+        for m, _ in self._moe.values():
+            m.close()
+        self._moe.clear()
+        for w in self._bundles.values():
+            w.free()
+        self._bundles.clear()
+        self.ctx.close()
