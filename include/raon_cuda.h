@@ -34,7 +34,7 @@ extern "C" {
 #define RC_ACT_SWIGLU 0 /* g*sigmoid(g)*u        (kernels/moe/reference.py:160-170) */
 #define RC_ACT_SITU 1   /* SiTU-GLU with betas   (host/backend.py:47-62)            */
 
-#define RC_ROUTER_SOFTMAX 0      /* softmax(x.Wr) -> top-k -> renormalise                  */
+#define RC_ROUTER_SOFTMAX 0      /* softmax(x.Wr + b) -> top-k -> renormalise (b: router bias, 0 unless set) */
 #define RC_ROUTER_SIGMOID_BIAS 1 /* sigmoid, top-k of score+bias (host/raon.py:1224-1247) */
 
 /* Upload flags. */
@@ -192,6 +192,37 @@ int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int rout
                         float *slot_w_dev, void *stream);
 int rc_moe_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int T, int k,
                    int with_shared, uint16_t *out_dev, void *stream);
+
+/* MoE prefill: the layer for T <= 4096 tokens on the 5th-generation tensor
+ * cores (tcgen05 grouped GEMM over expert-sorted token rows; the reference's
+ * grouped path, npu/backend.py:4845-4979 with kernels/moe_grouped/
+ * planner.py:76-108,286-322).  Same semantics as rc_moe_decode: router
+ * (top-k ids / weights [T][k] copied out when given), routed experts summed
+ * in ascending ID in f32 then RTNE, plus the shared expert.  x and out are
+ * [T][hidden] bf16, 16-byte aligned.  Scratch grows on the first call for a
+ * larger T (that call synchronises the device). */
+int rc_moe_prefill(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize,
+                   float scaling, int act, float gate_beta, float value_beta, uint16_t *out_dev,
+                   int32_t *ids_dev, float *w_dev, void *stream);
+
+/* rc_moe_prefill for caller-supplied routes ids / w [T][k] (distinct ids per
+ * token; an id whose expert is not loaded sets the device error word). */
+int rc_moe_prefill_experts(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev,
+                           const float *w_dev, int k, int act, float gate_beta, float value_beta,
+                           int with_shared, uint16_t *out_dev, void *stream);
+
+/* Expert-parallel halves of rc_moe_prefill, as rc_moe_decode_local /
+ * rc_moe_combine: slot rows slot_out [T][k+1][hidden] of the routed experts
+ * [expert_lo, expert_hi) and of the shared expert for tokens
+ * [shared_t0, shared_t0 + shared_tn), zeros elsewhere, and the slot weights
+ * [T][k]; after the ranks' slot rows are summed, rc_moe_prefill_combine gives
+ * the bytes of rc_moe_prefill on one GPU. */
+int rc_moe_prefill_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize,
+                         float scaling, int act, float gate_beta, float value_beta, int expert_lo,
+                         int expert_hi, int shared_t0, int shared_tn, uint16_t *slot_out_dev,
+                         float *slot_w_dev, void *stream);
+int rc_moe_prefill_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int T,
+                           int k, int with_shared, uint16_t *out_dev, void *stream);
 
 /* rc_gemv without any device allocation (this entry point has no counterpart
  * in the reference).  Arguments and results are those of rc_gemv; the context

@@ -67,6 +67,10 @@ SIGNATURES = {
     "rc_moe_decode": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _P, _P, _P, _P]),
     "rc_moe_decode_local": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _I, _I, _I, _I, _P, _P, _P]),
     "rc_moe_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _P]),
+    "rc_moe_prefill": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _P, _P, _P, _P]),
+    "rc_moe_prefill_experts": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _F, _I, _P, _P]),
+    "rc_moe_prefill_local": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _I, _I, _I, _I, _P, _P, _P]),
+    "rc_moe_prefill_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _P]),
 }
 
 _lib = None

@@ -1,0 +1,63 @@
+// Definitions shared by the MoE translation units (decode: q4nx_moe.cu,
+// prefill: q4nx_prefill.cu): limits, the per-layer device scratch and the
+// layer object behind the C-ABI handle ``rc_moe``.
+#pragma once
+
+#include <stdint.h>
+
+#include "rc_internal.cuh"
+
+namespace rc {
+
+constexpr int kMoeMaxK = 16;               // routed experts per token
+constexpr int kMoeMaxTokens = 16;          // tokens per call: two 8-column mma blocks
+constexpr int kMoeMaxExperts = 256;
+constexpr int kMoeWarps = 16;
+constexpr int kMoePartialBytes = 32 * 1024;   // per-CTA unit partials of one round
+constexpr int kMoeMaxStages = 8;
+constexpr int kMoeMaxGroupsPerCta = 4;     // down kernel: groups one CTA's tile range may touch
+
+// Per-call device scratch of a layer.
+struct MoeScratch {
+  float *logits;           // [T][E]
+  int *counter;            // [T + 1] arrival counters (per token, then "all tokens"), zero between calls
+  int32_t *ids;            // [T][k] rank order (best first)
+  float *weights;          // [T][k]
+  int32_t *slot_expert;    // [T][k+1] ascending ID, then the shared expert (or -1)
+  float *slot_w;           // [T][k]   weights in slot order
+  int *n_groups;           // [1]
+  int32_t *group_expert;   // [E+1]
+  uint32_t *group_mask;    // [E+1] tokens of each group
+  int32_t *group_dst;      // [E+1][16] slot row of (group, token)
+};
+
+// What one rank computes: routed experts [lo, hi) for every token, the shared
+// expert (id E) for the tokens in shared_mask.
+struct MoeOwned {
+  int lo, hi;
+  uint32_t shared_mask;
+};
+
+struct PfScratch;   // prefill scratch (q4nx_prefill.cu)
+
+}  // namespace rc
+
+// ------------------------------------------------------------- MoE object --
+struct rc_moe {
+  rc_ctx *ctx;
+  int hidden, inter, inter_pad, n_experts, has_shared;
+  rc_weight **gate_up;        // [E+1] host table of handles (null: not on this rank)
+  rc_weight **down;
+  const uint8_t **gu_tiles;   // [E+1] device pointer tables
+  const uint8_t **dn_tiles;
+  uint16_t *router_w;         // [E][hidden] bf16
+  float *router_bias;         // [E]
+  rc::MoeScratch s;
+  uint16_t *act;              // [E+1][16][inter_pad]  (pad columns stay zero)
+  uint16_t *down_out;         // [16][kMax+1][hidden]
+  rc::PfScratch *pf;          // prefill scratch, grown on demand (null until the first prefill)
+};
+
+namespace rc {
+void pf_free(rc_moe *m);   // releases m->pf (q4nx_prefill.cu)
+}  // namespace rc

@@ -34,40 +34,12 @@
 // byte for byte.
 #include <string.h>
 
+#include "moe_internal.cuh"
 #include "q4nx_core.cuh"
 #include "rc_device.cuh"
 #include "rc_internal.cuh"
 
 namespace rc {
-
-constexpr int kMoeMaxK = 16;               // routed experts per token
-constexpr int kMoeMaxTokens = 16;          // tokens per call: two 8-column mma blocks
-constexpr int kMoeMaxExperts = 256;
-constexpr int kMoeWarps = 16;
-constexpr int kMoePartialBytes = 32 * 1024;   // per-CTA unit partials of one round
-constexpr int kMoeMaxStages = 8;
-constexpr int kMoeMaxGroupsPerCta = 4;     // down kernel: groups one CTA's tile range may touch
-
-// Per-call device scratch of a layer.
-struct MoeScratch {
-  float *logits;           // [T][E]
-  int *counter;            // [T + 1] arrival counters (per token, then "all tokens"), zero between calls
-  int32_t *ids;            // [T][k] rank order (best first)
-  float *weights;          // [T][k]
-  int32_t *slot_expert;    // [T][k+1] ascending ID, then the shared expert (or -1)
-  float *slot_w;           // [T][k]   weights in slot order
-  int *n_groups;           // [1]
-  int32_t *group_expert;   // [E+1]
-  uint32_t *group_mask;    // [E+1] tokens of each group
-  int32_t *group_dst;      // [E+1][16] slot row of (group, token)
-};
-
-// What one rank computes: routed experts [lo, hi) for every token, the shared
-// expert (id E) for the tokens in shared_mask.
-struct MoeOwned {
-  int lo, hi;
-  uint32_t shared_mask;
-};
 
 // ------------------------------------------------------------ grouping --
 // One warp.  Reads the slot lists of T tokens (written by other threads or
@@ -230,10 +202,13 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
   float *selw = reinterpret_cast<float *>(sel + T * k);     // [T][k] weight of each rank
   for (int i = threadIdx.x; i < T * E; i += blockDim.x) {
     const float l = __ldcg(p.s.logits + i);
-    float sc = l, v = l;
+    float sc, v;
     if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
       sc = __double2float_rn(1.0 / (1.0 + exp(-(double)l)));
       v = sc + p.bias[i % E];
+    } else {
+      sc = l + p.bias[i % E];          // softmax of the biased logits (bias zero unless set)
+      v = sc;
     }
     score[i] = sc;
     val[i] = v;
@@ -626,20 +601,6 @@ __global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(const uint
 
 using namespace rc;
 
-// ------------------------------------------------------------- MoE object --
-struct rc_moe {
-  rc_ctx *ctx;
-  int hidden, inter, inter_pad, n_experts, has_shared;
-  rc_weight **gate_up;        // [E+1] host table of handles (null: not on this rank)
-  rc_weight **down;
-  const uint8_t **gu_tiles;   // [E+1] device pointer tables
-  const uint8_t **dn_tiles;
-  uint16_t *router_w;         // [E][hidden] bf16
-  float *router_bias;         // [E]
-  MoeScratch s;
-  uint16_t *act;              // [E+1][16][inter_pad]  (pad columns stay zero)
-  uint16_t *down_out;         // [16][kMax+1][hidden]
-};
 
 namespace rc {
 
@@ -952,6 +913,7 @@ int rc_moe_destroy(rc_moe *m) {
   if (!m) return RC_OK;
   cudaSetDevice(m->ctx->device);
   cudaDeviceSynchronize();
+  pf_free(m);
   for (int e = 0; e <= m->n_experts; ++e) {
     if (m->gate_up && m->gate_up[e]) rc_weight_free(m->gate_up[e]);
     if (m->down && m->down[e]) rc_weight_free(m->down[e]);

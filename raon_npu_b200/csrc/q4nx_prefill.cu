@@ -1,0 +1,959 @@
+// MoE prefill on the q4nx experts: a grouped GEMM on the 5th-generation
+// tensor cores (tcgen05, accumulators in tensor memory).
+//
+// Reference semantics are the decode path's (host/backend.py:466-510 per
+// token; the grouped combine of kernels/moe_grouped/planner.py:286-322):
+// gate/up linear (bf16), act -> RTNE, down linear (bf16), routed outputs
+// summed in ascending expert ID in f32 then RTNE, plus the shared expert.
+//
+// Pipeline for T tokens (T <= 4096):
+//   logits    f64 sums of exact bf16 products, rounded once to f32 (as decode)
+//   select    one warp per token: top-k (lower index wins ties), weights,
+//             ascending-ID slot list
+//   plan      one CTA: per-expert token bitmaps -> expert-sorted row order
+//             (tokens ascending within an expert), 64-row chunks
+//   gate/up   tcgen05 grouped GEMM, epilogue GLU -> act rows (permuted order)
+//   down      tcgen05 grouped GEMM -> down rows (permuted order)
+//   combine   per token, its slot rows in ascending ID (f32 multiply, then
+//             add, no FMA), RTNE, plus the shared row
+//
+// The grouped GEMM (one CTA per SM, 4 warps, persistent over work items
+// (64-token chunk, 128-row weight tile)):
+//   A  weight tile: the q4nx codes of 128 rows x 256 columns arrive by bulk
+//      copy in the t16 upload layout and are written to shared memory as
+//      bf16 (128 + code) -- exact -- in the 128-byte-swizzled K-major layout
+//      the tensor core reads;
+//   B  the chunk's 64 token rows x 256 columns, fetched with cp.async (the
+//      gate/up stage gathers them from x through the plan), swizzled the
+//      same way; the per-32-column group sums S of the rows come with them;
+//   D  one tcgen05.mma chain of K = 32 per quantisation group into its own
+//      tensor-memory accumulator (8 groups x 64 columns = 512 columns);
+//   promotion: thread r (= TMEM lane = weight row r) reads the 8 group
+//      accumulators with tcgen05.ld and adds scale * D + (min - 128 scale) * S
+//      in f32 registers -- the same arithmetic as the decode GEMV and as the
+//      reference NPU kernel's per-group scaling (grouped_mmul.cc:196-254).
+#include <string.h>
+
+#include "moe_internal.cuh"
+#include "rc_device.cuh"
+#include "rc_internal.cuh"
+
+namespace rc {
+
+constexpr int kPfMaxTokens = 4096;
+constexpr int kPfRows = 128;         // weight rows per tile: MMA M, TMEM lanes
+constexpr int kPfCols = 64;          // token columns per work item: max MMA N
+constexpr int kPfThreads = 128;
+constexpr int kPfTmemCols = 512;     // 8 group accumulators x 64 columns
+constexpr int kPfGroups = 8;         // 32-column quantisation groups per 256-column block
+
+// shared-memory map of the GEMM kernel (offsets from a 1024-byte aligned base)
+constexpr int kPfA = 0;                              // 4 sub-tiles x [128 rows x 128 B]
+constexpr int kPfASub = kPfRows * 128;               // 16 KB
+constexpr int kPfB = 4 * kPfASub;                    // 2 stages x 4 sub-tiles x [64 rows x 128 B]
+constexpr int kPfBSub = kPfCols * 128;               // 8 KB
+constexpr int kPfBStage = 4 * kPfBSub;
+constexpr int kPfU = kPfB + 2 * kPfBStage;           // 2 stages x 8 units of 2560 B
+constexpr int kPfUStage = 8 * kUnitBytes;
+constexpr int kPfS = kPfU + 2 * kPfUStage;           // group sums [8][64] f32
+constexpr int kPfBar = kPfS + kPfGroups * kPfCols * 4;   // 3 mbarriers + TMEM address
+constexpr int kPfSmem = kPfBar + 64;
+constexpr int kPfSmemAlloc = kPfSmem + 1024;         // room to align the base
+constexpr int kPfPlanSmemMax = kGemvSmemLimit - 4 * 1024;   // dynamic part of the plan kernel
+
+struct PfScratch {
+  int T_cap, P_cap, chunk_cap, E1;
+  float *logits;            // [T][E]
+  int32_t *ids;             // [T][k] rank order
+  float *weights;           // [T][k]
+  int32_t *slot_expert;     // [T][k+1] ascending ID, then the shared expert (or -1)
+  float *slot_w;            // [T][k]
+  int32_t *slot_row;        // [T][k+1] permuted row of each slot, -1 if not computed here
+  int32_t *row_token;       // [P] token of each permuted row
+  int32_t *cnt, *off;       // [E+1]
+  int32_t *n_chunks;        // [1]
+  int32_t *chunk_expert, *chunk_row0, *chunk_n;
+  uint16_t *act;            // [P][inter_pad]
+  uint16_t *down;           // [P][hidden]
+};
+
+// ------------------------------------------------------------ small PTX --
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Descriptor of a K-major operand tile in the 128-byte swizzle layout: rows
+// 128 B apart, 8-row groups 1024 B apart (version 1, SWIZZLE_128B).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor: f32 accumulator, bf16 A and B, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// Byte offset of element (r, kk) (kk < 64) in a 128-byte-swizzled K-major tile.
+__device__ __forceinline__ uint32_t sw128_off(int r, int kk) {
+  return (r >> 3) * 1024 + (r & 7) * 128 + ((((kk >> 3) ^ r) & 7) << 4) + (kk & 7) * 2;
+}
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(addr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------- router --
+// logits[t][e] = f32(sum_h f64(x[t][h]) * f64(wr[e][h])): one warp per (token, expert).
+__global__ void __launch_bounds__(256) pf_logits_kernel(const uint16_t *x, int hidden, const uint16_t *wr, int E,
+                                                        float *logits) {
+  const int t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 8 + warp;
+  if (e >= E) return;
+  const uint4 *xv = reinterpret_cast<const uint4 *>(x + (size_t)t * hidden);
+  const uint4 *wv = reinterpret_cast<const uint4 *>(wr + (size_t)e * hidden);
+  double a0 = 0.0, a1 = 0.0;
+#pragma unroll 4
+  for (int c = lane; c < hidden / 8; c += 32) {
+    const uint4 xa = __ldg(xv + c), wa = __ldg(wv + c);
+    const uint32_t xs[4] = {xa.x, xa.y, xa.z, xa.w}, ws[4] = {wa.x, wa.y, wa.z, wa.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a0 = fma((double)bf16_to_f32(xs[j] & 0xFFFFu), (double)bf16_to_f32(ws[j] & 0xFFFFu), a0);
+      a1 = fma((double)bf16_to_f32(xs[j] >> 16), (double)bf16_to_f32(ws[j] >> 16), a1);
+    }
+  }
+  double a = a0 + a1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+  if (lane == 0) logits[(size_t)t * E + e] = __double2float_rn(a);
+}
+
+struct PfSelectParams {
+  const float *logits;
+  const float *bias;
+  int T, E, k, mode, renorm, shared_id;
+  float scaling;
+  int32_t *ids;
+  float *weights;
+  int32_t *slot_expert;
+  float *slot_w;
+};
+
+// One warp per token: k rounds of warp argmax (lower index wins ties), the
+// routing weights, the ascending-ID slot list.
+__global__ void __launch_bounds__(256) pf_select_kernel(PfSelectParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= p.T) return;
+  const float *lg = p.logits + (size_t)t * p.E;
+  constexpr int kPer = kMoeMaxExperts / 32;
+  float val[kPer], score[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int ei = lane + 32 * i;
+    val[i] = -INFINITY;
+    score[i] = 0.f;
+    if (ei < p.E) {
+      const float l = lg[ei];
+      if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
+        score[i] = __double2float_rn(1.0 / (1.0 + exp(-(double)l)));
+        val[i] = score[i] + p.bias[ei];
+      } else {
+        score[i] = l + p.bias[ei];
+        val[i] = score[i];
+      }
+    }
+  }
+  int sel[kMoeMaxK];
+  float sel_score[kMoeMaxK];
+#pragma unroll 1
+  for (int r = 0; r < p.k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int ei = lane + 32 * i;
+      if (ei < p.E && (val[i] > bv || (val[i] == bv && ei < bi))) bv = val[i], bi = ei;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+    }
+    float sc = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if (lane + 32 * i == bi) sc = score[i], val[i] = -INFINITY;
+    sc = __shfl_sync(0xffffffffu, sc, bi & 31);
+    if (lane == 0) {
+      sel[r] = bi;
+      sel_score[r] = sc;
+    }
+  }
+  if (lane != 0) return;
+  float w[kMoeMaxK];
+  if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
+    float sum = 0.f;
+    for (int r = 0; r < p.k; ++r) sum += sel_score[r];
+    for (int r = 0; r < p.k; ++r) {
+      float c = sel_score[r];
+      if (p.renorm) c = c / (sum + 1e-20f);
+      w[r] = c * p.scaling;
+    }
+  } else {
+    const float mx = sel_score[0];
+    float sum = 0.f;
+    for (int r = 0; r < p.k; ++r) sum += expf(sel_score[r] - mx);
+    for (int r = 0; r < p.k; ++r) w[r] = expf(sel_score[r] - mx) / sum;
+  }
+  for (int r = 0; r < p.k; ++r) {
+    p.ids[(size_t)t * p.k + r] = sel[r];
+    p.weights[(size_t)t * p.k + r] = w[r];
+  }
+  int32_t *se = p.slot_expert + (size_t)t * (p.k + 1);
+  float *sw = p.slot_w + (size_t)t * p.k;
+  for (int r = 0; r < p.k; ++r) {   // ascending ID: position = number of smaller selected ids
+    int pos = 0;
+    for (int r2 = 0; r2 < p.k; ++r2) pos += sel[r2] < sel[r] ? 1 : 0;
+    se[pos] = sel[r];
+    sw[pos] = w[r];
+  }
+  se[p.k] = p.shared_id;
+}
+
+// Caller-supplied routes ids / w [T][k]: ascending-ID slot lists.
+__global__ void pf_slots_kernel(const int32_t *ids, const float *w, int T, int k, int shared_id, int32_t *slot_expert,
+                                float *slot_w) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const int32_t *id = ids + (size_t)t * k;
+  for (int r = 0; r < k; ++r) {
+    int pos = 0;
+    for (int r2 = 0; r2 < k; ++r2) pos += id[r2] < id[r] ? 1 : 0;
+    slot_expert[(size_t)t * (k + 1) + pos] = id[r];
+    slot_w[(size_t)t * k + pos] = w[(size_t)t * k + r];
+  }
+  slot_expert[(size_t)t * (k + 1) + k] = shared_id;
+}
+
+// ------------------------------------------------------------------ plan --
+struct PfPlanParams {
+  const int32_t *slot_expert;   // [T][k+1]
+  int T, k, E1;                 // E1 = experts + 1 (index E = shared)
+  int lo, hi;                   // routed experts computed here
+  int st0, st1;                 // tokens whose shared expert is computed here
+  int32_t *slot_row, *row_token, *cnt, *off, *n_chunks, *chunk_expert, *chunk_row0, *chunk_n;
+  int chunk_cap;
+};
+
+// One CTA.  Permuted rows are ordered by expert, then token: the row of
+// (token t, expert e) is off[e] + #{t' < t choosing e}, counted with
+// per-expert token bitmaps -- deterministic, independent of thread timing.
+__global__ void __launch_bounds__(1024) pf_plan_kernel(PfPlanParams p) {
+  extern __shared__ uint32_t pf_plan_smem[];
+  const int nw = (p.T + 31) / 32;
+  uint32_t *mask = pf_plan_smem;                 // [E1][nw]
+  uint32_t *pre = mask + (size_t)p.E1 * nw;      // [E1][nw] exclusive prefix popcounts
+  __shared__ int s_cnt[kMoeMaxExperts + 1], s_off[kMoeMaxExperts + 1], s_cofs[kMoeMaxExperts + 1];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+  const int k1 = p.k + 1;
+  auto computed = [&](int t, int r, int e) {
+    if (e < 0) return false;
+    return r < p.k ? (e >= p.lo && e < p.hi) : (t >= p.st0 && t < p.st1);
+  };
+  for (int i = tid; i < p.E1 * nw; i += blockDim.x) mask[i] = 0u;
+  __syncthreads();
+  for (int i = tid; i < p.T * k1; i += blockDim.x) {
+    const int t = i / k1, r = i - t * k1;
+    const int e = p.slot_expert[i];
+    if (computed(t, r, e)) atomicOr(mask + (size_t)e * nw + (t >> 5), 1u << (t & 31));
+  }
+  __syncthreads();
+  // per expert: exclusive prefix of popcounts over its words (one warp per expert)
+  for (int e = warp; e < p.E1; e += nwarps) {
+    int base = 0;
+    for (int w0 = 0; w0 < nw; w0 += 32) {
+      const int w = w0 + lane;
+      const int c = w < nw ? __popc(mask[(size_t)e * nw + w]) : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (w < nw) pre[(size_t)e * nw + w] = base + incl - c;
+      base += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) s_cnt[e] = base;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // expert offsets and chunk offsets (ascending expert ID; the shared expert last)
+    int base = 0, cbase = 0;
+    for (int e0 = 0; e0 < p.E1; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < p.E1 ? s_cnt[e] : 0;
+      const int nc = (c + kPfCols - 1) / kPfCols;
+      int incl = c, cincl = nc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        const int cv = __shfl_up_sync(0xffffffffu, cincl, o);
+        if (lane >= o) incl += v, cincl += cv;
+      }
+      if (e < p.E1) {
+        s_off[e] = base + incl - c;
+        s_cofs[e] = cbase + cincl - nc;
+        p.cnt[e] = c;
+        p.off[e] = base + incl - c;
+      }
+      base += __shfl_sync(0xffffffffu, incl, 31);
+      cbase += __shfl_sync(0xffffffffu, cincl, 31);
+    }
+    if (lane == 0) *p.n_chunks = cbase < p.chunk_cap ? cbase : p.chunk_cap;
+  }
+  __syncthreads();
+  for (int i = tid; i < p.T * k1; i += blockDim.x) {
+    const int t = i / k1, r = i - t * k1;
+    const int e = p.slot_expert[i];
+    int row = -1;
+    if (computed(t, r, e)) {
+      const uint32_t m = mask[(size_t)e * nw + (t >> 5)];
+      row = s_off[e] + (int)pre[(size_t)e * nw + (t >> 5)] + __popc(m & ((1u << (t & 31)) - 1u));
+      p.row_token[row] = t;
+    }
+    p.slot_row[i] = row;
+  }
+  for (int e = warp; e < p.E1; e += nwarps) {
+    const int c = s_cnt[e], nc = (c + kPfCols - 1) / kPfCols;
+    for (int j = lane; j < nc; j += 32) {
+      const int ci = s_cofs[e] + j;
+      if (ci < p.chunk_cap) {
+        p.chunk_expert[ci] = e;
+        p.chunk_row0[ci] = s_off[e] + j * kPfCols;
+        p.chunk_n[ci] = c - j * kPfCols < kPfCols ? c - j * kPfCols : kPfCols;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------- grouped GEMM --
+enum PfEpi : int { kPfEpiGlu = 0, kPfEpiDown = 1 };
+
+struct PfGemmParams {
+  const uint8_t *const *expert_tiles;   // [E+1] t16 tiles (null: not loaded)
+  int kb;                               // K / 256
+  int m_tiles;                          // weight rows / 128
+  const int32_t *n_chunks, *chunk_expert, *chunk_row0, *chunk_n;
+  const uint16_t *src;                  // gate/up: x [T][ld_src]; down: act [P][ld_src]
+  int ld_src;
+  const int32_t *row_token;             // gate/up: permuted row -> token row of x; down: null
+  uint16_t *y;                          // gate/up: act [P][ld_y]; down: down [P][ld_y]
+  int ld_y;
+  int act;
+  float gate_beta, value_beta;
+  int *err;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) {
+  extern __shared__ uint8_t pf_raw_smem[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(pf_raw_smem) + 1023) & ~(uintptr_t)1023);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint8_t *sA = sm + kPfA;
+  float *sS = reinterpret_cast<float *>(sm + kPfS);
+  const uint32_t bar_u0 = smem_addr(sm + kPfBar), bar_mma = bar_u0 + 16;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kPfBar + 32);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(kPfTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    mbar_init(bar_u0, 1);
+    mbar_init(bar_u0 + 8, 1);
+    mbar_init(bar_mma, 1);
+    mbar_fence_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint64_t pol = policy_evict_first();
+  const int n_items = *p.n_chunks * p.m_tiles;
+  uint32_t ph_u[2] = {0u, 0u}, ph_mma = 0u;
+  bool failed = false;
+
+  for (int item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
+    const int chunk = item % *p.n_chunks, m = item / *p.n_chunks;
+    const int e = p.chunk_expert[chunk], row0 = p.chunk_row0[chunk], n = p.chunk_n[chunk];
+    const int n16 = (n + 15) & ~15;
+    const uint8_t *wt = p.expert_tiles[e];
+    if (wt == nullptr) {
+      if (tid == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+      continue;
+    }
+    // source rows of this thread's B chunks (row = j*4 + warp, j < 16)
+    const uint16_t *srow[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int r = j * 4 + warp;
+      srow[j] = nullptr;
+      if (r < n) {
+        const int prow = row0 + r;
+        const int srcr = EPI == kPfEpiGlu ? p.row_token[prow] : prow;
+        srow[j] = p.src + (size_t)srcr * p.ld_src;
+      }
+    }
+    auto issue_units = [&](int kbi, int st) {
+      if (tid == 0) {
+        mbar_arrive_expect_tx(bar_u0 + 8 * st, kPfUStage);
+        for (int u = 0; u < 8; ++u)
+          bulk_copy_g2s(smem_addr(sm + kPfU + st * kPfUStage + u * kUnitBytes),
+                        wt + ((size_t)(8 * m + u) * p.kb + kbi) * kUnitBytes, kUnitBytes, bar_u0 + 8 * st, pol);
+      }
+    };
+    auto issue_b = [&](int kbi, int st) {
+      uint8_t *sB = sm + kPfB + st * kPfBStage;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int r = j * 4 + warp;                  // token row of the chunk
+        const int kc = lane;                         // 16-byte column chunk (8 bf16)
+        const uint32_t dst = smem_addr(sB + (kc >> 3) * kPfBSub + sw128_off(r, (kc & 7) * 8));
+        const uint16_t *src = srow[j] ? srow[j] + kbi * kUnitK + kc * 8 : p.src;
+        cp_async16(dst, src, srow[j] ? 16u : 0u);
+      }
+      cp_async_commit();
+    };
+
+    float acc[kPfCols];
+#pragma unroll
+    for (int i = 0; i < kPfCols; ++i) acc[i] = 0.f;
+    issue_units(0, 0);
+    issue_b(0, 0);
+    const int r_row = tid;                            // TMEM lane = weight row of the tile
+    const int u_row = r_row >> 4, rr = r_row & 15;
+    for (int kbi = 0; kbi < p.kb; ++kbi) {
+      const int st = kbi & 1;
+      if (kbi + 1 < p.kb) {
+        issue_units(kbi + 1, st ^ 1);
+        issue_b(kbi + 1, st ^ 1);
+        cp_async_wait_1();
+      } else {
+        cp_async_wait_all();
+      }
+      __syncthreads();                                // B(kbi) visible to all threads
+      // group sums of the B rows: thread -> (row tid % 64, groups 4*(tid/64) .. +3)
+      {
+        const uint8_t *sB = sm + kPfB + st * kPfBStage;
+        const int r = tid & 63;
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg) {
+          const int g = (tid >> 6) * 4 + gg;
+          float part = 0.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int kc = g * 4 + c;
+            const uint4 v = *reinterpret_cast<const uint4 *>(sB + (kc >> 3) * kPfBSub + sw128_off(r, (kc & 7) * 8));
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) part += bf16_to_f32(w4[q] & 0xFFFFu) + bf16_to_f32(w4[q] >> 16);
+          }
+          sS[g * kPfCols + r] = part;
+        }
+      }
+      // weight codes -> bf16 (128 + code) A tile
+      const bool ok_u = mbar_wait_bounded(bar_u0 + 8 * st, ph_u[st]);
+      ph_u[st] ^= 1u;
+      if (__syncthreads_or(!ok_u)) {
+        failed = true;
+        break;
+      }
+      {
+        const uint8_t *U = sm + kPfU + st * kPfUStage;
+#pragma unroll 4
+        for (int j = 0; j < 32; ++j) {
+          const int w = tid + kPfThreads * j;         // code word of the 8 units
+          const int u = w >> 9, wi = w & 511;
+          const int s = (wi >> 7) * 4 + (wi & 3), l = (wi >> 2) & 31;
+          const int g = l >> 2, q = l & 3;
+          const uint32_t word = *reinterpret_cast<const uint32_t *>(U + u * kUnitBytes + wi * 4);
+          const int ra = u * 16 + g, rb = ra + 8;
+          const int k0 = 16 * s + 2 * q;
+          const int sub0 = k0 >> 6, kk0 = k0 & 63;
+          const int sub1 = (k0 + 8) >> 6, kk1 = (k0 + 8) & 63;
+          *reinterpret_cast<uint32_t *>(sA + sub0 * kPfASub + sw128_off(ra, kk0)) = codes_to_bf16x2<0>(word);
+          *reinterpret_cast<uint32_t *>(sA + sub0 * kPfASub + sw128_off(rb, kk0)) = codes_to_bf16x2<1>(word);
+          *reinterpret_cast<uint32_t *>(sA + sub1 * kPfASub + sw128_off(ra, kk1)) = codes_to_bf16x2<2>(word);
+          *reinterpret_cast<uint32_t *>(sA + sub1 * kPfASub + sw128_off(rb, kk1)) = codes_to_bf16x2<3>(word);
+        }
+      }
+      // this thread's row parameters for the 8 groups
+      float sc[kPfGroups], mp[kPfGroups];
+      {
+        const uint8_t *P = sm + kPfU + st * kPfUStage + u_row * kUnitBytes + kUnitCodeBytes;
+#pragma unroll
+        for (int g = 0; g < kPfGroups; ++g) {
+          const uint32_t pw = *reinterpret_cast<const uint32_t *>(P + ((rr & 7) * 8 + g) * 8 + (rr >> 3) * 4);
+          sc[g] = bf16_lo_f32(pw);
+          mp[g] = fmaf(-128.f, sc[g], bf16_hi_f32(pw));
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+      if (tid == 0) {
+        const uint8_t *sB = sm + kPfB + st * kPfBStage;
+        const uint32_t idesc = umma_idesc_bf16(kPfRows, n16);
+#pragma unroll 1
+        for (int g = 0; g < kPfGroups; ++g) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int k0 = g * 32 + h * 16, sub = k0 >> 6, kk = k0 & 63;
+            umma_bf16(tbase + g * kPfCols, umma_desc_sw128(smem_addr(sA + sub * kPfASub) + kk * 2),
+                      umma_desc_sw128(smem_addr(sB + sub * kPfBSub) + kk * 2), idesc, (uint32_t)h);
+          }
+        }
+        umma_commit(bar_mma);
+      }
+      const bool ok_m = mbar_wait_bounded(bar_mma, ph_mma);
+      ph_mma ^= 1u;
+      if (__syncthreads_or(!ok_m)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      // promotion: acc += scale * D_g + (min - 128 scale) * S_g
+#pragma unroll 1
+      for (int g = 0; g < kPfGroups; ++g) {
+        const float s = sc[g], a3 = mp[g];
+        const float *Sg = sS + g * kPfCols;
+#pragma unroll
+        for (int c16 = 0; c16 < kPfCols / 16; ++c16) {
+          if (c16 * 16 < n16) {
+            uint32_t v[16];
+            tmem_ld16(tbase + ((uint32_t)(warp * 32) << 16) + g * kPfCols + c16 * 16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              acc[c16 * 16 + j] = fmaf(s, __uint_as_float(v[j]), fmaf(a3, Sg[c16 * 16 + j], acc[c16 * 16 + j]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncthreads();                                // TMEM, A and this stage's B/U free again
+    }
+    if (failed) break;
+    // ---- epilogue
+    if (EPI == kPfEpiGlu) {
+      const int col = 8 * (8 * m + u_row) + rr;       // rows rr < 8: gate, rr >= 8: up of the same column
+#pragma unroll
+      for (int t = 0; t < kPfCols; ++t) {
+        const float up = __shfl_down_sync(0xffffffffu, acc[t], 8);
+        if (rr < 8 && t < n) {
+          const float gate = bf16_round(acc[t]);
+          const float u = bf16_round(up);
+          const float v = p.act == RC_ACT_SITU ? act_situ(gate, u, p.gate_beta, p.value_beta) : act_swiglu(gate, u);
+          p.y[(size_t)(row0 + t) * p.ld_y + col] = f32_to_bf16_rne(v);
+        }
+      }
+    } else {
+      const int col = kPfRows * m + r_row;
+#pragma unroll
+      for (int t = 0; t < kPfCols; ++t)
+        if (t < n) p.y[(size_t)(row0 + t) * p.ld_y + col] = f32_to_bf16_rne(acc[t]);
+    }
+  }
+  if (failed && tid == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+  // let copies still in flight land before the shared memory is released
+  cp_async_wait_all();
+  if (failed && tid == 0) {
+    mbar_wait_bounded(bar_u0, ph_u[0]);
+    mbar_wait_bounded(bar_u0 + 8, ph_u[1]);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kPfTmemCols));
+}
+
+// --------------------------------------------------------------- combine --
+// Per token: routed = RTNE(sum over its slots in ascending ID of
+// f32(down[row]) * w), then RTNE(f32(routed) + f32(shared row)).
+constexpr int kPfCombineThreads = 128;
+
+__global__ void __launch_bounds__(kPfCombineThreads) pf_combine_kernel(const uint16_t *down, const int32_t *slot_row,
+                                                                         const float *slot_w, int k, int with_shared,
+                                                                         int hidden, uint16_t *out) {
+  const int t = blockIdx.y;
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v * 8 >= hidden) return;
+  const int32_t *sr = slot_row + (size_t)t * (k + 1);
+  uint4 r[kMoeMaxK];
+  float w[kMoeMaxK];
+#pragma unroll
+  for (int s = 0; s < kMoeMaxK; ++s) {
+    r[s] = make_uint4(0, 0, 0, 0);
+    w[s] = 0.f;
+    if (s < k) {
+      r[s] = __ldcg(reinterpret_cast<const uint4 *>(down + (size_t)sr[s] * hidden + (size_t)v * 8));
+      w[s] = slot_w[(size_t)t * k + s];
+    }
+  }
+  const uint4 sh = with_shared ? __ldcg(reinterpret_cast<const uint4 *>(down + (size_t)sr[k] * hidden + (size_t)v * 8))
+                               : make_uint4(0, 0, 0, 0);
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+  for (int s = 0; s < kMoeMaxK; ++s) {
+    if (s < k) {
+      const uint32_t q[4] = {r[s].x, r[s].y, r[s].z, r[s].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(bf16_to_f32(q[j] & 0xFFFFu), w[s]));
+        acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(bf16_to_f32(q[j] >> 16), w[s]));
+      }
+    }
+  }
+  const uint32_t shw[4] = {sh.x, sh.y, sh.z, sh.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t lo = f32_to_bf16_rne(acc[2 * j]), hi = f32_to_bf16_rne(acc[2 * j + 1]);
+    if (with_shared) {
+      lo = f32_to_bf16_rne(bf16_to_f32(lo) + bf16_to_f32(shw[j] & 0xFFFFu));
+      hi = f32_to_bf16_rne(bf16_to_f32(hi) + bf16_to_f32(shw[j] >> 16));
+    }
+    o[j] = lo | (hi << 16);
+  }
+  *reinterpret_cast<uint4 *>(out + (size_t)t * hidden + (size_t)v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Expert-parallel slot rows: slot_out[t][r] = down[slot_row[t][r]], or zeros
+// where the slot is computed on another rank.
+__global__ void pf_slot_rows_kernel(const uint16_t *down, const int32_t *slot_row, int hidden, uint16_t *slot_out) {
+  const int i = blockIdx.x;                       // (token, slot)
+  const int row = slot_row[i];
+  for (int v = threadIdx.x; v * 8 < hidden; v += blockDim.x) {
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (row >= 0) val = __ldcg(reinterpret_cast<const uint4 *>(down + (size_t)row * hidden + (size_t)v * 8));
+    *reinterpret_cast<uint4 *>(slot_out + (size_t)i * hidden + (size_t)v * 8) = val;
+  }
+}
+
+__global__ void pf_identity_rows_kernel(int32_t *rows, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) rows[i] = i;
+}
+
+// ------------------------------------------------------------------ host --
+static void pf_release(PfScratch *s) {
+  if (!s) return;
+  cudaFree(s->logits);
+  cudaFree(s->ids);
+  cudaFree(s->weights);
+  cudaFree(s->slot_expert);
+  cudaFree(s->slot_w);
+  cudaFree(s->slot_row);
+  cudaFree(s->row_token);
+  cudaFree(s->cnt);
+  cudaFree(s->off);
+  cudaFree(s->n_chunks);
+  cudaFree(s->chunk_expert);
+  cudaFree(s->chunk_row0);
+  cudaFree(s->chunk_n);
+  cudaFree(s->act);
+  cudaFree(s->down);
+  delete s;
+}
+
+void pf_free(rc_moe *m) {
+  pf_release(m->pf);
+  m->pf = nullptr;
+}
+
+// Scratch for T tokens (grown, never shrunk).  Allocation synchronises the
+// device, so size it before capturing a graph.
+static int pf_scratch(rc_moe *m, int T) {
+  if (m->pf && m->pf->T_cap >= T) return RC_OK;
+  RC_CUDA_TRY(cudaDeviceSynchronize());
+  pf_free(m);
+  PfScratch *s = new PfScratch();
+  const int E = m->n_experts, K = kMoeMaxK;
+  s->T_cap = T;
+  s->E1 = E + 1;
+  s->P_cap = T * (K + 1);
+  s->chunk_cap = s->P_cap / kPfCols + E + 1;
+  const size_t P = (size_t)s->P_cap;
+  cudaError_t e = cudaMalloc(&s->logits, (size_t)T * E * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->ids, (size_t)T * K * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->weights, (size_t)T * K * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->slot_expert, (size_t)T * (K + 1) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->slot_w, (size_t)T * K * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->slot_row, (size_t)T * (K + 1) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->row_token, P * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->cnt, (size_t)(E + 1) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->off, (size_t)(E + 1) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->n_chunks, 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->chunk_expert, (size_t)s->chunk_cap * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->chunk_row0, (size_t)s->chunk_cap * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->chunk_n, (size_t)s->chunk_cap * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->act, P * m->inter_pad * 2);
+  if (e == cudaSuccess) e = cudaMemset(s->act, 0, P * m->inter_pad * 2);
+  if (e == cudaSuccess) e = cudaMalloc(&s->down, P * m->hidden * 2);
+  if (e != cudaSuccess) {
+    pf_release(s);
+    set_error("MoE prefill scratch for %d tokens: %s", T, cudaGetErrorString(e));
+    return RC_ERR_CUDA;
+  }
+  m->pf = s;
+  return RC_OK;
+}
+
+template <int EPI>
+static cudaError_t pf_launch_gemm(const rc_ctx *ctx, const PfGemmParams &p, cudaStream_t s) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(pf_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemAlloc);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) configured[dev] = true;
+  }
+  // No programmatic overlap: a CTA of the next kernel must never sit on an SM
+  // waiting for this grid while holding what this grid needs (tensor memory).
+  pf_gemm_kernel<EPI><<<ctx->sm_count, kPfThreads, kPfSmemAlloc, s>>>(p);
+  return cudaGetLastError();
+}
+
+struct PfRun {
+  int T, k, act;
+  float gb, vb;
+  int lo, hi, st0, st1;        // computed experts / shared tokens
+};
+
+// plan + gate/up + down for slot lists already in m->pf (slot_expert, slot_w)
+static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t s) {
+  PfScratch *ps = m->pf;
+  PfPlanParams pp{};
+  pp.slot_expert = ps->slot_expert;
+  pp.T = r.T;
+  pp.k = r.k;
+  pp.E1 = m->n_experts + 1;
+  pp.lo = r.lo;
+  pp.hi = r.hi;
+  pp.st0 = r.st0;
+  pp.st1 = r.st1;
+  pp.slot_row = ps->slot_row;
+  pp.row_token = ps->row_token;
+  pp.cnt = ps->cnt;
+  pp.off = ps->off;
+  pp.n_chunks = ps->n_chunks;
+  pp.chunk_expert = ps->chunk_expert;
+  pp.chunk_row0 = ps->chunk_row0;
+  pp.chunk_n = ps->chunk_n;
+  pp.chunk_cap = ps->chunk_cap;
+  const int nw = (r.T + 31) / 32;
+  const size_t plan_smem = (size_t)2 * pp.E1 * nw * 4;
+  RC_CHECK_ARG(plan_smem <= (size_t)kPfPlanSmemMax, "prefill plan of %d tokens x %d experts exceeds shared memory",
+               r.T, pp.E1);
+  static bool configured[64] = {};
+  int dev = 0;
+  RC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 64 || !configured[dev]) {
+    RC_CUDA_TRY(cudaFuncSetAttribute(pf_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfPlanSmemMax));
+    if (dev < 64) configured[dev] = true;
+  }
+  pf_plan_kernel<<<1, 1024, plan_smem, s>>>(pp);
+  RC_CUDA_TRY(cudaGetLastError());
+
+  PfGemmParams g{};
+  g.expert_tiles = m->gu_tiles;
+  g.kb = m->hidden / kUnitK;
+  g.m_tiles = 2 * m->inter / kPfRows;
+  g.n_chunks = ps->n_chunks;
+  g.chunk_expert = ps->chunk_expert;
+  g.chunk_row0 = ps->chunk_row0;
+  g.chunk_n = ps->chunk_n;
+  g.src = x;
+  g.ld_src = m->hidden;
+  g.row_token = ps->row_token;
+  g.y = ps->act;
+  g.ld_y = m->inter_pad;
+  g.act = r.act;
+  g.gate_beta = r.gb;
+  g.value_beta = r.vb;
+  g.err = m->ctx->err;
+  RC_CUDA_TRY(pf_launch_gemm<kPfEpiGlu>(m->ctx, g, s));
+  PfGemmParams d = g;
+  d.expert_tiles = m->dn_tiles;
+  d.kb = m->inter_pad / kUnitK;
+  d.m_tiles = m->hidden / kPfRows;
+  d.src = ps->act;
+  d.ld_src = m->inter_pad;
+  d.row_token = nullptr;
+  d.y = ps->down;
+  d.ld_y = m->hidden;
+  RC_CUDA_TRY(pf_launch_gemm<kPfEpiDown>(m->ctx, d, s));
+  return RC_OK;
+}
+
+static int pf_route(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling,
+                    cudaStream_t s) {
+  PfScratch *ps = m->pf;
+  const int E = m->n_experts;
+  pf_logits_kernel<<<dim3((E + 7) / 8, T), 256, 0, s>>>(x, m->hidden, m->router_w, E, ps->logits);
+  RC_CUDA_TRY(cudaGetLastError());
+  PfSelectParams sp{};
+  sp.logits = ps->logits;
+  sp.bias = m->router_bias;
+  sp.T = T;
+  sp.E = E;
+  sp.k = k;
+  sp.mode = router;
+  sp.renorm = renorm;
+  sp.shared_id = m->has_shared ? E : -1;
+  sp.scaling = scaling;
+  sp.ids = ps->ids;
+  sp.weights = ps->weights;
+  sp.slot_expert = ps->slot_expert;
+  sp.slot_w = ps->slot_w;
+  pf_select_kernel<<<(T + 7) / 8, 256, 0, s>>>(sp);
+  RC_CUDA_TRY(cudaGetLastError());
+  return RC_OK;
+}
+
+static int pf_check(rc_moe *m, const uint16_t *x, int T, int k, int act, int lo, int hi) {
+  RC_CHECK_ARG(T >= 1 && T <= kPfMaxTokens, "prefill: T must be 1..%d", kPfMaxTokens);
+  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK && k <= m->n_experts, "prefill: k must be 1..%d and <= n_experts", kMoeMaxK);
+  RC_CHECK_ARG(act == RC_ACT_SWIGLU || act == RC_ACT_SITU, "unknown activation %d", act);
+  RC_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0, "token rows must be 16-byte aligned");
+  RC_CHECK_ARG((2 * m->inter) % kPfRows == 0 && m->hidden % kPfRows == 0,
+               "prefill needs 2*inter and hidden multiples of 128");
+  for (int e = lo; e < hi; ++e) RC_CHECK_ARG(m->gate_up[e] != nullptr, "expert %d is not loaded", e);
+  return RC_OK;
+}
+
+}  // namespace rc
+
+using namespace rc;
+
+extern "C" {
+
+int rc_moe_prefill(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
+                   int act, float gate_beta, float value_beta, uint16_t *out_dev, int32_t *ids_dev, float *w_dev,
+                   void *stream) {
+  RC_CHECK_ARG(m && x_dev && out_dev, "rc_moe_prefill: NULL argument");
+  RC_CHECK_ARG(router == RC_ROUTER_SOFTMAX || router == RC_ROUTER_SIGMOID_BIAS, "unknown router %d", router);
+  RC_CHECK_ARG((reinterpret_cast<uintptr_t>(out_dev) & 15) == 0, "out must be 16-byte aligned");
+  int rc = pf_check(m, x_dev, T, k, act, 0, m->n_experts);
+  if (rc) return rc;
+  RC_CHECK_ARG(!m->has_shared || m->gate_up[m->n_experts], "the shared expert is not loaded");
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  if ((rc = pf_scratch(m, T))) return rc;
+  const cudaStream_t s = pick_stream(m->ctx, stream);
+  if ((rc = pf_route(m, x_dev, T, k, router, renormalize, scaling, s))) return rc;
+  PfRun r{T, k, act, gate_beta, value_beta, 0, m->n_experts, 0, m->has_shared ? T : 0};
+  if ((rc = pf_experts(m, x_dev, r, s))) return rc;
+  pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
+                      s>>>(m->pf->down, m->pf->slot_row, m->pf->slot_w, k, m->has_shared, m->hidden, out_dev);
+  RC_CUDA_TRY(cudaGetLastError());
+  if (ids_dev) RC_CUDA_TRY(cudaMemcpyAsync(ids_dev, m->pf->ids, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
+  if (w_dev) RC_CUDA_TRY(cudaMemcpyAsync(w_dev, m->pf->weights, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
+  return RC_OK;
+}
+
+int rc_moe_prefill_experts(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev, const float *w_dev,
+                           int k, int act, float gate_beta, float value_beta, int with_shared, uint16_t *out_dev,
+                           void *stream) {
+  RC_CHECK_ARG(m && x_dev && ids_dev && w_dev && out_dev, "rc_moe_prefill_experts: NULL argument");
+  RC_CHECK_ARG((reinterpret_cast<uintptr_t>(out_dev) & 15) == 0, "out must be 16-byte aligned");
+  RC_CHECK_ARG(!with_shared || (m->has_shared && m->gate_up[m->n_experts]), "the shared expert is not loaded");
+  int rc = pf_check(m, x_dev, T, k, act, 0, 0);
+  if (rc) return rc;
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  if ((rc = pf_scratch(m, T))) return rc;
+  const cudaStream_t s = pick_stream(m->ctx, stream);
+  pf_slots_kernel<<<(T + 127) / 128, 128, 0, s>>>(ids_dev, w_dev, T, k, with_shared ? m->n_experts : -1,
+                                                 m->pf->slot_expert, m->pf->slot_w);
+  RC_CUDA_TRY(cudaGetLastError());
+  // every routed expert the caller names must be loaded: checked on the device
+  // side by a null tile table entry (error word), so no host copy of the ids
+  PfRun r{T, k, act, gate_beta, value_beta, 0, m->n_experts, 0, with_shared ? T : 0};
+  if ((rc = pf_experts(m, x_dev, r, s))) return rc;
+  pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
+                      s>>>(m->pf->down, m->pf->slot_row, m->pf->slot_w, k, with_shared, m->hidden, out_dev);
+  RC_CUDA_TRY(cudaGetLastError());
+  return RC_OK;
+}
+
+int rc_moe_prefill_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize,
+                         float scaling, int act, float gate_beta, float value_beta, int expert_lo, int expert_hi,
+                         int shared_t0, int shared_tn, uint16_t *slot_out_dev, float *slot_w_dev, void *stream) {
+  RC_CHECK_ARG(m && x_dev && slot_out_dev && slot_w_dev, "rc_moe_prefill_local: NULL argument");
+  RC_CHECK_ARG(router == RC_ROUTER_SOFTMAX || router == RC_ROUTER_SIGMOID_BIAS, "unknown router %d", router);
+  RC_CHECK_ARG((reinterpret_cast<uintptr_t>(slot_out_dev) & 15) == 0, "slot_out must be 16-byte aligned");
+  RC_CHECK_ARG(0 <= expert_lo && expert_lo <= expert_hi && expert_hi <= m->n_experts,
+               "expert range [%d, %d) outside 0..%d", expert_lo, expert_hi, m->n_experts);
+  RC_CHECK_ARG(shared_tn == 0 || (m->has_shared && shared_t0 >= 0 && shared_tn > 0 && shared_t0 + shared_tn <= T),
+               "shared token range [%d, +%d) invalid for T=%d", shared_t0, shared_tn, T);
+  int rc = pf_check(m, x_dev, T, k, act, expert_lo, expert_hi);
+  if (rc) return rc;
+  RC_CHECK_ARG(!shared_tn || m->gate_up[m->n_experts], "the shared expert is not loaded");
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  if ((rc = pf_scratch(m, T))) return rc;
+  const cudaStream_t s = pick_stream(m->ctx, stream);
+  if ((rc = pf_route(m, x_dev, T, k, router, renormalize, scaling, s))) return rc;
+  PfRun r{T, k, act, gate_beta, value_beta, expert_lo, expert_hi, shared_t0, shared_t0 + shared_tn};
+  if ((rc = pf_experts(m, x_dev, r, s))) return rc;
+  pf_slot_rows_kernel<<<T * (k + 1), 256, 0, s>>>(m->pf->down, m->pf->slot_row, m->hidden, slot_out_dev);
+  RC_CUDA_TRY(cudaGetLastError());
+  RC_CUDA_TRY(cudaMemcpyAsync(slot_w_dev, m->pf->slot_w, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
+  return RC_OK;
+}
+
+int rc_moe_prefill_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int T, int k,
+                           int with_shared, uint16_t *out_dev, void *stream) {
+  RC_CHECK_ARG(m && slot_out_dev && slot_w_dev && out_dev, "rc_moe_prefill_combine: NULL argument");
+  RC_CHECK_ARG(T >= 1 && T <= kPfMaxTokens && k >= 1 && k <= kMoeMaxK, "rc_moe_prefill_combine: bad T or k");
+  RC_CHECK_ARG(!with_shared || m->has_shared, "this MoE layer has no shared expert");
+  RC_CHECK_ARG(((reinterpret_cast<uintptr_t>(slot_out_dev) | reinterpret_cast<uintptr_t>(out_dev)) & 15) == 0,
+               "slot rows and out must be 16-byte aligned");
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  const cudaStream_t s = pick_stream(m->ctx, stream);
+  // slot rows laid out [T][k+1][hidden]: slot_row[t][r] = t*(k+1)+r
+  int rc = pf_scratch(m, T);
+  if (rc) return rc;
+  // identity slot-row table, so that the combine kernel is shared with the
+  // single-GPU path
+  pf_identity_rows_kernel<<<(T * (k + 1) + 255) / 256, 256, 0, s>>>(m->pf->slot_row, T * (k + 1));
+  RC_CUDA_TRY(cudaGetLastError());
+  pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
+                      s>>>(slot_out_dev, m->pf->slot_row, slot_w_dev, k, with_shared, m->hidden, out_dev);
+  RC_CUDA_TRY(cudaGetLastError());
+  return RC_OK;
+}
+
+}  // extern "C"

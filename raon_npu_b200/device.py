@@ -346,6 +346,45 @@ class MoeLayer:
             int(shared_tokens[1]), ctypes.c_void_p(_ptr(slot_out_dev)), ctypes.c_void_p(_ptr(slot_w_dev)),
             ctypes.c_void_p(_stream_for(stream, x_dev, slot_out_dev))), "rc_moe_decode_local")
 
+    def prefill(self, x_dev, k: int, out_dev, ids_dev=None, w_dev=None, router: str = "softmax",
+                renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
+                value_beta: float = 25.0, stream: int | None = None) -> None:
+        """The layer for T <= 4096 tokens on the tcgen05 grouped GEMM: x [T, hidden] -> out [T, hidden]."""
+        check(self.ctx.lib.rc_moe_prefill(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), _tokens(x_dev, self.hidden), int(k), ROUTER_CODES[router],
+            int(bool(renormalize)), float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta),
+            ctypes.c_void_p(_ptr(out_dev)), ctypes.c_void_p(_ptr(ids_dev)), ctypes.c_void_p(_ptr(w_dev)),
+            ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_prefill")
+
+    def prefill_experts(self, x_dev, ids_dev, w_dev, k: int, out_dev, act: str = "situ", gate_beta: float = 4.0,
+                        value_beta: float = 25.0, with_shared: bool = False, stream: int | None = None) -> None:
+        check(self.ctx.lib.rc_moe_prefill_experts(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), _tokens(x_dev, self.hidden), ctypes.c_void_p(_ptr(ids_dev)),
+            ctypes.c_void_p(_ptr(w_dev)), int(k), ACT_CODES[act], float(gate_beta), float(value_beta),
+            int(bool(with_shared)), ctypes.c_void_p(_ptr(out_dev)),
+            ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_prefill_experts")
+
+    def prefill_local(self, x_dev, k: int, slot_out_dev, slot_w_dev, experts: tuple[int, int] | None = None,
+                      shared_tokens: tuple[int, int] | None = None, router: str = "softmax",
+                      renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
+                      value_beta: float = 25.0, stream: int | None = None) -> None:
+        T = _tokens(x_dev, self.hidden)
+        lo, hi = (0, self.n_experts) if experts is None else (int(experts[0]), int(experts[1]))
+        if shared_tokens is None:
+            shared_tokens = (0, T) if self.has_shared else (0, 0)
+        check(self.ctx.lib.rc_moe_prefill_local(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), T, int(k), ROUTER_CODES[router], int(bool(renormalize)),
+            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), lo, hi, int(shared_tokens[0]),
+            int(shared_tokens[1]), ctypes.c_void_p(_ptr(slot_out_dev)), ctypes.c_void_p(_ptr(slot_w_dev)),
+            ctypes.c_void_p(_stream_for(stream, x_dev, slot_out_dev))), "rc_moe_prefill_local")
+
+    def prefill_combine(self, slot_out_dev, slot_w_dev, k: int, out_dev, tokens: int, with_shared: bool = True,
+                        stream: int | None = None) -> None:
+        check(self.ctx.lib.rc_moe_prefill_combine(
+            self.handle, ctypes.c_void_p(_ptr(slot_out_dev)), ctypes.c_void_p(_ptr(slot_w_dev)), int(tokens),
+            int(k), int(bool(with_shared)), ctypes.c_void_p(_ptr(out_dev)),
+            ctypes.c_void_p(_stream_for(stream, slot_out_dev, out_dev))), "rc_moe_prefill_combine")
+
     def combine(self, slot_out_dev, slot_w_dev, k: int, out_dev, tokens: int = 1, with_shared: bool = True,
                 stream: int | None = None) -> None:
         """slot rows [T, k+1, hidden] and slot weights [T, k] -> out [T, hidden]."""
