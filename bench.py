@@ -258,6 +258,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     weights.clear()
 
     moe = None if args.no_moe else run_moe(args, ctx, torch, dev, rank, world, local_rank, barrier)
+    prefill = None if args.no_moe else run_moe_prefill(args, ctx, torch, dev, rank, world, local_rank, barrier)
 
     if rank == 0:
         line = {
@@ -280,6 +281,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "per_shape": per_shape,
             "cpu_baseline": cpu,
             "moe": moe,
+            "moe_prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     ctx.close()
@@ -562,6 +564,147 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
     return res
 
 
+# ------------------------------------------------------- MoE prefill layer --
+# 512 tokens x hidden 2048 through the config-3 layer,
+# router logits biased b_e = -1.1 ln(rank_e) (rank: seeded permutation of
+# 1..128) so the expert load follows Zipf(1.1); the tensor-core grouped GEMM;
+# expert-parallel at N GPUs with the 512 tokens split over the ranks.
+PREFILL_TOKENS = 512
+
+
+def zipf_bias(n_experts: int) -> np.ndarray:
+    rank = np.random.default_rng(4321).permutation(n_experts) + 1
+    return (-1.1 * np.log(rank)).astype(np.float32)
+
+
+def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barrier):
+    import torch.distributed as dist
+    H, I, E, k = MOE["hidden"], MOE["inter"], MOE["experts"], MOE["k"]
+    T = PREFILL_TOKENS
+    if T % world:
+        return {"unavailable": f"{T} tokens do not split over {world} ranks"}
+    M = T // world
+    eb = moe_expert_bytes(H, I)
+    n_layers = 2
+    eps = build_moe_layers(ctx, torch, dev, n_layers)
+    bias = zipf_bias(E)
+    gen = torch.Generator(device=dev)
+    for li, ep in enumerate(eps):
+        gen.manual_seed(_moe_seed(li, 999))
+        wr = (torch.randn((E, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        ep.layer.set_router(wr.view(torch.int16).cpu().numpy().view(np.uint16), bias)
+    gen.manual_seed(9191 + rank)
+    xs = [torch.randn((M, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16).contiguous()
+          for _ in range(n_layers)]
+    outs = [torch.empty((M, H), dtype=torch.int16, device=dev) for _ in range(n_layers)]
+    for _ in range(args.warmup):
+        for li in range(n_layers):
+            eps[li].prefill(xs[li], outs[li])
+    torch.cuda.synchronize()
+    ctx.sync()
+    graphs, graph_err = [], None
+    try:
+        for li in range(n_layers):
+            graphs.append(capture_graph(torch, lambda li=li: eps[li].prefill(xs[li], outs[li])))
+    except Exception as e:                  # noqa: BLE001 - reported in the JSON line
+        graphs, graph_err = [], f"{type(e).__name__}: {e}"[:200]
+    ok = torch.tensor([1 if graphs else 0], dtype=torch.int32, device=dev)
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if not int(ok.item()):
+        graphs = []
+
+    def step(s):
+        li = s % n_layers
+        if graphs:
+            graphs[li].replay()
+        else:
+            eps[li].prefill(xs[li], outs[li])
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(_gpu_index(local_rank))
+    clocks.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.steps):
+        step(s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = ms
+    if world > 1:
+        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_max = float(tt.item())
+    del graphs
+    ctx.sync()
+    # this rank's algorithmic work per step: distinct owned experts the 512
+    # tokens hit (weights), and the rows it computes (flops)
+    lo, hi = eps[0].experts
+    per_layer = []
+    for li in range(n_layers):
+        xg = _gather_tokens(torch, dist, world, xs[li])
+        ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+        w = torch.empty((T, k), dtype=torch.float32, device=dev)
+        eps[li].layer.route(xg, T, k, ids, w)
+        torch.cuda.synchronize()
+        idn = ids.cpu().numpy()
+        mine = (idn >= lo) & (idn < hi)
+        rows = int(mine.sum()) + M
+        hit = len(np.unique(idn[mine])) + 1
+        nbytes = hit * eb + 2 * rows * H + 2 * rows * I + 2 * rows * H
+        flops = 2.0 * rows * (2 * I * H + H * I)
+        per_layer.append((nbytes, flops, rows, hit))
+    avg = [sum(p[i] for p in per_layer) / n_layers for i in range(4)]
+    tot = torch.tensor(avg[:2], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot)
+    avg_bytes, avg_flops = float(tot[0]) / world, float(tot[1]) / world
+    peak, peak_kind = peaks()
+    tflops_peak = _bf16_peak()
+    hbm_frac = avg_bytes / (ms_max * 1e-3) / 1e9 / peak
+    tc_frac = avg_flops / (ms_max * 1e-3) / 1e12 / tflops_peak
+    for ep in eps:
+        ep.layer.close()
+    return {
+        "metric": "MoE prefill layer tokens/s", "value": round(T / (ms_max * 1e-3), 1), "unit": "tokens/s",
+        "ms_per_step": round(ms_max, 4), "steps": args.steps, "scaling": "strong",
+        "config": {"workload": "MoE prefill grouped GEMM (BASELINE configs[3])", "tokens": T, "hidden": H,
+                   "intermediate": I, "experts": E, "shared_experts": 1, "top_k": k,
+                   "router": "softmax of logits + b_e, b_e = -1.1 ln(rank_e) (Zipf(1.1) load)",
+                   "parallelism": f"ep{world}", "tokens_per_rank": M, "layers_rotated": n_layers,
+                   "cuda_graph": bool(int(ok.item())), "graph_error": graph_err,
+                   "rank0_rows_per_step": round(avg[2]), "rank0_experts_hit": round(avg[3], 1)},
+        "roofline": {"bound": "hbm" if hbm_frac >= tc_frac else "tensor",
+                     "achieved": round(avg_bytes / (ms_max * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(hbm_frac, 4), "peak_source": peak_kind, "traffic": None,
+                     "tensor_tflops": round(avg_flops / (ms_max * 1e-3) / 1e12, 1),
+                     "tensor_peak_tflops": tflops_peak, "tensor_frac": round(tc_frac, 4),
+                     "per_rank_bytes_per_step": round(avg_bytes), "per_rank_flops_per_step": round(avg_flops),
+                     "kernel": "prefill layer per rank (router, plan, tcgen05 grouped gate/up + down GEMMs, "
+                               "combine; NCCL all-gather + reduce-scatter at N>1)"},
+        "gpu_launches": 7 * args.steps,
+        "clocks": clk,
+    }
+
+
+def _bf16_peak() -> float:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
+
+
 def _gpu_index(local_rank: int) -> int:
     if "CUDA_VISIBLE_DEVICES" in os.environ:
         return int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank])
@@ -694,6 +837,31 @@ def run_profile_moe(args):
     print(json.dumps({"profile": "moe", "tokens": args.tokens, "steps": args.launches}))
 
 
+def run_profile_prefill(args):
+    """A few plain config-4 prefill layers on one GPU (no timing) for an ncu
+    capture: ``python bench.py --profile prefill --launches 3``."""
+    import torch
+    from raon_npu_b200.device import Context
+    dev = torch.device("cuda", 0)
+    ctx = Context(0)
+    eps = build_moe_layers(ctx, torch, dev, 1)
+    E, H = MOE["experts"], MOE["hidden"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(_moe_seed(0, 999))
+    wr = (torch.randn((E, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    eps[0].layer.set_router(wr.view(torch.int16).cpu().numpy().view(np.uint16), zipf_bias(E))
+    gen.manual_seed(9191)
+    x = torch.randn((PREFILL_TOKENS, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16).contiguous()
+    out = torch.empty_like(x)
+    for _ in range(args.launches):
+        eps[0].prefill(x, out)
+    torch.cuda.synchronize()
+    ctx.sync()
+    eps[0].layer.close()
+    ctx.close()
+    print(json.dumps({"profile": "prefill", "tokens": PREFILL_TOKENS, "steps": args.launches}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -705,12 +873,15 @@ def main():
     ap.add_argument("--no-per-shape", action="store_true", help="skip the per-shape launch table")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode layer (configs[2])")
     ap.add_argument("--profile", default=None, help="NxK: run a few plain GEMV launches for ncu and exit; "
-                    "'moe': a few config-3 MoE decode steps")
+                    "'moe' / 'prefill': a few config-3 decode / config-4 prefill steps")
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--launches", type=int, default=4)
     args = ap.parse_args()
     if args.profile == "moe":
         run_profile_moe(args)
+        return
+    if args.profile == "prefill":
+        run_profile_prefill(args)
         return
     if args.profile:
         run_profile_case(args)

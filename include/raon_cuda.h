@@ -137,7 +137,7 @@ int rc_moe_set_expert(rc_moe *m, int expert, const uint8_t *gate_up, size_t gate
  * router, the per-expert correction bias f32 [n_experts] (or NULL). */
 int rc_moe_set_router(rc_moe *m, const uint16_t *router_w, const float *bias);
 
-/* Router for T <= 16 tokens x [T][hidden] (device): top-k ids (best first,
+/* Router for T <= 4096 tokens x [T][hidden] (device): top-k ids (best first,
  * lower index wins ties) and weights, optional f32 logits [T][n_experts].
  * Replaces the host router ``RaonModel._route_token`` (host/raon.py:1224-1247)
  * and the softmax top-k of the north-star configs. */

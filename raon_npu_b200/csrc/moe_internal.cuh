@@ -60,4 +60,8 @@ struct rc_moe {
 
 namespace rc {
 void pf_free(rc_moe *m);   // releases m->pf (q4nx_prefill.cu)
+// Router for 16 < T <= 4096 tokens (q4nx_prefill.cu): ids / weights [T][k],
+// logits [T][E] (each optional).
+int pf_route_tokens(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
+                    int32_t *ids_dev, float *w_dev, float *logits_dev, void *stream);
 }  // namespace rc

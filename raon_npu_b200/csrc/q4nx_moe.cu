@@ -979,8 +979,10 @@ int rc_moe_set_router(rc_moe *m, const uint16_t *router_w, const float *bias) {
 int rc_moe_route(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
                  int32_t *ids_dev, float *w_dev, float *logits_dev, void *stream) {
   RC_CHECK_ARG(m && x_dev, "rc_moe_route: NULL argument");
-  RC_MOE_CHECK_TK("rc_moe_route");
   RC_CHECK_ARG(router == RC_ROUTER_SOFTMAX || router == RC_ROUTER_SIGMOID_BIAS, "unknown router %d", router);
+  if (T > kMoeMaxTokens)   // the prefill router (same arithmetic, one warp per token)
+    return pf_route_tokens(m, x_dev, T, k, router, renormalize, scaling, ids_dev, w_dev, logits_dev, stream);
+  RC_MOE_CHECK_TK("rc_moe_route");
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   const cudaStream_t s = pick_stream(m->ctx, stream);
   int rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, all_owned(m, T, m->has_shared), s);

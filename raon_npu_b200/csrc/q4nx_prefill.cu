@@ -17,7 +17,7 @@
 //   combine   per token, its slot rows in ascending ID (f32 multiply, then
 //             add, no FMA), RTNE, plus the shared row
 //
-// The grouped GEMM (one CTA per SM, 4 warps, persistent over work items
+// The grouped GEMM (one CTA per SM, 8 warps, persistent over work items
 // (64-token chunk, 128-row weight tile)):
 //   A  weight tile: the q4nx codes of 128 rows x 256 columns arrive by bulk
 //      copy in the t16 upload layout and are written to shared memory as
@@ -28,9 +28,10 @@
 //      same way; the per-32-column group sums S of the rows come with them;
 //   D  one tcgen05.mma chain of K = 32 per quantisation group into its own
 //      tensor-memory accumulator (8 groups x 64 columns = 512 columns);
-//   promotion: thread r (= TMEM lane = weight row r) reads the 8 group
-//      accumulators with tcgen05.ld and adds scale * D + (min - 128 scale) * S
-//      in f32 registers -- the same arithmetic as the decode GEMV and as the
+//   promotion: the thread of weight row r (TMEM lane r; warps w and w+4 share
+//      the lanes and split the token columns) reads the 8 group accumulators
+//      with tcgen05.ld and adds scale * D + (min - 128 scale) * S in f32
+//      registers -- the same arithmetic as the decode GEMV and as the
 //      reference NPU kernel's per-group scaling (grouped_mmul.cc:196-254).
 #include <string.h>
 
@@ -43,7 +44,8 @@ namespace rc {
 constexpr int kPfMaxTokens = 4096;
 constexpr int kPfRows = 128;         // weight rows per tile: MMA M, TMEM lanes
 constexpr int kPfCols = 64;          // token columns per work item: max MMA N
-constexpr int kPfThreads = 128;
+constexpr int kPfThreads = 256;
+constexpr int kPfWarps = kPfThreads / 32;
 constexpr int kPfTmemCols = 512;     // 8 group accumulators x 64 columns
 constexpr int kPfGroups = 8;         // 32-column quantisation groups per 256-column block
 
@@ -121,29 +123,60 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- router --
-// logits[t][e] = f32(sum_h f64(x[t][h]) * f64(wr[e][h])): one warp per (token, expert).
-__global__ void __launch_bounds__(256) pf_logits_kernel(const uint16_t *x, int hidden, const uint16_t *wr, int E,
-                                                        float *logits) {
-  const int t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 8 + warp;
-  if (e >= E) return;
-  const uint4 *xv = reinterpret_cast<const uint4 *>(x + (size_t)t * hidden);
-  const uint4 *wv = reinterpret_cast<const uint4 *>(wr + (size_t)e * hidden);
-  double a0 = 0.0, a1 = 0.0;
-#pragma unroll 4
-  for (int c = lane; c < hidden / 8; c += 32) {
-    const uint4 xa = __ldg(xv + c), wa = __ldg(wv + c);
-    const uint32_t xs[4] = {xa.x, xa.y, xa.z, xa.w}, ws[4] = {wa.x, wa.y, wa.z, wa.w};
+// logits[t][e] = f32(sum_h f64(x[t][h]) * f64(wr[e][h])).  A CTA takes 8
+// experts x 32 tokens: the experts' router rows are staged in shared memory
+// once and reused by all 32 tokens; each warp takes 4 tokens, each lane 8
+// columns per 256-column step, one f64 accumulator per expert.
+constexpr int kPfLogitExperts = 8, kPfLogitTokens = 32;
+
+__global__ void __launch_bounds__(256) pf_logits_kernel(const uint16_t *x, int T, int hidden, const uint16_t *wr,
+                                                        int E, float *logits) {
+  extern __shared__ __align__(16) uint8_t pf_logit_smem[];
+  uint4 *w_s = reinterpret_cast<uint4 *>(pf_logit_smem);    // [8][hidden/8]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x * kPfLogitExperts, t0 = blockIdx.y * kPfLogitTokens;
+  const int v8 = hidden / 8;
+  for (int i = threadIdx.x; i < kPfLogitExperts * v8; i += blockDim.x) {
+    const int ei = i / v8, c = i - ei * v8;
+    w_s[i] = e0 + ei < E ? __ldg(reinterpret_cast<const uint4 *>(wr + (size_t)(e0 + ei) * hidden) + c)
+                         : make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  for (int tt = 0; tt < kPfLogitTokens / 8; ++tt) {
+    const int t = t0 + warp * (kPfLogitTokens / 8) + tt;
+    if (t >= T) break;
+    double acc[kPfLogitExperts];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      a0 = fma((double)bf16_to_f32(xs[j] & 0xFFFFu), (double)bf16_to_f32(ws[j] & 0xFFFFu), a0);
-      a1 = fma((double)bf16_to_f32(xs[j] >> 16), (double)bf16_to_f32(ws[j] >> 16), a1);
+    for (int ei = 0; ei < kPfLogitExperts; ++ei) acc[ei] = 0.0;
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + (size_t)t * hidden);
+    for (int c = lane; c < v8; c += 32) {
+      const uint4 xa = __ldg(xr + c);
+      const uint32_t xs[4] = {xa.x, xa.y, xa.z, xa.w};
+      double xd[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xd[2 * j] = (double)bf16_to_f32(xs[j] & 0xFFFFu);
+        xd[2 * j + 1] = (double)bf16_to_f32(xs[j] >> 16);
+      }
+#pragma unroll
+      for (int ei = 0; ei < kPfLogitExperts; ++ei) {
+        const uint4 wa = w_s[ei * v8 + c];
+        const uint32_t ws[4] = {wa.x, wa.y, wa.z, wa.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[ei] = fma(xd[2 * j], (double)bf16_to_f32(ws[j] & 0xFFFFu), acc[ei]);
+          acc[ei] = fma(xd[2 * j + 1], (double)bf16_to_f32(ws[j] >> 16), acc[ei]);
+        }
+      }
+    }
+#pragma unroll
+    for (int ei = 0; ei < kPfLogitExperts; ++ei) {
+      double a = acc[ei];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0 && e0 + ei < E) logits[(size_t)t * E + e0 + ei] = __double2float_rn(a);
     }
   }
-  double a = a0 + a1;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-  if (lane == 0) logits[(size_t)t * E + e] = __double2float_rn(a);
 }
 
 struct PfSelectParams {
@@ -379,6 +412,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
   extern __shared__ uint8_t pf_raw_smem[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(pf_raw_smem) + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lq = warp & 3;            // TMEM lane quarter this warp may read
+  const int ch = warp >> 2;           // token-column half this warp promotes
   uint8_t *sA = sm + kPfA;
   float *sS = reinterpret_cast<float *>(sm + kPfS);
   const uint32_t bar_u0 = smem_addr(sm + kPfBar), bar_mma = bar_u0 + 16;
@@ -400,12 +435,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint64_t pol = policy_evict_first();
-  const int n_items = *p.n_chunks * p.m_tiles;
+  const int n_chunks = *p.n_chunks;
+  const int n_items = n_chunks * p.m_tiles;
   uint32_t ph_u[2] = {0u, 0u}, ph_mma = 0u;
   bool failed = false;
+  const int r_row = 32 * lq + lane;                 // TMEM lane = weight row of the tile
+  const int u_row = r_row >> 4, rr = r_row & 15;
 
   for (int item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
-    const int chunk = item % *p.n_chunks, m = item / *p.n_chunks;
+    const int chunk = item % n_chunks, m = item / n_chunks;
     const int e = p.chunk_expert[chunk], row0 = p.chunk_row0[chunk], n = p.chunk_n[chunk];
     const int n16 = (n + 15) & ~15;
     const uint8_t *wt = p.expert_tiles[e];
@@ -413,11 +451,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
       if (tid == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
       continue;
     }
-    // source rows of this thread's B chunks (row = j*4 + warp, j < 16)
-    const uint16_t *srow[16];
+    // source rows of this thread's B chunks: token row warp + 8j, 16-byte column chunk `lane`
+    const uint16_t *srow[kPfCols / kPfWarps];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int r = j * 4 + warp;
+    for (int j = 0; j < kPfCols / kPfWarps; ++j) {
+      const int r = warp + kPfWarps * j;
       srow[j] = nullptr;
       if (r < n) {
         const int prow = row0 + r;
@@ -436,23 +474,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
     auto issue_b = [&](int kbi, int st) {
       uint8_t *sB = sm + kPfB + st * kPfBStage;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int r = j * 4 + warp;                  // token row of the chunk
-        const int kc = lane;                         // 16-byte column chunk (8 bf16)
-        const uint32_t dst = smem_addr(sB + (kc >> 3) * kPfBSub + sw128_off(r, (kc & 7) * 8));
-        const uint16_t *src = srow[j] ? srow[j] + kbi * kUnitK + kc * 8 : p.src;
+      for (int j = 0; j < kPfCols / kPfWarps; ++j) {
+        const int r = warp + kPfWarps * j;
+        const uint32_t dst = smem_addr(sB + (lane >> 3) * kPfBSub + sw128_off(r, (lane & 7) * 8));
+        const uint16_t *src = srow[j] ? srow[j] + kbi * kUnitK + lane * 8 : p.src;
         cp_async16(dst, src, srow[j] ? 16u : 0u);
       }
       cp_async_commit();
     };
 
-    float acc[kPfCols];
+    float acc[kPfCols / 2];
 #pragma unroll
-    for (int i = 0; i < kPfCols; ++i) acc[i] = 0.f;
+    for (int i = 0; i < kPfCols / 2; ++i) acc[i] = 0.f;
     issue_units(0, 0);
     issue_b(0, 0);
-    const int r_row = tid;                            // TMEM lane = weight row of the tile
-    const int u_row = r_row >> 4, rr = r_row & 15;
     for (int kbi = 0; kbi < p.kb; ++kbi) {
       const int st = kbi & 1;
       if (kbi + 1 < p.kb) {
@@ -463,13 +498,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
         cp_async_wait_all();
       }
       __syncthreads();                                // B(kbi) visible to all threads
-      // group sums of the B rows: thread -> (row tid % 64, groups 4*(tid/64) .. +3)
       {
+        // group sums of the B rows: (row idx & 63, group idx >> 6)
         const uint8_t *sB = sm + kPfB + st * kPfBStage;
-        const int r = tid & 63;
 #pragma unroll
-        for (int gg = 0; gg < 4; ++gg) {
-          const int g = (tid >> 6) * 4 + gg;
+        for (int i = 0; i < 2; ++i) {
+          const int idx = tid + kPfThreads * i;
+          const int r = idx & 63, g = idx >> 6;
           float part = 0.f;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -482,7 +517,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
           sS[g * kPfCols + r] = part;
         }
       }
-      // weight codes -> bf16 (128 + code) A tile
       const bool ok_u = mbar_wait_bounded(bar_u0 + 8 * st, ph_u[st]);
       ph_u[st] ^= 1u;
       if (__syncthreads_or(!ok_u)) {
@@ -490,22 +524,33 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
         break;
       }
       {
+        // weight codes -> bf16 (128 + code): one quad of fragment words (lanes
+        // 4g..4g+3 of step s) holds 8 consecutive columns of rows g and g+8
+        // twice over, written as four 16-byte swizzled chunks
         const uint8_t *U = sm + kPfU + st * kPfUStage;
-#pragma unroll 4
-        for (int j = 0; j < 32; ++j) {
-          const int w = tid + kPfThreads * j;         // code word of the 8 units
-          const int u = w >> 9, wi = w & 511;
-          const int s = (wi >> 7) * 4 + (wi & 3), l = (wi >> 2) & 31;
-          const int g = l >> 2, q = l & 3;
-          const uint32_t word = *reinterpret_cast<const uint32_t *>(U + u * kUnitBytes + wi * 4);
-          const int ra = u * 16 + g, rb = ra + 8;
-          const int k0 = 16 * s + 2 * q;
-          const int sub0 = k0 >> 6, kk0 = k0 & 63;
-          const int sub1 = (k0 + 8) >> 6, kk1 = (k0 + 8) & 63;
-          *reinterpret_cast<uint32_t *>(sA + sub0 * kPfASub + sw128_off(ra, kk0)) = codes_to_bf16x2<0>(word);
-          *reinterpret_cast<uint32_t *>(sA + sub0 * kPfASub + sw128_off(rb, kk0)) = codes_to_bf16x2<1>(word);
-          *reinterpret_cast<uint32_t *>(sA + sub1 * kPfASub + sw128_off(ra, kk1)) = codes_to_bf16x2<2>(word);
-          *reinterpret_cast<uint32_t *>(sA + sub1 * kPfASub + sw128_off(rb, kk1)) = codes_to_bf16x2<3>(word);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int gi = tid + kPfThreads * j;
+          const int u = gi >> 7, rem = gi & 127, s = rem >> 3, g = rem & 7;
+          const uint8_t *base = U + u * kUnitBytes + ((s >> 2) * 32 + 4 * g) * 16 + (s & 3) * 4;
+          uint32_t w[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) w[q] = *reinterpret_cast<const uint32_t *>(base + q * 16);
+          const int ra = 16 * u + g, rb = ra + 8;
+          uint8_t *A = sA + (s >> 2) * kPfASub;
+          const int kk = 16 * (s & 3);
+          *reinterpret_cast<uint4 *>(A + sw128_off(ra, kk)) =
+              make_uint4(codes_to_bf16x2<0>(w[0]), codes_to_bf16x2<0>(w[1]), codes_to_bf16x2<0>(w[2]),
+                         codes_to_bf16x2<0>(w[3]));
+          *reinterpret_cast<uint4 *>(A + sw128_off(ra, kk + 8)) =
+              make_uint4(codes_to_bf16x2<2>(w[0]), codes_to_bf16x2<2>(w[1]), codes_to_bf16x2<2>(w[2]),
+                         codes_to_bf16x2<2>(w[3]));
+          *reinterpret_cast<uint4 *>(A + sw128_off(rb, kk)) =
+              make_uint4(codes_to_bf16x2<1>(w[0]), codes_to_bf16x2<1>(w[1]), codes_to_bf16x2<1>(w[2]),
+                         codes_to_bf16x2<1>(w[3]));
+          *reinterpret_cast<uint4 *>(A + sw128_off(rb, kk + 8)) =
+              make_uint4(codes_to_bf16x2<3>(w[0]), codes_to_bf16x2<3>(w[1]), codes_to_bf16x2<3>(w[2]),
+                         codes_to_bf16x2<3>(w[3]));
         }
       }
       // this thread's row parameters for the 8 groups
@@ -544,20 +589,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
         break;
       }
       tc_fence_after();
-      // promotion: acc += scale * D_g + (min - 128 scale) * S_g
-#pragma unroll 1
-      for (int g = 0; g < kPfGroups; ++g) {
-        const float s = sc[g], a3 = mp[g];
-        const float *Sg = sS + g * kPfCols;
+      // promotion: acc += scale * D_g + (min - 128 scale) * S_g for this
+      // warp's 32 token columns
 #pragma unroll
-        for (int c16 = 0; c16 < kPfCols / 16; ++c16) {
-          if (c16 * 16 < n16) {
+      for (int g = 0; g < kPfGroups; ++g) {
+        const float sgl = sc[g], a3 = mp[g];
+        const float *Sg = sS + g * kPfCols + 32 * ch;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (32 * ch + 16 * h < n16) {
             uint32_t v[16];
-            tmem_ld16(tbase + ((uint32_t)(warp * 32) << 16) + g * kPfCols + c16 * 16, v);
+            tmem_ld16(tbase + ((uint32_t)(32 * lq) << 16) + g * kPfCols + 32 * ch + 16 * h, v);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              acc[c16 * 16 + j] = fmaf(s, __uint_as_float(v[j]), fmaf(a3, Sg[c16 * 16 + j], acc[c16 * 16 + j]));
+              acc[16 * h + j] = fmaf(sgl, __uint_as_float(v[j]), fmaf(a3, Sg[16 * h + j], acc[16 * h + j]));
           }
         }
       }
@@ -565,24 +611,27 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
       __syncthreads();                                // TMEM, A and this stage's B/U free again
     }
     if (failed) break;
-    // ---- epilogue
+    // ---- epilogue: this warp's 32 token columns
     if (EPI == kPfEpiGlu) {
       const int col = 8 * (8 * m + u_row) + rr;       // rows rr < 8: gate, rr >= 8: up of the same column
 #pragma unroll
-      for (int t = 0; t < kPfCols; ++t) {
+      for (int t = 0; t < kPfCols / 2; ++t) {
         const float up = __shfl_down_sync(0xffffffffu, acc[t], 8);
-        if (rr < 8 && t < n) {
+        const int tok = 32 * ch + t;
+        if (rr < 8 && tok < n) {
           const float gate = bf16_round(acc[t]);
           const float u = bf16_round(up);
           const float v = p.act == RC_ACT_SITU ? act_situ(gate, u, p.gate_beta, p.value_beta) : act_swiglu(gate, u);
-          p.y[(size_t)(row0 + t) * p.ld_y + col] = f32_to_bf16_rne(v);
+          p.y[(size_t)(row0 + tok) * p.ld_y + col] = f32_to_bf16_rne(v);
         }
       }
     } else {
       const int col = kPfRows * m + r_row;
 #pragma unroll
-      for (int t = 0; t < kPfCols; ++t)
-        if (t < n) p.y[(size_t)(row0 + t) * p.ld_y + col] = f32_to_bf16_rne(acc[t]);
+      for (int t = 0; t < kPfCols / 2; ++t) {
+        const int tok = 32 * ch + t;
+        if (tok < n) p.y[(size_t)(row0 + tok) * p.ld_y + col] = f32_to_bf16_rne(acc[t]);
+      }
     }
   }
   if (failed && tid == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
@@ -824,7 +873,17 @@ static int pf_route(rc_moe *m, const uint16_t *x, int T, int k, int router, int 
                     cudaStream_t s) {
   PfScratch *ps = m->pf;
   const int E = m->n_experts;
-  pf_logits_kernel<<<dim3((E + 7) / 8, T), 256, 0, s>>>(x, m->hidden, m->router_w, E, ps->logits);
+  const size_t lsm = (size_t)kPfLogitExperts * m->hidden * 2;
+  static bool configured[64] = {};
+  int dev = 0;
+  RC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 64 || !configured[dev]) {
+    RC_CUDA_TRY(cudaFuncSetAttribute(pf_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemLimit));
+    if (dev < 64) configured[dev] = true;
+  }
+  RC_CHECK_ARG(lsm <= (size_t)kGemvSmemLimit, "hidden %d too large for the prefill router", m->hidden);
+  pf_logits_kernel<<<dim3((E + kPfLogitExperts - 1) / kPfLogitExperts, (T + kPfLogitTokens - 1) / kPfLogitTokens),
+                     256, lsm, s>>>(x, T, m->hidden, m->router_w, E, ps->logits);
   RC_CUDA_TRY(cudaGetLastError());
   PfSelectParams sp{};
   sp.logits = ps->logits;
@@ -853,6 +912,25 @@ static int pf_check(rc_moe *m, const uint16_t *x, int T, int k, int act, int lo,
   RC_CHECK_ARG((2 * m->inter) % kPfRows == 0 && m->hidden % kPfRows == 0,
                "prefill needs 2*inter and hidden multiples of 128");
   for (int e = lo; e < hi; ++e) RC_CHECK_ARG(m->gate_up[e] != nullptr, "expert %d is not loaded", e);
+  return RC_OK;
+}
+
+int pf_route_tokens(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
+                    int32_t *ids_dev, float *w_dev, float *logits_dev, void *stream) {
+  RC_CHECK_ARG(T >= 1 && T <= kPfMaxTokens, "rc_moe_route: T must be 1..%d", kPfMaxTokens);
+  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK && k <= m->n_experts, "rc_moe_route: k must be 1..%d and <= n_experts",
+               kMoeMaxK);
+  RC_CHECK_ARG((reinterpret_cast<uintptr_t>(x_dev) & 15) == 0, "token rows must be 16-byte aligned");
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  int rc = pf_scratch(m, T);
+  if (rc) return rc;
+  const cudaStream_t s = pick_stream(m->ctx, stream);
+  if ((rc = pf_route(m, x_dev, T, k, router, renormalize, scaling, s))) return rc;
+  if (ids_dev) RC_CUDA_TRY(cudaMemcpyAsync(ids_dev, m->pf->ids, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
+  if (w_dev) RC_CUDA_TRY(cudaMemcpyAsync(w_dev, m->pf->weights, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
+  if (logits_dev)
+    RC_CUDA_TRY(
+        cudaMemcpyAsync(logits_dev, m->pf->logits, (size_t)T * m->n_experts * 4, cudaMemcpyDeviceToDevice, s));
   return RC_OK;
 }
 

@@ -80,6 +80,9 @@ class ExpertParallelMoe:
         import torch.distributed as dist
         M, H = x.shape
         N, k = self.world, self.k
+        if N == 1:                      # nothing to exchange: the single-GPU layer
+            self.layer.decode(x, k, out, **self.kw)
+            return
         T = N * M
         dev = x.device
         if N > 1:
@@ -98,6 +101,36 @@ class ExpertParallelMoe:
             mine = slots
         self.layer.combine(mine, sw[self.rank * M:(self.rank + 1) * M], k, out, tokens=M,
                            with_shared=self.layer.has_shared)
+
+    def prefill(self, x, out) -> None:
+        """Prefill of this rank's M tokens x [M, hidden] -> out [M, hidden]: the
+        same exchange as ``decode`` around the tensor-core grouped GEMM
+        (``MoeLayer.prefill_local`` / ``prefill_combine``)."""
+        import torch
+        import torch.distributed as dist
+        M, H = x.shape
+        N, k = self.world, self.k
+        if N == 1:
+            self.layer.prefill(x, k, out, **self.kw)
+            return
+        T = N * M
+        dev = x.device
+        if N > 1:
+            xg = self._buf("pxg", (T, H), torch.int16, dev)
+            dist.all_gather_into_tensor(_bf16(xg), _bf16(x), group=self.group)
+        else:
+            xg = x
+        slots = self._buf("pslots", (T, k + 1, H), torch.int16, dev)
+        sw = self._buf("psw", (T, k), torch.float32, dev)
+        shared = (self.rank * M, M) if self.layer.has_shared else (0, 0)
+        self.layer.prefill_local(xg, k, slots, sw, experts=self.experts, shared_tokens=shared, **self.kw)
+        if N > 1:
+            mine = self._buf("pmine", (M, k + 1, H), torch.int16, dev)
+            dist.reduce_scatter_tensor(_bf16(mine), _bf16(slots), op=dist.ReduceOp.SUM, group=self.group)
+        else:
+            mine = slots
+        self.layer.prefill_combine(mine, sw[self.rank * M:(self.rank + 1) * M], k, out, tokens=M,
+                                   with_shared=self.layer.has_shared)
 
     def decode_host(self, x: np.ndarray) -> np.ndarray:
         """Host entry point: x [M, hidden] bf16 bits -> out [M, hidden] (copies in
