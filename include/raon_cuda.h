@@ -224,6 +224,19 @@ int rc_moe_prefill_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int rou
 int rc_moe_prefill_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int T,
                            int k, int with_shared, uint16_t *out_dev, void *stream);
 
+/* Token sampling on bf16 logits [T][ld] (device), the reference's
+ * ``sample_token`` (serve/engine.py:84-140) in f64: presence penalty over each
+ * token row's seen ids (concatenated in seen_dev, row t at
+ * [seen_off[t], seen_off[t+1]); both NULL for none), then greedy argmax when
+ * temperature <= 0, else top-k (1..1024, ties kept) -> top-p -> temperature ->
+ * categorical draw with the caller's uniform u_dev[t] in [0, 1) (the value
+ * numpy's Generator.random() would feed Generator.choice).  out_dev [T] int32.
+ * A vocabulary-wide top-p without top-k is not supported (RC_ERR_INVALID). */
+int rc_sample_tokens(rc_ctx *ctx, const uint16_t *logits_dev, int ld, int T, int V, int top_k,
+                     double top_p, double temperature, double presence_penalty,
+                     const int32_t *seen_dev, const int32_t *seen_off_dev, const double *u_dev,
+                     int32_t *out_dev, void *stream);
+
 /* rc_gemv without any device allocation (this entry point has no counterpart
  * in the reference).  Arguments and results are those of rc_gemv; the context
  * is the one the weight was uploaded with.

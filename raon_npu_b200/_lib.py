@@ -36,6 +36,7 @@ _I = ctypes.c_int
 _U = ctypes.c_uint
 _SZ = ctypes.c_size_t
 _F = ctypes.c_float
+_D = ctypes.c_double
 
 # name -> (restype, argtypes); must list every function of include/raon_cuda.h.
 SIGNATURES = {
@@ -71,6 +72,7 @@ SIGNATURES = {
     "rc_moe_prefill_experts": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _F, _I, _P, _P]),
     "rc_moe_prefill_local": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _I, _I, _I, _I, _P, _P, _P]),
     "rc_moe_prefill_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _P]),
+    "rc_sample_tokens": (_I, [_P, _P, _I, _I, _I, _I, _D, _D, _D, _P, _P, _P, _P, _P]),
 }
 
 _lib = None

@@ -78,10 +78,18 @@ int check_error_word(rc_ctx *ctx) {
   RC_CUDA_TRY(cudaMemcpy(&word, ctx->err, sizeof(int), cudaMemcpyDeviceToHost));
   if (word) {
     RC_CUDA_TRY(cudaMemset(ctx->err, 0, sizeof(int)));
+    if (word == 2) {
+      set_error("sampler: more than 2048 tokens tie at the top-k threshold (device error word 2)");
+      return RC_ERR_INVALID;
+    }
     set_error("a kernel gave up a bounded wait (device error word %d)", word);
     return RC_ERR_TIMEOUT;
   }
   return RC_OK;
+}
+
+int ensure_sample_scratch(rc_ctx *ctx, size_t bytes) {
+  return grow_device(&ctx->sample_bits, &ctx->sample_bits_cap, bytes);
 }
 
 int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb) {
@@ -154,6 +162,7 @@ int rc_destroy(rc_ctx *ctx) {
   cudaFree(ctx->qflag);
   cudaFree(ctx->dev_x);
   cudaFree(ctx->dev_y);
+  cudaFree(ctx->sample_bits);
   if (ctx->pin_x) cudaFreeHost(ctx->pin_x);
   if (ctx->pin_y) cudaFreeHost(ctx->pin_y);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);

@@ -102,11 +102,15 @@ struct rc_ctx {
   size_t pin_x_cap, pin_y_cap;
   void *dev_x, *dev_y;
   size_t dev_x_cap, dev_y_cap;
+  // Sampler scratch: seen-token bitmaps.
+  void *sample_bits;
+  size_t sample_bits_cap;
 };
 
 namespace rc {
 int ensure_gemv_scratch(rc_ctx *ctx, int k, int n_tiles);
 int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb);
+int ensure_sample_scratch(rc_ctx *ctx, size_t bytes);
 int check_error_word(rc_ctx *ctx);
 // Words of one xfrag slot / floats of one gsum slot for K columns.
 inline size_t xfrag_slot_words(size_t k) { return 2 * k * 4; }

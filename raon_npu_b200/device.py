@@ -90,6 +90,23 @@ class Context:
               "rc_quantize_q4nx")
 
 
+def sample_tokens(ctx: "Context", logits_dev, u_dev, out_dev, top_k: int = 50, top_p: float = 0.9,
+                  temperature: float = 1.0, presence_penalty: float = 0.0, seen_dev=None, seen_off_dev=None,
+                  stream: int | None = None) -> None:
+    """Token ids [T] from bf16 logits [T, V] (``rc_sample_tokens``;
+    serve/engine.py:84-140 semantics, uniform draws u_dev [T] f64)."""
+    if logits_dev.dim() == 1:
+        T, V, ld = 1, int(logits_dev.shape[0]), int(logits_dev.shape[0])
+    else:
+        T, V = int(logits_dev.shape[0]), int(logits_dev.shape[1])
+        ld = int(logits_dev.stride(0))
+    check(ctx.lib.rc_sample_tokens(
+        ctx.handle, ctypes.c_void_p(_ptr(logits_dev)), ld, T, V, int(top_k), float(top_p), float(temperature),
+        float(presence_penalty), ctypes.c_void_p(_ptr(seen_dev)), ctypes.c_void_p(_ptr(seen_off_dev)),
+        ctypes.c_void_p(_ptr(u_dev)), ctypes.c_void_p(_ptr(out_dev)),
+        ctypes.c_void_p(_stream_for(stream, logits_dev, out_dev))), "rc_sample_tokens")
+
+
 class Q4nxWeight:
     """A q4nx matrix resident in HBM in the GEMV tile layout."""
 

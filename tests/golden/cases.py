@@ -28,6 +28,17 @@ LINEAR_CASES = {
 }
 
 MOE_CASE = dict(hidden=256, inter=256, experts=6, k=3, tokens=3, seed=31)
+
+# Sampler (serve/engine.py:84-140): name -> (vocab, seed, logit kind, options)
+SAMPLE_CASES = {
+    "vocab_k50_p09": (151936, 301, "normal", dict(temperature=1.0, top_p=0.9, top_k=50, presence_penalty=0.0)),
+    "vocab_penalty": (151936, 302, "normal", dict(temperature=1.0, top_p=0.9, top_k=50, presence_penalty=1.5)),
+    "temp07_k20_p095": (151936, 303, "normal", dict(temperature=0.7, top_p=0.95, top_k=20, presence_penalty=0.0)),
+    "greedy_penalty": (151936, 304, "normal", dict(temperature=0.0, top_p=0.9, top_k=50, presence_penalty=1.5)),
+    "ties_k5": (4096, 305, "ties", dict(temperature=1.0, top_p=0.99, top_k=5, presence_penalty=0.0)),
+    "small_p05": (1000, 306, "normal", dict(temperature=1.3, top_p=0.5, top_k=100, presence_penalty=0.5)),
+    "no_topk_p09": (3000, 307, "normal", dict(temperature=1.0, top_p=0.9, top_k=0, presence_penalty=0.0)),
+}
 ROUTER_CASE = dict(hidden=256, experts=16, k=4, tokens=8, seed=41, scaling=2.5)
 COMBINE_CASE = dict(tokens=20, k=4, hidden=64, seed=51)
 
@@ -133,3 +144,17 @@ def combine_inputs(tokens, k, hidden, seed):
     shared = _bf16_bits(rng.standard_normal((tokens, hidden)).astype(np.float32))
     w = rng.uniform(0.0, 1.0, (tokens, k)).astype(np.float32)
     return {"top_ids": ids, "rows": rows, "shared": shared, "top_w": w}
+
+
+def sample_inputs(vocab, seed, kind):
+    """(logits f32 holding bf16 values, seen token ids, the generator seed of the draw)."""
+    rng = np.random.default_rng(seed)
+    if kind == "ties":
+        x = np.round(rng.standard_normal(vocab) * 2.0).astype(np.float32)   # few distinct levels
+    else:
+        x = (rng.standard_normal(vocab) * 2.5).astype(np.float32)
+    bits = _bf16_bits(x)
+    logits = (bits.astype(np.uint32) << 16).view(np.float32)
+    order = np.argsort(-logits, kind="stable")
+    seen = [int(order[0]), int(order[3]), int(order[17]), int(rng.integers(vocab)), int(rng.integers(vocab))]
+    return logits, seen, seed + 1000

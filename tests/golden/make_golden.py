@@ -32,11 +32,12 @@ from host.backend import NumpyBackend  # noqa: E402
 from host.weights import Weights  # noqa: E402
 from host.raon import RaonModel  # noqa: E402
 from kernels.moe_grouped.planner import build_plan, scatter_b2  # noqa: E402
+from serve.engine import GenOptions, sample_token  # noqa: E402
 
 sys.path.insert(0, str(HERE.parent.parent))
 from tests.golden.cases import (  # noqa: E402
-    QUANT_CASES, LINEAR_CASES, MOE_CASE, ROUTER_CASE, COMBINE_CASE,
-    quant_input, linear_inputs, moe_inputs, router_inputs, combine_inputs,
+    QUANT_CASES, LINEAR_CASES, MOE_CASE, ROUTER_CASE, COMBINE_CASE, SAMPLE_CASES,
+    quant_input, linear_inputs, moe_inputs, router_inputs, combine_inputs, sample_inputs,
 )
 
 
@@ -143,7 +144,20 @@ def make_combine():
     np.savez_compressed(HERE / "combine.npz", routed=routed, shared=shared)
 
 
+def make_sample():
+    """serve.engine.sample_token on seeded logits: 20 draws per case (generator
+    seeds s, s+1, ...)."""
+    out = {}
+    for name, (vocab, seed, kind, opts) in SAMPLE_CASES.items():
+        logits, seen, gseed = sample_inputs(vocab, seed, kind)
+        o = GenOptions(**opts)
+        out[f"{name}/tokens"] = np.array(
+            [sample_token(logits, seen, o, np.random.default_rng(gseed + i)) for i in range(20)], np.int64)
+    np.savez_compressed(HERE / "sample.npz", **out)
+
+
 if __name__ == "__main__":
+    make_sample()
     make_quant()
     make_linear()
     make_moe()

@@ -222,3 +222,18 @@ def test_bf16_directed_rounding():
 def test_softmax_topk_lower_index_wins_ties():
     logits = np.array([0.5, 2.0, 2.0, -1.0, 2.0, 0.5], np.float32)
     np.testing.assert_array_equal(ob.topk_lower_index_wins(logits, 4), [1, 2, 4, 0])
+
+
+# ---------------------------------------------------------------- sampler --
+@pytest.mark.parametrize("name", list(cases.SAMPLE_CASES))
+def test_sampler_restatement_matches_reference_draws(name):
+    """serve/engine.py:84-140 run by the reference (tests/golden/sample.npz,
+    20 generator seeds per case) vs the oracle's restatement fed the same
+    generator's uniform draw."""
+    from oracle.sampling import sample_token_u
+    g = np.load(Path(cases.__file__).with_name("sample.npz"))
+    vocab, seed, kind, opts = cases.SAMPLE_CASES[name]
+    logits, seen, gseed = cases.sample_inputs(vocab, seed, kind)
+    got = [sample_token_u(logits, seen, opts["top_k"], opts["top_p"], opts["temperature"],
+                          opts["presence_penalty"], np.random.default_rng(gseed + i).random()) for i in range(20)]
+    np.testing.assert_array_equal(got, g[f"{name}/tokens"])
