@@ -259,6 +259,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     moe = None if args.no_moe else run_moe(args, ctx, torch, dev, rank, world, local_rank, barrier)
     prefill = None if args.no_moe else run_moe_prefill(args, ctx, torch, dev, rank, world, local_rank, barrier)
+    dstep = None if args.no_decode_step else run_decode_step(args, ctx, torch, dev, rank, world, local_rank,
+                                                             barrier)
 
     if rank == 0:
         line = {
@@ -282,6 +284,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "cpu_baseline": cpu,
             "moe": moe,
             "moe_prefill": prefill,
+            "decode_step": dstep,
         }
         print(json.dumps(line), flush=True)
     ctx.close()
@@ -697,6 +700,231 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
     }
 
 
+# ------------------------------------------------------ full decode step --
+# 48 layers, each a q4nx projection pair 2048->4096 ->
+# 2048 and the config-3 MoE block (residual add + RMS normalisation after the
+# MoE: a SwiGLU block is quadratic in its input, so an unnormalised residual
+# stream of random layers overflows within ~20 layers), then the
+# 2048->151936 lm-head and top-k 50 / top-p 0.9 sampling on the GPU; one token
+# per rank per step; projections replicated, experts sharded over the ranks.
+DECODE_LAYERS = 48
+LM_HEAD = (151936, 2048)
+
+
+def build_decode_model(ctx, torch, dev):
+    """Seeded random-init model: projections N(0, 1/K) (the variance of the
+    hidden stream stays put over 48 layers), experts and router N(0, 0.02)."""
+    import math
+    from raon_npu_b200.device import MoeLayer
+    from raon_npu_b200.expert_parallel import ExpertParallelMoe
+    H, I, E, k = MOE["hidden"], MOE["inter"], MOE["experts"], MOE["k"]
+    gen = torch.Generator(device=dev)
+
+    def q4(n, kk, seed, std):
+        gen.manual_seed(seed)
+        w = torch.randn((n, kk), generator=gen, device=dev) * std
+        packed = torch.empty(n * kk * 5 // 8, dtype=torch.uint8, device=dev)
+        ctx.quantize_q4nx(w, packed, n, kk)
+        del w
+        return packed
+
+    layers = []
+    for li in range(DECODE_LAYERS):
+        projs = []
+        for j, (n, kk) in enumerate([(4096, H), (H, 4096)]):
+            packed = q4(n, kk, 8_000_000 + 10 * li + j, 1.0 / math.sqrt(kk))
+            projs.append(ctx.upload_q4nx(packed, n, kk))
+        layer = MoeLayer(ctx, H, I, E, has_shared=True)
+        ep = ExpertParallelMoe(layer, k, act="swiglu", router="softmax")
+        for e in range(E + 1):
+            if ep.owns(e):
+                layer.set_expert(e, q4(2 * I, H, _moe_seed(100 + li, e), 0.02), q4(H, I, _moe_seed(100 + li, e) + 500,
+                                                                                  0.02))
+        gen.manual_seed(_moe_seed(100 + li, 999))
+        wr = (torch.randn((E, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        layer.set_router(wr.view(torch.int16).cpu().numpy().view(np.uint16))
+        layers.append((projs, ep))
+    lm = ctx.upload_q4nx(q4(LM_HEAD[0], LM_HEAD[1], 8_999_999, 0.02), LM_HEAD[0], LM_HEAD[1])
+    torch.cuda.synchronize()
+    return layers, lm
+
+
+def run_decode_step(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barrier):
+    import torch.distributed as dist
+    from raon_npu_b200.device import add_rms_bf16, sample_tokens
+    H = MOE["hidden"]
+    layers, lm = build_decode_model(ctx, torch, dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5151 + rank)
+    x0 = torch.randn((1, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16).contiguous()
+    h1 = torch.empty((1, 4096), dtype=torch.int16, device=dev)
+    h = torch.empty((1, H), dtype=torch.int16, device=dev)
+    mo = torch.empty((1, H), dtype=torch.int16, device=dev)
+    xs = [torch.empty((1, H), dtype=torch.int16, device=dev) for _ in range(2)]
+    logits = torch.empty((1, LM_HEAD[0]), dtype=torch.int16, device=dev)
+    u = torch.tensor([np.random.default_rng(77 + rank).random()], dtype=torch.float64, device=dev)
+    tok = torch.empty(1, dtype=torch.int32, device=dev)
+    trace = []
+
+    def step(record=False):
+        cur = x0
+        for li, ((wa, wb), ep) in enumerate(layers):
+            wa.gemv_into(cur, h1, 1)
+            wb.gemv_into(h1, h, 1)
+            if record:
+                trace.append(h.clone())
+            ep.decode(h, mo)
+            nxt = xs[li & 1]
+            add_rms_bf16(ctx, h, mo, nxt)
+            cur = nxt
+        lm.gemv_into(cur, logits, 1)
+        sample_tokens(ctx, logits, u, tok, top_k=50, top_p=0.9, temperature=1.0)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx.sync()
+    graph, graph_err = None, None
+    try:
+        graph = capture_graph(torch, step)
+    except Exception as e:                  # noqa: BLE001 - reported in the JSON line
+        graph, graph_err = None, f"{type(e).__name__}: {e}"[:200]
+    ok = torch.tensor([1 if graph is not None else 0], dtype=torch.int32, device=dev)
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if not int(ok.item()):
+        graph = None
+    run = graph.replay if graph is not None else step
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(_gpu_index(local_rank))
+    clocks.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    steps = max(3, args.steps // 4)
+    e0.record(stream)
+    for _ in range(steps):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / steps
+    ms_max = ms
+    if world > 1:
+        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_max = float(tt.item())
+    ctx.sync()
+
+    # end to end: host hidden row -> device, the step, the sampled id -> host
+    host_x = x0.cpu().numpy()
+    pin = torch.from_numpy(host_x.copy()).pin_memory()
+    tok_host = torch.empty(1, dtype=torch.int32).pin_memory()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        x0.copy_(pin, non_blocking=True)
+        run()
+        tok_host.copy_(tok, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    e2e_s = (time.perf_counter() - t0) / steps
+    if world > 1:
+        tt = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    del graph
+
+    # algorithmic bytes of one step on this rank: projections, the distinct
+    # owned experts the layer's gathered tokens chose, shared, router, lm-head
+    step(record=True)
+    torch.cuda.synchronize()
+    E, k, eb = MOE["experts"], MOE["k"], moe_expert_bytes(H, MOE["inter"])
+    lo, hi = layers[0][1].experts
+    nbytes = LM_HEAD[0] * LM_HEAD[1] * 5 // 8
+    for li, ((wa, wb), ep) in enumerate(layers):
+        hg = _gather_tokens(torch, dist, world, trace[li])
+        ids = torch.empty((hg.shape[0], k), dtype=torch.int32, device=dev)
+        w = torch.empty((hg.shape[0], k), dtype=torch.float32, device=dev)
+        ep.layer.route(hg, hg.shape[0], k, ids, w)
+        torch.cuda.synchronize()
+        idn = ids.cpu().numpy().ravel()
+        active = len({int(e) for e in idn if lo <= int(e) < hi})
+        nbytes += 2 * 4096 * H * 5 // 8 + (active + 1) * eb + E * H * 2
+    rb = torch.tensor([float(nbytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(rb)
+    avg_bytes = float(rb.item()) / world
+    peak, peak_kind = peaks()
+    achieved = avg_bytes / (ms_max * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = decode_step_cpu_sample(ctx, torch, dev, layers, lm, args.cpu_seconds)
+    for (wa, wb), ep in layers:
+        wa.free()
+        wb.free()
+        ep.layer.close()
+    lm.free()
+    return {
+        "metric": "decode step tokens/s (48 layers + lm-head + sampling)", "value": round(world / (ms_max * 1e-3), 2),
+        "unit": "tokens/s", "ms_per_step": round(ms_max, 4), "steps": steps, "scaling": "weak",
+        "config": {"workload": "synthetic full decode step (BASELINE configs[4])", "layers": DECODE_LAYERS,
+                   "per_layer": "q4nx 2048->4096->2048 projections + config-3 MoE (128+1 experts, top-8) + "
+                                "residual add with RMS normalisation", "lm_head": "2048->151936 q4nx", "sampling": "top-k 50, top-p 0.9, T=1",
+                   "tokens_per_rank": 1, "parallelism": f"projections replicated, experts ep{world}",
+                   "cuda_graph": graph_err is None and bool(int(ok.item())), "graph_error": graph_err,
+                   "l2": "each step streams ~2 GB of distinct weights (>> L2)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": None,
+                     "per_rank_bytes_per_step": round(avg_bytes),
+                     "kernel": "decode step per rank (96 GEMVs, 48 MoE layers, 48 adds, lm-head GEMV, sampler)"},
+        "e2e": {"value": round(world / e2e_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 2 * H,
+                "d2h_bytes_per_step": 4, "api": "graph replay with the hidden row copied in and the id copied out"},
+        "gpu_launches": (DECODE_LAYERS * 7 + 2) * steps,
+        "clocks": clk,
+        "cpu_baseline": cpu,
+    }
+
+
+def decode_step_cpu_sample(ctx, torch, dev, layers, lm, budget_s: float):
+    """The reference's CPU arithmetic for the step, timed on one layer (its
+    two projections and the MoE block for one token) and on the lm-head plus
+    sampler, extrapolated to 48 layers; f32 weights cached (dequantised on the
+    GPU, bit-identical to the reference's dequantiser)."""
+    from oracle import backend as ob
+    from oracle.sampling import sample_token_u
+
+    def f32(w):
+        out = torch.empty((w.n, w.k), dtype=torch.float32, device=dev)
+        w.dequant_into(out)
+        torch.cuda.synchronize()
+        return out.cpu().numpy()
+    (wa, wb), ep = layers[0]
+    fa, fb = f32(wa), f32(wb)
+    flm = f32(lm)
+    moe_tokens, moe_secs = moe_cpu_sample(16, budget_s / 2)
+    rng = np.random.default_rng(3)
+    x = ob.f32_to_bf16(rng.standard_normal(MOE["hidden"]).astype(np.float32))
+    t0 = time.perf_counter()
+    for _ in range(3):
+        ob.linear(fb, ob.linear(fa, x))
+    proj_s = (time.perf_counter() - t0) / 3
+    t0 = time.perf_counter()
+    lg = ob.linear(flm, x)
+    sample_token_u(ob.bf16_to_f32(lg), [], 50, 0.9, 1.0, 0.0, 0.5)
+    head_s = time.perf_counter() - t0
+    per_token = DECODE_LAYERS * (proj_s + moe_secs / moe_tokens) + head_s
+    return {"value": round(1.0 / per_token, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one layer (2 projections x3, MoE layer x{moe_tokens}) and the lm-head + sampler once, "
+                      f"numpy f32 with cached weights, extrapolated to {DECODE_LAYERS} layers"}
+
+
 def _bf16_peak() -> float:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -871,7 +1099,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-shape", action="store_true", help="skip the per-shape launch table")
-    ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode layer (configs[2])")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode / prefill layers (configs[2], [3])")
+    ap.add_argument("--no-decode-step", action="store_true", help="skip the 48-layer decode step (configs[4])")
     ap.add_argument("--profile", default=None, help="NxK: run a few plain GEMV launches for ncu and exit; "
                     "'moe' / 'prefill': a few config-3 decode / config-4 prefill steps")
     ap.add_argument("--tokens", type=int, default=1)

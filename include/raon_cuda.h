@@ -237,6 +237,16 @@ int rc_sample_tokens(rc_ctx *ctx, const uint16_t *logits_dev, int ld, int T, int
                      const int32_t *seen_dev, const int32_t *seen_off_dev, const double *u_dev,
                      int32_t *out_dev, void *stream);
 
+/* out = RTNE(f32(a) + f32(b)) over n bf16 values (device, 16-byte aligned):
+ * the residual add between the blocks of a decode step. */
+int rc_add_bf16(rc_ctx *ctx, const uint16_t *a_dev, const uint16_t *b_dev, uint16_t *out_dev, long long n,
+                void *stream);
+
+/* Per row r of [rows][n]: s = f32(a) + f32(b); out = RTNE(s / sqrt(mean(s^2) + eps)) -- the
+ * residual add followed by an RMS normalisation (no learned scale). */
+int rc_add_rms_bf16(rc_ctx *ctx, const uint16_t *a_dev, const uint16_t *b_dev, uint16_t *out_dev, int rows,
+                    int n, float eps, void *stream);
+
 /* rc_gemv without any device allocation (this entry point has no counterpart
  * in the reference).  Arguments and results are those of rc_gemv; the context
  * is the one the weight was uploaded with.

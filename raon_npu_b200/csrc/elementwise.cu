@@ -1,0 +1,100 @@
+// Elementwise glue of a decode step: the residual add of the hidden stream,
+// plain or followed by an RMS normalisation.
+#include "rc_device.cuh"
+#include "rc_internal.cuh"
+
+namespace rc {
+
+// out = RTNE(f32(a) + f32(b)), 8 bf16 per thread.
+__global__ void add_bf16_kernel(const uint16_t *a, const uint16_t *b, uint16_t *out, long long n) {
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (i + 8 <= n) {
+    const uint4 va = *reinterpret_cast<const uint4 *>(a + i), vb = *reinterpret_cast<const uint4 *>(b + i);
+    const uint32_t xa[4] = {va.x, va.y, va.z, va.w}, xb[4] = {vb.x, vb.y, vb.z, vb.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t lo = f32_to_bf16_rne(bf16_to_f32(xa[j] & 0xFFFFu) + bf16_to_f32(xb[j] & 0xFFFFu));
+      const uint32_t hi = f32_to_bf16_rne(bf16_to_f32(xa[j] >> 16) + bf16_to_f32(xb[j] >> 16));
+      o[j] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4 *>(out + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  } else {
+    for (long long j = i; j < n; ++j) out[j] = f32_to_bf16_rne(bf16_to_f32(a[j]) + bf16_to_f32(b[j]));
+  }
+}
+
+// out[r] = RTNE(s / sqrt(mean(s^2) + eps)), s = f32(a[r]) + f32(b[r]): the
+// residual add followed by an RMS normalisation without a learned scale, one
+// CTA per row.
+constexpr int kRmsThreads = 256;
+
+__global__ void __launch_bounds__(kRmsThreads) add_rms_bf16_kernel(const uint16_t *a, const uint16_t *b, uint16_t *out,
+                                                                   int n, float eps) {
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  __shared__ float part[kRmsThreads / 32];
+  const size_t base = (size_t)blockIdx.x * n;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = bf16_to_f32(a[base + i]) + bf16_to_f32(b[base + i]);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRmsThreads / 32; ++w) tot += part[w];
+  const float scale = rsqrtf(tot / (float)n + eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = bf16_to_f32(a[base + i]) + bf16_to_f32(b[base + i]);
+    out[base + i] = f32_to_bf16_rne(v * scale);
+  }
+}
+
+}  // namespace rc
+
+using namespace rc;
+
+extern "C" int rc_add_rms_bf16(rc_ctx *ctx, const uint16_t *a_dev, const uint16_t *b_dev, uint16_t *out_dev, int rows,
+                               int n, float eps, void *stream) {
+  RC_CHECK_ARG(ctx && a_dev && b_dev && out_dev && rows >= 1 && n >= 1, "rc_add_rms_bf16: bad argument");
+  RC_CUDA_TRY(cudaSetDevice(ctx->device));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows);
+  cfg.blockDim = dim3(kRmsThreads);
+  cfg.stream = pick_stream(ctx, stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, add_rms_bf16_kernel, a_dev, b_dev, out_dev, n, eps));
+  return RC_OK;
+}
+
+extern "C" int rc_add_bf16(rc_ctx *ctx, const uint16_t *a_dev, const uint16_t *b_dev, uint16_t *out_dev, long long n,
+                           void *stream) {
+  RC_CHECK_ARG(ctx && a_dev && b_dev && out_dev && n >= 0, "rc_add_bf16: bad argument");
+  RC_CHECK_ARG(((reinterpret_cast<uintptr_t>(a_dev) | reinterpret_cast<uintptr_t>(b_dev) |
+                 reinterpret_cast<uintptr_t>(out_dev)) & 15) == 0,
+               "rc_add_bf16: buffers must be 16-byte aligned");
+  if (n == 0) return RC_OK;
+  RC_CUDA_TRY(cudaSetDevice(ctx->device));
+  cudaLaunchConfig_t cfg = {};
+  const long long threads = (n + 7) / 8;
+  cfg.gridDim = dim3((unsigned)((threads + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = pick_stream(ctx, stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, add_bf16_kernel, a_dev, b_dev, out_dev, n));
+  return RC_OK;
+}

@@ -29,6 +29,7 @@ struct MoeScratch {
   int32_t *group_expert;   // [E+1]
   uint32_t *group_mask;    // [E+1] tokens of each group
   int32_t *group_dst;      // [E+1][16] slot row of (group, token)
+  int *err;                // the context's device error word
 };
 
 // What one rank computes: routed experts [lo, hi) for every token, the shared

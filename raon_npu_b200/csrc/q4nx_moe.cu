@@ -54,6 +54,7 @@ __device__ void build_groups(const int32_t *slot_expert, int T, int k, int n_exp
     const int t = pr / k, r = pr - t * k;
     const int e = __ldcg(slot_expert + t * (k + 1) + r);
     if (e >= own.lo && e < own.hi) atomicOr(smem_mask + e, 1u << t);
+    else if (e < 0 || e >= n_experts) atomicCAS(s.err, 0, kErrBadExpert);   // caller id out of range
   }
   __syncwarp();
   if (lane == 0) smem_mask[n_experts] = own.shared_mask;
@@ -219,10 +220,7 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
     const float v = val[i];
     const float *row = val + t * E;
     int ahead = 0;
-    for (int e2 = 0; e2 < E; ++e2) {
-      const float v2 = row[e2];
-      ahead += (v2 > v || (v2 == v && e2 < e0)) ? 1 : 0;
-    }
+    for (int e2 = 0; e2 < E; ++e2) ahead += route_before(row[e2], e2, v, e0) ? 1 : 0;
     rank[i] = ahead;
     if (ahead < k) sel[t * k + ahead] = e0;
   }
@@ -892,6 +890,7 @@ int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_sha
   if (e == cudaSuccess) e = cudaMalloc(&m->s.weights, T * K * 4);
   if (e == cudaSuccess) e = cudaMalloc(&m->s.slot_expert, T * (K + 1) * 4);
   if (e == cudaSuccess) e = cudaMalloc(&m->s.slot_w, T * K * 4);
+  m->s.err = ctx->err;
   if (e == cudaSuccess) e = cudaMalloc(&m->s.n_groups, 4);
   if (e == cudaSuccess) e = cudaMemset(m->s.n_groups, 0, 4);
   if (e == cudaSuccess) e = cudaMalloc(&m->s.group_expert, ne * 4);

@@ -217,25 +217,29 @@ __global__ void __launch_bounds__(256) pf_select_kernel(PfSelectParams p) {
   }
   int sel[kMoeMaxK];
   float sel_score[kMoeMaxK];
+  uint32_t live = 0u;                 // bit i: expert lane + 32 i still selectable
+#pragma unroll
+  for (int i = 0; i < kPer; ++i)
+    if (lane + 32 * i < p.E) live |= 1u << i;
 #pragma unroll 1
   for (int r = 0; r < p.k; ++r) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
+    float bv = 0.f;
+    int bi = -1;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const int ei = lane + 32 * i;
-      if (ei < p.E && (val[i] > bv || (val[i] == bv && ei < bi))) bv = val[i], bi = ei;
+      if (((live >> i) & 1u) && (bi < 0 || route_before(val[i], ei, bv, bi))) bv = val[i], bi = ei;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+      if (oi >= 0 && (bi < 0 || route_before(ov, oi, bv, bi))) bv = ov, bi = oi;
     }
     float sc = 0.f;
 #pragma unroll
     for (int i = 0; i < kPer; ++i)
-      if (lane + 32 * i == bi) sc = score[i], val[i] = -INFINITY;
+      if (lane + 32 * i == bi) sc = score[i], live &= ~(1u << i);
     sc = __shfl_sync(0xffffffffu, sc, bi & 31);
     if (lane == 0) {
       sel[r] = bi;
@@ -296,6 +300,7 @@ struct PfPlanParams {
   int st0, st1;                 // tokens whose shared expert is computed here
   int32_t *slot_row, *row_token, *cnt, *off, *n_chunks, *chunk_expert, *chunk_row0, *chunk_n;
   int chunk_cap;
+  int *err;
 };
 
 // One CTA.  Permuted rows are ordered by expert, then token: the row of
@@ -318,7 +323,8 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(PfPlanParams p) {
   for (int i = tid; i < p.T * k1; i += blockDim.x) {
     const int t = i / k1, r = i - t * k1;
     const int e = p.slot_expert[i];
-    if (computed(t, r, e)) atomicOr(mask + (size_t)e * nw + (t >> 5), 1u << (t & 31));
+    if (r < p.k && (e < 0 || e >= p.E1 - 1)) atomicCAS(p.err, 0, kErrBadExpert);   // caller id out of range
+    else if (computed(t, r, e)) atomicOr(mask + (size_t)e * nw + (t >> 5), 1u << (t & 31));
   }
   __syncthreads();
   // per expert: exclusive prefix of popcounts over its words (one warp per expert)
@@ -369,7 +375,7 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(PfPlanParams p) {
     const int t = i / k1, r = i - t * k1;
     const int e = p.slot_expert[i];
     int row = -1;
-    if (computed(t, r, e)) {
+    if (!(r < p.k && (e < 0 || e >= p.E1 - 1)) && computed(t, r, e)) {
       const uint32_t m = mask[(size_t)e * nw + (t >> 5)];
       row = s_off[e] + (int)pre[(size_t)e * nw + (t >> 5)] + __popc(m & ((1u << (t & 31)) - 1u));
       p.row_token[row] = t;
@@ -664,13 +670,14 @@ __global__ void __launch_bounds__(kPfCombineThreads) pf_combine_kernel(const uin
   for (int s = 0; s < kMoeMaxK; ++s) {
     r[s] = make_uint4(0, 0, 0, 0);
     w[s] = 0.f;
-    if (s < k) {
+    if (s < k && sr[s] >= 0) {     // a slot without a row (bad caller id, flagged by the plan) adds nothing
       r[s] = __ldcg(reinterpret_cast<const uint4 *>(down + (size_t)sr[s] * hidden + (size_t)v * 8));
       w[s] = slot_w[(size_t)t * k + s];
     }
   }
-  const uint4 sh = with_shared ? __ldcg(reinterpret_cast<const uint4 *>(down + (size_t)sr[k] * hidden + (size_t)v * 8))
-                               : make_uint4(0, 0, 0, 0);
+  const uint4 sh = with_shared && sr[k] >= 0
+                       ? __ldcg(reinterpret_cast<const uint4 *>(down + (size_t)sr[k] * hidden + (size_t)v * 8))
+                       : make_uint4(0, 0, 0, 0);
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;
@@ -824,6 +831,7 @@ static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t
   pp.chunk_row0 = ps->chunk_row0;
   pp.chunk_n = ps->chunk_n;
   pp.chunk_cap = ps->chunk_cap;
+  pp.err = m->ctx->err;
   const int nw = (r.T + 31) / 32;
   const size_t plan_smem = (size_t)2 * pp.E1 * nw * 4;
   RC_CHECK_ARG(plan_smem <= (size_t)kPfPlanSmemMax, "prefill plan of %d tokens x %d experts exceeds shared memory",

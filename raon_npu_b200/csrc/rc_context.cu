@@ -82,6 +82,14 @@ int check_error_word(rc_ctx *ctx) {
       set_error("sampler: more than 2048 tokens tie at the top-k threshold (device error word 2)");
       return RC_ERR_INVALID;
     }
+    if (word == 4) {
+      set_error("MoE: an expert id outside 0..n_experts-1 reached the device (device error word 4)");
+      return RC_ERR_INVALID;
+    }
+    if (word == 3) {
+      set_error("sampler: the logits have no orderable value (NaN) (device error word 3)");
+      return RC_ERR_INVALID;
+    }
     set_error("a kernel gave up a bounded wait (device error word %d)", word);
     return RC_ERR_TIMEOUT;
   }

@@ -75,6 +75,15 @@ __device__ __forceinline__ bool mbar_wait_bounded_warp(uint32_t bar, uint32_t pa
   return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
 }
 
+// Router order: larger value first; NaN after every number; equal values (and
+// NaNs among themselves) by lower index -- the order of numpy's stable argsort
+// of the negated values, a strict total order even on NaN input.
+__device__ __forceinline__ bool route_before(float a, int ia, float b, int ib) {
+  const bool na = a != a, nb = b != b;
+  if (na || nb) return nb ? (!na || ia < ib) : false;
+  return a > b || (a == b && ia < ib);
+}
+
 // ---------------------------------------------------------- bulk copies --
 // L2 policy for data that is streamed exactly once (weights).
 __device__ __forceinline__ uint64_t policy_evict_first() {

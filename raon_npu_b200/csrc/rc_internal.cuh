@@ -51,6 +51,7 @@ constexpr int kXSlots = 4;
 
 // Device error words (ctx->err): first failure wins.
 constexpr int kErrWaitTimeout = 1;
+constexpr int kErrBadExpert = 4;       // an expert id outside 0..E-1 reached the device
 
 void set_error(const char *fmt, ...);
 

@@ -29,6 +29,7 @@ constexpr int kSampleMaxCand = 2048;
 constexpr int kSampleMaxVocab = 1 << 20;
 constexpr int kSampleMaxTopK = 1024;
 constexpr int kErrSampleCandidates = 2;    // device error word: too many tied candidates
+constexpr int kErrSampleNoCandidates = 3;  // device error word: no orderable score (NaN logits)
 
 struct SampleParams {
   const uint16_t *logits;    // [T][ld] bf16
@@ -150,9 +151,11 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
   }
   __syncthreads();
   const int n = s_count;
-  if (n > kSampleMaxCand) {
+  // n == 0 only when the scores are not ordered (NaN logits): report it
+  // instead of drawing from an empty list
+  if (n > kSampleMaxCand || n == 0) {
     if (tid == 0) {
-      atomicCAS(p.err, 0, kErrSampleCandidates);
+      atomicCAS(p.err, 0, n == 0 ? kErrSampleNoCandidates : kErrSampleCandidates);
       p.out[t] = -1;
     }
     return;
@@ -236,6 +239,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
     c_score[i] = total;                          // cumulative
   }
   const double u = p.u[t];
+  if (keep < 1) keep = 1;   // the top token always stays (n >= 1 here)
   int tok = c_idx[keep - 1];
   for (int i = 0; i < keep; ++i) {
     if (c_score[i] / total > u) {

@@ -107,6 +107,26 @@ def sample_tokens(ctx: "Context", logits_dev, u_dev, out_dev, top_k: int = 50, t
         ctypes.c_void_p(_stream_for(stream, logits_dev, out_dev))), "rc_sample_tokens")
 
 
+def add_bf16(ctx: "Context", a_dev, b_dev, out_dev, stream: int | None = None) -> None:
+    """out = RTNE(f32(a) + f32(b)) elementwise (bf16 bit tensors of equal size)."""
+    n = int(a_dev.numel())
+    if int(b_dev.numel()) != n or int(out_dev.numel()) != n:
+        raise ValueError("add_bf16: tensors must have the same number of elements")
+    check(ctx.lib.rc_add_bf16(ctx.handle, ctypes.c_void_p(_ptr(a_dev)), ctypes.c_void_p(_ptr(b_dev)),
+                              ctypes.c_void_p(_ptr(out_dev)), n, ctypes.c_void_p(_stream_for(stream, a_dev, out_dev))),
+          "rc_add_bf16")
+
+
+def add_rms_bf16(ctx: "Context", a_dev, b_dev, out_dev, eps: float = 1e-6, stream: int | None = None) -> None:
+    """out = RTNE((a + b) / rms(a + b)) per row of [rows, n] bf16 bit tensors."""
+    if a_dev.shape != b_dev.shape or a_dev.shape != out_dev.shape:
+        raise ValueError("add_rms_bf16: tensors must have the same shape")
+    rows, n = (1, int(a_dev.shape[0])) if a_dev.dim() == 1 else (int(a_dev.shape[0]), int(a_dev.shape[1]))
+    check(ctx.lib.rc_add_rms_bf16(ctx.handle, ctypes.c_void_p(_ptr(a_dev)), ctypes.c_void_p(_ptr(b_dev)),
+                                  ctypes.c_void_p(_ptr(out_dev)), rows, n, float(eps),
+                                  ctypes.c_void_p(_stream_for(stream, a_dev, out_dev))), "rc_add_rms_bf16")
+
+
 class Q4nxWeight:
     """A q4nx matrix resident in HBM in the GEMV tile layout."""
 

@@ -31,7 +31,9 @@ def test_library_exports_every_declared_symbol(lib):
 
 def test_library_has_no_torch_dependency():
     out = subprocess.run(["ldd", str(LIB)], capture_output=True, text=True).stdout
-    assert "torch" not in out and "c10" not in out
+    # library names only: the load addresses in ldd's output are random hex
+    names = [line.split()[0] for line in out.splitlines() if line.strip()]
+    assert not any("torch" in n or "c10" in n for n in names), names
 
 
 def test_abi_version_and_error_text(lib):

@@ -471,3 +471,70 @@ def test_experts_grouped_matches_oracle(torch, ctx):
         assert_bf16_outputs_close(got_r[t], r_ref[t], mag)
         assert rms_rel(got_s[t], s_ref[t]) <= 2.0 ** -8
     layer.close()
+
+
+# ------------------------------------------------------------- robustness --
+@pytest.mark.parametrize("T", [3, 40])
+def test_router_ranks_nan_logits_last(torch, ctx, T):
+    """Experts whose router row holds a NaN get NaN logits; like numpy's stable
+    argsort of the negated values they rank after every number, among
+    themselves by index (T = 3: decode router, T = 40: prefill router)."""
+    layer, wr, rng = _router_layer(ctx, 256, 64, seed=83)
+    wr = wr.copy()
+    for e in (0, 1, 5, 9, 33):
+        wr[e, 7] = 0x7FC0
+    layer.set_router(wr)
+    x = q.f32_to_bf16(rng.standard_normal((T, 256)).astype(np.float32))
+    x[T - 1] = 0x7FC0                       # a NaN token row: every logit NaN
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    k = 8
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    layer.route(xd, T, k, ids, w)
+    torch.cuda.synchronize()
+    ctx.sync()
+    for t in range(T):
+        ref = ob.topk_lower_index_wins(ob.router_logits(x[t], wr), k)
+        np.testing.assert_array_equal(ids[t].cpu().numpy(), ref)
+    np.testing.assert_array_equal(ids[T - 1].cpu().numpy(), np.arange(k))
+    layer.close()
+
+
+def test_caller_expert_id_out_of_range_is_an_error(torch, ctx):
+    """Device-side routes are not validated on the host: an out-of-range id
+    sets the device error word and the next synchronisation raises."""
+    d = cases.moe_inputs(**cases.MOE_CASE)
+    layer = make_layer(ctx, d)
+    xd = torch.from_numpy(d["x"][:2].view(np.int16)).cuda()
+    ids = torch.tensor([[0, 1, 2], [3, 99, 4]], dtype=torch.int32, device="cuda")
+    w = torch.full((2, 3), 0.3, dtype=torch.float32, device="cuda")
+    out = torch.empty((2, 256), dtype=torch.int16, device="cuda")
+    layer.experts(xd, ids, w, 3, out, act="situ")
+    torch.cuda.synchronize()
+    with pytest.raises(ValueError):
+        ctx.sync()
+    layer.prefill_experts(xd, ids, w, 3, out, act="situ")
+    torch.cuda.synchronize()
+    with pytest.raises(ValueError):
+        ctx.sync()
+    ctx.sync()                              # the word was reported and cleared
+    layer.close()
+
+
+def test_residual_add_kernels_match_numpy(torch, ctx):
+    from raon_npu_b200.device import add_bf16, add_rms_bf16
+    rng = np.random.default_rng(9)
+    a = q.f32_to_bf16(rng.standard_normal((3, 2048)).astype(np.float32))
+    b = q.f32_to_bf16((rng.standard_normal((3, 2048)) * 3).astype(np.float32))
+    ad, bd = (torch.from_numpy(v.view(np.int16)).cuda() for v in (a, b))
+    out = torch.empty_like(ad)
+    add_bf16(ctx, ad, bd, out)
+    torch.cuda.synchronize()
+    s = q.bf16_to_f32(a) + q.bf16_to_f32(b)
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint16), q.f32_to_bf16(s))
+    add_rms_bf16(ctx, ad, bd, out)
+    torch.cuda.synchronize()
+    ctx.sync()
+    ref = s / np.sqrt(np.mean(s.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6)
+    got = q.bf16_to_f32(out.cpu().numpy().view(np.uint16))
+    assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1e-3)) <= 2 ** -7

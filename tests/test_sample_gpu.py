@@ -106,3 +106,15 @@ def test_sampler_reports_too_many_ties(torch, ctx):
     with pytest.raises(ValueError):
         ctx.sync()
     assert int(out.item()) == -1
+
+
+def test_sampler_reports_nan_logits(torch, ctx):
+    from raon_npu_b200.device import sample_tokens
+    ld = torch.full((1, 3000), 0x7FC0, dtype=torch.int16, device="cuda")
+    u = torch.full((1,), 0.5, dtype=torch.float64, device="cuda")
+    out = torch.empty(1, dtype=torch.int32, device="cuda")
+    sample_tokens(ctx, ld, u, out, top_k=50, top_p=0.9)
+    torch.cuda.synchronize()
+    with pytest.raises(ValueError):
+        ctx.sync()
+    assert int(out.item()) == -1
