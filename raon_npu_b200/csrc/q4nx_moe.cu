@@ -34,58 +34,13 @@
 // byte for byte.
 #include <string.h>
 
+#include "moe_device.cuh"
 #include "moe_internal.cuh"
 #include "q4nx_core.cuh"
 #include "rc_device.cuh"
 #include "rc_internal.cuh"
 
 namespace rc {
-
-// ------------------------------------------------------------ grouping --
-// One warp.  Reads the slot lists of T tokens (written by other threads or
-// CTAs: the caller fences), builds the ascending-ID group table.  Scratch
-// smem_mask / smem_gidx hold E+1 entries.
-__device__ void build_groups(const int32_t *slot_expert, int T, int k, int n_experts, MoeOwned own,
-                             const MoeScratch &s, uint32_t *smem_mask, int *smem_gidx, int lane) {
-  const int ne = n_experts + 1;
-  for (int e = lane; e < ne; e += 32) smem_mask[e] = 0u;
-  __syncwarp();
-  for (int pr = lane; pr < T * k; pr += 32) {
-    const int t = pr / k, r = pr - t * k;
-    const int e = __ldcg(slot_expert + t * (k + 1) + r);
-    if (e >= own.lo && e < own.hi) atomicOr(smem_mask + e, 1u << t);
-    else if (e < 0 || e >= n_experts) atomicCAS(s.err, 0, kErrBadExpert);   // caller id out of range
-  }
-  __syncwarp();
-  if (lane == 0) smem_mask[n_experts] = own.shared_mask;
-  __syncwarp();
-  int base = 0;
-  for (int c = 0; c < ne; c += 32) {
-    const int e = c + lane;
-    const uint32_t m = e < ne ? smem_mask[e] : 0u;
-    const uint32_t b = __ballot_sync(0xffffffffu, m != 0u);
-    if (m) {
-      const int gi = base + __popc(b & ((1u << lane) - 1u));
-      s.group_expert[gi] = e;
-      s.group_mask[gi] = m;
-      smem_gidx[e] = gi;
-    }
-    base += __popc(b);
-  }
-  if (lane == 0) *s.n_groups = base;
-  __syncwarp();
-  for (int pr = lane; pr < T * (k + 1); pr += 32) {
-    const int t = pr / (k + 1), r = pr - t * (k + 1);
-    const int e = __ldcg(slot_expert + pr);
-    bool mine;
-    if (r < k) {
-      mine = e >= own.lo && e < own.hi;
-    } else {
-      mine = e >= 0 && ((own.shared_mask >> t) & 1u);
-    }
-    if (mine) s.group_dst[smem_gidx[e] * kMoeMaxTokens + t] = pr;
-  }
-}
 
 // ----------------------------------------------------------------- router --
 struct RouteParams {
@@ -100,85 +55,76 @@ struct RouteParams {
 };
 
 constexpr int kRouteThreads = 256;
-constexpr int kRouteExpertsPerCta = 8;   // one warp per expert
-constexpr int kRouteChunk = 2048;        // columns per pass: 8 x 16-byte loads per lane
+constexpr int kRouteSlice = 256;         // router columns per warp step: one 16-byte load per lane
 
-// Phase 1 (every CTA, one warp per expert, all T tokens): logits as f64 sums
-// of exact bf16 x bf16 products, rounded once to f32.  The expert's router row
-// is fetched before waiting on the previous launch (it does not depend on
-// it); token rows are staged in shared memory 2048 columns at a time, so
-// every global fetch is one round trip for all lanes.  Phase 2 (the last CTA
-// to arrive): one warp per token selects the top k; then warp 0 builds the
-// group table.
+// Phase 1 (CTA e = expert e, all T tokens): warp w takes the 256-column
+// slices w, w+8, ...; a lane multiplies 8 columns, so every f64 chain is
+// short.  The router row is fetched before waiting on the previous launch;
+// the sums are exact f64 sums of exact bf16 x bf16 products, rounded once to
+// f32.  Phase 2 (the last CTA to arrive, all threads): top-k by rank counting
+// in the router order (larger first, NaN last, ties by lower index), the
+// routing weights, the ascending-ID slot lists and the group table.
 __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p) {
-  extern __shared__ __align__(16) uint8_t route_smem[];   // x chunk [T][kRouteChunk] bf16
+  extern __shared__ __align__(16) uint8_t route_smem[];     // phase 2 arrays
+  __shared__ double red[kRouteThreads / 32][kMoeMaxTokens];
   __shared__ uint32_t smask[kMoeMaxExperts + 1];
   __shared__ int sgidx[kMoeMaxExperts + 1];
   __shared__ int is_last;
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * kRouteExpertsPerCta + warp;
-  const int T = p.tokens;
-  uint4 *xs = reinterpret_cast<uint4 *>(route_smem);
-  // row stride of the staged chunk, in 16-byte vectors: the launch allocates
-  // T * min(hidden, kRouteChunk) bf16
-  const int vs = (p.hidden < kRouteChunk ? p.hidden : kRouteChunk) / 8;
+  const int e = blockIdx.x, T = p.tokens;
+  const int nslice = p.hidden / kRouteSlice;
   double acc[kMoeMaxTokens];
 #pragma unroll
   for (int t = 0; t < kMoeMaxTokens; ++t) acc[t] = 0.0;
-  for (int c0 = 0; c0 < p.hidden; c0 += kRouteChunk) {
-    const int cols = p.hidden - c0 < kRouteChunk ? p.hidden - c0 : kRouteChunk;
-    const int v8 = cols / 8;                       // 16-byte vectors per row in this chunk
-    uint4 wv[kRouteChunk / 256];
-#pragma unroll
-    for (int i = 0; i < kRouteChunk / 256; ++i) {
-      const int v = i * 32 + lane;
-      wv[i] = make_uint4(0, 0, 0, 0);
-      if (e < p.n_experts && v < v8)
-        wv[i] = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + c0) + v);
+  bool waited = false;
+  for (int sl = warp; sl < nslice; sl += kRouteThreads / 32) {
+    const int col = sl * kRouteSlice + lane * 8;
+    const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
+    if (!waited) {
+      pdl_wait_prior();                            // token rows come from the previous launch
+      waited = true;
     }
-    if (c0 == 0) pdl_wait_prior();                 // token rows come from the previous launch
-    __syncthreads();                               // previous chunk fully consumed
-    for (int i = threadIdx.x; i < T * v8; i += blockDim.x) {
-      const int t = i / v8, v = i - t * v8;
-      xs[t * vs + v] = *(reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.ldx + c0) + v);
+    uint4 xv[kMoeMaxTokens];
+#pragma unroll
+    for (int t = 0; t < kMoeMaxTokens; ++t)
+      if (t < T) xv[t] = *reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.ldx + col);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    double wd[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      wd[2 * j] = (double)bf16_to_f32(ww[j] & 0xFFFFu);
+      wd[2 * j + 1] = (double)bf16_to_f32(ww[j] >> 16);
     }
-    __syncthreads();
-    if (e < p.n_experts) {
 #pragma unroll
-      for (int t = 0; t < kMoeMaxTokens; ++t) {
-        if (t < T) {
+    for (int t = 0; t < kMoeMaxTokens; ++t) {
+      if (t < T) {
+        const uint32_t xw[4] = {xv[t].x, xv[t].y, xv[t].z, xv[t].w};
 #pragma unroll
-          for (int i = 0; i < kRouteChunk / 256; ++i) {
-            const int v = i * 32 + lane;
-            if (v < v8) {
-              const uint4 xv = xs[t * vs + v];
-              const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-              const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                acc[t] = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), (double)bf16_to_f32(ww[j] & 0xFFFFu), acc[t]);
-                acc[t] = fma((double)bf16_to_f32(xw[j] >> 16), (double)bf16_to_f32(ww[j] >> 16), acc[t]);
-              }
-            }
-          }
+        for (int j = 0; j < 4; ++j) {
+          acc[t] = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), wd[2 * j], acc[t]);
+          acc[t] = fma((double)bf16_to_f32(xw[j] >> 16), wd[2 * j + 1], acc[t]);
         }
       }
     }
   }
-  if (e < p.n_experts) {
 #pragma unroll
-    for (int t = 0; t < kMoeMaxTokens; ++t) {
-      if (t < T) {
-        double a = acc[t];
+  for (int t = 0; t < kMoeMaxTokens; ++t) {
+    if (t < T) {
+      double a = acc[t];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) p.s.logits[(size_t)t * p.n_experts + e] = __double2float_rn(a);
-      }
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) red[warp][t] = a;
     }
   }
-  // one release per CTA: the barrier orders the warps' logit stores before
-  // thread 0's (cumulative) fence and arrival
+  __syncthreads();
+  if (threadIdx.x < T) {
+    double a = 0.0;
+    for (int w = 0; w < kRouteThreads / 32; ++w) a += red[w][threadIdx.x];
+    p.s.logits[(size_t)threadIdx.x * p.n_experts + e] = __double2float_rn(a);
+  }
+  // one release per CTA: the barrier orders the logit stores before thread
+  // 0's (cumulative) fence and arrival
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -192,15 +138,14 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
   __syncthreads();
   if (!is_last) return;
 
-  // ---- phase 2 (last CTA, all threads): top-k of every token by counting,
-  // for each expert, the experts ahead of it (larger value, or equal value and
-  // lower index); rank < k selects.
+  // ---- phase 2 (last CTA)
   const int E = p.n_experts, k = p.k;
   float *val = reinterpret_cast<float *>(route_smem);      // [T][E]
   float *score = val + T * E;                               // [T][E]
   int *rank = reinterpret_cast<int *>(score + T * E);       // [T][E]
   int *sel = rank + T * E;                                  // [T][k] expert of each rank
   float *selw = reinterpret_cast<float *>(sel + T * k);     // [T][k] weight of each rank
+  int32_t *slots = reinterpret_cast<int32_t *>(selw + T * k);   // [T][k+1] ascending slot lists
   for (int i = threadIdx.x; i < T * E; i += blockDim.x) {
     const float l = __ldcg(p.s.logits + i);
     float sc, v;
@@ -215,14 +160,30 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
     val[i] = v;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < T * E; i += blockDim.x) {
-    const int t = i / E, e0 = i - t * E;
-    const float v = val[i];
-    const float *row = val + t * E;
+  // rank of (t, e): experts ahead of it; P adjacent lanes split the count
+  int P = 1;
+  while (P < 32 && T * E * P * 2 <= kRouteThreads) P *= 2;
+  const int items = T * E * P;
+  for (int i0 = 0; i0 < items; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
     int ahead = 0;
-    for (int e2 = 0; e2 < E; ++e2) ahead += route_before(row[e2], e2, v, e0) ? 1 : 0;
-    rank[i] = ahead;
-    if (ahead < k) sel[t * k + ahead] = e0;
+    int te = -1;
+    if (i < items) {
+      te = i / P;
+      const int part = i - te * P;
+      const int t = te / E, e0 = te - t * E;
+      const float v = val[te];
+      const float *row = val + t * E;
+      const int per = (E + P - 1) / P;
+      const int lo = part * per, hi = lo + per < E ? lo + per : E;
+      for (int e2 = lo; e2 < hi; ++e2) ahead += route_before(row[e2], e2, v, e0) ? 1 : 0;
+    }
+    for (int o = 1; o < P; o <<= 1) ahead += __shfl_down_sync(0xffffffffu, ahead, o, P);
+    if (i < items && (i % P) == 0) {
+      rank[te] = ahead;
+      const int t = te / E;
+      if (ahead < k) sel[t * k + ahead] = te - t * E;
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < T * k; i += blockDim.x) {
@@ -258,15 +219,19 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
       const uint32_t b = __ballot_sync(0xffffffffu, rk < k);
       if (rk < k) {
         const int pos = base + __popc(b & ((1u << lane) - 1u));
+        slots[t * (k + 1) + pos] = e1;
         p.s.slot_expert[t * (k + 1) + pos] = e1;
         p.s.slot_w[t * k + pos] = selw[t * k + rk];
       }
       base += __popc(b);
     }
-    if (lane == 0) p.s.slot_expert[t * (k + 1) + k] = p.shared_id;
+    if (lane == 0) {
+      slots[t * (k + 1) + k] = p.shared_id;
+      p.s.slot_expert[t * (k + 1) + k] = p.shared_id;
+    }
   }
   __syncthreads();
-  if (warp == 0) build_groups(p.s.slot_expert, T, k, E, p.own, p.s, smask, sgidx, lane);
+  if (warp == 0) build_groups(slots, T, k, E, p.own, p.s, smask, sgidx, lane);
 }
 
 // Slot lists from caller-supplied top ids / weights [T][k] (the
@@ -793,10 +758,9 @@ static int moe_route(rc_moe *m, const uint16_t *x, int T, int k, int mode, int r
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess && (dev >= 64 || !configured[dev])) {
-    constexpr int kPhase1Max = kMoeMaxTokens * kRouteChunk * 2;
-    constexpr int kPhase2Max = kMoeMaxTokens * kMoeMaxExperts * 12 + kMoeMaxTokens * kMoeMaxK * 8;
-    e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kPhase1Max > kPhase2Max ? kPhase1Max : kPhase2Max);
+    constexpr int kPhase2Max = kMoeMaxTokens * kMoeMaxExperts * 12 + kMoeMaxTokens * kMoeMaxK * 8 +
+                               kMoeMaxTokens * (kMoeMaxK + 1) * 4;
+    e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPhase2Max);
     if (e == cudaSuccess && dev < 64) configured[dev] = true;
   }
   if (e != cudaSuccess) {
@@ -804,12 +768,8 @@ static int moe_route(rc_moe *m, const uint16_t *x, int T, int k, int mode, int r
     return RC_ERR_CUDA;
   }
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = small_cfg(dim3((m->n_experts + kRouteExpertsPerCta - 1) / kRouteExpertsPerCta),
-                                     dim3(kRouteThreads), s, attr);
-  const int chunk = m->hidden < kRouteChunk ? m->hidden : kRouteChunk;
-  const size_t phase1 = (size_t)T * chunk * 2;
-  const size_t phase2 = (size_t)T * m->n_experts * 12 + (size_t)T * k * 8;
-  const size_t need = phase1 > phase2 ? phase1 : phase2;
+  cudaLaunchConfig_t cfg = small_cfg(dim3(m->n_experts), dim3(kRouteThreads), s, attr);
+  const size_t need = (size_t)T * m->n_experts * 12 + (size_t)T * k * 8 + (size_t)T * (k + 1) * 4;
   cfg.dynamicSmemBytes = (need + 15) / 16 * 16;
   e = cudaLaunchKernelEx(&cfg, moe_route_kernel, r);
   if (e != cudaSuccess) {
