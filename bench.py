@@ -433,9 +433,12 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
     import torch.distributed as dist
     H, E, k, M = MOE["hidden"], MOE["experts"], MOE["k"], MOE["tokens_per_rank"]
     eb = moe_expert_bytes(H, MOE["inter"])
-    per_rank_layer = (E // world + 1) * eb
-    # rotate over distinct layers so a step never finds its experts in L2
-    n_layers = min(16, max(2, -(-3 * 126_000_000 // per_rank_layer)))
+    # expert bytes one rank streams per step: its share of the experts the
+    # world*M tokens select, plus the shared expert
+    touched = (min(world * M * k, E) // world + 1) * eb
+    # rotate over enough distinct layers (each with its own fixed tokens, so
+    # its own experts) that a layer's experts left L2 long before it returns
+    n_layers = min(24, max(2, -(-3 * 126_000_000 // touched)))
     eps = build_moe_layers(ctx, torch, dev, n_layers)
     gen = torch.Generator(device=dev)
     gen.manual_seed(4242 + rank)
@@ -550,8 +553,9 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
                    "experts": E, "shared_experts": 1, "top_k": k, "router": "softmax, renormalised top-k",
                    "act": "swiglu", "tokens_per_rank": M, "parallelism": f"ep{world}",
                    "experts_per_rank": E // world, "layers_rotated": n_layers,
-                   "l2": "each step uses the next of %d distinct layers (%.0f MB of packed experts per rank)"
-                         % (n_layers, n_layers * per_rank_layer / 1e6),
+                   "l2": "each step uses the next of %d distinct layers with fixed tokens: the %.1f MB of "
+                         "experts a step streams per rank come back after %.0f MB of other layers' experts "
+                         "(L2 126 MB)" % (n_layers, touched / 1e6, (n_layers - 1) * touched / 1e6),
                    "cuda_graph": bool(int(ok.item())), "graph_error": graph_err},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": None,

@@ -137,6 +137,12 @@ int rc_moe_set_expert(rc_moe *m, int expert, const uint8_t *gate_up, size_t gate
  * router, the per-expert correction bias f32 [n_experts] (or NULL). */
 int rc_moe_set_router(rc_moe *m, const uint16_t *router_w, const float *bias);
 
+/* Decode path of rc_moe_decode / rc_moe_decode_local: enable != 0 (the
+ * default) runs router, experts and combine as one persistent cooperative
+ * kernel when the shape fits it; 0 always uses the separate launches.  Both
+ * give the same bytes. */
+int rc_moe_set_fused(rc_moe *m, int enable);
+
 /* Router for T <= 4096 tokens x [T][hidden] (device): top-k ids (best first,
  * lower index wins ties) and weights, optional f32 logits [T][n_experts].
  * Replaces the host router ``RaonModel._route_token`` (host/raon.py:1224-1247)

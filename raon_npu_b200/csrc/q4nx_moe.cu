@@ -54,12 +54,13 @@ struct RouteParams {
   MoeOwned own;
 };
 
-constexpr int kRouteThreads = 256;
+constexpr int kRouteThreads = 512;       // 16 warps: the slice order of the fused decode kernel
 constexpr int kRouteSlice = 256;         // router columns per warp step: one 16-byte load per lane
 
 // Phase 1 (CTA e = expert e, all T tokens): warp w takes the 256-column
-// slices w, w+8, ...; a lane multiplies 8 columns, so every f64 chain is
-// short.  The router row is fetched before waiting on the previous launch;
+// slices w, w+16, ...; a lane multiplies 8 columns, so every f64 chain is
+// short; the warps' sums are added in warp order (the order of the fused
+// decode kernel, so both round the same f64 sum).  The router row is fetched before waiting on the previous launch;
 // the sums are exact f64 sums of exact bf16 x bf16 products, rounded once to
 // f32.  Phase 2 (the last CTA to arrive, all threads): top-k by rank counting
 // in the router order (larger first, NaN last, ties by lower index), the
@@ -832,6 +833,7 @@ int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_sha
   m->inter_pad = (inter + 255) / 256 * 256;
   m->n_experts = n_experts;
   m->has_shared = has_shared ? 1 : 0;
+  m->fused = 1;
   const int ne = n_experts + 1;
   m->gate_up = new rc_weight *[ne]();
   m->down = new rc_weight *[ne]();
@@ -895,6 +897,7 @@ int rc_moe_destroy(rc_moe *m) {
   cudaFree(m->s.group_dst);
   cudaFree(m->act);
   cudaFree(m->down_out);
+  cudaFree(m->fz_bar);
   delete m;
   return RC_OK;
 }
@@ -919,6 +922,12 @@ int rc_moe_set_expert(rc_moe *m, int expert, const uint8_t *gate_up, size_t gate
   m->down[expert] = dn;
   RC_CUDA_TRY(cudaMemcpy(m->gu_tiles + expert, &gu->tiles, sizeof(void *), cudaMemcpyHostToDevice));
   RC_CUDA_TRY(cudaMemcpy(m->dn_tiles + expert, &dn->tiles, sizeof(void *), cudaMemcpyHostToDevice));
+  return RC_OK;
+}
+
+int rc_moe_set_fused(rc_moe *m, int enable) {
+  RC_CHECK_ARG(m, "rc_moe_set_fused: NULL argument");
+  m->fused = enable ? 1 : 0;
   return RC_OK;
 }
 
@@ -1039,6 +1048,10 @@ int rc_moe_decode(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, in
   if (rc) return rc;
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   const cudaStream_t s = pick_stream(m->ctx, stream);
+  if ((reinterpret_cast<uintptr_t>(x_dev) & 15) == 0 && (reinterpret_cast<uintptr_t>(out_dev) & 15) == 0 &&
+      moe_fused_fits(m, T, k, own))
+    return moe_fused_decode(m, x_dev, T, k, router, renormalize, scaling, act, gate_beta, value_beta, own,
+                            m->down_out, 0, out_dev, ids_dev, w_dev, nullptr, s);
   rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, own, s);
   if (rc) return rc;
   rc = moe_run_experts(m, x_dev, T, k, own, act, gate_beta, value_beta, nullptr, m->down_out, false, s);
@@ -1073,6 +1086,9 @@ int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int rout
   // experts computed elsewhere are zeroed by the gate/up launch, so the
   // ranks' slot rows can be summed in the exchange (x + 0 = x exactly).
   RC_CHECK_ARG((reinterpret_cast<uintptr_t>(slot_out_dev) & 15) == 0, "slot_out must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(x_dev) & 15) == 0 && moe_fused_fits(m, T, k, own))
+    return moe_fused_decode(m, x_dev, T, k, router, renormalize, scaling, act, gate_beta, value_beta, own,
+                            slot_out_dev, 1, nullptr, nullptr, nullptr, slot_w_dev, s);
   MoeScratch sc = m->s;
   sc.slot_w = slot_w_dev;
   rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, own, s, &sc);

@@ -1,0 +1,807 @@
+// The MoE decode layer for T <= 16 tokens as one persistent kernel: one CTA
+// per SM (a cooperative launch, so every CTA is resident) runs the whole
+// layer, phase after phase, with grid-wide barriers between the phases that
+// exchange data through global memory:
+//
+//   1 logits     CTA c computes the logits of experts c, c + grid, ...
+//                (f64 sums of exact bf16 products, rounded once to f32);
+//                meanwhile the shared expert's weights are prefetched to L2
+//   -- barrier --
+//   2 selection  every CTA reads the T x E logits and repeats the selection
+//                in its own shared memory: one warp per token takes the k
+//                best experts in the router order (larger first, NaN last,
+//                ties by lower index) by k warp-wide arg-max rounds, then the
+//                weights, the ascending-ID slot lists and the group table --
+//                identical inputs give identical tables, so no barrier is
+//                needed after it
+//   3 gate/up    the CTA's contiguous range of (group, row tile) tiles, its
+//                bytes first prefetched to L2; units dealt to 16 warps,
+//                per-unit partials summed in k-block order (a tile's result
+//                never depends on the partition); GLU epilogue -> act rows
+//   -- barrier --
+//   4 down       the same partition over the down tiles; the act rows of the
+//                range's groups staged in shared memory; slot rows out
+//   -- barrier --
+//   5 combine    ascending-ID f32 sum (multiply then add, no FMA), RTNE, plus
+//                the shared row
+//
+// Every warp streams its units through one ring of bulk copies that runs on
+// from its gate/up units into its down units, so the down weights are in
+// flight while gate/up is still computing.  The arithmetic of each tile, of
+// the routing and of the combine is the one of the separate kernels in
+// q4nx_moe.cu, so the bytes are the same.  Every wait is bounded.
+#include "moe_internal.cuh"
+#include "q4nx_core.cuh"
+#include "rc_device.cuh"
+#include "rc_internal.cuh"
+
+namespace rc {
+
+constexpr int kFzWarps = 16;
+constexpr int kFzThreads = kFzWarps * 32;
+constexpr int kFzMaxStages = 4;
+constexpr int kFzChunks = kMoeMaxExperts / 32;        // router values a lane holds per token
+constexpr uint32_t kFzPrefetchChunk = 16 * 1024;     // bytes per L2 prefetch instruction
+constexpr uint32_t kFzPrefetchBudget = 192 * 1024;   // L2 prefetch per CTA at the start of gate/up
+
+struct MoeFusedParams {
+  // tokens and router
+  const uint16_t *x;                 // [T][hidden]
+  int T, hidden, n_experts, k, mode, renorm;
+  float scaling;
+  const uint16_t *wr;                // [E][hidden]
+  const float *bias;                 // [E]
+  int shared_id;
+  MoeOwned own;
+  float *logits;                     // [T][E] scratch
+  int32_t *ids_out;                  // [T][k] rank order (optional)
+  float *w_out;                      // [T][k] (optional)
+  float *slot_w_out;                 // [T][k] ascending-ID order (optional)
+  // experts
+  const uint8_t *const *gu_tiles;    // [E+1]
+  const uint8_t *const *dn_tiles;    // [E+1]
+  int inter, inter_pad;
+  uint16_t *act;                     // [E+1][16][inter_pad]
+  uint16_t *slot_rows;               // [T][k+1][hidden]
+  int zero_foreign;                  // zero the slot rows of experts computed elsewhere
+  uint16_t *out;                     // [T][hidden], null: no combine
+  int act_kind;
+  float gate_beta, value_beta;
+  // launch geometry
+  int stages, round_gu, round_dn;
+  // shared-memory layout (byte offsets)
+  int off_stage, off_part, off_tab, off_sel, off_red, off_bar;
+  unsigned long long *bar;           // grid-barrier arrival count (only grows)
+  int *err;
+};
+
+// what build_activations / compute_unit read
+struct FzStage {
+  const void *x;
+  int x_dtype, ldx, tokens, slots, x_vec, kb;
+};
+
+// Router order as an unsigned key: larger value -> larger key, -0 equal to
+// +0, NaN (1) below every number, 0 = no candidate.  Equal keys are ordered
+// by lower expert index, so (key, index) is the router order (route_before).
+__device__ __forceinline__ uint32_t route_key(float v) {
+  if (v != v) return 1u;
+  uint32_t b = __float_as_uint(v);
+  if (b == 0x80000000u) b = 0u;
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// The group table of the ascending-ID slot lists, built by the whole CTA
+// (the same table as build_groups): one group per expert of [own.lo, own.hi)
+// that some token chose, ascending, then the shared expert for the tokens of
+// own.shared_mask; per (group, token) the slot row t*(k+1) + position.
+// Scratch: mask_s / gidx_s [E+1], cnt_s [(E+32)/32].
+__device__ void fz_build_groups(const int32_t *slots, int T, int k, int E, MoeOwned own, int32_t *g_expert,
+                                uint32_t *g_mask, int32_t *g_dst, int *n_groups, uint32_t *mask_s, int *gidx_s,
+                                int *cnt_s, int *err) {
+  const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31;
+  for (int e = tid; e <= E; e += nth) mask_s[e] = e == E ? own.shared_mask : 0u;
+  __syncthreads();
+  for (int pr = tid; pr < T * k; pr += nth) {
+    const int t = pr / k, r = pr - t * k;
+    const int e = slots[t * (k + 1) + r];
+    if (e >= own.lo && e < own.hi) atomicOr(mask_s + e, 1u << t);
+    else if (e < 0 || e >= E) atomicCAS(err, 0, kErrBadExpert);
+  }
+  __syncthreads();
+  const int nchunks = (E + 1 + 31) / 32;      // <= 9 <= warps
+  uint32_t m = 0, b = 0;
+  const int e = warp * 32 + lane;
+  if (warp < nchunks) {
+    m = e <= E ? mask_s[e] : 0u;
+    b = __ballot_sync(0xffffffffu, m != 0u);
+    if (lane == 0) cnt_s[warp] = __popc(b);
+  }
+  __syncthreads();
+  if (warp < nchunks) {
+    int base = 0;
+    for (int c = 0; c < warp; ++c) base += cnt_s[c];
+    if (m) {
+      const int gi = base + __popc(b & ((1u << lane) - 1u));
+      g_expert[gi] = e;
+      g_mask[gi] = m;
+      gidx_s[e] = gi;
+    }
+    if (warp == nchunks - 1 && lane == 0) *n_groups = base + __popc(b);
+  }
+  __syncthreads();
+  for (int pr = tid; pr < T * (k + 1); pr += nth) {
+    const int t = pr / (k + 1), r = pr - t * (k + 1);
+    const int ex = slots[pr];
+    const bool mine = r < k ? (ex >= own.lo && ex < own.hi) : (ex >= 0 && ((own.shared_mask >> t) & 1u));
+    if (mine) g_dst[gidx_s[ex] * kMoeMaxTokens + t] = pr;
+  }
+  __syncthreads();
+}
+
+// All CTAs meet.  Arrival n (counted over the layer's lifetime) belongs to
+// barrier n / grid, which is complete when the count reaches the next
+// multiple of the grid.  The arrival releases the CTA's writes (ordered
+// before it by the CTA barrier), the acquiring load makes the other CTAs'
+// writes visible.  Bounded: false after 1 s (error word set), CTA-uniform.
+__device__ bool fz_grid_barrier(unsigned long long *bar, int *err, int *ok_s) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const unsigned long long old = atom_add_release_gpu(bar, 1ull);
+    const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
+    if (ld_acquire_gpu(bar) < target) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_gpu(bar) < target) {
+        if (global_timer_ns() - t0 > 1000000000ull) {
+          ok = 0;
+          atomicCAS(err, 0, kErrWaitTimeout);
+          break;
+        }
+      }
+    }
+    *ok_s = ok;
+  }
+  __syncthreads();
+  return *ok_s != 0;
+}
+
+// L2 prefetch of [base, base + bytes) by one warp, in chunks.
+__device__ __forceinline__ void fz_prefetch(const uint8_t *base, uint32_t bytes, int lane) {
+  for (uint32_t o = (uint32_t)lane * kFzPrefetchChunk; o < bytes; o += 32 * kFzPrefetchChunk) {
+    const uint32_t n = bytes - o < kFzPrefetchChunk ? bytes - o : kFzPrefetchChunk;
+    prefetch_l2_bulk(base + o, n);
+  }
+}
+
+// One warp: L2 prefetch of tiles [c0, c0 + n_tiles) of the group-major tile
+// list (the tiles of one group lie back to back, kb units each), up to
+// ``budget`` bytes; returns what is left of the budget.
+__device__ uint32_t fz_prefetch_tiles(const uint8_t *const *g_ptr, int c0, int n_tiles, int gt, int kb,
+                                      uint32_t budget, int lane) {
+  int tg = c0;
+  const int c1 = c0 + n_tiles;
+  while (tg < c1 && budget > 0) {
+    const int grp = tg / gt;
+    const int t_end = (grp + 1) * gt < c1 ? (grp + 1) * gt : c1;
+    const uint8_t *b = g_ptr[grp];
+    if (b) {
+      uint32_t bytes = (uint32_t)(t_end - tg) * kb * kUnitBytes;
+      if (bytes > budget) bytes = budget;
+      fz_prefetch(b + (size_t)(tg - grp * gt) * kb * kUnitBytes, bytes, lane);
+      budget -= bytes;
+    }
+    tg = t_end;
+  }
+  return budget;
+}
+
+// The warp's unit stream across both phases: ring index j < n_gu is gate/up
+// unit warp + 16 j of the CTA's gate/up range, j >= n_gu is down unit
+// warp + 16 (j - n_gu) of its down range.
+struct FzUnits {
+  const uint8_t *const *g_gu;        // [groups] tile base of each group (shared memory; null: not loaded)
+  const uint8_t *const *g_dn;
+  int c0_gu, n_gu, c0_dn;
+  FastDiv kb_gu, gt_gu, kb_dn, gt_dn;
+  int n_total;
+
+  __device__ const uint8_t *src(int warp, int j) const {
+    const bool gu = j < n_gu;
+    const uint32_t u = warp + kFzWarps * (gu ? j : j - n_gu);
+    const FastDiv kb = gu ? kb_gu : kb_dn, gt = gu ? gt_gu : gt_dn;
+    const uint32_t ti = fdiv(u, kb), kbi = u - ti * kb.d;
+    const uint32_t tg = (gu ? c0_gu : c0_dn) + ti;
+    const uint32_t grp = fdiv(tg, gt), tile = tg - grp * gt.d;
+    const uint8_t *b = (gu ? g_gu : g_dn)[grp];
+    return b ? b + ((size_t)tile * kb.d + kbi) * kUnitBytes : nullptr;
+  }
+};
+
+// Ring state of a warp: slot / phase of the next unit to consume, copies
+// issued (lane 0's count), units consumed.
+struct FzRing {
+  int slot, issued, consumed;
+  uint32_t phase;
+  bool failed;
+};
+
+__device__ __forceinline__ void fz_issue(const FzUnits &un, int warp, int j, int sl, uint32_t ring_s, uint32_t bar0,
+                                         uint64_t pol) {
+  const uint8_t *src = un.src(warp, j);
+  if (src) {
+    mbar_arrive_expect_tx(bar0 + 8 * sl, kUnitBytes);
+    bulk_copy_g2s(ring_s + sl * kUnitBytes, src, kUnitBytes, bar0 + 8 * sl, pol);
+  } else {
+    mbar_arrive_expect_tx(bar0 + 8 * sl, 0);     // nothing to fetch: complete the phase at once
+  }
+}
+
+enum FzEpi : int { kFzGlu = 0, kFzDown = 1 };
+
+// One phase (gate/up or down) of this CTA: tiles [c0, c0 + n_tiles) of the
+// group-major tile list, units u = warp + 16 jj, rounds of R whole tiles.
+// Each unit's contribution goes to its own shared-memory partial; after a
+// round's barrier one warp per tile sums the tile's partials in k-block order
+// and runs the epilogue, so a tile's result depends on the tile alone.
+// j0 is the ring index of the warp's first unit of this phase.
+template <int EPI, int NTB>
+__device__ void fz_phase(const MoeFusedParams &p, uint8_t *smem, const FzStage &st, const FzUnits &un,
+                         const uint8_t *const *g_ptr, const uint32_t *g_mask, const int *g_dst, int g_lo, int c0,
+                         int n_tiles, FastDiv gt, FastDiv kbd, int R, int j0, int n_w, FzRing &rg) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.stages;
+  const int kb = (int)kbd.d, k = kb * kUnitK;
+  uint8_t *ring = smem + warp * S * kUnitBytes;
+  const uint32_t ring_s = smem_addr(ring);
+  const uint32_t bar0 = smem_addr(smem + p.off_bar) + warp * S * 8;
+  const uint32_t *xs = reinterpret_cast<const uint32_t *>(smem + p.off_stage);
+  constexpr int kBlocks = EPI == kFzGlu ? NTB : NTB * kMoeMaxGroupsPerCta;
+  const float *gs = reinterpret_cast<const float *>(smem + p.off_stage + xfrag_bytes(kBlocks, k));
+  float4 *part = reinterpret_cast<float4 *>(smem + p.off_part);
+  const uint64_t pol = policy_evict_first();
+  const int n_units = n_tiles * kb;
+  const int U = R * kb;
+  const int n_rounds = (n_units + U - 1) / U;
+  int jj = 0;
+  const int g = lane >> 2, qd = lane & 3;
+  for (int r = 0; r < n_rounds; ++r) {
+    const int u_end = (r + 1) * U < n_units ? (r + 1) * U : n_units;
+    for (; jj < n_w && warp + kFzWarps * jj < u_end; ++jj) {
+      const uint32_t u = warp + kFzWarps * jj;
+      const uint32_t ti = fdiv(u, kbd), kbi = u - ti * kb;
+      const uint32_t grp = fdiv(c0 + ti, gt);
+      if (!rg.failed) {
+        if (mbar_wait_bounded_warp(bar0 + 8 * rg.slot, rg.phase)) {
+          rg.consumed = j0 + jj + 1;
+        } else {
+          if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+          rg.failed = true;
+        }
+      }
+      if (!rg.failed && g_ptr[grp] != nullptr) {
+        Acc<NTB> acc;
+        acc_zero(acc);
+        const int blk = EPI == kFzGlu ? 0 : ((int)grp - g_lo) * NTB;
+        compute_unit<NTB, true>(ring + rg.slot * kUnitBytes, xs + (size_t)blk * (k / 64) * 256,
+                                gs + (size_t)blk * kb * 64, st, kbi, lane, acc);
+        float4 *dst = part + (size_t)(u - r * U) * NTB * 32 + lane;
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb)
+          dst[tb * 32] = make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3]);
+      }
+      __syncwarp();
+      const int jn = j0 + jj + S;                   // the ring index this slot takes next
+      if (!rg.failed && lane == 0 && jn < un.n_total) {
+        fz_issue(un, warp, jn, rg.slot, ring_s, bar0, pol);
+        ++rg.issued;
+      }
+      if (++rg.slot == S) rg.slot = 0, rg.phase ^= 1u;
+    }
+    __syncthreads();
+    const int t_lo = r * R, t_hi = t_lo + R < n_tiles ? t_lo + R : n_tiles;
+    for (int ti = t_lo + warp; ti < t_hi; ti += kFzWarps) {
+      const uint32_t tg = c0 + ti;
+      const uint32_t grp = fdiv(tg, gt), tile = tg - grp * gt.d;
+      const bool live = g_ptr[grp] != nullptr;
+      Acc<NTB> acc;
+      acc_zero(acc);
+      const float4 *src = part + (size_t)(ti - t_lo) * kb * NTB * 32 + lane;
+      for (int kbi = 0; kbi < kb; ++kbi) {
+        float4 v[NTB];
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb) v[tb] = src[(kbi * NTB + tb) * 32];
+        acc_add(acc, v);
+      }
+      const uint32_t mask = g_mask[grp];
+#pragma unroll
+      for (int tb = 0; tb < NTB; ++tb) {
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2) {
+          const int t = tb * 8 + 2 * qd + e2;
+          if (t >= p.T || !((mask >> t) & 1u)) continue;
+          if (EPI == kFzGlu) {
+            float v = 0.f;
+            if (live) {
+              const float gate = bf16_round(acc.v[tb][e2]);
+              const float up = bf16_round(acc.v[tb][2 + e2]);
+              v = p.act_kind == RC_ACT_SITU ? act_situ(gate, up, p.gate_beta, p.value_beta) : act_swiglu(gate, up);
+            }
+            p.act[((size_t)grp * 8 * NTB + t) * p.inter_pad + tile * 8 + g] = f32_to_bf16_rne(v);
+          } else {
+            uint16_t *y = p.slot_rows + (size_t)g_dst[grp * kMoeMaxTokens + t] * p.hidden + tile * kUnitRows + g;
+            y[0] = live ? f32_to_bf16_rne(acc.v[tb][e2]) : (uint16_t)0;
+            y[8] = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : (uint16_t)0;
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <int NTB>
+__global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  int *ok_s = reinterpret_cast<int *>(smem + p.off_red + kFzWarps * kMoeMaxTokens * 8);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = p.T, E = p.n_experts, k = p.k;
+  const int gt_gu_i = p.inter / 8, kb_gu_i = p.hidden / kUnitK;
+  const int gt_dn_i = p.hidden / kUnitRows, kb_dn_i = p.inter_pad / kUnitK;
+
+  // the shared expert's weights are needed whatever the routing: start
+  // bringing this CTA's slice of them into L2 now
+  if (warp == kFzWarps - 1 && p.shared_id >= 0 && p.own.shared_mask) {
+    const uint8_t *sg = p.gu_tiles[p.shared_id], *sd = p.dn_tiles[p.shared_id];
+    const uint32_t gbytes = (uint32_t)gt_gu_i * kb_gu_i * kUnitBytes;
+    const uint32_t dbytes = (uint32_t)gt_dn_i * kb_dn_i * kUnitBytes;
+    const uint32_t gs = (gbytes / gridDim.x + 15) / 16 * 16, ds = (dbytes / gridDim.x + 15) / 16 * 16;
+    const uint32_t go = gs * blockIdx.x, dof = ds * blockIdx.x;
+    if (sg && go < gbytes) fz_prefetch(sg + go, gbytes - go < gs ? gbytes - go : gs, lane);
+    if (sd && dof < dbytes) fz_prefetch(sd + dof, dbytes - dof < ds ? dbytes - dof : ds, lane);
+  }
+
+  // per-expert tables kept in shared memory for the whole kernel
+  const uint8_t **all_gu = reinterpret_cast<const uint8_t **>(smem + p.off_tab);    // [E+1]
+  const uint8_t **all_dn = all_gu + (E + 1);                                         // [E+1]
+  const uint8_t **g_gu = all_dn + (E + 1);                                           // [E+1] per group
+  const uint8_t **g_dn = g_gu + (E + 1);                                             // [E+1]
+  float *bias_s = reinterpret_cast<float *>(g_dn + (E + 1));                        // [E+1]
+  int32_t *g_expert = reinterpret_cast<int32_t *>(bias_s + (E + 1));                // [E+1]
+  uint32_t *g_mask = reinterpret_cast<uint32_t *>(g_expert + (E + 1));              // [E+1]
+  int32_t *g_dst = reinterpret_cast<int32_t *>(g_mask + (E + 1));                   // [E+1][16]
+  int *n_groups_s = g_dst + (E + 1) * kMoeMaxTokens;
+  auto load_tables = [&](int first, int stride) {
+    for (int i = first; i <= E; i += stride) {
+      all_gu[i] = p.gu_tiles[i];
+      all_dn[i] = p.dn_tiles[i];
+      bias_s[i] = i < E ? p.bias[i] : 0.f;
+    }
+  };
+  const int nslice = p.hidden / 256;
+  const int busy = nslice < kFzWarps ? nslice : kFzWarps;   // warps with router columns
+  // warps without router columns fetch the tables while the others compute
+  if (busy < kFzWarps && warp >= busy) load_tables(tid - busy * 32, (kFzWarps - busy) * 32);
+
+  // ------------------------------------------------------------ 1 logits
+  {
+    double *red = reinterpret_cast<double *>(smem + p.off_red);     // [16 warps][16 tokens]
+    for (int e = blockIdx.x; e < E; e += gridDim.x) {
+      double acc[kMoeMaxTokens];
+#pragma unroll
+      for (int t = 0; t < kMoeMaxTokens; ++t) acc[t] = 0.0;
+      for (int sl = warp; sl < nslice; sl += kFzWarps) {
+        const int col = sl * 256 + lane * 8;
+        const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
+        uint4 xv[kMoeMaxTokens];
+#pragma unroll
+        for (int t = 0; t < kMoeMaxTokens; ++t)
+          if (t < T) xv[t] = *reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.hidden + col);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        double wd[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          wd[2 * j] = (double)bf16_to_f32(ww[j] & 0xFFFFu);
+          wd[2 * j + 1] = (double)bf16_to_f32(ww[j] >> 16);
+        }
+#pragma unroll
+        for (int t = 0; t < kMoeMaxTokens; ++t) {
+          if (t < T) {
+            const uint32_t xw[4] = {xv[t].x, xv[t].y, xv[t].z, xv[t].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              acc[t] = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), wd[2 * j], acc[t]);
+              acc[t] = fma((double)bf16_to_f32(xw[j] >> 16), wd[2 * j + 1], acc[t]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < kMoeMaxTokens; ++t) {
+        if (t < T) {
+          double a = acc[t];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+          if (lane == 0) red[warp * kMoeMaxTokens + t] = a;
+        }
+      }
+      __syncthreads();
+      if (tid < T) {
+        double a = 0.0;
+        for (int w = 0; w < kFzWarps; ++w) a += red[w * kMoeMaxTokens + tid];
+        p.logits[(size_t)tid * E + e] = __double2float_rn(a);
+      }
+      __syncthreads();
+    }
+  }
+  if (busy == kFzWarps) load_tables(tid, blockDim.x);
+  if (!fz_grid_barrier(p.bar, p.err, ok_s)) return;
+
+  // --------------------------------------------------------- 2 selection
+  int32_t *slots = reinterpret_cast<int32_t *>(smem + p.off_sel);                   // [T][k+1]
+  float *slot_w = reinterpret_cast<float *>(slots + T * (k + 1));                   // [T][k]
+  {
+    // selection scratch in the staging area
+    int32_t *sel_e = reinterpret_cast<int32_t *>(smem + p.off_stage);               // [T][k] rank order
+    float *sel_sc = reinterpret_cast<float *>(sel_e + T * k);                       // [T][k] their scores
+    uint32_t *mask_s = reinterpret_cast<uint32_t *>(sel_sc + T * k);                // [E+1]
+    int *gidx_s = reinterpret_cast<int *>(mask_s + (E + 1));                        // [E+1]
+    int *cnt_s = gidx_s + (E + 1);                                                  // [9]
+    if (warp < T) {
+      const int t = warp;
+      uint32_t key[kFzChunks];
+      float sc[kFzChunks];
+#pragma unroll
+      for (int c = 0; c < kFzChunks; ++c) {
+        const int e = c * 32 + lane;
+        key[c] = 0u;
+        sc[c] = 0.f;
+        if (e < E) {
+          const float l = __ldcg(p.logits + (size_t)t * E + e);
+          float v;
+          if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
+            sc[c] = __double2float_rn(1.0 / (1.0 + exp(-(double)l)));
+            v = sc[c] + bias_s[e];
+          } else {
+            sc[c] = l + bias_s[e];       // softmax of the biased logits (bias zero unless set)
+            v = sc[c];
+          }
+          key[c] = route_key(v);
+        }
+      }
+      // k rounds of arg-max over the experts not taken yet: the largest key,
+      // the lowest index among equal keys (a lane's chunks ascend, so its
+      // first best is its lowest)
+      uint32_t taken = 0;
+      for (int r = 0; r < k; ++r) {
+        uint32_t bk = 0u;
+        int be = 0x7FFFFFFF;
+        float bs = 0.f;
+#pragma unroll
+        for (int c = 0; c < kFzChunks; ++c) {
+          if (!((taken >> c) & 1u) && key[c] > bk) {
+            bk = key[c];
+            be = c * 32 + lane;
+            bs = sc[c];
+          }
+        }
+        const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+        const int emin = (int)__reduce_min_sync(0xffffffffu, bk == kmax ? (unsigned)be : 0x7FFFFFFFu);
+        const float ws = __shfl_sync(0xffffffffu, bs, emin & 31);
+        if ((emin & 31) == lane) taken |= 1u << (emin >> 5);
+        if (lane == 0) {
+          sel_e[t * k + r] = emin;
+          sel_sc[t * k + r] = ws;
+        }
+      }
+      __syncwarp();
+      if (lane < k) {
+        const int r = lane;
+        const float *ss = sel_sc + t * k;
+        float w;
+        if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
+          float sum = 0.f;
+          for (int r2 = 0; r2 < k; ++r2) sum += ss[r2];
+          w = ss[r];
+          if (p.renorm) w = w / (sum + 1e-20f);
+          w = w * p.scaling;
+        } else {
+          // softmax over all experts renormalised over the top-k equals the
+          // softmax of the selected scores (the full denominator cancels)
+          const float mx = ss[0];
+          float sum = 0.f;
+          for (int r2 = 0; r2 < k; ++r2) sum += expf(ss[r2] - mx);
+          w = expf(ss[r] - mx) / sum;
+        }
+        const int e = sel_e[t * k + r];
+        int pos = 0;
+        for (int r2 = 0; r2 < k; ++r2) pos += sel_e[t * k + r2] < e ? 1 : 0;
+        slots[t * (k + 1) + pos] = e;
+        slot_w[t * k + pos] = w;
+        if (blockIdx.x == 0) {
+          if (p.ids_out) p.ids_out[t * k + r] = e;
+          if (p.w_out) p.w_out[t * k + r] = w;
+          if (p.slot_w_out) p.slot_w_out[t * k + pos] = w;
+        }
+      }
+      if (lane == 0) slots[t * (k + 1) + k] = p.shared_id;
+    }
+    __syncthreads();
+    fz_build_groups(slots, T, k, E, p.own, g_expert, g_mask, g_dst, n_groups_s, mask_s, gidx_s, cnt_s, p.err);
+    for (int i = tid; i < *n_groups_s; i += blockDim.x) {
+      g_gu[i] = all_gu[g_expert[i]];
+      g_dn[i] = all_dn[g_expert[i]];
+    }
+    __syncthreads();
+  }
+
+  // ------------------------------------------------- partitions and ring
+  const int ng = *n_groups_s;
+  const int tot_gu = ng * gt_gu_i, tot_dn = ng * gt_dn_i;
+  const int per_gu = (tot_gu + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int per_dn = (tot_dn + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int c0_gu = blockIdx.x * per_gu, c0_dn = blockIdx.x * per_dn;
+  const int nt_gu = c0_gu < tot_gu ? (c0_gu + per_gu < tot_gu ? per_gu : tot_gu - c0_gu) : 0;
+  const int nt_dn = c0_dn < tot_dn ? (c0_dn + per_dn < tot_dn ? per_dn : tot_dn - c0_dn) : 0;
+  const int nu_gu = nt_gu * kb_gu_i, nu_dn = nt_dn * kb_dn_i;
+  const int nw_gu = warp < nu_gu ? (nu_gu - 1 - warp) / kFzWarps + 1 : 0;
+  const int nw_dn = warp < nu_dn ? (nu_dn - 1 - warp) / kFzWarps + 1 : 0;
+  const FastDiv fkb_gu = make_fastdiv(kb_gu_i), fgt_gu = make_fastdiv(gt_gu_i);
+  const FastDiv fkb_dn = make_fastdiv(kb_dn_i), fgt_dn = make_fastdiv(gt_dn_i);
+  const int S = p.stages;
+  const uint32_t bar0 = smem_addr(smem + p.off_bar) + warp * S * 8;
+  const FzUnits un{g_gu, g_dn, c0_gu, nw_gu, c0_dn, fkb_gu, fgt_gu, fkb_dn, fgt_dn, nw_gu + nw_dn};
+  FzRing rg{0, 0, 0, 0u, false};
+  if (lane == 0 && un.n_total > 0) {
+    const uint32_t ring_s = smem_addr(smem + warp * S * kUnitBytes);
+    const uint64_t pol = policy_evict_first();
+    for (int sl = 0; sl < S; ++sl) mbar_init(bar0 + 8 * sl, 1);
+    mbar_fence_init();
+    for (int j = 0; j < un.n_total && j < S; ++j) {
+      fz_issue(un, warp, j, j, ring_s, bar0, pol);
+      ++rg.issued;
+    }
+  }
+  // the rest of the CTA's weights: L2 prefetch, gate/up first, then down
+  if (warp == kFzWarps - 1) {
+    const uint32_t left = fz_prefetch_tiles(g_gu, c0_gu, nt_gu, gt_gu_i, kb_gu_i, kFzPrefetchBudget, lane);
+    fz_prefetch_tiles(g_dn, c0_dn, nt_dn, gt_dn_i, kb_dn_i, left, lane);
+  }
+  // expert parallelism: zero the slot rows other ranks compute
+  if (p.zero_foreign) {
+    const int rows = T * (k + 1);
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+      const int t = r / (k + 1), pos = r - t * (k + 1);
+      const int e = slots[r];
+      const bool mine = pos < k ? (e >= p.own.lo && e < p.own.hi) : (e >= 0 && ((p.own.shared_mask >> t) & 1u));
+      if (mine) continue;
+      uint4 *dst = reinterpret_cast<uint4 *>(p.slot_rows + (size_t)r * p.hidden);
+      for (int i = tid; i < p.hidden / 8; i += blockDim.x) dst[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  // ------------------------------------------------------------ 3 gate/up
+  FzStage sx{p.x, RC_DTYPE_BF16, p.hidden, T, T, 1, kb_gu_i};
+  build_activations<true>(sx, NTB, reinterpret_cast<uint32_t *>(smem + p.off_stage),
+                          reinterpret_cast<float *>(smem + p.off_stage + xfrag_bytes(NTB, p.hidden)), tid,
+                          blockDim.x);
+  __syncthreads();
+  fz_phase<kFzGlu, NTB>(p, smem, sx, un, g_gu, g_mask, g_dst, 0, c0_gu, nt_gu, fgt_gu, fkb_gu, p.round_gu, 0, nw_gu,
+                        rg);
+  bool failed = __syncthreads_or(rg.failed) != 0;
+  if (!failed && !fz_grid_barrier(p.bar, p.err, ok_s)) failed = true;
+
+  // --------------------------------------------------------------- 4 down
+  if (!failed) {
+    const int g_lo = c0_dn / gt_dn_i;
+    const int g_hi = nt_dn ? (c0_dn + nt_dn - 1) / gt_dn_i : g_lo - 1;
+    FzStage sa{p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, RC_DTYPE_BF16, p.inter_pad,
+               (g_hi - g_lo + 1) * 8 * NTB, (g_hi - g_lo + 1) * 8 * NTB, 1, kb_dn_i};
+    build_activations<true>(sa, NTB * kMoeMaxGroupsPerCta, reinterpret_cast<uint32_t *>(smem + p.off_stage),
+                            reinterpret_cast<float *>(smem + p.off_stage +
+                                                      xfrag_bytes(NTB * kMoeMaxGroupsPerCta, p.inter_pad)),
+                            tid, blockDim.x);
+    __syncthreads();
+    fz_phase<kFzDown, NTB>(p, smem, sa, un, g_dn, g_mask, g_dst, g_lo, c0_dn, nt_dn, fgt_dn, fkb_dn, p.round_dn,
+                           nw_gu, nw_dn, rg);
+    failed = __syncthreads_or(rg.failed) != 0;
+  }
+  if (!failed && !fz_grid_barrier(p.bar, p.err, ok_s)) failed = true;
+
+  // ------------------------------------------------------------ 5 combine
+  if (!failed && p.out) {
+    const int vecs = p.hidden / 8;
+    const bool with_shared = p.shared_id >= 0 && p.own.shared_mask;
+    for (int i = blockIdx.x * blockDim.x + tid; i < T * vecs; i += gridDim.x * blockDim.x) {
+      const int t = i / vecs, v = i - t * vecs;
+      const uint16_t *rows = p.slot_rows + (size_t)t * (k + 1) * p.hidden + (size_t)v * 8;
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int s = 0; s < k; ++s) {
+        const uint4 r = __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)s * p.hidden));
+        const float w = slot_w[t * k + s];
+        const uint32_t q[4] = {r.x, r.y, r.z, r.w};
+        // product rounded, then sum rounded (no fused multiply-add)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(bf16_to_f32(q[j] & 0xFFFFu), w));
+          acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(bf16_to_f32(q[j] >> 16), w));
+        }
+      }
+      const uint4 sh = with_shared ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)k * p.hidden))
+                                   : make_uint4(0, 0, 0, 0);
+      const uint32_t shw[4] = {sh.x, sh.y, sh.z, sh.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t lo = f32_to_bf16_rne(acc[2 * j]), hi = f32_to_bf16_rne(acc[2 * j + 1]);
+        if (with_shared) {
+          lo = f32_to_bf16_rne(bf16_to_f32(lo) + bf16_to_f32(shw[j] & 0xFFFFu));
+          hi = f32_to_bf16_rne(bf16_to_f32(hi) + bf16_to_f32(shw[j] >> 16));
+        }
+        o[j] = lo | (hi << 16);
+      }
+      *reinterpret_cast<uint4 *>(p.out + (size_t)t * p.hidden + (size_t)v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  // after a failure, the copies still in flight land before the CTA's shared
+  // memory is released (ring indices consumed .. issued-1)
+  if (failed && lane == 0) {
+    for (int j = rg.consumed; j < rg.issued; ++j) mbar_wait_bounded(bar0 + 8 * (j % S), (uint32_t)(j / S) & 1u);
+  }
+}
+
+// ------------------------------------------------------------------- host --
+struct FzLayout {
+  int stages, round_gu, round_dn, off_stage, off_part, off_tab, off_sel, off_red, off_bar, smem;
+};
+
+static bool fz_layout(int ntb, int hidden, int inter_pad, int E, int T, int k, FzLayout *L) {
+  const int kb_gu = hidden / kUnitK, kb_dn = inter_pad / kUnitK;
+  const size_t st_x = xfrag_bytes(ntb, hidden) + gsum_bytes(ntb, hidden);
+  const size_t st_a = xfrag_bytes(ntb * kMoeMaxGroupsPerCta, inter_pad) + gsum_bytes(ntb * kMoeMaxGroupsPerCta,
+                                                                                     inter_pad);
+  const size_t st_sel = (size_t)T * k * 8 + (size_t)(E + 1) * 8 + 64;   // selection scratch
+  size_t stage = st_x > st_a ? st_x : st_a;
+  if (st_sel > stage) stage = st_sel;
+  const size_t tab = (size_t)(E + 1) * (4 * 8 + 4 + 4 + 4 + 4 * kMoeMaxTokens) + 16;   // expert and group tables
+  const size_t sel = (size_t)T * (k + 1) * 4 + (size_t)T * k * 4;
+  const size_t red = (size_t)kFzWarps * kMoeMaxTokens * 8 + 16;   // + the barrier verdict word
+  const int unit_part = ntb * 32 * 16;
+  for (int cap = kMoePartialBytes; cap >= 8 * 1024; cap /= 2) {
+    const int R_gu = cap / (kb_gu * unit_part), R_dn = cap / (kb_dn * unit_part);
+    if (R_gu < 1 || R_dn < 1) continue;
+    const size_t part = (size_t)(R_gu * kb_gu > R_dn * kb_dn ? R_gu * kb_gu : R_dn * kb_dn) * unit_part;
+    for (int S = kFzMaxStages; S >= 2; --S) {
+      size_t off = (size_t)kFzWarps * S * kUnitBytes;
+      const size_t o_stage = off;
+      off += (stage + 15) / 16 * 16;
+      const size_t o_part = off;
+      off += part;
+      const size_t o_tab = off;
+      off += (tab + 15) / 16 * 16;
+      const size_t o_sel = off;
+      off += (sel + 15) / 16 * 16;
+      const size_t o_red = off;
+      off += red;
+      const size_t o_bar = off;
+      off += (size_t)kFzWarps * S * 8;
+      if (off <= (size_t)kGemvSmemLimit) {
+        *L = FzLayout{S, R_gu, R_dn, (int)o_stage, (int)o_part, (int)o_tab, (int)o_sel, (int)o_red, (int)o_bar,
+                      (int)off};
+        return true;
+      }
+    }
+  }
+  return false;
+}
+
+
+// Whether the fused kernel takes this call: the shared-memory layout fits and
+// a CTA's down range touches at most kMoeMaxGroupsPerCta groups.
+bool moe_fused_fits(const rc_moe *m, int T, int k, const MoeOwned &own) {
+  if (!m->fused) return false;
+  FzLayout L;
+  if (!fz_layout(T <= 8 ? 1 : 2, m->hidden, m->inter_pad, m->n_experts, T, k, &L)) return false;
+  const int owned = own.hi - own.lo;
+  const int max_groups = (T * k < owned ? T * k : owned) + (own.shared_mask ? 1 : 0);
+  const int gt_dn = m->hidden / kUnitRows;
+  const int per_dn = (max_groups * gt_dn + m->ctx->sm_count - 1) / m->ctx->sm_count;
+  return per_dn - 1 <= (kMoeMaxGroupsPerCta - 1) * gt_dn;
+}
+
+// Runs the layer (out != null: combined rows into out) or its
+// expert-parallel local half (out == null: slot rows, zeroed where another
+// rank computes them, and the slot weights).  The caller checked
+// moe_fused_fits.
+int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling, int act,
+                     float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign, uint16_t *out,
+                     int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s) {
+  const int ntb = T <= 8 ? 1 : 2;
+  FzLayout L;
+  if (!fz_layout(ntb, m->hidden, m->inter_pad, m->n_experts, T, k, &L)) {
+    set_error("fused MoE decode: no shared-memory layout for T=%d k=%d", T, k);
+    return RC_ERR_INVALID;
+  }
+  rc_ctx *ctx = m->ctx;
+  if (!m->fz_bar) {
+    RC_CUDA_TRY(cudaMalloc(&m->fz_bar, sizeof(unsigned long long)));
+    RC_CUDA_TRY(cudaMemset(m->fz_bar, 0, sizeof(unsigned long long)));
+    m->fz_epoch = ctx->timeout_epoch;
+  }
+  if (m->fz_epoch != ctx->timeout_epoch) {
+    // a bounded wait gave up since the last launch: the arrival count may be
+    // left over from that launch
+    RC_CUDA_TRY(cudaMemsetAsync(m->fz_bar, 0, sizeof(unsigned long long), s));
+    m->fz_epoch = ctx->timeout_epoch;
+  }
+  MoeFusedParams p{};
+  p.x = x;
+  p.T = T;
+  p.hidden = m->hidden;
+  p.n_experts = m->n_experts;
+  p.k = k;
+  p.mode = router;
+  p.renorm = renorm;
+  p.scaling = scaling;
+  p.wr = m->router_w;
+  p.bias = m->router_bias;
+  p.shared_id = m->has_shared ? m->n_experts : -1;
+  p.own = own;
+  p.logits = m->s.logits;
+  p.ids_out = ids_out;
+  p.w_out = w_out;
+  p.slot_w_out = slot_w_out;
+  p.gu_tiles = m->gu_tiles;
+  p.dn_tiles = m->dn_tiles;
+  p.inter = m->inter;
+  p.inter_pad = m->inter_pad;
+  p.act = m->act;
+  p.slot_rows = slot_rows;
+  p.zero_foreign = zero_foreign;
+  p.out = out;
+  p.act_kind = act;
+  p.gate_beta = gb;
+  p.value_beta = vb;
+  p.stages = L.stages;
+  p.round_gu = L.round_gu;
+  p.round_dn = L.round_dn;
+  p.off_stage = L.off_stage;
+  p.off_part = L.off_part;
+  p.off_tab = L.off_tab;
+  p.off_sel = L.off_sel;
+  p.off_red = L.off_red;
+  p.off_bar = L.off_bar;
+  p.bar = m->fz_bar;
+  p.err = ctx->err;
+  static bool configured[64][2] = {};
+  int dev = 0;
+  RC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 64 || !configured[dev][ntb - 1]) {
+    if (ntb == 1)
+      RC_CUDA_TRY(cudaFuncSetAttribute(moe_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kGemvSmemLimit));
+    else
+      RC_CUDA_TRY(cudaFuncSetAttribute(moe_fused_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kGemvSmemLimit));
+    if (dev < 64) configured[dev][ntb - 1] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctx->sm_count);
+  cfg.blockDim = dim3(kFzThreads);
+  cfg.dynamicSmemBytes = L.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;      // every CTA resident: the grid barriers are safe
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (ntb == 1)
+    RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_fused_kernel<1>, p));
+  else
+    RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_fused_kernel<2>, p));
+  return RC_OK;
+}
+
+}  // namespace rc

@@ -90,6 +90,7 @@ int check_error_word(rc_ctx *ctx) {
       set_error("sampler: the logits have no orderable value (NaN) (device error word 3)");
       return RC_ERR_INVALID;
     }
+    ++ctx->timeout_epoch;
     set_error("a kernel gave up a bounded wait (device error word %d)", word);
     return RC_ERR_TIMEOUT;
   }

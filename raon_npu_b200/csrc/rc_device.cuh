@@ -104,6 +104,35 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void *src, uin
       : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (no completion to wait for).
+// src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// ------------------------------------------------- grid-scope atomics --
+__device__ __forceinline__ unsigned long long atom_add_release_gpu(unsigned long long *p, unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.add.release.gpu.global.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Division by a divisor fixed for a loop: q = umulhi(n, ceil(2^32 / d)),
+// exact while n * d < 2^32 (the callers' tile and unit indices stay below
+// 2^20 and their divisors below 2^12).
+struct FastDiv {
+  uint32_t d, m;
+};
+__host__ __device__ __forceinline__ FastDiv make_fastdiv(uint32_t d) {
+  return FastDiv{d, d <= 1 ? 0u : 0xFFFFFFFFu / d + 1u};
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, FastDiv f) { return f.d <= 1 ? n : __umulhi(n, f.m); }
+
 // ------------------------------------------- programmatic dependent launch --
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

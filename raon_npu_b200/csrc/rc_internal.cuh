@@ -97,6 +97,7 @@ struct rc_ctx {
   int *counters;        // [tiles], all zero between launches
   size_t counters_cap;
   int *err;             // device error word
+  unsigned timeout_epoch;   // bumped whenever a bounded device wait is found to have given up
   int *qflag;           // quantiser status word (non-finite input / overflow)
   // Host staging for rc_gemv_host.
   void *pin_x, *pin_y;

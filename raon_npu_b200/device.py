@@ -310,6 +310,11 @@ class MoeLayer:
                                              ctypes.c_void_p(None if b is None else b.ctypes.data)),
               "rc_moe_set_router")
 
+    def set_fused(self, enable: bool) -> None:
+        """Decode through one persistent kernel (default) or separate launches;
+        both give the same bytes."""
+        check(self.ctx.lib.rc_moe_set_fused(self.handle, int(bool(enable))), "rc_moe_set_fused")
+
     def route(self, x_dev, tokens: int, k: int, ids_dev, w_dev, logits_dev=None, router: str = "softmax",
               renormalize: bool = True, scaling: float = 1.0, stream: int | None = None) -> None:
         check(self.ctx.lib.rc_moe_route(

@@ -242,10 +242,13 @@ def _config3_layer(torch, ctx, n_experts=128, hidden=2048, inter=768, seed=91, o
         gen.manual_seed(seed * 1000 + e)
         gu = torch.randn((2 * inter, hidden), generator=gen, device="cuda") * 0.02
         dn = torch.randn((hidden, inter), generator=gen, device="cuda") * 0.02
+        ip = (inter + 255) // 256 * 256          # down K zero-padded to the 256-column tile
+        if ip != inter:
+            dn = torch.nn.functional.pad(dn, (0, ip - inter))
         pgu = torch.empty(2 * inter * hidden * 5 // 8, dtype=torch.uint8, device="cuda")
-        pdn = torch.empty(hidden * inter * 5 // 8, dtype=torch.uint8, device="cuda")
+        pdn = torch.empty(hidden * ip * 5 // 8, dtype=torch.uint8, device="cuda")
         ctx.quantize_q4nx(gu, pgu, 2 * inter, hidden)
-        ctx.quantize_q4nx(dn, pdn, hidden, inter)
+        ctx.quantize_q4nx(dn, pdn, hidden, ip)
         packed[e] = (pgu, pdn)
         if owned is None or e in owned:
             layer.set_expert(e, pgu, pdn)
@@ -258,7 +261,8 @@ def _config3_layer(torch, ctx, n_experts=128, hidden=2048, inter=768, seed=91, o
 def _oracle_expert(packed, e, hidden, inter):
     pgu, pdn = (t.cpu().numpy() for t in packed[e])
     fgu = q.dequantize_packed(pgu, 2 * inter, hidden)
-    return fgu[:inter], fgu[inter:], q.dequantize_packed(pdn, hidden, inter)
+    ip = (inter + 255) // 256 * 256
+    return fgu[:inter], fgu[inter:], q.dequantize_packed(pdn, hidden, ip)[:, :inter]
 
 
 def test_moe_decode_layer_config3(torch, ctx):
@@ -538,3 +542,90 @@ def test_residual_add_kernels_match_numpy(torch, ctx):
     ref = s / np.sqrt(np.mean(s.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6)
     got = q.bf16_to_f32(out.cpu().numpy().view(np.uint16))
     assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1e-3)) <= 2 ** -7
+
+
+# ------------------------------------------------ fused decode kernel --
+def _decode_both_paths(torch, layer, xd, k, **kw):
+    """(out, ids, w) of rc_moe_decode through the fused kernel and through the
+    separate launches."""
+    T = xd.shape[0]
+    res = []
+    for fused in (True, False):
+        layer.set_fused(fused)
+        out = torch.full((T, layer.hidden), 0x7FC0, dtype=torch.int16, device="cuda")
+        ids = torch.full((T, k), -7, dtype=torch.int32, device="cuda")
+        w = torch.full((T, k), float("nan"), dtype=torch.float32, device="cuda")
+        layer.decode(xd, k, out, ids, w, **kw)
+        torch.cuda.synchronize()
+        res.append((out, ids, w))
+    layer.set_fused(True)
+    return res
+
+
+@pytest.mark.parametrize("T", [1, 3, 8, 9, 16])
+@pytest.mark.parametrize("router", ["softmax", "sigmoid_bias"])
+def test_fused_decode_equals_separate_launches(torch, ctx, T, router):
+    """The persistent fused decode kernel (router, gate/up, down, combine in one
+    cooperative launch) gives exactly the bytes of the separate launches:
+    outputs, top-k ids and weights, for 1..16 tokens and both routers."""
+    layer, wr, _ = _config3_layer(torch, ctx)
+    if router == "sigmoid_bias":
+        rng_b = np.random.default_rng(31)
+        layer.set_router(wr, (rng_b.standard_normal(128) * 0.01).astype(np.float32))
+    rng = np.random.default_rng(200 + T)
+    x = q.f32_to_bf16(rng.standard_normal((T, 2048)).astype(np.float32))
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    kw = dict(act="swiglu", router=router)
+    if router == "sigmoid_bias":
+        kw.update(renormalize=True, scaling=2.5)
+    (fo, fi, fw), (so, si, sw) = _decode_both_paths(torch, layer, xd, 8, **kw)
+    ctx.sync()
+    assert torch.equal(fi, si)
+    assert torch.equal(fw, sw)
+    assert torch.equal(fo, so)
+    layer.close()
+
+
+@pytest.mark.parametrize("ranks,M", [(2, 1), (4, 4)])
+def test_fused_decode_local_equals_separate_launches(torch, ctx, ranks, M):
+    """Expert-parallel local halves: slot rows (zeros where another rank computes)
+    and slot weights identical between the fused kernel and the separate
+    launches."""
+    E = 32
+    T = ranks * M
+    per = E // ranks
+    rng = np.random.default_rng(300 + ranks)
+    x = q.f32_to_bf16(rng.standard_normal((T, 2048)).astype(np.float32))
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    for r in range(ranks):
+        layer, _, _ = _config3_layer(torch, ctx, n_experts=E, seed=96, owned=set(range(r * per, (r + 1) * per)) | {E})
+        got = []
+        for fused in (True, False):
+            layer.set_fused(fused)
+            slots = torch.full((T, 9, 2048), 0x7FC0, dtype=torch.int16, device="cuda")
+            sw = torch.full((T, 8), float("nan"), dtype=torch.float32, device="cuda")
+            layer.decode_local(xd, 8, slots, sw, experts=(r * per, (r + 1) * per), shared_tokens=(r * M, M),
+                               act="situ")
+            torch.cuda.synchronize()
+            got.append((slots, sw))
+        ctx.sync()
+        assert torch.equal(got[0][1], got[1][1]), r
+        assert torch.equal(got[0][0], got[1][0]), r
+        layer.close()
+
+
+@pytest.mark.parametrize("hidden,inter,E,k,T", [(512, 192, 8, 2, 5), (256, 64, 4, 4, 16), (2048, 768, 256, 16, 16),
+                                                 (4096, 1536, 64, 6, 2)])
+def test_fused_decode_edge_shapes(torch, ctx, hidden, inter, E, k, T):
+    """Shapes at the fused kernel's edges: fewer experts than CTAs, padded
+    intermediate size, k = E, the largest E / k / T, a wide hidden size."""
+    layer, wr, _ = _config3_layer(torch, ctx, n_experts=E, hidden=hidden, inter=inter, seed=97)
+    rng = np.random.default_rng(hidden + E)
+    x = q.f32_to_bf16(rng.standard_normal((T, hidden)).astype(np.float32))
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    (fo, fi, fw), (so, si, sw) = _decode_both_paths(torch, layer, xd, k, act="swiglu")
+    ctx.sync()
+    assert torch.equal(fi, si)
+    assert torch.equal(fw, sw)
+    assert torch.equal(fo, so)
+    layer.close()
