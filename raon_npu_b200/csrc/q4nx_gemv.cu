@@ -6,28 +6,32 @@
 // factorisation the reference's NPU kernel uses (kernels/gemv/q4nx_gemv.cc:88-124),
 // but with every product and partial sum kept in f32 (the reference's CPU
 // oracle, host/backend.py:402-417, multiplies the f32-dequantised weights).
-// D comes from the tensor cores: codes enter as exact bf16 values 128+code
-// (one LOP3 per two weights), so the mma yields D' = D + 128*S and the group
-// update is  acc += scale*D' + (min - 128*scale)*S  in f32.
+// Both terms run on the tensor cores (q4nx_core.cuh): codes as exact f16
+// subnormals against block-scaled f16 activations, the min term as a K = 8
+// contraction over the groups.
 //
-// Streaming.  A grid of at most one CTA per SM (8 warps each) splits the
-// matrix's units (16 rows x 256 columns, 2560 B) into contiguous ranges, one
-// per warp: either each CTA owns whole row tiles and its warps split them
-// (split tiles reduced in shared memory), or -- for a few tall tiles -- all
-// units are split evenly over the grid (split tiles reduced through global
-// partials: the last warp to arrive, by a per-tile counter, sums them and
-// resets the counter).  Either way the pieces of a tile are summed in warp
-// order.  Each warp owns a ring of 2..12 units in shared memory fed by 1-D
-// bulk copies (cp.async.bulk + mbarrier, L2 evict-first); for small matrices
-// the ring holds the warp's whole range, so every byte is requested up front.
-// The partition depends only on (N, K, SM count), never on T, so a row's
-// result is independent of the batch.
+// Streaming.  A grid of at most one CTA per SM splits the matrix's units (16
+// rows x 256 columns, 2560 B).  Two partitions, chosen from (N, K, SM count):
+//   whole tiles: CTA c owns the row tiles [c*NT/G, (c+1)*NT/G).  Warp w takes
+//     the tiles w, w+W, ... in chunks processed k-block by k-block (one
+//     k-block's activation fragments in registers, one register accumulator
+//     per tile) and finalises them itself; the last NT % W tiles run as
+//     rounds whose units are spread over all warps, reduced in shared memory.
+//   stream-K (a few tall tiles): all units split evenly over the grid in
+//     contiguous ranges; split tiles reduced through global partials (the
+//     last warp to arrive, by a per-tile counter, sums them and resets it).
+// A tile's pieces are summed in a fixed order.  Each warp owns a ring of
+// 2..12 units in shared memory fed by 1-D bulk copies (cp.async.bulk +
+// mbarrier, L2 evict-first); for small matrices the ring holds the warp's
+// whole range, so every byte is requested up front.  The partition and the
+// order of every sum never depend on T, so a row's result is independent of
+// the batch.
 //
 // Activations.  Each CTA stages the T x K activations once in shared memory,
-// already permuted into mma B-fragment order, together with the 32-column
-// group sums S; the unit loop then reads them with 16-byte shared loads.
-// (For K too large to stage, a small prep kernel writes the same layout to
-// global scratch and the unit loop reads it through the read-only path.)
+// already permuted into mma B-fragment order, together with the group-sum
+// fragments and block scales.  (For K too large to stage, a small prep kernel
+// writes the same layout to global scratch and the unit loop reads it through
+// the read-only path.)
 //
 // Launch chaining.  The kernel uses programmatic dependent launch: it issues
 // its first weight copies while the previous kernel in the stream is still
@@ -56,6 +60,7 @@ struct GemvParams {
   int kb;                  // K / 256
   int active_warps;        // stream-K partition: warps that own units (<= units)
   int mode;                // GemvPartition
+  int round_tiles;         // CTA-tile partition: tiles per reduction round
   int warps;               // warps per CTA (8 or 16)
   int stages;              // weight ring depth per warp
   int slots;               // token slots holding data (bf16: T, f32: 2T); others are never read back
@@ -67,7 +72,7 @@ struct GemvParams {
   int x_vec;               // x rows 16-byte aligned: vector loads allowed
   // ... or pre-permuted in global scratch (large-K path)
   const uint32_t *xfrag;
-  const float *gsum;
+  const void *aux;
   void *y;
   int ldy;
   const float *bias;       // f32 per row of the range, or null
@@ -79,10 +84,10 @@ struct GemvParams {
 };
 
 // Large-K path: the activations go to global scratch in the same layout.
-__global__ void gemv_prep_kernel(GemvParams p, int ntb, uint32_t *xfrag, float *gsum) {
+__global__ void gemv_prep_kernel(GemvParams p, int ntb, uint32_t *xfrag, void *aux) {
   pdl_launch_dependents();
   pdl_wait_prior();
-  build_activations<false>(p, ntb, xfrag, gsum, blockIdx.x * (long long)blockDim.x + threadIdx.x,
+  build_activations<false>(p, ntb, xfrag, aux, blockIdx.x * (long long)blockDim.x + threadIdx.x,
                            (long long)gridDim.x * blockDim.x);
 }
 
@@ -221,45 +226,222 @@ __device__ void flush_split_global(const GemvParams &p, uint32_t tile, int slot,
 //                 by several warps are reduced through global partials.
 enum GemvPartition : int { kPartTiles = 0, kPartStreamK = 1 };
 
+// kPartTiles: CTA c owns the whole tiles [c*NT/G, (c+1)*NT/G), nt of them.
+//   Main phase: warp w takes the whole tiles w, w+W, w+2W, ... (nt/W each, W
+//   warps) in chunks of up to kChunk tiles; a chunk runs k-block by k-block,
+//   so the warp loads a k-block's activation fragments once per chunk, adds
+//   each unit's result into its tile's register accumulator and finalises its
+//   own tiles -- no barrier, no shared partials.
+//   Remainder: the last nt % W tiles in rounds (RoundCursor): unit results in
+//   shared partials, summed per tile in k-block order after a barrier.
+// Either way a tile's result is the sum of its units' results in k-block
+// order, so it does not depend on the partition.
+template <int NTB>
+struct GemvChunk {
+  static constexpr int kChunk = NTB == 1 ? 4 : 1;          // tiles per chunk (register accumulators)
+};
+
+// A warp's main-phase units in processing order: chunk, k-block, tile.
+struct ChunkCursor {
+  int per_warp, kb, W, w;
+  int chunk, kbi, c, cn;
+  __device__ __forceinline__ void init(int per_warp_, int kb_, int W_, int w_, int C) {
+    per_warp = per_warp_, kb = kb_, W = W_, w = w_;
+    chunk = 0, kbi = 0, c = 0;
+    cn = per_warp < C ? per_warp : C;
+  }
+  __device__ __forceinline__ bool valid() const { return cn > 0; }
+  __device__ __forceinline__ int tile(int C) const { return w + (chunk * C + c) * W; }
+  __device__ __forceinline__ void next(int C) {
+    if (++c < cn) return;
+    c = 0;
+    if (++kbi < kb) return;
+    kbi = 0;
+    ++chunk;
+    const int left = per_warp - chunk * C;
+    cn = left <= 0 ? 0 : (left < C ? left : C);
+  }
+};
+
+template <int NTB, int EPI, bool STAGED>
+__device__ __forceinline__ void gemv_rounds(const GemvParams &p, uint8_t *smem) {
+  constexpr int C = GemvChunk<NTB>::kChunk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  const int kb = p.kb, k = kb * kUnitK, S = p.stages, R = p.round_tiles;
+  const int t0 = (int)((long long)blockIdx.x * p.n_tiles / gridDim.x);
+  const int t1 = (int)((long long)(blockIdx.x + 1) * p.n_tiles / gridDim.x);
+  const int nt = t1 - t0;
+  const int per_warp = nt / nw, n_main = per_warp * nw, n_rem = nt - n_main;
+
+  // shared memory: weight rings | activations | aux | round partials | barriers
+  uint8_t *ring = smem + warp * S * kUnitBytes;
+  const uint32_t ring_s = smem_addr(ring);
+  uint8_t *sp = smem + nw * S * kUnitBytes;
+  uint32_t *xs = reinterpret_cast<uint32_t *>(sp);
+  if (STAGED) sp += xfrag_bytes(NTB, k);
+  void *xa = sp;
+  if (STAGED) sp += xaux_bytes(NTB, k);
+  float4 *part = reinterpret_cast<float4 *>(sp);           // [R*kb][NTB][32 lanes]
+  sp += (size_t)R * kb * NTB * 32 * sizeof(float4);
+  const uint32_t bar0 = smem_addr(sp) + warp * S * 8;
+
+  // the issue cursor: main-phase units, then the remainder's (lane 0)
+  ChunkCursor im;
+  im.init(per_warp, kb, nw, warp, C);
+  RoundCursor ir;
+  ir.init(n_rem, R, kb, nw, warp);
+  const uint64_t pol = policy_evict_first();
+  int issued = 0;
+  auto issue = [&](int sl) {
+    int tile, kbi;
+    if (im.valid()) {
+      tile = im.tile(C), kbi = im.kbi;
+      im.next(C);
+    } else {
+      tile = n_main + ir.tile(), kbi = ir.kbi;
+      ir.next();
+    }
+    mbar_arrive_expect_tx(bar0 + 8 * sl, kUnitBytes);
+    bulk_copy_g2s(ring_s + sl * kUnitBytes, p.tiles + ((size_t)(t0 + tile) * kb + kbi) * kUnitBytes, kUnitBytes,
+                  bar0 + 8 * sl, pol);
+    ++issued;
+  };
+  const bool any = im.valid() || ir.valid();
+  if (lane == 0 && any) {
+    for (int sl = 0; sl < S; ++sl) mbar_init(bar0 + 8 * sl, 1);
+    mbar_fence_init();
+    for (int sl = 0; sl < S && (im.valid() || ir.valid()); ++sl) issue(sl);
+  }
+  pdl_launch_dependents();
+  // Weights are in flight; now wait for the producer of x (and for any earlier
+  // launch that shares the scratch) before touching anything it wrote.
+  pdl_wait_prior();
+  if (STAGED) {
+    build_activations<true>(p, NTB, xs, xa, threadIdx.x, blockDim.x);
+    __syncthreads();
+  }
+  const uint32_t *xf = STAGED ? xs : p.xfrag;
+  const void *auxp = STAGED ? xa : p.aux;
+
+  int j = 0, slot = 0, j_fail = 0;
+  uint32_t phase = 0;
+  bool failed = false;
+  XFrag<NTB> xr;
+  auto wait_unit = [&]() {
+    if (!failed && !mbar_wait_bounded_warp(bar0 + 8 * slot, phase)) {
+      if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+      failed = true;
+      j_fail = j;
+    }
+  };
+  auto release_unit = [&]() {
+    __syncwarp();
+    if (!failed && lane == 0 && (im.valid() || ir.valid())) issue(slot);
+    if (++slot == S) slot = 0, phase ^= 1u;
+    ++j;
+  };
+
+  // ---- main phase
+  for (int chunk = 0; chunk * C < per_warp; ++chunk) {
+    const int cn = per_warp - chunk * C < C ? per_warp - chunk * C : C;
+    Acc<NTB> acc[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) acc_zero(acc[c]);
+    for (int kbi = 0; kbi < kb; ++kbi) {
+      load_xfrag<NTB, STAGED>(xr, xf, auxp, NTB, 0, kb, kbi, lane);
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        if (c < cn) {
+          wait_unit();
+          if (!failed) unit_accumulate<NTB>(ring + slot * kUnitBytes, xr, lane, acc[c]);
+          release_unit();
+        }
+      }
+    }
+    if (!failed) {
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+        if (c < cn) finalize_tile<NTB, EPI>(p, (uint32_t)(t0 + warp + (chunk * C + c) * nw), lane, acc[c]);
+    }
+  }
+
+  // ---- remainder rounds
+  RoundCursor cur;
+  cur.init(n_rem, R, kb, nw, warp);
+  const int n_rounds = round_count(n_rem, R);
+  int xr_kbi = -1;
+  for (int r = 0; r < n_rounds; ++r) {
+    for (; cur.valid() && cur.round == r; cur.next()) {
+      wait_unit();
+      if (!failed) {
+        if (cur.kbi != xr_kbi) {
+          load_xfrag<NTB, STAGED>(xr, xf, auxp, NTB, 0, kb, cur.kbi, lane);
+          xr_kbi = cur.kbi;
+        }
+        float4 Q[NTB];
+        unit_result<NTB>(ring + slot * kUnitBytes, xr, lane, Q);
+        float4 *dst = part + (size_t)cur.slot() * NTB * 32 + lane;
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb) dst[tb * 32] = Q[tb];
+      }
+      release_unit();
+    }
+    __syncthreads();
+    const int t_lo = r * R, t_hi = t_lo + R < n_rem ? t_lo + R : n_rem;
+    for (int ti = t_lo + warp; ti < t_hi; ti += nw) {
+      Acc<NTB> acc;
+      acc_zero(acc);
+      const float4 *src = part + (size_t)(ti - t_lo) * kb * NTB * 32 + lane;
+      for (int kbi = 0; kbi < kb; ++kbi) {
+        float4 v[NTB];
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb) v[tb] = src[(kbi * NTB + tb) * 32];
+        acc_add(acc, v);
+      }
+      finalize_tile<NTB, EPI>(p, (uint32_t)(t0 + n_main + ti), lane, acc);
+    }
+    __syncthreads();
+  }
+  // after a timeout, wait (bounded) for the copies still in flight before the
+  // CTA's shared memory is released
+  if (failed && lane == 0) {
+    for (int jj = j_fail; jj < issued; ++jj) mbar_wait_bounded(bar0 + 8 * (jj % S), (uint32_t)(jj / S) & 1u);
+  }
+}
+
 template <int NTB, int EPI, bool STAGED>
 __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  if (p.mode == kPartTiles) {
+    gemv_rounds<NTB, EPI, STAGED>(p, smem);
+    return;
+  }
+  // kPartStreamK: the warps of the grid split all units evenly (contiguous
+  // ranges, k-block fastest); tiles shared by several warps are reduced
+  // through global partials.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t kb = (uint32_t)p.kb;
   const int k = p.kb * kUnitK;
-
-  // ---- this warp's unit range
-  uint32_t ub = 0, ue = 0, cta_u0 = 0, cta_units = 0, cta_warps = 0;
+  uint32_t ub = 0, ue = 0;
   const uint32_t units = (uint32_t)p.n_tiles * kb;
   const int nw = blockDim.x >> 5;              // 8 or 16 warps
   const uint32_t gw = blockIdx.x * nw + warp;
-  if (p.mode == kPartTiles) {
-    const uint32_t t0 = blockIdx.x * (uint32_t)p.n_tiles / gridDim.x;
-    const uint32_t t1 = (blockIdx.x + 1) * (uint32_t)p.n_tiles / gridDim.x;
-    cta_u0 = t0 * kb;
-    cta_units = (t1 - t0) * kb;
-    cta_warps = cta_units < (uint32_t)nw ? cta_units : (uint32_t)nw;
-    if ((uint32_t)warp < cta_warps) {
-      ub = cta_u0 + split_start(warp, cta_units, cta_warps);
-      ue = cta_u0 + split_start(warp + 1, cta_units, cta_warps);
-    }
-  } else if (gw < (uint32_t)p.active_warps) {
+  if (gw < (uint32_t)p.active_warps) {
     ub = split_start(gw, units, p.active_warps);
     ue = split_start(gw + 1, units, p.active_warps);
   }
   const int n = (int)(ue - ub);
 
-  // ---- shared memory: weight rings | activations | group sums | tile partials | barriers
+  // ---- shared memory: weight rings | activations | aux | barriers
   const int S = p.stages;
   uint8_t *ring = smem + warp * S * kUnitBytes;
   const uint32_t ring_s = smem_addr(ring);
   uint8_t *cur_p = smem + nw * S * kUnitBytes;
   uint32_t *xs = reinterpret_cast<uint32_t *>(cur_p);
   if (STAGED) cur_p += xfrag_bytes(NTB, k);
-  float *gs = reinterpret_cast<float *>(cur_p);
-  if (STAGED) cur_p += gsum_bytes(NTB, k);
-  float4 *tile_part = reinterpret_cast<float4 *>(cur_p);   // [warp][slot][tb][lane]
-  cur_p += (size_t)nw * 2 * 2 * 32 * sizeof(float4);
+  void *xa = cur_p;
+  if (STAGED) cur_p += xaux_bytes(NTB, k);
   const uint32_t bar0 = smem_addr(cur_p) + warp * S * 8;
 
   const uint64_t pol = policy_evict_first();
@@ -276,91 +458,79 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(GemvParams 
   // launch that shares the scratch) before touching anything it wrote.
   pdl_wait_prior();
   if (STAGED) {
-    build_activations<true>(p, NTB, xs, gs, threadIdx.x, blockDim.x);
+    build_activations<true>(p, NTB, xs, xa, threadIdx.x, blockDim.x);
     __syncthreads();
   }
+  if (n == 0) return;
   const uint32_t *xf = STAGED ? xs : p.xfrag;
-  const float *gsp = STAGED ? gs : p.gsum;
-
-  bool timed_out = false;
-  if (n > 0) {
-    Acc<NTB> acc;
-    acc_zero(acc);
-    uint32_t tile = ub / kb, kbi = ub - tile * kb;
-    uint32_t seg_k0 = kbi;     // first k-block of the current tile segment
-    int seg = 0;               // 0 = the warp's first tile segment
-    int slot = 0;
-    uint32_t phase = 0;        // parity of the ring slot's current fill
-    for (int j = 0; j < n; ++j) {
-      if (!mbar_wait_bounded_warp(bar0 + 8 * slot, phase)) {
-        if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
-        // Let the copies already issued (this unit's included) land before the
-        // CTA's shared memory goes away.
-        int s2 = slot;
-        uint32_t ph2 = phase;
-        for (int j2 = j; j2 < n && j2 < j + S; ++j2) {
-          mbar_wait_bounded(bar0 + 8 * s2, ph2);
-          if (++s2 == S) s2 = 0, ph2 ^= 1u;
-        }
-        timed_out = true;
-        break;
+  const void *auxp = STAGED ? xa : p.aux;
+  Acc<NTB> acc;
+  acc_zero(acc);
+  XFrag<NTB> xr;
+  uint32_t tile = ub / kb, kbi = ub - tile * kb;
+  uint32_t seg_k0 = kbi;     // first k-block of the current tile segment
+  int seg = 0;               // 0 = the warp's first tile segment
+  int slot = 0;
+  uint32_t phase = 0;        // parity of the ring slot's current fill
+  for (int j = 0; j < n; ++j) {
+    if (!mbar_wait_bounded_warp(bar0 + 8 * slot, phase)) {
+      if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+      // Let the copies already issued (this unit's included) land before the
+      // CTA's shared memory goes away.
+      int s2 = slot;
+      uint32_t ph2 = phase;
+      for (int j2 = j; j2 < n && j2 < j + S; ++j2) {
+        mbar_wait_bounded(bar0 + 8 * s2, ph2);
+        if (++s2 == S) s2 = 0, ph2 ^= 1u;
       }
-      compute_unit<NTB, STAGED>(ring + slot * kUnitBytes, xf, gsp, p, (int)kbi, lane, acc);
-      __syncwarp();
-      if (lane == 0 && j + S < n) {
-        mbar_arrive_expect_tx(bar0 + 8 * slot, kUnitBytes);
-        bulk_copy_g2s(ring_s + slot * kUnitBytes, p.tiles + (size_t)(ub + j + S) * kUnitBytes, kUnitBytes,
-                      bar0 + 8 * slot, pol);
-      }
-      if (++slot == S) slot = 0, phase ^= 1u;
-      const bool tile_end = kbi + 1 == kb;
-      if (tile_end || j + 1 == n) {
-        if (seg_k0 == 0 && tile_end) {
-          finalize_tile<NTB, EPI>(p, tile, lane, acc);
-        } else if (p.mode == kPartTiles) {
-#pragma unroll
-          for (int tb = 0; tb < NTB; ++tb)
-            tile_part[((warp * 2 + (seg ? 1 : 0)) * 2 + tb) * 32 + lane] =
-                make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3]);
-        } else {
-          flush_split_global<NTB, EPI>(p, tile, seg ? 1 : 0, gw, units, lane, acc);
-        }
-        acc_zero(acc);
-        ++tile;
-        kbi = 0;
-        seg_k0 = 0;
-        seg = 1;
-      } else {
-        ++kbi;
-      }
+      return;
+    }
+    load_xfrag<NTB, STAGED>(xr, xf, auxp, NTB, 0, p.kb, (int)kbi, lane);
+    unit_accumulate<NTB>(ring + slot * kUnitBytes, xr, lane, acc);
+    __syncwarp();
+    if (lane == 0 && j + S < n) {
+      mbar_arrive_expect_tx(bar0 + 8 * slot, kUnitBytes);
+      bulk_copy_g2s(ring_s + slot * kUnitBytes, p.tiles + (size_t)(ub + j + S) * kUnitBytes, kUnitBytes,
+                    bar0 + 8 * slot, pol);
+    }
+    if (++slot == S) slot = 0, phase ^= 1u;
+    const bool tile_end = kbi + 1 == kb;
+    if (tile_end || j + 1 == n) {
+      if (seg_k0 == 0 && tile_end)
+        finalize_tile<NTB, EPI>(p, tile, lane, acc);
+      else
+        flush_split_global<NTB, EPI>(p, tile, seg ? 1 : 0, gw, units, lane, acc);
+      acc_zero(acc);
+      ++tile;
+      kbi = 0;
+      seg_k0 = 0;
+      seg = 1;
+    } else {
+      ++kbi;
     }
   }
-  if (p.mode != kPartTiles) return;
-  // Tiles shared by warps of this CTA: the warp holding a tile's first unit
-  // sums the pieces in warp order once every warp has stored its partial.
-  __syncthreads();
-  if (n == 0 || timed_out) return;
-  const uint32_t tl = (ue - 1) / kb;                  // the warp's last tile
-  const uint32_t tl_first = tl * kb, tl_last = tl_first + kb - 1;
-  if (tl_first < ub || tl_last < ue) return;          // not the tile's first owner, or not split
-  const uint32_t w_last = split_owner(tl_last - cta_u0, cta_units, cta_warps);
-  Acc<NTB> sum;
-  acc_zero(sum);
-  for (uint32_t w2 = (uint32_t)warp; w2 <= w_last; ++w2) {
-    const int s2 = (w2 == (uint32_t)warp && tl != ub / kb) ? 1 : 0;
-    float4 v[NTB];
-#pragma unroll
-    for (int tb = 0; tb < NTB; ++tb) v[tb] = tile_part[((w2 * 2 + s2) * 2 + tb) * 32 + lane];
-    acc_add(sum, v);
-  }
-  finalize_tile<NTB, EPI>(p, tl, lane, sum);
 }
 
 // ------------------------------------------------------------------ host --
-static size_t gemv_smem_bytes(int ntb, int k, bool staged, int stages, int nw) {
+constexpr int kGemvRoundBytes = 32 * 1024;   // round partials of the CTA-tile partition
+
+// Tiles per round of the CTA-tile partition's remainder (the nt % W tiles
+// left after the warps' whole tiles): no more than any CTA's remainder, and
+// a round's unit partials fit kGemvRoundBytes (a function of the shape and
+// T; results do not depend on it).
+static int gemv_round_tiles(int ntb, int kb, int n_tiles, int grid, int warps) {
+  const int lo = n_tiles / grid, hi = (n_tiles + grid - 1) / grid;   // CTA ranges hold lo or hi tiles
+  int rem = hi % warps > lo % warps ? hi % warps : lo % warps;
+  if (rem < 1) rem = 1;
+  int r = kGemvRoundBytes / (kb * ntb * 32 * 16);
+  if (r < 1) r = 1;
+  return r < rem ? r : rem;
+}
+
+static size_t gemv_smem_bytes(int ntb, int k, bool staged, int stages, int nw, int round_tiles) {
   size_t b = (size_t)nw * stages * (kUnitBytes + 8);
-  b += (size_t)nw * 2 * 2 * 32 * 16;   // per-warp tile partials (CTA-tile partition)
-  if (staged) b += xfrag_bytes(ntb, k) + gsum_bytes(ntb, k);
+  b += (size_t)round_tiles * (k / kUnitK) * ntb * 32 * 16;   // round partials (CTA-tile partition)
+  if (staged) b += xfrag_bytes(ntb, k) + xaux_bytes(ntb, k);
   return b;
 }
 
@@ -368,9 +538,9 @@ static size_t gemv_smem_bytes(int ntb, int k, bool staged, int stages, int nw) {
 // (everything requested at once), bounded by shared memory for large ones.
 // Small rings keep the footprint low so consecutive launches can co-reside
 // on an SM under programmatic dependent launch.
-static int gemv_stages(int ntb, int k, bool staged, long long units_per_warp, int nw) {
+static int gemv_stages(int ntb, int k, bool staged, long long units_per_warp, int nw, int round_tiles) {
   int s = (int)(units_per_warp < 2 ? 2 : (units_per_warp > kGemvMaxStages ? kGemvMaxStages : units_per_warp));
-  while (s > 2 && gemv_smem_bytes(ntb, k, staged, s, nw) > (size_t)kGemvSmemLimit) --s;
+  while (s > 2 && gemv_smem_bytes(ntb, k, staged, s, nw, round_tiles) > (size_t)kGemvSmemLimit) --s;
   return s;
 }
 
@@ -402,7 +572,7 @@ static cudaError_t launch_main(const GemvParams &p, int grid, cudaStream_t s) {
   }
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(p.warps * 32),
-                                      gemv_smem_bytes(NTB, p.kb * kUnitK, STAGED, p.stages, p.warps),
+                                      gemv_smem_bytes(NTB, p.kb * kUnitK, STAGED, p.stages, p.warps, p.round_tiles),
                                       s, attr);
   return cudaLaunchKernelEx(&cfg, gemv_kernel<NTB, EPI, STAGED>, p);
 }
@@ -426,6 +596,7 @@ static cudaError_t launch_epi(const GemvParams &p, int epi, int grid, cudaStream
 struct GemvGeometry {
   int mode, grid, warps, active_warps;
   long long units_per_warp;
+  int tiles_per_cta;   // kPartTiles: the largest CTA range (0 for stream-K)
 };
 
 // Large matrices (>= 16 units per warp at 8 warps per SM) run one CTA of 16
@@ -445,6 +616,7 @@ GemvGeometry gemv_geometry(const rc_ctx *ctx, int n_tiles, int kb, int max_warps
   if (balanced || !fits32) {
     g.mode = kPartTiles;
     g.grid = (int)gt;
+    g.tiles_per_cta = (int)tiles_per_cta;
     g.active_warps = (int)(gt * nw);
     const long long cta_units = tiles_per_cta * kb;
     g.units_per_warp = (cta_units + nw - 1) / nw;
@@ -463,7 +635,7 @@ GemvGeometry gemv_geometry(const rc_ctx *ctx, int n_tiles, int kb, int max_warps
 
 // Whether ntb token blocks of K columns fit in shared memory next to the rings of nw warps.
 static bool gemv_can_stage(int ntb, int k, int nw) {
-  return gemv_smem_bytes(ntb, k, true, 2, nw) <= (size_t)kGemvSmemLimit;
+  return gemv_smem_bytes(ntb, k, true, 2, nw, 1) <= (size_t)kGemvSmemLimit;
 }
 
 // One launch over <= 16 bf16 token rows (<= 8 f32 rows).
@@ -504,14 +676,14 @@ int gemv_launch(rc_ctx *ctx, const uint8_t *tiles, int n_tiles, int k, const voi
   if (!staged) {
     const unsigned xs = ctx->launch_seq++ % kXSlots;
     p.xfrag = ctx->xfrag + xs * xfrag_slot_words(ctx->xfrag_k);
-    p.gsum = ctx->gsum + xs * gsum_slot_floats(ctx->xfrag_k);
+    p.aux = ctx->gsum + xs * gsum_slot_floats(ctx->xfrag_k);
     const long long work = (long long)p.slots * (k / 8);
     long long pg = (work + 255) / 256;
     if (pg > ctx->sm_count) pg = ctx->sm_count;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)pg), dim3(256), 0, s, attr);
     e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel, p, ntb, const_cast<uint32_t *>(p.xfrag),
-                           const_cast<float *>(p.gsum));
+                           const_cast<void *>(p.aux));
     if (e != cudaSuccess) {
       set_error("gemv prep launch: %s", cudaGetErrorString(e));
       return RC_ERR_CUDA;
@@ -521,7 +693,8 @@ int gemv_launch(rc_ctx *ctx, const uint8_t *tiles, int n_tiles, int k, const voi
   p.mode = geo.mode;
   p.warps = geo.warps;
   p.active_warps = geo.active_warps;
-  p.stages = gemv_stages(ntb, k, staged, geo.units_per_warp, geo.warps);
+  p.round_tiles = geo.mode == kPartTiles ? gemv_round_tiles(ntb, k / kUnitK, n_tiles, geo.grid, geo.warps) : 0;
+  p.stages = gemv_stages(ntb, k, staged, geo.units_per_warp, geo.warps, p.round_tiles);
   if (staged)
     e = ntb == 2 ? launch_epi<2, true>(p, epi, grid, s) : launch_epi<1, true>(p, epi, grid, s);
   else
@@ -605,7 +778,8 @@ static int gemv_launch_noalloc(rc_ctx *ctx, unsigned char *scratch, const uint8_
   p.mode = geo.mode;
   p.warps = geo.warps;
   p.active_warps = geo.active_warps;
-  p.stages = gemv_stages(ntb, k, true, geo.units_per_warp, geo.warps);
+  p.round_tiles = geo.mode == kPartTiles ? gemv_round_tiles(ntb, k / kUnitK, n_tiles, geo.grid, geo.warps) : 0;
+  p.stages = gemv_stages(ntb, k, true, geo.units_per_warp, geo.warps, p.round_tiles);
   const cudaError_t e =
       ntb == 2 ? launch_epi<2, true>(p, epi, geo.grid, s) : launch_epi<1, true>(p, epi, geo.grid, s);
   if (e != cudaSuccess) {

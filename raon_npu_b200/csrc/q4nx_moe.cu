@@ -323,14 +323,14 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
   uint8_t *ring = smem + warp * S * kUnitBytes;
   const uint32_t ring_s = smem_addr(ring);
   constexpr int kStageBlocks = EPI == kMoeEpiGlu ? NTB : NTB * kMoeMaxGroupsPerCta;
-  uint8_t *cur = smem + kMoeWarps * S * kUnitBytes;
-  uint32_t *xs = reinterpret_cast<uint32_t *>(cur);
-  cur += xfrag_bytes(kStageBlocks, k);
-  float *gs = reinterpret_cast<float *>(cur);
-  cur += gsum_bytes(kStageBlocks, k);
-  float4 *part = reinterpret_cast<float4 *>(cur);          // [R*kb][NTB][32 lanes]
-  cur += (size_t)R * kb * NTB * 32 * sizeof(float4);
-  const uint32_t bar0 = smem_addr(cur) + warp * S * 8;
+  uint8_t *sp = smem + kMoeWarps * S * kUnitBytes;
+  uint32_t *xs = reinterpret_cast<uint32_t *>(sp);
+  sp += xfrag_bytes(kStageBlocks, k);
+  void *xa = sp;
+  sp += xaux_bytes(kStageBlocks, k);
+  float4 *part = reinterpret_cast<float4 *>(sp);           // [R*kb][NTB][32 lanes]
+  sp += (size_t)R * kb * NTB * 32 * sizeof(float4);
+  const uint32_t bar0 = smem_addr(sp) + warp * S * 8;
 
   pdl_launch_dependents();
   // The group table is written by the previous launch: wait before reading it.
@@ -352,7 +352,6 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
   const int c0 = blockIdx.x * per;
   const int c1 = c0 + per < total ? c0 + per : total;
   const int n_tiles = c1 > c0 ? c1 - c0 : 0;
-  const int n_units = n_tiles * kb;
   int g_lo = 0;
   MoeGemvParams q = p;
   if (EPI == kMoeEpiDown) {
@@ -362,49 +361,49 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
     q.x = static_cast<const uint16_t *>(p.x) + (size_t)g_lo * 8 * NTB * p.ldx;
     q.tokens = q.slots = (g_hi - g_lo + 1) * 8 * NTB;
   }
-  // this warp's units: u = warp + kMoeWarps * j
-  const int n = warp < n_units ? (n_units - 1 - warp) / kMoeWarps + 1 : 0;
-
-  auto unit_src = [&](int j) -> const uint8_t * {
-    const int u = warp + kMoeWarps * j;
-    const int ti = u / kb, kbi = u - ti * kb;
-    const int tg = c0 + ti;
+  // this warp's units: its chunk of every round (k-block-major order)
+  RoundCursor cur;
+  cur.init(n_tiles, R, kb, kMoeWarps, warp);
+  RoundCursor iss = cur;                                   // the next unit to fetch (lane 0)
+  auto unit_src = [&](const RoundCursor &c) -> const uint8_t * {
+    const int tg = c0 + c.tile();
     const int grp = tg / p.group_tiles, tile = tg - grp * p.group_tiles;
     const uint8_t *b = p.expert_tiles[p.group_expert[grp]];
-    return b ? b + ((size_t)tile * kb + kbi) * kUnitBytes : nullptr;
+    return b ? b + ((size_t)tile * kb + c.kbi) * kUnitBytes : nullptr;
   };
   const uint64_t pol = policy_evict_first();
-  auto issue = [&](int j, int sl) {
-    const uint8_t *src = unit_src(j);
+  int issued = 0;                                          // copies issued so far (lane 0)
+  auto issue = [&](int sl) {
+    const uint8_t *src = unit_src(iss);
     if (src) {
       mbar_arrive_expect_tx(bar0 + 8 * sl, kUnitBytes);
       bulk_copy_g2s(ring_s + sl * kUnitBytes, src, kUnitBytes, bar0 + 8 * sl, pol);
     } else {
       mbar_arrive_expect_tx(bar0 + 8 * sl, 0);   // nothing to fetch: complete the phase at once
     }
+    iss.next();
+    ++issued;
   };
-  if (lane == 0 && n > 0) {
+  if (lane == 0 && cur.valid()) {
     for (int sl = 0; sl < S; ++sl) mbar_init(bar0 + 8 * sl, 1);
     mbar_fence_init();
-    for (int j = 0; j < n && j < S; ++j) issue(j, j);
+    for (int sl = 0; sl < S && iss.valid(); ++sl) issue(sl);
   }
-  build_activations<true>(q, kStageBlocks, xs, gs, threadIdx.x, blockDim.x);
+  build_activations<true>(q, kStageBlocks, xs, xa, threadIdx.x, blockDim.x);
   __syncthreads();
 
-  const int U = R * kb;                                    // units per round
-  const int n_rounds = (n_units + U - 1) / U;
-  int j = 0, slot_ring = 0;
+  const int n_rounds = round_count(n_tiles, R);
+  int j = 0, slot_ring = 0;                                // units consumed, ring slot of the next
   uint32_t phase = 0;
-  int issued = n < S ? n : S;                              // copies issued so far (lane 0)
   bool failed = false;
   int j_fail = 0;
   const int g = lane >> 2, qd = lane & 3;
+  XFrag<NTB> xr;
+  int xr_key = -1;                                         // (block, k-block) held in xr
   for (int r = 0; r < n_rounds; ++r) {
-    const int u_end = (r + 1) * U < n_units ? (r + 1) * U : n_units;
-    for (; j < n && warp + kMoeWarps * j < u_end; ++j) {
-      const int u = warp + kMoeWarps * j;
-      const int ti = u / kb, kbi = u - ti * kb;
-      const int tg = c0 + ti;
+    for (; cur.valid() && cur.round == r; cur.next(), ++j) {
+      const int kbi = cur.kbi;
+      const int tg = c0 + cur.tile();
       const int grp = tg / p.group_tiles;
       if (!failed && !mbar_wait_bounded_warp(bar0 + 8 * slot_ring, phase)) {
         if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
@@ -412,21 +411,19 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
         j_fail = j;
       }
       if (!failed && p.expert_tiles[p.group_expert[grp]] != nullptr) {
-        Acc<NTB> acc;
-        acc_zero(acc);
         const int blk = EPI == kMoeEpiGlu ? 0 : (grp - g_lo) * NTB;
-        compute_unit<NTB, true>(ring + slot_ring * kUnitBytes, xs + (size_t)blk * (k / 64) * 256,
-                                gs + (size_t)blk * kb * 64, p, kbi, lane, acc);
-        float4 *dst = part + (size_t)(u - r * U) * NTB * 32 + lane;
+        if (blk * kb + kbi != xr_key) {
+          load_xfrag<NTB, true>(xr, xs, xa, kStageBlocks, blk, kb, kbi, lane);
+          xr_key = blk * kb + kbi;
+        }
+        float4 Q[NTB];
+        unit_result<NTB>(ring + slot_ring * kUnitBytes, xr, lane, Q);
+        float4 *dst = part + (size_t)cur.slot() * NTB * 32 + lane;
 #pragma unroll
-        for (int tb = 0; tb < NTB; ++tb)
-          dst[tb * 32] = make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3]);
+        for (int tb = 0; tb < NTB; ++tb) dst[tb * 32] = Q[tb];
       }
       __syncwarp();
-      if (!failed && lane == 0 && j + S < n) {
-        issue(j + S, slot_ring);
-        ++issued;
-      }
+      if (!failed && lane == 0 && iss.valid()) issue(slot_ring);
       if (++slot_ring == S) slot_ring = 0, phase ^= 1u;
     }
     __syncthreads();
@@ -569,7 +566,7 @@ using namespace rc;
 namespace rc {
 
 static size_t moe_smem_bytes(int stage_blocks, int k, int stages, int partial_bytes) {
-  return (size_t)kMoeWarps * stages * (kUnitBytes + 8) + xfrag_bytes(stage_blocks, k) + gsum_bytes(stage_blocks, k) +
+  return (size_t)kMoeWarps * stages * (kUnitBytes + 8) + xfrag_bytes(stage_blocks, k) + xaux_bytes(stage_blocks, k) +
          partial_bytes;
 }
 

@@ -75,7 +75,7 @@ struct MoeFusedParams {
   int *err;
 };
 
-// what build_activations / compute_unit read
+// what build_activations reads
 struct FzStage {
   const void *x;
   int x_dtype, ldx, tokens, slots, x_vec, kb;
@@ -196,114 +196,108 @@ __device__ uint32_t fz_prefetch_tiles(const uint8_t *const *g_ptr, int c0, int n
   return budget;
 }
 
-// The warp's unit stream across both phases: ring index j < n_gu is gate/up
-// unit warp + 16 j of the CTA's gate/up range, j >= n_gu is down unit
-// warp + 16 (j - n_gu) of its down range.
-struct FzUnits {
-  const uint8_t *const *g_gu;        // [groups] tile base of each group (shared memory; null: not loaded)
-  const uint8_t *const *g_dn;
-  int c0_gu, n_gu, c0_dn;
-  FastDiv kb_gu, gt_gu, kb_dn, gt_dn;
-  int n_total;
+// One phase's units: tiles [c0, c0 + n_tiles) of the group-major tile list,
+// kb k-blocks each, rounds of R tiles (see RoundCursor).
+struct FzRange {
+  const uint8_t *const *g_ptr;       // [groups] tile base of each group (shared memory; null: not loaded)
+  int c0, n_tiles, R, kb;
+  FastDiv gt;                        // tiles per group
 
-  __device__ const uint8_t *src(int warp, int j) const {
-    const bool gu = j < n_gu;
-    const uint32_t u = warp + kFzWarps * (gu ? j : j - n_gu);
-    const FastDiv kb = gu ? kb_gu : kb_dn, gt = gu ? gt_gu : gt_dn;
-    const uint32_t ti = fdiv(u, kb), kbi = u - ti * kb.d;
-    const uint32_t tg = (gu ? c0_gu : c0_dn) + ti;
+  __device__ __forceinline__ const uint8_t *src(const RoundCursor &c) const {
+    const uint32_t tg = c0 + c.tile();
     const uint32_t grp = fdiv(tg, gt), tile = tg - grp * gt.d;
-    const uint8_t *b = (gu ? g_gu : g_dn)[grp];
-    return b ? b + ((size_t)tile * kb.d + kbi) * kUnitBytes : nullptr;
+    const uint8_t *b = g_ptr[grp];
+    return b ? b + ((size_t)tile * kb + c.kbi) * kUnitBytes : nullptr;
   }
 };
 
-// Ring state of a warp: slot / phase of the next unit to consume, copies
-// issued (lane 0's count), units consumed.
+// A warp's ring: the gate/up units of its chunks, then its down units.  The
+// issue cursor runs up to S units ahead of consumption, across the phase
+// boundary, so the first down weights are in flight during gate/up.
 struct FzRing {
+  RoundCursor iss;                   // next unit to fetch (lane 0)
+  int iss_phase;                     // 0 gate/up, 1 down, 2 none left
   int slot, issued, consumed;
-  uint32_t phase;
+  uint32_t parity;
   bool failed;
 };
 
-__device__ __forceinline__ void fz_issue(const FzUnits &un, int warp, int j, int sl, uint32_t ring_s, uint32_t bar0,
-                                         uint64_t pol) {
-  const uint8_t *src = un.src(warp, j);
+__device__ __forceinline__ void fz_issue(FzRing &rg, const FzRange *ph, int warp, uint32_t ring_s, uint32_t bar0,
+                                         uint64_t pol, int sl) {
+  const uint8_t *src = ph[rg.iss_phase].src(rg.iss);
   if (src) {
     mbar_arrive_expect_tx(bar0 + 8 * sl, kUnitBytes);
     bulk_copy_g2s(ring_s + sl * kUnitBytes, src, kUnitBytes, bar0 + 8 * sl, pol);
   } else {
     mbar_arrive_expect_tx(bar0 + 8 * sl, 0);     // nothing to fetch: complete the phase at once
   }
+  ++rg.issued;
+  rg.iss.next();
+  while (rg.iss_phase < 2 && !rg.iss.valid()) {
+    if (++rg.iss_phase < 2) rg.iss.init(ph[1].n_tiles, ph[1].R, ph[1].kb, kFzWarps, warp);
+  }
 }
 
 enum FzEpi : int { kFzGlu = 0, kFzDown = 1 };
 
-// One phase (gate/up or down) of this CTA: tiles [c0, c0 + n_tiles) of the
-// group-major tile list, units u = warp + 16 jj, rounds of R whole tiles.
-// Each unit's contribution goes to its own shared-memory partial; after a
-// round's barrier one warp per tile sums the tile's partials in k-block order
-// and runs the epilogue, so a tile's result depends on the tile alone.
-// j0 is the ring index of the warp's first unit of this phase.
+// One phase (gate/up or down) of this CTA over ph[EPI].  Each unit's result
+// goes to its own shared-memory partial; after a round's barrier one warp per
+// tile sums the tile's partials in k-block order and runs the epilogue, so a
+// tile's result depends on the tile alone.
 template <int EPI, int NTB>
-__device__ void fz_phase(const MoeFusedParams &p, uint8_t *smem, const FzStage &st, const FzUnits &un,
-                         const uint8_t *const *g_ptr, const uint32_t *g_mask, const int *g_dst, int g_lo, int c0,
-                         int n_tiles, FastDiv gt, FastDiv kbd, int R, int j0, int n_w, FzRing &rg) {
+__device__ void fz_phase(const MoeFusedParams &p, uint8_t *smem, const FzRange *ph, const uint32_t *g_mask,
+                         const int *g_dst, int g_lo, FzRing &rg) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const FzRange &pr = ph[EPI];
   const int S = p.stages;
-  const int kb = (int)kbd.d, k = kb * kUnitK;
+  const int kb = pr.kb, k = kb * kUnitK, R = pr.R, n_tiles = pr.n_tiles;
   uint8_t *ring = smem + warp * S * kUnitBytes;
   const uint32_t ring_s = smem_addr(ring);
   const uint32_t bar0 = smem_addr(smem + p.off_bar) + warp * S * 8;
   const uint32_t *xs = reinterpret_cast<const uint32_t *>(smem + p.off_stage);
   constexpr int kBlocks = EPI == kFzGlu ? NTB : NTB * kMoeMaxGroupsPerCta;
-  const float *gs = reinterpret_cast<const float *>(smem + p.off_stage + xfrag_bytes(kBlocks, k));
+  const void *xa = smem + p.off_stage + xfrag_bytes(kBlocks, k);
+  XFrag<NTB> xr;
+  int xr_key = -1;                              // (block, k-block) held in xr
   float4 *part = reinterpret_cast<float4 *>(smem + p.off_part);
   const uint64_t pol = policy_evict_first();
-  const int n_units = n_tiles * kb;
-  const int U = R * kb;
-  const int n_rounds = (n_units + U - 1) / U;
-  int jj = 0;
+  const int n_rounds = round_count(n_tiles, R);
+  RoundCursor cur;
+  cur.init(n_tiles, R, kb, kFzWarps, warp);
   const int g = lane >> 2, qd = lane & 3;
   for (int r = 0; r < n_rounds; ++r) {
-    const int u_end = (r + 1) * U < n_units ? (r + 1) * U : n_units;
-    for (; jj < n_w && warp + kFzWarps * jj < u_end; ++jj) {
-      const uint32_t u = warp + kFzWarps * jj;
-      const uint32_t ti = fdiv(u, kbd), kbi = u - ti * kb;
-      const uint32_t grp = fdiv(c0 + ti, gt);
+    for (; cur.valid() && cur.round == r; cur.next()) {
+      const uint32_t grp = fdiv(pr.c0 + cur.tile(), pr.gt);
       if (!rg.failed) {
-        if (mbar_wait_bounded_warp(bar0 + 8 * rg.slot, rg.phase)) {
-          rg.consumed = j0 + jj + 1;
+        if (mbar_wait_bounded_warp(bar0 + 8 * rg.slot, rg.parity)) {
+          ++rg.consumed;
         } else {
           if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
           rg.failed = true;
         }
       }
-      if (!rg.failed && g_ptr[grp] != nullptr) {
-        Acc<NTB> acc;
-        acc_zero(acc);
+      if (!rg.failed && pr.g_ptr[grp] != nullptr) {
         const int blk = EPI == kFzGlu ? 0 : ((int)grp - g_lo) * NTB;
-        compute_unit<NTB, true>(ring + rg.slot * kUnitBytes, xs + (size_t)blk * (k / 64) * 256,
-                                gs + (size_t)blk * kb * 64, st, kbi, lane, acc);
-        float4 *dst = part + (size_t)(u - r * U) * NTB * 32 + lane;
+        if (blk * kb + cur.kbi != xr_key) {
+          load_xfrag<NTB, true>(xr, xs, xa, kBlocks, blk, kb, cur.kbi, lane);
+          xr_key = blk * kb + cur.kbi;
+        }
+        float4 Q[NTB];
+        unit_result<NTB>(ring + rg.slot * kUnitBytes, xr, lane, Q);
+        float4 *dst = part + (size_t)cur.slot() * NTB * 32 + lane;
 #pragma unroll
-        for (int tb = 0; tb < NTB; ++tb)
-          dst[tb * 32] = make_float4(acc.v[tb][0], acc.v[tb][1], acc.v[tb][2], acc.v[tb][3]);
+        for (int tb = 0; tb < NTB; ++tb) dst[tb * 32] = Q[tb];
       }
       __syncwarp();
-      const int jn = j0 + jj + S;                   // the ring index this slot takes next
-      if (!rg.failed && lane == 0 && jn < un.n_total) {
-        fz_issue(un, warp, jn, rg.slot, ring_s, bar0, pol);
-        ++rg.issued;
-      }
-      if (++rg.slot == S) rg.slot = 0, rg.phase ^= 1u;
+      if (!rg.failed && lane == 0 && rg.iss_phase < 2) fz_issue(rg, ph, warp, ring_s, bar0, pol, rg.slot);
+      if (++rg.slot == S) rg.slot = 0, rg.parity ^= 1u;
     }
     __syncthreads();
     const int t_lo = r * R, t_hi = t_lo + R < n_tiles ? t_lo + R : n_tiles;
     for (int ti = t_lo + warp; ti < t_hi; ti += kFzWarps) {
-      const uint32_t tg = c0 + ti;
-      const uint32_t grp = fdiv(tg, gt), tile = tg - grp * gt.d;
-      const bool live = g_ptr[grp] != nullptr;
+      const uint32_t tg = pr.c0 + ti;
+      const uint32_t grp = fdiv(tg, pr.gt), tile = tg - grp * pr.gt.d;
+      const bool live = pr.g_ptr[grp] != nullptr;
       Acc<NTB> acc;
       acc_zero(acc);
       const float4 *src = part + (size_t)(ti - t_lo) * kb * NTB * 32 + lane;
@@ -543,24 +537,28 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
   const int c0_gu = blockIdx.x * per_gu, c0_dn = blockIdx.x * per_dn;
   const int nt_gu = c0_gu < tot_gu ? (c0_gu + per_gu < tot_gu ? per_gu : tot_gu - c0_gu) : 0;
   const int nt_dn = c0_dn < tot_dn ? (c0_dn + per_dn < tot_dn ? per_dn : tot_dn - c0_dn) : 0;
-  const int nu_gu = nt_gu * kb_gu_i, nu_dn = nt_dn * kb_dn_i;
-  const int nw_gu = warp < nu_gu ? (nu_gu - 1 - warp) / kFzWarps + 1 : 0;
-  const int nw_dn = warp < nu_dn ? (nu_dn - 1 - warp) / kFzWarps + 1 : 0;
-  const FastDiv fkb_gu = make_fastdiv(kb_gu_i), fgt_gu = make_fastdiv(gt_gu_i);
-  const FastDiv fkb_dn = make_fastdiv(kb_dn_i), fgt_dn = make_fastdiv(gt_dn_i);
   const int S = p.stages;
   const uint32_t bar0 = smem_addr(smem + p.off_bar) + warp * S * 8;
-  const FzUnits un{g_gu, g_dn, c0_gu, nw_gu, c0_dn, fkb_gu, fgt_gu, fkb_dn, fgt_dn, nw_gu + nw_dn};
-  FzRing rg{0, 0, 0, 0u, false};
-  if (lane == 0 && un.n_total > 0) {
+  // the two phases' ranges: per-CTA constants in shared memory (indexed by
+  // the ring's current phase at run time)
+  FzRange *ph = reinterpret_cast<FzRange *>(smem + p.off_red + kFzWarps * kMoeMaxTokens * 8 + 16);
+  if (tid == 0) {
+    ph[0] = FzRange{g_gu, c0_gu, nt_gu, p.round_gu, kb_gu_i, make_fastdiv(gt_gu_i)};
+    ph[1] = FzRange{g_dn, c0_dn, nt_dn, p.round_dn, kb_dn_i, make_fastdiv(gt_dn_i)};
+  }
+  __syncthreads();
+  FzRing rg{};
+  rg.iss.init(nt_gu, p.round_gu, kb_gu_i, kFzWarps, warp);
+  rg.iss_phase = 0;
+  while (rg.iss_phase < 2 && !rg.iss.valid()) {
+    if (++rg.iss_phase < 2) rg.iss.init(nt_dn, p.round_dn, kb_dn_i, kFzWarps, warp);
+  }
+  if (lane == 0 && rg.iss_phase < 2) {
     const uint32_t ring_s = smem_addr(smem + warp * S * kUnitBytes);
     const uint64_t pol = policy_evict_first();
     for (int sl = 0; sl < S; ++sl) mbar_init(bar0 + 8 * sl, 1);
     mbar_fence_init();
-    for (int j = 0; j < un.n_total && j < S; ++j) {
-      fz_issue(un, warp, j, j, ring_s, bar0, pol);
-      ++rg.issued;
-    }
+    for (int sl = 0; sl < S && rg.iss_phase < 2; ++sl) fz_issue(rg, ph, warp, ring_s, bar0, pol, sl);
   }
   // the rest of the CTA's weights: L2 prefetch, gate/up first, then down
   if (warp == kFzWarps - 1) {
@@ -583,11 +581,9 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
   // ------------------------------------------------------------ 3 gate/up
   FzStage sx{p.x, RC_DTYPE_BF16, p.hidden, T, T, 1, kb_gu_i};
   build_activations<true>(sx, NTB, reinterpret_cast<uint32_t *>(smem + p.off_stage),
-                          reinterpret_cast<float *>(smem + p.off_stage + xfrag_bytes(NTB, p.hidden)), tid,
-                          blockDim.x);
+                          smem + p.off_stage + xfrag_bytes(NTB, p.hidden), tid, blockDim.x);
   __syncthreads();
-  fz_phase<kFzGlu, NTB>(p, smem, sx, un, g_gu, g_mask, g_dst, 0, c0_gu, nt_gu, fgt_gu, fkb_gu, p.round_gu, 0, nw_gu,
-                        rg);
+  fz_phase<kFzGlu, NTB>(p, smem, ph, g_mask, g_dst, 0, rg);
   bool failed = __syncthreads_or(rg.failed) != 0;
   if (!failed && !fz_grid_barrier(p.bar, p.err, ok_s)) failed = true;
 
@@ -598,12 +594,10 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
     FzStage sa{p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, RC_DTYPE_BF16, p.inter_pad,
                (g_hi - g_lo + 1) * 8 * NTB, (g_hi - g_lo + 1) * 8 * NTB, 1, kb_dn_i};
     build_activations<true>(sa, NTB * kMoeMaxGroupsPerCta, reinterpret_cast<uint32_t *>(smem + p.off_stage),
-                            reinterpret_cast<float *>(smem + p.off_stage +
-                                                      xfrag_bytes(NTB * kMoeMaxGroupsPerCta, p.inter_pad)),
-                            tid, blockDim.x);
+                            smem + p.off_stage + xfrag_bytes(NTB * kMoeMaxGroupsPerCta, p.inter_pad), tid,
+                            blockDim.x);
     __syncthreads();
-    fz_phase<kFzDown, NTB>(p, smem, sa, un, g_dn, g_mask, g_dst, g_lo, c0_dn, nt_dn, fgt_dn, fkb_dn, p.round_dn,
-                           nw_gu, nw_dn, rg);
+    fz_phase<kFzDown, NTB>(p, smem, ph, g_mask, g_dst, g_lo, rg);
     failed = __syncthreads_or(rg.failed) != 0;
   }
   if (!failed && !fz_grid_barrier(p.bar, p.err, ok_s)) failed = true;
@@ -659,15 +653,16 @@ struct FzLayout {
 
 static bool fz_layout(int ntb, int hidden, int inter_pad, int E, int T, int k, FzLayout *L) {
   const int kb_gu = hidden / kUnitK, kb_dn = inter_pad / kUnitK;
-  const size_t st_x = xfrag_bytes(ntb, hidden) + gsum_bytes(ntb, hidden);
-  const size_t st_a = xfrag_bytes(ntb * kMoeMaxGroupsPerCta, inter_pad) + gsum_bytes(ntb * kMoeMaxGroupsPerCta,
+  const size_t st_x = xfrag_bytes(ntb, hidden) + xaux_bytes(ntb, hidden);
+  const size_t st_a = xfrag_bytes(ntb * kMoeMaxGroupsPerCta, inter_pad) + xaux_bytes(ntb * kMoeMaxGroupsPerCta,
                                                                                      inter_pad);
   const size_t st_sel = (size_t)T * k * 8 + (size_t)(E + 1) * 8 + 64;   // selection scratch
   size_t stage = st_x > st_a ? st_x : st_a;
   if (st_sel > stage) stage = st_sel;
   const size_t tab = (size_t)(E + 1) * (4 * 8 + 4 + 4 + 4 + 4 * kMoeMaxTokens) + 16;   // expert and group tables
   const size_t sel = (size_t)T * (k + 1) * 4 + (size_t)T * k * 4;
-  const size_t red = (size_t)kFzWarps * kMoeMaxTokens * 8 + 16;   // + the barrier verdict word
+  // + the barrier verdict word and the two phase ranges
+  const size_t red = (size_t)kFzWarps * kMoeMaxTokens * 8 + 16 + 2 * sizeof(FzRange);
   const int unit_part = ntb * 32 * 16;
   for (int cap = kMoePartialBytes; cap >= 8 * 1024; cap /= 2) {
     const int R_gu = cap / (kb_gu * unit_part), R_dn = cap / (kb_dn * unit_part);

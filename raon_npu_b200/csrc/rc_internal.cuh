@@ -91,7 +91,7 @@ struct rc_ctx {
   // GEMV scratch: fragment-ordered x, group sums, split-K partials, tile counters.
   uint32_t *xfrag;      // kXSlots x [2 token blocks][K/64][32 lanes][8 words]
   size_t xfrag_k;       // K capacity of one xfrag / gsum slot
-  float *gsum;          // kXSlots x [2][K/256][4][8][2]
+  float *gsum;          // kXSlots x aux words of 2 token blocks (group-sum fragments, block scales)
   unsigned launch_seq;  // picks the activation slot of the next launch
   float *partials;      // [warps][2][2 token blocks][32 lanes][4]
   int *counters;        // [tiles], all zero between launches
@@ -114,8 +114,8 @@ int ensure_gemv_scratch(rc_ctx *ctx, int k, int n_tiles);
 int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb);
 int ensure_sample_scratch(rc_ctx *ctx, size_t bytes);
 int check_error_word(rc_ctx *ctx);
-// Words of one xfrag slot / floats of one gsum slot for K columns.
+// Words of one xfrag slot / floats of one aux slot for K columns (2 token blocks).
 inline size_t xfrag_slot_words(size_t k) { return 2 * k * 4; }
-inline size_t gsum_slot_floats(size_t k) { return k / 2; }
+inline size_t gsum_slot_floats(size_t k) { return 17 * k / 16; }
 cudaStream_t pick_stream(rc_ctx *ctx, void *stream);
 }  // namespace rc
