@@ -4,8 +4,7 @@
 // exchange data through global memory:
 //
 //   1 logits     CTA c computes the logits of experts c, c + grid, ...
-//                (f64 sums of exact bf16 products, rounded once to f32);
-//                meanwhile the shared expert's weights are prefetched to L2
+//                (f64 sums of exact bf16 products, rounded once to f32)
 //   -- barrier --
 //   2 selection  every CTA reads the T x E logits and repeats the selection
 //                in its own shared memory: one warp per token takes the k
@@ -14,8 +13,8 @@
 //                weights, the ascending-ID slot lists and the group table --
 //                identical inputs give identical tables, so no barrier is
 //                needed after it
-//   3 gate/up    the CTA's contiguous range of (group, row tile) tiles, its
-//                bytes first prefetched to L2; units dealt to 16 warps,
+//   3 gate/up    the CTA's contiguous range of (group, row tile) tiles; units
+//                dealt to 16 warps k-block-major (RoundCursor),
 //                per-unit partials summed in k-block order (a tile's result
 //                never depends on the partition); GLU epilogue -> act rows
 //   -- barrier --
@@ -41,8 +40,6 @@ constexpr int kFzWarps = 16;
 constexpr int kFzThreads = kFzWarps * 32;
 constexpr int kFzMaxStages = 4;
 constexpr int kFzChunks = kMoeMaxExperts / 32;        // router values a lane holds per token
-constexpr uint32_t kFzPrefetchChunk = 16 * 1024;     // bytes per L2 prefetch instruction
-constexpr uint32_t kFzPrefetchBudget = 192 * 1024;   // L2 prefetch per CTA at the start of gate/up
 
 struct MoeFusedParams {
   // tokens and router
@@ -134,7 +131,7 @@ __device__ void fz_build_groups(const int32_t *slots, int T, int k, int E, MoeOw
     const int t = pr / (k + 1), r = pr - t * (k + 1);
     const int ex = slots[pr];
     const bool mine = r < k ? (ex >= own.lo && ex < own.hi) : (ex >= 0 && ((own.shared_mask >> t) & 1u));
-    if (mine) g_dst[gidx_s[ex] * kMoeMaxTokens + t] = pr;
+    if (mine) g_dst[gidx_s[ex] * T + t] = pr;
   }
   __syncthreads();
 }
@@ -164,36 +161,6 @@ __device__ bool fz_grid_barrier(unsigned long long *bar, int *err, int *ok_s) {
   }
   __syncthreads();
   return *ok_s != 0;
-}
-
-// L2 prefetch of [base, base + bytes) by one warp, in chunks.
-__device__ __forceinline__ void fz_prefetch(const uint8_t *base, uint32_t bytes, int lane) {
-  for (uint32_t o = (uint32_t)lane * kFzPrefetchChunk; o < bytes; o += 32 * kFzPrefetchChunk) {
-    const uint32_t n = bytes - o < kFzPrefetchChunk ? bytes - o : kFzPrefetchChunk;
-    prefetch_l2_bulk(base + o, n);
-  }
-}
-
-// One warp: L2 prefetch of tiles [c0, c0 + n_tiles) of the group-major tile
-// list (the tiles of one group lie back to back, kb units each), up to
-// ``budget`` bytes; returns what is left of the budget.
-__device__ uint32_t fz_prefetch_tiles(const uint8_t *const *g_ptr, int c0, int n_tiles, int gt, int kb,
-                                      uint32_t budget, int lane) {
-  int tg = c0;
-  const int c1 = c0 + n_tiles;
-  while (tg < c1 && budget > 0) {
-    const int grp = tg / gt;
-    const int t_end = (grp + 1) * gt < c1 ? (grp + 1) * gt : c1;
-    const uint8_t *b = g_ptr[grp];
-    if (b) {
-      uint32_t bytes = (uint32_t)(t_end - tg) * kb * kUnitBytes;
-      if (bytes > budget) bytes = budget;
-      fz_prefetch(b + (size_t)(tg - grp * gt) * kb * kUnitBytes, bytes, lane);
-      budget -= bytes;
-    }
-    tg = t_end;
-  }
-  return budget;
 }
 
 // One phase's units: tiles [c0, c0 + n_tiles) of the group-major tile list,
@@ -323,7 +290,7 @@ __device__ void fz_phase(const MoeFusedParams &p, uint8_t *smem, const FzRange *
             }
             p.act[((size_t)grp * 8 * NTB + t) * p.inter_pad + tile * 8 + g] = f32_to_bf16_rne(v);
           } else {
-            uint16_t *y = p.slot_rows + (size_t)g_dst[grp * kMoeMaxTokens + t] * p.hidden + tile * kUnitRows + g;
+            uint16_t *y = p.slot_rows + (size_t)g_dst[grp * p.T + t] * p.hidden + tile * kUnitRows + g;
             y[0] = live ? f32_to_bf16_rne(acc.v[tb][e2]) : (uint16_t)0;
             y[8] = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : (uint16_t)0;
           }
@@ -343,18 +310,6 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
   const int gt_gu_i = p.inter / 8, kb_gu_i = p.hidden / kUnitK;
   const int gt_dn_i = p.hidden / kUnitRows, kb_dn_i = p.inter_pad / kUnitK;
 
-  // the shared expert's weights are needed whatever the routing: start
-  // bringing this CTA's slice of them into L2 now
-  if (warp == kFzWarps - 1 && p.shared_id >= 0 && p.own.shared_mask) {
-    const uint8_t *sg = p.gu_tiles[p.shared_id], *sd = p.dn_tiles[p.shared_id];
-    const uint32_t gbytes = (uint32_t)gt_gu_i * kb_gu_i * kUnitBytes;
-    const uint32_t dbytes = (uint32_t)gt_dn_i * kb_dn_i * kUnitBytes;
-    const uint32_t gs = (gbytes / gridDim.x + 15) / 16 * 16, ds = (dbytes / gridDim.x + 15) / 16 * 16;
-    const uint32_t go = gs * blockIdx.x, dof = ds * blockIdx.x;
-    if (sg && go < gbytes) fz_prefetch(sg + go, gbytes - go < gs ? gbytes - go : gs, lane);
-    if (sd && dof < dbytes) fz_prefetch(sd + dof, dbytes - dof < ds ? dbytes - dof : ds, lane);
-  }
-
   // per-expert tables kept in shared memory for the whole kernel
   const uint8_t **all_gu = reinterpret_cast<const uint8_t **>(smem + p.off_tab);    // [E+1]
   const uint8_t **all_dn = all_gu + (E + 1);                                         // [E+1]
@@ -364,7 +319,7 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
   int32_t *g_expert = reinterpret_cast<int32_t *>(bias_s + (E + 1));                // [E+1]
   uint32_t *g_mask = reinterpret_cast<uint32_t *>(g_expert + (E + 1));              // [E+1]
   int32_t *g_dst = reinterpret_cast<int32_t *>(g_mask + (E + 1));                   // [E+1][16]
-  int *n_groups_s = g_dst + (E + 1) * kMoeMaxTokens;
+  int *n_groups_s = g_dst + (E + 1) * T;
   auto load_tables = [&](int first, int stride) {
     for (int i = first; i <= E; i += stride) {
       all_gu[i] = p.gu_tiles[i];
@@ -560,11 +515,6 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
     mbar_fence_init();
     for (int sl = 0; sl < S && rg.iss_phase < 2; ++sl) fz_issue(rg, ph, warp, ring_s, bar0, pol, sl);
   }
-  // the rest of the CTA's weights: L2 prefetch, gate/up first, then down
-  if (warp == kFzWarps - 1) {
-    const uint32_t left = fz_prefetch_tiles(g_gu, c0_gu, nt_gu, gt_gu_i, kb_gu_i, kFzPrefetchBudget, lane);
-    fz_prefetch_tiles(g_dn, c0_dn, nt_dn, gt_dn_i, kb_dn_i, left, lane);
-  }
   // expert parallelism: zero the slot rows other ranks compute
   if (p.zero_foreign) {
     const int rows = T * (k + 1);
@@ -651,24 +601,40 @@ struct FzLayout {
   int stages, round_gu, round_dn, off_stage, off_part, off_tab, off_sel, off_red, off_bar, smem;
 };
 
-static bool fz_layout(int ntb, int hidden, int inter_pad, int E, int T, int k, FzLayout *L) {
+// The largest number of groups a call can have on this rank.
+static int fz_max_groups(int T, int k, const MoeOwned &own) {
+  const int owned = own.hi - own.lo;
+  return (T * k < owned ? T * k : owned) + (own.shared_mask ? 1 : 0);
+}
+
+// Shared-memory layout of one call.  The deepest weight ring (up to 4 units
+// per warp) comes first; the round partials hold at most the tiles a CTA can
+// get in either phase, and shrink before the ring does.
+static bool fz_layout(const rc_moe *m, int T, int k, const MoeOwned &own, FzLayout *L) {
+  const int ntb = T <= 8 ? 1 : 2, E = m->n_experts, grid = m->ctx->sm_count;
+  const int hidden = m->hidden, inter_pad = m->inter_pad;
   const int kb_gu = hidden / kUnitK, kb_dn = inter_pad / kUnitK;
+  const int mg = fz_max_groups(T, k, own);
+  const int per_gu = (mg * (m->inter / 8) + grid - 1) / grid;          // tiles per CTA, at most
+  const int per_dn = (mg * (hidden / kUnitRows) + grid - 1) / grid;
   const size_t st_x = xfrag_bytes(ntb, hidden) + xaux_bytes(ntb, hidden);
   const size_t st_a = xfrag_bytes(ntb * kMoeMaxGroupsPerCta, inter_pad) + xaux_bytes(ntb * kMoeMaxGroupsPerCta,
                                                                                      inter_pad);
   const size_t st_sel = (size_t)T * k * 8 + (size_t)(E + 1) * 8 + 64;   // selection scratch
   size_t stage = st_x > st_a ? st_x : st_a;
   if (st_sel > stage) stage = st_sel;
-  const size_t tab = (size_t)(E + 1) * (4 * 8 + 4 + 4 + 4 + 4 * kMoeMaxTokens) + 16;   // expert and group tables
+  const size_t tab = (size_t)(E + 1) * (4 * 8 + 4 + 4 + 4 + 4 * T) + 16;   // expert and group tables
   const size_t sel = (size_t)T * (k + 1) * 4 + (size_t)T * k * 4;
   // + the barrier verdict word and the two phase ranges
   const size_t red = (size_t)kFzWarps * kMoeMaxTokens * 8 + 16 + 2 * sizeof(FzRange);
   const int unit_part = ntb * 32 * 16;
-  for (int cap = kMoePartialBytes; cap >= 8 * 1024; cap /= 2) {
-    const int R_gu = cap / (kb_gu * unit_part), R_dn = cap / (kb_dn * unit_part);
-    if (R_gu < 1 || R_dn < 1) continue;
-    const size_t part = (size_t)(R_gu * kb_gu > R_dn * kb_dn ? R_gu * kb_gu : R_dn * kb_dn) * unit_part;
-    for (int S = kFzMaxStages; S >= 2; --S) {
+  for (int S = kFzMaxStages; S >= 2; --S) {
+    for (int cap = kMoePartialBytes; cap >= 4 * 1024; cap /= 2) {
+      int R_gu = cap / (kb_gu * unit_part), R_dn = cap / (kb_dn * unit_part);
+      if (R_gu < 1 || R_dn < 1) continue;
+      if (R_gu > per_gu) R_gu = per_gu > 0 ? per_gu : 1;
+      if (R_dn > per_dn) R_dn = per_dn > 0 ? per_dn : 1;
+      const size_t part = (size_t)(R_gu * kb_gu > R_dn * kb_dn ? R_gu * kb_gu : R_dn * kb_dn) * unit_part;
       size_t off = (size_t)kFzWarps * S * kUnitBytes;
       const size_t o_stage = off;
       off += (stage + 15) / 16 * 16;
@@ -692,15 +658,13 @@ static bool fz_layout(int ntb, int hidden, int inter_pad, int E, int T, int k, F
   return false;
 }
 
-
 // Whether the fused kernel takes this call: the shared-memory layout fits and
 // a CTA's down range touches at most kMoeMaxGroupsPerCta groups.
 bool moe_fused_fits(const rc_moe *m, int T, int k, const MoeOwned &own) {
   if (!m->fused) return false;
   FzLayout L;
-  if (!fz_layout(T <= 8 ? 1 : 2, m->hidden, m->inter_pad, m->n_experts, T, k, &L)) return false;
-  const int owned = own.hi - own.lo;
-  const int max_groups = (T * k < owned ? T * k : owned) + (own.shared_mask ? 1 : 0);
+  if (!fz_layout(m, T, k, own, &L)) return false;
+  const int max_groups = fz_max_groups(T, k, own);
   const int gt_dn = m->hidden / kUnitRows;
   const int per_dn = (max_groups * gt_dn + m->ctx->sm_count - 1) / m->ctx->sm_count;
   return per_dn - 1 <= (kMoeMaxGroupsPerCta - 1) * gt_dn;
@@ -715,7 +679,7 @@ int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int
                      int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s) {
   const int ntb = T <= 8 ? 1 : 2;
   FzLayout L;
-  if (!fz_layout(ntb, m->hidden, m->inter_pad, m->n_experts, T, k, &L)) {
+  if (!fz_layout(m, T, k, own, &L)) {
     set_error("fused MoE decode: no shared-memory layout for T=%d k=%d", T, k);
     return RC_ERR_INVALID;
   }

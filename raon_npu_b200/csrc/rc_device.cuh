@@ -105,12 +105,6 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void *src, uin
       : "memory");
 }
 
-// Bulk prefetch of [src, src + bytes) into L2 (no completion to wait for).
-// src 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // ------------------------------------------------- grid-scope atomics --
 __device__ __forceinline__ unsigned long long atom_add_release_gpu(unsigned long long *p, unsigned long long v) {
   unsigned long long old;
