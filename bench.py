@@ -50,6 +50,13 @@ METRIC = "q4nx GEMV HBM GB/s vs 8 TB/s; MoE layer tokens/s at 1/2/4/8 B200"
 HBM_FALLBACK_GBS = 6650.0
 
 
+# DRAM traffic of the timed work, from ncu captures of the same commands on a
+# B200 (dram__bytes_read.sum + dram__bytes_write.sum): the GEMV launches of
+# one sweep step; one config-3 decode layer at T = 1 (moe_fused_kernel); the
+# two grouped GEMMs of one 512-token prefill layer.  Single-GPU figures.
+MEASURED_TRAFFIC = {"gemv_step": 1033.4e6, "moe_layer_t1": 27.61e6, "prefill_gemms": 246.57e6}
+
+
 def algo_bytes(n: int, k: int, t: int) -> int:
     return n * k * 5 // 8 + 2 * t * k + 2 * t * n
 
@@ -275,7 +282,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                        "algorithmic_bytes_per_step": sb},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "traffic": None, "kernel": "q4nx_gemv (x-prep + stream-K GEMV pairs, event-timed step)"},
+                         "traffic": MEASURED_TRAFFIC["gemv_step"],
+                         "traffic_source": "ncu launch list of the sweep step, all gemv_kernel launches",
+                         "kernel": "q4nx_gemv_kernel (20 launches per step, event-timed step)"},
             "e2e": {"value": round(world * sb / e2e_s / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "rc_gemv_host (synchronous per GEMV)"},
             "gpu_launches": launches_per_step * args.steps,
@@ -558,10 +567,12 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
                          "(L2 126 MB)" % (n_layers, touched / 1e6, (n_layers - 1) * touched / 1e6),
                    "cuda_graph": bool(int(ok.item())), "graph_error": graph_err},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": None,
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "traffic": MEASURED_TRAFFIC["moe_layer_t1"] if world == 1 and M == 1 else None,
+                     "traffic_source": "ncu capture of one moe_fused_kernel launch (T = 1)",
                      "per_rank_bytes_per_step": round(avg_rank_bytes),
-                     "kernel": "MoE layer step per rank (router+grouping, grouped gate/up GEMV, grouped down "
-                               "GEMV, combine; NCCL all-gather + reduce-scatter at N>1)"},
+                     "kernel": "MoE layer step per rank (one persistent kernel: router, top-k, grouped gate/up "
+                               "and down GEMVs, combine; NCCL all-gather + reduce-scatter at N>1)"},
         "e2e": {"value": round(world * M / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * M * H,
                 "d2h_bytes_per_step": 2 * M * H, "api": "ExpertParallelMoe.decode_host (synchronous)"},
         "gpu_launches": 4 * args.steps,
@@ -693,7 +704,9 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
                    "rank0_rows_per_step": round(avg[2]), "rank0_experts_hit": round(avg[3], 1)},
         "roofline": {"bound": "hbm" if hbm_frac >= tc_frac else "tensor",
                      "achieved": round(avg_bytes / (ms_max * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(hbm_frac, 4), "peak_source": peak_kind, "traffic": None,
+                     "frac": round(hbm_frac, 4), "peak_source": peak_kind,
+                     "traffic": MEASURED_TRAFFIC["prefill_gemms"] if world == 1 else None,
+                     "traffic_source": "ncu capture of the two pf_gemm_kernel launches of one layer",
                      "tensor_tflops": round(avg_flops / (ms_max * 1e-3) / 1e12, 1),
                      "tensor_peak_tflops": tflops_peak, "tensor_frac": round(tc_frac, 4),
                      "per_rank_bytes_per_step": round(avg_bytes), "per_rank_flops_per_step": round(avg_flops),
