@@ -553,6 +553,14 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
                "sample": f"{n_tok} decode tokens through the oracle's numpy MoE layer (router, 8 routed + "
                          f"shared SwiGLU experts, ascending-ID combine; host/backend.py:466-510, "
                          f"host/raon.py:1224-1327 restated), f32 weights cached (16 weight sets, id mod 16)"}
+    transport = "none" if world == 1 else eps[0].transport
+    if world == 1 or transport == "p2p":
+        per_step, kdesc = 1, "one persistent kernel: router, top-k, grouped gate/up and down GEMVs, combine" + (
+            "; token rows and expert rows exchanged over NVLink peer stores inside it" if world > 1 else "")
+    else:
+        per_step, kdesc = 2, ("persistent kernel (router, top-k, local experts) + combine, NCCL all-gather and "
+                              "reduce-scatter around them")
+    barrier()
     for ep in eps:
         ep.layer.close()
     res = {
@@ -565,17 +573,16 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
                    "l2": "each step uses the next of %d distinct layers with fixed tokens: the %.1f MB of "
                          "experts a step streams per rank come back after %.0f MB of other layers' experts "
                          "(L2 126 MB)" % (n_layers, touched / 1e6, (n_layers - 1) * touched / 1e6),
-                   "cuda_graph": bool(int(ok.item())), "graph_error": graph_err},
+                   "cuda_graph": bool(int(ok.item())), "graph_error": graph_err, "ep_transport": transport},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": MEASURED_TRAFFIC["moe_layer_t1"] if world == 1 and M == 1 else None,
                      "traffic_source": "ncu capture of one moe_fused_kernel launch (T = 1)",
                      "per_rank_bytes_per_step": round(avg_rank_bytes),
-                     "kernel": "MoE layer step per rank (one persistent kernel: router, top-k, grouped gate/up "
-                               "and down GEMVs, combine; NCCL all-gather + reduce-scatter at N>1)"},
+                     "kernel": f"MoE layer step per rank ({kdesc})"},
         "e2e": {"value": round(world * M / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * M * H,
                 "d2h_bytes_per_step": 2 * M * H, "api": "ExpertParallelMoe.decode_host (synchronous)"},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": per_step * args.steps,
         "clocks": clk,
         "cpu_baseline": cpu,
     }

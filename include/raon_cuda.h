@@ -199,6 +199,36 @@ int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int rout
 int rc_moe_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int T, int k,
                    int with_shared, uint16_t *out_dev, void *stream);
 
+/* Expert parallelism over peer memory (NVLink), the exchange inside the
+ * decode kernel (replaces the reference's expert-parallel all-gather /
+ * reduce-scatter around the local expert GEMVs, and the NCCL path through
+ * rc_moe_decode_local).  ``world`` ranks, one process per GPU and every GPU
+ * distinct (at most RC_EP_MAX_RANKS), each hold the routed experts
+ * [rank*E/world, (rank+1)*E/world) plus the shared expert and decode
+ * ``tokens_per_rank`` tokens per call (world * tokens_per_rank <= 16).
+ *
+ * rc_moe_ep_init allocates this rank's exchange buffer and writes an
+ * RC_EP_HANDLE_BYTES blob to handle_out (its CUDA IPC handle, the GPU's UUID
+ * and the geometry).  Once every rank has every blob, rc_moe_ep_open(peer)
+ * maps each other rank's buffer; it checks that the blob is that rank's, of
+ * the same geometry, and from a different GPU.  rc_moe_ep_decode is then one
+ * persistent kernel per call: the rank's token rows are stored into every
+ * peer's buffer, every rank routes all world*M tokens, computes its experts
+ * for every token and the shared expert for its own, stores each expert row
+ * straight into the buffer of the token's owner (exactly one rank writes each
+ * row) and combines its own tokens into out_dev [M][hidden] -- the bytes of
+ * rc_moe_decode on one GPU.  Every rank makes the same sequence of calls on
+ * one stream.  Every wait for a peer is bounded (1 s): the call then fails
+ * with RC_ERR_TIMEOUT at the next synchronising call, and the exchange state
+ * is lost -- rc_moe_ep_decode refuses until rc_moe_ep_init and
+ * rc_moe_ep_open are run again on every rank. */
+#define RC_EP_MAX_RANKS 8
+#define RC_EP_HANDLE_BYTES 128
+int rc_moe_ep_init(rc_moe *m, int rank, int world, int tokens_per_rank, void *handle_out);
+int rc_moe_ep_open(rc_moe *m, int peer, const void *handle);
+int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int renormalize, float scaling,
+                     int act, float gate_beta, float value_beta, uint16_t *out_dev, void *stream);
+
 /* MoE prefill: the layer for T <= 4096 tokens on the 5th-generation tensor
  * cores (tcgen05 grouped GEMM over expert-sorted token rows; the reference's
  * grouped path, npu/backend.py:4845-4979 with kernels/moe_grouped/

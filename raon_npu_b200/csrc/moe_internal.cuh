@@ -41,6 +41,48 @@ struct MoeOwned {
 
 struct PfScratch;   // prefill scratch (q4nx_prefill.cu)
 
+// Expert parallelism over peer memory: this rank's exchange buffer
+//   [0, kEpFlagBytes)  u64 counters: [0] token-row arrivals, [1] expert-row
+//                      arrivals (every rank adds 1 per call), [2] calls done
+//   tok                [world*M][hidden] bf16: every rank's token rows
+//   red                [M][kMoeMaxK+1][hidden] bf16: the expert rows of this
+//                      rank's tokens, each written by the rank that owns the
+//                      expert (slot k: the shared expert, written here)
+constexpr int kEpMaxRanks = 8;
+constexpr size_t kEpFlagBytes = 256;
+struct MoeEp {
+  int rank, world, M;
+  uint8_t *base;                    // this rank's exchange buffer
+  size_t bytes;
+  uint8_t *peer[kEpMaxRanks];       // every rank's buffer, mapped here (own: base)
+  bool mapped[kEpMaxRanks];
+  uint8_t uuid[kEpMaxRanks][16];    // the GPU each buffer lives on
+  uint8_t **peer_dev;               // device copy of peer[]
+  unsigned epoch;                   // ctx->timeout_epoch at rc_moe_ep_init
+};
+// The blob rc_moe_ep_init hands out: IPC handle, GPU UUID, geometry.
+struct MoeEpBlob {
+  uint8_t ipc[64];
+  uint8_t uuid[16];
+  int32_t rank, world, M, hidden, n_experts, has_shared;
+  uint64_t bytes;
+};
+static_assert(sizeof(MoeEpBlob) <= 128, "exchange blob exceeds RC_EP_HANDLE_BYTES");
+inline size_t ep_tok_off() { return kEpFlagBytes; }
+inline size_t ep_red_off(int world, int M, int hidden) { return kEpFlagBytes + (size_t)world * M * hidden * 2; }
+inline size_t ep_bytes(int world, int M, int hidden) {
+  return ep_red_off(world, M, hidden) + (size_t)M * (kMoeMaxK + 1) * hidden * 2;
+}
+
+// What the fused kernel needs of an expert-parallel call (null: one GPU).
+struct MoeEpArgs {
+  int rank, world, M;
+  uint8_t *const *peer_dev;
+  unsigned long long *flags;
+  uint32_t tok_off, red_off;
+  const uint16_t *x_own;
+};
+
 }  // namespace rc
 
 // ------------------------------------------------------------- MoE object --
@@ -60,6 +102,7 @@ struct rc_moe {
   int fused;                  // decode through the single persistent kernel when the shape fits
   unsigned long long *fz_bar; // grid-barrier arrival count of the fused kernel (only grows)
   unsigned fz_epoch;          // ctx->timeout_epoch when fz_bar was last known consistent
+  rc::MoeEp *ep;              // peer-memory expert parallelism (null until rc_moe_ep_init)
 };
 
 namespace rc {
@@ -68,9 +111,11 @@ void pf_free(rc_moe *m);   // releases m->pf (q4nx_prefill.cu)
 // logits [T][E] (each optional).
 // Fused decode (q4nx_moe_fused.cu).
 bool moe_fused_fits(const rc_moe *m, int T, int k, const MoeOwned &own);
+bool moe_fused_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own);
 int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling, int act,
                      float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign, uint16_t *out,
-                     int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s);
+                     int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s,
+                     const MoeEpArgs *ep = nullptr);
 int pf_route_tokens(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
                     int32_t *ids_dev, float *w_dev, float *logits_dev, void *stream);
 }  // namespace rc

@@ -867,6 +867,18 @@ int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_sha
   return RC_OK;
 }
 
+// Unmaps the peers' exchange buffers and frees this rank's.
+static void ep_release(rc_moe *m) {
+  MoeEp *ep = m->ep;
+  if (!ep) return;
+  for (int r = 0; r < ep->world; ++r)
+    if (r != ep->rank && ep->mapped[r]) cudaIpcCloseMemHandle(ep->peer[r]);
+  cudaFree(ep->base);
+  cudaFree(ep->peer_dev);
+  delete ep;
+  m->ep = nullptr;
+}
+
 int rc_moe_destroy(rc_moe *m) {
   if (!m) return RC_OK;
   cudaSetDevice(m->ctx->device);
@@ -895,6 +907,7 @@ int rc_moe_destroy(rc_moe *m) {
   cudaFree(m->act);
   cudaFree(m->down_out);
   cudaFree(m->fz_bar);
+  ep_release(m);
   delete m;
   return RC_OK;
 }
@@ -1101,6 +1114,126 @@ int rc_moe_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   return moe_combine(m, slot_out_dev, slot_w_dev, T, k, with_shared, out_dev, nullptr, nullptr,
                      pick_stream(m->ctx, stream));
+}
+
+int rc_moe_ep_init(rc_moe *m, int rank, int world, int tokens_per_rank, void *handle_out) {
+  RC_CHECK_ARG(m && handle_out, "rc_moe_ep_init: NULL argument");
+  RC_CHECK_ARG(world >= 2 && world <= kEpMaxRanks, "rc_moe_ep_init: world must be 2..%d", kEpMaxRanks);
+  RC_CHECK_ARG(rank >= 0 && rank < world, "rc_moe_ep_init: rank %d outside 0..%d", rank, world - 1);
+  RC_CHECK_ARG(tokens_per_rank >= 1 && world * tokens_per_rank <= kMoeMaxTokens,
+               "rc_moe_ep_init: world * tokens_per_rank must be 1..%d", kMoeMaxTokens);
+  RC_CHECK_ARG(m->n_experts >= world, "rc_moe_ep_init: %d experts cannot be split over %d ranks", m->n_experts,
+               world);
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  RC_CUDA_TRY(cudaDeviceSynchronize());
+  ep_release(m);
+  MoeEp *ep = new MoeEp();
+  ep->rank = rank;
+  ep->world = world;
+  ep->M = tokens_per_rank;
+  ep->bytes = ep_bytes(world, tokens_per_rank, m->hidden);
+  ep->epoch = m->ctx->timeout_epoch;
+  m->ep = ep;
+  cudaDeviceProp prop;
+  MoeEpBlob blob{};
+  cudaError_t e = cudaGetDeviceProperties(&prop, m->ctx->device);
+  if (e == cudaSuccess) e = cudaMalloc(&ep->base, ep->bytes);
+  if (e == cudaSuccess) e = cudaMemset(ep->base, 0, ep->bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&ep->peer_dev, kEpMaxRanks * sizeof(uint8_t *));
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, ep->base);
+  if (e != cudaSuccess) {
+    set_error("rc_moe_ep_init: %s", cudaGetErrorString(e));
+    ep_release(m);
+    return RC_ERR_CUDA;
+  }
+  ep->peer[rank] = ep->base;
+  ep->mapped[rank] = true;
+  memcpy(ep->uuid[rank], &prop.uuid, 16);
+  memcpy(blob.ipc, &h, sizeof(h));
+  memcpy(blob.uuid, &prop.uuid, 16);
+  blob.rank = rank;
+  blob.world = world;
+  blob.M = tokens_per_rank;
+  blob.hidden = m->hidden;
+  blob.n_experts = m->n_experts;
+  blob.has_shared = m->has_shared;
+  blob.bytes = ep->bytes;
+  memset(handle_out, 0, RC_EP_HANDLE_BYTES);
+  memcpy(handle_out, &blob, sizeof(blob));
+  return RC_OK;
+}
+
+int rc_moe_ep_open(rc_moe *m, int peer, const void *handle) {
+  RC_CHECK_ARG(m && handle, "rc_moe_ep_open: NULL argument");
+  MoeEp *ep = m->ep;
+  RC_CHECK_ARG(ep, "rc_moe_ep_open: rc_moe_ep_init has not run");
+  RC_CHECK_ARG(peer >= 0 && peer < ep->world, "rc_moe_ep_open: peer %d outside 0..%d", peer, ep->world - 1);
+  MoeEpBlob blob;
+  memcpy(&blob, handle, sizeof(blob));
+  if (peer == ep->rank) {
+    RC_CHECK_ARG(memcmp(blob.uuid, ep->uuid[peer], 16) == 0 && blob.rank == peer,
+                 "rc_moe_ep_open: the blob given for this rank is not its own");
+    return RC_OK;
+  }
+  RC_CHECK_ARG(!ep->mapped[peer], "rc_moe_ep_open: peer %d is already mapped", peer);
+  RC_CHECK_ARG(blob.rank == peer && blob.world == ep->world && blob.M == ep->M && blob.hidden == m->hidden &&
+                   blob.n_experts == m->n_experts && blob.has_shared == m->has_shared && blob.bytes == ep->bytes,
+               "rc_moe_ep_open: the blob of peer %d describes another rank or layer geometry", peer);
+  for (int r = 0; r < ep->world; ++r)
+    RC_CHECK_ARG(!ep->mapped[r] || memcmp(blob.uuid, ep->uuid[r], 16) != 0,
+                 "rc_moe_ep_open: peers %d and %d are on the same GPU (one rank per GPU)", peer, r);
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  cudaIpcMemHandle_t h;
+  memcpy(&h, blob.ipc, sizeof(h));
+  void *ptr = nullptr;
+  RC_CUDA_TRY(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  ep->peer[peer] = static_cast<uint8_t *>(ptr);
+  ep->mapped[peer] = true;
+  memcpy(ep->uuid[peer], blob.uuid, 16);
+  RC_CUDA_TRY(cudaMemcpy(ep->peer_dev, ep->peer, kEpMaxRanks * sizeof(uint8_t *), cudaMemcpyHostToDevice));
+  return RC_OK;
+}
+
+int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int renormalize, float scaling, int act,
+                     float gate_beta, float value_beta, uint16_t *out_dev, void *stream) {
+  RC_CHECK_ARG(m && x_dev && out_dev, "rc_moe_ep_decode: NULL argument");
+  MoeEp *ep = m->ep;
+  RC_CHECK_ARG(ep, "rc_moe_ep_decode: rc_moe_ep_init has not run");
+  for (int r = 0; r < ep->world; ++r)
+    RC_CHECK_ARG(ep->mapped[r], "rc_moe_ep_decode: the buffer of rank %d is not mapped (rc_moe_ep_open)", r);
+  if (ep->epoch != m->ctx->timeout_epoch) {
+    set_error("rc_moe_ep_decode: a bounded wait gave up since rc_moe_ep_init; the exchange counters are lost, "
+              "run rc_moe_ep_init and rc_moe_ep_open again on every rank");
+    return RC_ERR_TIMEOUT;
+  }
+  const int T = ep->world * ep->M;
+  RC_MOE_CHECK_TK("rc_moe_ep_decode");
+  RC_CHECK_ARG(act == RC_ACT_SWIGLU || act == RC_ACT_SITU, "unknown activation %d", act);
+  RC_CHECK_ARG(router == RC_ROUTER_SOFTMAX || router == RC_ROUTER_SIGMOID_BIAS, "unknown router %d", router);
+  RC_CHECK_ARG((reinterpret_cast<uintptr_t>(x_dev) & 15) == 0 && (reinterpret_cast<uintptr_t>(out_dev) & 15) == 0,
+               "rc_moe_ep_decode: x and out must be 16-byte aligned");
+  MoeOwned own;
+  own.lo = (int)((long long)ep->rank * m->n_experts / ep->world);
+  own.hi = (int)((long long)(ep->rank + 1) * m->n_experts / ep->world);
+  own.shared_mask = m->has_shared ? token_mask(ep->rank * ep->M, ep->M) : 0u;
+  int rc = check_loaded(m, own);
+  if (rc) return rc;
+  RC_CHECK_ARG(moe_fused_shape_ok(m, T, k, own),
+               "rc_moe_ep_decode: T=%d k=%d does not fit the persistent decode kernel", T, k);
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  MoeEpArgs a;
+  a.rank = ep->rank;
+  a.world = ep->world;
+  a.M = ep->M;
+  a.peer_dev = ep->peer_dev;
+  a.flags = reinterpret_cast<unsigned long long *>(ep->base);
+  a.tok_off = (uint32_t)ep_tok_off();
+  a.red_off = (uint32_t)ep_red_off(ep->world, ep->M, m->hidden);
+  a.x_own = x_dev;
+  return moe_fused_decode(m, reinterpret_cast<const uint16_t *>(ep->base + ep_tok_off()), T, k, router,
+                          renormalize, scaling, act, gate_beta, value_beta, own, m->down_out, 0, out_dev, nullptr,
+                          nullptr, nullptr, pick_stream(m->ctx, stream), &a);
 }
 
 }  // extern "C"

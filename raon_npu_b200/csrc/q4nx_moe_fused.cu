@@ -40,6 +40,10 @@ constexpr int kFzWarps = 16;
 constexpr int kFzThreads = kFzWarps * 32;
 constexpr int kFzMaxStages = 4;
 constexpr int kFzChunks = kMoeMaxExperts / 32;        // router values a lane holds per token
+// the "red" area: [16 warps][16 tokens] f64 partial logits, the barrier
+// verdict word, then the peer buffer table (8 pointers) and the two phase
+// ranges
+constexpr int kFzRedBytes = kFzWarps * kMoeMaxTokens * 8 + 16;
 
 struct MoeFusedParams {
   // tokens and router
@@ -70,6 +74,13 @@ struct MoeFusedParams {
   int off_stage, off_part, off_tab, off_sel, off_red, off_bar;
   unsigned long long *bar;           // grid-barrier arrival count (only grows)
   int *err;
+  // expert parallelism over peer memory (ep_world > 1): x is this rank's
+  // exchange buffer's token rows, out its own tokens' rows
+  int ep_world, ep_rank, ep_M;
+  uint8_t *const *ep_peer;           // [world] every rank's exchange buffer
+  unsigned long long *ep_flags;      // this rank's counters (token rows, expert rows, calls)
+  uint32_t ep_tok_off, ep_red_off;   // byte offsets in an exchange buffer
+  const uint16_t *ep_x_own;          // this rank's token rows [M][hidden]
 };
 
 // what build_activations reads
@@ -163,6 +174,28 @@ __device__ bool fz_grid_barrier(unsigned long long *bar, int *err, int *ok_s) {
   return *ok_s != 0;
 }
 
+// Wait until a counter that peer GPUs add to reaches ``target``.  Bounded:
+// false after 1 s (error word set), CTA-uniform.
+__device__ bool fz_wait_sys(const unsigned long long *ctr, unsigned long long target, int *err, int *ok_s) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    if (ld_acquire_sys(ctr) < target) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(ctr) < target) {
+        if (global_timer_ns() - t0 > 1000000000ull) {
+          ok = 0;
+          atomicCAS(err, 0, kErrWaitTimeout);
+          break;
+        }
+      }
+    }
+    *ok_s = ok;
+  }
+  __syncthreads();
+  return *ok_s != 0;
+}
+
 // One phase's units: tiles [c0, c0 + n_tiles) of the group-major tile list,
 // kb k-blocks each, rounds of R tiles (see RoundCursor).
 struct FzRange {
@@ -216,6 +249,7 @@ __device__ void fz_phase(const MoeFusedParams &p, uint8_t *smem, const FzRange *
                          const int *g_dst, int g_lo, FzRing &rg) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const FzRange &pr = ph[EPI];
+  uint8_t *const *ep_peer_s = reinterpret_cast<uint8_t *const *>(smem + p.off_red + kFzRedBytes);
   const int S = p.stages;
   const int kb = pr.kb, k = kb * kUnitK, R = pr.R, n_tiles = pr.n_tiles;
   uint8_t *ring = smem + warp * S * kUnitBytes;
@@ -290,7 +324,17 @@ __device__ void fz_phase(const MoeFusedParams &p, uint8_t *smem, const FzRange *
             }
             p.act[((size_t)grp * 8 * NTB + t) * p.inter_pad + tile * 8 + g] = f32_to_bf16_rne(v);
           } else {
-            uint16_t *y = p.slot_rows + (size_t)g_dst[grp * p.T + t] * p.hidden + tile * kUnitRows + g;
+            const int srow = g_dst[grp * p.T + t];     // slot row t*(k+1) + position
+            uint16_t *y;
+            if (p.ep_world > 1) {
+              // straight into the buffer of the token's owner
+              const int tt = srow / (p.k + 1), pos = srow - tt * (p.k + 1);
+              const int owner = tt / p.ep_M, tl = tt - owner * p.ep_M;
+              y = reinterpret_cast<uint16_t *>(ep_peer_s[owner] + p.ep_red_off) +
+                  ((size_t)tl * (p.k + 1) + pos) * p.hidden + tile * kUnitRows + g;
+            } else {
+              y = p.slot_rows + (size_t)srow * p.hidden + tile * kUnitRows + g;
+            }
             y[0] = live ? f32_to_bf16_rne(acc.v[tb][e2]) : (uint16_t)0;
             y[8] = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : (uint16_t)0;
           }
@@ -305,10 +349,33 @@ template <int NTB>
 __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   int *ok_s = reinterpret_cast<int *>(smem + p.off_red + kFzWarps * kMoeMaxTokens * 8);
+  uint8_t **ep_peer_s = reinterpret_cast<uint8_t **>(smem + p.off_red + kFzRedBytes);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = p.T, E = p.n_experts, k = p.k;
   const int gt_gu_i = p.inter / 8, kb_gu_i = p.hidden / kUnitK;
   const int gt_dn_i = p.hidden / kUnitRows, kb_dn_i = p.inter_pad / kUnitK;
+
+  // ---- expert parallelism: every rank's token rows into every rank's buffer
+  unsigned long long ep_calls = 0;
+  if (p.ep_world > 1) {
+    ep_calls = *reinterpret_cast<volatile unsigned long long *>(p.ep_flags + 2);
+    if (tid < p.ep_world) ep_peer_s[tid] = p.ep_peer[tid];
+    __syncthreads();
+    if (blockIdx.x == 0) {
+      const int n16 = p.ep_M * p.hidden / 8;
+      const uint4 *src = reinterpret_cast<const uint4 *>(p.ep_x_own);
+      for (int r = 0; r < p.ep_world; ++r) {
+        uint4 *dst = reinterpret_cast<uint4 *>(ep_peer_s[r] + p.ep_tok_off) + (size_t)p.ep_rank * n16;
+        for (int i = tid; i < n16; i += blockDim.x) dst[i] = src[i];
+      }
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence_system();
+        for (int r = 0; r < p.ep_world; ++r)
+          red_add_release_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r]) + 0, 1ull);
+      }
+    }
+  }
 
   // per-expert tables kept in shared memory for the whole kernel
   const uint8_t **all_gu = reinterpret_cast<const uint8_t **>(smem + p.off_tab);    // [E+1]
@@ -332,6 +399,8 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
   // warps without router columns fetch the tables while the others compute
   if (busy < kFzWarps && warp >= busy) load_tables(tid - busy * 32, (kFzWarps - busy) * 32);
 
+  if (p.ep_world > 1 && !fz_wait_sys(p.ep_flags + 0, (ep_calls + 1) * p.ep_world, p.err, ok_s)) return;
+
   // ------------------------------------------------------------ 1 logits
   {
     double *red = reinterpret_cast<double *>(smem + p.off_red);     // [16 warps][16 tokens]
@@ -345,7 +414,7 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
         uint4 xv[kMoeMaxTokens];
 #pragma unroll
         for (int t = 0; t < kMoeMaxTokens; ++t)
-          if (t < T) xv[t] = *reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.hidden + col);
+          if (t < T) xv[t] = __ldcg(reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.hidden + col));
         const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
         double wd[8];
 #pragma unroll
@@ -496,7 +565,7 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
   const uint32_t bar0 = smem_addr(smem + p.off_bar) + warp * S * 8;
   // the two phases' ranges: per-CTA constants in shared memory (indexed by
   // the ring's current phase at run time)
-  FzRange *ph = reinterpret_cast<FzRange *>(smem + p.off_red + kFzWarps * kMoeMaxTokens * 8 + 16);
+  FzRange *ph = reinterpret_cast<FzRange *>(smem + p.off_red + kFzRedBytes + kEpMaxRanks * 8);
   if (tid == 0) {
     ph[0] = FzRange{g_gu, c0_gu, nt_gu, p.round_gu, kb_gu_i, make_fastdiv(gt_gu_i)};
     ph[1] = FzRange{g_dn, c0_dn, nt_dn, p.round_dn, kb_dn_i, make_fastdiv(gt_dn_i)};
@@ -550,15 +619,31 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
     fz_phase<kFzDown, NTB>(p, smem, ph, g_mask, g_dst, g_lo, rg);
     failed = __syncthreads_or(rg.failed) != 0;
   }
+  if (p.ep_world > 1 && tid == 0) __threadfence_system();   // this CTA's rows to peers, before the barrier
   if (!failed && !fz_grid_barrier(p.bar, p.err, ok_s)) failed = true;
+  if (p.ep_world > 1 && !failed) {
+    // every rank's rows for this rank's tokens have been written once every
+    // rank has passed its own barrier 3 and signalled
+    if (blockIdx.x == 0 && tid == 0) {
+      __threadfence_system();
+      for (int r = 0; r < p.ep_world; ++r)
+        red_add_release_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r]) + 1, 1ull);
+    }
+    if (!fz_wait_sys(p.ep_flags + 1, (ep_calls + 1) * p.ep_world, p.err, ok_s)) failed = true;
+  }
 
   // ------------------------------------------------------------ 5 combine
   if (!failed && p.out) {
     const int vecs = p.hidden / 8;
     const bool with_shared = p.shared_id >= 0 && p.own.shared_mask;
-    for (int i = blockIdx.x * blockDim.x + tid; i < T * vecs; i += gridDim.x * blockDim.x) {
-      const int t = i / vecs, v = i - t * vecs;
-      const uint16_t *rows = p.slot_rows + (size_t)t * (k + 1) * p.hidden + (size_t)v * 8;
+    const bool ep = p.ep_world > 1;
+    const int n_out = ep ? p.ep_M : T;             // tokens combined here
+    const uint16_t *ep_rows = ep ? reinterpret_cast<const uint16_t *>(ep_peer_s[p.ep_rank] + p.ep_red_off) : nullptr;
+    for (int i = blockIdx.x * blockDim.x + tid; i < n_out * vecs; i += gridDim.x * blockDim.x) {
+      const int to = i / vecs, v = i - to * vecs;      // output row
+      const int t = ep ? p.ep_rank * p.ep_M + to : to;  // token of the call
+      const uint16_t *rows = (ep ? ep_rows + (size_t)to * (k + 1) * p.hidden : p.slot_rows + (size_t)t * (k + 1) * p.hidden) +
+                             (size_t)v * 8;
       float acc[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
@@ -586,9 +671,11 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
         }
         o[j] = lo | (hi << 16);
       }
-      *reinterpret_cast<uint4 *>(p.out + (size_t)t * p.hidden + (size_t)v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4 *>(p.out + (size_t)to * p.hidden + (size_t)v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
+  if (p.ep_world > 1 && !failed && blockIdx.x == 0 && tid == 0)
+    *reinterpret_cast<volatile unsigned long long *>(p.ep_flags + 2) = ep_calls + 1;
   // after a failure, the copies still in flight land before the CTA's shared
   // memory is released (ring indices consumed .. issued-1)
   if (failed && lane == 0) {
@@ -626,7 +713,7 @@ static bool fz_layout(const rc_moe *m, int T, int k, const MoeOwned &own, FzLayo
   const size_t tab = (size_t)(E + 1) * (4 * 8 + 4 + 4 + 4 + 4 * T) + 16;   // expert and group tables
   const size_t sel = (size_t)T * (k + 1) * 4 + (size_t)T * k * 4;
   // + the barrier verdict word and the two phase ranges
-  const size_t red = (size_t)kFzWarps * kMoeMaxTokens * 8 + 16 + 2 * sizeof(FzRange);
+  const size_t red = (size_t)kFzRedBytes + kEpMaxRanks * 8 + 2 * sizeof(FzRange);
   const int unit_part = ntb * 32 * 16;
   for (int S = kFzMaxStages; S >= 2; --S) {
     for (int cap = kMoePartialBytes; cap >= 4 * 1024; cap /= 2) {
@@ -658,10 +745,15 @@ static bool fz_layout(const rc_moe *m, int T, int k, const MoeOwned &own, FzLayo
   return false;
 }
 
-// Whether the fused kernel takes this call: the shared-memory layout fits and
-// a CTA's down range touches at most kMoeMaxGroupsPerCta groups.
+// Whether the fused kernel takes this call: it is switched on (rc_moe_set_fused)
+// and the shape is one it can run.
 bool moe_fused_fits(const rc_moe *m, int T, int k, const MoeOwned &own) {
-  if (!m->fused) return false;
+  return m->fused && moe_fused_shape_ok(m, T, k, own);
+}
+
+// Whether the fused kernel can run this shape: the shared-memory layout fits
+// and a CTA's down range touches at most kMoeMaxGroupsPerCta groups.
+bool moe_fused_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own) {
   FzLayout L;
   if (!fz_layout(m, T, k, own, &L)) return false;
   const int max_groups = fz_max_groups(T, k, own);
@@ -672,11 +764,13 @@ bool moe_fused_fits(const rc_moe *m, int T, int k, const MoeOwned &own) {
 
 // Runs the layer (out != null: combined rows into out) or its
 // expert-parallel local half (out == null: slot rows, zeroed where another
-// rank computes them, and the slot weights).  The caller checked
+// rank computes them, and the slot weights).  With ep, x is this rank's
+// exchange buffer's token rows (every rank's tokens once the kernel has
+// exchanged them), out this rank's own M rows.  The caller checked
 // moe_fused_fits.
 int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling, int act,
                      float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign, uint16_t *out,
-                     int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s) {
+                     int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s, const MoeEpArgs *ep) {
   const int ntb = T <= 8 ? 1 : 2;
   FzLayout L;
   if (!fz_layout(m, T, k, own, &L)) {
@@ -734,6 +828,17 @@ int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int
   p.off_bar = L.off_bar;
   p.bar = m->fz_bar;
   p.err = ctx->err;
+  p.ep_world = 1;
+  if (ep) {
+    p.ep_world = ep->world;
+    p.ep_rank = ep->rank;
+    p.ep_M = ep->M;
+    p.ep_peer = ep->peer_dev;
+    p.ep_flags = ep->flags;
+    p.ep_tok_off = ep->tok_off;
+    p.ep_red_off = ep->red_off;
+    p.ep_x_own = ep->x_own;
+  }
   static bool configured[64][2] = {};
   int dev = 0;
   RC_CUDA_TRY(cudaGetDevice(&dev));

@@ -117,6 +117,17 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
   return v;
 }
 
+// System scope (peer GPUs over NVLink): a releasing add to a counter in
+// another GPU's memory, and an acquiring load of a counter peers add to.
+__device__ __forceinline__ void red_add_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Division by a divisor fixed for a loop: q = umulhi(n, ceil(2^32 / d)),
 // exact while n * d < 2^32 (the callers' tile and unit indices stay below
 // 2^20 and their divisors below 2^12).

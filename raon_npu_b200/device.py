@@ -388,6 +388,35 @@ class MoeLayer:
             int(shared_tokens[1]), ctypes.c_void_p(_ptr(slot_out_dev)), ctypes.c_void_p(_ptr(slot_w_dev)),
             ctypes.c_void_p(_stream_for(stream, x_dev, slot_out_dev))), "rc_moe_decode_local")
 
+    # -- expert parallelism over peer memory ------------------------------
+    EP_HANDLE_BYTES = 128
+
+    def ep_init(self, rank: int, world: int, tokens_per_rank: int) -> bytes:
+        """Allocates this rank's exchange buffer; returns the blob (IPC handle,
+        GPU UUID, geometry) every other rank passes to ``ep_open``."""
+        blob = ctypes.create_string_buffer(self.EP_HANDLE_BYTES)
+        check(self.ctx.lib.rc_moe_ep_init(self.handle, int(rank), int(world), int(tokens_per_rank),
+                                          ctypes.cast(blob, ctypes.c_void_p)), "rc_moe_ep_init")
+        return blob.raw
+
+    def ep_open(self, peer: int, blob: bytes) -> None:
+        """Maps rank ``peer``'s exchange buffer (a no-op check for this rank's own blob)."""
+        if len(blob) != self.EP_HANDLE_BYTES:
+            raise ValueError(f"an exchange blob has {self.EP_HANDLE_BYTES} bytes")
+        buf = ctypes.create_string_buffer(bytes(blob), self.EP_HANDLE_BYTES)
+        check(self.ctx.lib.rc_moe_ep_open(self.handle, int(peer), ctypes.cast(buf, ctypes.c_void_p)),
+              "rc_moe_ep_open")
+
+    def ep_decode(self, x_dev, k: int, out_dev, router: str = "softmax", renormalize: bool = True,
+                  scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0, value_beta: float = 25.0,
+                  stream: int | None = None) -> None:
+        """This rank's tokens x [M, hidden] -> out [M, hidden], the exchange with
+        the other ranks inside the kernel (every rank calls it together)."""
+        check(self.ctx.lib.rc_moe_ep_decode(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), int(k), ROUTER_CODES[router], int(bool(renormalize)),
+            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(_ptr(out_dev)),
+            ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_ep_decode")
+
     def prefill(self, x_dev, k: int, out_dev, ids_dev=None, w_dev=None, router: str = "softmax",
                 renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
                 value_beta: float = 25.0, stream: int | None = None) -> None:

@@ -23,6 +23,14 @@ The result of every token is byte-identical to the single-GPU decode
 (``MoeLayer.decode``): each expert's rows come out of whole-tile GEMVs whose
 columns do not interact, the exchange is exact and the combine is the same
 kernel.  Two collectives per layer, each a few KB per token.
+
+Transport ``"p2p"`` (the default on NCCL groups whose ranks sit on distinct
+GPUs) does all four steps in one persistent kernel per rank
+(``MoeLayer.ep_decode``): every rank stores its token rows into every rank's
+exchange buffer over NVLink, and each expert row straight into the buffer of
+the token's owner -- no collective launches, no zero rows, no sum.  The
+buffers are CUDA IPC mappings set up once per token count with one
+``all_gather`` of the ranks' handles.  ``"nccl"`` keeps the collectives.
 """
 
 from __future__ import annotations
@@ -45,7 +53,8 @@ class ExpertParallelMoe:
     """
 
     def __init__(self, layer, k: int, group=None, act: str = "swiglu", router: str = "softmax",
-                 renormalize: bool = True, scaling: float = 1.0, gate_beta: float = 4.0, value_beta: float = 25.0):
+                 renormalize: bool = True, scaling: float = 1.0, gate_beta: float = 4.0, value_beta: float = 25.0,
+                 transport: str = "auto"):
         import torch.distributed as dist
         self.layer = layer
         self.k = int(k)
@@ -60,6 +69,49 @@ class ExpertParallelMoe:
         self.kw = dict(router=router, renormalize=renormalize, scaling=scaling, act=act, gate_beta=gate_beta,
                        value_beta=value_beta)
         self._bufs: dict = {}
+        if transport not in ("auto", "p2p", "nccl"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
+        self._ep_M = None               # token count the peer buffers are set up for (p2p)
+
+    def _use_p2p(self, M: int) -> bool:
+        """Whether this call goes through the in-kernel peer exchange; sets the
+        buffers up (collectively) the first time a token count is seen."""
+        import torch
+        import torch.distributed as dist
+        if self.transport == "nccl" or self.world == 1:
+            return False
+        if self._ep_M == M:
+            return True
+        if self.transport == "auto" and (dist.get_backend(self.group) != "nccl" or self.world * M > 16
+                                         or not hasattr(self.layer, "ep_init")):
+            return False
+        dev = torch.device("cuda", torch.cuda.current_device())
+        nb = self.layer.EP_HANDLE_BYTES
+        mine = torch.zeros(nb, dtype=torch.uint8, device=dev)
+        ok, why = 1, ""
+        try:
+            mine.copy_(torch.frombuffer(bytearray(self.layer.ep_init(self.rank, self.world, M)), dtype=torch.uint8))
+        except Exception as e:          # every rank still takes the collective steps below
+            ok, why = 0, str(e)
+        blobs = torch.empty(self.world * nb, dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(blobs, mine, group=self.group)
+        if ok:
+            host = blobs.cpu().numpy().tobytes()
+            try:
+                for r in range(self.world):
+                    self.layer.ep_open(r, host[r * nb:(r + 1) * nb])
+            except Exception as e:
+                ok, why = 0, str(e)
+        flag = torch.tensor([ok], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        if int(flag.item()) == 0:
+            if self.transport == "p2p":
+                raise RuntimeError(f"peer-memory expert parallelism unavailable: {why or 'failed on another rank'}")
+            self.transport = "nccl"
+            return False
+        self._ep_M = M
+        return True
 
     def owns(self, expert: int) -> bool:
         """Experts this rank loads: its routed range and the shared expert (id E)."""
@@ -82,6 +134,9 @@ class ExpertParallelMoe:
         N, k = self.world, self.k
         if N == 1:                      # nothing to exchange: the single-GPU layer
             self.layer.decode(x, k, out, **self.kw)
+            return
+        if self._use_p2p(M):
+            self.layer.ep_decode(x, k, out, **self.kw)
             return
         T = N * M
         dev = x.device

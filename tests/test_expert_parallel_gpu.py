@@ -1,10 +1,16 @@
-"""Expert-parallel MoE decode over NCCL on 2+ GPUs of one box.
+"""Expert-parallel MoE decode on 2+ GPUs of one box.
 
 Each rank (one process per GPU) holds E/N routed experts and the shared
-expert and decodes its own tokens through ``ExpertParallelMoe`` (NCCL
-all-gather, grouped expert GEMVs, NCCL reduce-scatter, combine).  Every
-rank's output must equal, byte for byte, the single-GPU ``MoeLayer.decode``
-of the same tokens with all experts loaded.  Skipped with fewer than 2 GPUs.
+expert and decodes its own tokens through ``ExpertParallelMoe``, over both
+transports: ``"nccl"`` (all-gather, grouped expert GEMVs, reduce-scatter,
+combine) and ``"p2p"`` (one persistent kernel that exchanges token and expert
+rows through the ranks' peer-mapped buffers).  Every rank's output must
+equal, byte for byte, the single-GPU ``MoeLayer.decode`` of the same tokens
+with all experts loaded.  The p2p case also makes a peer wait run out on
+purpose -- rank 1 skips one call, so rank 0's kernel waits for token rows
+that never come -- and checks that rank 0 gets the timeout status after the
+1 s bound and that the layer then refuses further exchange calls.  Skipped
+with fewer than 2 GPUs.
 """
 
 from __future__ import annotations
@@ -45,7 +51,7 @@ def _layer(torch, ctx, owned):
     return layer
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, transport):
     import datetime
     import torch
     import torch.distributed as dist
@@ -61,7 +67,7 @@ def _worker(rank, world, port, out_dir):
         ctx = Context(rank)
         per = E // world
         layer = _layer(torch, ctx, set(range(rank * per, (rank + 1) * per)) | {E})
-        ep = ExpertParallelMoe(layer, K, act="swiglu")
+        ep = ExpertParallelMoe(layer, K, act="swiglu", transport=transport)
         full = _layer(torch, ctx, set(range(E + 1)))
         gen = torch.Generator(device="cuda")
         res = []
@@ -77,6 +83,24 @@ def _worker(rank, world, port, out_dir):
         host = ep.decode_host(x.cpu().numpy().view(np.uint16))
         res.append(bool(np.array_equal(host, ref.cpu().numpy().view(np.uint16))))
         ctx.sync()
+        if transport == "p2p":
+            res.append(ep._ep_M == M)           # the peer path really ran
+            dist.barrier()
+            # rank 1 skips this call: rank 0's wait for its token rows runs out
+            if rank == 0:
+                layer.ep_decode(x, K, out, act="swiglu")
+                try:
+                    ctx.sync()
+                    res.append(False)
+                except RuntimeError as e:
+                    res.append("bounded wait" in str(e))
+                try:
+                    layer.ep_decode(x, K, out, act="swiglu")
+                    res.append(False)
+                except RuntimeError as e:
+                    res.append("rc_moe_ep_init" in str(e))
+            torch.cuda.synchronize()
+            dist.barrier()
         np.save(os.path.join(out_dir, f"ok{rank}.npy"), np.array(res))
         layer.close()
         full.close()
@@ -86,13 +110,15 @@ def _worker(rank, world, port, out_dir):
 
 
 @pytest.mark.timeout(600)
-def test_expert_parallel_nccl_matches_single_gpu_bytes(tmp_path):
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_expert_parallel_matches_single_gpu_bytes(tmp_path, transport):
     import torch
     import torch.multiprocessing as mp
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), transport), nprocs=world,
+                       start_method="spawn")
     for r in range(world):
         ok = np.load(tmp_path / f"ok{r}.npy")
         assert ok.all(), (r, ok)
