@@ -396,7 +396,9 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(PfPlanParams p) {
 }
 
 // ---------------------------------------------------------- grouped GEMM --
-enum PfEpi : int { kPfEpiGlu = 0, kPfEpiDown = 1 };
+// epilogues: the GLU of gate/up with either activation (one per kernel, so
+// only one activation body is compiled into it), or the plain down rows
+enum PfEpi : int { kPfEpiSwiglu = 0, kPfEpiSitu = 1, kPfEpiDown = 2 };
 
 struct PfGemmParams {
   const uint8_t *const *expert_tiles;   // [E+1] t16 tiles (null: not loaded)
@@ -465,7 +467,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
       srow[j] = nullptr;
       if (r < n) {
         const int prow = row0 + r;
-        const int srcr = EPI == kPfEpiGlu ? p.row_token[prow] : prow;
+        const int srcr = EPI != kPfEpiDown ? p.row_token[prow] : prow;
         srow[j] = p.src + (size_t)srcr * p.ld_src;
       }
     }
@@ -577,13 +579,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
       if (tid == 0) {
         const uint8_t *sB = sm + kPfB + st * kPfBStage;
         const uint32_t idesc = umma_idesc_bf16(kPfRows, n16);
-#pragma unroll 1
+        // descriptors advance by (byte offset >> 4) in their start-address
+        // field (no carry: shared addresses stay below 256 KB).  One thread
+        // issues an MMA only every ~60 cycles, so the issue loop is kept to an
+        // add per operand.
+        const uint64_t da = umma_desc_sw128(smem_addr(sA)), db = umma_desc_sw128(smem_addr(sB));
+#pragma unroll
         for (int g = 0; g < kPfGroups; ++g) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int k0 = g * 32 + h * 16, sub = k0 >> 6, kk = k0 & 63;
-            umma_bf16(tbase + g * kPfCols, umma_desc_sw128(smem_addr(sA + sub * kPfASub) + kk * 2),
-                      umma_desc_sw128(smem_addr(sB + sub * kPfBSub) + kk * 2), idesc, (uint32_t)h);
+            umma_bf16(tbase + g * kPfCols, da + (uint64_t)((sub * kPfASub + kk * 2) >> 4),
+                      db + (uint64_t)((sub * kPfBSub + kk * 2) >> 4), idesc, (uint32_t)h);
           }
         }
         umma_commit(bar_mma);
@@ -601,15 +608,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
       for (int g = 0; g < kPfGroups; ++g) {
         const float sgl = sc[g], a3 = mp[g];
         const float *Sg = sS + g * kPfCols + 32 * ch;
+        if (32 * ch < n16) {
+          // both 16-column halves in flight before one wait
+          uint32_t v[2][16];
+          const uint32_t ta = tbase + ((uint32_t)(32 * lq) << 16) + g * kPfCols + 32 * ch;
+          tmem_ld16(ta, v[0]);
+          if (32 * ch + 16 < n16) tmem_ld16(ta + 16, v[1]);
+          tmem_wait_ld();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (32 * ch + 16 * h < n16) {
-            uint32_t v[16];
-            tmem_ld16(tbase + ((uint32_t)(32 * lq) << 16) + g * kPfCols + 32 * ch + 16 * h, v);
-            tmem_wait_ld();
+          for (int h = 0; h < 2; ++h) {
+            if (32 * ch + 16 * h < n16) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              acc[16 * h + j] = fmaf(sgl, __uint_as_float(v[j]), fmaf(a3, Sg[16 * h + j], acc[16 * h + j]));
+              for (int j = 0; j < 16; ++j)
+                acc[16 * h + j] = fmaf(sgl, __uint_as_float(v[h][j]), fmaf(a3, Sg[16 * h + j], acc[16 * h + j]));
+            }
           }
         }
       }
@@ -618,7 +630,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
     }
     if (failed) break;
     // ---- epilogue: this warp's 32 token columns
-    if (EPI == kPfEpiGlu) {
+    if (EPI != kPfEpiDown) {
       const int col = 8 * (8 * m + u_row) + rr;       // rows rr < 8: gate, rr >= 8: up of the same column
 #pragma unroll
       for (int t = 0; t < kPfCols / 2; ++t) {
@@ -627,7 +639,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
         if (rr < 8 && tok < n) {
           const float gate = bf16_round(acc[t]);
           const float u = bf16_round(up);
-          const float v = p.act == RC_ACT_SITU ? act_situ(gate, u, p.gate_beta, p.value_beta) : act_swiglu(gate, u);
+          const float v = EPI == kPfEpiSitu ? act_situ(gate, u, p.gate_beta, p.value_beta) : act_swiglu(gate, u);
           p.y[(size_t)(row0 + tok) * p.ld_y + col] = f32_to_bf16_rne(v);
         }
       }
@@ -863,7 +875,10 @@ static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t
   g.gate_beta = r.gb;
   g.value_beta = r.vb;
   g.err = m->ctx->err;
-  RC_CUDA_TRY(pf_launch_gemm<kPfEpiGlu>(m->ctx, g, s));
+  if (r.act == RC_ACT_SITU)
+    RC_CUDA_TRY(pf_launch_gemm<kPfEpiSitu>(m->ctx, g, s));
+  else
+    RC_CUDA_TRY(pf_launch_gemm<kPfEpiSwiglu>(m->ctx, g, s));
   PfGemmParams d = g;
   d.expert_tiles = m->dn_tiles;
   d.kb = m->inter_pad / kUnitK;
