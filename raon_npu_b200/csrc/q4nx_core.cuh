@@ -106,19 +106,17 @@ __device__ __forceinline__ float warp_absmax(const float (&v)[8]) {
   return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
 }
 
-// Build the fragment-ordered activations and their aux words for all token
-// slots of ntb blocks.  Called by every thread of the CTA (or grid); ``stride``
-// threads cooperate, ``first`` and ``stride`` multiples of 32 apart per warp,
-// so a warp's 32 consecutive items are exactly one (slot, 256-column block):
-// the block maximum is a warp reduction.  Each group of 32 columns is summed
-// as four sequential 8-element partials combined pairwise, a fixed order.
 // One staged item: eight activations v of a slot (one warp = one 256-column
 // block of that slot): block scale, f16 fragment words, group sums, aux words.
-template <class P>
-__device__ __forceinline__ void stage_item(const P &p, float (&v)[8], int slot, int c8, int k64, uint32_t *xf,
+// Each group of 32 columns is summed as four sequential 8-element partials
+// combined pairwise, a fixed order.  BF16: v came from bf16 input (slot =
+// token); otherwise from f32 input, odd slots holding the residual of the
+// even slot's f16 value.
+template <bool BF16>
+__device__ __forceinline__ void stage_core(float (&v)[8], int slot, int c8, int k64, int kb, uint32_t *xf,
                                            uint16_t *bmin16, float *inv) {
   int s = block_shift(warp_absmax(v));
-  if (p.x_dtype != RC_DTYPE_BF16 && (slot & 1)) {
+  if (!BF16 && (slot & 1)) {
     // the residual of the hi slot's f16 value, with its own block scale
     const float sc = pow2f(s), isc = pow2f(-s);
 #pragma unroll
@@ -133,7 +131,7 @@ __device__ __forceinline__ void stage_item(const P &p, float (&v)[8], int slot, 
     const float a = v[2 * i] * sc, c = v[2 * i + 1] * sc;
     const __half2 h = __floats2half2_rn(a, c);
     hw[i] = *reinterpret_cast<const uint32_t *>(&h);
-    if (p.x_dtype == RC_DTYPE_BF16) {
+    if (BF16) {
       // a bf16 value times 2^s is exact in f16 (down to the f16 subnormal
       // range, 2^-29 of the block maximum): sum the exact values
       part += a;
@@ -153,7 +151,7 @@ __device__ __forceinline__ void stage_item(const P &p, float (&v)[8], int slot, 
   part += __shfl_xor_sync(0xffffffffu, part, 2);
   if ((c8 & 3) == 0) {
     const int grp = c8 >> 2, kbi = grp >> 3, gi = grp & 7;
-    const size_t u = (size_t)tb * p.kb + kbi;
+    const size_t u = (size_t)tb * kb + kbi;
     const float sp = part * 5.9604644775390625e-08f;   // S' 2^-24 (exact)
     const uint16_t s1 = f32_to_bf16_rne(sp);
     const float r1 = sp - bf16_to_f32(s1);
@@ -164,18 +162,38 @@ __device__ __forceinline__ void stage_item(const P &p, float (&v)[8], int slot, 
     w[4] = f32_to_bf16_rne(r1 - bf16_to_f32(s2));
     w[6] = 0;
   }
-  if ((c8 & 31) == 0) inv[((size_t)tb * p.kb + (c8 >> 5)) * 8 + g] = pow2f(-s);
+  if ((c8 & 31) == 0) inv[((size_t)tb * kb + (c8 >> 5)) * 8 + g] = pow2f(-s);
 }
+
+// A staged bf16 item as an out-of-line call: the batched loop below calls it
+// from several unrolled sites; one body keeps a kernel with many phases small
+// enough for the instruction cache.
+static __device__ __noinline__ void stage_item_bf16(uint4 raw, int slot, int c8, int k64, int kb, uint32_t *xf,
+                                             uint16_t *bmin16, float *inv) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = bf16_lo_f32(w[i]);
+    v[2 * i + 1] = bf16_hi_f32(w[i]);
+  }
+  stage_core<true>(v, slot, c8, k64, kb, xf, bmin16, inv);
+}
+
+// How a build_activations instance is compiled: either input dtype (by
+// p.x_dtype) with the item code inline (the GEMV kernels: fastest), or bf16
+// input only with one out-of-line item body (the persistent decode kernel,
+// whose many phases must share the instruction cache).
+enum StageMode : int { kStageAny = 0, kStageBf16Compact = 1 };
 
 // Build the fragment-ordered activations and their aux words for all token
 // slots of ntb blocks.  Called by every thread of the CTA (or grid); ``stride``
 // threads cooperate, ``first`` and ``stride`` multiples of 32 apart per warp,
 // so a warp's 32 consecutive items are exactly one (slot, 256-column block):
-// the block maximum is a warp reduction.  Each group of 32 columns is summed
-// as four sequential 8-element partials combined pairwise, a fixed order.
-// A thread issues the loads of a batch of items before processing any (one
-// memory round trip per batch): 8 packed bf16 items, or 4 f32 items.
-template <bool SHARED, class P>
+// the block maximum is a warp reduction.  A thread issues the loads of a batch
+// of items before processing any (one memory round trip per batch): 8 packed
+// bf16 items, or 4 f32 items.
+template <bool SHARED, class P, int DT = kStageAny>
 __device__ __forceinline__ void build_activations(const P &p, int ntb, uint32_t *xf, void *aux, long long first,
                                                   long long stride) {
   const int k = p.kb * kUnitK, k64 = k / 64, c8n = k / 8;
@@ -187,7 +205,7 @@ __device__ __forceinline__ void build_activations(const P &p, int ntb, uint32_t 
   // 32-bit indices: slots <= 32 and K / 8 < 2^20, so total < 2^25
   const int total = p.slots * c8n;   // multiple of 32: whole warps iterate together
   const int first32 = (int)first, stride32 = (int)stride;
-  if (p.x_dtype == RC_DTYPE_BF16) {
+  if (DT == kStageBf16Compact || p.x_dtype == RC_DTYPE_BF16) {
     constexpr int kBatch = 8;
     for (int base0 = first32; base0 < total; base0 += stride32 * kBatch) {
       uint4 raw[kBatch];
@@ -215,18 +233,23 @@ __device__ __forceinline__ void build_activations(const P &p, int ntb, uint32_t 
         const int idx = base0 + b * stride32;
         if (idx >= total) break;
         const int slot = idx / c8n, c8 = idx - slot * c8n;
-        const uint32_t w[4] = {raw[b].x, raw[b].y, raw[b].z, raw[b].w};
-        float v[8];
+        if (DT == kStageBf16Compact) {
+          stage_item_bf16(raw[b], slot, c8, k64, p.kb, xf, bmin16, inv);
+        } else {
+          const uint32_t w[4] = {raw[b].x, raw[b].y, raw[b].z, raw[b].w};
+          float v[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          v[2 * i] = bf16_lo_f32(w[i]);
-          v[2 * i + 1] = bf16_hi_f32(w[i]);
+          for (int i = 0; i < 4; ++i) {
+            v[2 * i] = bf16_lo_f32(w[i]);
+            v[2 * i + 1] = bf16_hi_f32(w[i]);
+          }
+          stage_core<true>(v, slot, c8, k64, p.kb, xf, bmin16, inv);
         }
-        stage_item(p, v, slot, c8, k64, xf, bmin16, inv);
       }
     }
     return;
   }
+  if (DT == kStageBf16Compact) return;
   constexpr int kBatch = 4;
   for (int base0 = first32; base0 < total; base0 += stride32 * kBatch) {
     float v[kBatch][8];
@@ -243,7 +266,7 @@ __device__ __forceinline__ void build_activations(const P &p, int ntb, uint32_t 
       const int idx = base0 + b * stride32;
       if (idx >= total) break;
       const int slot = idx / c8n, c8 = idx - slot * c8n;
-      stage_item(p, v[b], slot, c8, k64, xf, bmin16, inv);
+      stage_core<false>(v[b], slot, c8, k64, p.kb, xf, bmin16, inv);
     }
   }
 }

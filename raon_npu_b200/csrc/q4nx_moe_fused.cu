@@ -99,6 +99,28 @@ __device__ __forceinline__ uint32_t route_key(float v) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+// An expert's routing score and its router-order key: sigmoid(logit)
+// (selected by score + bias), or the biased logit (softmax router; bias zero
+// unless set).  Out of line: the unrolled selection calls it for each of a
+// lane's experts, and one copy of the f64 exponential keeps the code small.
+struct FzScore {
+  uint32_t key;
+  float score;
+};
+static __device__ __noinline__ FzScore fz_score(float l, float bias, int mode) {
+  FzScore r;
+  float v;
+  if (mode == RC_ROUTER_SIGMOID_BIAS) {
+    r.score = __double2float_rn(1.0 / (1.0 + exp(-(double)l)));
+    v = r.score + bias;
+  } else {
+    r.score = l + bias;
+    v = r.score;
+  }
+  r.key = route_key(v);
+  return r;
+}
+
 // The group table of the ascending-ID slot lists, built by the whole CTA
 // (the same table as build_groups): one group per expert of [own.lo, own.hi)
 // that some token chose, ascending, then the shared expert for the tokens of
@@ -240,6 +262,11 @@ __device__ __forceinline__ void fz_issue(FzRing &rg, const FzRange *ph, int warp
 
 enum FzEpi : int { kFzGlu = 0, kFzDown = 1 };
 
+// The GLU activation, out of line (one body for the epilogue's unrolled sites).
+static __device__ __noinline__ float fz_glu(float gate, float up, int kind, float gb, float vb) {
+  return kind == RC_ACT_SITU ? act_situ(gate, up, gb, vb) : act_swiglu(gate, up);
+}
+
 // One phase (gate/up or down) of this CTA over ph[EPI].  Each unit's result
 // goes to its own shared-memory partial; after a round's barrier one warp per
 // tile sums the tile's partials in k-block order and runs the epilogue, so a
@@ -320,7 +347,7 @@ __device__ void fz_phase(const MoeFusedParams &p, uint8_t *smem, const FzRange *
             if (live) {
               const float gate = bf16_round(acc.v[tb][e2]);
               const float up = bf16_round(acc.v[tb][2 + e2]);
-              v = p.act_kind == RC_ACT_SITU ? act_situ(gate, up, p.gate_beta, p.value_beta) : act_swiglu(gate, up);
+              v = fz_glu(gate, up, p.act_kind, p.gate_beta, p.value_beta);
             }
             p.act[((size_t)grp * 8 * NTB + t) * p.inter_pad + tile * 8 + g] = f32_to_bf16_rne(v);
           } else {
@@ -405,42 +432,44 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
   {
     double *red = reinterpret_cast<double *>(smem + p.off_red);     // [16 warps][16 tokens]
     for (int e = blockIdx.x; e < E; e += gridDim.x) {
-      double acc[kMoeMaxTokens];
+      // tokens four at a time (a rolled loop: the kernel's code must stay
+      // small); each token's sum runs in the same order as with all at once
+      for (int t0 = 0; t0 < T; t0 += 4) {
+        double acc[4] = {0.0, 0.0, 0.0, 0.0};
+        for (int sl = warp; sl < nslice; sl += kFzWarps) {
+          const int col = sl * 256 + lane * 8;
+          const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
+          uint4 xv[4];
 #pragma unroll
-      for (int t = 0; t < kMoeMaxTokens; ++t) acc[t] = 0.0;
-      for (int sl = warp; sl < nslice; sl += kFzWarps) {
-        const int col = sl * 256 + lane * 8;
-        const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
-        uint4 xv[kMoeMaxTokens];
+          for (int q = 0; q < 4; ++q)
+            if (t0 + q < T) xv[q] = __ldcg(reinterpret_cast<const uint4 *>(p.x + (size_t)(t0 + q) * p.hidden + col));
+          const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+          double wd[8];
 #pragma unroll
-        for (int t = 0; t < kMoeMaxTokens; ++t)
-          if (t < T) xv[t] = __ldcg(reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.hidden + col));
-        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-        double wd[8];
+          for (int j = 0; j < 4; ++j) {
+            wd[2 * j] = (double)bf16_to_f32(ww[j] & 0xFFFFu);
+            wd[2 * j + 1] = (double)bf16_to_f32(ww[j] >> 16);
+          }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          wd[2 * j] = (double)bf16_to_f32(ww[j] & 0xFFFFu);
-          wd[2 * j + 1] = (double)bf16_to_f32(ww[j] >> 16);
-        }
+          for (int q = 0; q < 4; ++q) {
+            if (t0 + q < T) {
+              const uint32_t xw[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w};
 #pragma unroll
-        for (int t = 0; t < kMoeMaxTokens; ++t) {
-          if (t < T) {
-            const uint32_t xw[4] = {xv[t].x, xv[t].y, xv[t].z, xv[t].w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              acc[t] = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), wd[2 * j], acc[t]);
-              acc[t] = fma((double)bf16_to_f32(xw[j] >> 16), wd[2 * j + 1], acc[t]);
+              for (int j = 0; j < 4; ++j) {
+                acc[q] = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), wd[2 * j], acc[q]);
+                acc[q] = fma((double)bf16_to_f32(xw[j] >> 16), wd[2 * j + 1], acc[q]);
+              }
             }
           }
         }
-      }
 #pragma unroll
-      for (int t = 0; t < kMoeMaxTokens; ++t) {
-        if (t < T) {
-          double a = acc[t];
+        for (int q = 0; q < 4; ++q) {
+          if (t0 + q < T) {
+            double a = acc[q];
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-          if (lane == 0) red[warp * kMoeMaxTokens + t] = a;
+            for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+            if (lane == 0) red[warp * kMoeMaxTokens + t0 + q] = a;
+          }
         }
       }
       __syncthreads();
@@ -475,16 +504,9 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
         key[c] = 0u;
         sc[c] = 0.f;
         if (e < E) {
-          const float l = __ldcg(p.logits + (size_t)t * E + e);
-          float v;
-          if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
-            sc[c] = __double2float_rn(1.0 / (1.0 + exp(-(double)l)));
-            v = sc[c] + bias_s[e];
-          } else {
-            sc[c] = l + bias_s[e];       // softmax of the biased logits (bias zero unless set)
-            v = sc[c];
-          }
-          key[c] = route_key(v);
+          const FzScore r = fz_score(__ldcg(p.logits + (size_t)t * E + e), bias_s[e], p.mode);
+          sc[c] = r.score;
+          key[c] = r.key;
         }
       }
       // k rounds of arg-max over the experts not taken yet: the largest key,
@@ -599,8 +621,9 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
 
   // ------------------------------------------------------------ 3 gate/up
   FzStage sx{p.x, RC_DTYPE_BF16, p.hidden, T, T, 1, kb_gu_i};
-  build_activations<true>(sx, NTB, reinterpret_cast<uint32_t *>(smem + p.off_stage),
-                          smem + p.off_stage + xfrag_bytes(NTB, p.hidden), tid, blockDim.x);
+  build_activations<true, FzStage, kStageBf16Compact>(sx, NTB, reinterpret_cast<uint32_t *>(smem + p.off_stage),
+                                                      smem + p.off_stage + xfrag_bytes(NTB, p.hidden), tid,
+                                                      blockDim.x);
   __syncthreads();
   fz_phase<kFzGlu, NTB>(p, smem, ph, g_mask, g_dst, 0, rg);
   bool failed = __syncthreads_or(rg.failed) != 0;
@@ -612,9 +635,9 @@ __global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams
     const int g_hi = nt_dn ? (c0_dn + nt_dn - 1) / gt_dn_i : g_lo - 1;
     FzStage sa{p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, RC_DTYPE_BF16, p.inter_pad,
                (g_hi - g_lo + 1) * 8 * NTB, (g_hi - g_lo + 1) * 8 * NTB, 1, kb_dn_i};
-    build_activations<true>(sa, NTB * kMoeMaxGroupsPerCta, reinterpret_cast<uint32_t *>(smem + p.off_stage),
-                            smem + p.off_stage + xfrag_bytes(NTB * kMoeMaxGroupsPerCta, p.inter_pad), tid,
-                            blockDim.x);
+    build_activations<true, FzStage, kStageBf16Compact>(
+        sa, NTB * kMoeMaxGroupsPerCta, reinterpret_cast<uint32_t *>(smem + p.off_stage),
+        smem + p.off_stage + xfrag_bytes(NTB * kMoeMaxGroupsPerCta, p.inter_pad), tid, blockDim.x);
     __syncthreads();
     fz_phase<kFzDown, NTB>(p, smem, ph, g_mask, g_dst, g_lo, rg);
     failed = __syncthreads_or(rg.failed) != 0;
