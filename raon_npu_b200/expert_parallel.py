@@ -86,7 +86,9 @@ class ExpertParallelMoe:
         if self.transport == "auto" and (dist.get_backend(self.group) != "nccl" or self.world * M > 16
                                          or not hasattr(self.layer, "ep_init")):
             return False
-        dev = torch.device("cuda", torch.cuda.current_device())
+        # the handshake's tensors live where the group's backend moves them
+        on_gpu = dist.get_backend(self.group) == "nccl"
+        dev = torch.device("cuda", torch.cuda.current_device()) if on_gpu else torch.device("cpu")
         nb = self.layer.EP_HANDLE_BYTES
         mine = torch.zeros(nb, dtype=torch.uint8, device=dev)
         ok, why = 1, ""

@@ -135,3 +135,73 @@ def test_single_process_owns_every_expert():
     ep = ExpertParallelMoe(L(), 2)
     assert ep.world == 1 and ep.experts == (0, 6)
     assert all(ep.owns(e) for e in range(7))
+
+
+class HandshakeLayer:
+    """Stand-in with the peer-memory entry points of ``MoeLayer``: records the
+    blobs it is given; ``fail_init`` makes ``ep_init`` raise on this rank."""
+    EP_HANDLE_BYTES = 128
+
+    def __init__(self, rank, fail_init=False):
+        self.rank, self.fail_init = rank, fail_init
+        self.n_experts, self.hidden, self.has_shared = E, HIDDEN, True
+        self.opened, self.decoded = {}, []
+
+    def ep_init(self, rank, world, m):
+        if self.fail_init:
+            raise RuntimeError("rc_moe_ep_init: injected failure")
+        self.geometry = (rank, world, m)
+        return bytes([rank, world, m]) + bytes(self.EP_HANDLE_BYTES - 3)
+
+    def ep_open(self, peer, blob):
+        assert len(blob) == self.EP_HANDLE_BYTES
+        self.opened[peer] = bytes(blob[:3])
+
+    def ep_decode(self, x, k, out, **_):
+        self.decoded.append((tuple(x.shape), k))
+        out.copy_(x)
+
+
+def _handshake_worker(rank, world, port, result_dir, fail_rank):
+    import torch
+    import torch.distributed as dist
+    from raon_npu_b200.expert_parallel import ExpertParallelMoe
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        layer = HandshakeLayer(rank, fail_init=rank == fail_rank)
+        ep = ExpertParallelMoe(layer, K, transport="p2p")
+        x = torch.arange(M * HIDDEN, dtype=torch.int16).reshape(M, HIDDEN) + rank
+        out = torch.empty_like(x)
+        try:
+            ep.decode(x, out)
+            ep.decode(x, out)          # set up once per token count
+            res = {"ok": True, "opened": layer.opened, "decoded": layer.decoded, "geometry": layer.geometry,
+                   "same": bool(torch.equal(out, x))}
+        except RuntimeError as e:
+            res = {"ok": False, "error": str(e)}
+        np.save(os.path.join(result_dir, f"h{rank}.npy"), np.array([res], dtype=object), allow_pickle=True)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("fail_rank", [-1, 1])
+def test_peer_memory_handshake(tmp_path, fail_rank):
+    """Every rank opens every rank's blob, in rank order, once per token count;
+    a rank whose set-up fails makes every rank raise (no rank waits for it)."""
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_handshake_worker, args=(world, _free_port(), str(tmp_path), fail_rank), nprocs=world,
+                       start_method="spawn")
+    for rank in range(world):
+        res = np.load(tmp_path / f"h{rank}.npy", allow_pickle=True)[0]
+        if fail_rank >= 0:
+            assert not res["ok"] and "peer-memory expert parallelism unavailable" in res["error"], res
+            continue
+        assert res["ok"], res
+        assert res["geometry"] == (rank, world, M)
+        assert res["opened"] == {r: bytes([r, world, M]) for r in range(world)}
+        assert res["decoded"] == [((M, HIDDEN), K), ((M, HIDDEN), K)]
+        assert res["same"]
