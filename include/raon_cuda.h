@@ -229,10 +229,22 @@ int rc_moe_ep_open(rc_moe *m, int peer, const void *handle);
 int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int renormalize, float scaling,
                      int act, float gate_beta, float value_beta, uint16_t *out_dev, void *stream);
 
-/* MoE prefill: the layer for T <= 4096 tokens on the 5th-generation tensor
- * cores (tcgen05 grouped GEMM over expert-sorted token rows; the reference's
- * grouped path, npu/backend.py:4845-4979 with kernels/moe_grouped/
- * planner.py:76-108,286-322).  Same semantics as rc_moe_decode: router
+/* Which kernel runs the prefill experts' GEMMs (same routing, plan and
+ * combine; results within the oracle tolerance of each other):
+ * RC_PREFILL_GEMV (default) -- a grouped GEMV over 8-token blocks with the
+ * decode GEMV's register-fragment (mma.sync) unit arithmetic;
+ * RC_PREFILL_TCGEN05 -- the tcgen05 grouped GEMM over 64-token chunks.  With
+ * per-32-column scales tcgen05 needs a separate accumulator per group, 16
+ * MMA instructions per (128-row tile, 256-column block) whatever the tile's
+ * token count, which the few tokens most experts get cannot amortise. */
+#define RC_PREFILL_GEMV 0
+#define RC_PREFILL_TCGEN05 1
+int rc_moe_set_prefill_kernel(rc_moe *m, int kernel);
+
+/* MoE prefill: the layer for T <= 4096 tokens over expert-sorted token rows
+ * (the reference's grouped path, npu/backend.py:4845-4979 with
+ * kernels/moe_grouped/planner.py:76-108,286-322; the experts' GEMMs as
+ * rc_moe_set_prefill_kernel selects).  Same semantics as rc_moe_decode: router
  * (top-k ids / weights [T][k] copied out when given), routed experts summed
  * in ascending ID in f32 then RTNE, plus the shared expert.  x and out are
  * [T][hidden] bf16, 16-byte aligned.  Scratch grows on the first call for a

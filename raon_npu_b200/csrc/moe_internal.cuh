@@ -103,6 +103,7 @@ struct rc_moe {
   unsigned long long *fz_bar; // grid-barrier arrival count of the fused kernel (only grows)
   unsigned fz_epoch;          // ctx->timeout_epoch when fz_bar was last known consistent
   rc::MoeEp *ep;              // peer-memory expert parallelism (null until rc_moe_ep_init)
+  int prefill_kernel;         // RC_PREFILL_GEMV (register fragments) or RC_PREFILL_TCGEN05
 };
 
 namespace rc {

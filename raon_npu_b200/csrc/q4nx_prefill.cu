@@ -36,6 +36,7 @@
 #include <string.h>
 
 #include "moe_internal.cuh"
+#include "q4nx_core.cuh"
 #include "rc_device.cuh"
 #include "rc_internal.cuh"
 
@@ -44,6 +45,7 @@ namespace rc {
 constexpr int kPfMaxTokens = 4096;
 constexpr int kPfRows = 128;         // weight rows per tile: MMA M, TMEM lanes
 constexpr int kPfCols = 64;          // token columns per work item: max MMA N
+constexpr int kPfBlk = 8;            // token rows per block of the register-fragment (mma.sync) path
 constexpr int kPfThreads = 256;
 constexpr int kPfWarps = kPfThreads / 32;
 constexpr int kPfTmemCols = 512;     // 8 group accumulators x 64 columns
@@ -61,10 +63,10 @@ constexpr int kPfS = kPfU + 2 * kPfUStage;           // group sums [8][64] f32
 constexpr int kPfBar = kPfS + kPfGroups * kPfCols * 4;   // 3 mbarriers + TMEM address
 constexpr int kPfSmem = kPfBar + 64;
 constexpr int kPfSmemAlloc = kPfSmem + 1024;         // room to align the base
-constexpr int kPfPlanSmemMax = kGemvSmemLimit - 4 * 1024;   // dynamic part of the plan kernel
+constexpr int kPfPlanSmemMax = kGemvSmemLimit - 8 * 1024;   // dynamic part of the plan kernel (static: ~4.1 KB)
 
 struct PfScratch {
-  int T_cap, P_cap, chunk_cap, E1;
+  int T_cap, P_cap, chunk_cap, blk_cap, E1;
   float *logits;            // [T][E]
   int32_t *ids;             // [T][k] rank order
   float *weights;           // [T][k]
@@ -73,10 +75,13 @@ struct PfScratch {
   int32_t *slot_row;        // [T][k+1] permuted row of each slot, -1 if not computed here
   int32_t *row_token;       // [P] token of each permuted row
   int32_t *cnt, *off;       // [E+1]
-  int32_t *n_chunks;        // [1]
+  int32_t *n_chunks;        // [2]: 64-row chunks, 8-row blocks
   int32_t *chunk_expert, *chunk_row0, *chunk_n;
   uint16_t *act;            // [P][inter_pad]
   uint16_t *down;           // [P][hidden]
+  int32_t *blk_expert, *blk_row0, *blk_n;   // 8-row token blocks of the permuted rows
+  uint32_t *xf;             // the blocks' staged activations (f16 fragments), for K up to max(hidden, inter_pad)
+  void *xaux;               // and their aux words
 };
 
 // ------------------------------------------------------------ small PTX --
@@ -300,6 +305,8 @@ struct PfPlanParams {
   int st0, st1;                 // tokens whose shared expert is computed here
   int32_t *slot_row, *row_token, *cnt, *off, *n_chunks, *chunk_expert, *chunk_row0, *chunk_n;
   int chunk_cap;
+  int32_t *blk_expert, *blk_row0, *blk_n;
+  int blk_cap;
   int *err;
 };
 
@@ -311,7 +318,8 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(PfPlanParams p) {
   const int nw = (p.T + 31) / 32;
   uint32_t *mask = pf_plan_smem;                 // [E1][nw]
   uint32_t *pre = mask + (size_t)p.E1 * nw;      // [E1][nw] exclusive prefix popcounts
-  __shared__ int s_cnt[kMoeMaxExperts + 1], s_off[kMoeMaxExperts + 1], s_cofs[kMoeMaxExperts + 1];
+  __shared__ int s_cnt[kMoeMaxExperts + 1], s_off[kMoeMaxExperts + 1], s_cofs[kMoeMaxExperts + 1],
+      s_bofs[kMoeMaxExperts + 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
   const int k1 = p.k + 1;
   auto computed = [&](int t, int r, int e) {
@@ -347,28 +355,34 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(PfPlanParams p) {
   __syncthreads();
   if (warp == 0) {
     // expert offsets and chunk offsets (ascending expert ID; the shared expert last)
-    int base = 0, cbase = 0;
+    int base = 0, cbase = 0, bbase = 0;
     for (int e0 = 0; e0 < p.E1; e0 += 32) {
       const int e = e0 + lane;
       const int c = e < p.E1 ? s_cnt[e] : 0;
-      const int nc = (c + kPfCols - 1) / kPfCols;
-      int incl = c, cincl = nc;
+      const int nc = (c + kPfCols - 1) / kPfCols, nb = (c + kPfBlk - 1) / kPfBlk;
+      int incl = c, cincl = nc, bincl = nb;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
         const int cv = __shfl_up_sync(0xffffffffu, cincl, o);
-        if (lane >= o) incl += v, cincl += cv;
+        const int bv = __shfl_up_sync(0xffffffffu, bincl, o);
+        if (lane >= o) incl += v, cincl += cv, bincl += bv;
       }
       if (e < p.E1) {
         s_off[e] = base + incl - c;
         s_cofs[e] = cbase + cincl - nc;
+        s_bofs[e] = bbase + bincl - nb;
         p.cnt[e] = c;
         p.off[e] = base + incl - c;
       }
       base += __shfl_sync(0xffffffffu, incl, 31);
       cbase += __shfl_sync(0xffffffffu, cincl, 31);
+      bbase += __shfl_sync(0xffffffffu, bincl, 31);
     }
-    if (lane == 0) *p.n_chunks = cbase < p.chunk_cap ? cbase : p.chunk_cap;
+    if (lane == 0) {
+      p.n_chunks[0] = cbase < p.chunk_cap ? cbase : p.chunk_cap;
+      p.n_chunks[1] = bbase < p.blk_cap ? bbase : p.blk_cap;
+    }
   }
   __syncthreads();
   for (int i = tid; i < p.T * k1; i += blockDim.x) {
@@ -383,13 +397,21 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(PfPlanParams p) {
     p.slot_row[i] = row;
   }
   for (int e = warp; e < p.E1; e += nwarps) {
-    const int c = s_cnt[e], nc = (c + kPfCols - 1) / kPfCols;
+    const int c = s_cnt[e], nc = (c + kPfCols - 1) / kPfCols, nb = (c + kPfBlk - 1) / kPfBlk;
     for (int j = lane; j < nc; j += 32) {
       const int ci = s_cofs[e] + j;
       if (ci < p.chunk_cap) {
         p.chunk_expert[ci] = e;
         p.chunk_row0[ci] = s_off[e] + j * kPfCols;
         p.chunk_n[ci] = c - j * kPfCols < kPfCols ? c - j * kPfCols : kPfCols;
+      }
+    }
+    for (int j = lane; j < nb; j += 32) {
+      const int bi = s_bofs[e] + j;
+      if (bi < p.blk_cap) {
+        p.blk_expert[bi] = e;
+        p.blk_row0[bi] = s_off[e] + j * kPfBlk;
+        p.blk_n[bi] = c - j * kPfBlk < kPfBlk ? c - j * kPfBlk : kPfBlk;
       }
     }
   }
@@ -664,6 +686,179 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kPfTmemCols));
 }
 
+// ------------------------------------------------ register-fragment path --
+// The experts' GEMMs as a grouped GEMV over 8-row token blocks, with the unit
+// arithmetic of the decode GEMV (codes as exact f16 subnormals in mma.sync A
+// fragments; activations as block-scaled f16 B fragments; min term on bf16
+// mmas; per-unit partials summed per tile in k-block order).  tcgen05 needs
+// a separate accumulator per 32-column quantisation group, so it pays 16 MMA
+// instructions per (128-row tile, k-block) whatever the tile's token count;
+// with the few tokens most experts get, these register fragments do the same
+// work with far fewer instructions.
+
+// Staged activations of the 8-row token blocks (slot 8 b + t = row t of block
+// b; rows past the block's count zero), one warp per (slot, 256-column
+// block).  Gate/up: row t of block b is x[row_token[row0 + t]]; down:
+// act[row0 + t].
+__global__ void __launch_bounds__(256) pf_stage_blocks_kernel(const uint16_t *src, int K, const int32_t *row_token,
+                                                              const int32_t *n_blocks, const int32_t *blk_row0,
+                                                              const int32_t *blk_n, int blk_cap, uint32_t *xf,
+                                                              void *aux) {
+  const int nb = *n_blocks, KB = K / kUnitK, k64 = K / 64, lane = threadIdx.x & 31;
+  const int total = nb * kPfBlk * KB;
+  uint16_t *bmin16 = static_cast<uint16_t *>(aux);
+  float *inv = reinterpret_cast<float *>(bmin16 + (size_t)blk_cap * KB * 256);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += nw) {
+    const int slot = w / KB, kbi = w - slot * KB;
+    const int b = slot / kPfBlk, t = slot - b * kPfBlk;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    if (t < blk_n[b]) {
+      const int row = blk_row0[b] + t;
+      const int srow = row_token ? row_token[row] : row;
+      const uint4 raw = *reinterpret_cast<const uint4 *>(src + (size_t)srow * K + kbi * kUnitK + lane * 8);
+      const uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = bf16_lo_f32(wd[i]);
+        v[2 * i + 1] = bf16_hi_f32(wd[i]);
+      }
+    }
+    stage_core<true>(v, slot, kbi * 32 + lane, k64, KB, xf, bmin16, inv);
+  }
+}
+
+struct PfGemvParams {
+  const uint8_t *const *expert_tiles;   // [E+1] t16 tiles (null: not loaded)
+  int kb, tiles;                        // k-blocks; 16-row tiles of an expert's matrix
+  const int32_t *n_blocks, *blk_expert, *blk_row0, *blk_n;
+  const uint32_t *xf;                   // staged blocks (pf_stage_blocks_kernel)
+  const void *xaux;
+  int blk_cap;
+  uint16_t *y;                          // gate/up: act [P][ld_y]; down: down [P][ld_y]
+  int ld_y;
+  float gate_beta, value_beta;
+  int stages, round;                    // ring depth per warp; tiles per round
+  int *err;
+};
+constexpr int kPgWarps = 16, kPgThreads = kPgWarps * 32;
+constexpr int kPgPartBytes = 48 * 1024;
+
+// One CTA per SM, persistent over a contiguous range of the block-major
+// (block, 16-row tile) list; each warp streams its units (k-block-major
+// within a round, RoundCursor) through a ring of bulk copies.
+template <int EPI>
+__global__ void __launch_bounds__(kPgThreads, 1) pf_gemv_kernel(PfGemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, qd = lane & 3;
+  const int S = p.stages, KB = p.kb, R = p.round;
+  uint8_t *ring = smem + warp * S * kUnitBytes;
+  const uint32_t ring_s = smem_addr(ring);
+  float4 *part = reinterpret_cast<float4 *>(smem + kPgWarps * S * kUnitBytes);
+  const uint32_t bar0 = smem_addr(smem + kPgWarps * S * kUnitBytes + kPgPartBytes) + warp * S * 8;
+  const int nb = *p.n_blocks;
+  const int total = nb * p.tiles;
+  const int per = (total + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int c0 = blockIdx.x * per;
+  const int nt = c0 < total ? (c0 + per < total ? per : total - c0) : 0;
+  const FastDiv gt = make_fastdiv(p.tiles);
+  RoundCursor iss, cur;
+  iss.init(nt, R, KB, kPgWarps, warp);
+  cur.init(nt, R, KB, kPgWarps, warp);
+  int issued = 0, consumed = 0;
+  auto issue = [&](int sl) {
+    const uint32_t tg = c0 + iss.tile(), blk = fdiv(tg, gt), tile = tg - blk * gt.d;
+    const uint8_t *wt = p.expert_tiles[p.blk_expert[blk]];
+    if (wt) {
+      mbar_arrive_expect_tx(bar0 + 8 * sl, kUnitBytes);
+      bulk_copy_g2s_plain(ring_s + sl * kUnitBytes, wt + ((size_t)tile * KB + iss.kbi) * kUnitBytes, kUnitBytes,
+                          bar0 + 8 * sl);
+    } else {
+      mbar_arrive_expect_tx(bar0 + 8 * sl, 0);     // nothing to fetch: complete the phase at once
+    }
+    ++issued;
+    iss.next();
+  };
+  if (lane == 0) {
+    for (int sl = 0; sl < S; ++sl) mbar_init(bar0 + 8 * sl, 1);
+    mbar_fence_init();
+    for (int sl = 0; sl < S && iss.valid(); ++sl) issue(sl);
+  }
+  __syncwarp();
+  XFrag<1> xr;
+  int xr_key = -1;
+  int slot = 0;
+  uint32_t parity = 0;
+  bool failed = false;
+  const int n_rounds = round_count(nt, R);
+  for (int r = 0; r < n_rounds; ++r) {
+    for (; cur.valid() && cur.round == r; cur.next()) {
+      const uint32_t blk = fdiv(c0 + cur.tile(), gt);
+      if (!failed) {
+        if (mbar_wait_bounded_warp(bar0 + 8 * slot, parity)) {
+          ++consumed;
+        } else {
+          if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+          failed = true;
+        }
+      }
+      if (!failed && p.expert_tiles[p.blk_expert[blk]] != nullptr) {
+        if ((int)blk * KB + cur.kbi != xr_key) {
+          load_xfrag<1, false>(xr, p.xf, p.xaux, p.blk_cap, blk, KB, cur.kbi, lane);
+          xr_key = blk * KB + cur.kbi;
+        }
+        float4 Q[1];
+        unit_result<1>(ring + slot * kUnitBytes, xr, lane, Q);
+        part[(size_t)cur.slot() * 32 + lane] = Q[0];
+      }
+      __syncwarp();
+      if (!failed && lane == 0 && iss.valid()) issue(slot);
+      if (++slot == S) slot = 0, parity ^= 1u;
+    }
+    __syncthreads();
+    const int t_lo = r * R, t_hi = t_lo + R < nt ? t_lo + R : nt;
+    for (int ti = t_lo + warp; ti < t_hi; ti += kPgWarps) {
+      const uint32_t tg = c0 + ti, blk = fdiv(tg, gt), tile = tg - blk * gt.d;
+      const uint8_t *wt = p.expert_tiles[p.blk_expert[blk]];
+      if (wt == nullptr) {
+        if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+        continue;
+      }
+      Acc<1> acc;
+      acc_zero(acc);
+      const float4 *src = part + (size_t)(ti - t_lo) * KB * 32 + lane;
+      for (int kbi = 0; kbi < KB; ++kbi) {
+        float4 v[1] = {src[kbi * 32]};
+        acc_add(acc, v);
+      }
+      const int n = p.blk_n[blk], row0 = p.blk_row0[blk];
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) {
+        const int t = 2 * qd + e2;
+        if (t >= n) continue;
+        if (EPI != kPfEpiDown) {
+          const float gate = bf16_round(acc.v[0][e2]);
+          const float up = bf16_round(acc.v[0][2 + e2]);
+          const float v = EPI == kPfEpiSitu ? act_situ(gate, up, p.gate_beta, p.value_beta) : act_swiglu(gate, up);
+          p.y[(size_t)(row0 + t) * p.ld_y + tile * 8 + g] = f32_to_bf16_rne(v);
+        } else {
+          uint16_t *y = p.y + (size_t)(row0 + t) * p.ld_y + tile * kUnitRows + g;
+          y[0] = f32_to_bf16_rne(acc.v[0][e2]);
+          y[8] = f32_to_bf16_rne(acc.v[0][2 + e2]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // after a failure, the copies still in flight land before the shared
+  // memory is released
+  if (failed && lane == 0) {
+    for (int j = consumed; j < issued; ++j) mbar_wait_bounded(bar0 + 8 * (j % S), (uint32_t)(j / S) & 1u);
+  }
+}
+
 // --------------------------------------------------------------- combine --
 // Per token: routed = RTNE(sum over its slots in ascending ID of
 // f32(down[row]) * w), then RTNE(f32(routed) + f32(shared row)).
@@ -753,6 +948,11 @@ static void pf_release(PfScratch *s) {
   cudaFree(s->chunk_n);
   cudaFree(s->act);
   cudaFree(s->down);
+  cudaFree(s->blk_expert);
+  cudaFree(s->blk_row0);
+  cudaFree(s->blk_n);
+  cudaFree(s->xf);
+  cudaFree(s->xaux);
   delete s;
 }
 
@@ -773,6 +973,8 @@ static int pf_scratch(rc_moe *m, int T) {
   s->E1 = E + 1;
   s->P_cap = T * (K + 1);
   s->chunk_cap = s->P_cap / kPfCols + E + 1;
+  s->blk_cap = s->P_cap / kPfBlk + E + 1;
+  const int kmax = m->hidden > m->inter_pad ? m->hidden : m->inter_pad;
   const size_t P = (size_t)s->P_cap;
   cudaError_t e = cudaMalloc(&s->logits, (size_t)T * E * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->ids, (size_t)T * K * 4);
@@ -783,7 +985,12 @@ static int pf_scratch(rc_moe *m, int T) {
   if (e == cudaSuccess) e = cudaMalloc(&s->row_token, P * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->cnt, (size_t)(E + 1) * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->off, (size_t)(E + 1) * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&s->n_chunks, 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->n_chunks, 8);
+  if (e == cudaSuccess) e = cudaMalloc(&s->blk_expert, (size_t)s->blk_cap * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->blk_row0, (size_t)s->blk_cap * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->blk_n, (size_t)s->blk_cap * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->xf, xfrag_bytes(s->blk_cap, kmax));
+  if (e == cudaSuccess) e = cudaMalloc(&s->xaux, xaux_bytes(s->blk_cap, kmax));
   if (e == cudaSuccess) e = cudaMalloc(&s->chunk_expert, (size_t)s->chunk_cap * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->chunk_row0, (size_t)s->chunk_cap * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->chunk_n, (size_t)s->chunk_cap * 4);
@@ -816,11 +1023,71 @@ static cudaError_t pf_launch_gemm(const rc_ctx *ctx, const PfGemmParams &p, cuda
   return cudaGetLastError();
 }
 
+template <int EPI>
+static cudaError_t pf_launch_gemv(const rc_ctx *ctx, const PfGemvParams &p, size_t smem, cudaStream_t s) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(pf_gemv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemLimit);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) configured[dev] = true;
+  }
+  pf_gemv_kernel<EPI><<<ctx->sm_count, kPgThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
 struct PfRun {
   int T, k, act;
   float gb, vb;
   int lo, hi, st0, st1;        // computed experts / shared tokens
 };
+
+// gate/up + down on the register-fragment path (after the plan): stage the
+// blocks' rows, grouped GEMV, for each of the two matrices
+static int pf_experts_gemv(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t s) {
+  PfScratch *ps = m->pf;
+  constexpr int kStages = 4;
+  const size_t smem = (size_t)kPgWarps * kStages * kUnitBytes + kPgPartBytes + (size_t)kPgWarps * kStages * 8;
+  PfGemvParams g{};
+  g.expert_tiles = m->gu_tiles;
+  g.kb = m->hidden / kUnitK;
+  g.tiles = 2 * m->inter / kUnitRows;
+  g.n_blocks = ps->n_chunks + 1;
+  g.blk_expert = ps->blk_expert;
+  g.blk_row0 = ps->blk_row0;
+  g.blk_n = ps->blk_n;
+  g.xf = ps->xf;
+  g.xaux = ps->xaux;
+  g.blk_cap = ps->blk_cap;
+  g.y = ps->act;
+  g.ld_y = m->inter_pad;
+  g.gate_beta = r.gb;
+  g.value_beta = r.vb;
+  g.stages = kStages;
+  g.round = kPgPartBytes / (g.kb * 32 * 16);
+  g.err = m->ctx->err;
+  pf_stage_blocks_kernel<<<m->ctx->sm_count * 4, 256, 0, s>>>(x, m->hidden, ps->row_token, g.n_blocks, ps->blk_row0,
+                                                               ps->blk_n, ps->blk_cap, ps->xf, ps->xaux);
+  RC_CUDA_TRY(cudaGetLastError());
+  if (r.act == RC_ACT_SITU)
+    RC_CUDA_TRY(pf_launch_gemv<kPfEpiSitu>(m->ctx, g, smem, s));
+  else
+    RC_CUDA_TRY(pf_launch_gemv<kPfEpiSwiglu>(m->ctx, g, smem, s));
+  PfGemvParams d = g;
+  d.expert_tiles = m->dn_tiles;
+  d.kb = m->inter_pad / kUnitK;
+  d.tiles = m->hidden / kUnitRows;
+  d.y = ps->down;
+  d.ld_y = m->hidden;
+  d.round = kPgPartBytes / (d.kb * 32 * 16);
+  pf_stage_blocks_kernel<<<m->ctx->sm_count * 4, 256, 0, s>>>(ps->act, m->inter_pad, nullptr, d.n_blocks,
+                                                               ps->blk_row0, ps->blk_n, ps->blk_cap, ps->xf, ps->xaux);
+  RC_CUDA_TRY(cudaGetLastError());
+  RC_CUDA_TRY(pf_launch_gemv<kPfEpiDown>(m->ctx, d, smem, s));
+  return RC_OK;
+}
 
 // plan + gate/up + down for slot lists already in m->pf (slot_expert, slot_w)
 static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t s) {
@@ -843,6 +1110,10 @@ static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t
   pp.chunk_row0 = ps->chunk_row0;
   pp.chunk_n = ps->chunk_n;
   pp.chunk_cap = ps->chunk_cap;
+  pp.blk_expert = ps->blk_expert;
+  pp.blk_row0 = ps->blk_row0;
+  pp.blk_n = ps->blk_n;
+  pp.blk_cap = ps->blk_cap;
   pp.err = m->ctx->err;
   const int nw = (r.T + 31) / 32;
   const size_t plan_smem = (size_t)2 * pp.E1 * nw * 4;
@@ -858,6 +1129,7 @@ static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t
   pf_plan_kernel<<<1, 1024, plan_smem, s>>>(pp);
   RC_CUDA_TRY(cudaGetLastError());
 
+  if (m->prefill_kernel == RC_PREFILL_GEMV) return pf_experts_gemv(m, x, r, s);
   PfGemmParams g{};
   g.expert_tiles = m->gu_tiles;
   g.kb = m->hidden / kUnitK;
@@ -962,6 +1234,13 @@ int pf_route_tokens(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, 
 using namespace rc;
 
 extern "C" {
+
+int rc_moe_set_prefill_kernel(rc_moe *m, int kernel) {
+  RC_CHECK_ARG(m, "rc_moe_set_prefill_kernel: NULL argument");
+  RC_CHECK_ARG(kernel == RC_PREFILL_GEMV || kernel == RC_PREFILL_TCGEN05, "unknown prefill kernel %d", kernel);
+  m->prefill_kernel = kernel;
+  return RC_OK;
+}
 
 int rc_moe_prefill(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
                    int act, float gate_beta, float value_beta, uint16_t *out_dev, int32_t *ids_dev, float *w_dev,

@@ -105,6 +105,13 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void *src, uin
       : "memory");
 }
 
+// The same without a cache hint (weights that several CTAs re-read soon).
+__device__ __forceinline__ void bulk_copy_g2s_plain(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 // ------------------------------------------------- grid-scope atomics --
 __device__ __forceinline__ unsigned long long atom_add_release_gpu(unsigned long long *p, unsigned long long v) {
   unsigned long long old;

@@ -315,6 +315,14 @@ class MoeLayer:
         both give the same bytes."""
         check(self.ctx.lib.rc_moe_set_fused(self.handle, int(bool(enable))), "rc_moe_set_fused")
 
+    def set_prefill_kernel(self, kernel: str) -> None:
+        """"gemv" (default: register-fragment grouped GEMV over 8-token blocks) or
+        "tcgen05" (tensor-core grouped GEMM over 64-token chunks)."""
+        codes = {"gemv": 0, "tcgen05": 1}
+        if kernel not in codes:
+            raise ValueError(f"unknown prefill kernel {kernel!r}")
+        check(self.ctx.lib.rc_moe_set_prefill_kernel(self.handle, codes[kernel]), "rc_moe_set_prefill_kernel")
+
     def route(self, x_dev, tokens: int, k: int, ids_dev, w_dev, logits_dev=None, router: str = "softmax",
               renormalize: bool = True, scaling: float = 1.0, stream: int | None = None) -> None:
         check(self.ctx.lib.rc_moe_route(

@@ -63,11 +63,16 @@ def _oracle_token(experts, shared, wr, x, k, act, bias=None):
     return out, ids, mag
 
 
-def test_prefill_small_layer_matches_oracle(torch, ctx):
+KERNELS = ["gemv", "tcgen05"]
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_prefill_small_layer_matches_oracle(torch, ctx, kernel):
     """hidden 256, intermediate 256, 6 experts + shared, top-3, SiTU, T = 37."""
     from raon_npu_b200.device import MoeLayer
     d = cases.moe_inputs(hidden=256, inter=256, experts=7, k=3, tokens=37, seed=201)
     layer = MoeLayer(ctx, 256, 256, 6, has_shared=True)
+    layer.set_prefill_kernel(kernel)
     for e, (pgu, pdn) in d["packed"].items():
         layer.set_expert(e, pgu, pdn)            # expert 6 is the shared one
     rng = np.random.default_rng(202)
@@ -100,8 +105,10 @@ def c4(torch, ctx):
     layer.close()
 
 
-def test_prefill_config4_shapes_match_oracle_and_decode(torch, ctx, c4):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_prefill_config4_shapes_match_oracle_and_decode(torch, ctx, c4, kernel):
     layer, wr, packed, bias = c4
+    layer.set_prefill_kernel(kernel)
     T = 200
     rng = np.random.default_rng(98)
     x = q.f32_to_bf16(rng.standard_normal((T, 2048)).astype(np.float32))
@@ -134,10 +141,16 @@ def test_prefill_config4_shapes_match_oracle_and_decode(torch, ctx, c4):
     # differ from each other by at most the sum of the two
     for t in range(T):
         assert rms_rel(got[t], ref_dec[t]) <= 4e-3, t
+    if kernel == "gemv":
+        # the register-fragment path runs the decode's unit arithmetic on the
+        # same per-token staging: the bytes are the decode's
+        assert torch.equal(out, dec)
 
 
-def test_prefill_tokens_are_batch_invariant(torch, ctx, c4):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_prefill_tokens_are_batch_invariant(torch, ctx, c4, kernel):
     layer = c4[0]
+    layer.set_prefill_kernel(kernel)
     rng = np.random.default_rng(99)
     x = q.f32_to_bf16(rng.standard_normal((300, 2048)).astype(np.float32))
     xd = _dev(torch, x, np.int16)
@@ -153,8 +166,10 @@ def test_prefill_tokens_are_batch_invariant(torch, ctx, c4):
     assert torch.equal(a[5:6], c)
 
 
-def test_prefill_caller_routes_reproduce_routed_call(torch, ctx, c4):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_prefill_caller_routes_reproduce_routed_call(torch, ctx, c4, kernel):
     layer = c4[0]
+    layer.set_prefill_kernel(kernel)
     rng = np.random.default_rng(100)
     x = q.f32_to_bf16(rng.standard_normal((90, 2048)).astype(np.float32))
     xd = _dev(torch, x, np.int16)
