@@ -703,7 +703,7 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
     return {
         "metric": "MoE prefill layer tokens/s", "value": round(T / (ms_max * 1e-3), 1), "unit": "tokens/s",
         "ms_per_step": round(ms_max, 4), "steps": args.steps, "scaling": "strong",
-        "config": {"workload": "MoE prefill grouped GEMM (BASELINE configs[3])", "tokens": T, "hidden": H,
+        "config": {"workload": "MoE prefill layer (BASELINE configs[3])", "tokens": T, "hidden": H,
                    "intermediate": I, "experts": E, "shared_experts": 1, "top_k": k,
                    "router": "softmax of logits + b_e, b_e = -1.1 ln(rank_e) (Zipf(1.1) load)",
                    "parallelism": f"ep{world}", "tokens_per_rank": M, "layers_rotated": n_layers,
@@ -713,13 +713,14 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
                      "achieved": round(avg_bytes / (ms_max * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(hbm_frac, 4), "peak_source": peak_kind,
                      "traffic": MEASURED_TRAFFIC["prefill_gemms"] if world == 1 else None,
-                     "traffic_source": "ncu capture of the two pf_gemm_kernel launches of one layer",
+                     "traffic_source": "ncu capture of the two pf_gemv_kernel launches of one layer (512 tokens)",
                      "tensor_tflops": round(avg_flops / (ms_max * 1e-3) / 1e12, 1),
                      "tensor_peak_tflops": tflops_peak, "tensor_frac": round(tc_frac, 4),
                      "per_rank_bytes_per_step": round(avg_bytes), "per_rank_flops_per_step": round(avg_flops),
-                     "kernel": "prefill layer per rank (router, plan, tcgen05 grouped gate/up + down GEMMs, "
-                               "combine; NCCL all-gather + reduce-scatter at N>1)"},
-        "gpu_launches": 7 * args.steps,
+                     "kernel": "prefill layer per rank (router, plan, grouped gate/up + down GEMVs over 8-token "
+                               "blocks on register-fragment mma, combine; NCCL all-gather + reduce-scatter at "
+                               "N>1)"},
+        "gpu_launches": (8 if world == 1 else 9) * args.steps,
         "clocks": clk,
     }
 
