@@ -40,6 +40,12 @@ SAMPLE_CASES = {
     "no_topk_p09": (3000, 307, "normal", dict(temperature=1.0, top_p=0.9, top_k=0, presence_penalty=0.0)),
 }
 ROUTER_CASE = dict(hidden=256, experts=16, k=4, tokens=8, seed=41, scaling=2.5)
+# bfp16ebs8 (quant/bfp16.py): name -> (rows N, cols K, seed, kind, GEMV rows x)
+BFP16_CASES = {
+    "normal_128x256": (128, 256, 61, "normal", 3),
+    "normal_256x512": (256, 512, 62, "normal", 2),
+    "edge_128x512": (128, 512, 63, "edge", 3),
+}
 COMBINE_CASE = dict(tokens=20, k=4, hidden=64, seed=51)
 
 
@@ -71,6 +77,27 @@ def quant_input(n: int, k: int, seed: int, kind: str) -> np.ndarray:
         w[1, 96:128] = 1e-40                    # subnormal constant group
         return w
     raise ValueError(kind)
+
+
+def bfp16_input(n: int, k: int, seed: int, kind: str, t: int) -> tuple[np.ndarray, np.ndarray]:
+    """(f32 weights [n, k], bf16 bit rows x [t, k]) for a bfp16ebs8 case.  The
+    edge kind mixes groups that round up to +128 (exponent carry), reach -128,
+    are all zero, or are tiny enough for the layout's exponent floor."""
+    rng = np.random.default_rng(seed)
+    if kind == "normal":
+        w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    elif kind == "edge":
+        w = (rng.standard_normal((n, k)) * np.exp2(rng.integers(-12, 6, (n, 1)))).astype(np.float32)
+        w[:, 0:8] = 1.9999                      # rounds to mantissa 128: exponent + 1
+        w[:, 8:16] = -1.9999                    # rounds to -128: kept
+        w[:, 16:24] = 0.0
+        w[:, 24:32] = 3e-38                     # exponent field 1: below the layout's floor
+        w[0::3, 32:40] = np.linspace(-7.0, 7.0, 8, dtype=np.float32)
+        w[1::3, 40:48] = 2.5e-3                 # ties of the mantissa rounding at some exponents
+    else:
+        raise ValueError(kind)
+    x = _bf16_bits(rng.standard_normal((t, k)).astype(np.float32))
+    return w, x
 
 
 def q4nx_weight(w: np.ndarray, q) -> tuple[bytes, np.ndarray]:

@@ -4,7 +4,8 @@ Run from the repository root where the reference checkout is readable:
 
     RAON_REFERENCE=/path/to/raon-npu python tests/golden/make_golden.py
 
-It imports the reference's ``quant.q4nx``, ``host.backend.NumpyBackend``,
+It imports the reference's ``quant.q4nx``, ``quant.bfp16``,
+``kernels/gemv_bfp16/reference.py``, ``host.backend.NumpyBackend``,
 ``host.raon.RaonModel._route_token`` and ``kernels.moe_grouped.planner`` and
 records their outputs on seeded inputs into ``tests/golden/*.npz``.  The tests
 regenerate the same inputs from the seeds recorded here and check the oracle
@@ -36,8 +37,8 @@ from serve.engine import GenOptions, sample_token  # noqa: E402
 
 sys.path.insert(0, str(HERE.parent.parent))
 from tests.golden.cases import (  # noqa: E402
-    QUANT_CASES, LINEAR_CASES, MOE_CASE, ROUTER_CASE, COMBINE_CASE, SAMPLE_CASES,
-    quant_input, linear_inputs, moe_inputs, router_inputs, combine_inputs, sample_inputs,
+    QUANT_CASES, LINEAR_CASES, MOE_CASE, ROUTER_CASE, COMBINE_CASE, SAMPLE_CASES, BFP16_CASES,
+    quant_input, linear_inputs, moe_inputs, router_inputs, combine_inputs, sample_inputs, bfp16_input,
 )
 
 
@@ -156,7 +157,37 @@ def make_sample():
     np.savez_compressed(HERE / "sample.npz", **out)
 
 
+def make_bfp16():
+    """quant/bfp16.py's codec and GEMV packing, and kernels/gemv_bfp16/
+    reference.py's bit-level GEMV model, on seeded matrices.  The reference
+    module is loaded from its file (its package imports the NPU toolchain)."""
+    import importlib.util
+    import warnings
+    from quant import bfp16 as rb
+    spec = importlib.util.spec_from_file_location("gemv_bfp16_reference",
+                                                  Path(REF) / "kernels/gemv_bfp16/reference.py")
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    out = {}
+    for name, (n, k, seed, kind, t) in BFP16_CASES.items():
+        w, x = bfp16_input(n, k, seed, kind, t)
+        enc = rb.bfp16ebs8_encode(w)
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            packed, stats = rb.pack_bfp16_gemv(w, return_stats=True)
+        e, m = rb.parse_bfp16_gemv_raw(packed, K=k, M=n)
+        out[f"{name}/encode_sha"] = np.array(sha(enc.tobytes()))
+        out[f"{name}/packed_sha"] = np.array(sha(packed))
+        out[f"{name}/exponents"] = e
+        out[f"{name}/mantissas_sha"] = np.array(sha(m.tobytes()))
+        out[f"{name}/flushed"] = np.array(stats["flushed_nonzero_blocks"])
+        out[f"{name}/y"] = np.stack([ref.bfp16_gemv_bit_reference(w, (x[i].astype(np.uint32) << 16).view(
+            np.float32))[1] for i in range(t)])
+    np.savez_compressed(HERE / "bfp16.npz", **out)
+
+
 if __name__ == "__main__":
+    make_bfp16()
     make_sample()
     make_quant()
     make_linear()
