@@ -53,8 +53,8 @@ HBM_FALLBACK_GBS = 6650.0
 # DRAM traffic of the timed work, from ncu captures of the same commands on a
 # B200 (dram__bytes_read.sum + dram__bytes_write.sum): the GEMV launches of
 # one sweep step; one config-3 decode layer at T = 1 (moe_fused_kernel); the
-# two grouped GEMMs of one 512-token prefill layer.  Single-GPU figures.
-MEASURED_TRAFFIC = {"gemv_step": 1033.4e6, "moe_layer_t1": 27.61e6, "prefill_gemms": 246.57e6}
+# two grouped GEMVs of one 512-token prefill layer.  Single-GPU figures.
+MEASURED_TRAFFIC = {"gemv_step": 1033.4e6, "moe_layer_t1": 27.30e6, "prefill_gemms": 300.75e6}
 
 
 def algo_bytes(n: int, k: int, t: int) -> int:

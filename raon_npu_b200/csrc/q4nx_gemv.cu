@@ -649,7 +649,14 @@ int gemv_launch(rc_ctx *ctx, const uint8_t *tiles, int n_tiles, int k, const voi
   // itself may still fall back to global scratch; that changes no arithmetic.
   const GemvGeometry geo =
       gemv_geometry(ctx, n_tiles, k / kUnitK, gemv_can_stage(2, k, kGemvMaxWarps) ? kGemvMaxWarps : kGemvWarps);
-  const bool staged = gemv_can_stage(ntb, k, geo.warps);
+  // Per-CTA staging repeats the whole of x in every CTA: worth it while that
+  // work (items per thread) is at most twice a warp's units (measured on B200:
+  // 2048x4096, 4096x2048 and 512x2048 at T = 1..16); otherwise one prep launch
+  // spread over the grid stages x once (its launch overlaps the weight
+  // prefetch under programmatic dependent launch).  Either way the fragments,
+  // and so the results, are the same.
+  const long long stage_items = (long long)slots * (k / 8) / (geo.warps * 32);
+  const bool staged = gemv_can_stage(ntb, k, geo.warps) && stage_items <= 2 * geo.units_per_warp;
   int rc = ensure_gemv_scratch(ctx, staged ? 0 : k, n_tiles);
   if (rc) return rc;
   GemvParams p{};
