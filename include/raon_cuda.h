@@ -82,6 +82,18 @@ int rc_upload_q4nx(rc_ctx *ctx, const uint8_t *packed, size_t nbytes, int n, int
  * Synchronous; RC_ERR_INVALID for non-finite input, as the reference. */
 int rc_quantize_q4nx(rc_ctx *ctx, const float *w_dev, int n, int k, uint8_t *packed_dev, void *stream);
 
+/* Upload a bfp16ebs8 matrix (9-bit block floating point: 8-column groups
+ * sharing an exponent byte, int8 mantissas; the reference's second weight
+ * format, quant/bfp16.py:1-60) from the reference's GEMV packing
+ * ``pack_bfp16_gemv`` (quant/bfp16.py:190-292), N*K*9/8 bytes, kept unchanged
+ * in HBM.  rc_gemv / rc_gemv_host then compute its GEMV as the reference's
+ * kernels/gemv_bfp16 does (reference.py:118-182: exact products with bf16
+ * activations, f32 accumulation, RTNE), bf16 activations only; the MoE, the
+ * q4nx dequantiser and rc_gemv_noalloc take q4nx matrices only.  Flags:
+ * RC_UPLOAD_SRC_DEVICE. */
+int rc_upload_bfp16(rc_ctx *ctx, const uint8_t *packed, size_t nbytes, int n, int k, unsigned flags,
+                    rc_weight **out);
+
 int rc_weight_free(rc_weight *w);
 int rc_weight_info(const rc_weight *w, int *n, int *k, size_t *device_bytes, unsigned *flags);
 

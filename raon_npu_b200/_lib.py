@@ -48,6 +48,7 @@ SIGNATURES = {
     "rc_sync": (_I, [_P]),
     "rc_sm_count": (_I, [_P, ctypes.POINTER(_I)]),
     "rc_upload_q4nx": (_I, [_P, _P, _SZ, _I, _I, _U, ctypes.POINTER(_P)]),
+    "rc_upload_bfp16": (_I, [_P, _P, _SZ, _I, _I, _U, ctypes.POINTER(_P)]),
     "rc_quantize_q4nx": (_I, [_P, _P, _I, _I, _P, _P]),
     "rc_weight_free": (_I, [_P]),
     "rc_weight_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_SZ), ctypes.POINTER(_U)]),

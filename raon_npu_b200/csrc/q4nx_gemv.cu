@@ -820,6 +820,13 @@ int rc_gemv(rc_ctx *ctx, const rc_weight *w, const void *x_dev, int x_dtype, int
   RC_CHECK_ARG(ldy >= nrows, "rc_gemv: ldy (%d) < nrows (%d)", ldy, nrows);
   RC_CUDA_TRY(cudaSetDevice(ctx->device));
   const cudaStream_t s = pick_stream(ctx, stream);
+  if (w->format == kFormatBfp16) {
+    RC_CHECK_ARG(x_dtype == RC_DTYPE_BF16, "rc_gemv: a bfp16ebs8 matrix takes bf16 activations");
+    RC_CHECK_ARG((ldx % 8) == 0 && (reinterpret_cast<uintptr_t>(x_dev) & 15) == 0,
+                 "rc_gemv: bfp16ebs8 activations must be 16-byte aligned rows (ldx a multiple of 8)");
+    return bfp16_gemv(ctx, w, static_cast<const uint16_t *>(x_dev), ldx, T, y_dev, y_dtype, ldy, row0, nrows,
+                      bias_dev ? bias_dev + row0 : nullptr, s);
+  }
   const int per = x_dtype == RC_DTYPE_F32 ? kMaxTokensPerLaunch / 2 : kMaxTokensPerLaunch;
   const size_t xe = x_dtype == RC_DTYPE_F32 ? 4 : 2;
   const size_t ye = y_dtype == RC_DTYPE_F32 ? 4 : 2;
@@ -871,6 +878,7 @@ int rc_gemv_noalloc(const rc_weight *w, const void *x_dev, int x_dtype, int ldx,
     return RC_ERR_NOT_FOUND;
   }
   rc_ctx *ctx = w->ctx;
+  RC_CHECK_ARG(w->format == kFormatQ4nx, "rc_gemv_noalloc: takes q4nx matrices only");
   RC_CHECK_ARG(!(w->flags & RC_UPLOAD_GATE_UP), "rc_gemv_noalloc: a gate/up-interleaved matrix is only usable by the MoE path");
   RC_CHECK_ARG(x_dtype == RC_DTYPE_BF16 || x_dtype == RC_DTYPE_F32, "rc_gemv_noalloc: x_dtype must be BF16 or F32");
   RC_CHECK_ARG(y_dtype == RC_DTYPE_F32 || (y_dtype == RC_DTYPE_BF16 && x_dtype == RC_DTYPE_BF16),

@@ -322,6 +322,7 @@ int rc_weight_info(const rc_weight *w, int *n, int *k, size_t *device_bytes, uns
 }
 
 int rc_dequant_q4nx(rc_ctx *ctx, const rc_weight *w, float *out_dev, void *stream) {
+  RC_CHECK_ARG(!w || w->format == kFormatQ4nx, "rc_dequant_q4nx: not a q4nx matrix");
   RC_CHECK_ARG(ctx && out_dev, "rc_dequant_q4nx: NULL argument");
   if (!w) {
     set_error("rc_dequant_q4nx: unknown weight handle");

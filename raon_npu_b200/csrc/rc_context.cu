@@ -166,6 +166,7 @@ int rc_destroy(rc_ctx *ctx) {
   cudaFree(ctx->xfrag);
   cudaFree(ctx->gsum);
   cudaFree(ctx->partials);
+  cudaFree(ctx->bf_partials);
   cudaFree(ctx->counters);
   cudaFree(ctx->err);
   cudaFree(ctx->qflag);

@@ -75,11 +75,16 @@ void set_error(const char *fmt, ...);
 
 }  // namespace rc
 
+// weight formats
+constexpr int kFormatQ4nx = 0;    // 4-bit codes with per-32-column scale/min (t16 units)
+constexpr int kFormatBfp16 = 1;   // 9-bit bfp16ebs8 in the reference's GEMV packing
+
 struct rc_weight {
   rc_ctx *ctx;
   int n, k;            // logical rows (N) and columns (K)
   unsigned flags;      // RC_UPLOAD_* flags it was uploaded with
-  uint8_t *tiles;      // t16 layout, n/16 * k/256 units
+  int format;          // kFormatQ4nx or kFormatBfp16
+  uint8_t *tiles;      // q4nx: t16 layout, n/16 * k/256 units; bfp16: the reference's packed bytes
   size_t bytes;
   float *bias;         // optional f32 [n] on the device
 };
@@ -94,6 +99,8 @@ struct rc_ctx {
   float *gsum;          // kXSlots x aux words of 2 token blocks (group-sum fragments, block scales)
   unsigned launch_seq;  // picks the activation slot of the next launch
   float *partials;      // [warps][2][2 token blocks][32 lanes][4]
+  float *bf_partials;   // bfp16 GEMV k-slice partials [slices][T][rows]
+  size_t bf_partials_cap;
   int *counters;        // [tiles], all zero between launches
   size_t counters_cap;
   int *err;             // device error word
@@ -114,6 +121,8 @@ int ensure_gemv_scratch(rc_ctx *ctx, int k, int n_tiles);
 int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb);
 int ensure_sample_scratch(rc_ctx *ctx, size_t bytes);
 int check_error_word(rc_ctx *ctx);
+int bfp16_gemv(rc_ctx *ctx, const rc_weight *w, const uint16_t *x, int ldx, int T, void *y, int y_dtype, int ldy,
+               int row0, int nrows, const float *bias, cudaStream_t s);   // bfp16_gemv.cu
 // Words of one xfrag slot / floats of one aux slot for K columns (2 token blocks).
 inline size_t xfrag_slot_words(size_t k) { return 2 * k * 4; }
 inline size_t gsum_slot_floats(size_t k) { return 17 * k / 16; }

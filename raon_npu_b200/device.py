@@ -82,6 +82,10 @@ class Context:
     def upload_q4nx(self, packed, n: int, k: int, gate_up: bool = False) -> "Q4nxWeight":
         return Q4nxWeight(self, packed, n, k, gate_up=gate_up)
 
+    def upload_bfp16(self, packed, n: int, k: int) -> "Bfp16Weight":
+        """A bfp16ebs8 matrix from the reference's ``pack_bfp16_gemv`` bytes (N*K*9/8)."""
+        return Bfp16Weight(self, packed, n, k)
+
     def quantize_q4nx(self, w_dev, packed_dev, n: int, k: int, stream: int | None = None) -> None:
         """f32 [n, k] device weights -> pack_gemv bytes on the device (synchronous)."""
         check(self.lib.rc_quantize_q4nx(self.handle, ctypes.c_void_p(_ptr(w_dev)), int(n), int(k),
@@ -129,6 +133,8 @@ def add_rms_bf16(ctx: "Context", a_dev, b_dev, out_dev, eps: float = 1e-6, strea
 
 class Q4nxWeight:
     """A q4nx matrix resident in HBM in the GEMV tile layout."""
+    _UPLOAD = "rc_upload_q4nx"
+    _BITS = 5
 
     def __init__(self, ctx: Context, packed, n: int, k: int, gate_up: bool = False):
         self.ctx = ctx
@@ -146,12 +152,12 @@ class Q4nxWeight:
                 import torch
                 torch.cuda.current_stream(packed.device).synchronize()
         h = ctypes.c_void_p()
-        check(ctx.lib.rc_upload_q4nx(ctx.handle, ctypes.c_void_p(src), nbytes, int(n), int(k), flags,
-                                     ctypes.byref(h)), "rc_upload_q4nx")
+        check(getattr(ctx.lib, self._UPLOAD)(ctx.handle, ctypes.c_void_p(src), nbytes, int(n), int(k), flags,
+                                             ctypes.byref(h)), self._UPLOAD)
         del keep
         self.handle = h
         self.n, self.k, self.gate_up = int(n), int(k), bool(gate_up)
-        self.device_bytes = n * k * 5 // 8
+        self.device_bytes = n * k * self._BITS // 8
         ctx._adopt(self)
 
     def set_bias(self, bias: np.ndarray) -> int:
@@ -231,6 +237,17 @@ class Q4nxWeight:
 
 ACT_CODES = {"swiglu": _lib.RC_ACT_SWIGLU, "situ": _lib.RC_ACT_SITU}
 ROUTER_CODES = {"softmax": _lib.RC_ROUTER_SOFTMAX, "sigmoid_bias": _lib.RC_ROUTER_SIGMOID_BIAS}
+
+
+class Bfp16Weight(Q4nxWeight):
+    """A bfp16ebs8 matrix (9-bit block floating point, the reference's
+    ``quant/bfp16.py``) resident in HBM in the reference's GEMV packing; used
+    through the same ``gemv_into`` / ``gemv_host`` calls (bf16 activations)."""
+    _UPLOAD = "rc_upload_bfp16"
+    _BITS = 9
+
+    def __init__(self, ctx: Context, packed, n: int, k: int):
+        super().__init__(ctx, packed, n, k, gate_up=False)
 
 
 def _buf(packed):
