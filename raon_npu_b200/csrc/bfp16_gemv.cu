@@ -15,10 +15,11 @@
 // (one CTA of 16 warps per SM), each warp streaming its items' units through a
 // ring of bulk copies.  A lane takes 4 rows (row quad j) of 4 groups (group
 // octet): per group it turns the 32 mantissas into f32 exactly (a byte
-// permute onto 2**23 and one subtraction), sums each row's 8 products with the
-// token's activations in f32 (the products of an 8-bit mantissa and a bf16
-// value are exact), and adds the sum times the group's power-of-two scale
-// (exact) into the row's accumulator.  The 8 lanes of a row quad are summed
+// permute onto 2**23, then one packed subtraction per two), sums each row's 8
+// products with the token's activations in packed f32x2 lanes (columns 2c
+// and 2c + 1; the products of an 8-bit mantissa and a bf16 value are exact),
+// and adds the sum times the group's power-of-two scale (exact) into the
+// row's accumulator.  The 8 lanes of a row quad are summed
 // at the item's end.  With one k-slice the epilogue writes y; with several,
 // f32 partials go to scratch and a finalize pass sums them in slice order, so
 // the result does not depend on timing.
@@ -56,11 +57,11 @@ __device__ __forceinline__ const uint8_t *bf_unit(const uint8_t *w, int t, int k
   return w + ((size_t)((size_t)slice * KB + kb) * 4 + r) * kBfBlockBytes + half * kBfUnitBytes;
 }
 
-// Exact int8 -> f32 for byte b of a word whose bytes were XOR'd with 0x80:
-// 0x4B0000bb is 2**23 + (m + 128).
-__device__ __forceinline__ float bf_byte_f32(uint32_t biased, int b) {
-  const uint32_t bits = __byte_perm(biased, 0x4B000000u, 0x7440u | (uint32_t)b);
-  return __uint_as_float(bits) - 8388736.0f;        // 2**23 + 128
+// Byte b of a word whose bytes were XOR'd with 0x80, as the f32 2**23 +
+// (m + 128) (bits 0x4B0000bb); subtracting 2**23 + 128 leaves the int8
+// mantissa m exactly.
+__device__ __forceinline__ float bf_byte_bits(uint32_t biased, int b) {
+  return __uint_as_float(__byte_perm(biased, 0x4B000000u, 0x7440u | (uint32_t)b));
 }
 
 template <int TB, bool F32OUT>
@@ -122,12 +123,16 @@ __global__ void __launch_bounds__(kBfThreads, 1) bfp16_gemv_kernel(BfParams p) {
         const int g = go * 4 + i;                   // group of this unit (8 columns)
         const uint8_t *G = U + g * kBfGroupBytes;
         const uint32_t ew = *reinterpret_cast<const uint32_t *>(G + 4 * j);   // exponents of rows 4j..4j+3
-        float mf[8][4];
+        // mantissas of rows 4j..4j+3 as f32 pairs of adjacent columns (2cp, 2cp+1)
+        float2 mf[4][4];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t mw = *reinterpret_cast<const uint32_t *>(G + 16 + 16 * c + 4 * j) ^ 0x80808080u;
+        for (int cp = 0; cp < 4; ++cp) {
+          const uint32_t m0 = *reinterpret_cast<const uint32_t *>(G + 16 + 32 * cp + 4 * j) ^ 0x80808080u;
+          const uint32_t m1 = *reinterpret_cast<const uint32_t *>(G + 32 + 32 * cp + 4 * j) ^ 0x80808080u;
 #pragma unroll
-          for (int r = 0; r < 4; ++r) mf[c][r] = bf_byte_f32(mw, r);
+          for (int r = 0; r < 4; ++r)
+            mf[r][cp] = __fadd2_rn(make_float2(bf_byte_bits(m0, r), bf_byte_bits(m1, r)),
+                                   make_float2(-8388736.0f, -8388736.0f));   // 2**23 + 128
         }
         float sc[4];
 #pragma unroll
@@ -142,18 +147,15 @@ __global__ void __launch_bounds__(kBfThreads, 1) bfp16_gemv_kernel(BfParams p) {
           if (tk < p.tokens) {
             const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(p.x + (size_t)tk * p.ldx + col));
             const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-            float xf[8];
+            float2 xf[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              xf[2 * q] = bf16_lo_f32(xw[q]);
-              xf[2 * q + 1] = bf16_hi_f32(xw[q]);
-            }
+            for (int q = 0; q < 4; ++q) xf[q] = make_float2(bf16_lo_f32(xw[q]), bf16_hi_f32(xw[q]));
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-              float s = mf[0][r] * xf[0];
+              float2 s2 = __fmul2_rn(mf[r][0], xf[0]);
 #pragma unroll
-              for (int c = 1; c < 8; ++c) s = fmaf(mf[c][r], xf[c], s);
-              acc[r][tk] = fmaf(sc[r], s, acc[r][tk]);
+              for (int cp = 1; cp < 4; ++cp) s2 = __ffma2_rn(mf[r][cp], xf[cp], s2);
+              acc[r][tk] = fmaf(sc[r], s2.x + s2.y, acc[r][tk]);
             }
           }
         }
