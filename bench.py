@@ -231,8 +231,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # Per-shape launch times (rank 0): back-to-back launches over rotating
     # copies whose total exceeds L2, so each launch streams from HBM.
     per_shape = []
+    bfp16 = None
     if rank == 0 and not args.no_per_shape:
         per_shape = measure_per_shape(ctx, torch, dev, gen, stream, weights)
+        bfp16 = measure_bfp16(ctx, torch, dev, gen)
 
     # End to end through the host-buffer C-ABI entry point (rc_gemv_host):
     # pinned host x -> device, GEMV, y -> host, every GEMV of the step.
@@ -290,6 +292,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
             "per_shape": per_shape,
+            "bfp16": bfp16,
             "cpu_baseline": cpu,
             "moe": moe,
             "moe_prefill": prefill,
@@ -297,6 +300,59 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         }
         print(json.dumps(line), flush=True)
     ctx.close()
+
+
+def measure_bfp16(ctx, torch, dev, gen):
+    """The bfp16ebs8 GEMV (the reference's second weight format, rc_upload_bfp16
+    + rc_gemv) on the sweep's shapes: synthetic packed blocks made on the device
+    (exponent bytes 118..124, i.e. weights around 2^-9..2^-3, random int8
+    mantissas), back-to-back launches over rotating copies larger than L2."""
+    peak, _ = peaks()
+    out = []
+    for n, k in SHAPES:
+        nbytes = n * k * 9 // 8
+        copies = max(1, min(64, (400 << 20) // nbytes))
+        cps = []
+        for c in range(copies):
+            gen.manual_seed(9000 + n + k + c)
+            blk = torch.randint(0, 256, (nbytes // 144, 144), generator=gen, device=dev, dtype=torch.uint8)
+            blk[:, :16] = torch.randint(118, 125, (nbytes // 144, 16), generator=gen, device=dev, dtype=torch.uint8)
+            cps.append(ctx.upload_bfp16(blk.view(-1), n, k))
+            del blk
+        launches = max(20, min(200, copies * 2))
+        for t in TOKENS:
+            x = torch.randn((t, k), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16).contiguous()
+            y = torch.empty((t, n), dtype=torch.int16, device=dev)
+            for i in range(min(launches, 10)):
+                cps[i % len(cps)].gemv_into(x, y, t)
+            torch.cuda.synchronize()
+
+            def seq():
+                for i in range(launches):
+                    cps[i % len(cps)].gemv_into(x, y, t)
+            g = capture_graph(torch, seq)
+            g.replay()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            st = torch.cuda.current_stream(dev)
+            e0.record(st)
+            g.replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / launches
+            del g
+            gbs = (nbytes + 2 * t * (n + k)) / (us * 1e-6) / 1e9
+            out.append({"k_to_n": f"{k}->{n}", "t": t, "us_per_launch": round(us, 3), "gbs": round(gbs, 1),
+                        "frac": round(gbs / peak, 4), "copies": len(cps)})
+        for w in cps:
+            w.free()
+    ctx.sync()
+    lm = [e for e in out if e["k_to_n"] == f"{LM_HEAD[1]}->{LM_HEAD[0]}"]
+    return {"workload": "bfp16ebs8 GEMV (9-bit weights, 8-column groups; SURVEY 8(f) row 1)",
+            "bytes_per_weight": 9 / 8, "kernel": "bfp16_gemv_kernel (16-row half blocks by bulk copy, "
+            "f32x2 CUDA-core products; split-K with ordered finalize for small N)",
+            "lm_head": {e["t"]: {"gbs": e["gbs"], "frac": e["frac"]} for e in lm}, "per_shape": out}
 
 
 def measure_per_shape(ctx, torch, dev, gen, stream, weights):
