@@ -1101,19 +1101,28 @@ def run_reference(args, rank: int):
 
 def run_profile_case(args):
     """A few plain launches of one GEMV shape (no timing) for an ncu capture:
-    ``python bench.py --profile 4096x2048 --tokens 1 --launches 4``."""
+    ``python bench.py --profile 4096x2048 --tokens 1 --launches 4`` (q4nx) or
+    ``--profile bfp16:151936x2048`` (bfp16ebs8)."""
     import torch
     from raon_npu_b200.device import Context
-    n, k = (int(v) for v in args.profile.split("x"))
+    bfp16 = args.profile.startswith("bfp16:")
+    n, k = (int(v) for v in args.profile.split(":")[-1].split("x"))
     dev = torch.device("cuda", 0)
     ctx = Context(0)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1)
-    w = torch.randn((n, k), generator=gen, device=dev) * 0.02
-    packed = torch.empty(n * k * 5 // 8, dtype=torch.uint8, device=dev)
-    ctx.quantize_q4nx(w, packed, n, k)
-    copies = max(1, min(64, (256 << 20) // (n * k * 5 // 8)))
-    ws = [ctx.upload_q4nx(packed, n, k) for _ in range(copies)]
+    if bfp16:   # ``--profile bfp16:NxK``: synthetic bfp16ebs8 blocks as in measure_bfp16
+        nbytes = n * k * 9 // 8
+        packed = torch.randint(0, 256, (nbytes // 144, 144), generator=gen, device=dev, dtype=torch.uint8)
+        packed[:, :16] = torch.randint(118, 125, (nbytes // 144, 16), generator=gen, device=dev, dtype=torch.uint8)
+        copies = max(1, min(64, (256 << 20) // nbytes))
+        ws = [ctx.upload_bfp16(packed.view(-1), n, k) for _ in range(copies)]
+    else:
+        w = torch.randn((n, k), generator=gen, device=dev) * 0.02
+        packed = torch.empty(n * k * 5 // 8, dtype=torch.uint8, device=dev)
+        ctx.quantize_q4nx(w, packed, n, k)
+        copies = max(1, min(64, (256 << 20) // (n * k * 5 // 8)))
+        ws = [ctx.upload_q4nx(packed, n, k) for _ in range(copies)]
     x = torch.randn((args.tokens, k), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16)
     y = torch.empty((args.tokens, n), dtype=torch.int16, device=dev)
     for i in range(args.launches):
