@@ -1,0 +1,233 @@
+"""On-disk weight bundles: read the exporter's ``manifest.json`` + ``*.bin``
+files, verify them, and upload them straight to the GPU.
+
+Follows the reference's bundle contract (``npu/backend.py:104-117`` the
+bundle record, ``:285-346`` path resolution and verification, ``:729-752``
+canonical sizes, ``:1095-1118`` expert slices; ``export/README.md`` the
+manifest keys):
+
+* ``manifest.json`` is a dict with a ``bundles`` list (or a bare list); each
+  entry has ``bundle`` (name), ``format`` (``q4nx_gemv``, ``bfp16_gemv``,
+  ``q4nx_gemv_bundle``, ``bfp16_gemv_bundle``; ``host_safetensors`` entries are
+  host tensors and skipped), ``file`` (relative to the manifest), ``size_bytes``,
+  ``original_shape``, ``padded_shape``, ``sha256`` and, for MoE bundles,
+  ``expert_count`` / ``expert_bytes``.
+* A file must resolve inside the weights directory; its size must equal both
+  the manifest's ``size_bytes`` and the canonical size of its format and padded
+  shape (q4nx: 5 bits, bfp16ebs8: 9 bits per weight; MoE bundles: experts x
+  matrix bytes); its SHA-256 must match (checked once per file version: path,
+  size and modification time).
+* A ``*_gemv`` bundle is one [M, K] matrix (its padded shape) in the GEMV
+  packing that ``rc_upload_q4nx`` / ``rc_upload_bfp16`` take unchanged; a
+  ``*_gemv_bundle`` holds ``expert_count`` such matrices back to back.
+
+Errors are the reference's: ``ValueError`` for a bad manifest, size or digest,
+``FileNotFoundError`` for a missing file, ``KeyError`` for an unknown bundle.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import re
+from dataclasses import dataclass
+from pathlib import Path
+
+GEMV_FORMATS = ("q4nx_gemv", "bfp16_gemv")
+MOE_FORMATS = ("q4nx_gemv_bundle", "bfp16_gemv_bundle")
+
+_SHA_CACHE: dict[tuple[str, int, int], str] = {}
+
+
+@dataclass(frozen=True)
+class Bundle:
+    name: str
+    fmt: str
+    file: str
+    size_bytes: int
+    original_shape: tuple[int, ...]
+    padded_shape: tuple[int, ...]
+    sha256: str
+    layer: int | None = None
+    expert_count: int = 0
+    expert_bytes: int = 0
+
+    @property
+    def rows(self) -> int:
+        return self.padded_shape[-2]
+
+    @property
+    def cols(self) -> int:
+        return self.padded_shape[-1]
+
+    @property
+    def weight_format(self) -> str:
+        return "q4nx" if self.fmt.startswith("q4nx") else "bfp16"
+
+
+def matrix_bytes(fmt: str, rows: int, cols: int) -> int:
+    """Packed bytes of one [rows, cols] matrix (``npu/backend.py:729-752``)."""
+    if fmt.startswith("q4nx"):
+        if rows % 32 or cols % 256:
+            raise ValueError(f"q4nx shape [{rows}, {cols}] is not tile-aligned (32 x 256)")
+        return rows * cols * 5 // 8
+    if fmt.startswith("bfp16"):
+        if cols % 8:
+            raise ValueError(f"bfp16 shape [{rows}, {cols}] is not block-aligned (8 columns)")
+        return rows * (cols // 8) * 9
+    raise ValueError(f"unknown bundle format {fmt!r}")
+
+
+def _positive_int(v) -> bool:
+    return isinstance(v, int) and not isinstance(v, bool) and v >= 0
+
+
+def read_manifest(weights_dir) -> dict[str, Bundle]:
+    """Parse and validate ``weights_dir/manifest.json``; no file is read besides it."""
+    root = Path(weights_dir)
+    payload = json.loads((root / "manifest.json").read_text())
+    if isinstance(payload, dict):
+        entries = payload.get("bundles")
+        if not isinstance(entries, list):
+            raise ValueError("manifest dict missing 'bundles' list")
+    elif isinstance(payload, list):
+        entries = payload
+    else:
+        raise ValueError("invalid manifest top-level structure")
+    out: dict[str, Bundle] = {}
+    for item in entries:
+        if not isinstance(item, dict):
+            raise ValueError(f"invalid manifest bundle entry: {item!r}")
+        fmt = item.get("format")
+        if fmt == "host_safetensors":
+            continue
+        name = item.get("bundle")
+        if not isinstance(name, str) or not name:
+            raise ValueError(f"manifest bundle entry without a name: {item!r}")
+        if name in out:
+            raise ValueError(f"duplicate bundle in manifest: {name}")
+        if fmt not in GEMV_FORMATS + MOE_FORMATS:
+            raise ValueError(f"unknown format {fmt!r} for bundle {name}")
+        rel = item.get("file")
+        if not isinstance(rel, str) or not rel:
+            raise ValueError(f"manifest file missing for {name}")
+        size = item.get("size_bytes")
+        if not _positive_int(size):
+            raise ValueError(f"invalid size_bytes for {name}: {size!r}")
+        sha = item.get("sha256")
+        if not isinstance(sha, str) or not re.fullmatch(r"[0-9a-fA-F]{64}", sha):
+            raise ValueError(f"invalid sha256 for {name}: {sha!r}")
+        padded, orig = item.get("padded_shape"), item.get("original_shape")
+        dims = 3 if fmt in MOE_FORMATS else 2
+        for key, shape in (("padded_shape", padded), ("original_shape", orig)):
+            if not (isinstance(shape, list) and len(shape) == dims and all(_positive_int(v) and v > 0 for v in shape)):
+                raise ValueError(f"invalid {key} for {name}: {shape!r}")
+        if any(o > p for o, p in zip(orig[-2:], padded[-2:])):
+            raise ValueError(f"original_shape {orig} exceeds padded_shape {padded} for {name}")
+        mbytes = matrix_bytes(fmt, padded[-2], padded[-1])
+        count = ebytes = 0
+        if fmt in MOE_FORMATS:
+            count, ebytes = item.get("expert_count"), item.get("expert_bytes")
+            if not _positive_int(count) or count != padded[0] or orig[0] != padded[0]:
+                raise ValueError(f"expert_count mismatch for {name}: {count!r} vs shape {padded}")
+            if ebytes != mbytes:
+                raise ValueError(f"expert_bytes mismatch for {name}: {ebytes!r} != {mbytes}")
+            canonical = mbytes * count
+        else:
+            canonical = mbytes
+        if size != canonical:
+            raise ValueError(f"canonical size_bytes mismatch for {name}: {size} != {canonical}")
+        _resolve(root, rel, name)
+        out[name] = Bundle(name=name, fmt=fmt, file=rel, size_bytes=size, original_shape=tuple(orig),
+                           padded_shape=tuple(padded), sha256=sha.lower(), layer=item.get("layer"),
+                           expert_count=count, expert_bytes=ebytes)
+    return out
+
+
+def _resolve(root: Path, rel: str, name: str) -> Path:
+    """The bundle file, which must lie inside the weights directory (``npu/backend.py:285-291``)."""
+    base = root.resolve()
+    path = (base / rel).resolve()
+    try:
+        path.relative_to(base)
+    except ValueError as exc:
+        raise ValueError(f"manifest file escapes the weights directory for {name}: {rel!r}") from exc
+    return path
+
+
+def verify(weights_dir, b: Bundle) -> Path:
+    """Size and SHA-256 of a bundle file, streamed; cached per file version (``npu/backend.py:319-346``)."""
+    path = _resolve(Path(weights_dir), b.file, b.name)
+    try:
+        st = path.stat()
+    except FileNotFoundError as exc:
+        raise FileNotFoundError(f"missing bundle binary: {path}") from exc
+    if st.st_size != b.size_bytes:
+        raise ValueError(f"size_bytes mismatch for {b.name}: file has {st.st_size}, manifest has {b.size_bytes}")
+    key = (str(path), st.st_size, st.st_mtime_ns)
+    digest = _SHA_CACHE.get(key)
+    if digest is None:
+        h = hashlib.sha256()
+        with path.open("rb") as f:
+            for block in iter(lambda: f.read(1 << 20), b""):
+                h.update(block)
+        digest = h.hexdigest()
+    if digest != b.sha256:
+        raise ValueError(f"sha256 mismatch for {b.name}: {digest} != {b.sha256}")
+    _SHA_CACHE[key] = digest
+    return path
+
+
+def read_matrix(weights_dir, b: Bundle, expert: int | None = None) -> bytes:
+    """The packed bytes of a ``*_gemv`` bundle, or of one expert of a
+    ``*_gemv_bundle`` (``npu/backend.py:1095-1118``), after verification."""
+    path = verify(weights_dir, b)
+    if b.fmt in GEMV_FORMATS:
+        if expert is not None:
+            raise ValueError(f"{b.name} is a single matrix, not an expert bundle")
+        return path.read_bytes()
+    if expert is None or not (0 <= expert < b.expert_count):
+        raise ValueError(f"invalid expert slice request: {b.name} expert={expert}")
+    with path.open("rb") as f:
+        f.seek(expert * b.expert_bytes)
+        chunk = f.read(b.expert_bytes)
+    if len(chunk) != b.expert_bytes:
+        raise ValueError(f"short read in {path} for expert {expert}: got {len(chunk)}, expected {b.expert_bytes}")
+    return chunk
+
+
+class BundleLoader:
+    """Uploads verified bundles of a weights directory to a ``device.Context``."""
+
+    def __init__(self, ctx, weights_dir):
+        self.ctx = ctx
+        self.dir = Path(weights_dir)
+        self.bundles = read_manifest(self.dir)
+
+    def __getitem__(self, name: str) -> Bundle:
+        try:
+            return self.bundles[name]
+        except KeyError:
+            raise KeyError(f"unknown bundle {name!r}") from None
+
+    def upload(self, name: str, expert: int | None = None):
+        """A ``Q4nxWeight`` / ``Bfp16Weight`` of the bundle's matrix (padded shape)."""
+        import numpy as np
+        b = self[name]
+        data = np.frombuffer(read_matrix(self.dir, b, expert), dtype=np.uint8)
+        if b.weight_format == "q4nx":
+            return self.ctx.upload_q4nx(data, b.rows, b.cols)
+        return self.ctx.upload_bfp16(data, b.rows, b.cols)
+
+    def load_moe_experts(self, layer, gate_up: str, down: str, experts=None) -> None:
+        """Feed a ``MoeLayer`` its experts from two q4nx expert bundles (gate/up
+        [2I, H] and K-padded down [H, I_pad], the MoE's packing; ``experts``
+        defaults to all of them, the shared one being id E if present)."""
+        gu, dn = self[gate_up], self[down]
+        for b in (gu, dn):
+            if b.fmt != "q4nx_gemv_bundle":
+                raise ValueError(f"{b.name}: the MoE layer takes q4nx expert bundles, not {b.fmt}")
+        if gu.expert_count != dn.expert_count:
+            raise ValueError(f"expert counts differ: {gu.name} {gu.expert_count}, {dn.name} {dn.expert_count}")
+        for e in (range(gu.expert_count) if experts is None else experts):
+            layer.set_expert(e, read_matrix(self.dir, gu, e), read_matrix(self.dir, dn, e))

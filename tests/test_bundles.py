@@ -1,0 +1,154 @@
+"""On-disk bundles (``raon_npu_b200.bundles``): manifest validation, file
+verification and expert slices on CPU, following the reference's bundle
+contract (``npu/backend.py:104-117,285-346,729-752,1095-1118``); one GPU test
+that a bundle-uploaded matrix computes exactly what the direct upload does."""
+
+from __future__ import annotations
+
+import hashlib
+import json
+
+import numpy as np
+import pytest
+
+from raon_npu_b200 import bundles as bd
+
+
+def _write(tmp, entries, files):
+    """files: rel -> bytes; entries: manifest bundle dicts (sha/size filled in when absent)."""
+    for rel, data in files.items():
+        p = tmp / rel
+        p.parent.mkdir(parents=True, exist_ok=True)
+        p.write_bytes(data)
+    for e in entries:
+        data = files.get(e["file"], b"")
+        e.setdefault("size_bytes", len(data))
+        e.setdefault("sha256", hashlib.sha256(data).hexdigest())
+    (tmp / "manifest.json").write_text(json.dumps({"version": "1.0", "bundles": entries}))
+
+
+def _entry(name, fmt, rel, shape, **kw):
+    e = {"bundle": name, "format": fmt, "file": rel, "original_shape": list(shape), "padded_shape": list(shape)}
+    e.update(kw)
+    return e
+
+
+def _rand(n, seed=0):
+    return np.random.default_rng(seed).integers(0, 256, n, dtype=np.uint8).tobytes()
+
+
+@pytest.fixture
+def good(tmp_path):
+    files = {"L00/proj.bin": _rand(128 * 256 * 5 // 8, 1), "lm_head.bin": _rand(128 * 512 * 9 // 8, 2),
+             "L01/moe_b1.bin": _rand(3 * 256 * 256 * 5 // 8, 3)}
+    entries = [_entry("L00/proj", "q4nx_gemv", "L00/proj.bin", (128, 256), layer=0),
+               _entry("lm_head", "bfp16_gemv", "lm_head.bin", (128, 512)),
+               _entry("L01/moe_b1", "q4nx_gemv_bundle", "L01/moe_b1.bin", (3, 256, 256), layer=1,
+                      expert_count=3, expert_bytes=256 * 256 * 5 // 8),
+               {"bundle": "host_global", "format": "host_safetensors", "file": "host_global.safetensors"}]
+    _write(tmp_path, entries, files)
+    return tmp_path, files
+
+
+def test_manifest_reads_and_slices(good):
+    root, files = good
+    m = bd.read_manifest(root)
+    assert set(m) == {"L00/proj", "lm_head", "L01/moe_b1"}          # host tensors are skipped
+    assert m["lm_head"].weight_format == "bfp16" and (m["lm_head"].rows, m["lm_head"].cols) == (128, 512)
+    assert bd.read_matrix(root, m["L00/proj"]) == files["L00/proj.bin"]
+    eb = m["L01/moe_b1"].expert_bytes
+    for e in range(3):
+        assert bd.read_matrix(root, m["L01/moe_b1"], e) == files["L01/moe_b1.bin"][e * eb:(e + 1) * eb]
+    with pytest.raises(ValueError):
+        bd.read_matrix(root, m["L01/moe_b1"], 3)
+    with pytest.raises(ValueError):
+        bd.read_matrix(root, m["L00/proj"], 0)
+
+
+def test_bare_list_manifest(tmp_path):
+    files = {"a.bin": _rand(128 * 256 * 5 // 8)}
+    _write(tmp_path, [_entry("a", "q4nx_gemv", "a.bin", (128, 256))], files)
+    payload = json.loads((tmp_path / "manifest.json").read_text())["bundles"]
+    (tmp_path / "manifest.json").write_text(json.dumps(payload))
+    assert list(bd.read_manifest(tmp_path)) == ["a"]
+
+
+@pytest.mark.parametrize("change, message", [
+    (lambda e: e.update(size_bytes=e["size_bytes"] + 1), "size_bytes"),
+    (lambda e: e.update(sha256="xyz"), "sha256"),
+    (lambda e: e.update(file="../outside.bin"), "escapes"),
+    (lambda e: e.update(format="q8_gemv"), "unknown format"),
+    (lambda e: e.update(padded_shape=[128, 300], original_shape=[128, 300]), "tile-aligned"),
+    (lambda e: e.update(original_shape=[256, 256]), "exceeds"),
+])
+def test_manifest_rejections(tmp_path, change, message):
+    files = {"a.bin": _rand(128 * 256 * 5 // 8)}
+    e = _entry("a", "q4nx_gemv", "a.bin", (128, 256))
+    _write(tmp_path, [e], files)
+    change(e)
+    (tmp_path / "manifest.json").write_text(json.dumps({"bundles": [e]}))
+    with pytest.raises(ValueError, match=message):
+        bd.read_manifest(tmp_path)
+
+
+def test_duplicate_and_expert_geometry(tmp_path):
+    files = {"a.bin": _rand(128 * 256 * 5 // 8), "m.bin": _rand(2 * 128 * 256 * 5 // 8)}
+    a = _entry("a", "q4nx_gemv", "a.bin", (128, 256))
+    _write(tmp_path, [a, dict(a)], files)
+    with pytest.raises(ValueError, match="duplicate"):
+        bd.read_manifest(tmp_path)
+    m = _entry("m", "q4nx_gemv_bundle", "m.bin", (2, 128, 256), expert_count=2, expert_bytes=999)
+    _write(tmp_path, [m], files)
+    with pytest.raises(ValueError, match="expert_bytes"):
+        bd.read_manifest(tmp_path)
+
+
+def test_file_tampering_detected(good):
+    root, files = good
+    m = bd.read_manifest(root)
+    data = bytearray(files["L00/proj.bin"])
+    data[5] ^= 1
+    (root / "L00/proj.bin").write_bytes(bytes(data))
+    with pytest.raises(ValueError, match="sha256"):
+        bd.read_matrix(root, m["L00/proj"])
+    (root / "lm_head.bin").write_bytes(files["lm_head.bin"][:-9])
+    with pytest.raises(ValueError, match="size_bytes"):
+        bd.read_matrix(root, m["lm_head"])
+    (root / "lm_head.bin").unlink()
+    with pytest.raises(FileNotFoundError):
+        bd.read_matrix(root, m["lm_head"])
+
+
+@pytest.mark.gpu
+def test_bundle_upload_matches_direct_upload(tmp_path):
+    import torch
+    from oracle import bfp16 as ob16
+    from oracle import q4nx as oq
+    from raon_npu_b200.build import build
+    from raon_npu_b200.device import Context
+    build()
+    rng = np.random.default_rng(11)
+    wq = (rng.standard_normal((256, 512)) * 0.02).astype(np.float32)
+    q = oq.pack_gemv(*oq.quantize(wq))
+    wb = (rng.standard_normal((384, 512)) * 0.02).astype(np.float32)
+    bb = ob16.pack_gemv(wb)
+    _write(tmp_path, [_entry("q", "q4nx_gemv", "q.bin", (256, 512)), _entry("b", "bfp16_gemv", "b.bin", (384, 512))],
+           {"q.bin": q, "b.bin": bb})
+    ctx = Context(0)
+    try:
+        loader = bd.BundleLoader(ctx, tmp_path)
+        x = torch.randn((3, 512), device="cuda").to(torch.bfloat16).view(torch.int16).contiguous()
+        for name, direct in (("q", ctx.upload_q4nx(np.frombuffer(q, np.uint8), 256, 512)),
+                             ("b", ctx.upload_bfp16(np.frombuffer(bb, np.uint8), 384, 512))):
+            w = loader.upload(name)
+            y0 = torch.empty((3, w.n), dtype=torch.int16, device="cuda")
+            y1 = torch.empty_like(y0)
+            w.gemv_into(x, y0, 3)
+            direct.gemv_into(x, y1, 3)
+            torch.cuda.synchronize()
+            assert torch.equal(y0, y1), name
+            w.free()
+            direct.free()
+        ctx.sync()
+    finally:
+        ctx.close()
