@@ -174,6 +174,29 @@ class CudaBackend(Backend):
         self.register_bundle(name, packed, n, k)
         self.map_name(name, name, 0, n, orig_k=orig_k, bias=bias)
 
+    def load_bundles(self, weights_dir):
+        """Upload every single-matrix bundle (q4nx or bfp16ebs8) of an exporter
+        weights directory (``manifest.json`` + ``*.bin``, size and SHA-256
+        checked) and expose each of its components under the component's name
+        (a bundle without components under its own name), with the unpadded K
+        of ``original_shape`` as the activation width.  Returns the
+        ``BundleLoader``; its ``load_moe_experts`` feeds a registered MoE layer
+        from expert bundles."""
+        from .bundles import GEMV_FORMATS, BundleLoader, Component
+        loader = BundleLoader(self.ctx, weights_dir)
+        for b in loader.bundles.values():
+            if b.fmt not in GEMV_FORMATS:
+                continue
+            w = loader.upload(b.name)
+            old = self._bundles.pop(b.name, None)
+            if old is not None:
+                old.free()
+            self._bundles[b.name] = w
+            orig_k = b.original_shape[-1] if b.original_shape[-1] != b.cols else None
+            for c in b.components or (Component(b.name, 0, b.original_shape[-2]),):
+                self.map_name(c.name, b.name, c.row_start, c.row_end, orig_k=orig_k)
+        return loader
+
     def __contains__(self, name: str) -> bool:
         return name in self._names
 

@@ -10,8 +10,10 @@ manifest keys):
   entry has ``bundle`` (name), ``format`` (``q4nx_gemv``, ``bfp16_gemv``,
   ``q4nx_gemv_bundle``, ``bfp16_gemv_bundle``; ``host_safetensors`` entries are
   host tensors and skipped), ``file`` (relative to the manifest), ``size_bytes``,
-  ``original_shape``, ``padded_shape``, ``sha256`` and, for MoE bundles,
-  ``expert_count`` / ``expert_bytes``.
+  ``original_shape``, ``padded_shape``, ``sha256``, for MoE bundles
+  ``expert_count`` / ``expert_bytes``, and optionally ``components``: the
+  tensors packed into the bundle, each ``{"name", "row_start", "row_end"}``
+  (``npu/backend.py:88-99,893-911``; several projections share one bundle).
 * A file must resolve inside the weights directory; its size must equal both
   the manifest's ``size_bytes`` and the canonical size of its format and padded
   shape (q4nx: 5 bits, bfp16ebs8: 9 bits per weight; MoE bundles: experts x
@@ -40,6 +42,15 @@ _SHA_CACHE: dict[tuple[str, int, int], str] = {}
 
 
 @dataclass(frozen=True)
+class Component:
+    """A named tensor inside a bundle: rows [row_start, row_end) of its matrix."""
+    name: str
+    row_start: int
+    row_end: int
+    expert_id: int | None = None
+
+
+@dataclass(frozen=True)
 class Bundle:
     name: str
     fmt: str
@@ -51,6 +62,7 @@ class Bundle:
     layer: int | None = None
     expert_count: int = 0
     expert_bytes: int = 0
+    components: tuple[Component, ...] = ()
 
     @property
     def rows(self) -> int:
@@ -95,6 +107,7 @@ def read_manifest(weights_dir) -> dict[str, Bundle]:
     else:
         raise ValueError("invalid manifest top-level structure")
     out: dict[str, Bundle] = {}
+    seen_components: set[str] = set()
     for item in entries:
         if not isinstance(item, dict):
             raise ValueError(f"invalid manifest bundle entry: {item!r}")
@@ -138,10 +151,35 @@ def read_manifest(weights_dir) -> dict[str, Bundle]:
         if size != canonical:
             raise ValueError(f"canonical size_bytes mismatch for {name}: {size} != {canonical}")
         _resolve(root, rel, name)
+        comps = _components(item.get("components", []), name, orig[-2], seen_components)
         out[name] = Bundle(name=name, fmt=fmt, file=rel, size_bytes=size, original_shape=tuple(orig),
                            padded_shape=tuple(padded), sha256=sha.lower(), layer=item.get("layer"),
-                           expert_count=count, expert_bytes=ebytes)
+                           expert_count=count, expert_bytes=ebytes, components=comps)
     return out
+
+
+def _components(raw, bundle: str, rows: int, seen: set[str]) -> tuple[Component, ...]:
+    """Validate a bundle's ``components`` list: named entries, unique over the
+    manifest, rows inside the bundle's original rows (absent rows = all of them)."""
+    if not isinstance(raw, list):
+        raise ValueError(f"invalid components for {bundle}: {raw!r}")
+    out = []
+    for c in raw:
+        if not isinstance(c, dict) or not isinstance(c.get("name"), str) or not c["name"]:
+            raise ValueError(f"invalid component entry for {bundle}: {c!r}")
+        cname = c["name"]
+        if cname in seen:
+            raise ValueError(f"duplicate component {cname!r} (bundle {bundle})")
+        seen.add(cname)
+        r0, r1 = c.get("row_start", 0), c.get("row_end", rows)
+        if not (_positive_int(r0) and _positive_int(r1) and r0 < r1 <= rows):
+            raise ValueError(f"row range of component {cname!r} outside bundle {bundle} of {rows} rows: "
+                             f"({r0!r}, {r1!r})")
+        eid = c.get("expert_id")
+        if eid is not None and not _positive_int(eid):
+            raise ValueError(f"invalid expert_id of component {cname!r}: {eid!r}")
+        out.append(Component(cname, r0, r1, eid))
+    return tuple(out)
 
 
 def _resolve(root: Path, rel: str, name: str) -> Path:

@@ -119,6 +119,69 @@ def test_file_tampering_detected(good):
         bd.read_matrix(root, m["lm_head"])
 
 
+def test_components(tmp_path):
+    files = {"a.bin": _rand(128 * 512 * 5 // 8), "b.bin": _rand(128 * 256 * 5 // 8)}
+    a = _entry("a", "q4nx_gemv", "a.bin", (128, 512), original_shape=[120, 448],
+               components=[{"name": "q_proj", "row_start": 0, "row_end": 64},
+                           {"name": "kv_proj", "row_start": 64, "row_end": 120}])
+    b = _entry("b", "q4nx_gemv", "b.bin", (128, 256))
+    _write(tmp_path, [a, b], files)
+    m = bd.read_manifest(tmp_path)
+    assert m["a"].components == (bd.Component("q_proj", 0, 64), bd.Component("kv_proj", 64, 120))
+    assert m["b"].components == ()
+    for comps, message in (([{"name": "x", "row_start": 0, "row_end": 129}], "outside"),
+                           ([{"name": "x", "row_start": 5, "row_end": 5}], "outside"),
+                           ([{"name": "q_proj"}], "duplicate"),
+                           ([{"row_start": 0}], "invalid component"),
+                           ({"name": "x"}, "invalid components")):
+        b2 = dict(b, components=comps)
+        _write(tmp_path, [a, b2], files)
+        with pytest.raises(ValueError, match=message):
+            bd.read_manifest(tmp_path)
+
+
+@pytest.mark.gpu
+def test_backend_load_bundles_components(tmp_path):
+    """CudaBackend.load_bundles: components are row slices of the uploaded
+    matrix, and an unpadded activation of original K equals the zero-padded one."""
+    from oracle import bfp16 as ob16
+    from oracle import q4nx as oq
+    from raon_npu_b200.backend import CudaBackend
+    rng = np.random.default_rng(5)
+    wq = (rng.standard_normal((256, 512)) * 0.02).astype(np.float32)
+    wq[:, 448:] = 0.0
+    q = oq.pack_gemv(*oq.quantize(wq))
+    wb = (rng.standard_normal((128, 256)) * 0.02).astype(np.float32)
+    bb = ob16.pack_gemv(wb)
+    _write(tmp_path, [_entry("L0/qkv", "q4nx_gemv", "q.bin", (256, 512), original_shape=[200, 448],
+                             components=[{"name": "q_proj", "row_start": 0, "row_end": 136},
+                                         {"name": "kv_proj", "row_start": 136, "row_end": 200}]),
+                      _entry("lm_head", "bfp16_gemv", "b.bin", (128, 256))],
+           {"q.bin": q, "b.bin": bb})
+    be = CudaBackend(0)
+    try:
+        be.load_bundles(tmp_path)
+        direct = be.ctx.upload_q4nx(np.frombuffer(q, np.uint8), 256, 512)
+        x = (rng.standard_normal((3, 448)) * 0.5).astype(np.float32)
+        x16 = (x.view(np.uint32) >> 16).astype(np.uint16)
+        xp = np.zeros((3, 512), np.uint16)
+        xp[:, :448] = x16
+        full = direct.gemv_host(xp)
+        assert np.array_equal(be.linear("q_proj", x16), full[:, :136])
+        assert np.array_equal(be.linear("kv_proj", x16), full[:, 136:200])
+        with pytest.raises(KeyError):
+            be.linear("L0/qkv", x16)
+        xl = np.ascontiguousarray(xp[:, :256])
+        yl = be.linear("lm_head", xl)
+        e, mnt = ob16.parse_gemv(bb, 256, 128)
+        ref = np.stack([ob16.gemv(e, mnt, xl[t]) for t in range(3)])
+        diff = np.abs(yl.astype(np.int32) - ref.astype(np.int32))
+        assert diff.max() <= 1 and (diff > 0).mean() <= 0.05
+        direct.free()
+    finally:
+        be.close()
+
+
 @pytest.mark.gpu
 def test_bundle_upload_matches_direct_upload(tmp_path):
     import torch
