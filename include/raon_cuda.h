@@ -42,6 +42,14 @@ extern "C" {
 #define RC_UPLOAD_GATE_UP 2u    /* rows are [gate; up] halves (kernels/moe/pack.py:136-172):
                                    store them interleaved so the GEMV epilogue can apply
                                    the GLU activation in registers                        */
+#define RC_UPLOAD_DOWN_BFP16 4u /* rc_moe_set_expert: ``down`` is a bfp16ebs8 matrix in the
+                                   reference's pack_bfp16_gemv bytes (its moe_b2 expert
+                                   bundles, npu/backend.py:640-652), [hidden][inter_pad]
+                                   at 9 bits a weight; every expert of a layer has the
+                                   same down format.  Such a layer runs rc_moe_experts,
+                                   rc_moe_experts_grouped and rc_moe_decode(_local)
+                                   through the separate launches (T <= 16); the prefill
+                                   and rc_moe_ep_decode entry points refuse it.            */
 
 typedef struct rc_ctx rc_ctx;
 typedef struct rc_weight rc_weight;
@@ -141,7 +149,8 @@ typedef struct rc_moe rc_moe;
 int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_shared, rc_moe **out);
 int rc_moe_destroy(rc_moe *m);
 
-/* Upload expert ``expert`` (0..n_experts-1, or n_experts for the shared one). */
+/* Upload expert ``expert`` (0..n_experts-1, or n_experts for the shared one):
+ * flags RC_UPLOAD_SRC_DEVICE and RC_UPLOAD_DOWN_BFP16. */
 int rc_moe_set_expert(rc_moe *m, int expert, const uint8_t *gate_up, size_t gate_up_bytes,
                       const uint8_t *down, size_t down_bytes, unsigned flags);
 

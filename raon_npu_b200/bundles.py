@@ -258,14 +258,16 @@ class BundleLoader:
         return self.ctx.upload_bfp16(data, b.rows, b.cols)
 
     def load_moe_experts(self, layer, gate_up: str, down: str, experts=None) -> None:
-        """Feed a ``MoeLayer`` its experts from two q4nx expert bundles (gate/up
-        [2I, H] and K-padded down [H, I_pad], the MoE's packing; ``experts``
-        defaults to all of them, the shared one being id E if present)."""
+        """Feed a ``MoeLayer`` its experts from two expert bundles: q4nx gate/up
+        [2I, H] and K-padded down [H, I_pad] in q4nx or bfp16ebs8 (the
+        reference's ``moe_b1`` / ``moe_b2``); ``experts`` defaults to all of
+        them, the shared one being id E if present."""
         gu, dn = self[gate_up], self[down]
-        for b in (gu, dn):
-            if b.fmt != "q4nx_gemv_bundle":
-                raise ValueError(f"{b.name}: the MoE layer takes q4nx expert bundles, not {b.fmt}")
+        if gu.fmt != "q4nx_gemv_bundle":
+            raise ValueError(f"{gu.name}: the MoE layer takes q4nx gate/up bundles, not {gu.fmt}")
+        if dn.fmt not in MOE_FORMATS:
+            raise ValueError(f"{dn.name}: not an expert bundle ({dn.fmt})")
         if gu.expert_count != dn.expert_count:
             raise ValueError(f"expert counts differ: {gu.name} {gu.expert_count}, {dn.name} {dn.expert_count}")
         for e in (range(gu.expert_count) if experts is None else experts):
-            layer.set_expert(e, read_matrix(self.dir, gu, e), read_matrix(self.dir, dn, e))
+            layer.set_expert(e, read_matrix(self.dir, gu, e), read_matrix(self.dir, dn, e), down_format=dn.weight_format)

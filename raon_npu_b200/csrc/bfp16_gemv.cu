@@ -64,6 +64,56 @@ __device__ __forceinline__ float bf_byte_bits(uint32_t biased, int b) {
   return __uint_as_float(__byte_perm(biased, 0x4B000000u, 0x7440u | (uint32_t)b));
 }
 
+// One unit (16 rows x 256 columns) into the accumulators of a lane: rows
+// 4j..4j+3, groups go*4..go*4+3 of the unit, columns col0 + 8g.. of the
+// activation rows tk with bit tk set in tmask (tk < TB).
+template <int TB>
+__device__ __forceinline__ void bf_unit_mac(const uint8_t *U, int j, int go, const uint16_t *x, int ldx, int col0,
+                                            uint32_t tmask, float (&acc)[4][TB]) {
+#pragma unroll 1
+  for (int i = 0; i < 4; ++i) {
+    const int g = go * 4 + i;                       // group of this unit (8 columns)
+    const uint8_t *G = U + g * kBfGroupBytes;
+    const uint32_t ew = *reinterpret_cast<const uint32_t *>(G + 4 * j);   // exponents of rows 4j..4j+3
+    // mantissas of rows 4j..4j+3 as f32 pairs of adjacent columns (2cp, 2cp+1)
+    float2 mf[4][4];
+#pragma unroll
+    for (int cp = 0; cp < 4; ++cp) {
+      const uint32_t m0 = *reinterpret_cast<const uint32_t *>(G + 16 + 32 * cp + 4 * j) ^ 0x80808080u;
+      const uint32_t m1 = *reinterpret_cast<const uint32_t *>(G + 32 + 32 * cp + 4 * j) ^ 0x80808080u;
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        mf[r][cp] = __fadd2_rn(make_float2(bf_byte_bits(m0, r), bf_byte_bits(m1, r)),
+                               make_float2(-8388736.0f, -8388736.0f));   // 2**23 + 128
+    }
+    float sc[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      int e = (int)((ew >> (8 * r)) & 0xFFu);
+      e = e < 7 ? 7 : e;                            // the reference kernel's clamp
+      sc[r] = __uint_as_float((uint32_t)(e - 6) << 23);   // 2**(e - 133)
+    }
+    const int col = col0 + g * 8;
+#pragma unroll
+    for (int tk = 0; tk < TB; ++tk) {
+      if ((tmask >> tk) & 1u) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x + (size_t)tk * ldx + col));
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+        float2 xf[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) xf[q] = make_float2(bf16_lo_f32(xw[q]), bf16_hi_f32(xw[q]));
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float2 s2 = __fmul2_rn(mf[r][0], xf[0]);
+#pragma unroll
+          for (int cp = 1; cp < 4; ++cp) s2 = __ffma2_rn(mf[r][cp], xf[cp], s2);
+          acc[r][tk] = fmaf(sc[r], s2.x + s2.y, acc[r][tk]);
+        }
+      }
+    }
+  }
+}
+
 template <int TB, bool F32OUT>
 __global__ void __launch_bounds__(kBfThreads, 1) bfp16_gemv_kernel(BfParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -117,49 +167,7 @@ __global__ void __launch_bounds__(kBfThreads, 1) bfp16_gemv_kernel(BfParams p) {
         break;
       }
       ++consumed;
-      const uint8_t *U = ring + slot * kBfUnitBytes;
-#pragma unroll 1
-      for (int i = 0; i < 4; ++i) {
-        const int g = go * 4 + i;                   // group of this unit (8 columns)
-        const uint8_t *G = U + g * kBfGroupBytes;
-        const uint32_t ew = *reinterpret_cast<const uint32_t *>(G + 4 * j);   // exponents of rows 4j..4j+3
-        // mantissas of rows 4j..4j+3 as f32 pairs of adjacent columns (2cp, 2cp+1)
-        float2 mf[4][4];
-#pragma unroll
-        for (int cp = 0; cp < 4; ++cp) {
-          const uint32_t m0 = *reinterpret_cast<const uint32_t *>(G + 16 + 32 * cp + 4 * j) ^ 0x80808080u;
-          const uint32_t m1 = *reinterpret_cast<const uint32_t *>(G + 32 + 32 * cp + 4 * j) ^ 0x80808080u;
-#pragma unroll
-          for (int r = 0; r < 4; ++r)
-            mf[r][cp] = __fadd2_rn(make_float2(bf_byte_bits(m0, r), bf_byte_bits(m1, r)),
-                                   make_float2(-8388736.0f, -8388736.0f));   // 2**23 + 128
-        }
-        float sc[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          int e = (int)((ew >> (8 * r)) & 0xFFu);
-          e = e < 7 ? 7 : e;                        // the reference kernel's clamp
-          sc[r] = __uint_as_float((uint32_t)(e - 6) << 23);   // 2**(e - 133)
-        }
-        const int col = kb * 256 + g * 8;
-#pragma unroll
-        for (int tk = 0; tk < TB; ++tk) {
-          if (tk < p.tokens) {
-            const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(p.x + (size_t)tk * p.ldx + col));
-            const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-            float2 xf[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) xf[q] = make_float2(bf16_lo_f32(xw[q]), bf16_hi_f32(xw[q]));
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-              float2 s2 = __fmul2_rn(mf[r][0], xf[0]);
-#pragma unroll
-              for (int cp = 1; cp < 4; ++cp) s2 = __ffma2_rn(mf[r][cp], xf[cp], s2);
-              acc[r][tk] = fmaf(sc[r], s2.x + s2.y, acc[r][tk]);
-            }
-          }
-        }
-      }
+      bf_unit_mac<TB>(ring + slot * kBfUnitBytes, j, go, p.x, p.ldx, kb * 256, (1u << p.tokens) - 1u, acc);
       __syncwarp();
       if (lane == 0 && iss_item < items) issue(slot);
       if (++slot == kBfStages) slot = 0, parity ^= 1u;
@@ -294,6 +302,134 @@ int bfp16_gemv(rc_ctx *ctx, const rc_weight *w, const uint16_t *x, int ldx, int 
       set_error("bfp16 gemv launch: %s", cudaGetErrorString(e));
       return RC_ERR_CUDA;
     }
+  }
+  return RC_OK;
+}
+
+// Down projection of an MoE layer whose experts' down matrices are
+// bfp16ebs8 (the reference's moe_b2 bundles, npu/backend.py:640-652): the
+// groups of the slot table (expert, token mask, slot row per token) times
+// their activation rows.  Items are (group, 16-row tile); a warp streams an
+// item's k-blocks through its ring like the dense kernel and writes the
+// group's tokens' rows of the tile as bf16 (zeros for an expert not loaded
+// here, as the q4nx down kernel does).  Each output is one warp's f32 sum in
+// k-block order, so a slot row does not depend on the grouping or the grid.
+template <int TB>
+__global__ void __launch_bounds__(kBfThreads, 1) bfp16_moe_down_kernel(BfMoeDown p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = lane & 3, go = lane >> 2;
+  uint8_t *ring = smem + warp * kBfStages * kBfUnitBytes;
+  const uint32_t ring_s = smem_addr(ring);
+  const uint32_t bar0 = smem_addr(smem + (size_t)kBfWarps * kBfStages * kBfUnitBytes) + warp * kBfStages * 8;
+  const int W = gridDim.x * kBfWarps, w0 = blockIdx.x * kBfWarps + warp;
+  const int tiles = p.hidden / kBfRows, KB = p.inter_pad / 256;
+  const int items = *p.n_groups * tiles;
+  auto weights = [&](int item) { return p.w[p.group_expert[item / tiles]]; };
+  int iss_item = w0, iss_kb = 0, issued = 0;
+  auto issue = [&](int sl) {
+    const uint8_t *w = weights(iss_item);
+    if (w) {
+      mbar_arrive_expect_tx(bar0 + 8 * sl, kBfUnitBytes);
+      bulk_copy_g2s_plain(ring_s + sl * kBfUnitBytes, bf_unit(w, iss_item % tiles, iss_kb, KB), kBfUnitBytes,
+                          bar0 + 8 * sl);
+    } else {
+      mbar_arrive_expect_tx(bar0 + 8 * sl, 0);      // nothing to fetch: the phase completes at once
+    }
+    ++issued;
+    if (++iss_kb == KB) iss_kb = 0, iss_item += W;
+  };
+  if (lane == 0) {
+    for (int sl = 0; sl < kBfStages; ++sl) mbar_init(bar0 + 8 * sl, 1);
+    mbar_fence_init();
+    for (int sl = 0; sl < kBfStages && iss_item < items; ++sl) issue(sl);
+  }
+  __syncwarp();
+  int slot = 0, consumed = 0;
+  uint32_t parity = 0;
+  bool failed = false;
+  for (int item = w0; item < items && !failed; item += W) {
+    const int grp = item / tiles, t = item - grp * tiles;
+    const bool live = weights(item) != nullptr;
+    const uint32_t mask = p.group_mask[grp] & (p.T >= 32 ? ~0u : (1u << p.T) - 1u);
+    const uint16_t *xg = p.x + (size_t)grp * p.rows_per_group * p.ldx;
+    float acc[4][TB];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int tk = 0; tk < TB; ++tk) acc[r][tk] = 0.f;
+    for (int kb = 0; kb < KB; ++kb) {
+      if (!mbar_wait_bounded_warp(bar0 + 8 * slot, parity)) {
+        if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+        failed = true;
+        break;
+      }
+      ++consumed;
+      if (live) bf_unit_mac<TB>(ring + slot * kBfUnitBytes, j, go, xg, p.ldx, kb * 256, mask, acc);
+      __syncwarp();
+      if (lane == 0 && iss_item < items) issue(slot);
+      if (++slot == kBfStages) slot = 0, parity ^= 1u;
+    }
+    if (failed) break;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int tk = 0; tk < TB; ++tk) {
+        float v = acc[r][tk];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        acc[r][tk] = v;
+      }
+    if (go == 0) {
+#pragma unroll
+      for (int tk = 0; tk < TB; ++tk) {
+        if (!((mask >> tk) & 1u)) continue;
+        uint16_t *y = p.y + (size_t)p.group_dst[grp * p.dst_stride + tk] * p.ldy + t * kBfRows + 4 * j;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) y[r] = live ? f32_to_bf16_rne(acc[r][tk]) : (uint16_t)0;
+      }
+    }
+  }
+  if (failed && lane == 0) {
+    for (int q = consumed; q < issued; ++q)
+      mbar_wait_bounded(bar0 + 8 * (q % kBfStages), (uint32_t)(q / kBfStages) & 1u);
+  }
+}
+
+template <int TB>
+static cudaError_t bf_moe_launch(const rc_ctx *ctx, const BfMoeDown &d, int grid, cudaStream_t s) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(bfp16_moe_down_kernel<TB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfSmem);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) configured[dev] = true;
+  }
+  bfp16_moe_down_kernel<TB><<<grid, kBfThreads, kBfSmem, s>>>(d);
+  return cudaGetLastError();
+}
+
+int bfp16_moe_down(rc_ctx *ctx, const BfMoeDown &d, cudaStream_t s) {
+  RC_CHECK_ARG(d.T >= 1 && d.T <= 16 && d.T <= d.rows_per_group && d.T <= d.dst_stride,
+               "bfp16 MoE down: %d tokens outside 1..16", d.T);
+  RC_CHECK_ARG(d.hidden % 128 == 0 && d.inter_pad % 256 == 0 && d.ldx % 8 == 0,
+               "bfp16 MoE down: hidden %d / inter_pad %d not block-aligned", d.hidden, d.inter_pad);
+  const long long items = (long long)d.max_groups * (d.hidden / kBfRows);
+  if (items <= 0) return RC_OK;
+  const long long want = (items + kBfWarps - 1) / kBfWarps;
+  const int grid = (int)(want < ctx->sm_count ? want : ctx->sm_count);
+  cudaError_t e;
+  if (d.T <= 1) e = bf_moe_launch<1>(ctx, d, grid, s);
+  else if (d.T <= 2) e = bf_moe_launch<2>(ctx, d, grid, s);
+  else if (d.T <= 4) e = bf_moe_launch<4>(ctx, d, grid, s);
+  else if (d.T <= 8) e = bf_moe_launch<8>(ctx, d, grid, s);
+  else e = bf_moe_launch<16>(ctx, d, grid, s);
+  if (e != cudaSuccess) {
+    set_error("bfp16 MoE down launch: %s", cudaGetErrorString(e));
+    return RC_ERR_CUDA;
   }
   return RC_OK;
 }

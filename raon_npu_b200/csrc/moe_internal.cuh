@@ -104,6 +104,7 @@ struct rc_moe {
   unsigned fz_epoch;          // ctx->timeout_epoch when fz_bar was last known consistent
   rc::MoeEp *ep;              // peer-memory expert parallelism (null until rc_moe_ep_init)
   int prefill_kernel;         // RC_PREFILL_GEMV (register fragments) or RC_PREFILL_TCGEN05
+  int down_fmt;               // kFormatQ4nx or kFormatBfp16 (RC_UPLOAD_DOWN_BFP16), one for every expert
 };
 
 namespace rc {

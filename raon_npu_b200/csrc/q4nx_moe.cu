@@ -698,6 +698,26 @@ static int moe_run_experts(rc_moe *m, const uint16_t *x, int T, int k, const Moe
       return RC_ERR_CUDA;
     }
   }
+  if (m->down_fmt == kFormatBfp16) {
+    BfMoeDown b{};
+    b.w = m->dn_tiles;
+    b.n_groups = m->s.n_groups;
+    b.group_expert = m->s.group_expert;
+    b.group_mask = m->s.group_mask;
+    b.group_dst = m->s.group_dst;
+    b.dst_stride = kMoeMaxTokens;
+    b.x = m->act;
+    b.ldx = m->inter_pad;
+    b.rows_per_group = 8 * ntb;
+    b.T = T;
+    b.hidden = m->hidden;
+    b.inter_pad = m->inter_pad;
+    b.y = down_out;
+    b.ldy = m->hidden;
+    b.max_groups = mg;
+    b.err = m->ctx->err;
+    return bfp16_moe_down(m->ctx, b, s);
+  }
   MoeGemvParams d = g;
   d.expert_tiles = m->dn_tiles;
   d.skip_last_group = 0;
@@ -831,6 +851,7 @@ int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_sha
   m->n_experts = n_experts;
   m->has_shared = has_shared ? 1 : 0;
   m->fused = 1;
+  m->down_fmt = kFormatQ4nx;
   const int ne = n_experts + 1;
   m->gate_up = new rc_weight *[ne]();
   m->down = new rc_weight *[ne]();
@@ -917,11 +938,20 @@ int rc_moe_set_expert(rc_moe *m, int expert, const uint8_t *gate_up, size_t gate
   RC_CHECK_ARG(m && gate_up && down, "rc_moe_set_expert: NULL argument");
   RC_CHECK_ARG(expert >= 0 && expert <= m->n_experts, "expert id %d out of range 0..%d", expert, m->n_experts);
   RC_CHECK_ARG(expert < m->n_experts || m->has_shared, "this MoE layer has no shared expert");
-  RC_CHECK_ARG((flags & ~(unsigned)RC_UPLOAD_SRC_DEVICE) == 0, "rc_moe_set_expert: unknown flags 0x%x", flags);
+  RC_CHECK_ARG((flags & ~(unsigned)(RC_UPLOAD_SRC_DEVICE | RC_UPLOAD_DOWN_BFP16)) == 0,
+               "rc_moe_set_expert: unknown flags 0x%x", flags);
+  const int fmt = (flags & RC_UPLOAD_DOWN_BFP16) ? kFormatBfp16 : kFormatQ4nx;
+  for (int e = 0; e <= m->n_experts; ++e)
+    RC_CHECK_ARG(e == expert || !m->down[e] || m->down[e]->format == fmt,
+                 "rc_moe_set_expert: expert %d's down matrix is %s but expert %d's is %s (one format per layer)",
+                 expert, fmt == kFormatBfp16 ? "bfp16ebs8" : "q4nx", e,
+                 fmt == kFormatBfp16 ? "q4nx" : "bfp16ebs8");
+  const unsigned src = flags & RC_UPLOAD_SRC_DEVICE;
   rc_weight *gu = nullptr, *dn = nullptr;
-  int rc = rc_upload_q4nx(m->ctx, gate_up, gate_up_bytes, 2 * m->inter, m->hidden, flags | RC_UPLOAD_GATE_UP, &gu);
+  int rc = rc_upload_q4nx(m->ctx, gate_up, gate_up_bytes, 2 * m->inter, m->hidden, src | RC_UPLOAD_GATE_UP, &gu);
   if (rc) return rc;
-  rc = rc_upload_q4nx(m->ctx, down, down_bytes, m->hidden, m->inter_pad, flags, &dn);
+  rc = fmt == kFormatBfp16 ? rc_upload_bfp16(m->ctx, down, down_bytes, m->hidden, m->inter_pad, src, &dn)
+                           : rc_upload_q4nx(m->ctx, down, down_bytes, m->hidden, m->inter_pad, src, &dn);
   if (rc) {
     rc_weight_free(gu);
     return rc;
@@ -930,6 +960,7 @@ int rc_moe_set_expert(rc_moe *m, int expert, const uint8_t *gate_up, size_t gate
   if (m->down[expert]) rc_weight_free(m->down[expert]);
   m->gate_up[expert] = gu;
   m->down[expert] = dn;
+  m->down_fmt = fmt;
   RC_CUDA_TRY(cudaMemcpy(m->gu_tiles + expert, &gu->tiles, sizeof(void *), cudaMemcpyHostToDevice));
   RC_CUDA_TRY(cudaMemcpy(m->dn_tiles + expert, &dn->tiles, sizeof(void *), cudaMemcpyHostToDevice));
   return RC_OK;
@@ -1219,6 +1250,8 @@ int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int re
   own.shared_mask = m->has_shared ? token_mask(ep->rank * ep->M, ep->M) : 0u;
   int rc = check_loaded(m, own);
   if (rc) return rc;
+  RC_CHECK_ARG(m->down_fmt == kFormatQ4nx,
+               "rc_moe_ep_decode: the persistent decode kernel takes q4nx down matrices, not bfp16ebs8");
   RC_CHECK_ARG(moe_fused_shape_ok(m, T, k, own),
                "rc_moe_ep_decode: T=%d k=%d does not fit the persistent decode kernel", T, k);
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));

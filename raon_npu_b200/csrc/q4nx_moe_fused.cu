@@ -777,6 +777,7 @@ bool moe_fused_fits(const rc_moe *m, int T, int k, const MoeOwned &own) {
 // Whether the fused kernel can run this shape: the shared-memory layout fits
 // and a CTA's down range touches at most kMoeMaxGroupsPerCta groups.
 bool moe_fused_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own) {
+  if (m->down_fmt != kFormatQ4nx) return false;   // q4nx unit arithmetic only
   FzLayout L;
   if (!fz_layout(m, T, k, own, &L)) return false;
   const int max_groups = fz_max_groups(T, k, own);

@@ -1201,6 +1201,8 @@ static int pf_route(rc_moe *m, const uint16_t *x, int T, int k, int router, int 
 
 static int pf_check(rc_moe *m, const uint16_t *x, int T, int k, int act, int lo, int hi) {
   RC_CHECK_ARG(T >= 1 && T <= kPfMaxTokens, "prefill: T must be 1..%d", kPfMaxTokens);
+  RC_CHECK_ARG(m->down_fmt == kFormatQ4nx, "prefill: the grouped prefill kernels take q4nx down matrices, "
+               "not bfp16ebs8 (decode them 16 tokens at a time with rc_moe_decode)");
   RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK && k <= m->n_experts, "prefill: k must be 1..%d and <= n_experts", kMoeMaxK);
   RC_CHECK_ARG(act == RC_ACT_SWIGLU || act == RC_ACT_SITU, "unknown activation %d", act);
   RC_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0, "token rows must be 16-byte aligned");

@@ -121,6 +121,24 @@ int ensure_gemv_scratch(rc_ctx *ctx, int k, int n_tiles);
 int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb);
 int ensure_sample_scratch(rc_ctx *ctx, size_t bytes);
 int check_error_word(rc_ctx *ctx);
+// Grouped down projection of an MoE layer with bfp16ebs8 down matrices
+// (bfp16_gemv.cu); the group tables are those of the q4nx MoE kernels.
+struct BfMoeDown {
+  const uint8_t *const *w;      // [E+1] device table of expert down matrices [hidden][inter_pad] (null: not here)
+  const int *n_groups;          // device
+  const int32_t *group_expert;  // [group]
+  const uint32_t *group_mask;   // [group] tokens of the group
+  const int32_t *group_dst;     // [group][dst_stride] slot row of (group, token)
+  int dst_stride;
+  const uint16_t *x;            // activation of (group g, token t): row g * rows_per_group + t, stride ldx
+  int ldx, rows_per_group, T;
+  int hidden, inter_pad;
+  uint16_t *y;                  // slot rows, stride ldy
+  int ldy;
+  int max_groups;               // upper bound of *n_groups (grid size only)
+  int *err;
+};
+int bfp16_moe_down(rc_ctx *ctx, const BfMoeDown &d, cudaStream_t s);
 int bfp16_gemv(rc_ctx *ctx, const rc_weight *w, const uint16_t *x, int ldx, int T, void *y, int y_dtype, int ldy,
                int row0, int nrows, const float *bias, cudaStream_t s);   // bfp16_gemv.cu
 // Words of one xfrag slot / floats of one aux slot for K columns (2 token blocks).

@@ -306,13 +306,19 @@ class MoeLayer:
         except Exception:
             pass
 
-    def set_expert(self, expert: int, gate_up_packed, down_packed) -> None:
+    def set_expert(self, expert: int, gate_up_packed, down_packed, down_format: str = "q4nx") -> None:
+        """``down_format="bfp16"``: ``down_packed`` is the bfp16ebs8 GEMV packing
+        of the K-padded down matrix (the reference's ``moe_b2`` bundles); every
+        expert of a layer must use the same down format."""
+        if down_format not in ("q4nx", "bfp16"):
+            raise ValueError(f"unknown down format {down_format!r}")
         gp, gn, gf, gk = _buf(gate_up_packed)
         dp, dn, df, dk = _buf(down_packed)
         if gf != df:
             raise ValueError("gate_up and down must both be host or both be device buffers")
+        flags = gf | (4 if down_format == "bfp16" else 0)          # RC_UPLOAD_DOWN_BFP16
         check(self.ctx.lib.rc_moe_set_expert(self.handle, int(expert), ctypes.c_void_p(gp), gn, ctypes.c_void_p(dp),
-                                             dn, gf), "rc_moe_set_expert")
+                                             dn, flags), "rc_moe_set_expert")
         del gk, dk
         self.loaded.add(int(expert))
 
