@@ -267,6 +267,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     weights.clear()
 
     moe = None if args.no_moe else run_moe(args, ctx, torch, dev, rank, world, local_rank, barrier)
+    moe_bf = None
+    if moe is not None and world == 1 and bfp16 is not None:
+        moe_bf = measure_moe_bfp16_down(args, ctx, torch, dev)
     prefill = None if args.no_moe else run_moe_prefill(args, ctx, torch, dev, rank, world, local_rank, barrier)
     dstep = None if args.no_decode_step else run_decode_step(args, ctx, torch, dev, rank, world, local_rank,
                                                              barrier)
@@ -295,6 +298,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "bfp16": bfp16,
             "cpu_baseline": cpu,
             "moe": moe,
+            "moe_bfp16_down": moe_bf,
             "moe_prefill": prefill,
             "decode_step": dstep,
         }
@@ -448,6 +452,82 @@ def build_moe_layers(ctx, torch, dev, n_layers: int):
         eps.append(ep)
     torch.cuda.synchronize()
     return eps
+
+
+def measure_moe_bfp16_down(args, ctx, torch, dev):
+    """The config-3 decode layer (T = 1) with the experts' down matrices in
+    bfp16ebs8, as the reference's production bundles store them (moe_b2):
+    router, q4nx gate/up with the GLU epilogue, the grouped bfp16 down kernel
+    and the combine as separate launches in one CUDA graph per layer.
+    Synthetic down blocks are made on the device (exponent bytes 118..124,
+    random int8 mantissas); layers rotate as in the q4nx measurement."""
+    from raon_npu_b200.device import MoeLayer
+    H, I, E, k = MOE["hidden"], MOE["inter"], MOE["experts"], MOE["k"]
+    ip = (I + 255) // 256 * 256
+    eb = 2 * I * H * 5 // 8 + H * ip * 9 // 8
+    touched = (k + 1) * eb
+    n_layers = min(24, max(2, -(-3 * 126_000_000 // touched)))
+    gen = torch.Generator(device=dev)
+    layers = []
+    for li in range(n_layers):
+        layer = MoeLayer(ctx, H, I, E, has_shared=True)
+        for e in range(E + 1):
+            gen.manual_seed(_moe_seed(li, e))
+            gu = torch.randn((2 * I, H), generator=gen, device=dev) * 0.02
+            pgu = torch.empty(2 * I * H * 5 // 8, dtype=torch.uint8, device=dev)
+            ctx.quantize_q4nx(gu, pgu, 2 * I, H)
+            blk = torch.randint(0, 256, (H * ip * 9 // 8 // 144, 144), generator=gen, device=dev, dtype=torch.uint8)
+            blk[:, :16] = torch.randint(118, 125, (blk.shape[0], 16), generator=gen, device=dev, dtype=torch.uint8)
+            layer.set_expert(e, pgu, blk.view(-1), down_format="bfp16")
+        gen.manual_seed(_moe_seed(li, 999))
+        wr = (torch.randn((E, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        layer.set_router(wr.view(torch.int16).cpu().numpy().view(np.uint16))
+        layers.append(layer)
+    gen.manual_seed(4343)
+    xs = [torch.randn((1, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16).contiguous()
+          for _ in range(n_layers)]
+    outs = [torch.empty((1, H), dtype=torch.int16, device=dev) for _ in range(n_layers)]
+    for _ in range(args.warmup):
+        for li in range(n_layers):
+            layers[li].decode(xs[li], k, outs[li])
+    torch.cuda.synchronize()
+    ctx.sync()
+    graphs = [capture_graph(torch, lambda li=li: layers[li].decode(xs[li], k, outs[li])) for li in range(n_layers)]
+    for s in range(args.warmup * n_layers):
+        graphs[s % n_layers].replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for s in range(args.steps):
+        graphs[s % n_layers].replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    del graphs
+    ctx.sync()
+    step_bytes = []
+    for li in range(n_layers):
+        ids = torch.empty((1, k), dtype=torch.int32, device=dev)
+        w = torch.empty((1, k), dtype=torch.float32, device=dev)
+        layers[li].route(xs[li], 1, k, ids, w)
+        torch.cuda.synchronize()
+        step_bytes.append((len(set(ids.cpu().numpy().ravel().tolist())) + 1) * eb + E * H * 2 + 4 * H)
+    b = sum(step_bytes[s % n_layers] for s in range(args.steps)) / args.steps
+    for layer in layers:
+        layer.close()
+    peak, peak_kind = peaks()
+    gbs = b / (ms * 1e-3) / 1e9
+    return {"metric": "MoE decode layer tokens/s", "value": round(1 / (ms * 1e-3), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms, 5), "steps": args.steps,
+            "config": {"workload": "config-3 MoE decode layer, T = 1, down matrices bfp16ebs8 (9-bit), "
+                                   "gate/up q4nx", "layers_rotated": n_layers,
+                       "path": "separate launches (router, gate/up GEMV + GLU, grouped bfp16 down, combine) "
+                               "in one CUDA graph per layer"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_source": peak_kind,
+                         "bytes_per_step": round(b), "expert_bytes": eb}}
 
 
 def moe_cpu_sample(n_tokens: int, budget_s: float):
