@@ -515,6 +515,20 @@ def measure_moe_bfp16_down(args, ctx, torch, dev):
         torch.cuda.synchronize()
         step_bytes.append((len(set(ids.cpu().numpy().ravel().tolist())) + 1) * eb + E * H * 2 + 4 * H)
     b = sum(step_bytes[s % n_layers] for s in range(args.steps)) / args.steps
+    # prefill of 512 tokens through the first two layers (register-fragment gate/up, bfp16 grouped down)
+    xp = torch.randn((PREFILL_TOKENS, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16)
+    op = torch.empty_like(xp)
+    for _ in range(args.warmup):
+        layers[0].prefill(xp, k, op)
+    pgraphs = [capture_graph(torch, lambda li=li: layers[li].prefill(xp, k, op)) for li in range(2)]
+    torch.cuda.synchronize()
+    e0.record(st)
+    for s in range(args.steps):
+        pgraphs[s % 2].replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    pms = e0.elapsed_time(e1) / args.steps
+    del pgraphs
     for layer in layers:
         layer.close()
     peak, peak_kind = peaks()
@@ -527,7 +541,11 @@ def measure_moe_bfp16_down(args, ctx, torch, dev):
                                "in one CUDA graph per layer"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_source": peak_kind,
-                         "bytes_per_step": round(b), "expert_bytes": eb}}
+                         "bytes_per_step": round(b), "expert_bytes": eb},
+            "prefill": {"tokens": PREFILL_TOKENS, "ms_per_step": round(pms, 4),
+                        "tokens_per_s": round(PREFILL_TOKENS / (pms * 1e-3), 1),
+                        "router": "softmax, unbiased", "path": "router, plan, register-fragment gate/up GEMV, "
+                        "bfp16 grouped down over 8-row expert blocks, combine (one CUDA graph)"}}
 
 
 def moe_cpu_sample(n_tokens: int, budget_s: float):
@@ -689,7 +707,7 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
                "sample": f"{n_tok} decode tokens through the oracle's numpy MoE layer (router, 8 routed + "
                          f"shared SwiGLU experts, ascending-ID combine; host/backend.py:466-510, "
                          f"host/raon.py:1224-1327 restated), f32 weights cached (16 weight sets, id mod 16)"}
-    transport = "none" if world == 1 else eps[0].transport
+    transport = eps[0].active_transport
     if world == 1 or transport == "p2p":
         per_step, kdesc = 1, "one persistent kernel: router, top-k, grouped gate/up and down GEMVs, combine" + (
             "; token rows and expert rows exchanged over NVLink peer stores inside it" if world > 1 else "")

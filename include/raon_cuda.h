@@ -48,8 +48,9 @@ extern "C" {
                                    at 9 bits a weight; every expert of a layer has the
                                    same down format.  Such a layer runs rc_moe_experts,
                                    rc_moe_experts_grouped and rc_moe_decode(_local)
-                                   through the separate launches (T <= 16); the prefill
-                                   and rc_moe_ep_decode entry points refuse it.            */
+                                   through the separate launches (T <= 16) and the
+                                   prefill entry points on the register-fragment
+                                   path; rc_moe_ep_decode refuses it.                     */
 
 typedef struct rc_ctx rc_ctx;
 typedef struct rc_weight rc_weight;

@@ -314,7 +314,7 @@ int bfp16_gemv(rc_ctx *ctx, const rc_weight *w, const uint16_t *x, int ldx, int 
 // group's tokens' rows of the tile as bf16 (zeros for an expert not loaded
 // here, as the q4nx down kernel does).  Each output is one warp's f32 sum in
 // k-block order, so a slot row does not depend on the grouping or the grid.
-template <int TB>
+template <int TB, bool BLOCKS>
 __global__ void __launch_bounds__(kBfThreads, 1) bfp16_moe_down_kernel(BfMoeDown p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -325,7 +325,10 @@ __global__ void __launch_bounds__(kBfThreads, 1) bfp16_moe_down_kernel(BfMoeDown
   const int W = gridDim.x * kBfWarps, w0 = blockIdx.x * kBfWarps + warp;
   const int tiles = p.hidden / kBfRows, KB = p.inter_pad / 256;
   const int items = *p.n_groups * tiles;
-  auto weights = [&](int item) { return p.w[p.group_expert[item / tiles]]; };
+  auto weights = [&](int item) -> const uint8_t * {
+    const int e = p.group_expert[item / tiles];
+    return e >= 0 ? p.w[e] : nullptr;
+  };
   int iss_item = w0, iss_kb = 0, issued = 0;
   auto issue = [&](int sl) {
     const uint8_t *w = weights(iss_item);
@@ -351,8 +354,16 @@ __global__ void __launch_bounds__(kBfThreads, 1) bfp16_moe_down_kernel(BfMoeDown
   for (int item = w0; item < items && !failed; item += W) {
     const int grp = item / tiles, t = item - grp * tiles;
     const bool live = weights(item) != nullptr;
-    const uint32_t mask = p.group_mask[grp] & (p.T >= 32 ? ~0u : (1u << p.T) - 1u);
-    const uint16_t *xg = p.x + (size_t)grp * p.rows_per_group * p.ldx;
+    uint32_t mask;
+    const uint16_t *xg;
+    if (BLOCKS) {
+      const int n = p.blk_n[grp];
+      mask = n >= TB ? (TB >= 32 ? ~0u : (1u << TB) - 1u) : (1u << n) - 1u;
+      xg = p.x + (size_t)p.blk_row0[grp] * p.ldx;
+    } else {
+      mask = p.group_mask[grp] & (p.T >= 32 ? ~0u : (1u << p.T) - 1u);
+      xg = p.x + (size_t)grp * p.rows_per_group * p.ldx;
+    }
     float acc[4][TB];
 #pragma unroll
     for (int r = 0; r < 4; ++r)
@@ -385,7 +396,8 @@ __global__ void __launch_bounds__(kBfThreads, 1) bfp16_moe_down_kernel(BfMoeDown
 #pragma unroll
       for (int tk = 0; tk < TB; ++tk) {
         if (!((mask >> tk) & 1u)) continue;
-        uint16_t *y = p.y + (size_t)p.group_dst[grp * p.dst_stride + tk] * p.ldy + t * kBfRows + 4 * j;
+        const size_t yrow = BLOCKS ? (size_t)p.blk_row0[grp] + tk : (size_t)p.group_dst[grp * p.dst_stride + tk];
+        uint16_t *y = p.y + yrow * p.ldy + t * kBfRows + 4 * j;
 #pragma unroll
         for (int r = 0; r < 4; ++r) y[r] = live ? f32_to_bf16_rne(acc[r][tk]) : (uint16_t)0;
       }
@@ -397,23 +409,25 @@ __global__ void __launch_bounds__(kBfThreads, 1) bfp16_moe_down_kernel(BfMoeDown
   }
 }
 
-template <int TB>
+template <int TB, bool BLOCKS = false>
 static cudaError_t bf_moe_launch(const rc_ctx *ctx, const BfMoeDown &d, int grid, cudaStream_t s) {
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(bfp16_moe_down_kernel<TB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfSmem);
+    e = cudaFuncSetAttribute(bfp16_moe_down_kernel<TB, BLOCKS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kBfSmem);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured[dev] = true;
   }
-  bfp16_moe_down_kernel<TB><<<grid, kBfThreads, kBfSmem, s>>>(d);
+  bfp16_moe_down_kernel<TB, BLOCKS><<<grid, kBfThreads, kBfSmem, s>>>(d);
   return cudaGetLastError();
 }
 
 int bfp16_moe_down(rc_ctx *ctx, const BfMoeDown &d, cudaStream_t s) {
-  RC_CHECK_ARG(d.T >= 1 && d.T <= 16 && d.T <= d.rows_per_group && d.T <= d.dst_stride,
+  const bool blocks = d.blk_row0 != nullptr;
+  RC_CHECK_ARG(blocks || (d.T >= 1 && d.T <= 16 && d.T <= d.rows_per_group && d.T <= d.dst_stride),
                "bfp16 MoE down: %d tokens outside 1..16", d.T);
   RC_CHECK_ARG(d.hidden % 128 == 0 && d.inter_pad % 256 == 0 && d.ldx % 8 == 0,
                "bfp16 MoE down: hidden %d / inter_pad %d not block-aligned", d.hidden, d.inter_pad);
@@ -422,7 +436,8 @@ int bfp16_moe_down(rc_ctx *ctx, const BfMoeDown &d, cudaStream_t s) {
   const long long want = (items + kBfWarps - 1) / kBfWarps;
   const int grid = (int)(want < ctx->sm_count ? want : ctx->sm_count);
   cudaError_t e;
-  if (d.T <= 1) e = bf_moe_launch<1>(ctx, d, grid, s);
+  if (blocks) e = bf_moe_launch<8, true>(ctx, d, grid, s);     // blocks of at most 8 rows
+  else if (d.T <= 1) e = bf_moe_launch<1>(ctx, d, grid, s);
   else if (d.T <= 2) e = bf_moe_launch<2>(ctx, d, grid, s);
   else if (d.T <= 4) e = bf_moe_launch<4>(ctx, d, grid, s);
   else if (d.T <= 8) e = bf_moe_launch<8>(ctx, d, grid, s);

@@ -1075,6 +1075,24 @@ static int pf_experts_gemv(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStr
     RC_CUDA_TRY(pf_launch_gemv<kPfEpiSitu>(m->ctx, g, smem, s));
   else
     RC_CUDA_TRY(pf_launch_gemv<kPfEpiSwiglu>(m->ctx, g, smem, s));
+  if (m->down_fmt == kFormatBfp16) {
+    BfMoeDown b{};
+    b.w = m->dn_tiles;
+    b.n_groups = g.n_blocks;
+    b.group_expert = ps->blk_expert;
+    b.blk_row0 = ps->blk_row0;
+    b.blk_n = ps->blk_n;
+    b.x = ps->act;
+    b.ldx = m->inter_pad;
+    b.T = 8;
+    b.hidden = m->hidden;
+    b.inter_pad = m->inter_pad;
+    b.y = ps->down;
+    b.ldy = m->hidden;
+    b.max_groups = ps->blk_cap;
+    b.err = m->ctx->err;
+    return bfp16_moe_down(m->ctx, b, s);
+  }
   PfGemvParams d = g;
   d.expert_tiles = m->dn_tiles;
   d.kb = m->inter_pad / kUnitK;
@@ -1129,7 +1147,8 @@ static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t
   pf_plan_kernel<<<1, 1024, plan_smem, s>>>(pp);
   RC_CUDA_TRY(cudaGetLastError());
 
-  if (m->prefill_kernel == RC_PREFILL_GEMV) return pf_experts_gemv(m, x, r, s);
+  // bfp16ebs8 down matrices: the register-fragment path's blocks feed the bfp16 grouped down kernel
+  if (m->prefill_kernel == RC_PREFILL_GEMV || m->down_fmt == kFormatBfp16) return pf_experts_gemv(m, x, r, s);
   PfGemmParams g{};
   g.expert_tiles = m->gu_tiles;
   g.kb = m->hidden / kUnitK;
@@ -1201,8 +1220,6 @@ static int pf_route(rc_moe *m, const uint16_t *x, int T, int k, int router, int 
 
 static int pf_check(rc_moe *m, const uint16_t *x, int T, int k, int act, int lo, int hi) {
   RC_CHECK_ARG(T >= 1 && T <= kPfMaxTokens, "prefill: T must be 1..%d", kPfMaxTokens);
-  RC_CHECK_ARG(m->down_fmt == kFormatQ4nx, "prefill: the grouped prefill kernels take q4nx down matrices, "
-               "not bfp16ebs8 (decode them 16 tokens at a time with rc_moe_decode)");
   RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK && k <= m->n_experts, "prefill: k must be 1..%d and <= n_experts", kMoeMaxK);
   RC_CHECK_ARG(act == RC_ACT_SWIGLU || act == RC_ACT_SITU, "unknown activation %d", act);
   RC_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0, "token rows must be 16-byte aligned");

@@ -122,14 +122,17 @@ int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb);
 int ensure_sample_scratch(rc_ctx *ctx, size_t bytes);
 int check_error_word(rc_ctx *ctx);
 // Grouped down projection of an MoE layer with bfp16ebs8 down matrices
-// (bfp16_gemv.cu); the group tables are those of the q4nx MoE kernels.
+// (bfp16_gemv.cu).  Decode: the group tables of the q4nx MoE kernels.
+// Prefill (blk_row0 != null): 8-row blocks of the permuted rows, block b =
+// expert group_expert[b], rows blk_row0[b] .. + blk_n[b] of x and of y.
 struct BfMoeDown {
   const uint8_t *const *w;      // [E+1] device table of expert down matrices [hidden][inter_pad] (null: not here)
-  const int *n_groups;          // device
+  const int *n_groups;          // device: groups (decode) or blocks (prefill)
   const int32_t *group_expert;  // [group]
   const uint32_t *group_mask;   // [group] tokens of the group
   const int32_t *group_dst;     // [group][dst_stride] slot row of (group, token)
   int dst_stride;
+  const int32_t *blk_row0, *blk_n;  // prefill blocks (null: decode groups)
   const uint16_t *x;            // activation of (group g, token t): row g * rows_per_group + t, stride ldx
   int ldx, rows_per_group, T;
   int hidden, inter_pad;

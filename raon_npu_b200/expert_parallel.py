@@ -115,6 +115,14 @@ class ExpertParallelMoe:
         self._ep_M = M
         return True
 
+    @property
+    def active_transport(self) -> str:
+        """The exchange decode calls use now: "p2p" once the peer buffers are
+        set up, "nccl" otherwise, "none" on one rank."""
+        if self.world == 1:
+            return "none"
+        return "p2p" if self._ep_M is not None else "nccl"
+
     def owns(self, expert: int) -> bool:
         """Experts this rank loads: its routed range and the shared expert (id E)."""
         lo, hi = self.experts

@@ -117,9 +117,41 @@ def test_decode_with_bfp16_down_routes_through_separate_launches(torch, ctx):
     layer.close()
 
 
+@pytest.mark.parametrize("kernel", ["gemv", "tcgen05"])
+def test_prefill_with_bfp16_down_equals_decode_chain(torch, ctx, kernel):
+    """rc_moe_prefill on a bfp16-down layer (either prefill kernel setting: the
+    bfp16 down runs on the register-fragment path's 8-row blocks) gives the
+    bytes of the decode chain on the routes it chose, 16 tokens at a time, and
+    the oracle's outputs within the MoE bar."""
+    hidden, inter, E, k, T = 1024, 768, 12, 4, 40
+    rng = np.random.default_rng(31)
+    packed, experts = _bfp16_experts(rng, hidden, inter, E + 1)
+    layer = _layer(ctx, packed, hidden, inter, E, has_shared=True)
+    layer.set_prefill_kernel(kernel)
+    wr = q.f32_to_bf16((rng.standard_normal((E, hidden)) * 0.02).astype(np.float32))
+    layer.set_router(wr)
+    x = q.f32_to_bf16(rng.standard_normal((T, hidden)).astype(np.float32))
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    out = torch.empty_like(xd)
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    layer.prefill(xd, k, out, ids, w, act="swiglu")
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint16)
+    idh, wh = ids.cpu().numpy(), w.cpu().numpy()
+    for t0 in range(0, T, 16):
+        again = layer.experts_host(x[t0:t0 + 16], idh[t0:t0 + 16], wh[t0:t0 + 16], act="swiglu", with_shared=True)
+        np.testing.assert_array_equal(got[t0:t0 + 16], again)
+    for t in (0, T // 2, T - 1):
+        routed = ob.moe_experts(experts, x[t], idh[t], wh[t], act="swiglu")
+        sh = ob.expert_forward(*experts[E], x[t], "swiglu")
+        mag = ob.moe_term_magnitude(experts, x[t], idh[t], wh[t], "swiglu", shared_down_u16=sh)
+        assert_bf16_outputs_close(got[t], ob.moe_token_with_shared(routed, sh), mag)
+    layer.close()
+
+
 def test_bfp16_down_refusals(torch, ctx):
-    """One down format per layer; the prefill and peer-memory decode kernels
-    take q4nx down matrices only and say so."""
+    """One down format per layer, and a down matrix of the wrong size, are refused."""
     from raon_npu_b200.device import MoeLayer
     hidden, inter, E = 256, 256, 4
     rng = np.random.default_rng(3)
@@ -131,9 +163,6 @@ def test_bfp16_down_refusals(torch, ctx):
     with pytest.raises(ValueError):
         layer.set_expert(1, packed[1][0], packed[1][1][:-9], down_format="bfp16")
     layer.set_expert(0, packed[0][0], packed[0][1], down_format="bfp16")     # replacing the same expert is fine
-    x = torch.zeros((4, hidden), dtype=torch.int16, device="cuda")
-    with pytest.raises(ValueError, match="q4nx down"):
-        layer.prefill(x, 2, torch.empty_like(x))
     layer.close()
     q_layer = MoeLayer(ctx, hidden, inter, E, has_shared=False)
     with pytest.raises(ValueError, match="unknown down format"):
