@@ -454,19 +454,13 @@ def build_moe_layers(ctx, torch, dev, n_layers: int):
     return eps
 
 
-def measure_moe_bfp16_down(args, ctx, torch, dev):
-    """The config-3 decode layer (T = 1) with the experts' down matrices in
-    bfp16ebs8, as the reference's production bundles store them (moe_b2):
-    router, q4nx gate/up with the GLU epilogue, the grouped bfp16 down kernel
-    and the combine as separate launches in one CUDA graph per layer.
-    Synthetic down blocks are made on the device (exponent bytes 118..124,
-    random int8 mantissas); layers rotate as in the q4nx measurement."""
+def build_bfp16_down_layers(ctx, torch, dev, n_layers: int):
+    """n_layers config-3 layers with q4nx gate/up (seeded as the q4nx layers)
+    and synthetic bfp16ebs8 down matrices made on the device (exponent bytes
+    118..124, random int8 mantissas)."""
     from raon_npu_b200.device import MoeLayer
-    H, I, E, k = MOE["hidden"], MOE["inter"], MOE["experts"], MOE["k"]
+    H, I, E = MOE["hidden"], MOE["inter"], MOE["experts"]
     ip = (I + 255) // 256 * 256
-    eb = 2 * I * H * 5 // 8 + H * ip * 9 // 8
-    touched = (k + 1) * eb
-    n_layers = min(24, max(2, -(-3 * 126_000_000 // touched)))
     gen = torch.Generator(device=dev)
     layers = []
     for li in range(n_layers):
@@ -483,6 +477,24 @@ def measure_moe_bfp16_down(args, ctx, torch, dev):
         wr = (torch.randn((E, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
         layer.set_router(wr.view(torch.int16).cpu().numpy().view(np.uint16))
         layers.append(layer)
+    torch.cuda.synchronize()
+    return layers
+
+
+def measure_moe_bfp16_down(args, ctx, torch, dev):
+    """The config-3 decode layer (T = 1) with the experts' down matrices in
+    bfp16ebs8, as the reference's production bundles store them (moe_b2):
+    router, q4nx gate/up with the GLU epilogue, the grouped bfp16 down kernel
+    and the combine as separate launches in one CUDA graph per layer.
+    Synthetic down blocks are made on the device (exponent bytes 118..124,
+    random int8 mantissas); layers rotate as in the q4nx measurement."""
+    H, I, E, k = MOE["hidden"], MOE["inter"], MOE["experts"], MOE["k"]
+    ip = (I + 255) // 256 * 256
+    eb = 2 * I * H * 5 // 8 + H * ip * 9 // 8
+    touched = (k + 1) * eb
+    n_layers = min(24, max(2, -(-3 * 126_000_000 // touched)))
+    gen = torch.Generator(device=dev)
+    layers = build_bfp16_down_layers(ctx, torch, dev, n_layers)
     gen.manual_seed(4343)
     xs = [torch.randn((1, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16).contiguous()
           for _ in range(n_layers)]
@@ -1278,6 +1290,34 @@ def run_profile_prefill(args):
     print(json.dumps({"profile": "prefill", "tokens": PREFILL_TOKENS, "steps": args.launches}))
 
 
+def run_profile_moe_bfp16(args):
+    """One config-3 layer with bfp16ebs8 down matrices on one GPU (no timing)
+    for an ncu capture: ``--launches`` decode calls of ``--tokens`` tokens,
+    then ``--launches`` 512-token prefills."""
+    import torch
+    from raon_npu_b200.device import Context
+    dev = torch.device("cuda", 0)
+    ctx = Context(0)
+    layer = build_bfp16_down_layers(ctx, torch, dev, 1)[0]
+    H, k = MOE["hidden"], MOE["k"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4343)
+    x = torch.randn((args.tokens, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16).contiguous()
+    out = torch.empty_like(x)
+    xp = torch.randn((PREFILL_TOKENS, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16)
+    op = torch.empty_like(xp)
+    for _ in range(args.launches):
+        layer.decode(x, k, out)
+    for _ in range(args.launches):
+        layer.prefill(xp, k, op)
+    torch.cuda.synchronize()
+    ctx.sync()
+    layer.close()
+    ctx.close()
+    print(json.dumps({"profile": "moe_bfp16", "tokens": args.tokens, "prefill_tokens": PREFILL_TOKENS,
+                      "steps": args.launches}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1290,7 +1330,8 @@ def main():
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode / prefill layers (configs[2], [3])")
     ap.add_argument("--no-decode-step", action="store_true", help="skip the 48-layer decode step (configs[4])")
     ap.add_argument("--profile", default=None, help="NxK: run a few plain GEMV launches for ncu and exit; "
-                    "'moe' / 'prefill': a few config-3 decode / config-4 prefill steps")
+                    "'moe' / 'prefill': a few config-3 decode / config-4 prefill steps; 'moe_bfp16': decode "
+                    "and prefill calls of a layer with bfp16ebs8 down matrices; 'bfp16:NxK': bfp16 GEMVs")
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--launches", type=int, default=4)
     args = ap.parse_args()
@@ -1299,6 +1340,9 @@ def main():
         return
     if args.profile == "prefill":
         run_profile_prefill(args)
+        return
+    if args.profile == "moe_bfp16":
+        run_profile_moe_bfp16(args)
         return
     if args.profile:
         run_profile_case(args)
