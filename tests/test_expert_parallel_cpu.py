@@ -133,7 +133,7 @@ def test_single_process_owns_every_expert():
     if dist.is_initialized():
         pytest.skip("needs a process without a default group")
     ep = ExpertParallelMoe(L(), 2)
-    assert ep.world == 1 and ep.experts == (0, 6)
+    assert ep.world == 1 and ep.experts == (0, 6) and ep.active_transport == "none"
     assert all(ep.owns(e) for e in range(7))
 
 
@@ -178,7 +178,7 @@ def _handshake_worker(rank, world, port, result_dir, fail_rank):
             ep.decode(x, out)
             ep.decode(x, out)          # set up once per token count
             res = {"ok": True, "opened": layer.opened, "decoded": layer.decoded, "geometry": layer.geometry,
-                   "same": bool(torch.equal(out, x))}
+                   "same": bool(torch.equal(out, x)), "active": ep.active_transport}
         except RuntimeError as e:
             res = {"ok": False, "error": str(e)}
         np.save(os.path.join(result_dir, f"h{rank}.npy"), np.array([res], dtype=object), allow_pickle=True)
@@ -205,3 +205,4 @@ def test_peer_memory_handshake(tmp_path, fail_rank):
         assert res["opened"] == {r: bytes([r, world, M]) for r in range(world)}
         assert res["decoded"] == [((M, HIDDEN), K), ((M, HIDDEN), K)]
         assert res["same"]
+        assert res["active"] == "p2p"
