@@ -322,7 +322,12 @@ __global__ void __launch_bounds__(kBfThreads, 1) bfp16_moe_down_kernel(BfMoeDown
   uint8_t *ring = smem + warp * kBfStages * kBfUnitBytes;
   const uint32_t ring_s = smem_addr(ring);
   const uint32_t bar0 = smem_addr(smem + (size_t)kBfWarps * kBfStages * kBfUnitBytes) + warp * kBfStages * 8;
-  const int W = gridDim.x * kBfWarps, w0 = blockIdx.x * kBfWarps + warp;
+  // Decode groups: items are dealt warp-major over the CTAs, so a grid larger
+  // than items / 16 spreads a small item count over more SMs.  Prefill blocks:
+  // CTA-major, so the tiles of one block (the same activation rows) share a
+  // CTA's L1.
+  const int W = gridDim.x * kBfWarps;
+  const int w0 = BLOCKS ? blockIdx.x * kBfWarps + warp : warp * gridDim.x + blockIdx.x;
   const int tiles = p.hidden / kBfRows, KB = p.inter_pad / 256;
   const int items = *p.n_groups * tiles;
   auto weights = [&](int item) -> const uint8_t * {
@@ -433,7 +438,7 @@ int bfp16_moe_down(rc_ctx *ctx, const BfMoeDown &d, cudaStream_t s) {
                "bfp16 MoE down: hidden %d / inter_pad %d not block-aligned", d.hidden, d.inter_pad);
   const long long items = (long long)d.max_groups * (d.hidden / kBfRows);
   if (items <= 0) return RC_OK;
-  const long long want = (items + kBfWarps - 1) / kBfWarps;
+  const long long want = (items + kBfWarps / 2 - 1) / (kBfWarps / 2);   // ~8 busy warps per SM for small counts
   const int grid = (int)(want < ctx->sm_count ? want : ctx->sm_count);
   cudaError_t e;
   if (blocks) e = bf_moe_launch<8, true>(ctx, d, grid, s);     // blocks of at most 8 rows
