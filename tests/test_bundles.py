@@ -140,6 +140,38 @@ def test_components(tmp_path):
             bd.read_manifest(tmp_path)
 
 
+def test_load_moe_experts_passes_the_down_format(tmp_path):
+    """q4nx gate/up (moe_b1) with a bfp16ebs8 down bundle (moe_b2): every
+    expert's slices reach the layer with ``down_format="bfp16"``; a bfp16
+    gate/up bundle is refused."""
+    E, H, I = 3, 256, 256
+    gu_b, dn_b = 2 * I * H * 5 // 8, H * I * 9 // 8
+    files = {"b1.bin": _rand(E * gu_b, 4), "b2.bin": _rand(E * dn_b, 5), "b2q.bin": _rand(E * dn_b, 6)}
+    _write(tmp_path, [_entry("L1/moe_b1", "q4nx_gemv_bundle", "b1.bin", (E, 2 * I, H), expert_count=E,
+                             expert_bytes=gu_b),
+                      _entry("L1/moe_b2", "bfp16_gemv_bundle", "b2.bin", (E, H, I), expert_count=E,
+                             expert_bytes=dn_b),
+                      _entry("L1/bad_b1", "bfp16_gemv_bundle", "b2q.bin", (E, H, I), expert_count=E,
+                             expert_bytes=dn_b)], files)
+
+    class Layer:
+        def __init__(self):
+            self.calls = []
+
+        def set_expert(self, e, gu, dn, down_format="q4nx"):
+            self.calls.append((e, gu, dn, down_format))
+
+    loader = bd.BundleLoader(None, tmp_path)
+    layer = Layer()
+    loader.load_moe_experts(layer, "L1/moe_b1", "L1/moe_b2")
+    assert [c[0] for c in layer.calls] == [0, 1, 2]
+    for e, gu, dn, fmt in layer.calls:
+        assert fmt == "bfp16"
+        assert gu == files["b1.bin"][e * gu_b:(e + 1) * gu_b] and dn == files["b2.bin"][e * dn_b:(e + 1) * dn_b]
+    with pytest.raises(ValueError, match="gate/up"):
+        loader.load_moe_experts(layer, "L1/bad_b1", "L1/moe_b2")
+
+
 @pytest.mark.gpu
 def test_backend_load_bundles_components(tmp_path):
     """CudaBackend.load_bundles: components are row slices of the uploaded
