@@ -117,6 +117,41 @@ def test_decode_with_bfp16_down_routes_through_separate_launches(torch, ctx):
     layer.close()
 
 
+def test_bfp16_down_expert_parallel_halves_reproduce_single_gpu_bytes(torch, ctx):
+    """The NCCL-transport halves (rc_moe_decode_local on two layers holding
+    half of the experts each, rank 0 also the shared one; slot rows merged,
+    then rc_moe_combine) give exactly the bytes of the whole layer's decode."""
+    hidden, inter, E, k = 1024, 512, 16, 4
+    rng = np.random.default_rng(41)
+    packed, _ = _bfp16_experts(rng, hidden, inter, E + 1)
+    wr = q.f32_to_bf16((rng.standard_normal((E, hidden)) * 0.02).astype(np.float32))
+    full = _layer(ctx, packed, hidden, inter, E, has_shared=True)
+    r0 = _layer(ctx, {e: packed[e] for e in list(range(E // 2)) + [E]}, hidden, inter, E, has_shared=True)
+    r1 = _layer(ctx, {e: packed[e] for e in range(E // 2, E)}, hidden, inter, E, has_shared=True)
+    for layer in (full, r0, r1):
+        layer.set_router(wr)
+    for _ in range(3):
+        x = q.f32_to_bf16(rng.standard_normal(hidden).astype(np.float32))
+        xd = torch.from_numpy(x.view(np.int16)).cuda()
+        ref = torch.empty(hidden, dtype=torch.int16, device="cuda")
+        full.decode(xd, k, ref, act="swiglu")
+        slots = [torch.empty((k + 1, hidden), dtype=torch.int16, device="cuda") for _ in range(2)]
+        sw = [torch.empty(k, dtype=torch.float32, device="cuda") for _ in range(2)]
+        r0.decode_local(xd, k, slots[0], sw[0], experts=(0, E // 2), shared_tokens=(0, 1), act="swiglu")
+        r1.decode_local(xd, k, slots[1], sw[1], experts=(E // 2, E), shared_tokens=(0, 0), act="swiglu")
+        torch.cuda.synchronize()
+        a, b = slots
+        assert bool(((a == 0) | (b == 0)).all())
+        assert torch.equal(sw[0], sw[1])
+        out = torch.empty(hidden, dtype=torch.int16, device="cuda")
+        r0.combine(torch.where(a != 0, a, b), sw[0], k, out, with_shared=True)
+        torch.cuda.synchronize()
+        ctx.sync()
+        assert torch.equal(out, ref)
+    for layer in (full, r0, r1):
+        layer.close()
+
+
 @pytest.mark.parametrize("kernel", ["gemv", "tcgen05"])
 def test_prefill_with_bfp16_down_equals_decode_chain(torch, ctx, kernel):
     """rc_moe_prefill on a bfp16-down layer (either prefill kernel setting: the
