@@ -291,6 +291,7 @@ class MoeLayer:
             bool(has_shared)
         self.inter_pad = (self.inter + 255) // 256 * 256
         self.loaded: set[int] = set()
+        self.down_format = "q4nx"          # of the experts loaded so far (one format per layer)
         ctx._adopt(self)
 
     def close(self) -> None:
@@ -320,6 +321,7 @@ class MoeLayer:
         check(self.ctx.lib.rc_moe_set_expert(self.handle, int(expert), ctypes.c_void_p(gp), gn, ctypes.c_void_p(dp),
                                              dn, flags), "rc_moe_set_expert")
         del gk, dk
+        self.down_format = down_format
         self.loaded.add(int(expert))
 
     def set_router(self, router_w_bits: np.ndarray, bias: np.ndarray | None = None) -> None:

@@ -83,8 +83,13 @@ class ExpertParallelMoe:
             return False
         if self._ep_M == M:
             return True
+        # the peer-memory kernel computes q4nx down matrices only (every rank's
+        # layer has the same format, so every rank decides alike)
+        q4nx_down = getattr(self.layer, "down_format", "q4nx") == "q4nx"
+        if self.transport == "p2p" and not q4nx_down:
+            raise RuntimeError("peer-memory expert parallelism needs q4nx down matrices; use transport='nccl'")
         if self.transport == "auto" and (dist.get_backend(self.group) != "nccl" or self.world * M > 16
-                                         or not hasattr(self.layer, "ep_init")):
+                                         or not hasattr(self.layer, "ep_init") or not q4nx_down):
             return False
         # the handshake's tensors live where the group's backend moves them
         on_gpu = dist.get_backend(self.group) == "nccl"

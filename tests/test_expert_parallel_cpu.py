@@ -206,3 +206,38 @@ def test_peer_memory_handshake(tmp_path, fail_rank):
         assert res["decoded"] == [((M, HIDDEN), K), ((M, HIDDEN), K)]
         assert res["same"]
         assert res["active"] == "p2p"
+
+
+def _bfp16_down_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+    from raon_npu_b200.expert_parallel import ExpertParallelMoe
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        layer = HandshakeLayer(rank)
+        layer.down_format = "bfp16"
+        x = torch.zeros((M, HIDDEN), dtype=torch.int16)
+        try:
+            ExpertParallelMoe(layer, K, transport="p2p").decode(x, torch.empty_like(x))
+            res = {"ok": True}
+        except RuntimeError as e:
+            res = {"ok": False, "error": str(e), "opened": layer.opened}
+        np.save(os.path.join(result_dir, f"b{rank}.npy"), np.array([res], dtype=object), allow_pickle=True)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_peer_memory_transport_refuses_bfp16_down_layers(tmp_path):
+    """A layer whose down matrices are bfp16ebs8 is refused by the peer-memory
+    transport on every rank before any exchange (the persistent kernel computes
+    q4nx down matrices only); transport='auto' takes NCCL for it."""
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_bfp16_down_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    for rank in range(world):
+        res = np.load(tmp_path / f"b{rank}.npy", allow_pickle=True)[0]
+        assert not res["ok"] and "q4nx down" in res["error"] and res["opened"] == {}, res
