@@ -353,7 +353,7 @@ def measure_bfp16(ctx, torch, dev, gen):
             w.free()
     ctx.sync()
     lm = [e for e in out if e["k_to_n"] == f"{LM_HEAD[1]}->{LM_HEAD[0]}"]
-    return {"workload": "bfp16ebs8 GEMV (9-bit weights, 8-column groups; SURVEY 8(f) row 1)",
+    return {"workload": "bfp16ebs8 GEMV (9-bit weights, 8-column groups sharing an exponent byte)",
             "bytes_per_weight": 9 / 8, "kernel": "bfp16_gemv_kernel (16-row half blocks by bulk copy, "
             "f32x2 CUDA-core products; split-K with ordered finalize for small N)",
             "lm_head": {e["t"]: {"gbs": e["gbs"], "frac": e["frac"]} for e in lm}, "per_shape": out}
