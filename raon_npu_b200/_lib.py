@@ -20,7 +20,9 @@ RC_OK, RC_ERR_INVALID, RC_ERR_NOT_FOUND, RC_ERR_CUDA, RC_ERR_TIMEOUT = 0, 1, 2, 
 RC_DTYPE_BF16, RC_DTYPE_F32 = 0, 1
 RC_ACT_SWIGLU, RC_ACT_SITU = 0, 1
 RC_ROUTER_SOFTMAX, RC_ROUTER_SIGMOID_BIAS = 0, 1
-RC_UPLOAD_SRC_DEVICE, RC_UPLOAD_GATE_UP = 1, 2
+RC_UPLOAD_SRC_DEVICE, RC_UPLOAD_GATE_UP, RC_UPLOAD_DOWN_BFP16 = 1, 2, 4
+RC_EP_MAX_RANKS, RC_EP_HANDLE_BYTES = 8, 128
+RC_PREFILL_GEMV, RC_PREFILL_TCGEN05 = 0, 1
 
 
 class RaonCudaError(RuntimeError):

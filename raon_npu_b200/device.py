@@ -317,7 +317,7 @@ class MoeLayer:
         dp, dn, df, dk = _buf(down_packed)
         if gf != df:
             raise ValueError("gate_up and down must both be host or both be device buffers")
-        flags = gf | (4 if down_format == "bfp16" else 0)          # RC_UPLOAD_DOWN_BFP16
+        flags = gf | (_lib.RC_UPLOAD_DOWN_BFP16 if down_format == "bfp16" else 0)
         check(self.ctx.lib.rc_moe_set_expert(self.handle, int(expert), ctypes.c_void_p(gp), gn, ctypes.c_void_p(dp),
                                              dn, flags), "rc_moe_set_expert")
         del gk, dk
@@ -343,7 +343,7 @@ class MoeLayer:
     def set_prefill_kernel(self, kernel: str) -> None:
         """"gemv" (default: register-fragment grouped GEMV over 8-token blocks) or
         "tcgen05" (tensor-core grouped GEMM over 64-token chunks)."""
-        codes = {"gemv": 0, "tcgen05": 1}
+        codes = {"gemv": _lib.RC_PREFILL_GEMV, "tcgen05": _lib.RC_PREFILL_TCGEN05}
         if kernel not in codes:
             raise ValueError(f"unknown prefill kernel {kernel!r}")
         check(self.ctx.lib.rc_moe_set_prefill_kernel(self.handle, codes[kernel]), "rc_moe_set_prefill_kernel")
@@ -422,7 +422,7 @@ class MoeLayer:
             ctypes.c_void_p(_stream_for(stream, x_dev, slot_out_dev))), "rc_moe_decode_local")
 
     # -- expert parallelism over peer memory ------------------------------
-    EP_HANDLE_BYTES = 128
+    EP_HANDLE_BYTES = _lib.RC_EP_HANDLE_BYTES
 
     def ep_init(self, rank: int, world: int, tokens_per_rank: int) -> bytes:
         """Allocates this rank's exchange buffer; returns the blob (IPC handle,

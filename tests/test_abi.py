@@ -20,6 +20,15 @@ def test_header_declares_what_the_binding_declares():
     assert _lib.header_functions() == sorted(_lib.SIGNATURES)
 
 
+def test_python_constants_match_the_header_defines():
+    """Every ``#define RC_*`` integer of the header has the same value in the binding."""
+    import re
+    defines = dict(re.findall(r"^#define (RC_[A-Z0-9_]+) (\d+)u?\b", _lib.HEADER.read_text(), re.M))
+    assert defines, "no integer defines found"
+    for name, value in defines.items():
+        assert getattr(_lib, name) == int(value), name
+
+
 def test_library_exports_every_declared_symbol(lib):
     for name in _lib.header_functions():
         assert hasattr(lib, name), name
