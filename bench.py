@@ -1,31 +1,33 @@
-"""Benchmark of the q4nx decode GEMV on B200.
+"""Benchmark of raon-npu's q4nx GEMV / MoE hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = one pass of the GEMV decode sweep: token rows T in {1,2,4,8,16} over
-the shapes (K -> N) 2048->4096, 4096->2048, 2048->512 and the lm-head
-2048->151936, q4nx weights from N(0, 0.02) f32, activations bf16 N(0, 1)
-(synthetic, seeded).  The dense GEMV does not shard: at N GPUs every rank runs
-an independent replica (one process per GPU, torchrun), and ``value`` is the
-algorithmic bytes of all ranks over the slowest rank's time ("weak" scaling).
+One step = one config-3 MoE decode layer (hidden 2048,
+128 routed experts + 1 shared, intermediate 768, softmax top-8, SwiGLU, q4nx
+weights N(0, 0.02), bf16 tokens N(0, 1); synthetic and seeded) over one token
+per rank, the routed experts sharded expert-parallel over the N ranks (one
+process per GPU, torchrun), the token and expert rows exchanged inside the
+decode kernel over NVLink peer memory.  ``value`` = tokens of all ranks per
+second over the slowest rank's device time ("weak" scaling: the per-rank
+work stays put as N grows); ``roofline`` = each rank's algorithmic bytes (the
+packed weights of the distinct experts it streams, the shared expert, the
+router weights and token rows) over that time, against the measured HBM copy
+bandwidth.  Steps rotate over distinct layers, so no step finds its experts
+in L2.  At N > 1 ``ep_parity`` decodes 16 tokens through the expert-parallel
+layer and through one GPU holding every expert and compares the bytes.
 
-Metric: q4nx GEMV HBM GB/s = algorithmic bytes (N*K*5/8 packed weights +
-2*T*K + 2*T*N activation/output bytes per GEMV) / device time.  Each GEMV of a
-step reads a different copy of its matrix and a step streams ~1 GB, far more
-than the 126 MB L2, so no timed GEMV is served from L2.
-
-The line also carries ``moe``: the config-3 MoE decode layer (BASELINE
-configs[2]; hidden 2048, 128 experts + 1 shared, top-8 softmax router, SwiGLU
-2048->768->2048 in q4nx), one token per rank per step, the routed experts
-sharded expert-parallel over the N ranks (all-gather of the token rows,
-local grouped expert GEMVs, reduce-scatter of the slot rows over NCCL): total
-tokens/s over the slowest rank's device time, with each rank's HBM roofline
-(packed bytes of the distinct experts it streams per step).  Steps rotate
-over distinct layers so no step finds its experts in L2.
+Sub-objects: ``gemv_sweep`` -- the q4nx GEMV decode sweep (configs[1]: T in
+{1,2,4,8,16} over 2048->4096, 4096->2048, 2048->512 and the 2048->151936
+lm-head; dense, replicas only), GB/s of algorithmic bytes (N*K*5/8 packed
+weights + 2*T*K + 2*T*N); ``config1`` -- the 4096x2048 T = 1 GEMV
+(configs[0]); ``moe_prefill`` -- 512 tokens with a Zipf(1.1) expert load
+(configs[3]); ``decode_step`` -- 48 layers + lm-head + sampling;
+``per_shape``, ``bfp16`` and ``moe_bfp16_down`` at N = 1.
 
 ``--impl reference`` times the reference's own CPU arithmetic for this path
-(the numpy restatement in ``oracle/``: f32-dequantised weights, f32 dot,
-bf16 RTNE -- ``host/backend.py:402-417``) on the host cores, rank 0 only.
+(the numpy restatement in ``oracle/`` of ``NumpyBackend`` and the router,
+f32-dequantised weights cached) on the host cores with every BLAS thread,
+rank 0 only, on the same MoE decode layer.
 """
 
 from __future__ import annotations
@@ -52,9 +54,14 @@ HBM_FALLBACK_GBS = 6650.0
 
 # DRAM traffic of the timed work, from ncu captures of the same commands on a
 # B200 (dram__bytes_read.sum + dram__bytes_write.sum): the GEMV launches of
-# one sweep step; one config-3 decode layer at T = 1 (moe_fused_kernel); the
+# one sweep step; one config-3 decode layer at T = 1 (rc_moe_fused_kernel); the
 # two grouped GEMVs of one 512-token prefill layer.  Single-GPU figures.
 MEASURED_TRAFFIC = {"gemv_step": 1033.4e6, "moe_layer_t1": 27.30e6, "prefill_gemms": 300.75e6}
+TRAFFIC_SOURCE = {
+    "gemv_step": "profiles/gemv_sweep_launch_list.md (all rc_q4nx_gemv_kernel launches of one step)",
+    "moe_layer_t1": "profiles/moe_decode_fused_t1.md (one rc_moe_fused_kernel launch, T = 1)",
+    "prefill_gemms": "profiles/moe_prefill_gemv_t512.md (the two grouped GEMV launches of a 512-token layer)",
+}
 
 
 def algo_bytes(n: int, k: int, t: int) -> int:
@@ -144,6 +151,11 @@ def capture_graph(torch, fn):
 
 
 def run_ours(args, rank: int, world: int, local_rank: int):
+    """Our arm.  The JSON line's ``value`` is the config-3 MoE decode layer
+    (the half of the metric that shards): tokens/s of all
+    ranks, one token per rank per step, experts expert-parallel over the
+    ranks.  The GEMV sweep and config 1 follow as sub-objects,
+    then prefill and the 48-layer decode step."""
     import torch
     import torch.distributed as dist
     from raon_npu_b200.device import Context
@@ -151,6 +163,53 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     ctx = Context(local_rank)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    moe = run_moe(args, ctx, torch, dev, rank, world, local_rank, barrier)
+    sweep = None if args.no_gemv else run_gemv_sweep(args, ctx, torch, dev, rank, world, local_rank, barrier)
+    prefill = None if args.no_prefill else run_moe_prefill(args, ctx, torch, dev, rank, world, local_rank, barrier)
+    dstep = None if args.no_decode_step else run_decode_step(args, ctx, torch, dev, rank, world, local_rank,
+                                                             barrier)
+    moe_bf = None
+    if world == 1 and not args.no_extras:
+        moe_bf = measure_moe_bfp16_down(args, ctx, torch, dev)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": moe["value"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": moe["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u4 codes (q4nx), bf16 act, f32 acc",
+            "data": "synthetic: q4nx weights from N(0,0.02) f32 (torch cuda generator, seeded, quantised on the "
+                    "GPU bit-identically to the reference quantiser), bf16 x N(0,1)",
+            "config": moe["config"],
+            "roofline": moe["roofline"],
+            "e2e": moe["e2e"],
+            "cpu_baseline": moe["cpu_baseline"],
+            "gpu_launches": moe["gpu_launches"],
+            "clocks": moe["clocks"],
+            "ep_parity": moe["ep_parity"],
+            "moe_phases_us": moe.get("phases_us"),
+            "moe_prefill": prefill,
+            "decode_step": dstep,
+            "gemv_sweep": sweep["sweep"] if sweep else None,
+            "config1": sweep["config1"] if sweep else None,
+            "per_shape": sweep["per_shape"] if sweep else None,
+            "bfp16": sweep["bfp16"] if sweep else None,
+            "moe_bfp16_down": moe_bf,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+
+
+def run_gemv_sweep(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barrier):
+    """the q4nx GEMV decode sweep (dense GEMV: replicas
+    only, so at N GPUs each rank runs its own copy); config 1 as its own
+    entry; the per-shape launch table and the bfp16ebs8 GEMV (rank 0, N = 1)."""
+    import torch.distributed as dist
     stream = torch.cuda.current_stream(dev)
     gen = torch.Generator(device=dev)
 
@@ -182,10 +241,6 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 cps = weights[(n, k)]
                 cps[ti % len(cps)].gemv_into(xs[(n, k, t)], ys[(n, k, t)], t)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
     # Eager warm-up (sizes the scratch), then capture one step in a CUDA graph:
     # a decode step is a fixed launch sequence, replayed without host overhead.
     for _ in range(args.warmup):
@@ -193,14 +248,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     torch.cuda.synchronize()
     ctx.sync()
     step_graph = capture_graph(torch, step)
-    stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         step_graph.replay()
     torch.cuda.synchronize()
     ctx.sync()
     barrier()
-    step = step_graph.replay
-
     clocks = ClockSampler(_gpu_index(local_rank))
     clocks.start()
     time.sleep(0.3)
@@ -210,53 +262,70 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        step_graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1) / args.steps
-    ms_max = ms
-    if world > 1:
-        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms_max = float(tt.item())
+    ms_max = _max_over_ranks(torch, dist, dev, world, ms)
+    del step_graph
     ctx.sync()
-
     sb = step_bytes()
-    value = world * sb / (ms_max * 1e-3) / 1e9
     peak, peak_kind = peaks()
     achieved = sb / (ms * 1e-3) / 1e9
 
-    # Per-shape launch times (rank 0): back-to-back launches over rotating
-    # copies whose total exceeds L2, so each launch streams from HBM.
-    per_shape = []
-    bfp16 = None
-    if rank == 0 and not args.no_per_shape:
+    # Per-shape launch times (rank 0, one GPU): back-to-back launches over
+    # rotating copies whose total exceeds L2, so each launch streams from HBM.
+    per_shape, bfp16 = None, None
+    if rank == 0 and world == 1 and not args.no_extras:
         per_shape = measure_per_shape(ctx, torch, dev, gen, stream, weights)
         bfp16 = measure_bfp16(ctx, torch, dev, gen)
 
     # End to end through the host-buffer C-ABI entry point (rc_gemv_host):
     # pinned host x -> device, GEMV, y -> host, every GEMV of the step.
     host_x = {key: x.cpu().numpy().view(np.uint16) for key, x in xs.items()}
-    e2e_steps = max(2, min(args.steps, 5))
-    for _ in range(1):
+
+    def e2e_pass():
         for ti, t in enumerate(TOKENS):
             for n, k in SHAPES:
                 weights[(n, k)][ti % len(weights[(n, k)])].gemv_host(host_x[(n, k, t)])
+    e2e_pass()
     barrier()
+    e2e_steps = max(2, min(args.steps, 5))
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        for ti, t in enumerate(TOKENS):
-            for n, k in SHAPES:
-                weights[(n, k)][ti % len(weights[(n, k)])].gemv_host(host_x[(n, k, t)])
-    e2e_s = (time.perf_counter() - t0) / e2e_steps
-    if world > 1:
-        tt = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_s = float(tt.item())
+        e2e_pass()
+    e2e_s = _max_over_ranks(torch, dist, dev, world, (time.perf_counter() - t0) / e2e_steps)
     h2d = sum(2 * t * k for t in TOKENS for n, k in SHAPES)
     d2h = sum(2 * t * n for t in TOKENS for n, k in SHAPES)
+
+    # Config 1 (4096 x 2048, T = 1) on its own: device time per launch from the
+    # per-shape table, end to end through rc_gemv_host, the oracle's f32 GEMV.
+    config1 = None
+    if rank == 0 and world == 1:
+        n1, k1 = 4096, 2048
+        w1 = weights[(n1, k1)][0]
+        x1 = host_x[(n1, k1, 1)]
+        for _ in range(3):
+            w1.gemv_host(x1)
+        reps = 200
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            w1.gemv_host(x1)
+        e2e1 = (time.perf_counter() - t0) / reps
+        b1 = algo_bytes(n1, k1, 1)
+        row = [e for e in (per_shape or []) if e["k_to_n"] == f"{k1}->{n1}" and e["t"] == 1]
+        config1 = {"workload": "BASELINE configs[0]: q4nx GEMV 4096x2048 (out x in), T = 1",
+                   "algorithmic_bytes": b1,
+                   "us_per_launch": row[0]["us_per_launch"] if row else None,
+                   "gbs": row[0]["gbs"] if row else None, "frac": row[0]["frac"] if row else None,
+                   "timing": "back-to-back launches over rotating copies larger than L2 (CUDA events)",
+                   "e2e": {"value": round(b1 / e2e1 / 1e9, 3), "unit": "GB/s", "us_per_call": round(e2e1 * 1e6, 2),
+                           "h2d_bytes_per_step": 2 * k1, "d2h_bytes_per_step": 2 * n1,
+                           "api": "rc_gemv_host (synchronous)"}}
+        if not args.no_cpu_baseline:
+            config1["cpu_baseline"] = cpu_config1(ctx, torch, dev, w1, x1, budget_s=min(5.0, args.cpu_seconds))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -265,45 +334,42 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         for w in ws:
             w.free()
     weights.clear()
+    sweep = {
+        "metric": "q4nx GEMV HBM GB/s (BASELINE configs[1] sweep)", "value": round(world * sb / (ms_max * 1e-3) / 1e9, 2),
+        "unit": "GB/s", "ms_per_step": round(ms_max, 4), "steps": args.steps,
+        "config": {"shapes_k_to_n": [f"{k}->{n}" for n, k in SHAPES], "tokens": TOKENS,
+                   "parallelism": f"replicas x{world} (dense GEMV does not shard)",
+                   "l2": "each step streams %.2f GB of distinct weights" % (sb / 1e9),
+                   "algorithmic_bytes_per_step": sb},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "traffic": MEASURED_TRAFFIC["gemv_step"], "traffic_source": TRAFFIC_SOURCE["gemv_step"],
+                     "kernel": "rc_q4nx_gemv_kernel (20 launches per step)"},
+        "e2e": {"value": round(world * sb / e2e_s / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "api": "rc_gemv_host (synchronous per GEMV)"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk,
+        "cpu_baseline": cpu,
+    }
+    return {"sweep": sweep, "config1": config1, "per_shape": _compact_shapes(per_shape), "bfp16": bfp16}
 
-    moe = None if args.no_moe else run_moe(args, ctx, torch, dev, rank, world, local_rank, barrier)
-    moe_bf = None
-    if moe is not None and world == 1 and bfp16 is not None:
-        moe_bf = measure_moe_bfp16_down(args, ctx, torch, dev)
-    prefill = None if args.no_moe else run_moe_prefill(args, ctx, torch, dev, rank, world, local_rank, barrier)
-    dstep = None if args.no_decode_step else run_decode_step(args, ctx, torch, dev, rank, world, local_rank,
-                                                             barrier)
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes, bf16 act, f32 acc",
-            "data": "synthetic: q4nx weights from N(0,0.02) f32 (torch cuda generator, seeded), bf16 x N(0,1)",
-            "config": {"workload": "q4nx GEMV decode sweep (BASELINE configs[1])",
-                       "shapes_k_to_n": [f"{k}->{n}" for n, k in SHAPES], "tokens": TOKENS,
-                       "parallelism": f"replicas x{world} (dense GEMV does not shard)",
-                       "l2": "inputs larger than L2: each step streams %.2f GB of distinct weights" % (sb / 1e9),
-                       "algorithmic_bytes_per_step": sb},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "traffic": MEASURED_TRAFFIC["gemv_step"],
-                         "traffic_source": "ncu launch list of the sweep step, all gemv_kernel launches",
-                         "kernel": "q4nx_gemv_kernel (20 launches per step, event-timed step)"},
-            "e2e": {"value": round(world * sb / e2e_s / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "api": "rc_gemv_host (synchronous per GEMV)"},
-            "gpu_launches": launches_per_step * args.steps,
-            "clocks": clk,
-            "per_shape": per_shape,
-            "bfp16": bfp16,
-            "cpu_baseline": cpu,
-            "moe": moe,
-            "moe_bfp16_down": moe_bf,
-            "moe_prefill": prefill,
-            "decode_step": dstep,
-        }
-        print(json.dumps(line), flush=True)
-    ctx.close()
+def _max_over_ranks(torch, dist, dev, world: int, v: float) -> float:
+    if world == 1:
+        return v
+    tt = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    return float(tt.item())
+
+
+def _compact_shapes(rows):
+    """Per-shape launch table as {"KxN": {T: [us per launch, fraction of peak]}}."""
+    if rows is None:
+        return None
+    out = {}
+    for e in rows:
+        out.setdefault(e["k_to_n"], {})[e["t"]] = [e["us_per_launch"], e["frac"]]
+    return out
 
 
 def measure_bfp16(ctx, torch, dev, gen):
@@ -352,11 +418,8 @@ def measure_bfp16(ctx, torch, dev, gen):
         for w in cps:
             w.free()
     ctx.sync()
-    lm = [e for e in out if e["k_to_n"] == f"{LM_HEAD[1]}->{LM_HEAD[0]}"]
-    return {"workload": "bfp16ebs8 GEMV (9-bit weights, 8-column groups sharing an exponent byte)",
-            "bytes_per_weight": 9 / 8, "kernel": "bfp16_gemv_kernel (16-row half blocks by bulk copy, "
-            "f32x2 CUDA-core products; split-K with ordered finalize for small N)",
-            "lm_head": {e["t"]: {"gbs": e["gbs"], "frac": e["frac"]} for e in lm}, "per_shape": out}
+    return {"workload": "bfp16ebs8 GEMV (9-bit weights), synthetic blocks, rotating copies > L2",
+            "kernel": "rc_bfp16_gemv_kernel", "per_shape_us_frac": _compact_shapes(out)}
 
 
 def measure_per_shape(ctx, torch, dev, gen, stream, weights):
@@ -424,19 +487,20 @@ def _moe_seed(layer: int, expert: int) -> int:
     return 7_000_000 + 1000 * layer + expert
 
 
-def build_moe_layers(ctx, torch, dev, n_layers: int):
-    """n_layers distinct config-3 layers; this rank loads its own experts and
-    the shared one (weights seeded per (layer, expert), so every rank agrees)."""
+def build_moe_layers(ctx, torch, dev, n_layers: int, first: int = 0, all_experts: bool = False):
+    """n_layers distinct config-3 layers (layer ids first, first + 1, ...); this
+    rank loads its own experts and the shared one, or every expert with
+    ``all_experts`` (weights seeded per (layer, expert), so every rank agrees)."""
     from raon_npu_b200.device import MoeLayer
     from raon_npu_b200.expert_parallel import ExpertParallelMoe
     H, I, E, k = MOE["hidden"], MOE["inter"], MOE["experts"], MOE["k"]
     gen = torch.Generator(device=dev)
     eps = []
-    for li in range(n_layers):
+    for li in range(first, first + n_layers):
         layer = MoeLayer(ctx, H, I, E, has_shared=True)
         ep = ExpertParallelMoe(layer, k, act="swiglu", router="softmax")
         for e in range(E + 1):
-            if not ep.owns(e):
+            if not (all_experts or ep.owns(e)):
                 continue
             gen.manual_seed(_moe_seed(li, e))
             gu = torch.randn((2 * I, H), generator=gen, device=dev) * 0.02
@@ -560,7 +624,25 @@ def measure_moe_bfp16_down(args, ctx, torch, dev):
                         "bfp16 grouped down over 8-row expert blocks, combine (one CUDA graph)"}}
 
 
-def moe_cpu_sample(n_tokens: int, budget_s: float):
+def cpu_threads() -> dict:
+    """Give the CPU legs every host core: ``torchrun`` sets OMP_NUM_THREADS=1
+    for its workers, so the BLAS thread pools are raised to os.cpu_count()
+    explicitly.  Returns the threads each pool now uses."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+        threadpool_limits(limits=n)
+        pools = {f"{i.get('internal_api')}": i.get("num_threads") for i in threadpool_info()}
+    except Exception as e:          # noqa: BLE001 - reported in the JSON line
+        pools = {"threadpoolctl": f"unavailable: {type(e).__name__}"}
+    nums = [v for v in pools.values() if isinstance(v, int)]
+    return {"threads": max(nums) if nums else 1, "pools": pools}
+
+
+_MOE_CPU_CACHE: dict = {}
+
+
+def moe_cpu_sample(n_tokens: int, budget_s: float, bias: np.ndarray | None = None):
     """The reference's CPU arithmetic for one config-3 decode layer (oracle port:
     router, routed experts in ascending ID, shared expert), timed per token
     over f32-dequantised weights cached.  To bound the setup, 16 distinct
@@ -572,7 +654,7 @@ def moe_cpu_sample(n_tokens: int, budget_s: float):
     H, I, E, k = MOE["hidden"], MOE["inter"], MOE["experts"], MOE["k"]
     rng = np.random.default_rng(77)
     wr = q.f32_to_bf16((rng.standard_normal((E, H)) * 0.02).astype(np.float32))
-    cache = {}
+    cache = _MOE_CPU_CACHE
 
     def expert(e):
         if e not in cache:
@@ -585,13 +667,35 @@ def moe_cpu_sample(n_tokens: int, budget_s: float):
     shared = expert(E)
     while done < n_tokens and (secs < budget_s or done == 0):
         x = q.f32_to_bf16(rng.standard_normal(H).astype(np.float32))
-        ids, _, _ = ob.route_softmax(x, wr, k)
-        experts = {int(e): expert(int(e) % 16) for e in ids}
         t0 = time.perf_counter()
-        ob.moe_decode_layer(experts, shared, wr, x, k, act="swiglu")
+        if bias is None:
+            ids, _, _ = ob.route_softmax(x, wr, k)
+            experts = {int(e): expert(int(e) % 16) for e in ids}
+            t0 = time.perf_counter()
+            ob.moe_decode_layer(experts, shared, wr, x, k, act="swiglu")
+        else:
+            # the prefill router of config 4: softmax of the biased logits
+            logits = (ob.router_logits(x, wr) + bias).astype(np.float32)
+            ids = ob.topk_lower_index_wins(logits, k)
+            sel = logits[ids].astype(np.float64)
+            ew = np.exp(sel - sel.max())
+            w = (ew / ew.sum()).astype(np.float32)
+            experts = {int(e): expert(int(e) % 16) for e in ids}
+            routed = ob.moe_experts(experts, x, ids, w, act="swiglu")
+            ob.moe_token_with_shared(routed, ob.expert_forward(*shared, x, "swiglu"))
         secs += time.perf_counter() - t0
         done += 1
     return done, secs
+
+
+def moe_cpu_baseline(budget_s: float) -> dict:
+    th = cpu_threads()
+    n_tok, secs = moe_cpu_sample(256, budget_s)
+    return {"value": round(n_tok / secs, 2), "unit": "tokens/s", "cores": th["threads"], "kind": "port",
+            "blas_threads": th["pools"],
+            "sample": f"{n_tok} decode tokens through the oracle's numpy MoE layer (router, 8 routed + shared "
+                      f"SwiGLU experts, ascending-ID combine; host/backend.py:466-510, host/raon.py:1224-1327 "
+                      f"restated), f32 weights cached (16 weight sets, id mod 16)"}
 
 
 def _gather_tokens(torch, dist, world, x):
@@ -600,6 +704,44 @@ def _gather_tokens(torch, dist, world, x):
     g = torch.empty((world * x.shape[0], x.shape[1]), dtype=x.dtype, device=x.device)
     dist.all_gather_into_tensor(g.view(torch.bfloat16), x.view(torch.bfloat16))
     return g
+
+
+def moe_ep_parity(ctx, torch, dev, rank: int, world: int, ep) -> dict:
+    """N > 1: the same 16 tokens through the expert-parallel layer (16/N per
+    rank, its exchange inside the decode kernel over NVLink peer memory) and
+    through a one-GPU ``rc_moe_decode`` of the same layer holding every expert
+    (rank 0): ``equal`` when every byte agrees."""
+    import torch.distributed as dist
+    H, k = MOE["hidden"], MOE["k"]
+    M = 16 // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6161)                       # the same 16 tokens on every rank
+    xall = torch.randn((world * M, H), generator=gen, device=dev).to(torch.bfloat16).view(torch.int16)
+    mine = xall[rank * M:(rank + 1) * M].contiguous()
+    out = torch.empty((M, H), dtype=torch.int16, device=dev)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ep.decode(mine, out)
+    transport = ep.active_transport
+    torch.cuda.synchronize()
+    ctx.sync()
+    got = torch.empty((world * M, H), dtype=torch.int16, device=dev)
+    dist.all_gather_into_tensor(got.view(torch.bfloat16), out.view(torch.bfloat16))
+    ok, diff = 1, 0
+    if rank == 0:
+        full = build_moe_layers(ctx, torch, dev, 1, first=0, all_experts=True)[0]
+        ref = torch.empty_like(got)
+        full.layer.decode(xall, k, ref, act="swiglu")
+        torch.cuda.synchronize()
+        ctx.sync()
+        diff = int((ref != got).sum().item())
+        ok = int(diff == 0)
+        full.layer.close()
+    flag = torch.tensor([ok, diff], dtype=torch.int64, device=dev)
+    dist.broadcast(flag, 0)
+    return {"equal": bool(flag[0].item()), "tokens": world * M, "tokens_per_rank": M,
+            "differing_values": int(flag[1].item()), "transport": transport,
+            "reference": "rc_moe_decode of the same layer with all 129 experts on rank 0's GPU"}
 
 
 def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barrier):
@@ -665,12 +807,7 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    ms_max = ms
-    if world > 1:
-        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms_max = float(tt.item())
+    ms_max = _max_over_ranks(torch, dist, dev, world, e0.elapsed_time(e1) / args.steps)
     del graphs
     ctx.sync()
 
@@ -697,7 +834,7 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
     achieved = avg_rank_bytes / (ms_max * 1e-3) / 1e9
 
     # End to end through the host entry point: pinned host token rows -> device,
-    # expert-parallel decode (collectives included), rows back to the host.
+    # expert-parallel decode (exchange included), rows back to the host.
     host_x = [x.cpu().numpy().view(np.uint16) for x in xs]
     e2e_n = max(2 * n_layers, min(args.steps, 64))
     for li in range(n_layers):
@@ -706,53 +843,43 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
     t0 = time.perf_counter()
     for s in range(e2e_n):
         eps[s % n_layers].decode_host(host_x[s % n_layers])
-    e2e_s = (time.perf_counter() - t0) / e2e_n
-    if world > 1:
-        tt = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_s = float(tt.item())
+    e2e_s = _max_over_ranks(torch, dist, dev, world, (time.perf_counter() - t0) / e2e_n)
 
+    transport = eps[0].active_transport
+    parity = moe_ep_parity(ctx, torch, dev, rank, world, eps[0]) if world > 1 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        n_tok, secs = moe_cpu_sample(64, args.cpu_seconds)
-        cpu = {"value": round(n_tok / secs, 2), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{n_tok} decode tokens through the oracle's numpy MoE layer (router, 8 routed + "
-                         f"shared SwiGLU experts, ascending-ID combine; host/backend.py:466-510, "
-                         f"host/raon.py:1224-1327 restated), f32 weights cached (16 weight sets, id mod 16)"}
-    transport = eps[0].active_transport
+        cpu = moe_cpu_baseline(args.cpu_seconds)
     if world == 1 or transport == "p2p":
-        per_step, kdesc = 1, "one persistent kernel: router, top-k, grouped gate/up and down GEMVs, combine" + (
-            "; token rows and expert rows exchanged over NVLink peer stores inside it" if world > 1 else "")
+        per_step, kdesc = 1, "rc_moe_fused_kernel: router, top-k, grouped gate/up and down GEMVs, combine" + (
+            "; token and expert rows exchanged over NVLink peer stores inside it" if world > 1 else "")
     else:
-        per_step, kdesc = 2, ("persistent kernel (router, top-k, local experts) + combine, NCCL all-gather and "
-                              "reduce-scatter around them")
+        per_step, kdesc = 2, ("rc_moe_fused_kernel (local experts) + combine, NCCL all-gather and reduce-scatter "
+                              "around them")
     barrier()
     for ep in eps:
         ep.layer.close()
-    res = {
-        "metric": "MoE decode layer tokens/s", "value": round(world * M / (ms_max * 1e-3), 1), "unit": "tokens/s",
-        "ms_per_step": round(ms_max, 5), "steps": args.steps, "scaling": "weak",
-        "config": {"workload": "MoE decode layer (BASELINE configs[2])", "hidden": H, "intermediate": MOE["inter"],
-                   "experts": E, "shared_experts": 1, "top_k": k, "router": "softmax, renormalised top-k",
-                   "act": "swiglu", "tokens_per_rank": M, "parallelism": f"ep{world}",
-                   "experts_per_rank": E // world, "layers_rotated": n_layers,
-                   "l2": "each step uses the next of %d distinct layers with fixed tokens: the %.1f MB of "
-                         "experts a step streams per rank come back after %.0f MB of other layers' experts "
-                         "(L2 126 MB)" % (n_layers, touched / 1e6, (n_layers - 1) * touched / 1e6),
-                   "cuda_graph": bool(int(ok.item())), "graph_error": graph_err, "ep_transport": transport},
+    return {
+        "value": round(world * M / (ms_max * 1e-3), 1), "ms_per_step": round(ms_max, 5),
+        "config": {"workload": "MoE decode layer (BASELINE configs[2]): hidden 2048, 128 experts + 1 shared, "
+                               "I=768, softmax top-8, SwiGLU, q4nx", "tokens_per_rank": M,
+                   "parallelism": f"ep{world}", "experts_per_rank": E // world, "transport": transport,
+                   "l2": "steps rotate over %d distinct layers; a layer's %.1f MB of experts return after "
+                         "%.0f MB of other layers' (> L2 126 MB)" % (n_layers, touched / 1e6,
+                                                                      (n_layers - 1) * touched / 1e6),
+                   "cuda_graph": bool(int(ok.item())), "graph_error": graph_err},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": MEASURED_TRAFFIC["moe_layer_t1"] if world == 1 and M == 1 else None,
-                     "traffic_source": "ncu capture of one moe_fused_kernel launch (T = 1)",
-                     "per_rank_bytes_per_step": round(avg_rank_bytes),
-                     "kernel": f"MoE layer step per rank ({kdesc})"},
+                     "traffic_source": TRAFFIC_SOURCE["moe_layer_t1"],
+                     "per_rank_bytes_per_step": round(avg_rank_bytes), "kernel": kdesc},
         "e2e": {"value": round(world * M / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * M * H,
                 "d2h_bytes_per_step": 2 * M * H, "api": "ExpertParallelMoe.decode_host (synchronous)"},
         "gpu_launches": per_step * args.steps,
         "clocks": clk,
         "cpu_baseline": cpu,
+        "ep_parity": parity,
     }
-    return res
 
 
 # ------------------------------------------------------- MoE prefill layer --
@@ -864,31 +991,53 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
     tflops_peak = _bf16_peak()
     hbm_frac = avg_bytes / (ms_max * 1e-3) / 1e9 / peak
     tc_frac = avg_flops / (ms_max * 1e-3) / 1e12 / tflops_peak
+
+    # end to end: this rank's token rows from pinned host memory, the layer
+    # (exchange included), its rows back to the host
+    host_x = [x.cpu().numpy().view(np.uint16) for x in xs]
+    for li in range(n_layers):
+        eps[li].prefill_host(host_x[li])
+    barrier()
+    e2e_n = max(2, min(args.steps, 10))
+    t0 = time.perf_counter()
+    for s_ in range(e2e_n):
+        eps[s_ % n_layers].prefill_host(host_x[s_ % n_layers])
+    e2e_s = _max_over_ranks(torch, dist, dev, world, (time.perf_counter() - t0) / e2e_n)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        th = cpu_threads()
+        n_tok, secs = moe_cpu_sample(PREFILL_TOKENS, args.cpu_seconds / 2, bias=bias)
+        cpu = {"value": round(n_tok / secs, 2), "unit": "tokens/s", "cores": th["threads"], "kind": "port",
+               "sample": f"{n_tok} of the layer's tokens through the oracle per token (biased softmax router, "
+                         f"NumpyBackend.moe_experts restated + shared expert), f32 weights cached"}
     for ep in eps:
         ep.layer.close()
     return {
         "metric": "MoE prefill layer tokens/s", "value": round(T / (ms_max * 1e-3), 1), "unit": "tokens/s",
-        "ms_per_step": round(ms_max, 4), "steps": args.steps, "scaling": "strong",
-        "config": {"workload": "MoE prefill layer (BASELINE configs[3])", "tokens": T, "hidden": H,
-                   "intermediate": I, "experts": E, "shared_experts": 1, "top_k": k,
-                   "router": "softmax of logits + b_e, b_e = -1.1 ln(rank_e) (Zipf(1.1) load)",
-                   "parallelism": f"ep{world}", "tokens_per_rank": M, "layers_rotated": n_layers,
+        "ms_per_step": round(ms_max, 4), "scaling": "strong",
+        "config": {"workload": "MoE prefill layer (BASELINE configs[3]): 512 tokens, Zipf(1.1) expert load",
+                   "parallelism": f"ep{world}", "tokens_per_rank": M, "kernel": prefill_kernel_desc(world),
                    "cuda_graph": bool(int(ok.item())), "graph_error": graph_err,
                    "rank0_rows_per_step": round(avg[2]), "rank0_experts_hit": round(avg[3], 1)},
         "roofline": {"bound": "hbm" if hbm_frac >= tc_frac else "tensor",
                      "achieved": round(avg_bytes / (ms_max * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(hbm_frac, 4), "peak_source": peak_kind,
                      "traffic": MEASURED_TRAFFIC["prefill_gemms"] if world == 1 else None,
-                     "traffic_source": "ncu capture of the two pf_gemv_kernel launches of one layer (512 tokens)",
+                     "traffic_source": TRAFFIC_SOURCE["prefill_gemms"],
                      "tensor_tflops": round(avg_flops / (ms_max * 1e-3) / 1e12, 1),
                      "tensor_peak_tflops": tflops_peak, "tensor_frac": round(tc_frac, 4),
-                     "per_rank_bytes_per_step": round(avg_bytes), "per_rank_flops_per_step": round(avg_flops),
-                     "kernel": "prefill layer per rank (router, plan, grouped gate/up + down GEMVs over 8-token "
-                               "blocks on register-fragment mma, combine; NCCL all-gather + reduce-scatter at "
-                               "N>1)"},
+                     "per_rank_bytes_per_step": round(avg_bytes), "per_rank_flops_per_step": round(avg_flops)},
+        "e2e": {"value": round(T / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * M * H,
+                "d2h_bytes_per_step": 2 * M * H, "api": "ExpertParallelMoe.prefill_host (synchronous)"},
         "gpu_launches": (8 if world == 1 else 9) * args.steps,
         "clocks": clk,
+        "cpu_baseline": cpu,
     }
+
+
+def prefill_kernel_desc(world: int) -> str:
+    return ("router, plan, grouped gate/up + down GEMVs over 8-token blocks (register-fragment mma), combine"
+            + ("; NCCL all-gather + reduce-scatter" if world > 1 else ""))
 
 
 # ------------------------------------------------------ full decode step --
@@ -1062,19 +1211,25 @@ def run_decode_step(args, ctx, torch, dev, rank: int, world: int, local_rank: in
         wb.free()
         ep.layer.close()
     lm.free()
+    # DRAM traffic of the step, scaled from single-kernel captures: the GEMV
+    # launches move 0.995x their algorithmic bytes (sweep launch list) and one
+    # T = 1 MoE layer moves MEASURED_TRAFFIC["moe_layer_t1"] (one GPU only)
+    traffic = None
+    if world == 1:
+        gemv_ratio = MEASURED_TRAFFIC["gemv_step"] / step_bytes()
+        traffic = round(DECODE_LAYERS * (2 * 4096 * H * 5 // 8 * gemv_ratio + MEASURED_TRAFFIC["moe_layer_t1"])
+                        + LM_HEAD[0] * LM_HEAD[1] * 5 // 8 * gemv_ratio)
     return {
         "metric": "decode step tokens/s (48 layers + lm-head + sampling)", "value": round(world / (ms_max * 1e-3), 2),
         "unit": "tokens/s", "ms_per_step": round(ms_max, 4), "steps": steps, "scaling": "weak",
-        "config": {"workload": "synthetic full decode step (BASELINE configs[4])", "layers": DECODE_LAYERS,
-                   "per_layer": "q4nx 2048->4096->2048 projections + config-3 MoE (128+1 experts, top-8) + "
-                                "residual add with RMS normalisation", "lm_head": "2048->151936 q4nx", "sampling": "top-k 50, top-p 0.9, T=1",
+        "config": {"workload": "synthetic full decode step (BASELINE configs[4]): 48 x (q4nx 2048->4096->2048 + "
+                               "config-3 MoE + residual/RMS), lm-head 2048->151936, top-k 50 / top-p 0.9",
                    "tokens_per_rank": 1, "parallelism": f"projections replicated, experts ep{world}",
-                   "cuda_graph": graph_err is None and bool(int(ok.item())), "graph_error": graph_err,
-                   "l2": "each step streams ~2 GB of distinct weights (>> L2)"},
+                   "cuda_graph": graph_err is None and bool(int(ok.item())), "graph_error": graph_err},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": None,
-                     "per_rank_bytes_per_step": round(avg_bytes),
-                     "kernel": "decode step per rank (96 GEMVs, 48 MoE layers, 48 adds, lm-head GEMV, sampler)"},
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": traffic,
+                     "traffic_source": "scaled from the GEMV sweep and MoE layer captures (see those sources)",
+                     "per_rank_bytes_per_step": round(avg_bytes)},
         "e2e": {"value": round(world / e2e_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 2 * H,
                 "d2h_bytes_per_step": 4, "api": "graph replay with the hidden row copied in and the id copied out"},
         "gpu_launches": (DECODE_LAYERS * 7 + 2) * steps,
@@ -1090,6 +1245,7 @@ def decode_step_cpu_sample(ctx, torch, dev, layers, lm, budget_s: float):
     GPU, bit-identical to the reference's dequantiser)."""
     from oracle import backend as ob
     from oracle.sampling import sample_token_u
+    th = cpu_threads()
 
     def f32(w):
         out = torch.empty((w.n, w.k), dtype=torch.float32, device=dev)
@@ -1111,7 +1267,7 @@ def decode_step_cpu_sample(ctx, torch, dev, layers, lm, budget_s: float):
     sample_token_u(ob.bf16_to_f32(lg), [], 50, 0.9, 1.0, 0.0, 0.5)
     head_s = time.perf_counter() - t0
     per_token = DECODE_LAYERS * (proj_s + moe_secs / moe_tokens) + head_s
-    return {"value": round(1.0 / per_token, 3), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": round(1.0 / per_token, 3), "unit": "tokens/s", "cores": th["threads"], "kind": "port",
             "sample": f"one layer (2 projections x3, MoE layer x{moe_tokens}) and the lm-head + sampler once, "
                       f"numpy f32 with cached weights, extrapolated to {DECODE_LAYERS} layers"}
 
@@ -1151,6 +1307,7 @@ def cpu_gemv_sweep_sample(weights_f32: dict, xs_u16: dict, budget_s: float):
 
 
 def cpu_baseline(ctx, torch, dev, weights, host_x, budget_s: float):
+    th = cpu_threads()
     w32 = {}
     for (n, k), cps in weights.items():
         out = torch.empty((n, k), dtype=torch.float32, device=dev)
@@ -1159,17 +1316,48 @@ def cpu_baseline(ctx, torch, dev, weights, host_x, budget_s: float):
         w32[(n, k)] = out.cpu().numpy()
         del out
     done, secs, passes, keys = cpu_gemv_sweep_sample(w32, host_x, budget_s)
-    return {"value": round(done / secs / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": round(done / secs / 1e9, 3), "unit": "GB/s", "cores": th["threads"], "kind": "port",
             "sample": f"{passes} pass(es) of the full sweep ({len(keys)} GEMVs) through the oracle's numpy f32 "
-                      f"GEMV (host/backend.py:402-417 restated), f32 weights cached; "
-                      f"OPENBLAS_NUM_THREADS={os.environ.get('OPENBLAS_NUM_THREADS', 'unset')}"}
+                      f"GEMV (host/backend.py:402-417 restated), f32 weights cached"}
+
+
+def cpu_config1(ctx, torch, dev, w, x_u16, budget_s: float) -> dict:
+    """Config 1 through the oracle's f32 GEMV with the dequantised weights cached
+    (the reference's steady state); GB/s of the same algorithmic bytes."""
+    from oracle import backend as ob
+    th = cpu_threads()
+    out = torch.empty((w.n, w.k), dtype=torch.float32, device=dev)
+    w.dequant_into(out)
+    torch.cuda.synchronize()
+    w32 = out.cpu().numpy()
+    del out
+    ob.linear(w32, x_u16)
+    n, secs = 0, 0.0
+    while secs < budget_s and n < 2000:
+        t0 = time.perf_counter()
+        ob.linear(w32, x_u16)
+        secs += time.perf_counter() - t0
+        n += 1
+    return {"value": round(n * algo_bytes(w.n, w.k, 1) / secs / 1e9, 3), "unit": "GB/s",
+            "us_per_call": round(secs / n * 1e6, 1), "cores": th["threads"], "kind": "port",
+            "sample": f"{n} calls of the oracle's NumpyBackend.linear restatement, f32 weights cached"}
 
 
 def run_reference(args, rank: int):
-    """Reference arm: the reference's CPU implementation of the path (oracle port)."""
+    """Reference arm: the reference's CPU implementation of the path (the
+    oracle port of NumpyBackend and the router), on the host cores with every
+    BLAS thread, rank 0 only.  ``value``: the config-3 MoE decode layer,
+    tokens/s (our arm's headline metric and config); the GEMV sweep follows."""
     if rank != 0:
         return
     from oracle import q4nx as q
+    th = cpu_threads()
+    # MoE decode layer: warm-up tokens (they also build the cached weights),
+    # then one token per step, as our arm's one token per rank per step
+    moe_cpu_sample(max(1, args.warmup), 0.0)
+    n_tok, secs = moe_cpu_sample(args.steps, float("inf"))
+    v = n_tok / secs
+    # GEMV sweep (configs[1]) on a bounded sample
     rng = np.random.default_rng(0)
     w32, xs = {}, {}
     for si, (n, k) in enumerate(SHAPES):
@@ -1179,33 +1367,25 @@ def run_reference(args, rank: int):
     for t in TOKENS:
         for n, k in SHAPES:
             xs[(n, k, t)] = q.f32_to_bf16(rng.standard_normal((t, k)).astype(np.float32))
-    for _ in range(args.warmup):
-        cpu_gemv_sweep_sample(w32, xs, 0.0)
-    t0 = time.perf_counter()
-    done = 0
-    for _ in range(args.steps):
-        d, _, _, _ = cpu_gemv_sweep_sample(w32, xs, 0.0)
-        done += d
-    secs = time.perf_counter() - t0
-    v = done / secs / 1e9
-    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3),
+    cpu_gemv_sweep_sample(w32, xs, 0.0)
+    done, gsecs, passes, _ = cpu_gemv_sweep_sample(w32, xs, min(args.cpu_seconds, 10.0))
+    gv = done / gsecs / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / n_tok * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (dequantised weights)",
             "data": "synthetic: q4nx weights from N(0,0.02) f32 (numpy default_rng, seeded), bf16 x N(0,1)",
-            "config": {"workload": "q4nx GEMV decode sweep (BASELINE configs[1])",
-                       "shapes_k_to_n": [f"{k}->{n}" for n, k in SHAPES], "tokens": TOKENS},
-            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": "one full sweep per step through the numpy restatement of "
-                                       "NumpyBackend.linear (host/backend.py:402-417), f32 weights cached"},
-            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    if not args.no_moe:
-        n_tok, msecs = moe_cpu_sample(64, args.cpu_seconds)
-        line["moe"] = {"metric": "MoE decode layer tokens/s", "value": round(n_tok / msecs, 2), "unit": "tokens/s",
-                       "config": {"workload": "MoE decode layer (BASELINE configs[2])", "parallelism": "1 host"},
-                       "cpu_baseline": {"value": round(n_tok / msecs, 2), "unit": "tokens/s",
-                                        "cores": os.cpu_count(), "kind": "port",
-                                        "sample": f"{n_tok} decode tokens, oracle numpy MoE layer, f32 weights "
-                                                  f"cached (16 weight sets, id mod 16)"}}
+            "config": {"workload": "MoE decode layer (BASELINE configs[2]): hidden 2048, 128 experts + 1 shared, "
+                                   "I=768, softmax top-8, SwiGLU, q4nx", "tokens_per_step": 1,
+                       "parallelism": "host CPU (the reference has no multi-device path)"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": th["threads"], "kind": "port",
+                             "blas_threads": th["pools"],
+                             "sample": f"{n_tok} decode tokens, one per step, through the oracle's numpy MoE "
+                                       f"layer (NumpyBackend.moe_experts + router + shared expert restated), "
+                                       f"f32 weights cached (16 weight sets, id mod 16)"},
+            "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gemv_sweep": {"value": round(gv, 3), "unit": "GB/s", "passes": passes,
+                           "sample": "the configs[1] sweep through the oracle's NumpyBackend.linear restatement, "
+                                     "f32 weights cached"}}
     print(json.dumps(line), flush=True)
 
 
@@ -1326,9 +1506,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-per-shape", action="store_true", help="skip the per-shape launch table")
-    ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode / prefill layers (configs[2], [3])")
+    ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV sweep and config 1 (configs[0], [1])")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the MoE prefill layer (configs[3])")
     ap.add_argument("--no-decode-step", action="store_true", help="skip the 48-layer decode step (configs[4])")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the per-shape launch table, the bfp16ebs8 GEMV and the bfp16-down MoE layer")
     ap.add_argument("--profile", default=None, help="NxK: run a few plain GEMV launches for ncu and exit; "
                     "'moe' / 'prefill': a few config-3 decode / config-4 prefill steps; 'moe_bfp16': decode "
                     "and prefill calls of a layer with bfp16ebs8 down matrices; 'bfp16:NxK': bfp16 GEMVs")

@@ -194,7 +194,10 @@ int rc_moe_experts_host(rc_moe *m, const uint16_t *x_host, int T, const int32_t 
  * routed_out [T][hidden] and, when shared_gu [T][2*inter] (the shared
  * expert's gate | up rows, computed by the caller) is given, the shared
  * expert's down rows shared_out [T][hidden] = linear(shared_down,
- * RTNE(act(gate, up))). */
+ * RTNE(act(gate, up))).  T is 1..4096: above 16 tokens the routed experts run
+ * on the prefill kernels (rc_moe_prefill_experts) and the shared rows in
+ * 16-token chunks of the decode kernels; every token's bytes are those of a
+ * call of at most 16 tokens. */
 int rc_moe_experts_grouped(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev,
                            const float *w_dev, int k, const uint16_t *shared_gu_dev, int act,
                            float gate_beta, float value_beta, uint16_t *routed_out_dev,
@@ -318,8 +321,9 @@ int rc_add_rms_bf16(rc_ctx *ctx, const uint16_t *a_dev, const uint16_t *b_dev, u
                     int n, float eps, void *stream);
 
 /* rc_gemv without any device allocation (this entry point has no counterpart
- * in the reference).  Arguments and results are those of rc_gemv; the context
- * is the one the weight was uploaded with.
+ * in the reference).  Arguments and results are those of rc_gemv, bit for
+ * bit, for q4nx matrices only: a bfp16ebs8 matrix gets RC_ERR_INVALID.  The
+ * context is the one the weight was uploaded with.
  *
  * Who needs it: callers that must not allocate device memory while they run
  * a GEMV -- a latency-critical serving thread that cannot afford the implicit
@@ -336,7 +340,10 @@ int rc_add_rms_bf16(rc_ctx *ctx, const uint16_t *a_dev, const uint16_t *b_dev, u
  * make this first call before any stream capture.  Every call shares the
  * array, which keeps the last call's contents: each call clears the counters
  * it uses, and calls that overlap on the GPU (different streams or threads)
- * race -- keep them ordered on one stream.
+ * race -- keep them ordered on one stream.  The looked-up address is kept for
+ * the life of the process: after a cudaDeviceReset (which also ends every
+ * context and weight of this library on that device) the entry point must not
+ * be called again in that process.
  *
  * Limits (RC_ERR_INVALID beyond them): nrows <= 262,144; the activations of
  * one launch must fit in shared memory -- K <= 5,120 for up to 16 bf16 rows

@@ -283,13 +283,14 @@ class CudaBackend(Backend):
     def moe_experts_grouped(self, layer, x, top_ids, top_weights, shared_gu, gate_beta=4.0, value_beta=25.0):
         """T tokens at once (npu/backend.py:4845-4979): returns (routed [T, C],
         shared_down [T, C]), shared_down = down(RTNE(act(shared_gu))) of the
-        layer's shared expert.  Token rows are independent, so any T is
-        processed in device calls of up to 16 tokens with identical bytes."""
+        layer's shared expert.  One device call for the whole batch: up to 16
+        tokens on the decode kernels, more (up to 4096) with the routed experts
+        on the prefill kernels; a token's bytes are the same either way."""
         import torch
         m, act = self._moe_layer(layer)
         if not isinstance(x, np.ndarray) or x.dtype != np.uint16 or x.ndim != 2 or x.shape[1] != m.hidden \
-                or x.shape[0] < 1:
-            raise ValueError(f"x must be a [T, {m.hidden}] uint16 ndarray with T >= 1")
+                or not 1 <= x.shape[0] <= 4096:
+            raise ValueError(f"x must be a [T, {m.hidden}] uint16 ndarray with 1 <= T <= 4096")
         T = x.shape[0]
         k = np.asarray(top_ids).shape[-1] if np.ndim(top_ids) == 2 else 0
         ids, w = check_moe_routes(top_ids, top_weights, m.n_experts, k, tokens=T)
@@ -299,19 +300,15 @@ class CudaBackend(Backend):
                 or shared_gu.shape != (T, 2 * m.inter):
             raise ValueError(f"shared_gu must be a [T, {2 * m.inter}] uint16 ndarray")
         dev = torch.device("cuda", self.ctx.device)
-        routed = np.empty((T, m.hidden), np.uint16)
-        shared = np.empty((T, m.hidden), np.uint16)
-        for t0 in range(0, T, 16):
-            t1 = min(T, t0 + 16)
-            xd = torch.from_numpy(np.ascontiguousarray(x[t0:t1]).view(np.int16)).to(dev)
-            idd = torch.from_numpy(np.ascontiguousarray(ids[t0:t1])).to(dev)
-            wd = torch.from_numpy(np.ascontiguousarray(w[t0:t1])).to(dev)
-            gd = torch.from_numpy(np.ascontiguousarray(shared_gu[t0:t1]).view(np.int16)).to(dev)
-            ro = torch.empty((t1 - t0, m.hidden), dtype=torch.int16, device=dev)
-            so = torch.empty((t1 - t0, m.hidden), dtype=torch.int16, device=dev)
-            m.experts_grouped(xd, idd, wd, k, ro, gd, so, act=act, gate_beta=gate_beta, value_beta=value_beta)
-            routed[t0:t1] = ro.cpu().numpy().view(np.uint16)
-            shared[t0:t1] = so.cpu().numpy().view(np.uint16)
+        xd = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(dev)
+        idd = torch.from_numpy(np.ascontiguousarray(ids)).to(dev)
+        wd = torch.from_numpy(np.ascontiguousarray(w)).to(dev)
+        gd = torch.from_numpy(np.ascontiguousarray(shared_gu).view(np.int16)).to(dev)
+        ro = torch.empty((T, m.hidden), dtype=torch.int16, device=dev)
+        so = torch.empty((T, m.hidden), dtype=torch.int16, device=dev)
+        m.experts_grouped(xd, idd, wd, k, ro, gd, so, act=act, gate_beta=gate_beta, value_beta=value_beta)
+        routed = ro.cpu().numpy().view(np.uint16)
+        shared = so.cpu().numpy().view(np.uint16)
         self.ctx.sync()
         return routed, shared
 

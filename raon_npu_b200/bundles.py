@@ -38,7 +38,25 @@ from pathlib import Path
 GEMV_FORMATS = ("q4nx_gemv", "bfp16_gemv")
 MOE_FORMATS = ("q4nx_gemv_bundle", "bfp16_gemv_bundle")
 
-_SHA_CACHE: dict[tuple[str, int, int], str] = {}
+
+class _DigestMemo:
+    """SHA-256 hex digests of files, remembered per file version: a file whose
+    device, inode, size and change times are unchanged is not read again."""
+
+    def __init__(self):
+        self._by_version: dict[tuple[int, int, int, int, int], str] = {}
+
+    def sha256(self, path: Path, st) -> str:
+        version = (st.st_dev, st.st_ino, st.st_size, st.st_mtime_ns, st.st_ctime_ns)
+        known = self._by_version.get(version)
+        if known is None:
+            with path.open("rb") as f:
+                known = hashlib.file_digest(f, "sha256").hexdigest()
+            self._by_version[version] = known
+        return known
+
+
+_DIGESTS = _DigestMemo()
 
 
 @dataclass(frozen=True)
@@ -194,25 +212,17 @@ def _resolve(root: Path, rel: str, name: str) -> Path:
 
 
 def verify(weights_dir, b: Bundle) -> Path:
-    """Size and SHA-256 of a bundle file, streamed; cached per file version (``npu/backend.py:319-346``)."""
+    """The bundle's file after checking it against the manifest: it exists,
+    its length is ``size_bytes`` and its SHA-256 is ``sha256`` (the contract of
+    ``npu/backend.py:319-346``; the digest is computed once per file version)."""
     path = _resolve(Path(weights_dir), b.file, b.name)
-    try:
-        st = path.stat()
-    except FileNotFoundError as exc:
-        raise FileNotFoundError(f"missing bundle binary: {path}") from exc
+    if not path.is_file():
+        raise FileNotFoundError(f"bundle {b.name}: no file at {path}")
+    st = path.stat()
     if st.st_size != b.size_bytes:
-        raise ValueError(f"size_bytes mismatch for {b.name}: file has {st.st_size}, manifest has {b.size_bytes}")
-    key = (str(path), st.st_size, st.st_mtime_ns)
-    digest = _SHA_CACHE.get(key)
-    if digest is None:
-        h = hashlib.sha256()
-        with path.open("rb") as f:
-            for block in iter(lambda: f.read(1 << 20), b""):
-                h.update(block)
-        digest = h.hexdigest()
-    if digest != b.sha256:
-        raise ValueError(f"sha256 mismatch for {b.name}: {digest} != {b.sha256}")
-    _SHA_CACHE[key] = digest
+        raise ValueError(f"bundle {b.name}: {path.name} holds {st.st_size} bytes, size_bytes says {b.size_bytes}")
+    if _DIGESTS.sha256(path, st) != b.sha256:
+        raise ValueError(f"bundle {b.name}: the sha256 of {path.name} differs from the manifest's")
     return path
 
 

@@ -115,7 +115,7 @@ __device__ __forceinline__ void bf_unit_mac(const uint8_t *U, int j, int go, con
 }
 
 template <int TB, bool F32OUT>
-__global__ void __launch_bounds__(kBfThreads, 1) bfp16_gemv_kernel(BfParams p) {
+__global__ void __launch_bounds__(kBfThreads, 1) rc_bfp16_gemv_kernel(BfParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = lane & 3, go = lane >> 2;           // row quad, group octet
@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(kBfThreads, 1) bfp16_gemv_kernel(BfParams p) {
 
 // Sum of the k-slices' partials in slice order, bias, output.
 template <bool F32OUT>
-__global__ void bfp16_finalize_kernel(BfParams p) {
+__global__ void rc_bfp16_finalize_kernel(BfParams p) {
   const int rows = p.n_tiles * kBfRows;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * p.tokens) return;
@@ -236,15 +236,15 @@ static cudaError_t bf_launch(const rc_ctx *ctx, const BfParams &p, int grid, cud
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(bfp16_gemv_kernel<TB, F32OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfSmem);
+    e = cudaFuncSetAttribute(rc_bfp16_gemv_kernel<TB, F32OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfSmem);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured[dev] = true;
   }
-  bfp16_gemv_kernel<TB, F32OUT><<<grid, kBfThreads, kBfSmem, s>>>(p);
+  rc_bfp16_gemv_kernel<TB, F32OUT><<<grid, kBfThreads, kBfSmem, s>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess || p.slices == 1) return e;
   const int n = p.n_tiles * kBfRows * p.tokens;
-  bfp16_finalize_kernel<F32OUT><<<(n + 255) / 256, 256, 0, s>>>(p);
+  rc_bfp16_finalize_kernel<F32OUT><<<(n + 255) / 256, 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -315,7 +315,7 @@ int bfp16_gemv(rc_ctx *ctx, const rc_weight *w, const uint16_t *x, int ldx, int 
 // here, as the q4nx down kernel does).  Each output is one warp's f32 sum in
 // k-block order, so a slot row does not depend on the grouping or the grid.
 template <int TB, bool BLOCKS>
-__global__ void __launch_bounds__(kBfThreads, 1) bfp16_moe_down_kernel(BfMoeDown p) {
+__global__ void __launch_bounds__(kBfThreads, 1) rc_bfp16_moe_down_kernel(BfMoeDown p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = lane & 3, go = lane >> 2;
@@ -421,12 +421,12 @@ static cudaError_t bf_moe_launch(const rc_ctx *ctx, const BfMoeDown &d, int grid
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(bfp16_moe_down_kernel<TB, BLOCKS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(rc_bfp16_moe_down_kernel<TB, BLOCKS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kBfSmem);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured[dev] = true;
   }
-  bfp16_moe_down_kernel<TB, BLOCKS><<<grid, kBfThreads, kBfSmem, s>>>(d);
+  rc_bfp16_moe_down_kernel<TB, BLOCKS><<<grid, kBfThreads, kBfSmem, s>>>(d);
   return cudaGetLastError();
 }
 

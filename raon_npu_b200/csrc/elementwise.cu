@@ -6,7 +6,7 @@
 namespace rc {
 
 // out = RTNE(f32(a) + f32(b)), 8 bf16 per thread.
-__global__ void add_bf16_kernel(const uint16_t *a, const uint16_t *b, uint16_t *out, long long n) {
+__global__ void rc_add_bf16_kernel(const uint16_t *a, const uint16_t *b, uint16_t *out, long long n) {
   pdl_launch_dependents();
   pdl_wait_prior();
   const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
@@ -31,7 +31,7 @@ __global__ void add_bf16_kernel(const uint16_t *a, const uint16_t *b, uint16_t *
 // CTA per row.
 constexpr int kRmsThreads = 256;
 
-__global__ void __launch_bounds__(kRmsThreads) add_rms_bf16_kernel(const uint16_t *a, const uint16_t *b, uint16_t *out,
+__global__ void __launch_bounds__(kRmsThreads) rc_add_rms_bf16_kernel(const uint16_t *a, const uint16_t *b, uint16_t *out,
                                                                    int n, float eps) {
   pdl_launch_dependents();
   pdl_wait_prior();
@@ -73,7 +73,7 @@ extern "C" int rc_add_rms_bf16(rc_ctx *ctx, const uint16_t *a_dev, const uint16_
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, add_rms_bf16_kernel, a_dev, b_dev, out_dev, n, eps));
+  RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, rc_add_rms_bf16_kernel, a_dev, b_dev, out_dev, n, eps));
   return RC_OK;
 }
 
@@ -95,6 +95,6 @@ extern "C" int rc_add_bf16(rc_ctx *ctx, const uint16_t *a_dev, const uint16_t *b
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, add_bf16_kernel, a_dev, b_dev, out_dev, n));
+  RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, rc_add_bf16_kernel, a_dev, b_dev, out_dev, n));
   return RC_OK;
 }

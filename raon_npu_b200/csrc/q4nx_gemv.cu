@@ -84,7 +84,7 @@ struct GemvParams {
 };
 
 // Large-K path: the activations go to global scratch in the same layout.
-__global__ void gemv_prep_kernel(GemvParams p, int ntb, uint32_t *xfrag, void *aux) {
+__global__ void rc_gemv_prep_kernel(GemvParams p, int ntb, uint32_t *xfrag, void *aux) {
   pdl_launch_dependents();
   pdl_wait_prior();
   build_activations<false>(p, ntb, xfrag, aux, blockIdx.x * (long long)blockDim.x + threadIdx.x,
@@ -411,7 +411,7 @@ __device__ __forceinline__ void gemv_rounds(const GemvParams &p, uint8_t *smem) 
 }
 
 template <int NTB, int EPI, bool STAGED>
-__global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(GemvParams p) {
+__global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) rc_q4nx_gemv_kernel(GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   if (p.mode == kPartTiles) {
     gemv_rounds<NTB, EPI, STAGED>(p, smem);
@@ -565,7 +565,7 @@ static cudaError_t launch_main(const GemvParams &p, int grid, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(gemv_kernel<NTB, EPI, STAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(rc_q4nx_gemv_kernel<NTB, EPI, STAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kGemvSmemLimit);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
@@ -574,7 +574,7 @@ static cudaError_t launch_main(const GemvParams &p, int grid, cudaStream_t s) {
   cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(p.warps * 32),
                                       gemv_smem_bytes(NTB, p.kb * kUnitK, STAGED, p.stages, p.warps, p.round_tiles),
                                       s, attr);
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<NTB, EPI, STAGED>, p);
+  return cudaLaunchKernelEx(&cfg, rc_q4nx_gemv_kernel<NTB, EPI, STAGED>, p);
 }
 
 template <int NTB, bool STAGED>
@@ -689,7 +689,7 @@ int gemv_launch(rc_ctx *ctx, const uint8_t *tiles, int n_tiles, int k, const voi
     if (pg > ctx->sm_count) pg = ctx->sm_count;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)pg), dim3(256), 0, s, attr);
-    e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel, p, ntb, const_cast<uint32_t *>(p.xfrag),
+    e = cudaLaunchKernelEx(&cfg, rc_gemv_prep_kernel, p, ntb, const_cast<uint32_t *>(p.xfrag),
                            const_cast<void *>(p.aux));
     if (e != cudaSuccess) {
       set_error("gemv prep launch: %s", cudaGetErrorString(e));

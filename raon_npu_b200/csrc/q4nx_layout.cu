@@ -39,7 +39,7 @@ __device__ __forceinline__ uint32_t ref_scale_min(const RefLayout &L, int n, int
 }
 
 // One thread per 32-bit word of the t16 layout (640 words per unit).
-__global__ void repack_kernel(RefLayout L, uint32_t *dst, long long units, int inter) {
+__global__ void rc_repack_kernel(RefLayout L, uint32_t *dst, long long units, int inter) {
   const long long words = units * (kUnitBytes / 4);
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < words;
        idx += (long long)gridDim.x * blockDim.x) {
@@ -74,7 +74,7 @@ __global__ void repack_kernel(RefLayout L, uint32_t *dst, long long units, int i
 }
 
 // f32(f64(min) + f64(scale) * code), written in logical row order.
-__global__ void dequant_kernel(const uint32_t *tiles, float *out, int n_rows, int k, int inter) {
+__global__ void rc_dequant_kernel(const uint32_t *tiles, float *out, int n_rows, int k, int inter) {
   const int kb = k / kUnitK;
   const long long total = (long long)n_rows * k;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
@@ -140,7 +140,7 @@ __device__ __forceinline__ float bf16_next_up(float f) {
 // bytes of pack_gemv (even row = low nibble).  Mirrors quant/q4nx.py:127-200
 // with every f64 step an explicitly rounded IEEE operation, so codes, scales
 // and mins are bit-identical to the reference's numpy quantiser.
-__global__ void quantize_pack_kernel(const float *w, int n, int k, uint8_t *out, int *flag) {
+__global__ void rc_quantize_pack_kernel(const float *w, int n, int k, uint8_t *out, int *flag) {
   const int groups = k / 32, kb = k / kUnitK;
   const long long work = (long long)(n / 2) * groups;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < work;
@@ -241,7 +241,7 @@ int rc_upload_q4nx(rc_ctx *ctx, const uint8_t *packed, size_t nbytes, int n, int
     RefLayout L{src, k / kUnitK};
     const long long units = (long long)(n / kUnitRows) * (k / kUnitK);
     const long long words = units * (kUnitBytes / 4);
-    repack_kernel<<<grid_for(words, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+    rc_repack_kernel<<<grid_for(words, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
         L, reinterpret_cast<uint32_t *>(w->tiles), units, inter);
     e = cudaGetLastError();
   }
@@ -265,7 +265,7 @@ int rc_quantize_q4nx(rc_ctx *ctx, const float *w_dev, int n, int k, uint8_t *pac
   const cudaStream_t s = pick_stream(ctx, stream);
   RC_CUDA_TRY(cudaMemsetAsync(ctx->qflag, 0, sizeof(int), s));
   const long long work = (long long)(n / 2) * (k / 32);
-  quantize_pack_kernel<<<grid_for(work, 128, ctx->sm_count), 128, 0, s>>>(w_dev, n, k, packed_dev, ctx->qflag);
+  rc_quantize_pack_kernel<<<grid_for(work, 128, ctx->sm_count), 128, 0, s>>>(w_dev, n, k, packed_dev, ctx->qflag);
   RC_CUDA_TRY(cudaGetLastError());
   int flag = 0;
   RC_CUDA_TRY(cudaMemcpyAsync(&flag, ctx->qflag, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -331,7 +331,7 @@ int rc_dequant_q4nx(rc_ctx *ctx, const rc_weight *w, float *out_dev, void *strea
   RC_CUDA_TRY(cudaSetDevice(ctx->device));
   const long long total = (long long)w->n * w->k;
   const int inter = (w->flags & RC_UPLOAD_GATE_UP) ? w->n / 2 : 0;
-  dequant_kernel<<<grid_for(total, 256, ctx->sm_count), 256, 0, pick_stream(ctx, stream)>>>(
+  rc_dequant_kernel<<<grid_for(total, 256, ctx->sm_count), 256, 0, pick_stream(ctx, stream)>>>(
       reinterpret_cast<const uint32_t *>(w->tiles), out_dev, w->n, w->k, inter);
   RC_CUDA_TRY(cudaGetLastError());
   return RC_OK;

@@ -65,7 +65,7 @@ constexpr int kRouteSlice = 256;         // router columns per warp step: one 16
 // f32.  Phase 2 (the last CTA to arrive, all threads): top-k by rank counting
 // in the router order (larger first, NaN last, ties by lower index), the
 // routing weights, the ascending-ID slot lists and the group table.
-__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p) {
+__global__ void __launch_bounds__(kRouteThreads) rc_moe_route_kernel(RouteParams p) {
   extern __shared__ __align__(16) uint8_t route_smem[];     // phase 2 arrays
   __shared__ double red[kRouteThreads / 32][kMoeMaxTokens];
   __shared__ uint32_t smask[kMoeMaxExperts + 1];
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
 // Slot lists from caller-supplied top ids / weights [T][k] (the
 // Backend.moe_experts boundary): per token sort ascending by ID, append the
 // shared expert; then the group table.  One warp.
-__global__ void moe_slots_kernel(const int32_t *ids, const float *w, int T, int k, int n_experts, int shared_id,
+__global__ void rc_moe_slots_kernel(const int32_t *ids, const float *w, int T, int k, int n_experts, int shared_id,
                                  MoeOwned own, MoeScratch s) {
   __shared__ uint32_t smask[kMoeMaxExperts + 1];
   __shared__ int sgidx[kMoeMaxExperts + 1];
@@ -316,7 +316,7 @@ struct MoeGemvParams {
 // epilogue.  A tile's result therefore depends on the tile alone, never on
 // the partition, the grid or the other groups of the launch.
 template <int EPI, int NTB>
-__global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvParams p) {
+__global__ void __launch_bounds__(kMoeWarps * 32, 1) rc_moe_gemv_kernel(MoeGemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb = p.kb, k = kb * kUnitK, S = p.stages, R = p.round_tiles;
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_gemv_kernel(MoeGemvPara
 // Shared-expert activations from caller-supplied gate|up rows [T][2*inter]
 // (the grouped boundary): act[g_shared][t][c] = RTNE(act(gu[t][c], gu[t][inter + c]))
 // for c < inter; the pad columns of act stay zero.
-__global__ void moe_shared_act_kernel(const uint16_t *gu, int T, int inter, int inter_pad, const int *n_groups,
+__global__ void rc_moe_shared_act_kernel(const uint16_t *gu, int T, int inter, int inter_pad, const int *n_groups,
                                       int rows_per_group, int act, float gb, float vb, uint16_t *act_out) {
   pdl_launch_dependents();
   pdl_wait_prior();
@@ -498,7 +498,7 @@ __global__ void moe_shared_act_kernel(const uint16_t *gu, int T, int inter, int 
 // columns and fetches all k+1 rows before summing (one memory round trip).
 constexpr int kCombineThreads = 128;
 
-__global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(const uint16_t *down, const float *slot_w,
+__global__ void __launch_bounds__(kCombineThreads) rc_moe_combine_kernel(const uint16_t *down, const float *slot_w,
                                                                         int k, int with_shared, int hidden,
                                                                         uint16_t *out, uint16_t *routed_out,
                                                                         uint16_t *shared_out) {
@@ -577,7 +577,7 @@ static cudaError_t launch_moe_gemv_t(const rc_ctx *ctx, MoeGemvParams p, int max
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(moe_gemv_kernel<EPI, NTB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(rc_moe_gemv_kernel<EPI, NTB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kGemvSmemLimit);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured[dev] = true;
@@ -614,7 +614,7 @@ static cudaError_t launch_moe_gemv_t(const rc_ctx *ctx, MoeGemvParams p, int max
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, moe_gemv_kernel<EPI, NTB>, p);
+  return cudaLaunchKernelEx(&cfg, rc_moe_gemv_kernel<EPI, NTB>, p);
 }
 
 template <int EPI>
@@ -691,7 +691,7 @@ static int moe_run_experts(rc_moe *m, const uint16_t *x, int T, int k, const Moe
   if (g.skip_last_group) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = small_cfg(dim3((m->inter + 255) / 256, T), dim3(256), s, attr);
-    e = cudaLaunchKernelEx(&cfg, moe_shared_act_kernel, shared_gu, T, m->inter, m->inter_pad,
+    e = cudaLaunchKernelEx(&cfg, rc_moe_shared_act_kernel, shared_gu, T, m->inter, m->inter_pad,
                            (const int *)m->s.n_groups, 8 * ntb, act, gb, vb, m->act);
     if (e != cudaSuccess) {
       set_error("moe shared activation launch: %s", cudaGetErrorString(e));
@@ -745,7 +745,7 @@ static int moe_combine(rc_moe *m, const uint16_t *down, const float *slot_w, int
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = small_cfg(dim3((m->hidden / 8 + kCombineThreads - 1) / kCombineThreads, T),
                                      dim3(kCombineThreads), s, attr);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_combine_kernel, down, slot_w, k, with_shared, m->hidden, out,
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, rc_moe_combine_kernel, down, slot_w, k, with_shared, m->hidden, out,
                                            routed_out, shared_out);
   if (e != cudaSuccess) {
     set_error("moe combine launch: %s", cudaGetErrorString(e));
@@ -778,7 +778,7 @@ static int moe_route(rc_moe *m, const uint16_t *x, int T, int k, int mode, int r
   if (e == cudaSuccess && (dev >= 64 || !configured[dev])) {
     constexpr int kPhase2Max = kMoeMaxTokens * kMoeMaxExperts * 12 + kMoeMaxTokens * kMoeMaxK * 8 +
                                kMoeMaxTokens * (kMoeMaxK + 1) * 4;
-    e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPhase2Max);
+    e = cudaFuncSetAttribute(rc_moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPhase2Max);
     if (e == cudaSuccess && dev < 64) configured[dev] = true;
   }
   if (e != cudaSuccess) {
@@ -789,7 +789,7 @@ static int moe_route(rc_moe *m, const uint16_t *x, int T, int k, int mode, int r
   cudaLaunchConfig_t cfg = small_cfg(dim3(m->n_experts), dim3(kRouteThreads), s, attr);
   const size_t need = (size_t)T * m->n_experts * 12 + (size_t)T * k * 8 + (size_t)T * (k + 1) * 4;
   cfg.dynamicSmemBytes = (need + 15) / 16 * 16;
-  e = cudaLaunchKernelEx(&cfg, moe_route_kernel, r);
+  e = cudaLaunchKernelEx(&cfg, rc_moe_route_kernel, r);
   if (e != cudaSuccess) {
     set_error("moe router launch: %s", cudaGetErrorString(e));
     return RC_ERR_CUDA;
@@ -801,7 +801,7 @@ static int moe_slots(rc_moe *m, const int32_t *ids, const float *w, int T, int k
                      cudaStream_t s) {
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = small_cfg(dim3(1), dim3(32), s, attr);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_slots_kernel, ids, w, T, k, m->n_experts,
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, rc_moe_slots_kernel, ids, w, T, k, m->n_experts,
                                            m->has_shared ? m->n_experts : -1, own, m->s);
   if (e != cudaSuccess) {
     set_error("moe slot list launch: %s", cudaGetErrorString(e));
@@ -1062,10 +1062,36 @@ int rc_moe_experts_grouped(rc_moe *m, const uint16_t *x_dev, int T, const int32_
                            int k, const uint16_t *shared_gu_dev, int act, float gate_beta, float value_beta,
                            uint16_t *routed_out_dev, uint16_t *shared_out_dev, void *stream) {
   RC_CHECK_ARG(m && x_dev && ids_dev && w_dev && routed_out_dev, "rc_moe_experts_grouped: NULL argument");
-  RC_MOE_CHECK_TK("rc_moe_experts_grouped");
   RC_CHECK_ARG(act == RC_ACT_SWIGLU || act == RC_ACT_SITU, "unknown activation %d", act);
   RC_CHECK_ARG(!shared_gu_dev || (shared_out_dev && m->has_shared && m->down[m->n_experts]),
                "shared_gu needs shared_out and a loaded shared expert");
+  if (T > kMoeMaxTokens) {
+    // Prefill-sized call: the routed experts of all T tokens in one pass of
+    // the prefill kernels (a token's bytes equal the decode path's), then the
+    // shared expert's down rows in 16-token chunks of the decode kernels with
+    // no routed expert in the computed range.
+    int rc = rc_moe_prefill_experts(m, x_dev, T, ids_dev, w_dev, k, act, gate_beta, value_beta, 0, routed_out_dev,
+                                    stream);
+    if (rc || !shared_gu_dev) return rc;
+    RC_CHECK_ARG((reinterpret_cast<uintptr_t>(shared_gu_dev) & 15) == 0 && (m->inter * 4) % 16 == 0,
+                 "shared_gu rows must be 16-byte aligned");
+    const cudaStream_t s = pick_stream(m->ctx, stream);
+    for (int t0 = 0; t0 < T; t0 += kMoeMaxTokens) {
+      const int tn = T - t0 < kMoeMaxTokens ? T - t0 : kMoeMaxTokens;
+      MoeOwned own;
+      own.lo = own.hi = 0;
+      own.shared_mask = token_mask(0, tn);
+      if ((rc = moe_slots(m, ids_dev + (size_t)t0 * k, w_dev + (size_t)t0 * k, tn, k, own, s))) return rc;
+      if ((rc = moe_run_experts(m, x_dev + (size_t)t0 * m->hidden, tn, k, own, act, gate_beta, value_beta,
+                                shared_gu_dev + (size_t)t0 * 2 * m->inter, m->down_out, false, s)))
+        return rc;
+      if ((rc = moe_combine(m, m->down_out, m->s.slot_w, tn, k, 0, nullptr, nullptr,
+                            shared_out_dev + (size_t)t0 * m->hidden, s)))
+        return rc;
+    }
+    return RC_OK;
+  }
+  RC_MOE_CHECK_TK("rc_moe_experts_grouped");
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   const cudaStream_t s = pick_stream(m->ctx, stream);
   const MoeOwned own = all_owned(m, T, shared_gu_dev != nullptr);

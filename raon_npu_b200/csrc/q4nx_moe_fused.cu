@@ -373,7 +373,7 @@ __device__ void fz_phase(const MoeFusedParams &p, uint8_t *smem, const FzRange *
 }
 
 template <int NTB>
-__global__ void __launch_bounds__(kFzThreads, 1) moe_fused_kernel(MoeFusedParams p) {
+__global__ void __launch_bounds__(kFzThreads, 1) rc_moe_fused_kernel(MoeFusedParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   int *ok_s = reinterpret_cast<int *>(smem + p.off_red + kFzWarps * kMoeMaxTokens * 8);
   uint8_t **ep_peer_s = reinterpret_cast<uint8_t **>(smem + p.off_red + kFzRedBytes);
@@ -868,10 +868,10 @@ int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int
   RC_CUDA_TRY(cudaGetDevice(&dev));
   if (dev >= 64 || !configured[dev][ntb - 1]) {
     if (ntb == 1)
-      RC_CUDA_TRY(cudaFuncSetAttribute(moe_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      RC_CUDA_TRY(cudaFuncSetAttribute(rc_moe_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kGemvSmemLimit));
     else
-      RC_CUDA_TRY(cudaFuncSetAttribute(moe_fused_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      RC_CUDA_TRY(cudaFuncSetAttribute(rc_moe_fused_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kGemvSmemLimit));
     if (dev < 64) configured[dev][ntb - 1] = true;
   }
@@ -886,9 +886,9 @@ int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (ntb == 1)
-    RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_fused_kernel<1>, p));
+    RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, rc_moe_fused_kernel<1>, p));
   else
-    RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_fused_kernel<2>, p));
+    RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, rc_moe_fused_kernel<2>, p));
   return RC_OK;
 }
 

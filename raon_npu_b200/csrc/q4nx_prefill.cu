@@ -134,7 +134,7 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // columns per 256-column step, one f64 accumulator per expert.
 constexpr int kPfLogitExperts = 8, kPfLogitTokens = 32;
 
-__global__ void __launch_bounds__(256) pf_logits_kernel(const uint16_t *x, int T, int hidden, const uint16_t *wr,
+__global__ void __launch_bounds__(256) rc_pf_logits_kernel(const uint16_t *x, int T, int hidden, const uint16_t *wr,
                                                         int E, float *logits) {
   extern __shared__ __align__(16) uint8_t pf_logit_smem[];
   uint4 *w_s = reinterpret_cast<uint4 *>(pf_logit_smem);    // [8][hidden/8]
@@ -197,7 +197,7 @@ struct PfSelectParams {
 
 // One warp per token: k rounds of warp argmax (lower index wins ties), the
 // routing weights, the ascending-ID slot list.
-__global__ void __launch_bounds__(256) pf_select_kernel(PfSelectParams p) {
+__global__ void __launch_bounds__(256) rc_pf_select_kernel(PfSelectParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= p.T) return;
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(256) pf_select_kernel(PfSelectParams p) {
 }
 
 // Caller-supplied routes ids / w [T][k]: ascending-ID slot lists.
-__global__ void pf_slots_kernel(const int32_t *ids, const float *w, int T, int k, int shared_id, int32_t *slot_expert,
+__global__ void rc_pf_slots_kernel(const int32_t *ids, const float *w, int T, int k, int shared_id, int32_t *slot_expert,
                                 float *slot_w) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
@@ -313,7 +313,7 @@ struct PfPlanParams {
 // One CTA.  Permuted rows are ordered by expert, then token: the row of
 // (token t, expert e) is off[e] + #{t' < t choosing e}, counted with
 // per-expert token bitmaps -- deterministic, independent of thread timing.
-__global__ void __launch_bounds__(1024) pf_plan_kernel(PfPlanParams p) {
+__global__ void __launch_bounds__(1024) rc_pf_plan_kernel(PfPlanParams p) {
   extern __shared__ uint32_t pf_plan_smem[];
   const int nw = (p.T + 31) / 32;
   uint32_t *mask = pf_plan_smem;                 // [E1][nw]
@@ -438,7 +438,7 @@ struct PfGemmParams {
 };
 
 template <int EPI>
-__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) {
+__global__ void __launch_bounds__(kPfThreads, 1) rc_pf_gemm_kernel(PfGemmParams p) {
   extern __shared__ uint8_t pf_raw_smem[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(pf_raw_smem) + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -700,7 +700,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfGemmParams p) 
 // b; rows past the block's count zero), one warp per (slot, 256-column
 // block).  Gate/up: row t of block b is x[row_token[row0 + t]]; down:
 // act[row0 + t].
-__global__ void __launch_bounds__(256) pf_stage_blocks_kernel(const uint16_t *src, int K, const int32_t *row_token,
+__global__ void __launch_bounds__(256) rc_pf_stage_blocks_kernel(const uint16_t *src, int K, const int32_t *row_token,
                                                               const int32_t *n_blocks, const int32_t *blk_row0,
                                                               const int32_t *blk_n, int blk_cap, uint32_t *xf,
                                                               void *aux) {
@@ -734,7 +734,7 @@ struct PfGemvParams {
   const uint8_t *const *expert_tiles;   // [E+1] t16 tiles (null: not loaded)
   int kb, tiles;                        // k-blocks; 16-row tiles of an expert's matrix
   const int32_t *n_blocks, *blk_expert, *blk_row0, *blk_n;
-  const uint32_t *xf;                   // staged blocks (pf_stage_blocks_kernel)
+  const uint32_t *xf;                   // staged blocks (rc_pf_stage_blocks_kernel)
   const void *xaux;
   int blk_cap;
   uint16_t *y;                          // gate/up: act [P][ld_y]; down: down [P][ld_y]
@@ -750,7 +750,7 @@ constexpr int kPgPartBytes = 48 * 1024;
 // (block, 16-row tile) list; each warp streams its units (k-block-major
 // within a round, RoundCursor) through a ring of bulk copies.
 template <int EPI>
-__global__ void __launch_bounds__(kPgThreads, 1) pf_gemv_kernel(PfGemvParams p) {
+__global__ void __launch_bounds__(kPgThreads, 1) rc_pf_gemv_kernel(PfGemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, qd = lane & 3;
   const int S = p.stages, KB = p.kb, R = p.round;
@@ -864,7 +864,7 @@ __global__ void __launch_bounds__(kPgThreads, 1) pf_gemv_kernel(PfGemvParams p) 
 // f32(down[row]) * w), then RTNE(f32(routed) + f32(shared row)).
 constexpr int kPfCombineThreads = 128;
 
-__global__ void __launch_bounds__(kPfCombineThreads) pf_combine_kernel(const uint16_t *down, const int32_t *slot_row,
+__global__ void __launch_bounds__(kPfCombineThreads) rc_pf_combine_kernel(const uint16_t *down, const int32_t *slot_row,
                                                                          const float *slot_w, int k, int with_shared,
                                                                          int hidden, uint16_t *out) {
   const int t = blockIdx.y;
@@ -915,7 +915,7 @@ __global__ void __launch_bounds__(kPfCombineThreads) pf_combine_kernel(const uin
 
 // Expert-parallel slot rows: slot_out[t][r] = down[slot_row[t][r]], or zeros
 // where the slot is computed on another rank.
-__global__ void pf_slot_rows_kernel(const uint16_t *down, const int32_t *slot_row, int hidden, uint16_t *slot_out) {
+__global__ void rc_pf_slot_rows_kernel(const uint16_t *down, const int32_t *slot_row, int hidden, uint16_t *slot_out) {
   const int i = blockIdx.x;                       // (token, slot)
   const int row = slot_row[i];
   for (int v = threadIdx.x; v * 8 < hidden; v += blockDim.x) {
@@ -925,7 +925,7 @@ __global__ void pf_slot_rows_kernel(const uint16_t *down, const int32_t *slot_ro
   }
 }
 
-__global__ void pf_identity_rows_kernel(int32_t *rows, int n) {
+__global__ void rc_pf_identity_rows_kernel(int32_t *rows, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) rows[i] = i;
 }
@@ -1013,13 +1013,13 @@ static cudaError_t pf_launch_gemm(const rc_ctx *ctx, const PfGemmParams &p, cuda
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(pf_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemAlloc);
+    e = cudaFuncSetAttribute(rc_pf_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemAlloc);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured[dev] = true;
   }
   // No programmatic overlap: a CTA of the next kernel must never sit on an SM
   // waiting for this grid while holding what this grid needs (tensor memory).
-  pf_gemm_kernel<EPI><<<ctx->sm_count, kPfThreads, kPfSmemAlloc, s>>>(p);
+  rc_pf_gemm_kernel<EPI><<<ctx->sm_count, kPfThreads, kPfSmemAlloc, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -1030,11 +1030,11 @@ static cudaError_t pf_launch_gemv(const rc_ctx *ctx, const PfGemvParams &p, size
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(pf_gemv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemLimit);
+    e = cudaFuncSetAttribute(rc_pf_gemv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemLimit);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured[dev] = true;
   }
-  pf_gemv_kernel<EPI><<<ctx->sm_count, kPgThreads, smem, s>>>(p);
+  rc_pf_gemv_kernel<EPI><<<ctx->sm_count, kPgThreads, smem, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -1068,7 +1068,7 @@ static int pf_experts_gemv(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStr
   g.stages = kStages;
   g.round = kPgPartBytes / (g.kb * 32 * 16);
   g.err = m->ctx->err;
-  pf_stage_blocks_kernel<<<m->ctx->sm_count * 4, 256, 0, s>>>(x, m->hidden, ps->row_token, g.n_blocks, ps->blk_row0,
+  rc_pf_stage_blocks_kernel<<<m->ctx->sm_count * 4, 256, 0, s>>>(x, m->hidden, ps->row_token, g.n_blocks, ps->blk_row0,
                                                                ps->blk_n, ps->blk_cap, ps->xf, ps->xaux);
   RC_CUDA_TRY(cudaGetLastError());
   if (r.act == RC_ACT_SITU)
@@ -1100,7 +1100,7 @@ static int pf_experts_gemv(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStr
   d.y = ps->down;
   d.ld_y = m->hidden;
   d.round = kPgPartBytes / (d.kb * 32 * 16);
-  pf_stage_blocks_kernel<<<m->ctx->sm_count * 4, 256, 0, s>>>(ps->act, m->inter_pad, nullptr, d.n_blocks,
+  rc_pf_stage_blocks_kernel<<<m->ctx->sm_count * 4, 256, 0, s>>>(ps->act, m->inter_pad, nullptr, d.n_blocks,
                                                                ps->blk_row0, ps->blk_n, ps->blk_cap, ps->xf, ps->xaux);
   RC_CUDA_TRY(cudaGetLastError());
   RC_CUDA_TRY(pf_launch_gemv<kPfEpiDown>(m->ctx, d, smem, s));
@@ -1141,10 +1141,10 @@ static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t
   int dev = 0;
   RC_CUDA_TRY(cudaGetDevice(&dev));
   if (dev >= 64 || !configured[dev]) {
-    RC_CUDA_TRY(cudaFuncSetAttribute(pf_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfPlanSmemMax));
+    RC_CUDA_TRY(cudaFuncSetAttribute(rc_pf_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfPlanSmemMax));
     if (dev < 64) configured[dev] = true;
   }
-  pf_plan_kernel<<<1, 1024, plan_smem, s>>>(pp);
+  rc_pf_plan_kernel<<<1, 1024, plan_smem, s>>>(pp);
   RC_CUDA_TRY(cudaGetLastError());
 
   // bfp16ebs8 down matrices: the register-fragment path's blocks feed the bfp16 grouped down kernel
@@ -1192,11 +1192,11 @@ static int pf_route(rc_moe *m, const uint16_t *x, int T, int k, int router, int 
   int dev = 0;
   RC_CUDA_TRY(cudaGetDevice(&dev));
   if (dev >= 64 || !configured[dev]) {
-    RC_CUDA_TRY(cudaFuncSetAttribute(pf_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemLimit));
+    RC_CUDA_TRY(cudaFuncSetAttribute(rc_pf_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemLimit));
     if (dev < 64) configured[dev] = true;
   }
   RC_CHECK_ARG(lsm <= (size_t)kGemvSmemLimit, "hidden %d too large for the prefill router", m->hidden);
-  pf_logits_kernel<<<dim3((E + kPfLogitExperts - 1) / kPfLogitExperts, (T + kPfLogitTokens - 1) / kPfLogitTokens),
+  rc_pf_logits_kernel<<<dim3((E + kPfLogitExperts - 1) / kPfLogitExperts, (T + kPfLogitTokens - 1) / kPfLogitTokens),
                      256, lsm, s>>>(x, T, m->hidden, m->router_w, E, ps->logits);
   RC_CUDA_TRY(cudaGetLastError());
   PfSelectParams sp{};
@@ -1213,7 +1213,7 @@ static int pf_route(rc_moe *m, const uint16_t *x, int T, int k, int router, int 
   sp.weights = ps->weights;
   sp.slot_expert = ps->slot_expert;
   sp.slot_w = ps->slot_w;
-  pf_select_kernel<<<(T + 7) / 8, 256, 0, s>>>(sp);
+  rc_pf_select_kernel<<<(T + 7) / 8, 256, 0, s>>>(sp);
   RC_CUDA_TRY(cudaGetLastError());
   return RC_OK;
 }
@@ -1276,7 +1276,7 @@ int rc_moe_prefill(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, i
   if ((rc = pf_route(m, x_dev, T, k, router, renormalize, scaling, s))) return rc;
   PfRun r{T, k, act, gate_beta, value_beta, 0, m->n_experts, 0, m->has_shared ? T : 0};
   if ((rc = pf_experts(m, x_dev, r, s))) return rc;
-  pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
+  rc_pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
                       s>>>(m->pf->down, m->pf->slot_row, m->pf->slot_w, k, m->has_shared, m->hidden, out_dev);
   RC_CUDA_TRY(cudaGetLastError());
   if (ids_dev) RC_CUDA_TRY(cudaMemcpyAsync(ids_dev, m->pf->ids, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
@@ -1295,14 +1295,14 @@ int rc_moe_prefill_experts(rc_moe *m, const uint16_t *x_dev, int T, const int32_
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   if ((rc = pf_scratch(m, T))) return rc;
   const cudaStream_t s = pick_stream(m->ctx, stream);
-  pf_slots_kernel<<<(T + 127) / 128, 128, 0, s>>>(ids_dev, w_dev, T, k, with_shared ? m->n_experts : -1,
+  rc_pf_slots_kernel<<<(T + 127) / 128, 128, 0, s>>>(ids_dev, w_dev, T, k, with_shared ? m->n_experts : -1,
                                                  m->pf->slot_expert, m->pf->slot_w);
   RC_CUDA_TRY(cudaGetLastError());
   // every routed expert the caller names must be loaded: checked on the device
   // side by a null tile table entry (error word), so no host copy of the ids
   PfRun r{T, k, act, gate_beta, value_beta, 0, m->n_experts, 0, with_shared ? T : 0};
   if ((rc = pf_experts(m, x_dev, r, s))) return rc;
-  pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
+  rc_pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
                       s>>>(m->pf->down, m->pf->slot_row, m->pf->slot_w, k, with_shared, m->hidden, out_dev);
   RC_CUDA_TRY(cudaGetLastError());
   return RC_OK;
@@ -1327,7 +1327,7 @@ int rc_moe_prefill_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int rou
   if ((rc = pf_route(m, x_dev, T, k, router, renormalize, scaling, s))) return rc;
   PfRun r{T, k, act, gate_beta, value_beta, expert_lo, expert_hi, shared_t0, shared_t0 + shared_tn};
   if ((rc = pf_experts(m, x_dev, r, s))) return rc;
-  pf_slot_rows_kernel<<<T * (k + 1), 256, 0, s>>>(m->pf->down, m->pf->slot_row, m->hidden, slot_out_dev);
+  rc_pf_slot_rows_kernel<<<T * (k + 1), 256, 0, s>>>(m->pf->down, m->pf->slot_row, m->hidden, slot_out_dev);
   RC_CUDA_TRY(cudaGetLastError());
   RC_CUDA_TRY(cudaMemcpyAsync(slot_w_dev, m->pf->slot_w, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
   return RC_OK;
@@ -1347,9 +1347,9 @@ int rc_moe_prefill_combine(rc_moe *m, const uint16_t *slot_out_dev, const float 
   if (rc) return rc;
   // identity slot-row table, so that the combine kernel is shared with the
   // single-GPU path
-  pf_identity_rows_kernel<<<(T * (k + 1) + 255) / 256, 256, 0, s>>>(m->pf->slot_row, T * (k + 1));
+  rc_pf_identity_rows_kernel<<<(T * (k + 1) + 255) / 256, 256, 0, s>>>(m->pf->slot_row, T * (k + 1));
   RC_CUDA_TRY(cudaGetLastError());
-  pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
+  rc_pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
                       s>>>(slot_out_dev, m->pf->slot_row, slot_w_dev, k, with_shared, m->hidden, out_dev);
   RC_CUDA_TRY(cudaGetLastError());
   return RC_OK;

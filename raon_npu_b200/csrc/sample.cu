@@ -46,7 +46,7 @@ struct SampleParams {
 // bf16 bits -> order-preserving 16-bit key (larger value -> larger key)
 __device__ __forceinline__ uint32_t bf16_key(uint32_t b) { return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u); }
 
-__global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) {
+__global__ void __launch_bounds__(kSampleThreads) rc_sample_kernel(SampleParams p) {
   __shared__ double c_score[kSampleMaxCand];
   __shared__ int c_idx[kSampleMaxCand];
   __shared__ unsigned hist[256];
@@ -283,7 +283,7 @@ int rc_sample_tokens(rc_ctx *ctx, const uint16_t *logits_dev, int ld, int T, int
   p.out = out_dev;
   p.seen_bits = static_cast<uint32_t *>(ctx->sample_bits);
   p.err = ctx->err;
-  sample_kernel<<<T, kSampleThreads, 0, pick_stream(ctx, stream)>>>(p);
+  rc_sample_kernel<<<T, kSampleThreads, 0, pick_stream(ctx, stream)>>>(p);
   RC_CUDA_TRY(cudaGetLastError());
   return RC_OK;
 }

@@ -202,26 +202,35 @@ class ExpertParallelMoe:
         self.layer.prefill_combine(mine, sw[self.rank * M:(self.rank + 1) * M], k, out, tokens=M,
                                    with_shared=self.layer.has_shared)
 
-    def decode_host(self, x: np.ndarray) -> np.ndarray:
-        """Host entry point: x [M, hidden] bf16 bits -> out [M, hidden] (copies in
-        from pinned memory, decodes, copies out, waits)."""
+    def _host_call(self, x: np.ndarray, run, tag: str) -> np.ndarray:
+        """x [M, hidden] bf16 bits on the host -> run(x_dev, out_dev) -> out on
+        the host: pinned copies in and out around the call, then a wait."""
         import torch
         xs = np.ascontiguousarray(x, dtype=np.uint16)
         M, H = xs.shape
         dev = torch.device("cuda", torch.cuda.current_device())
-        pin_in = self._buf("pin_in", (M, H), torch.int16, torch.device("cpu"))
-        if not pin_in.is_pinned():
-            pin_in = pin_in.pin_memory()
-            self._bufs["pin_in"] = pin_in
-        pin_out = self._buf("pin_out", (M, H), torch.int16, torch.device("cpu"))
-        if not pin_out.is_pinned():
-            pin_out = pin_out.pin_memory()
-            self._bufs["pin_out"] = pin_out
+        pins = []
+        for name in ("in", "out"):
+            pin = self._buf(f"{tag}_pin_{name}", (M, H), torch.int16, torch.device("cpu"))
+            if not pin.is_pinned():
+                pin = pin.pin_memory()
+                self._bufs[f"{tag}_pin_{name}"] = pin
+            pins.append(pin)
+        pin_in, pin_out = pins
         pin_in.numpy()[:] = xs.view(np.int16)
-        xd = self._buf("x_dev", (M, H), torch.int16, dev)
-        od = self._buf("out_dev", (M, H), torch.int16, dev)
+        xd = self._buf(f"{tag}_x_dev", (M, H), torch.int16, dev)
+        od = self._buf(f"{tag}_out_dev", (M, H), torch.int16, dev)
         xd.copy_(pin_in, non_blocking=True)
-        self.decode(xd, od)
+        run(xd, od)
         pin_out.copy_(od, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
         return pin_out.numpy().copy().view(np.uint16)
+
+    def decode_host(self, x: np.ndarray) -> np.ndarray:
+        """Host entry point: x [M, hidden] bf16 bits -> out [M, hidden] (copies in
+        from pinned memory, decodes, copies out, waits)."""
+        return self._host_call(x, self.decode, "dec")
+
+    def prefill_host(self, x: np.ndarray) -> np.ndarray:
+        """``prefill`` on host buffers, as ``decode_host``."""
+        return self._host_call(x, self.prefill, "pf")

@@ -29,3 +29,14 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+def pytest_terminal_summary(terminalreporter):
+    """The largest MoE output errors against the oracle seen in this run."""
+    mod = sys.modules.get("tests.test_moe_gpu")
+    stats = getattr(mod, "PARITY", None)
+    if stats and stats["outputs"]:
+        terminalreporter.write_line(
+            f"MoE parity: {stats['outputs']} bf16 output rows against the oracle; largest RMS relative error "
+            f"{stats['rms_max']:.3e} (bar 2e-3), largest normwise max error {stats['normwise_max']:.3e} "
+            f"(bar 2^-8 = {2.0 ** -8:.3e})")

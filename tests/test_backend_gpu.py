@@ -144,9 +144,10 @@ def test_moe_experts_validation(be):
 
 
 def test_moe_experts_grouped_matches_oracle(be):
-    """moe_experts_grouped for T = 20 tokens (two device calls of <= 16 tokens):
-    routed sums and shared down rows against the oracle; the routed rows equal
-    the per-token moe_experts bytes."""
+    """moe_experts_grouped for T = 20 tokens (more than 16: the routed experts
+    run on the prefill kernels in one call): routed sums and shared down rows
+    against the oracle; the routed rows equal the per-token moe_experts bytes,
+    and both halves equal a 16-token call (decode kernels) byte for byte."""
     d = cases.moe_inputs(hidden=2048, inter=768, experts=16, k=8, tokens=20, seed=65)
     rng = np.random.default_rng(66)
     gu = (rng.standard_normal((2 * 768, 2048)) * 0.02).astype(np.float32)
@@ -164,5 +165,8 @@ def test_moe_experts_grouped_matches_oracle(be):
         assert rms_rel(shared[t], s_ref[t]) <= 2.0 ** -8
     for t in (0, 7, 19):
         np.testing.assert_array_equal(be.moe_experts(5, d["x"][t], d["top_ids"][t], d["top_w"][t]), routed[t])
+    r16, s16 = be.moe_experts_grouped(5, d["x"][:16], d["top_ids"][:16], d["top_w"][:16], shared_gu[:16])
+    np.testing.assert_array_equal(r16, routed[:16])
+    np.testing.assert_array_equal(s16, shared[:16])
     with pytest.raises(ValueError):
         be.moe_experts_grouped(5, d["x"], d["top_ids"], d["top_w"], shared_gu[:, :100])
