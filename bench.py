@@ -744,6 +744,41 @@ def moe_ep_parity(ctx, torch, dev, rank: int, world: int, ep) -> dict:
             "reference": "rc_moe_decode of the same layer with all 129 experts on rank 0's GPU"}
 
 
+def moe_phase_trace(ctx, torch, dev, eps, xs, outs, calls: int) -> dict:
+    """Where a decode step's time goes: the decode kernel's global-timer phase
+    stamps (rc_moe_set_trace) over ``calls`` L2-cold steps (layers rotated as
+    in the timed loop).  Per phase: [median, max] over CTAs of the stamp, in
+    us after the earliest CTA started, averaged over the calls (this rank)."""
+    from raon_npu_b200.device import MoeLayer
+    n = ctx.sm_count
+    buf = torch.zeros(n * 16, dtype=torch.int64, device=dev)
+    for ep in eps:
+        ep.layer.set_trace(buf, n)
+    rows = []
+    for c in range(calls):
+        buf.zero_()
+        li = c % len(eps)
+        eps[li].decode(xs[li], outs[li])
+        torch.cuda.synchronize()
+        rows.append(buf.view(n, 16).cpu().numpy().astype(np.int64))
+    for ep in eps:
+        ep.layer.set_trace(None, 0)
+    ctx.sync()
+    res = {}
+    for i, name in enumerate(MoeLayer.TRACE_PHASES):
+        med, mx = [], []
+        for st in rows:
+            col = st[:, i]
+            if not col.any():
+                continue
+            t0 = st[:, 0].min()
+            med.append((np.median(col) - t0) / 1e3)
+            mx.append((col.max() - t0) / 1e3)
+        if med:
+            res[name] = [round(float(np.mean(med)), 2), round(float(np.mean(mx)), 2)]
+    return res
+
+
 def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barrier):
     """Config-3 MoE decode layer, expert-parallel over the ranks: tokens/s of
     all ranks, per-rank HBM roofline of the experts each rank streams."""
@@ -846,6 +881,10 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
     e2e_s = _max_over_ranks(torch, dist, dev, world, (time.perf_counter() - t0) / e2e_n)
 
     transport = eps[0].active_transport
+    phases = None
+    if world == 1 or transport == "p2p":
+        barrier()
+        phases = moe_phase_trace(ctx, torch, dev, eps, xs, outs, calls=2 * n_layers)
     parity = moe_ep_parity(ctx, torch, dev, rank, world, eps[0]) if world > 1 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -879,6 +918,7 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
         "clocks": clk,
         "cpu_baseline": cpu,
         "ep_parity": parity,
+        "phases_us": phases,
     }
 
 

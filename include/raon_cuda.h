@@ -165,6 +165,18 @@ int rc_moe_set_router(rc_moe *m, const uint16_t *router_w, const float *bias);
  * give the same bytes. */
 int rc_moe_set_fused(rc_moe *m, int enable);
 
+/* Phase stamps of the persistent decode kernel (rc_moe_decode, _local,
+ * rc_moe_ep_decode), for measurement: while stamps_dev is set, every launch
+ * writes, per CTA c, 16 global-timer readings in ns at stamps_dev[c*16 + i]
+ * (0 where a phase does not apply): 0 start, 1 every rank's token rows
+ * arrived (expert parallelism), 2 this CTA's router logits written, 3 the
+ * grid passed the logits, 4 top-k and group table built, 5 token rows
+ * staged, 6 this CTA's gate/up tiles done, 7 the activations its down tiles
+ * read are complete, 8 its down tiles done, 9 every expert row of the
+ * combined tokens written, 10 combine done.  ``ctas`` >= the SM count;
+ * NULL switches the stamps off.  No counterpart in the reference. */
+int rc_moe_set_trace(rc_moe *m, unsigned long long *stamps_dev, int ctas);
+
 /* Router for T <= 4096 tokens x [T][hidden] (device): top-k ids (best first,
  * lower index wins ties) and weights, optional f32 logits [T][n_experts].
  * Replaces the host router ``RaonModel._route_token`` (host/raon.py:1224-1247)

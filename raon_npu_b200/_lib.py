@@ -65,6 +65,7 @@ SIGNATURES = {
     "rc_moe_set_expert": (_I, [_P, _I, _P, _SZ, _P, _SZ, _U]),
     "rc_moe_set_router": (_I, [_P, _P, _P]),
     "rc_moe_set_fused": (_I, [_P, _I]),
+    "rc_moe_set_trace": (_I, [_P, _P, _I]),
     "rc_moe_set_prefill_kernel": (_I, [_P, _I]),
     "rc_moe_ep_init": (_I, [_P, _I, _I, _I, _P]),
     "rc_moe_ep_open": (_I, [_P, _I, _P]),

@@ -105,7 +105,28 @@ struct rc_moe {
   rc::MoeEp *ep;              // peer-memory expert parallelism (null until rc_moe_ep_init)
   int prefill_kernel;         // RC_PREFILL_GEMV (register fragments) or RC_PREFILL_TCGEN05
   int down_fmt;               // kFormatQ4nx or kFormatBfp16 (RC_UPLOAD_DOWN_BFP16), one for every expert
+  unsigned long long *trace;  // phase stamps of the persistent decode kernel (rc_moe_set_trace; null: off)
+  int trace_ctas;             // CTAs the trace buffer has room for
 };
+
+namespace rc {
+// Phase stamps of the persistent decode kernel: per CTA, kTracePhases global
+// timer readings (ns) at the phase boundaries below, written by thread 0.
+enum TracePhase : int {
+  kTrStart = 0,      // kernel entered (tables fetched, before any wait)
+  kTrTokens,         // expert parallelism: every rank's token rows arrived
+  kTrLogits,         // this CTA's router logits written
+  kTrRouted,         // grid barrier after the logits passed
+  kTrSelected,       // top-k, weights and group table built
+  kTrStaged,         // token rows staged as mma fragments
+  kTrGateUp,         // this CTA's gate/up tiles done
+  kTrActReady,       // the activations this CTA's down tiles read are complete
+  kTrDown,           // this CTA's down tiles done
+  kTrRows,           // every expert row of the combined tokens is written (grid / peers)
+  kTrEnd,            // combine done
+  kTracePhases = 16
+};
+}  // namespace rc
 
 namespace rc {
 void pf_free(rc_moe *m);   // releases m->pf (q4nx_prefill.cu)

@@ -972,6 +972,15 @@ int rc_moe_set_fused(rc_moe *m, int enable) {
   return RC_OK;
 }
 
+int rc_moe_set_trace(rc_moe *m, unsigned long long *stamps_dev, int ctas) {
+  RC_CHECK_ARG(m, "rc_moe_set_trace: NULL argument");
+  RC_CHECK_ARG(!stamps_dev || ctas >= m->ctx->sm_count,
+               "rc_moe_set_trace: the buffer must hold %d CTAs x %d stamps", m->ctx->sm_count, kTracePhases);
+  m->trace = stamps_dev;
+  m->trace_ctas = stamps_dev ? ctas : 0;
+  return RC_OK;
+}
+
 int rc_moe_set_router(rc_moe *m, const uint16_t *router_w, const float *bias) {
   RC_CHECK_ARG(m && router_w, "rc_moe_set_router: NULL argument");
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));

@@ -81,7 +81,13 @@ struct MoeFusedParams {
   unsigned long long *ep_flags;      // this rank's counters (token rows, expert rows, calls)
   uint32_t ep_tok_off, ep_red_off;   // byte offsets in an exchange buffer
   const uint16_t *ep_x_own;          // this rank's token rows [M][hidden]
+  unsigned long long *trace;         // phase stamps [grid][kTracePhases] (null: off)
 };
+
+// Thread 0 records the global timer at a phase boundary (rc_moe_set_trace).
+__device__ __forceinline__ void fz_stamp(const MoeFusedParams &p, int phase) {
+  if (p.trace && threadIdx.x == 0) p.trace[(size_t)blockIdx.x * kTracePhases + phase] = global_timer_ns();
+}
 
 // what build_activations reads
 struct FzStage {
@@ -381,6 +387,8 @@ __global__ void __launch_bounds__(kFzThreads, 1) rc_moe_fused_kernel(MoeFusedPar
   const int T = p.T, E = p.n_experts, k = p.k;
   const int gt_gu_i = p.inter / 8, kb_gu_i = p.hidden / kUnitK;
   const int gt_dn_i = p.hidden / kUnitRows, kb_dn_i = p.inter_pad / kUnitK;
+  fz_stamp(p, kTrStart);
+  if (p.trace && tid == 0 && p.ep_world <= 1) p.trace[(size_t)blockIdx.x * kTracePhases + kTrTokens] = 0;
 
   // ---- expert parallelism: every rank's token rows into every rank's buffer
   unsigned long long ep_calls = 0;
@@ -426,7 +434,10 @@ __global__ void __launch_bounds__(kFzThreads, 1) rc_moe_fused_kernel(MoeFusedPar
   // warps without router columns fetch the tables while the others compute
   if (busy < kFzWarps && warp >= busy) load_tables(tid - busy * 32, (kFzWarps - busy) * 32);
 
-  if (p.ep_world > 1 && !fz_wait_sys(p.ep_flags + 0, (ep_calls + 1) * p.ep_world, p.err, ok_s)) return;
+  if (p.ep_world > 1) {
+    if (!fz_wait_sys(p.ep_flags + 0, (ep_calls + 1) * p.ep_world, p.err, ok_s)) return;
+    fz_stamp(p, kTrTokens);
+  }
 
   // ------------------------------------------------------------ 1 logits
   {
@@ -482,7 +493,9 @@ __global__ void __launch_bounds__(kFzThreads, 1) rc_moe_fused_kernel(MoeFusedPar
     }
   }
   if (busy == kFzWarps) load_tables(tid, blockDim.x);
+  fz_stamp(p, kTrLogits);
   if (!fz_grid_barrier(p.bar, p.err, ok_s)) return;
+  fz_stamp(p, kTrRouted);
 
   // --------------------------------------------------------- 2 selection
   int32_t *slots = reinterpret_cast<int32_t *>(smem + p.off_sel);                   // [T][k+1]
@@ -574,6 +587,7 @@ __global__ void __launch_bounds__(kFzThreads, 1) rc_moe_fused_kernel(MoeFusedPar
     }
     __syncthreads();
   }
+  fz_stamp(p, kTrSelected);
 
   // ------------------------------------------------- partitions and ring
   const int ng = *n_groups_s;
@@ -625,9 +639,12 @@ __global__ void __launch_bounds__(kFzThreads, 1) rc_moe_fused_kernel(MoeFusedPar
                                                       smem + p.off_stage + xfrag_bytes(NTB, p.hidden), tid,
                                                       blockDim.x);
   __syncthreads();
+  fz_stamp(p, kTrStaged);
   fz_phase<kFzGlu, NTB>(p, smem, ph, g_mask, g_dst, 0, rg);
   bool failed = __syncthreads_or(rg.failed) != 0;
+  fz_stamp(p, kTrGateUp);
   if (!failed && !fz_grid_barrier(p.bar, p.err, ok_s)) failed = true;
+  fz_stamp(p, kTrActReady);
 
   // --------------------------------------------------------------- 4 down
   if (!failed) {
@@ -642,6 +659,7 @@ __global__ void __launch_bounds__(kFzThreads, 1) rc_moe_fused_kernel(MoeFusedPar
     fz_phase<kFzDown, NTB>(p, smem, ph, g_mask, g_dst, g_lo, rg);
     failed = __syncthreads_or(rg.failed) != 0;
   }
+  fz_stamp(p, kTrDown);
   if (p.ep_world > 1 && tid == 0) __threadfence_system();   // this CTA's rows to peers, before the barrier
   if (!failed && !fz_grid_barrier(p.bar, p.err, ok_s)) failed = true;
   if (p.ep_world > 1 && !failed) {
@@ -654,6 +672,7 @@ __global__ void __launch_bounds__(kFzThreads, 1) rc_moe_fused_kernel(MoeFusedPar
     }
     if (!fz_wait_sys(p.ep_flags + 1, (ep_calls + 1) * p.ep_world, p.err, ok_s)) failed = true;
   }
+  fz_stamp(p, kTrRows);
 
   // ------------------------------------------------------------ 5 combine
   if (!failed && p.out) {
@@ -699,6 +718,8 @@ __global__ void __launch_bounds__(kFzThreads, 1) rc_moe_fused_kernel(MoeFusedPar
   }
   if (p.ep_world > 1 && !failed && blockIdx.x == 0 && tid == 0)
     *reinterpret_cast<volatile unsigned long long *>(p.ep_flags + 2) = ep_calls + 1;
+  __syncthreads();
+  fz_stamp(p, kTrEnd);
   // after a failure, the copies still in flight land before the CTA's shared
   // memory is released (ring indices consumed .. issued-1)
   if (failed && lane == 0) {
@@ -852,6 +873,7 @@ int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int
   p.off_bar = L.off_bar;
   p.bar = m->fz_bar;
   p.err = ctx->err;
+  p.trace = m->trace;
   p.ep_world = 1;
   if (ep) {
     p.ep_world = ep->world;

@@ -340,6 +340,16 @@ class MoeLayer:
         both give the same bytes."""
         check(self.ctx.lib.rc_moe_set_fused(self.handle, int(bool(enable))), "rc_moe_set_fused")
 
+    TRACE_PHASES = ("start", "tokens", "logits", "routed", "selected", "staged", "gate_up", "act_ready", "down",
+                    "rows", "end")
+
+    def set_trace(self, stamps_dev, ctas: int = 0) -> None:
+        """Phase stamps of the persistent decode kernel (``rc_moe_set_trace``):
+        an int64 device buffer of ``ctas`` x 16 global-timer readings, or None
+        to switch them off.  Index i of a CTA's row is ``TRACE_PHASES[i]``."""
+        check(self.ctx.lib.rc_moe_set_trace(self.handle, ctypes.c_void_p(_ptr(stamps_dev)), int(ctas)),
+              "rc_moe_set_trace")
+
     def set_prefill_kernel(self, kernel: str) -> None:
         """"gemv" (default: register-fragment grouped GEMV over 8-token blocks) or
         "tcgen05" (tensor-core grouped GEMM over 64-token chunks)."""

@@ -72,12 +72,13 @@ def rms_rel(got, ref):
 # pytest terminal summary): RMS relative and normwise max relative error.
 PARITY = {"outputs": 0, "rms_max": 0.0, "normwise_max": 0.0}
 # The normwise max error max|y - y_ref| / max|y_ref| of a bf16 output is
-# asserted at one bf16 step (2^-8): the north star's 2e-3 is a bar on f32
-# results, while neighbouring bf16 values at an output's largest elements are
-# 2^-8 = 3.9e-3 apart, so two correct implementations whose last rounding
-# falls either way there already differ by that much.  The observed maximum is
-# reported beside the bar.
-MAX_NORMWISE = 2.0 ** -8
+# asserted at one bf16 step of the largest output (2^-7): the north star's
+# 2e-3 is a bar on f32 results, while neighbouring bf16 values are 2^-8 to
+# 2^-7 of their magnitude apart (3.9e-3 to 7.8e-3), so two correct
+# implementations whose last rounding falls either way at a large output
+# already differ by that much.  The observed maximum is reported beside the
+# bar in the pytest summary.
+MAX_NORMWISE = 2.0 ** -7
 
 
 def assert_bf16_outputs_close(got, ref, magnitude=None, tol=2e-3):
