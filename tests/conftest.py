@@ -37,6 +37,7 @@ def pytest_terminal_summary(terminalreporter):
     stats = getattr(mod, "PARITY", None)
     if stats and stats["outputs"]:
         terminalreporter.write_line(
-            f"MoE parity: {stats['outputs']} bf16 output rows against the oracle; largest RMS relative error "
-            f"{stats['rms_max']:.3e} (bar 2e-3), largest normwise max error {stats['normwise_max']:.3e} "
-            f"(bar 2^-7 = {2.0 ** -7:.3e})")
+            f"MoE parity: {stats['outputs']} bf16 output rows against the oracle; largest row RMS relative "
+            f"error {stats['rms_max']:.3e} (bar {mod.ROW_RMS:g}), largest call RMS {stats['call_rms_max']:.3e} "
+            f"(bar {mod.CALL_RMS:g}), largest normwise max error {stats['normwise_max']:.3e} "
+            f"(bar 2^-6 = {mod.MAX_NORMWISE:.3e})")

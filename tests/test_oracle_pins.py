@@ -237,3 +237,53 @@ def test_sampler_restatement_matches_reference_draws(name):
     got = [sample_token_u(logits, seen, opts["top_k"], opts["top_p"], opts["temperature"],
                           opts["presence_penalty"], np.random.default_rng(gseed + i).random()) for i in range(20)]
     np.testing.assert_array_equal(got, g[f"{name}/tokens"])
+
+
+# ------------------------------------------------- spread of the MoE bar --
+def _moe_layer_rows(x, experts, shared, ids, w, f64_dots: bool):
+    """The oracle's MoE layer (bf16 roundings of gate, up, activation, down;
+    ascending-ID f32 combine; shared expert added) with every GEMV's dot
+    products in f32 (numpy, as NumpyBackend) or in f64 rounded to f32."""
+    def lin(wm, xb):
+        xf = q.bf16_to_f32(xb)
+        y = np.dot(xf.astype(np.float64), wm.T.astype(np.float64)).astype(np.float32) if f64_dots \
+            else np.dot(xf, wm.T)
+        return q.f32_to_bf16(y.astype(np.float32))
+
+    def expert(e, xb):
+        wg, wu, wd = experts[e] if e >= 0 else shared
+        return lin(wd, q.f32_to_bf16(ob.glu(lin(wg, xb), lin(wu, xb), "swiglu")))
+    out = []
+    for t in range(x.shape[0]):
+        acc = np.zeros(x.shape[1], np.float32)
+        for r in np.argsort(ids[t], kind="stable"):
+            acc += q.bf16_to_f32(expert(int(ids[t, r]), x[t])) * np.float32(w[t, r])
+        out.append(ob.moe_token_with_shared(q.f32_to_bf16(acc), expert(-1, x[t])))
+    return np.stack(out)
+
+
+def test_moe_outputs_of_two_summation_orders_differ_within_the_bars():
+    """Two correct restatements of the MoE layer that differ only in the order
+    of the f32 sums (numpy f32 dot products vs f64 ones rounded to f32) give
+    different bf16 outputs -- the bf16 roundings turn 1e-7 differences into
+    one-step flips -- and stay inside the bars the GPU MoE tests apply."""
+    from tests.test_moe_gpu import CALL_RMS, MAX_NORMWISE, ROW_RMS
+    rng = np.random.default_rng(5)
+    H, I, E, k, T = 2048, 768, 16, 8, 24
+
+    def bfw(shape):
+        return q.bf16_to_f32(q.f32_to_bf16((rng.standard_normal(shape) * 0.02).astype(np.float32)))
+    experts = {e: (bfw((I, H)), bfw((I, H)), bfw((H, I))) for e in range(E)}
+    shared = (bfw((I, H)), bfw((I, H)), bfw((H, I)))
+    x = q.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)])
+    w = rng.uniform(0.05, 0.3, (T, k)).astype(np.float32)
+    a = _moe_layer_rows(x, experts, shared, ids, w, f64_dots=False)
+    b = _moe_layer_rows(x, experts, shared, ids, w, f64_dots=True)
+    af, bf = (q.bf16_to_f32(v).astype(np.float64) for v in (a, b))
+    err = np.abs(af - bf)
+    assert (a != b).any()                       # not bit-exact across summation orders
+    row_rms = np.sqrt((err ** 2).mean(axis=1)) / np.sqrt((bf ** 2).mean(axis=1))
+    assert row_rms.max() <= ROW_RMS
+    assert np.sqrt((err ** 2).mean()) / np.sqrt((bf ** 2).mean()) <= CALL_RMS
+    assert (err.max(axis=1) / np.abs(bf).max(axis=1)).max() <= MAX_NORMWISE

@@ -18,7 +18,7 @@ import pytest
 from oracle import backend as ob
 from oracle import q4nx as q
 from tests.golden import cases
-from tests.test_moe_gpu import _config3_layer, _oracle_expert, assert_bf16_outputs_close, rms_rel
+from tests.test_moe_gpu import _config3_layer, _oracle_expert, assert_bf16_outputs_close, assert_call_rms, rms_rel
 
 pytestmark = pytest.mark.gpu
 
@@ -85,10 +85,13 @@ def test_prefill_small_layer_matches_oracle(torch, ctx, kernel):
     torch.cuda.synchronize()
     ctx.sync()
     got = out.cpu().numpy().view(np.uint16)
+    refs = []
     for t in range(37):
         ref, r_ids, mag = _oracle_token(lambda e: d["experts"][e], d["experts"][6], wr, x[t], 3, "situ")
         np.testing.assert_array_equal(ids[t].cpu().numpy(), r_ids)
         assert_bf16_outputs_close(got[t], ref, mag)
+        refs.append(ref)
+    assert_call_rms(got, np.stack(refs))
     layer.close()
 
 
