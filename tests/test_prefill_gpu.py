@@ -2,8 +2,9 @@
 oracle, the decode path and itself.
 
 Bars: routing bit-exact (the decode router's ids); outputs against the oracle
-with the MoE bar of tests/test_moe_gpu.py (per element one bf16 step of each
-accumulated term plus the final rounding, RMS relative error <= 2e-3).
+with the MoE bars of tests/test_moe_gpu.py (per element one bf16 step of each
+accumulated term plus either side's last rounding, row RMS relative error
+<= 4e-3, call RMS <= 2e-3).
 Bit-exact properties: a token's bytes do not depend on the other tokens of
 the call (columns of the tensor-core GEMM do not interact), caller-supplied
 routes reproduce the routed call, and the expert-parallel halves summed over
@@ -140,8 +141,8 @@ def test_prefill_config4_shapes_match_oracle_and_decode(torch, ctx, c4, kernel):
         ref, r_ids, mag = _oracle_token(expert, expert(32), wr, x[t], 8, "swiglu", bias)
         np.testing.assert_array_equal(ids[t].cpu().numpy(), r_ids)
         assert_bf16_outputs_close(got[t], ref, mag)
-    # prefill and decode each stay within 2e-3 RMS of the reference, so they
-    # differ from each other by at most the sum of the two
+    # the tensor-core kernel sums in another order than the decode path:
+    # their rows differ by rounding flips only
     for t in range(T):
         assert rms_rel(got[t], ref_dec[t]) <= 4e-3, t
     if kernel == "gemv":
