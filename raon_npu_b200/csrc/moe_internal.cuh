@@ -139,6 +139,15 @@ int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int
                      float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign, uint16_t *out,
                      int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s,
                      const MoeEpArgs *ep = nullptr);
+bool moe_decode_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own);
+int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling,
+                          int act, float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign,
+                          uint16_t *out, int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s,
+                          const MoeEpArgs *ep = nullptr);
+bool moe_persistent_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own);
+int moe_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling, int act,
+                   float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign, uint16_t *out,
+                   int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s, const MoeEpArgs *ep = nullptr);
 int pf_route_tokens(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
                     int32_t *ids_dev, float *w_dev, float *logits_dev, void *stream);
 }  // namespace rc

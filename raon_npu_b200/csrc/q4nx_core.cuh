@@ -302,6 +302,7 @@ template <int NTB>
 struct XFrag {
   uint4 xa[4], xb[4];                 // NTB == 1
   const uint4 *xv[NTB];               // NTB == 2: the lane's fragments of step 0
+  int step;                           // NTB == 2: uint4 stride from one 4-step group to the next
   bool shared;
   uint4 bm[NTB];
   float2 inv[NTB];
@@ -313,11 +314,11 @@ __device__ __forceinline__ void xfrag_step(const XFrag<NTB> &r, int tb, int s4, 
     xa = r.xa[s4];
     xb = r.xb[s4];
   } else if (r.shared) {
-    xa = r.xv[tb][s4 * 64];
-    xb = r.xv[tb][s4 * 64 + 1];
+    xa = r.xv[tb][s4 * r.step];
+    xb = r.xv[tb][s4 * r.step + 1];
   } else {
-    xa = __ldg(r.xv[tb] + s4 * 64);
-    xb = __ldg(r.xv[tb] + s4 * 64 + 1);
+    xa = __ldg(r.xv[tb] + s4 * r.step);
+    xb = __ldg(r.xv[tb] + s4 * r.step + 1);
   }
 }
 
@@ -331,6 +332,7 @@ __device__ __forceinline__ void load_xfrag(XFrag<NTB> &r, const uint32_t *xf, co
   const uint4 *bm = static_cast<const uint4 *>(aux);
   const float *inv = reinterpret_cast<const float *>(bm + nu * 32);
   r.shared = SHARED;
+  r.step = 64;
 #pragma unroll
   for (int tb = 0; tb < NTB; ++tb) {
     const int blk = tb0 + tb;

@@ -1,0 +1,974 @@
+// The MoE decode layer for T <= 16 tokens as one persistent kernel, laid out
+// for a small instruction footprint: every phase of a layer runs once per
+// launch, so code that is executed once per SM is fetched from L2 on every
+// launch; the kernel therefore keeps one out-of-line body for the unit loop
+// of both expert phases, one for activation staging and compact routing code.
+//
+// One CTA per SM (cooperative launch: every CTA resident), 16 warps:
+//
+//   0 tokens     (expert parallelism) every rank's token rows arrive in this
+//                rank's exchange buffer
+//   1 stage      the token rows become mma B fragments in shared memory,
+//                slot-compact (only the T token columns are stored)
+//   2 logits     CTA c computes the logits of experts c, c + grid, ...
+//                (f64 sums of exact bf16 products, rounded once to f32)
+//   -- grid barrier --
+//   3 selection  one warp per token: k rounds of warp arg-max over router
+//                keys (larger first, NaN last, ties by lower index), the
+//                weights, the ascending-ID slot lists; the CTA builds the group
+//                table (identical everywhere: no barrier after it)
+//   4 gate/up    the CTA's contiguous range of (group, row tile) tiles, units
+//                dealt to the warps k-block-major (RoundCursor), per-unit
+//                partials summed in k-block order, GLU epilogue -> act rows
+//   -- grid barrier --
+//   5 down       the same over the down tiles; act rows of the range's
+//                groups staged slot-compact; slot rows out
+//   -- grid barrier (and, with expert parallelism, every rank's rows) --
+//   6 combine    ascending-ID f32 sum (multiply then add, no FMA), RTNE, plus
+//                the shared row
+//
+// Each warp streams its units through a ring of bulk copies that runs on
+// from its gate/up units into its down units.  The unit arithmetic, the
+// partition rules and the combine are those of the separate kernels in
+// q4nx_moe.cu, so a token's bytes do not depend on which path ran.  Every
+// wait is bounded (1 s): it sets the error word and the kernel unwinds.
+#include "moe_internal.cuh"
+#include "q4nx_core.cuh"
+#include "rc_device.cuh"
+#include "rc_internal.cuh"
+
+namespace rc {
+
+constexpr int kDcWarps = 16;
+constexpr int kDcThreads = kDcWarps * 32;
+constexpr int kDcMaxStages = 6;
+constexpr int kDcChunks = kMoeMaxExperts / 32;   // router values a lane holds per token
+// "red" area: [16 warps][16 tokens] f64 partial logits, the barrier verdict
+// word, then the peer buffer table and the two phase ranges
+constexpr int kDcRedBytes = kDcWarps * kMoeMaxTokens * 8 + 16;
+
+struct DcParams {
+  const uint16_t *x;                 // [T][hidden]
+  int T, hidden, n_experts, k, mode, renorm;
+  float scaling;
+  const uint16_t *wr;                // [E][hidden]
+  const float *bias;                 // [E]
+  int shared_id;
+  MoeOwned own;
+  float *logits;                     // [T][E] scratch
+  int32_t *ids_out;                  // [T][k] rank order (optional)
+  float *w_out;                      // [T][k] (optional)
+  float *slot_w_out;                 // [T][k] ascending-ID order (optional)
+  const uint8_t *const *gu_tiles;    // [E+1]
+  const uint8_t *const *dn_tiles;    // [E+1]
+  int inter, inter_pad;
+  uint16_t *act;                     // [E+1][16][inter_pad]
+  uint16_t *slot_rows;               // [T][k+1][hidden]
+  int zero_foreign;                  // zero the slot rows of experts computed elsewhere
+  uint16_t *out;                     // [T][hidden], null: no combine
+  int act_kind;
+  float gate_beta, value_beta;
+  int stages, round_gu, round_dn;
+  int off_stage, off_part, off_tab, off_sel, off_red, off_bar;
+  unsigned long long *bar;           // grid-barrier arrival count (only grows)
+  int *err;
+  int ep_world, ep_rank, ep_M;
+  uint8_t *const *ep_peer;
+  unsigned long long *ep_flags;
+  uint32_t ep_tok_off, ep_red_off;
+  const uint16_t *ep_x_own;
+  unsigned long long *trace;         // phase stamps [grid][kTracePhases] (null: off)
+};
+
+__device__ __forceinline__ void dc_stamp(const DcParams &p, int phase) {
+  if (p.trace && threadIdx.x == 0) p.trace[(size_t)blockIdx.x * kTracePhases + phase] = global_timer_ns();
+}
+
+// Router order as an unsigned key: larger value -> larger key, -0 equal to
+// +0, NaN (1) below every number, 0 = no candidate.  Equal keys are ordered
+// by lower expert index.
+__device__ __forceinline__ uint32_t dc_route_key(float v) {
+  if (v != v) return 1u;
+  uint32_t b = __float_as_uint(v);
+  if (b == 0x80000000u) b = 0u;
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// The sigmoid routing score, out of line (one copy of the f64 exponential).
+static __device__ __noinline__ float dc_sigmoid(float l) { return __double2float_rn(1.0 / (1.0 + exp(-(double)l))); }
+
+// --------------------------------------------------------- staging ------
+// Slot-compact fragments of a staging area that holds nblk blocks (the token
+// set, or one block per expert group) of Tsl token slots over kb k-blocks:
+//   frag word ((((b*kb + kbi)*4 + s4)*Tsl + t)*4 + q)*8 + (s%4)*2 + j holds
+//     the f16 pair {x'[t][16s+2q+8j], x'[t][16s+2q+8j+1]} of k16-step s of
+//     k-block kbi (the mma B fragment of lane 4g+q for column g = t % 8);
+//   bmin uint4 ((b*kb + kbi)*Tsl + t)*4 + q: bf16 {S'1, S'2, S'3, 0} pairs of
+//     groups 2q, 2q+1 (the min-term fragment);
+//   inv ((b*kb + kbi)*Tsl + t): the block's 2^-s.
+// Values, scales and sums are those of stage_core (q4nx_core.cuh); only the
+// storage is compact (no room for token columns that do not exist).
+__host__ __device__ constexpr size_t dc_stage_bytes(int nblk, int tsl, int kb) {
+  return (size_t)nblk * tsl * kb * (512 + 64 + 4);
+}
+
+// One warp per (block, slot, k-block) task; tasks w0, w0 + nw, ... of
+// nblk * Tsl * kb.  Row of (b, t): src + (b * row_blk + t) * ld.
+static __device__ __noinline__ void dc_stage(const uint16_t *src, int ld, int row_blk, int nblk, int tsl, int kb,
+                                             uint8_t *area, int w0, int nw) {
+  const int lane = threadIdx.x & 31;
+  uint32_t *frag = reinterpret_cast<uint32_t *>(area);
+  uint16_t *bmin16 = reinterpret_cast<uint16_t *>(area + (size_t)nblk * tsl * kb * 512);
+  float *inv = reinterpret_cast<float *>(area + (size_t)nblk * tsl * kb * 576);
+  const int ntask = nblk * tsl * kb;
+  #pragma unroll 1
+  for (int i = w0; i < ntask; i += nw) {
+    const int b = i / (tsl * kb), r = i - b * tsl * kb, t = r / kb, kbi = r - t * kb;
+    const uint4 raw = __ldcg(reinterpret_cast<const uint4 *>(src + ((size_t)b * row_blk + t) * ld +
+                                                               kbi * kUnitK + lane * 8));
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = bf16_lo_f32(w[j]);
+      v[2 * j + 1] = bf16_hi_f32(w[j]);
+    }
+    const int s = block_shift(warp_absmax(v));
+    const float sc = pow2f(s);
+    uint32_t hw[4];
+    float part = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = v[2 * j] * sc, c = v[2 * j + 1] * sc;
+      const __half2 h = __floats2half2_rn(a, c);
+      hw[j] = *reinterpret_cast<const uint32_t *>(&h);
+      part += a;   // a bf16 value times 2^s is exact in f16: sum the exact values
+      part += c;
+    }
+    const size_t u = (size_t)b * kb + kbi;
+    const int st = lane >> 1, jj = lane & 1;
+    uint32_t *fw = frag + (((u * 4 + (st >> 2)) * tsl + t) * 4) * 8 + (st & 3) * 2 + jj;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) fw[q * 8] = hw[q];
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    if ((lane & 3) == 0) {
+      const int gi = lane >> 2;
+      const float sp = part * 5.9604644775390625e-08f;   // S' 2^-24 (exact)
+      const uint16_t s1 = f32_to_bf16_rne(sp);
+      const float r1 = sp - bf16_to_f32(s1);
+      const uint16_t s2 = f32_to_bf16_rne(r1);
+      uint16_t *bw = bmin16 + ((u * tsl + t) * 4 + (gi >> 1)) * 8 + (gi & 1);
+      bw[0] = s1;
+      bw[2] = s2;
+      bw[4] = f32_to_bf16_rne(r1 - bf16_to_f32(s2));
+      bw[6] = 0;
+    }
+    if (lane == 0) inv[u * tsl + t] = pow2f(-s);
+  }
+}
+
+// The lane's fragments of k-block kbi of block blk.  Columns of token slots
+// that do not exist read the last slot's data: mma columns do not interact,
+// and those columns' results are never stored.
+template <int NTB>
+__device__ __forceinline__ void dc_load_frag(XFrag<NTB> &r, const uint8_t *area, int nblk, int tsl, int kb, int blk,
+                                             int kbi, int lane) {
+  const uint4 *frag = reinterpret_cast<const uint4 *>(area);
+  const uint4 *bmin = reinterpret_cast<const uint4 *>(area + (size_t)nblk * tsl * kb * 512);
+  const float *inv = reinterpret_cast<const float *>(area + (size_t)nblk * tsl * kb * 576);
+  const int g = lane >> 2, q = lane & 3;
+  const size_t u = (size_t)blk * kb + kbi;
+  r.shared = true;
+  r.step = 8 * tsl;
+#pragma unroll
+  for (int tb = 0; tb < NTB; ++tb) {
+    const int t = min(tb * 8 + g, tsl - 1);
+    const uint4 *xv = frag + ((u * 4 * tsl + t) * 4 + q) * 2;
+    r.xv[tb] = xv;
+    if (NTB == 1) {
+#pragma unroll
+      for (int s4 = 0; s4 < 4; ++s4) {
+        r.xa[s4] = xv[s4 * r.step];
+        r.xb[s4] = xv[s4 * r.step + 1];
+      }
+    }
+    r.bm[tb] = bmin[(u * tsl + t) * 4 + q];
+    const int t0 = min(tb * 8 + 2 * q, tsl - 1), t1 = min(tb * 8 + 2 * q + 1, tsl - 1);
+    r.inv[tb] = make_float2(inv[u * tsl + t0], inv[u * tsl + t1]);
+  }
+}
+
+// ------------------------------------------------------------ waits -----
+// All CTAs meet (arrival n belongs to barrier n / grid).  Bounded: false after
+// 1 s (error word set), CTA-uniform.
+static __device__ __noinline__ bool dc_grid_barrier(unsigned long long *bar, int *err, int *ok_s) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const unsigned long long old = atom_add_release_gpu(bar, 1ull);
+    const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
+    if (ld_acquire_gpu(bar) < target) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_gpu(bar) < target) {
+        if (global_timer_ns() - t0 > 1000000000ull) {
+          ok = 0;
+          atomicCAS(err, 0, kErrWaitTimeout);
+          break;
+        }
+      }
+    }
+    *ok_s = ok;
+  }
+  __syncthreads();
+  return *ok_s != 0;
+}
+
+// Wait until a counter that peer GPUs add to reaches ``target``.  Bounded.
+static __device__ __noinline__ bool dc_wait_sys(const unsigned long long *ctr, unsigned long long target, int *err,
+                                                int *ok_s) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    if (ld_acquire_sys(ctr) < target) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(ctr) < target) {
+        if (global_timer_ns() - t0 > 1000000000ull) {
+          ok = 0;
+          atomicCAS(err, 0, kErrWaitTimeout);
+          break;
+        }
+      }
+    }
+    *ok_s = ok;
+  }
+  __syncthreads();
+  return *ok_s != 0;
+}
+
+// ------------------------------------------------------ units and rings --
+// One phase's units: tiles [c0, c0 + n_tiles) of the group-major tile list,
+// kb k-blocks each, rounds of R tiles (RoundCursor).
+struct DcRange {
+  const uint8_t *const *g_ptr;       // [groups] tile base of each group (null: not loaded)
+  int c0, n_tiles, R, kb;
+  FastDiv gt;                        // tiles per group
+
+  __device__ __forceinline__ const uint8_t *src(const RoundCursor &c) const {
+    const uint32_t tg = c0 + c.tile();
+    const uint32_t grp = fdiv(tg, gt), tile = tg - grp * gt.d;
+    const uint8_t *b = g_ptr[grp];
+    return b ? b + ((size_t)tile * kb + c.kbi) * kUnitBytes : nullptr;
+  }
+};
+
+// A warp's ring: its gate/up units, then its down units; the issue cursor
+// runs up to S units ahead of consumption, across the phase boundary.
+struct DcRing {
+  RoundCursor iss;
+  int iss_phase;                     // 0 gate/up, 1 down, 2 none left
+  int slot, issued, consumed;
+  uint32_t parity;
+  bool failed;
+};
+
+static __device__ __noinline__ void dc_issue(DcRing &rg, const DcRange *ph, int warp, uint32_t ring_s, uint32_t bar0,
+                                             int sl) {
+  const uint8_t *src = ph[rg.iss_phase].src(rg.iss);
+  if (src) {
+    mbar_arrive_expect_tx(bar0 + 8 * sl, kUnitBytes);
+    bulk_copy_g2s(ring_s + sl * kUnitBytes, src, kUnitBytes, bar0 + 8 * sl, policy_evict_first());
+  } else {
+    mbar_arrive_expect_tx(bar0 + 8 * sl, 0);
+  }
+  ++rg.issued;
+  rg.iss.next();
+  while (rg.iss_phase < 2 && !rg.iss.valid()) {
+    if (++rg.iss_phase < 2) rg.iss.init(ph[1].n_tiles, ph[1].R, ph[1].kb, kDcWarps, warp);
+  }
+}
+
+static __device__ __noinline__ float dc_glu(float gate, float up, int kind, float gb, float vb) {
+  return kind == RC_ACT_SITU ? act_situ(gate, up, gb, vb) : act_swiglu(gate, up);
+}
+
+// One phase (epi 0: gate/up with the GLU epilogue, 1: down) of this CTA.
+// Each unit's result goes to its own shared-memory partial; after a round's
+// barrier one warp per tile sums the tile's partials in k-block order and
+// runs the epilogue, so a tile's result depends on the tile alone.
+template <int NTB>
+static __device__ __noinline__ void dc_phase(const DcParams &p, uint8_t *smem, const DcRange *ph, int epi,
+                                             const uint8_t *stage, int nblk, int tsl, const uint32_t *g_mask,
+                                             const int *g_dst, int g_lo, DcRing &rg) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const DcRange &pr = ph[epi];
+  uint8_t *const *ep_peer_s = reinterpret_cast<uint8_t *const *>(smem + p.off_red + kDcRedBytes);
+  const int S = p.stages;
+  const int kb = pr.kb, R = pr.R, n_tiles = pr.n_tiles;
+  uint8_t *ring = smem + warp * S * kUnitBytes;
+  const uint32_t ring_s = smem_addr(ring);
+  const uint32_t bar0 = smem_addr(smem + p.off_bar) + warp * S * 8;
+  XFrag<NTB> xr;
+  int xr_key = -1;                              // (block, k-block) held in xr
+  float4 *part = reinterpret_cast<float4 *>(smem + p.off_part);
+  const int n_rounds = round_count(n_tiles, R);
+  RoundCursor cur;
+  cur.init(n_tiles, R, kb, kDcWarps, warp);
+  const int g = lane >> 2, qd = lane & 3;
+  for (int r = 0; r < n_rounds; ++r) {
+    for (; cur.valid() && cur.round == r; cur.next()) {
+      const uint32_t grp = fdiv(pr.c0 + cur.tile(), pr.gt);
+      if (!rg.failed) {
+        if (mbar_wait_bounded_warp(bar0 + 8 * rg.slot, rg.parity)) {
+          ++rg.consumed;
+        } else {
+          if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+          rg.failed = true;
+        }
+      }
+      if (!rg.failed && pr.g_ptr[grp] != nullptr) {
+        const int blk = epi == 0 ? 0 : (int)grp - g_lo;
+        if (blk * kb + cur.kbi != xr_key) {
+          dc_load_frag<NTB>(xr, stage, nblk, tsl, kb, blk, cur.kbi, lane);
+          xr_key = blk * kb + cur.kbi;
+        }
+        float4 Q[NTB];
+        unit_result<NTB>(ring + rg.slot * kUnitBytes, xr, lane, Q);
+        float4 *dst = part + (size_t)cur.slot() * NTB * 32 + lane;
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb) dst[tb * 32] = Q[tb];
+      }
+      __syncwarp();
+      if (!rg.failed && lane == 0 && rg.iss_phase < 2) dc_issue(rg, ph, warp, ring_s, bar0, rg.slot);
+      if (++rg.slot == S) rg.slot = 0, rg.parity ^= 1u;
+    }
+    __syncthreads();
+    const int t_lo = r * R, t_hi = t_lo + R < n_tiles ? t_lo + R : n_tiles;
+    for (int ti = t_lo + warp; ti < t_hi; ti += kDcWarps) {
+      const uint32_t tg = pr.c0 + ti;
+      const uint32_t grp = fdiv(tg, pr.gt), tile = tg - grp * pr.gt.d;
+      const bool live = pr.g_ptr[grp] != nullptr;
+      Acc<NTB> acc;
+      acc_zero(acc);
+      const float4 *src = part + (size_t)(ti - t_lo) * kb * NTB * 32 + lane;
+      for (int kbi = 0; kbi < kb; ++kbi) {
+        float4 v[NTB];
+#pragma unroll
+        for (int tb = 0; tb < NTB; ++tb) v[tb] = src[(kbi * NTB + tb) * 32];
+        acc_add(acc, v);
+      }
+      const uint32_t mask = g_mask[grp];
+#pragma unroll
+      for (int tb = 0; tb < NTB; ++tb) {
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2) {
+          const int t = tb * 8 + 2 * qd + e2;
+          if (t >= p.T || !((mask >> t) & 1u)) continue;
+          if (epi == 0) {
+            float v = 0.f;
+            if (live) v = dc_glu(bf16_round(acc.v[tb][e2]), bf16_round(acc.v[tb][2 + e2]), p.act_kind,
+                                 p.gate_beta, p.value_beta);
+            p.act[((size_t)grp * 8 * NTB + t) * p.inter_pad + tile * 8 + g] = f32_to_bf16_rne(v);
+          } else {
+            const int srow = g_dst[grp * p.T + t];     // slot row t*(k+1) + position
+            uint16_t *y;
+            if (p.ep_world > 1) {
+              // straight into the buffer of the token's owner
+              const int tt = srow / (p.k + 1), pos = srow - tt * (p.k + 1);
+              const int owner = tt / p.ep_M, tl = tt - owner * p.ep_M;
+              y = reinterpret_cast<uint16_t *>(ep_peer_s[owner] + p.ep_red_off) +
+                  ((size_t)tl * (p.k + 1) + pos) * p.hidden + tile * kUnitRows + g;
+            } else {
+              y = p.slot_rows + (size_t)srow * p.hidden + tile * kUnitRows + g;
+            }
+            y[0] = live ? f32_to_bf16_rne(acc.v[tb][e2]) : (uint16_t)0;
+            y[8] = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : (uint16_t)0;
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------- routing -----
+// The logits of experts blockIdx.x, + grid, ... for all T tokens: warp w sums
+// the 256-column slices w, w + 16, ... in f64 (exact bf16 products), the CTA
+// adds the warps' sums in warp order and rounds once to f32.
+static __device__ __noinline__ void dc_logits(const DcParams &p, double *red) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = p.T, E = p.n_experts, nslice = p.hidden / kUnitK;
+  #pragma unroll 1
+  for (int e = blockIdx.x; e < E; e += gridDim.x) {
+    #pragma unroll 1
+    for (int t = 0; t < T; ++t) {
+      double acc = 0.0;
+      #pragma unroll 1
+      for (int sl = warp; sl < nslice; sl += kDcWarps) {
+        const int col = sl * kUnitK + lane * 8;
+        const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
+        const uint4 xv = __ldcg(reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.hidden + col));
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), (double)bf16_to_f32(ww[j] & 0xFFFFu), acc);
+          acc = fma((double)bf16_to_f32(xw[j] >> 16), (double)bf16_to_f32(ww[j] >> 16), acc);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) red[warp * kMoeMaxTokens + t] = acc;
+    }
+    __syncthreads();
+    if (tid < T) {
+      double a = 0.0;
+      #pragma unroll 1
+      for (int w = 0; w < kDcWarps; ++w) a += red[w * kMoeMaxTokens + tid];
+      p.logits[(size_t)tid * E + e] = __double2float_rn(a);
+    }
+    __syncthreads();
+  }
+}
+
+// Top-k of token ``warp`` (one warp per token): k rounds of warp-wide arg-max
+// over router keys, then the weights and the ascending-ID slot list.
+static __device__ __noinline__ void dc_select(const DcParams &p, const float *bias_s, int32_t *slots, float *slot_w,
+                                              int32_t *sel_e, float *sel_sc) {
+  const int lane = threadIdx.x & 31, t = threadIdx.x >> 5;
+  const int E = p.n_experts, k = p.k;
+  uint32_t key[kDcChunks];
+  float sc[kDcChunks];
+#pragma unroll
+  for (int c = 0; c < kDcChunks; ++c) {
+    const int e = c * 32 + lane;
+    key[c] = 0u;
+    sc[c] = 0.f;
+    if (e < E) {
+      const float l = __ldcg(p.logits + (size_t)t * E + e);
+      float v;
+      if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
+        sc[c] = dc_sigmoid(l);
+        v = sc[c] + bias_s[e];
+      } else {
+        sc[c] = l + bias_s[e];
+        v = sc[c];
+      }
+      key[c] = dc_route_key(v);
+    }
+  }
+  uint32_t taken = 0;
+  #pragma unroll 1
+  for (int r = 0; r < k; ++r) {
+    uint32_t bk = 0u;
+    int be = 0x7FFFFFFF;
+    float bs = 0.f;
+#pragma unroll
+    for (int c = 0; c < kDcChunks; ++c) {
+      if (!((taken >> c) & 1u) && key[c] > bk) {
+        bk = key[c];
+        be = c * 32 + lane;
+        bs = sc[c];
+      }
+    }
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+    const int emin = (int)__reduce_min_sync(0xffffffffu, bk == kmax ? (unsigned)be : 0x7FFFFFFFu);
+    const float ws = __shfl_sync(0xffffffffu, bs, emin & 31);
+    if ((emin & 31) == lane) taken |= 1u << (emin >> 5);
+    if (lane == 0) {
+      sel_e[t * k + r] = emin;
+      sel_sc[t * k + r] = ws;
+    }
+  }
+  __syncwarp();
+  if (lane < k) {
+    const int r = lane;
+    const float *ss = sel_sc + t * k;
+    float w;
+    if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
+      float sum = 0.f;
+      #pragma unroll 1
+      for (int r2 = 0; r2 < k; ++r2) sum += ss[r2];
+      w = ss[r];
+      if (p.renorm) w = w / (sum + 1e-20f);
+      w = w * p.scaling;
+    } else {
+      // softmax over all experts renormalised over the top-k equals the
+      // softmax of the selected scores (the full denominator cancels)
+      const float mx = ss[0];
+      float sum = 0.f;
+      #pragma unroll 1
+      for (int r2 = 0; r2 < k; ++r2) sum += expf(ss[r2] - mx);
+      w = expf(ss[r] - mx) / sum;
+    }
+    const int e = sel_e[t * k + r];
+    int pos = 0;
+    #pragma unroll 1
+    for (int r2 = 0; r2 < k; ++r2) pos += sel_e[t * k + r2] < e ? 1 : 0;
+    slots[t * (k + 1) + pos] = e;
+    slot_w[t * k + pos] = w;
+    if (blockIdx.x == 0) {
+      if (p.ids_out) p.ids_out[t * k + r] = e;
+      if (p.w_out) p.w_out[t * k + r] = w;
+      if (p.slot_w_out) p.slot_w_out[t * k + pos] = w;
+    }
+  }
+  if (lane == 0) slots[t * (k + 1) + k] = p.shared_id;
+}
+
+// The group table of the ascending-ID slot lists, built by the whole CTA: one
+// group per expert of [own.lo, own.hi) that some token chose, ascending, then
+// the shared expert for the tokens of own.shared_mask; per (group, token) the
+// slot row t*(k+1) + position.
+static __device__ __noinline__ void dc_groups(const int32_t *slots, int T, int k, int E, MoeOwned own,
+                                              int32_t *g_expert, uint32_t *g_mask, int32_t *g_dst, int *n_groups,
+                                              uint32_t *mask_s, int *gidx_s, int *cnt_s, int *err) {
+  const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31;
+  #pragma unroll 1
+  for (int e = tid; e <= E; e += nth) mask_s[e] = e == E ? own.shared_mask : 0u;
+  __syncthreads();
+  #pragma unroll 1
+  for (int pr = tid; pr < T * k; pr += nth) {
+    const int t = pr / k, r = pr - t * k;
+    const int e = slots[t * (k + 1) + r];
+    if (e >= own.lo && e < own.hi) atomicOr(mask_s + e, 1u << t);
+    else if (e < 0 || e >= E) atomicCAS(err, 0, kErrBadExpert);
+  }
+  __syncthreads();
+  const int nchunks = (E + 1 + 31) / 32;      // <= 9 <= warps
+  uint32_t m = 0, b = 0;
+  const int e = warp * 32 + lane;
+  if (warp < nchunks) {
+    m = e <= E ? mask_s[e] : 0u;
+    b = __ballot_sync(0xffffffffu, m != 0u);
+    if (lane == 0) cnt_s[warp] = __popc(b);
+  }
+  __syncthreads();
+  if (warp < nchunks) {
+    int base = 0;
+    #pragma unroll 1
+    for (int c = 0; c < warp; ++c) base += cnt_s[c];
+    if (m) {
+      const int gi = base + __popc(b & ((1u << lane) - 1u));
+      g_expert[gi] = e;
+      g_mask[gi] = m;
+      gidx_s[e] = gi;
+    }
+    if (warp == nchunks - 1 && lane == 0) *n_groups = base + __popc(b);
+  }
+  __syncthreads();
+  #pragma unroll 1
+  for (int pr = tid; pr < T * (k + 1); pr += nth) {
+    const int t = pr / (k + 1), r = pr - t * (k + 1);
+    const int ex = slots[pr];
+    const bool mine = r < k ? (ex >= own.lo && ex < own.hi) : (ex >= 0 && ((own.shared_mask >> t) & 1u));
+    if (mine) g_dst[gidx_s[ex] * T + t] = pr;
+  }
+  __syncthreads();
+}
+
+// ascending-ID f32 combine (product rounded, then sum rounded) of the slot
+// rows of token t, RTNE, then RTNE(routed + shared)
+static __device__ __noinline__ void dc_combine(const DcParams &p, const float *slot_w, const uint16_t *ep_rows) {
+  const int k = p.k, vecs = p.hidden / 8;
+  const bool with_shared = p.shared_id >= 0 && p.own.shared_mask;
+  const bool ep = p.ep_world > 1;
+  const int n_out = ep ? p.ep_M : p.T;
+  #pragma unroll 1
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_out * vecs; i += gridDim.x * blockDim.x) {
+    const int to = i / vecs, v = i - to * vecs;
+    const int t = ep ? p.ep_rank * p.ep_M + to : to;
+    const uint16_t *rows = (ep ? ep_rows + (size_t)to * (k + 1) * p.hidden
+                               : p.slot_rows + (size_t)t * (k + 1) * p.hidden) + (size_t)v * 8;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    #pragma unroll 1
+    for (int s = 0; s < k; ++s) {
+      const uint4 r = __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)s * p.hidden));
+      const float w = slot_w[t * k + s];
+      const uint32_t q[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(bf16_to_f32(q[j] & 0xFFFFu), w));
+        acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(bf16_to_f32(q[j] >> 16), w));
+      }
+    }
+    const uint4 sh = with_shared ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)k * p.hidden))
+                                 : make_uint4(0, 0, 0, 0);
+    const uint32_t shw[4] = {sh.x, sh.y, sh.z, sh.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t lo = f32_to_bf16_rne(acc[2 * j]), hi = f32_to_bf16_rne(acc[2 * j + 1]);
+      if (with_shared) {
+        lo = f32_to_bf16_rne(bf16_to_f32(lo) + bf16_to_f32(shw[j] & 0xFFFFu));
+        hi = f32_to_bf16_rne(bf16_to_f32(hi) + bf16_to_f32(shw[j] >> 16));
+      }
+      o[j] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4 *>(p.out + (size_t)to * p.hidden + (size_t)v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ------------------------------------------------------------- kernel ---
+template <int NTB>
+__global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  int *ok_s = reinterpret_cast<int *>(smem + p.off_red + kDcWarps * kMoeMaxTokens * 8);
+  uint8_t **ep_peer_s = reinterpret_cast<uint8_t **>(smem + p.off_red + kDcRedBytes);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = p.T, E = p.n_experts, k = p.k;
+  const int gt_gu_i = p.inter / 8, kb_gu_i = p.hidden / kUnitK;
+  const int gt_dn_i = p.hidden / kUnitRows, kb_dn_i = p.inter_pad / kUnitK;
+  uint8_t *stage = smem + p.off_stage;
+  dc_stamp(p, kTrStart);
+
+  // ---- expert parallelism: every rank's token rows into every rank's buffer
+  unsigned long long ep_calls = 0;
+  if (p.ep_world > 1) {
+    ep_calls = *reinterpret_cast<volatile unsigned long long *>(p.ep_flags + 2);
+    if (tid < p.ep_world) ep_peer_s[tid] = p.ep_peer[tid];
+    __syncthreads();
+    if (blockIdx.x == 0) {
+      const int n16 = p.ep_M * p.hidden / 8;
+      const uint4 *src = reinterpret_cast<const uint4 *>(p.ep_x_own);
+      for (int r = 0; r < p.ep_world; ++r) {
+        uint4 *dst = reinterpret_cast<uint4 *>(ep_peer_s[r] + p.ep_tok_off) + (size_t)p.ep_rank * n16;
+        for (int i = tid; i < n16; i += blockDim.x) dst[i] = src[i];
+      }
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence_system();
+        for (int r = 0; r < p.ep_world; ++r)
+          red_add_release_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r]) + 0, 1ull);
+      }
+    }
+  }
+
+  // per-expert tables kept in shared memory for the whole kernel
+  const uint8_t **all_gu = reinterpret_cast<const uint8_t **>(smem + p.off_tab);    // [E+1]
+  const uint8_t **all_dn = all_gu + (E + 1);
+  const uint8_t **g_gu = all_dn + (E + 1);
+  const uint8_t **g_dn = g_gu + (E + 1);
+  float *bias_s = reinterpret_cast<float *>(g_dn + (E + 1));
+  int32_t *g_expert = reinterpret_cast<int32_t *>(bias_s + (E + 1));
+  uint32_t *g_mask = reinterpret_cast<uint32_t *>(g_expert + (E + 1));
+  int32_t *g_dst = reinterpret_cast<int32_t *>(g_mask + (E + 1));                   // [E+1][T]
+  int *n_groups_s = g_dst + (E + 1) * T;
+  uint32_t *mask_s = reinterpret_cast<uint32_t *>(n_groups_s + 4);                 // [E+1]
+  int *gidx_s = reinterpret_cast<int *>(mask_s + (E + 1));                         // [E+1]
+  int *cnt_s = gidx_s + (E + 1);                                                   // [9]
+  for (int i = tid; i <= E; i += blockDim.x) {
+    all_gu[i] = p.gu_tiles[i];
+    all_dn[i] = p.dn_tiles[i];
+    bias_s[i] = i < E ? p.bias[i] : 0.f;
+  }
+  if (p.ep_world > 1) {
+    if (!dc_wait_sys(p.ep_flags + 0, (ep_calls + 1) * p.ep_world, p.err, ok_s)) return;
+    dc_stamp(p, kTrTokens);
+  } else if (p.trace && tid == 0) {
+    p.trace[(size_t)blockIdx.x * kTracePhases + kTrTokens] = 0;
+  }
+
+  // ------------------------------------------- 1 stage, 2 logits
+  dc_stage(p.x, p.hidden, 0, 1, T, kb_gu_i, stage, warp, kDcWarps);
+  dc_logits(p, reinterpret_cast<double *>(smem + p.off_red));
+  dc_stamp(p, kTrLogits);
+  if (!dc_grid_barrier(p.bar, p.err, ok_s)) return;
+  dc_stamp(p, kTrRouted);
+
+  // -------------------------------------------------------- 3 selection
+  int32_t *slots = reinterpret_cast<int32_t *>(smem + p.off_sel);                   // [T][k+1]
+  float *slot_w = reinterpret_cast<float *>(slots + T * (k + 1));                   // [T][k]
+  int32_t *sel_e = reinterpret_cast<int32_t *>(slot_w + T * k);                     // [T][k]
+  float *sel_sc = reinterpret_cast<float *>(sel_e + T * k);                         // [T][k]
+  if (warp < T) dc_select(p, bias_s, slots, slot_w, sel_e, sel_sc);
+  __syncthreads();
+  dc_groups(slots, T, k, E, p.own, g_expert, g_mask, g_dst, n_groups_s, mask_s, gidx_s, cnt_s, p.err);
+  for (int i = tid; i < *n_groups_s; i += blockDim.x) {
+    g_gu[i] = all_gu[g_expert[i]];
+    g_dn[i] = all_dn[g_expert[i]];
+  }
+  __syncthreads();
+  dc_stamp(p, kTrSelected);
+
+  // ------------------------------------------- partitions and ring
+  const int ng = *n_groups_s;
+  const int tot_gu = ng * gt_gu_i, tot_dn = ng * gt_dn_i;
+  const int per_gu = (tot_gu + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int per_dn = (tot_dn + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int c0_gu = blockIdx.x * per_gu, c0_dn = blockIdx.x * per_dn;
+  const int nt_gu = c0_gu < tot_gu ? (c0_gu + per_gu < tot_gu ? per_gu : tot_gu - c0_gu) : 0;
+  const int nt_dn = c0_dn < tot_dn ? (c0_dn + per_dn < tot_dn ? per_dn : tot_dn - c0_dn) : 0;
+  const int S = p.stages;
+  const uint32_t bar0 = smem_addr(smem + p.off_bar) + warp * S * 8;
+  DcRange *ph = reinterpret_cast<DcRange *>(smem + p.off_red + kDcRedBytes + kEpMaxRanks * 8);
+  if (tid == 0) {
+    ph[0] = DcRange{g_gu, c0_gu, nt_gu, p.round_gu, kb_gu_i, make_fastdiv(gt_gu_i)};
+    ph[1] = DcRange{g_dn, c0_dn, nt_dn, p.round_dn, kb_dn_i, make_fastdiv(gt_dn_i)};
+  }
+  __syncthreads();
+  DcRing rg{};
+  rg.iss.init(nt_gu, p.round_gu, kb_gu_i, kDcWarps, warp);
+  rg.iss_phase = 0;
+  while (rg.iss_phase < 2 && !rg.iss.valid()) {
+    if (++rg.iss_phase < 2) rg.iss.init(nt_dn, p.round_dn, kb_dn_i, kDcWarps, warp);
+  }
+  if (lane == 0 && rg.iss_phase < 2) {
+    const uint32_t ring_s = smem_addr(smem + warp * S * kUnitBytes);
+    for (int sl = 0; sl < S; ++sl) mbar_init(bar0 + 8 * sl, 1);
+    mbar_fence_init();
+    for (int sl = 0; sl < S && rg.iss_phase < 2; ++sl) dc_issue(rg, ph, warp, ring_s, bar0, sl);
+  }
+  __syncwarp();   // the ring's barriers are initialised before any lane waits on them
+  // expert parallelism: zero the slot rows other ranks compute
+  if (p.zero_foreign) {
+    const int rows = T * (k + 1);
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+      const int t = r / (k + 1), pos = r - t * (k + 1);
+      const int e = slots[r];
+      const bool mine = pos < k ? (e >= p.own.lo && e < p.own.hi) : (e >= 0 && ((p.own.shared_mask >> t) & 1u));
+      if (mine) continue;
+      uint4 *dst = reinterpret_cast<uint4 *>(p.slot_rows + (size_t)r * p.hidden);
+      for (int i = tid; i < p.hidden / 8; i += blockDim.x) dst[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  dc_stamp(p, kTrStaged);
+
+  // ------------------------------------------------------------ 4 gate/up
+  dc_phase<NTB>(p, smem, ph, 0, stage, 1, T, g_mask, g_dst, 0, rg);
+  bool failed = __syncthreads_or(rg.failed) != 0;
+  dc_stamp(p, kTrGateUp);
+  if (!failed && !dc_grid_barrier(p.bar, p.err, ok_s)) failed = true;
+  dc_stamp(p, kTrActReady);
+
+  // --------------------------------------------------------------- 5 down
+  if (!failed) {
+    const int g_lo = c0_dn / gt_dn_i;
+    const int g_hi = nt_dn ? (c0_dn + nt_dn - 1) / gt_dn_i : g_lo - 1;
+    const int nblk = g_hi - g_lo + 1;
+    if (nblk > 0)
+      dc_stage(p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, p.inter_pad, 8 * NTB, nblk, T, kb_dn_i, stage, warp,
+               kDcWarps);
+    __syncthreads();
+    dc_phase<NTB>(p, smem, ph, 1, stage, nblk > 0 ? nblk : 1, T, g_mask, g_dst, g_lo, rg);
+    failed = __syncthreads_or(rg.failed) != 0;
+  }
+  dc_stamp(p, kTrDown);
+  if (p.ep_world > 1 && tid == 0) __threadfence_system();   // this CTA's rows to peers, before the barrier
+  if (!failed && !dc_grid_barrier(p.bar, p.err, ok_s)) failed = true;
+  if (p.ep_world > 1 && !failed) {
+    // every rank's rows for this rank's tokens have been written once every
+    // rank has passed its own barrier and signalled
+    if (blockIdx.x == 0 && tid == 0) {
+      __threadfence_system();
+      for (int r = 0; r < p.ep_world; ++r)
+        red_add_release_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r]) + 1, 1ull);
+    }
+    if (!dc_wait_sys(p.ep_flags + 1, (ep_calls + 1) * p.ep_world, p.err, ok_s)) failed = true;
+  }
+  dc_stamp(p, kTrRows);
+
+  // ------------------------------------------------------------ 6 combine
+  if (!failed && p.out)
+    dc_combine(p, slot_w, p.ep_world > 1 ? reinterpret_cast<const uint16_t *>(ep_peer_s[p.ep_rank] + p.ep_red_off)
+                                         : nullptr);
+  if (p.ep_world > 1 && !failed && blockIdx.x == 0 && tid == 0)
+    *reinterpret_cast<volatile unsigned long long *>(p.ep_flags + 2) = ep_calls + 1;
+  __syncthreads();
+  dc_stamp(p, kTrEnd);
+  // after a failure, the copies still in flight land before the CTA's shared
+  // memory is released (ring indices consumed .. issued-1)
+  if (failed && lane == 0) {
+    for (int j = rg.consumed; j < rg.issued; ++j) mbar_wait_bounded(bar0 + 8 * (j % S), (uint32_t)(j / S) & 1u);
+  }
+}
+
+// ------------------------------------------------------------------- host --
+struct DcLayout {
+  int stages, round_gu, round_dn, off_stage, off_part, off_tab, off_sel, off_red, off_bar, smem;
+};
+
+static int dc_max_groups(int T, int k, const MoeOwned &own) {
+  const int owned = own.hi - own.lo;
+  return (T * k < owned ? T * k : owned) + (own.shared_mask ? 1 : 0);
+}
+
+// Shared-memory layout of one call: the deepest weight ring first; the round
+// partials hold at most the tiles a CTA can get in either phase and shrink
+// before the ring does.
+static bool dc_layout(const rc_moe *m, int T, int k, const MoeOwned &own, DcLayout *L) {
+  const int ntb = T <= 8 ? 1 : 2, E = m->n_experts, grid = m->ctx->sm_count;
+  const int hidden = m->hidden, inter_pad = m->inter_pad;
+  const int kb_gu = hidden / kUnitK, kb_dn = inter_pad / kUnitK;
+  const int mg = dc_max_groups(T, k, own);
+  const int per_gu = (mg * (m->inter / 8) + grid - 1) / grid;
+  const int per_dn = (mg * (hidden / kUnitRows) + grid - 1) / grid;
+  // the down range of a CTA touches at most kMoeMaxGroupsPerCta groups
+  size_t stage = dc_stage_bytes(1, T, kb_gu);
+  const size_t st_a = dc_stage_bytes(kMoeMaxGroupsPerCta, T, kb_dn);
+  if (st_a > stage) stage = st_a;
+  const size_t tab = (size_t)(E + 1) * (4 * 8 + 4 + 4 + 4 + 4 * T + 4 + 4) + 16 + 64;
+  const size_t sel = (size_t)T * (k + 1) * 4 + (size_t)T * k * 4 * 3;
+  const size_t red = (size_t)kDcRedBytes + kEpMaxRanks * 8 + 2 * sizeof(DcRange);
+  const int unit_part = ntb * 32 * 16;
+  for (int S = kDcMaxStages; S >= 2; --S) {
+    for (int cap = 64 * 1024; cap >= 4 * 1024; cap /= 2) {
+      int R_gu = cap / (kb_gu * unit_part), R_dn = cap / (kb_dn * unit_part);
+      if (R_gu < 1 || R_dn < 1) continue;
+      if (R_gu > per_gu) R_gu = per_gu > 0 ? per_gu : 1;
+      if (R_dn > per_dn) R_dn = per_dn > 0 ? per_dn : 1;
+      const size_t part = (size_t)(R_gu * kb_gu > R_dn * kb_dn ? R_gu * kb_gu : R_dn * kb_dn) * unit_part;
+      size_t off = (size_t)kDcWarps * S * kUnitBytes;
+      const size_t o_stage = off;
+      off += (stage + 15) / 16 * 16;
+      const size_t o_part = off;
+      off += part;
+      const size_t o_tab = off;
+      off += (tab + 15) / 16 * 16;
+      const size_t o_sel = off;
+      off += (sel + 15) / 16 * 16;
+      const size_t o_red = off;
+      off += (red + 15) / 16 * 16;
+      const size_t o_bar = off;
+      off += (size_t)kDcWarps * S * 8;
+      if (off <= (size_t)kGemvSmemLimit) {
+        *L = DcLayout{S, R_gu, R_dn, (int)o_stage, (int)o_part, (int)o_tab, (int)o_sel, (int)o_red, (int)o_bar,
+                      (int)off};
+        return true;
+      }
+    }
+  }
+  return false;
+}
+
+bool moe_decode_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own) {
+  if (m->down_fmt != kFormatQ4nx) return false;   // q4nx unit arithmetic only
+  DcLayout L;
+  if (!dc_layout(m, T, k, own, &L)) return false;
+  const int max_groups = dc_max_groups(T, k, own);
+  const int gt_dn = m->hidden / kUnitRows;
+  const int per_dn = (max_groups * gt_dn + m->ctx->sm_count - 1) / m->ctx->sm_count;
+  return per_dn - 1 <= (kMoeMaxGroupsPerCta - 1) * gt_dn;
+}
+
+int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling,
+                          int act, float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign,
+                          uint16_t *out, int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s,
+                          const MoeEpArgs *ep) {
+  const int ntb = T <= 8 ? 1 : 2;
+  DcLayout L;
+  if (!dc_layout(m, T, k, own, &L)) {
+    set_error("MoE decode: no shared-memory layout for T=%d k=%d", T, k);
+    return RC_ERR_INVALID;
+  }
+  rc_ctx *ctx = m->ctx;
+  if (!m->fz_bar) {
+    RC_CUDA_TRY(cudaMalloc(&m->fz_bar, sizeof(unsigned long long)));
+    RC_CUDA_TRY(cudaMemset(m->fz_bar, 0, sizeof(unsigned long long)));
+    m->fz_epoch = ctx->timeout_epoch;
+  }
+  if (m->fz_epoch != ctx->timeout_epoch) {
+    // a bounded wait gave up since the last launch: the arrival count may be
+    // left over from that launch
+    RC_CUDA_TRY(cudaMemsetAsync(m->fz_bar, 0, sizeof(unsigned long long), s));
+    m->fz_epoch = ctx->timeout_epoch;
+  }
+  DcParams p{};
+  p.x = x;
+  p.T = T;
+  p.hidden = m->hidden;
+  p.n_experts = m->n_experts;
+  p.k = k;
+  p.mode = router;
+  p.renorm = renorm;
+  p.scaling = scaling;
+  p.wr = m->router_w;
+  p.bias = m->router_bias;
+  p.shared_id = m->has_shared ? m->n_experts : -1;
+  p.own = own;
+  p.logits = m->s.logits;
+  p.ids_out = ids_out;
+  p.w_out = w_out;
+  p.slot_w_out = slot_w_out;
+  p.gu_tiles = m->gu_tiles;
+  p.dn_tiles = m->dn_tiles;
+  p.inter = m->inter;
+  p.inter_pad = m->inter_pad;
+  p.act = m->act;
+  p.slot_rows = slot_rows;
+  p.zero_foreign = zero_foreign;
+  p.out = out;
+  p.act_kind = act;
+  p.gate_beta = gb;
+  p.value_beta = vb;
+  p.stages = L.stages;
+  p.round_gu = L.round_gu;
+  p.round_dn = L.round_dn;
+  p.off_stage = L.off_stage;
+  p.off_part = L.off_part;
+  p.off_tab = L.off_tab;
+  p.off_sel = L.off_sel;
+  p.off_red = L.off_red;
+  p.off_bar = L.off_bar;
+  p.bar = m->fz_bar;
+  p.err = ctx->err;
+  p.trace = m->trace;
+  p.ep_world = 1;
+  if (ep) {
+    p.ep_world = ep->world;
+    p.ep_rank = ep->rank;
+    p.ep_M = ep->M;
+    p.ep_peer = ep->peer_dev;
+    p.ep_flags = ep->flags;
+    p.ep_tok_off = ep->tok_off;
+    p.ep_red_off = ep->red_off;
+    p.ep_x_own = ep->x_own;
+  }
+  static bool configured[64][2] = {};
+  int dev = 0;
+  RC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 64 || !configured[dev][ntb - 1]) {
+    if (ntb == 1)
+      RC_CUDA_TRY(cudaFuncSetAttribute(rc_moe_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kGemvSmemLimit));
+    else
+      RC_CUDA_TRY(cudaFuncSetAttribute(rc_moe_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kGemvSmemLimit));
+    if (dev < 64) configured[dev][ntb - 1] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctx->sm_count);
+  cfg.blockDim = dim3(kDcThreads);
+  cfg.dynamicSmemBytes = L.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;      // every CTA resident: the grid barriers are safe
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (ntb == 1)
+    RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, rc_moe_decode_kernel<1>, p));
+  else
+    RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, rc_moe_decode_kernel<2>, p));
+  return RC_OK;
+}
+
+// The persistent decode path of a layer: this kernel (rc_moe_set_fused 1, the
+// default), or the earlier single-phase-per-template kernel of
+// q4nx_moe_fused.cu (2).  Both give the same bytes.
+bool moe_persistent_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own) {
+  return m->fused == 2 ? moe_fused_shape_ok(m, T, k, own) : moe_decode_shape_ok(m, T, k, own);
+}
+
+int moe_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling, int act,
+                   float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign, uint16_t *out,
+                   int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s, const MoeEpArgs *ep) {
+  if (m->fused == 2)
+    return moe_fused_decode(m, x, T, k, router, renorm, scaling, act, gb, vb, own, slot_rows, zero_foreign, out,
+                            ids_out, w_out, slot_w_out, s, ep);
+  return moe_decode_persistent(m, x, T, k, router, renorm, scaling, act, gb, vb, own, slot_rows, zero_foreign, out,
+                               ids_out, w_out, slot_w_out, s, ep);
+}
+
+}  // namespace rc

@@ -792,7 +792,7 @@ static bool fz_layout(const rc_moe *m, int T, int k, const MoeOwned &own, FzLayo
 // Whether the fused kernel takes this call: it is switched on (rc_moe_set_fused)
 // and the shape is one it can run.
 bool moe_fused_fits(const rc_moe *m, int T, int k, const MoeOwned &own) {
-  return m->fused && moe_fused_shape_ok(m, T, k, own);
+  return m->fused && moe_persistent_shape_ok(m, T, k, own);
 }
 
 // Whether the fused kernel can run this shape: the shared-memory layout fits
