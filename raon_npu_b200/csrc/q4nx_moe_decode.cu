@@ -1,37 +1,40 @@
-// The MoE decode layer for T <= 16 tokens as one persistent kernel, laid out
-// for a small instruction footprint: every phase of a layer runs once per
-// launch, so code that is executed once per SM is fetched from L2 on every
-// launch; the kernel therefore keeps one out-of-line body for the unit loop
-// of both expert phases, one for activation staging and compact routing code.
+// The MoE decode layer for T <= 16 tokens as one persistent kernel.
 //
 // One CTA per SM (cooperative launch: every CTA resident), 16 warps:
 //
 //   0 tokens     (expert parallelism) every rank's token rows arrive in this
 //                rank's exchange buffer
-//   1 stage      the token rows become mma B fragments in shared memory,
-//                slot-compact (only the T token columns are stored)
+//   1 stage      the CTA's router rows are requested; the token rows become
+//                mma B fragments in shared memory, slot-compact (only the T
+//                token columns are stored)
 //   2 logits     CTA c computes the logits of experts c, c + grid, ...
 //                (f64 sums of exact bf16 products, rounded once to f32)
 //   -- grid barrier --
-//   3 selection  one warp per token: k rounds of warp arg-max over router
-//                keys (larger first, NaN last, ties by lower index), the
-//                weights, the ascending-ID slot lists; the CTA builds the group
-//                table (identical everywhere: no barrier after it)
-//   4 gate/up    the CTA's contiguous range of (group, row tile) tiles, units
-//                dealt to the warps k-block-major (RoundCursor), per-unit
-//                partials summed in k-block order, GLU epilogue -> act rows
+//   3 selection  every CTA ranks the T x E router keys (larger first, NaN
+//                last, ties by lower index) by counting, takes the k best per
+//                token, the weights, the ascending-ID slot lists and the group
+//                table -- identical inputs, identical tables, no barrier
+//   4 stream     the CTA's share of the layer -- a contiguous range of
+//                (group, row tile) tiles of gate/up, then one of down -- is a
+//                stream of 2560-byte units fetched in chunks of a few units
+//                (one mbarrier, one to three bulk copies each) into a ring of
+//                chunk slots; at T = 1 the whole share is requested at once
+//   5 gate/up    rounds of whole tiles: unit i of a round goes to warp i % 16
+//                (a warp keeps one k-block), each unit's result to its own
+//                slot-compact partial; a tile is the sum of its units in
+//                k-block order; GLU epilogue -> act rows
 //   -- grid barrier --
-//   5 down       the same over the down tiles; act rows of the range's
-//                groups staged slot-compact; slot rows out
+//   6 down       act rows of the CTA's down groups staged slot-compact; the
+//                same rounds; slot rows out (with expert parallelism, into
+//                the buffer of the token's owner)
 //   -- grid barrier (and, with expert parallelism, every rank's rows) --
-//   6 combine    ascending-ID f32 sum (multiply then add, no FMA), RTNE, plus
+//   7 combine    ascending-ID f32 sum (multiply then add, no FMA), RTNE, plus
 //                the shared row
 //
-// Each warp streams its units through a ring of bulk copies that runs on
-// from its gate/up units into its down units.  The unit arithmetic, the
-// partition rules and the combine are those of the separate kernels in
-// q4nx_moe.cu, so a token's bytes do not depend on which path ran.  Every
-// wait is bounded (1 s): it sets the error word and the kernel unwinds.
+// The unit arithmetic, the partition of tiles over CTAs and the combine are
+// those of the separate kernels in q4nx_moe.cu (a tile's result depends on
+// the tile alone), so a token's bytes do not depend on which path ran.
+// Every wait is bounded (1 s): it sets the error word and the kernel unwinds.
 #include "moe_internal.cuh"
 #include "q4nx_core.cuh"
 #include "rc_device.cuh"
@@ -41,10 +44,10 @@ namespace rc {
 
 constexpr int kDcWarps = 16;
 constexpr int kDcThreads = kDcWarps * 32;
-constexpr int kDcMaxStages = 6;
-constexpr int kDcChunks = kMoeMaxExperts / 32;   // router values a lane holds per token
+constexpr int kDcChunk = 6;         // units per chunk
+constexpr int kDcMaxChunks = 32;    // chunk slots at most (shared memory decides)
 // "red" area: [16 warps][16 tokens] f64 partial logits, the barrier verdict
-// word, then the peer buffer table and the two phase ranges
+// word, then the peer buffer table
 constexpr int kDcRedBytes = kDcWarps * kMoeMaxTokens * 8 + 16;
 
 struct DcParams {
@@ -68,8 +71,10 @@ struct DcParams {
   uint16_t *out;                     // [T][hidden], null: no combine
   int act_kind;
   float gate_beta, value_beta;
-  int stages, round_gu, round_dn;
-  int off_stage, off_part, off_tab, off_sel, off_red, off_bar;
+  int chunk_slots;                   // B: chunk slots of the unit ring
+  int round_units;                   // units a round may hold (partials)
+  int stage_blk;                     // act blocks (groups) the staging area holds
+  int off_buf, off_stage, off_part, off_tab, off_sel, off_red, off_bar;
   unsigned long long *bar;           // grid-barrier arrival count (only grows)
   int *err;
   int ep_world, ep_rank, ep_M;
@@ -85,8 +90,8 @@ __device__ __forceinline__ void dc_stamp(const DcParams &p, int phase) {
 }
 
 // Router order as an unsigned key: larger value -> larger key, -0 equal to
-// +0, NaN (1) below every number, 0 = no candidate.  Equal keys are ordered
-// by lower expert index.
+// +0, NaN (1) below every number.  Equal keys are ordered by lower expert
+// index, so (key, index) is a strict total order.
 __device__ __forceinline__ uint32_t dc_route_key(float v) {
   if (v != v) return 1u;
   uint32_t b = __float_as_uint(v);
@@ -121,7 +126,7 @@ static __device__ __noinline__ void dc_stage(const uint16_t *src, int ld, int ro
   uint16_t *bmin16 = reinterpret_cast<uint16_t *>(area + (size_t)nblk * tsl * kb * 512);
   float *inv = reinterpret_cast<float *>(area + (size_t)nblk * tsl * kb * 576);
   const int ntask = nblk * tsl * kb;
-  #pragma unroll 1
+#pragma unroll 1
   for (int i = w0; i < ntask; i += nw) {
     const int b = i / (tsl * kb), r = i - b * tsl * kb, t = r / kb, kbi = r - t * kb;
     const uint4 raw = __ldcg(reinterpret_cast<const uint4 *>(src + ((size_t)b * row_blk + t) * ld +
@@ -246,45 +251,59 @@ static __device__ __noinline__ bool dc_wait_sys(const unsigned long long *ctr, u
   return *ok_s != 0;
 }
 
-// ------------------------------------------------------ units and rings --
-// One phase's units: tiles [c0, c0 + n_tiles) of the group-major tile list,
-// kb k-blocks each, rounds of R tiles (RoundCursor).
-struct DcRange {
-  const uint8_t *const *g_ptr;       // [groups] tile base of each group (null: not loaded)
-  int c0, n_tiles, R, kb;
-  FastDiv gt;                        // tiles per group
-
-  __device__ __forceinline__ const uint8_t *src(const RoundCursor &c) const {
-    const uint32_t tg = c0 + c.tile();
-    const uint32_t grp = fdiv(tg, gt), tile = tg - grp * gt.d;
-    const uint8_t *b = g_ptr[grp];
-    return b ? b + ((size_t)tile * kb + c.kbi) * kUnitBytes : nullptr;
-  }
+// ------------------------------------------------------- unit stream ----
+// The CTA's units: gate/up tiles [c0[0], c0[0] + nt[0]) of the group-major
+// tile list (kb[0] k-blocks each), then down tiles [c0[1], c0[1] + nt[1]);
+// unit s of the stream is (tile, k-block) in memory order, so each group's
+// part of a phase is one contiguous byte range.
+struct DcStream {
+  const uint8_t *const *g_ptr[2];    // per phase: tile base of each group (shared memory)
+  int c0[2], nt[2], kb[2], gt[2];
+  int units0, units;                 // gate/up units; all units
+  int nchunk;                        // chunks of kDcChunk units
 };
 
-// A warp's ring: its gate/up units, then its down units; the issue cursor
-// runs up to S units ahead of consumption, across the phase boundary.
-struct DcRing {
-  RoundCursor iss;
-  int iss_phase;                     // 0 gate/up, 1 down, 2 none left
-  int slot, issued, consumed;
-  uint32_t parity;
-  bool failed;
-};
+// The global address and the contiguous extent (in units, <= n) of unit s.
+__device__ __forceinline__ const uint8_t *dc_unit_src(const DcStream &st, int s, int n, int *run) {
+  const int ph = s < st.units0 ? 0 : 1;
+  const int u = ph ? s - st.units0 : s;
+  const int kb = st.kb[ph];
+  const int tg = st.c0[ph] + u / kb;                      // tile in the group-major list
+  const int grp = tg / st.gt[ph], tile = tg - grp * st.gt[ph];
+  // units left in this group of this phase
+  const int grp_end_tile = (grp + 1) * st.gt[ph] < st.c0[ph] + st.nt[ph] ? (grp + 1) * st.gt[ph]
+                                                                           : st.c0[ph] + st.nt[ph];
+  const int left = (grp_end_tile - tg) * kb - (u % kb);
+  *run = left < n ? left : n;
+  const uint8_t *b = st.g_ptr[ph][grp];
+  return b ? b + ((size_t)tile * kb + u % kb) * kUnitBytes : nullptr;
+}
 
-static __device__ __noinline__ void dc_issue(DcRing &rg, const DcRange *ph, int warp, uint32_t ring_s, uint32_t bar0,
-                                             int sl) {
-  const uint8_t *src = ph[rg.iss_phase].src(rg.iss);
-  if (src) {
-    mbar_arrive_expect_tx(bar0 + 8 * sl, kUnitBytes);
-    bulk_copy_g2s(ring_s + sl * kUnitBytes, src, kUnitBytes, bar0 + 8 * sl, policy_evict_first());
-  } else {
-    mbar_arrive_expect_tx(bar0 + 8 * sl, 0);
+// Request chunk j into its slot (one thread): one bulk copy per contiguous
+// run (a chunk may cross a group or the phase boundary); units of experts
+// that are not loaded here are not fetched.
+static __device__ __noinline__ void dc_issue_chunk(const DcStream &st, int j, uint8_t *buf, uint32_t bar0,
+                                                   int slots) {
+  const int slot = j % slots;
+  const uint32_t bar = bar0 + 8 * slot;
+  const int s0 = j * kDcChunk, s1 = s0 + kDcChunk < st.units ? s0 + kDcChunk : st.units;
+  int bytes = 0;
+#pragma unroll 1
+  for (int s = s0; s < s1;) {
+    int run;
+    const uint8_t *src = dc_unit_src(st, s, s1 - s, &run);
+    if (src) bytes += run * kUnitBytes;
+    s += run;
   }
-  ++rg.issued;
-  rg.iss.next();
-  while (rg.iss_phase < 2 && !rg.iss.valid()) {
-    if (++rg.iss_phase < 2) rg.iss.init(ph[1].n_tiles, ph[1].R, ph[1].kb, kDcWarps, warp);
+  mbar_arrive_expect_tx(bar, bytes);
+  const uint64_t pol = policy_evict_first();
+  const uint32_t dst0 = smem_addr(buf) + slot * kDcChunk * kUnitBytes;
+#pragma unroll 1
+  for (int s = s0; s < s1;) {
+    int run;
+    const uint8_t *src = dc_unit_src(st, s, s1 - s, &run);
+    if (src) bulk_copy_g2s(dst0 + (s - s0) * kUnitBytes, src, run * kUnitBytes, bar, pol);
+    s += run;
   }
 }
 
@@ -292,121 +311,140 @@ static __device__ __noinline__ float dc_glu(float gate, float up, int kind, floa
   return kind == RC_ACT_SITU ? act_situ(gate, up, gb, vb) : act_swiglu(gate, up);
 }
 
-// One phase (epi 0: gate/up with the GLU epilogue, 1: down) of this CTA.
-// Each unit's result goes to its own shared-memory partial; after a round's
-// barrier one warp per tile sums the tile's partials in k-block order and
-// runs the epilogue, so a tile's result depends on the tile alone.
+// Slot-compact partials: per unit of a round, the lanes whose result columns
+// exist -- token block tb keeps lanes with quad index < qn(T, tb) -- as float4.
+__host__ __device__ __forceinline__ int dc_qn(int T, int tb) {
+  const int n = (T - 8 * tb + 1) / 2;
+  return n < 0 ? 0 : (n > 4 ? 4 : n);
+}
+
+// One phase's rounds (ph 0: gate/up with the GLU epilogue, 1: down).
 template <int NTB>
-static __device__ __noinline__ void dc_phase(const DcParams &p, uint8_t *smem, const DcRange *ph, int epi,
-                                             const uint8_t *stage, int nblk, int tsl, const uint32_t *g_mask,
-                                             const int *g_dst, int g_lo, DcRing &rg) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const DcRange &pr = ph[epi];
+static __device__ __noinline__ void dc_rounds(const DcParams &p, uint8_t *smem, const DcStream &st, int ph,
+                                              const uint8_t *stage, int nblk, const uint32_t *g_mask,
+                                              const int *g_dst, int g_lo, int *issued, bool *failed) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, T = p.T;
   uint8_t *const *ep_peer_s = reinterpret_cast<uint8_t *const *>(smem + p.off_red + kDcRedBytes);
-  const int S = p.stages;
-  const int kb = pr.kb, R = pr.R, n_tiles = pr.n_tiles;
-  uint8_t *ring = smem + warp * S * kUnitBytes;
-  const uint32_t ring_s = smem_addr(ring);
-  const uint32_t bar0 = smem_addr(smem + p.off_bar) + warp * S * 8;
-  XFrag<NTB> xr;
-  int xr_key = -1;                              // (block, k-block) held in xr
+  uint8_t *buf = smem + p.off_buf;
+  const uint32_t bar0 = smem_addr(smem + p.off_bar);
   float4 *part = reinterpret_cast<float4 *>(smem + p.off_part);
-  const int n_rounds = round_count(n_tiles, R);
-  RoundCursor cur;
-  cur.init(n_tiles, R, kb, kDcWarps, warp);
+  const int B = p.chunk_slots;
+  const int kb = st.kb[ph], nt = st.nt[ph], gt = st.gt[ph], c0 = st.c0[ph];
+  const int base = ph ? st.units0 : 0;
+  const int qn0 = dc_qn(T, 0), qn1 = NTB == 2 ? dc_qn(T, 1) : 0, rec = 8 * (qn0 + qn1);
   const int g = lane >> 2, qd = lane & 3;
-  for (int r = 0; r < n_rounds; ++r) {
-    for (; cur.valid() && cur.round == r; cur.next()) {
-      const uint32_t grp = fdiv(pr.c0 + cur.tile(), pr.gt);
-      if (!rg.failed) {
-        if (mbar_wait_bounded_warp(bar0 + 8 * rg.slot, rg.parity)) {
-          ++rg.consumed;
-        } else {
+  const int tiles_per_round = p.round_units / kb;
+  XFrag<NTB> xr;
+  int xr_key = -1;
+#pragma unroll 1
+  for (int t0 = 0; t0 < nt; t0 += tiles_per_round) {
+    const int t1 = t0 + tiles_per_round < nt ? t0 + tiles_per_round : nt;
+    const int nu = (t1 - t0) * kb;
+    bool wfail = false;                        // this warp gave up a wait
+    if (!*failed) {
+#pragma unroll 1
+      for (int i = warp; i < nu; i += kDcWarps) {
+        const int u = t0 * kb + i, s = base + u;
+        const int j = s / kDcChunk;
+        if (!mbar_wait_bounded_warp(bar0 + 8 * (j % B), (uint32_t)(j / B) & 1u)) {
           if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
-          rg.failed = true;
+          wfail = true;
+          break;
         }
-      }
-      if (!rg.failed && pr.g_ptr[grp] != nullptr) {
-        const int blk = epi == 0 ? 0 : (int)grp - g_lo;
-        if (blk * kb + cur.kbi != xr_key) {
-          dc_load_frag<NTB>(xr, stage, nblk, tsl, kb, blk, cur.kbi, lane);
-          xr_key = blk * kb + cur.kbi;
+        const int tg = c0 + u / kb, kbi = u % kb;
+        const int grp = tg / gt;
+        if (st.g_ptr[ph][grp] == nullptr) continue;
+        const int blk = ph ? grp - g_lo : 0;
+        if (blk * kb + kbi != xr_key) {
+          dc_load_frag<NTB>(xr, stage, nblk, T, kb, blk, kbi, lane);
+          xr_key = blk * kb + kbi;
         }
         float4 Q[NTB];
-        unit_result<NTB>(ring + rg.slot * kUnitBytes, xr, lane, Q);
-        float4 *dst = part + (size_t)cur.slot() * NTB * 32 + lane;
-#pragma unroll
-        for (int tb = 0; tb < NTB; ++tb) dst[tb * 32] = Q[tb];
+        unit_result<NTB>(buf + ((size_t)(j % B) * kDcChunk + s % kDcChunk) * kUnitBytes, xr, lane, Q);
+        float4 *dst = part + (size_t)i * rec;
+        if (qd < qn0) dst[g * qn0 + qd] = Q[0];
+        if (NTB == 2 && qd < qn1) dst[8 * qn0 + g * qn1 + qd] = Q[NTB - 1];
       }
-      __syncwarp();
-      if (!rg.failed && lane == 0 && rg.iss_phase < 2) dc_issue(rg, ph, warp, ring_s, bar0, rg.slot);
-      if (++rg.slot == S) rg.slot = 0, rg.parity ^= 1u;
     }
-    __syncthreads();
-    const int t_lo = r * R, t_hi = t_lo + R < n_tiles ? t_lo + R : n_tiles;
-    for (int ti = t_lo + warp; ti < t_hi; ti += kDcWarps) {
-      const uint32_t tg = pr.c0 + ti;
-      const uint32_t grp = fdiv(tg, pr.gt), tile = tg - grp * pr.gt.d;
-      const bool live = pr.g_ptr[grp] != nullptr;
-      Acc<NTB> acc;
-      acc_zero(acc);
-      const float4 *src = part + (size_t)(ti - t_lo) * kb * NTB * 32 + lane;
-      for (int kbi = 0; kbi < kb; ++kbi) {
-        float4 v[NTB];
+    // a wait that ran out in any warp stops the phase (CTA-uniform verdict)
+    if (__syncthreads_or(wfail)) *failed = true;
+    if (!*failed) {
+      // a tile is the sum of its units' results in k-block order
+#pragma unroll 1
+      for (int ti = t0 + warp; ti < t1; ti += kDcWarps) {
+        const int tg = c0 + ti, grp = tg / gt, tile = tg - grp * gt;
+        const bool live = st.g_ptr[ph][grp] != nullptr;
+        Acc<NTB> acc;
+        acc_zero(acc);
+        const float4 *src = part + (size_t)(ti - t0) * kb * rec;
+#pragma unroll 1
+        for (int kbi = 0; kbi < kb; ++kbi) {
+          float4 v[NTB];
+          v[0] = qd < qn0 ? src[(size_t)kbi * rec + g * qn0 + qd] : make_float4(0.f, 0.f, 0.f, 0.f);
+          if (NTB == 2)
+            v[NTB - 1] = qd < qn1 ? src[(size_t)kbi * rec + 8 * qn0 + g * qn1 + qd] : make_float4(0.f, 0.f, 0.f, 0.f);
+          acc_add(acc, v);
+        }
+        const uint32_t mask = g_mask[grp];
 #pragma unroll
-        for (int tb = 0; tb < NTB; ++tb) v[tb] = src[(kbi * NTB + tb) * 32];
-        acc_add(acc, v);
-      }
-      const uint32_t mask = g_mask[grp];
+        for (int tb = 0; tb < NTB; ++tb) {
 #pragma unroll
-      for (int tb = 0; tb < NTB; ++tb) {
-#pragma unroll
-        for (int e2 = 0; e2 < 2; ++e2) {
-          const int t = tb * 8 + 2 * qd + e2;
-          if (t >= p.T || !((mask >> t) & 1u)) continue;
-          if (epi == 0) {
-            float v = 0.f;
-            if (live) v = dc_glu(bf16_round(acc.v[tb][e2]), bf16_round(acc.v[tb][2 + e2]), p.act_kind,
-                                 p.gate_beta, p.value_beta);
-            p.act[((size_t)grp * 8 * NTB + t) * p.inter_pad + tile * 8 + g] = f32_to_bf16_rne(v);
-          } else {
-            const int srow = g_dst[grp * p.T + t];     // slot row t*(k+1) + position
-            uint16_t *y;
-            if (p.ep_world > 1) {
-              // straight into the buffer of the token's owner
-              const int tt = srow / (p.k + 1), pos = srow - tt * (p.k + 1);
-              const int owner = tt / p.ep_M, tl = tt - owner * p.ep_M;
-              y = reinterpret_cast<uint16_t *>(ep_peer_s[owner] + p.ep_red_off) +
-                  ((size_t)tl * (p.k + 1) + pos) * p.hidden + tile * kUnitRows + g;
+          for (int e2 = 0; e2 < 2; ++e2) {
+            const int t = tb * 8 + 2 * qd + e2;
+            if (t >= T || !((mask >> t) & 1u)) continue;
+            if (ph == 0) {
+              float v = 0.f;
+              if (live) v = dc_glu(bf16_round(acc.v[tb][e2]), bf16_round(acc.v[tb][2 + e2]), p.act_kind,
+                                   p.gate_beta, p.value_beta);
+              p.act[((size_t)grp * 8 * NTB + t) * p.inter_pad + tile * 8 + g] = f32_to_bf16_rne(v);
             } else {
-              y = p.slot_rows + (size_t)srow * p.hidden + tile * kUnitRows + g;
+              const int srow = g_dst[grp * T + t];     // slot row t*(k+1) + position
+              uint16_t *y;
+              if (p.ep_world > 1) {
+                // straight into the buffer of the token's owner
+                const int tt = srow / (p.k + 1), pos = srow - tt * (p.k + 1);
+                const int owner = tt / p.ep_M, tl = tt - owner * p.ep_M;
+                y = reinterpret_cast<uint16_t *>(ep_peer_s[owner] + p.ep_red_off) +
+                    ((size_t)tl * (p.k + 1) + pos) * p.hidden + tile * kUnitRows + g;
+              } else {
+                y = p.slot_rows + (size_t)srow * p.hidden + tile * kUnitRows + g;
+              }
+              y[0] = live ? f32_to_bf16_rne(acc.v[tb][e2]) : (uint16_t)0;
+              y[8] = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : (uint16_t)0;
             }
-            y[0] = live ? f32_to_bf16_rne(acc.v[tb][e2]) : (uint16_t)0;
-            y[8] = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : (uint16_t)0;
           }
         }
       }
     }
     __syncthreads();
+    // chunks whose units all lie before this round's end are consumed: their
+    // slots take the next chunks of the stream
+    if (!*failed && threadIdx.x == 0) {
+      const int done = (base + t1 * kb) / kDcChunk;
+#pragma unroll 1
+      for (; *issued < st.nchunk && *issued < done + B; ++*issued) dc_issue_chunk(st, *issued, buf, bar0, B);
+    }
   }
 }
 
 // ---------------------------------------------------------- routing -----
 // The logits of experts blockIdx.x, + grid, ... for all T tokens: warp w sums
 // the 256-column slices w, w + 16, ... in f64 (exact bf16 products), the CTA
-// adds the warps' sums in warp order and rounds once to f32.
-static __device__ __noinline__ void dc_logits(const DcParams &p, double *red) {
+// adds the warps' sums in warp order and rounds once to f32.  ``wpre`` is the
+// lane's router slice of this CTA's first expert, requested before staging.
+static __device__ __noinline__ void dc_logits(const DcParams &p, double *red, uint4 wpre) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = p.T, E = p.n_experts, nslice = p.hidden / kUnitK;
-  #pragma unroll 1
+#pragma unroll 1
   for (int e = blockIdx.x; e < E; e += gridDim.x) {
-    #pragma unroll 1
+#pragma unroll 1
     for (int t = 0; t < T; ++t) {
       double acc = 0.0;
-      #pragma unroll 1
+#pragma unroll 1
       for (int sl = warp; sl < nslice; sl += kDcWarps) {
         const int col = sl * kUnitK + lane * 8;
-        const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
+        const uint4 wv = (e == (int)blockIdx.x && sl == warp)
+                             ? wpre : __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
         const uint4 xv = __ldcg(reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.hidden + col));
         const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
@@ -422,7 +460,7 @@ static __device__ __noinline__ void dc_logits(const DcParams &p, double *red) {
     __syncthreads();
     if (tid < T) {
       double a = 0.0;
-      #pragma unroll 1
+#pragma unroll 1
       for (int w = 0; w < kDcWarps; ++w) a += red[w * kMoeMaxTokens + tid];
       p.logits[(size_t)tid * E + e] = __double2float_rn(a);
     }
@@ -430,63 +468,66 @@ static __device__ __noinline__ void dc_logits(const DcParams &p, double *red) {
   }
 }
 
-// Top-k of token ``warp`` (one warp per token): k rounds of warp-wide arg-max
-// over router keys, then the weights and the ascending-ID slot list.
-static __device__ __noinline__ void dc_select(const DcParams &p, const float *bias_s, int32_t *slots, float *slot_w,
-                                              int32_t *sel_e, float *sel_sc) {
-  const int lane = threadIdx.x & 31, t = threadIdx.x >> 5;
-  const int E = p.n_experts, k = p.k;
-  uint32_t key[kDcChunks];
-  float sc[kDcChunks];
-#pragma unroll
-  for (int c = 0; c < kDcChunks; ++c) {
-    const int e = c * 32 + lane;
-    key[c] = 0u;
-    sc[c] = 0.f;
-    if (e < E) {
-      const float l = __ldcg(p.logits + (size_t)t * E + e);
-      float v;
-      if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
-        sc[c] = dc_sigmoid(l);
-        v = sc[c] + bias_s[e];
-      } else {
-        sc[c] = l + bias_s[e];
-        v = sc[c];
-      }
-      key[c] = dc_route_key(v);
+// Selection by the whole CTA: every (token, expert) pair counts the experts
+// ahead of it in router order (a larger key, or an equal key and a lower
+// index); the pairs ranked below k are the top-k, best first.  Four threads
+// share a pair when there are few pairs.  Then per token (warp t, lane r < k)
+// the weight, the ascending-ID slot position and the expert's token mask.
+// ``scratch`` holds T*E keys and scores.
+static __device__ __noinline__ void dc_select(const DcParams &p, const float *bias_s, uint8_t *scratch,
+                                              int32_t *slots, float *slot_w, int32_t *sel_e, float *sel_sc,
+                                              uint32_t *mask_s) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int T = p.T, E = p.n_experts, k = p.k, n = T * E;
+  uint32_t *key_s = reinterpret_cast<uint32_t *>(scratch);
+  float *sc_s = reinterpret_cast<float *>(key_s + n);
+#pragma unroll 1
+  for (int i = tid; i < n; i += kDcThreads) {
+    const int e = i - (i / E) * E;
+    const float l = __ldcg(p.logits + i);
+    float sc, v;
+    if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
+      sc = dc_sigmoid(l);
+      v = sc + bias_s[e];
+    } else {
+      sc = l + bias_s[e];
+      v = sc;
+    }
+    sc_s[i] = sc;
+    key_s[i] = dc_route_key(v);
+  }
+  __syncthreads();
+  const int sub = n * 4 <= kDcThreads ? 4 : 1;           // threads per pair
+  const int per = (E + sub - 1) / sub;
+#pragma unroll 1
+  for (int i0 = tid / sub; i0 < n; i0 += kDcThreads / sub) {
+    const int t = i0 / E, e = i0 - t * E, part = tid - (tid / sub) * sub;
+    const uint32_t my = key_s[i0];
+    const uint32_t *kr = key_s + t * E;
+    const int lo = part * per, hi = lo + per < E ? lo + per : E;
+    int rank = 0;
+#pragma unroll 4
+    for (int e2 = lo; e2 < hi; ++e2) {
+      const uint32_t o = kr[e2];
+      rank += (o > my || (o == my && e2 < e)) ? 1 : 0;
+    }
+    if (sub == 4) {
+      rank += __shfl_xor_sync(0xffffffffu, rank, 1);
+      rank += __shfl_xor_sync(0xffffffffu, rank, 2);
+    }
+    if (rank < k && part == 0) {
+      sel_e[t * k + rank] = e;
+      sel_sc[t * k + rank] = sc_s[i0];
     }
   }
-  uint32_t taken = 0;
-  #pragma unroll 1
-  for (int r = 0; r < k; ++r) {
-    uint32_t bk = 0u;
-    int be = 0x7FFFFFFF;
-    float bs = 0.f;
-#pragma unroll
-    for (int c = 0; c < kDcChunks; ++c) {
-      if (!((taken >> c) & 1u) && key[c] > bk) {
-        bk = key[c];
-        be = c * 32 + lane;
-        bs = sc[c];
-      }
-    }
-    const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
-    const int emin = (int)__reduce_min_sync(0xffffffffu, bk == kmax ? (unsigned)be : 0x7FFFFFFFu);
-    const float ws = __shfl_sync(0xffffffffu, bs, emin & 31);
-    if ((emin & 31) == lane) taken |= 1u << (emin >> 5);
-    if (lane == 0) {
-      sel_e[t * k + r] = emin;
-      sel_sc[t * k + r] = ws;
-    }
-  }
-  __syncwarp();
-  if (lane < k) {
-    const int r = lane;
+  __syncthreads();
+  if (warp < T && lane < k) {
+    const int t = warp, r = lane;
     const float *ss = sel_sc + t * k;
     float w;
     if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
       float sum = 0.f;
-      #pragma unroll 1
+#pragma unroll 1
       for (int r2 = 0; r2 < k; ++r2) sum += ss[r2];
       w = ss[r];
       if (p.renorm) w = w / (sum + 1e-20f);
@@ -496,71 +537,61 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
       // softmax of the selected scores (the full denominator cancels)
       const float mx = ss[0];
       float sum = 0.f;
-      #pragma unroll 1
+#pragma unroll 1
       for (int r2 = 0; r2 < k; ++r2) sum += expf(ss[r2] - mx);
       w = expf(ss[r] - mx) / sum;
     }
     const int e = sel_e[t * k + r];
     int pos = 0;
-    #pragma unroll 1
+#pragma unroll 1
     for (int r2 = 0; r2 < k; ++r2) pos += sel_e[t * k + r2] < e ? 1 : 0;
     slots[t * (k + 1) + pos] = e;
     slot_w[t * k + pos] = w;
+    if (e >= p.own.lo && e < p.own.hi) atomicOr(mask_s + e, 1u << t);
     if (blockIdx.x == 0) {
       if (p.ids_out) p.ids_out[t * k + r] = e;
       if (p.w_out) p.w_out[t * k + r] = w;
       if (p.slot_w_out) p.slot_w_out[t * k + pos] = w;
     }
+    if (r == 0) slots[t * (k + 1) + k] = p.shared_id;
   }
-  if (lane == 0) slots[t * (k + 1) + k] = p.shared_id;
+  __syncthreads();
 }
 
-// The group table of the ascending-ID slot lists, built by the whole CTA: one
+// The group table from the experts' token masks (warp 0, then the CTA): one
 // group per expert of [own.lo, own.hi) that some token chose, ascending, then
 // the shared expert for the tokens of own.shared_mask; per (group, token) the
-// slot row t*(k+1) + position.
-static __device__ __noinline__ void dc_groups(const int32_t *slots, int T, int k, int E, MoeOwned own,
-                                              int32_t *g_expert, uint32_t *g_mask, int32_t *g_dst, int *n_groups,
-                                              uint32_t *mask_s, int *gidx_s, int *cnt_s, int *err) {
-  const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31;
-  #pragma unroll 1
-  for (int e = tid; e <= E; e += nth) mask_s[e] = e == E ? own.shared_mask : 0u;
-  __syncthreads();
-  #pragma unroll 1
-  for (int pr = tid; pr < T * k; pr += nth) {
-    const int t = pr / k, r = pr - t * k;
-    const int e = slots[t * (k + 1) + r];
-    if (e >= own.lo && e < own.hi) atomicOr(mask_s + e, 1u << t);
-    else if (e < 0 || e >= E) atomicCAS(err, 0, kErrBadExpert);
-  }
-  __syncthreads();
-  const int nchunks = (E + 1 + 31) / 32;      // <= 9 <= warps
-  uint32_t m = 0, b = 0;
-  const int e = warp * 32 + lane;
-  if (warp < nchunks) {
-    m = e <= E ? mask_s[e] : 0u;
-    b = __ballot_sync(0xffffffffu, m != 0u);
-    if (lane == 0) cnt_s[warp] = __popc(b);
-  }
-  __syncthreads();
-  if (warp < nchunks) {
+// slot row t*(k+1) + position; the groups' tile tables.
+static __device__ __noinline__ void dc_groups(const DcParams &p, const int32_t *slots, const uint32_t *mask_s,
+                                              int *gidx_s, int32_t *g_expert, uint32_t *g_mask, int32_t *g_dst,
+                                              int *n_groups, const uint8_t **all_gu, const uint8_t **all_dn,
+                                              const uint8_t **g_gu, const uint8_t **g_dn) {
+  const int tid = threadIdx.x, lane = tid & 31, T = p.T, k = p.k, E = p.n_experts;
+  if (tid < 32) {
     int base = 0;
-    #pragma unroll 1
-    for (int c = 0; c < warp; ++c) base += cnt_s[c];
-    if (m) {
-      const int gi = base + __popc(b & ((1u << lane) - 1u));
-      g_expert[gi] = e;
-      g_mask[gi] = m;
-      gidx_s[e] = gi;
+#pragma unroll 1
+    for (int c = 0; c <= E; c += 32) {
+      const int e = c + lane;
+      const uint32_t m = e <= E ? mask_s[e] : 0u;
+      const uint32_t b = __ballot_sync(0xffffffffu, m != 0u);
+      if (m) {
+        const int gi = base + __popc(b & ((1u << lane) - 1u));
+        g_expert[gi] = e;
+        g_mask[gi] = m;
+        gidx_s[e] = gi;
+        g_gu[gi] = all_gu[e];
+        g_dn[gi] = all_dn[e];
+      }
+      base += __popc(b);
     }
-    if (warp == nchunks - 1 && lane == 0) *n_groups = base + __popc(b);
+    if (lane == 0) *n_groups = base;
   }
   __syncthreads();
-  #pragma unroll 1
-  for (int pr = tid; pr < T * (k + 1); pr += nth) {
+#pragma unroll 1
+  for (int pr = tid; pr < T * (k + 1); pr += kDcThreads) {
     const int t = pr / (k + 1), r = pr - t * (k + 1);
     const int ex = slots[pr];
-    const bool mine = r < k ? (ex >= own.lo && ex < own.hi) : (ex >= 0 && ((own.shared_mask >> t) & 1u));
+    const bool mine = r < k ? (ex >= p.own.lo && ex < p.own.hi) : (ex >= 0 && ((p.own.shared_mask >> t) & 1u));
     if (mine) g_dst[gidx_s[ex] * T + t] = pr;
   }
   __syncthreads();
@@ -573,7 +604,7 @@ static __device__ __noinline__ void dc_combine(const DcParams &p, const float *s
   const bool with_shared = p.shared_id >= 0 && p.own.shared_mask;
   const bool ep = p.ep_world > 1;
   const int n_out = ep ? p.ep_M : p.T;
-  #pragma unroll 1
+#pragma unroll 1
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_out * vecs; i += gridDim.x * blockDim.x) {
     const int to = i / vecs, v = i - to * vecs;
     const int t = ep ? p.ep_rank * p.ep_M + to : to;
@@ -582,7 +613,7 @@ static __device__ __noinline__ void dc_combine(const DcParams &p, const float *s
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    #pragma unroll 1
+#pragma unroll 1
     for (int s = 0; s < k; ++s) {
       const uint4 r = __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)s * p.hidden));
       const float w = slot_w[t * k + s];
@@ -618,10 +649,16 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   uint8_t **ep_peer_s = reinterpret_cast<uint8_t **>(smem + p.off_red + kDcRedBytes);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = p.T, E = p.n_experts, k = p.k;
-  const int gt_gu_i = p.inter / 8, kb_gu_i = p.hidden / kUnitK;
-  const int gt_dn_i = p.hidden / kUnitRows, kb_dn_i = p.inter_pad / kUnitK;
+  const int gt_gu = p.inter / 8, kb_gu = p.hidden / kUnitK;
+  const int gt_dn = p.hidden / kUnitRows, kb_dn = p.inter_pad / kUnitK;
   uint8_t *stage = smem + p.off_stage;
   dc_stamp(p, kTrStart);
+
+  // the lane's router slice of this CTA's first expert, in flight while the
+  // tables load and the token rows are staged
+  uint4 wpre = make_uint4(0, 0, 0, 0);
+  if ((int)blockIdx.x < E && warp < p.hidden / kUnitK)
+    wpre = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)blockIdx.x * p.hidden + warp * kUnitK + lane * 8));
 
   // ---- expert parallelism: every rank's token rows into every rank's buffer
   unsigned long long ep_calls = 0;
@@ -653,15 +690,16 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   float *bias_s = reinterpret_cast<float *>(g_dn + (E + 1));
   int32_t *g_expert = reinterpret_cast<int32_t *>(bias_s + (E + 1));
   uint32_t *g_mask = reinterpret_cast<uint32_t *>(g_expert + (E + 1));
-  int32_t *g_dst = reinterpret_cast<int32_t *>(g_mask + (E + 1));                   // [E+1][T]
-  int *n_groups_s = g_dst + (E + 1) * T;
-  uint32_t *mask_s = reinterpret_cast<uint32_t *>(n_groups_s + 4);                 // [E+1]
+  uint32_t *mask_s = g_mask + (E + 1);                                              // [E+1]
   int *gidx_s = reinterpret_cast<int *>(mask_s + (E + 1));                         // [E+1]
-  int *cnt_s = gidx_s + (E + 1);                                                   // [9]
-  for (int i = tid; i <= E; i += blockDim.x) {
+  int *n_groups_s = gidx_s + (E + 1);                                              // [4]
+  int32_t *g_dst = n_groups_s + 4;                                                 // [E+1][T]
+#pragma unroll 1
+  for (int i = tid; i <= E; i += kDcThreads) {
     all_gu[i] = p.gu_tiles[i];
     all_dn[i] = p.dn_tiles[i];
     bias_s[i] = i < E ? p.bias[i] : 0.f;
+    mask_s[i] = i == E ? p.own.shared_mask : 0u;
   }
   if (p.ep_world > 1) {
     if (!dc_wait_sys(p.ep_flags + 0, (ep_calls + 1) * p.ep_world, p.err, ok_s)) return;
@@ -671,8 +709,8 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   }
 
   // ------------------------------------------- 1 stage, 2 logits
-  dc_stage(p.x, p.hidden, 0, 1, T, kb_gu_i, stage, warp, kDcWarps);
-  dc_logits(p, reinterpret_cast<double *>(smem + p.off_red));
+  dc_stage(p.x, p.hidden, 0, 1, T, kb_gu, stage, warp, kDcWarps);
+  dc_logits(p, reinterpret_cast<double *>(smem + p.off_red), wpre);
   dc_stamp(p, kTrLogits);
   if (!dc_grid_barrier(p.bar, p.err, ok_s)) return;
   dc_stamp(p, kTrRouted);
@@ -682,77 +720,78 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   float *slot_w = reinterpret_cast<float *>(slots + T * (k + 1));                   // [T][k]
   int32_t *sel_e = reinterpret_cast<int32_t *>(slot_w + T * k);                     // [T][k]
   float *sel_sc = reinterpret_cast<float *>(sel_e + T * k);                         // [T][k]
-  if (warp < T) dc_select(p, bias_s, slots, slot_w, sel_e, sel_sc);
-  __syncthreads();
-  dc_groups(slots, T, k, E, p.own, g_expert, g_mask, g_dst, n_groups_s, mask_s, gidx_s, cnt_s, p.err);
-  for (int i = tid; i < *n_groups_s; i += blockDim.x) {
-    g_gu[i] = all_gu[g_expert[i]];
-    g_dn[i] = all_dn[g_expert[i]];
-  }
-  __syncthreads();
+  // the unit buffer is free until the first chunk is requested: key scratch
+  dc_select(p, bias_s, smem + p.off_buf, slots, slot_w, sel_e, sel_sc, mask_s);
+  dc_groups(p, slots, mask_s, gidx_s, g_expert, g_mask, g_dst, n_groups_s, all_gu, all_dn, g_gu, g_dn);
   dc_stamp(p, kTrSelected);
 
-  // ------------------------------------------- partitions and ring
+  // ------------------------------------------- 4 partitions and stream
   const int ng = *n_groups_s;
-  const int tot_gu = ng * gt_gu_i, tot_dn = ng * gt_dn_i;
+  const int tot_gu = ng * gt_gu, tot_dn = ng * gt_dn;
   const int per_gu = (tot_gu + (int)gridDim.x - 1) / (int)gridDim.x;
   const int per_dn = (tot_dn + (int)gridDim.x - 1) / (int)gridDim.x;
   const int c0_gu = blockIdx.x * per_gu, c0_dn = blockIdx.x * per_dn;
   const int nt_gu = c0_gu < tot_gu ? (c0_gu + per_gu < tot_gu ? per_gu : tot_gu - c0_gu) : 0;
   const int nt_dn = c0_dn < tot_dn ? (c0_dn + per_dn < tot_dn ? per_dn : tot_dn - c0_dn) : 0;
-  const int S = p.stages;
-  const uint32_t bar0 = smem_addr(smem + p.off_bar) + warp * S * 8;
-  DcRange *ph = reinterpret_cast<DcRange *>(smem + p.off_red + kDcRedBytes + kEpMaxRanks * 8);
+  DcStream st;
+  st.g_ptr[0] = g_gu;
+  st.g_ptr[1] = g_dn;
+  st.c0[0] = c0_gu;
+  st.c0[1] = c0_dn;
+  st.nt[0] = nt_gu;
+  st.nt[1] = nt_dn;
+  st.kb[0] = kb_gu;
+  st.kb[1] = kb_dn;
+  st.gt[0] = gt_gu;
+  st.gt[1] = gt_dn;
+  st.units0 = nt_gu * kb_gu;
+  st.units = st.units0 + nt_dn * kb_dn;
+  st.nchunk = (st.units + kDcChunk - 1) / kDcChunk;
+  const int B = p.chunk_slots;
+  const uint32_t bar0 = smem_addr(smem + p.off_bar);
+  int issued = 0;                                   // chunks requested (thread 0)
+  __syncthreads();                                  // the selection scratch in the ring is dead
   if (tid == 0) {
-    ph[0] = DcRange{g_gu, c0_gu, nt_gu, p.round_gu, kb_gu_i, make_fastdiv(gt_gu_i)};
-    ph[1] = DcRange{g_dn, c0_dn, nt_dn, p.round_dn, kb_dn_i, make_fastdiv(gt_dn_i)};
-  }
-  __syncthreads();
-  DcRing rg{};
-  rg.iss.init(nt_gu, p.round_gu, kb_gu_i, kDcWarps, warp);
-  rg.iss_phase = 0;
-  while (rg.iss_phase < 2 && !rg.iss.valid()) {
-    if (++rg.iss_phase < 2) rg.iss.init(nt_dn, p.round_dn, kb_dn_i, kDcWarps, warp);
-  }
-  if (lane == 0 && rg.iss_phase < 2) {
-    const uint32_t ring_s = smem_addr(smem + warp * S * kUnitBytes);
-    for (int sl = 0; sl < S; ++sl) mbar_init(bar0 + 8 * sl, 1);
+#pragma unroll 1
+    for (int j = 0; j < B; ++j) mbar_init(bar0 + 8 * j, 1);
     mbar_fence_init();
-    for (int sl = 0; sl < S && rg.iss_phase < 2; ++sl) dc_issue(rg, ph, warp, ring_s, bar0, sl);
+#pragma unroll 1
+    for (; issued < st.nchunk && issued < B; ++issued) dc_issue_chunk(st, issued, smem + p.off_buf, bar0, B);
   }
-  __syncwarp();   // the ring's barriers are initialised before any lane waits on them
   // expert parallelism: zero the slot rows other ranks compute
   if (p.zero_foreign) {
     const int rows = T * (k + 1);
+#pragma unroll 1
     for (int r = blockIdx.x; r < rows; r += gridDim.x) {
       const int t = r / (k + 1), pos = r - t * (k + 1);
       const int e = slots[r];
       const bool mine = pos < k ? (e >= p.own.lo && e < p.own.hi) : (e >= 0 && ((p.own.shared_mask >> t) & 1u));
       if (mine) continue;
       uint4 *dst = reinterpret_cast<uint4 *>(p.slot_rows + (size_t)r * p.hidden);
+#pragma unroll 1
       for (int i = tid; i < p.hidden / 8; i += blockDim.x) dst[i] = make_uint4(0, 0, 0, 0);
     }
   }
+  __syncthreads();   // the chunk barriers are initialised before any warp waits on them
   dc_stamp(p, kTrStaged);
 
-  // ------------------------------------------------------------ 4 gate/up
-  dc_phase<NTB>(p, smem, ph, 0, stage, 1, T, g_mask, g_dst, 0, rg);
-  bool failed = __syncthreads_or(rg.failed) != 0;
+  // ------------------------------------------------------------ 5 gate/up
+  bool failed = false;
+  dc_rounds<NTB>(p, smem, st, 0, stage, 1, g_mask, g_dst, 0, &issued, &failed);
   dc_stamp(p, kTrGateUp);
   if (!failed && !dc_grid_barrier(p.bar, p.err, ok_s)) failed = true;
   dc_stamp(p, kTrActReady);
 
-  // --------------------------------------------------------------- 5 down
+  // --------------------------------------------------------------- 6 down
   if (!failed) {
-    const int g_lo = c0_dn / gt_dn_i;
-    const int g_hi = nt_dn ? (c0_dn + nt_dn - 1) / gt_dn_i : g_lo - 1;
+    const int g_lo = c0_dn / gt_dn;
+    const int g_hi = nt_dn ? (c0_dn + nt_dn - 1) / gt_dn : g_lo - 1;
     const int nblk = g_hi - g_lo + 1;
     if (nblk > 0)
-      dc_stage(p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, p.inter_pad, 8 * NTB, nblk, T, kb_dn_i, stage, warp,
+      dc_stage(p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, p.inter_pad, 8 * NTB, nblk, T, kb_dn, stage, warp,
                kDcWarps);
     __syncthreads();
-    dc_phase<NTB>(p, smem, ph, 1, stage, nblk > 0 ? nblk : 1, T, g_mask, g_dst, g_lo, rg);
-    failed = __syncthreads_or(rg.failed) != 0;
+    dc_rounds<NTB>(p, smem, st, 1, stage, nblk > 0 ? nblk : 1, g_mask, g_dst, g_lo, &issued, &failed);
   }
   dc_stamp(p, kTrDown);
   if (p.ep_world > 1 && tid == 0) __threadfence_system();   // this CTA's rows to peers, before the barrier
@@ -769,7 +808,7 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   }
   dc_stamp(p, kTrRows);
 
-  // ------------------------------------------------------------ 6 combine
+  // ------------------------------------------------------------ 7 combine
   if (!failed && p.out)
     dc_combine(p, slot_w, p.ep_world > 1 ? reinterpret_cast<const uint16_t *>(ep_peer_s[p.ep_rank] + p.ep_red_off)
                                          : nullptr);
@@ -777,16 +816,19 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
     *reinterpret_cast<volatile unsigned long long *>(p.ep_flags + 2) = ep_calls + 1;
   __syncthreads();
   dc_stamp(p, kTrEnd);
-  // after a failure, the copies still in flight land before the CTA's shared
-  // memory is released (ring indices consumed .. issued-1)
-  if (failed && lane == 0) {
-    for (int j = rg.consumed; j < rg.issued; ++j) mbar_wait_bounded(bar0 + 8 * (j % S), (uint32_t)(j / S) & 1u);
+  // after a failure, the chunks still in flight land before the CTA's shared
+  // memory is released: every slot's last requested chunk is waited for
+  if (failed && tid == 0) {
+#pragma unroll 1
+    for (int j = issued - B > 0 ? issued - B : 0; j < issued; ++j)
+      mbar_wait_bounded(bar0 + 8 * (j % B), (uint32_t)(j / B) & 1u);
   }
 }
 
 // ------------------------------------------------------------------- host --
 struct DcLayout {
-  int stages, round_gu, round_dn, off_stage, off_part, off_tab, off_sel, off_red, off_bar, smem;
+  int chunk_slots, round_units, stage_blk;
+  int off_buf, off_stage, off_part, off_tab, off_sel, off_red, off_bar, smem;
 };
 
 static int dc_max_groups(int T, int k, const MoeOwned &own) {
@@ -794,50 +836,57 @@ static int dc_max_groups(int T, int k, const MoeOwned &own) {
   return (T * k < owned ? T * k : owned) + (own.shared_mask ? 1 : 0);
 }
 
-// Shared-memory layout of one call: the deepest weight ring first; the round
-// partials hold at most the tiles a CTA can get in either phase and shrink
-// before the ring does.
+// Shared-memory layout of one call.  Fixed parts: the staging area (token
+// fragments, or the act fragments of the groups one CTA's down range can
+// touch), the tables, the selection lists, the reduction area.  The rest is
+// split between the unit ring (B chunk slots) and the round partials, a
+// round holding at most B - 1 chunks of units and at least one tile of
+// either phase.
 static bool dc_layout(const rc_moe *m, int T, int k, const MoeOwned &own, DcLayout *L) {
   const int ntb = T <= 8 ? 1 : 2, E = m->n_experts, grid = m->ctx->sm_count;
   const int hidden = m->hidden, inter_pad = m->inter_pad;
-  const int kb_gu = hidden / kUnitK, kb_dn = inter_pad / kUnitK;
+  const int kb_gu = hidden / kUnitK, kb_dn = inter_pad / kUnitK, gt_dn = hidden / kUnitRows;
   const int mg = dc_max_groups(T, k, own);
-  const int per_gu = (mg * (m->inter / 8) + grid - 1) / grid;
-  const int per_dn = (mg * (hidden / kUnitRows) + grid - 1) / grid;
-  // the down range of a CTA touches at most kMoeMaxGroupsPerCta groups
+  const int per_dn = (mg * gt_dn + grid - 1) / grid;
+  int blk = 1 + (per_dn + gt_dn - 2) / gt_dn;              // groups a CTA's down range can touch
+  if (blk > mg) blk = mg > 0 ? mg : 1;
   size_t stage = dc_stage_bytes(1, T, kb_gu);
-  const size_t st_a = dc_stage_bytes(kMoeMaxGroupsPerCta, T, kb_dn);
+  const size_t st_a = dc_stage_bytes(blk, T, kb_dn);
   if (st_a > stage) stage = st_a;
-  const size_t tab = (size_t)(E + 1) * (4 * 8 + 4 + 4 + 4 + 4 * T + 4 + 4) + 16 + 64;
+  const size_t tab = (size_t)(E + 1) * (4 * 8 + 4 * 5 + 4 * T) + 16;
   const size_t sel = (size_t)T * (k + 1) * 4 + (size_t)T * k * 4 * 3;
-  const size_t red = (size_t)kDcRedBytes + kEpMaxRanks * 8 + 2 * sizeof(DcRange);
-  const int unit_part = ntb * 32 * 16;
-  for (int S = kDcMaxStages; S >= 2; --S) {
-    for (int cap = 64 * 1024; cap >= 4 * 1024; cap /= 2) {
-      int R_gu = cap / (kb_gu * unit_part), R_dn = cap / (kb_dn * unit_part);
-      if (R_gu < 1 || R_dn < 1) continue;
-      if (R_gu > per_gu) R_gu = per_gu > 0 ? per_gu : 1;
-      if (R_dn > per_dn) R_dn = per_dn > 0 ? per_dn : 1;
-      const size_t part = (size_t)(R_gu * kb_gu > R_dn * kb_dn ? R_gu * kb_gu : R_dn * kb_dn) * unit_part;
-      size_t off = (size_t)kDcWarps * S * kUnitBytes;
-      const size_t o_stage = off;
-      off += (stage + 15) / 16 * 16;
-      const size_t o_part = off;
-      off += part;
-      const size_t o_tab = off;
-      off += (tab + 15) / 16 * 16;
-      const size_t o_sel = off;
-      off += (sel + 15) / 16 * 16;
-      const size_t o_red = off;
-      off += (red + 15) / 16 * 16;
-      const size_t o_bar = off;
-      off += (size_t)kDcWarps * S * 8;
-      if (off <= (size_t)kGemvSmemLimit) {
-        *L = DcLayout{S, R_gu, R_dn, (int)o_stage, (int)o_part, (int)o_tab, (int)o_sel, (int)o_red, (int)o_bar,
-                      (int)off};
-        return true;
-      }
-    }
+  const size_t red = (size_t)kDcRedBytes + kEpMaxRanks * 8;
+  const size_t pb = (size_t)128 * (dc_qn(T, 0) + (ntb == 2 ? dc_qn(T, 1) : 0));
+  const int need = kb_gu > kb_dn ? kb_gu : kb_dn;           // units of the widest tile
+  const size_t fixed = (stage + 15) / 16 * 16 + (tab + 15) / 16 * 16 + (sel + 15) / 16 * 16 +
+                       (red + 15) / 16 * 16 + (size_t)kDcMaxChunks * 8;
+  if (fixed >= (size_t)kGemvSmemLimit) return false;
+  const size_t rest = (size_t)kGemvSmemLimit - fixed;
+  for (int B = kDcMaxChunks; B >= 2; --B) {
+    const int ru = (B - 1) * kDcChunk;
+    if (ru < need) break;
+    const size_t bytes = (size_t)B * kDcChunk * kUnitBytes + ((size_t)ru * pb + 15) / 16 * 16;
+    if (bytes > rest) continue;
+    // the selection scratch (T*E keys and scores) lives in the unit ring
+    if ((size_t)T * E * 8 > (size_t)B * kDcChunk * kUnitBytes) continue;
+    size_t off = 0;
+    const size_t o_buf = off;
+    off += (size_t)B * kDcChunk * kUnitBytes;
+    const size_t o_stage = off;
+    off += (stage + 15) / 16 * 16;
+    const size_t o_part = off;
+    off += ((size_t)ru * pb + 15) / 16 * 16;
+    const size_t o_tab = off;
+    off += (tab + 15) / 16 * 16;
+    const size_t o_sel = off;
+    off += (sel + 15) / 16 * 16;
+    const size_t o_red = off;
+    off += (red + 15) / 16 * 16;
+    const size_t o_bar = off;
+    off += (size_t)kDcMaxChunks * 8;
+    *L = DcLayout{B, ru, blk, (int)o_buf, (int)o_stage, (int)o_part, (int)o_tab, (int)o_sel, (int)o_red,
+                  (int)o_bar, (int)off};
+    return true;
   }
   return false;
 }
@@ -845,11 +894,7 @@ static bool dc_layout(const rc_moe *m, int T, int k, const MoeOwned &own, DcLayo
 bool moe_decode_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own) {
   if (m->down_fmt != kFormatQ4nx) return false;   // q4nx unit arithmetic only
   DcLayout L;
-  if (!dc_layout(m, T, k, own, &L)) return false;
-  const int max_groups = dc_max_groups(T, k, own);
-  const int gt_dn = m->hidden / kUnitRows;
-  const int per_dn = (max_groups * gt_dn + m->ctx->sm_count - 1) / m->ctx->sm_count;
-  return per_dn - 1 <= (kMoeMaxGroupsPerCta - 1) * gt_dn;
+  return dc_layout(m, T, k, own, &L);
 }
 
 int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling,
@@ -902,9 +947,10 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
   p.act_kind = act;
   p.gate_beta = gb;
   p.value_beta = vb;
-  p.stages = L.stages;
-  p.round_gu = L.round_gu;
-  p.round_dn = L.round_dn;
+  p.chunk_slots = L.chunk_slots;
+  p.round_units = L.round_units;
+  p.stage_blk = L.stage_blk;
+  p.off_buf = L.off_buf;
   p.off_stage = L.off_stage;
   p.off_part = L.off_part;
   p.off_tab = L.off_tab;
@@ -955,8 +1001,8 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
 }
 
 // The persistent decode path of a layer: this kernel (rc_moe_set_fused 1, the
-// default), or the earlier single-phase-per-template kernel of
-// q4nx_moe_fused.cu (2).  Both give the same bytes.
+// default), or the earlier kernel of q4nx_moe_fused.cu (2).  Both give the
+// same bytes.
 bool moe_persistent_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own) {
   return m->fused == 2 ? moe_fused_shape_ok(m, T, k, own) : moe_decode_shape_ok(m, T, k, own);
 }
