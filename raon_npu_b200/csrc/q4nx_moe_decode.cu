@@ -341,29 +341,48 @@ static __device__ __noinline__ void dc_rounds(const DcParams &p, uint8_t *smem, 
     const int t1 = t0 + tiles_per_round < nt ? t0 + tiles_per_round : nt;
     const int nu = (t1 - t0) * kb;
     bool wfail = false;                        // this warp gave up a wait
-    if (!*failed) {
+    if (!*failed && warp < nu) {
+      // unit i = warp + 16 n of the round: (tile, k-block) of the phase, its
+      // group, its chunk and place in the chunk, advanced by 16 units a step
+      // without divisions
+      int u = t0 * kb + warp;
+      int tile_r = u / kb, kbi = u - tile_r * kb;                // tile of the phase range
+      int tg = c0 + tile_r, grp = tg / gt, tin = tg - grp * gt;   // group and tile within it
+      int sidx = base + u, j = sidx / kDcChunk, off = sidx - j * kDcChunk;
+      int slot = j % B;
+      uint32_t par = (uint32_t)(j / B) & 1u;
+      const int dt = kDcWarps / kb, dk = kDcWarps - dt * kb;     // 16 units = dt tiles + dk k-blocks
+      const int dj = kDcWarps / kDcChunk, doff = kDcWarps - dj * kDcChunk;
 #pragma unroll 1
       for (int i = warp; i < nu; i += kDcWarps) {
-        const int u = t0 * kb + i, s = base + u;
-        const int j = s / kDcChunk;
-        if (!mbar_wait_bounded_warp(bar0 + 8 * (j % B), (uint32_t)(j / B) & 1u)) {
+        if (!mbar_wait_bounded_warp(bar0 + 8 * slot, par)) {
           if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
           wfail = true;
           break;
         }
-        const int tg = c0 + u / kb, kbi = u % kb;
-        const int grp = tg / gt;
-        if (st.g_ptr[ph][grp] == nullptr) continue;
-        const int blk = ph ? grp - g_lo : 0;
-        if (blk * kb + kbi != xr_key) {
-          dc_load_frag<NTB>(xr, stage, nblk, T, kb, blk, kbi, lane);
-          xr_key = blk * kb + kbi;
+        if (st.g_ptr[ph][grp] != nullptr) {
+          const int blk = ph ? grp - g_lo : 0;
+          if (blk * kb + kbi != xr_key) {
+            dc_load_frag<NTB>(xr, stage, nblk, T, kb, blk, kbi, lane);
+            xr_key = blk * kb + kbi;
+          }
+          float4 Q[NTB];
+          unit_result<NTB>(buf + ((size_t)slot * kDcChunk + off) * kUnitBytes, xr, lane, Q);
+          float4 *dst = part + (size_t)i * rec;
+          if (qd < qn0) dst[g * qn0 + qd] = Q[0];
+          if (NTB == 2 && qd < qn1) dst[8 * qn0 + g * qn1 + qd] = Q[NTB - 1];
         }
-        float4 Q[NTB];
-        unit_result<NTB>(buf + ((size_t)(j % B) * kDcChunk + s % kDcChunk) * kUnitBytes, xr, lane, Q);
-        float4 *dst = part + (size_t)i * rec;
-        if (qd < qn0) dst[g * qn0 + qd] = Q[0];
-        if (NTB == 2 && qd < qn1) dst[8 * qn0 + g * qn1 + qd] = Q[NTB - 1];
+        // next unit of this warp
+        kbi += dk;
+        int tstep = dt;
+        if (kbi >= kb) kbi -= kb, ++tstep;
+        tin += tstep;
+        while (tin >= gt) tin -= gt, ++grp;
+        off += doff;
+        int cstep = dj;
+        if (off >= kDcChunk) off -= kDcChunk, ++cstep;
+        slot += cstep;
+        while (slot >= B) slot -= B, par ^= 1u;
       }
     }
     // a wait that ran out in any warp stops the phase (CTA-uniform verdict)
@@ -418,30 +437,38 @@ static __device__ __noinline__ void dc_rounds(const DcParams &p, uint8_t *smem, 
     }
     __syncthreads();
     // chunks whose units all lie before this round's end are consumed: their
-    // slots take the next chunks of the stream
-    if (!*failed && threadIdx.x == 0) {
+    // slots take the next chunks of the stream (chunk j by warp j % 16)
+    if (!*failed) {
       const int done = (base + t1 * kb) / kDcChunk;
+      const int hi = done + B < st.nchunk ? done + B : st.nchunk;
+      if (lane == 0) {
 #pragma unroll 1
-      for (; *issued < st.nchunk && *issued < done + B; ++*issued) dc_issue_chunk(st, *issued, buf, bar0, B);
+        for (int jj = *issued + (warp - *issued % kDcWarps + kDcWarps) % kDcWarps; jj < hi; jj += kDcWarps)
+          dc_issue_chunk(st, jj, buf, bar0, B);
+      }
+      if (hi > *issued) *issued = hi;
     }
   }
 }
 
 // ---------------------------------------------------------- routing -----
-// The logits of experts blockIdx.x, + grid, ... for all T tokens: warp w sums
-// the 256-column slices w, w + 16, ... in f64 (exact bf16 products), the CTA
-// adds the warps' sums in warp order and rounds once to f32.  ``wpre`` is the
-// lane's router slice of this CTA's first expert, requested before staging.
-static __device__ __noinline__ void dc_logits(const DcParams &p, double *red, uint4 wpre) {
+// The logits of experts blockIdx.x, + grid, ... for all T tokens, by warps
+// 0 .. nlog-1 (nlog = the 256-column slices, at most 16): warp w sums the
+// slices w, w + nlog, ... in f64 (exact bf16 products), the warps' sums are
+// added in warp order and rounded once to f32.  ``wpre`` is the lane's router
+// slice of this CTA's first expert, requested at kernel entry.  The logit
+// warps meet on named barrier 1; the other warps stage meanwhile.
+static __device__ __noinline__ void dc_logits(const DcParams &p, double *red, uint4 wpre, int nlog) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = p.T, E = p.n_experts, nslice = p.hidden / kUnitK;
+  if (warp >= nlog) return;
 #pragma unroll 1
   for (int e = blockIdx.x; e < E; e += gridDim.x) {
 #pragma unroll 1
     for (int t = 0; t < T; ++t) {
       double acc = 0.0;
 #pragma unroll 1
-      for (int sl = warp; sl < nslice; sl += kDcWarps) {
+      for (int sl = warp; sl < nslice; sl += nlog) {
         const int col = sl * kUnitK + lane * 8;
         const uint4 wv = (e == (int)blockIdx.x && sl == warp)
                              ? wpre : __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
@@ -457,14 +484,14 @@ static __device__ __noinline__ void dc_logits(const DcParams &p, double *red, ui
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
       if (lane == 0) red[warp * kMoeMaxTokens + t] = acc;
     }
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;" ::"r"(nlog * 32) : "memory");
     if (tid < T) {
       double a = 0.0;
 #pragma unroll 1
-      for (int w = 0; w < kDcWarps; ++w) a += red[w * kMoeMaxTokens + tid];
+      for (int w = 0; w < nlog; ++w) a += red[w * kMoeMaxTokens + tid];
       p.logits[(size_t)tid * E + e] = __double2float_rn(a);
     }
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;" ::"r"(nlog * 32) : "memory");
   }
 }
 
@@ -521,37 +548,40 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
     }
   }
   __syncthreads();
-  if (warp < T && lane < k) {
+  if (warp < T) {
+    // lane r < k holds the token's r-th best expert; the weights' sums run
+    // over the ranks in order (shuffles), as a single thread would add them
     const int t = warp, r = lane;
-    const float *ss = sel_sc + t * k;
-    float w;
+    const bool sel = r < k;
+    const int e = sel ? sel_e[t * k + r] : 0x7FFFFFFF;
+    const float sc = sel ? sel_sc[t * k + r] : 0.f;
+    float w, sum = 0.f;
     if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
-      float sum = 0.f;
 #pragma unroll 1
-      for (int r2 = 0; r2 < k; ++r2) sum += ss[r2];
-      w = ss[r];
+      for (int r2 = 0; r2 < k; ++r2) sum += __shfl_sync(0xffffffffu, sc, r2);
+      w = sc;
       if (p.renorm) w = w / (sum + 1e-20f);
       w = w * p.scaling;
     } else {
       // softmax over all experts renormalised over the top-k equals the
       // softmax of the selected scores (the full denominator cancels)
-      const float mx = ss[0];
-      float sum = 0.f;
+      const float ex = expf(sc - __shfl_sync(0xffffffffu, sc, 0));
 #pragma unroll 1
-      for (int r2 = 0; r2 < k; ++r2) sum += expf(ss[r2] - mx);
-      w = expf(ss[r] - mx) / sum;
+      for (int r2 = 0; r2 < k; ++r2) sum += __shfl_sync(0xffffffffu, ex, r2);
+      w = ex / sum;
     }
-    const int e = sel_e[t * k + r];
     int pos = 0;
 #pragma unroll 1
-    for (int r2 = 0; r2 < k; ++r2) pos += sel_e[t * k + r2] < e ? 1 : 0;
-    slots[t * (k + 1) + pos] = e;
-    slot_w[t * k + pos] = w;
-    if (e >= p.own.lo && e < p.own.hi) atomicOr(mask_s + e, 1u << t);
-    if (blockIdx.x == 0) {
-      if (p.ids_out) p.ids_out[t * k + r] = e;
-      if (p.w_out) p.w_out[t * k + r] = w;
-      if (p.slot_w_out) p.slot_w_out[t * k + pos] = w;
+    for (int r2 = 0; r2 < k; ++r2) pos += __shfl_sync(0xffffffffu, e, r2) < e ? 1 : 0;
+    if (sel) {
+      slots[t * (k + 1) + pos] = e;
+      slot_w[t * k + pos] = w;
+      if (e >= p.own.lo && e < p.own.hi) atomicOr(mask_s + e, 1u << t);
+      if (blockIdx.x == 0) {
+        if (p.ids_out) p.ids_out[t * k + r] = e;
+        if (p.w_out) p.w_out[t * k + r] = w;
+        if (p.slot_w_out) p.slot_w_out[t * k + pos] = w;
+      }
     }
     if (r == 0) slots[t * (k + 1) + k] = p.shared_id;
   }
@@ -709,8 +739,16 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   }
 
   // ------------------------------------------- 1 stage, 2 logits
-  dc_stage(p.x, p.hidden, 0, 1, T, kb_gu, stage, warp, kDcWarps);
-  dc_logits(p, reinterpret_cast<double *>(smem + p.off_red), wpre);
+  // warps 0 .. nlog-1 compute the logits while the others stage the tokens
+  // (all warps stage after the logits when the slices take every warp)
+  const int nlog = kb_gu < kDcWarps ? kb_gu : kDcWarps;
+  if (nlog < kDcWarps) {
+    if (warp >= nlog) dc_stage(p.x, p.hidden, 0, 1, T, kb_gu, stage, warp - nlog, kDcWarps - nlog);
+    else dc_logits(p, reinterpret_cast<double *>(smem + p.off_red), wpre, nlog);
+  } else {
+    dc_logits(p, reinterpret_cast<double *>(smem + p.off_red), wpre, nlog);
+    dc_stage(p.x, p.hidden, 0, 1, T, kb_gu, stage, warp, kDcWarps);
+  }
   dc_stamp(p, kTrLogits);
   if (!dc_grid_barrier(p.bar, p.err, ok_s)) return;
   dc_stamp(p, kTrRouted);
@@ -749,14 +787,14 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   st.nchunk = (st.units + kDcChunk - 1) / kDcChunk;
   const int B = p.chunk_slots;
   const uint32_t bar0 = smem_addr(smem + p.off_bar);
-  int issued = 0;                                   // chunks requested (thread 0)
-  __syncthreads();                                  // the selection scratch in the ring is dead
-  if (tid == 0) {
+  if (tid < B) mbar_init(bar0 + 8 * tid, 1);
+  mbar_fence_init();
+  __syncthreads();            // the barriers are initialised; the selection scratch in the ring is dead
+  // chunks requested so far (the same count in every thread); chunk j by warp j % 16
+  int issued = st.nchunk < B ? st.nchunk : B;
+  if (lane == 0) {
 #pragma unroll 1
-    for (int j = 0; j < B; ++j) mbar_init(bar0 + 8 * j, 1);
-    mbar_fence_init();
-#pragma unroll 1
-    for (; issued < st.nchunk && issued < B; ++issued) dc_issue_chunk(st, issued, smem + p.off_buf, bar0, B);
+    for (int j = warp; j < issued; j += kDcWarps) dc_issue_chunk(st, j, smem + p.off_buf, bar0, B);
   }
   // expert parallelism: zero the slot rows other ranks compute
   if (p.zero_foreign) {
@@ -772,7 +810,6 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
       for (int i = tid; i < p.hidden / 8; i += blockDim.x) dst[i] = make_uint4(0, 0, 0, 0);
     }
   }
-  __syncthreads();   // the chunk barriers are initialised before any warp waits on them
   dc_stamp(p, kTrStaged);
 
   // ------------------------------------------------------------ 5 gate/up
