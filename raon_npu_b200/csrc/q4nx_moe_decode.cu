@@ -46,6 +46,9 @@ constexpr int kDcWarps = 16;
 constexpr int kDcThreads = kDcWarps * 32;
 constexpr int kDcChunk = 6;         // units per chunk
 constexpr int kDcMaxChunks = 32;    // chunk slots at most (shared memory decides)
+// dynamic shared memory of one CTA: the opt-in limit less the static copies
+// of the parameters and the stream description
+constexpr int kDcSmemLimit = kGemvSmemLimit - 1024;
 // "red" area: [16 warps][16 tokens] f64 partial logits, the barrier verdict
 // word, then the peer buffer table
 constexpr int kDcRedBytes = kDcWarps * kMoeMaxTokens * 8 + 16;
@@ -319,10 +322,12 @@ __host__ __device__ __forceinline__ int dc_qn(int T, int tb) {
 }
 
 // One phase's rounds (ph 0: gate/up with the GLU epilogue, 1: down).
+// ``issued``: chunks requested so far; returns (chunks requested << 1) | a
+// wait ran out.  ``p`` and ``st`` live in shared memory.
 template <int NTB>
-static __device__ __noinline__ void dc_rounds(const DcParams &p, uint8_t *smem, const DcStream &st, int ph,
-                                              const uint8_t *stage, int nblk, const uint32_t *g_mask,
-                                              const int *g_dst, int g_lo, int *issued, bool *failed) {
+static __device__ __noinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const DcStream &st, int ph,
+                                             const uint8_t *stage, int nblk, const uint32_t *g_mask,
+                                             const int *g_dst, int g_lo, int issued, bool failed) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, T = p.T;
   uint8_t *const *ep_peer_s = reinterpret_cast<uint8_t *const *>(smem + p.off_red + kDcRedBytes);
   uint8_t *buf = smem + p.off_buf;
@@ -341,7 +346,7 @@ static __device__ __noinline__ void dc_rounds(const DcParams &p, uint8_t *smem, 
     const int t1 = t0 + tiles_per_round < nt ? t0 + tiles_per_round : nt;
     const int nu = (t1 - t0) * kb;
     bool wfail = false;                        // this warp gave up a wait
-    if (!*failed && warp < nu) {
+    if (!failed && warp < nu) {
       // unit i = warp + 16 n of the round: (tile, k-block) of the phase, its
       // group, its chunk and place in the chunk, advanced by 16 units a step
       // without divisions
@@ -386,8 +391,8 @@ static __device__ __noinline__ void dc_rounds(const DcParams &p, uint8_t *smem, 
       }
     }
     // a wait that ran out in any warp stops the phase (CTA-uniform verdict)
-    if (__syncthreads_or(wfail)) *failed = true;
-    if (!*failed) {
+    if (__syncthreads_or(wfail)) failed = true;
+    if (!failed) {
       // a tile is the sum of its units' results in k-block order
 #pragma unroll 1
       for (int ti = t0 + warp; ti < t1; ti += kDcWarps) {
@@ -438,17 +443,18 @@ static __device__ __noinline__ void dc_rounds(const DcParams &p, uint8_t *smem, 
     __syncthreads();
     // chunks whose units all lie before this round's end are consumed: their
     // slots take the next chunks of the stream (chunk j by warp j % 16)
-    if (!*failed) {
+    if (!failed) {
       const int done = (base + t1 * kb) / kDcChunk;
       const int hi = done + B < st.nchunk ? done + B : st.nchunk;
       if (lane == 0) {
 #pragma unroll 1
-        for (int jj = *issued + (warp - *issued % kDcWarps + kDcWarps) % kDcWarps; jj < hi; jj += kDcWarps)
+        for (int jj = issued + (warp - issued % kDcWarps + kDcWarps) % kDcWarps; jj < hi; jj += kDcWarps)
           dc_issue_chunk(st, jj, buf, bar0, B);
       }
-      if (hi > *issued) *issued = hi;
+      if (hi > issued) issued = hi;
     }
   }
+  return (issued << 1) | (failed ? 1 : 0);
 }
 
 // ---------------------------------------------------------- routing -----
@@ -673,8 +679,14 @@ static __device__ __noinline__ void dc_combine(const DcParams &p, const float *s
 
 // ------------------------------------------------------------- kernel ---
 template <int NTB>
-__global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p) {
+__global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p_arg) {
   extern __shared__ __align__(128) uint8_t smem[];
+  // the parameters and the stream description are read by out-of-line
+  // functions: shared-memory copies keep them off the thread stacks
+  __shared__ DcParams p;
+  __shared__ DcStream st;
+  if (threadIdx.x == 0) p = p_arg;
+  __syncthreads();
   int *ok_s = reinterpret_cast<int *>(smem + p.off_red + kDcWarps * kMoeMaxTokens * 8);
   uint8_t **ep_peer_s = reinterpret_cast<uint8_t **>(smem + p.off_red + kDcRedBytes);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -771,27 +783,29 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   const int c0_gu = blockIdx.x * per_gu, c0_dn = blockIdx.x * per_dn;
   const int nt_gu = c0_gu < tot_gu ? (c0_gu + per_gu < tot_gu ? per_gu : tot_gu - c0_gu) : 0;
   const int nt_dn = c0_dn < tot_dn ? (c0_dn + per_dn < tot_dn ? per_dn : tot_dn - c0_dn) : 0;
-  DcStream st;
-  st.g_ptr[0] = g_gu;
-  st.g_ptr[1] = g_dn;
-  st.c0[0] = c0_gu;
-  st.c0[1] = c0_dn;
-  st.nt[0] = nt_gu;
-  st.nt[1] = nt_dn;
-  st.kb[0] = kb_gu;
-  st.kb[1] = kb_dn;
-  st.gt[0] = gt_gu;
-  st.gt[1] = gt_dn;
-  st.units0 = nt_gu * kb_gu;
-  st.units = st.units0 + nt_dn * kb_dn;
-  st.nchunk = (st.units + kDcChunk - 1) / kDcChunk;
+  if (tid == 0) {
+    st.g_ptr[0] = g_gu;
+    st.g_ptr[1] = g_dn;
+    st.c0[0] = c0_gu;
+    st.c0[1] = c0_dn;
+    st.nt[0] = nt_gu;
+    st.nt[1] = nt_dn;
+    st.kb[0] = kb_gu;
+    st.kb[1] = kb_dn;
+    st.gt[0] = gt_gu;
+    st.gt[1] = gt_dn;
+    st.units0 = nt_gu * kb_gu;
+    st.units = st.units0 + nt_dn * kb_dn;
+    st.nchunk = (st.units + kDcChunk - 1) / kDcChunk;
+  }
   const int B = p.chunk_slots;
   const uint32_t bar0 = smem_addr(smem + p.off_bar);
   if (tid < B) mbar_init(bar0 + 8 * tid, 1);
   mbar_fence_init();
   __syncthreads();            // the barriers are initialised; the selection scratch in the ring is dead
   // chunks requested so far (the same count in every thread); chunk j by warp j % 16
-  int issued = st.nchunk < B ? st.nchunk : B;
+  const int nchunk = (nt_gu * kb_gu + nt_dn * kb_dn + kDcChunk - 1) / kDcChunk;
+  int issued = nchunk < B ? nchunk : B;
   if (lane == 0) {
 #pragma unroll 1
     for (int j = warp; j < issued; j += kDcWarps) dc_issue_chunk(st, j, smem + p.off_buf, bar0, B);
@@ -814,7 +828,9 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
 
   // ------------------------------------------------------------ 5 gate/up
   bool failed = false;
-  dc_rounds<NTB>(p, smem, st, 0, stage, 1, g_mask, g_dst, 0, &issued, &failed);
+  int rv = dc_rounds<NTB>(p, smem, st, 0, stage, 1, g_mask, g_dst, 0, issued, failed);
+  issued = rv >> 1;
+  failed = (rv & 1) != 0;
   dc_stamp(p, kTrGateUp);
   if (!failed && !dc_grid_barrier(p.bar, p.err, ok_s)) failed = true;
   dc_stamp(p, kTrActReady);
@@ -828,7 +844,9 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
       dc_stage(p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, p.inter_pad, 8 * NTB, nblk, T, kb_dn, stage, warp,
                kDcWarps);
     __syncthreads();
-    dc_rounds<NTB>(p, smem, st, 1, stage, nblk > 0 ? nblk : 1, g_mask, g_dst, g_lo, &issued, &failed);
+    rv = dc_rounds<NTB>(p, smem, st, 1, stage, nblk > 0 ? nblk : 1, g_mask, g_dst, g_lo, issued, failed);
+    issued = rv >> 1;
+    failed = (rv & 1) != 0;
   }
   dc_stamp(p, kTrDown);
   if (p.ep_world > 1 && tid == 0) __threadfence_system();   // this CTA's rows to peers, before the barrier
@@ -897,8 +915,8 @@ static bool dc_layout(const rc_moe *m, int T, int k, const MoeOwned &own, DcLayo
   const int need = kb_gu > kb_dn ? kb_gu : kb_dn;           // units of the widest tile
   const size_t fixed = (stage + 15) / 16 * 16 + (tab + 15) / 16 * 16 + (sel + 15) / 16 * 16 +
                        (red + 15) / 16 * 16 + (size_t)kDcMaxChunks * 8;
-  if (fixed >= (size_t)kGemvSmemLimit) return false;
-  const size_t rest = (size_t)kGemvSmemLimit - fixed;
+  if (fixed >= (size_t)kDcSmemLimit) return false;
+  const size_t rest = (size_t)kDcSmemLimit - fixed;
   for (int B = kDcMaxChunks; B >= 2; --B) {
     const int ru = (B - 1) * kDcChunk;
     if (ru < need) break;
@@ -1014,10 +1032,10 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
   if (dev >= 64 || !configured[dev][ntb - 1]) {
     if (ntb == 1)
       RC_CUDA_TRY(cudaFuncSetAttribute(rc_moe_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kGemvSmemLimit));
+                                       kDcSmemLimit));
     else
       RC_CUDA_TRY(cudaFuncSetAttribute(rc_moe_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kGemvSmemLimit));
+                                       kDcSmemLimit));
     if (dev < 64) configured[dev][ntb - 1] = true;
   }
   cudaLaunchConfig_t cfg = {};
