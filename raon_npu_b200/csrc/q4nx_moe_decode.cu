@@ -310,7 +310,7 @@ static __device__ __noinline__ void dc_issue_chunk(const DcStream &st, int j, ui
   }
 }
 
-static __device__ __noinline__ float dc_glu(float gate, float up, int kind, float gb, float vb) {
+__device__ __forceinline__ float dc_glu(float gate, float up, int kind, float gb, float vb) {
   return kind == RC_ACT_SITU ? act_situ(gate, up, gb, vb) : act_swiglu(gate, up);
 }
 
@@ -325,7 +325,7 @@ __host__ __device__ __forceinline__ int dc_qn(int T, int tb) {
 // ``issued``: chunks requested so far; returns (chunks requested << 1) | a
 // wait ran out.  ``p`` and ``st`` live in shared memory.
 template <int NTB>
-static __device__ __noinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const DcStream &st, int ph,
+__device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const DcStream &st, int ph,
                                              const uint8_t *stage, int nblk, const uint32_t *g_mask,
                                              const int *g_dst, int g_lo, int issued, bool failed) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, T = p.T;
@@ -503,10 +503,9 @@ static __device__ __noinline__ void dc_logits(const DcParams &p, double *red, ui
 
 // Selection by the whole CTA: every (token, expert) pair counts the experts
 // ahead of it in router order (a larger key, or an equal key and a lower
-// index); the pairs ranked below k are the top-k, best first.  Four threads
-// share a pair when there are few pairs.  Then per token (warp t, lane r < k)
-// the weight, the ascending-ID slot position and the expert's token mask.
-// ``scratch`` holds T*E keys and scores.
+// index); the pairs ranked below k are the top-k, best first.  Then per token
+// (warp t, lane r < k) the weight, the ascending-ID slot position and the
+// expert's token mask.  ``scratch`` holds T*E keys and scores.
 static __device__ __noinline__ void dc_select(const DcParams &p, const float *bias_s, uint8_t *scratch,
                                               int32_t *slots, float *slot_w, int32_t *sel_e, float *sel_sc,
                                               uint32_t *mask_s) {
@@ -530,27 +529,29 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
     key_s[i] = dc_route_key(v);
   }
   __syncthreads();
-  const int sub = n * 4 <= kDcThreads ? 4 : 1;           // threads per pair
-  const int per = (E + sub - 1) / sub;
+  // ranks: warp w takes the candidates (t, c) with c = w, w + 16, ...; the
+  // lanes hold token t's keys (lane l: experts l, l + 32, ...), each lane
+  // counts the keys ahead of the candidate, one warp sum gives its rank
 #pragma unroll 1
-  for (int i0 = tid / sub; i0 < n; i0 += kDcThreads / sub) {
-    const int t = i0 / E, e = i0 - t * E, part = tid - (tid / sub) * sub;
-    const uint32_t my = key_s[i0];
+  for (int t = 0; t < T; ++t) {
     const uint32_t *kr = key_s + t * E;
-    const int lo = part * per, hi = lo + per < E ? lo + per : E;
-    int rank = 0;
-#pragma unroll 4
-    for (int e2 = lo; e2 < hi; ++e2) {
-      const uint32_t o = kr[e2];
-      rank += (o > my || (o == my && e2 < e)) ? 1 : 0;
-    }
-    if (sub == 4) {
-      rank += __shfl_xor_sync(0xffffffffu, rank, 1);
-      rank += __shfl_xor_sync(0xffffffffu, rank, 2);
-    }
-    if (rank < k && part == 0) {
-      sel_e[t * k + rank] = e;
-      sel_sc[t * k + rank] = sc_s[i0];
+    uint32_t kk[kMoeMaxExperts / 32];
+#pragma unroll
+    for (int m = 0; m < kMoeMaxExperts / 32; ++m) kk[m] = m * 32 + lane < E ? kr[m * 32 + lane] : 0u;
+#pragma unroll 2
+    for (int c = warp; c < E; c += kDcWarps) {
+      const uint32_t kc = kr[c];
+      int cnt = 0;
+#pragma unroll
+      for (int m = 0; m < kMoeMaxExperts / 32; ++m) {
+        const int e2 = m * 32 + lane;
+        cnt += (e2 < E && (kk[m] > kc || (kk[m] == kc && e2 < c))) ? 1 : 0;
+      }
+      const int rank = (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
+      if (rank < k && lane == 0) {
+        sel_e[t * k + rank] = c;
+        sel_sc[t * k + rank] = sc_s[t * E + c];
+      }
     }
   }
   __syncthreads();
@@ -634,34 +635,41 @@ static __device__ __noinline__ void dc_groups(const DcParams &p, const int32_t *
 }
 
 // ascending-ID f32 combine (product rounded, then sum rounded) of the slot
-// rows of token t, RTNE, then RTNE(routed + shared)
+// rows of token t, RTNE, then RTNE(routed + shared).  Item i (8 columns of
+// one token) goes to CTA i % grid, so every CTA takes a few; a thread
+// requests all k + 1 slot rows before it sums them.
 static __device__ __noinline__ void dc_combine(const DcParams &p, const float *slot_w, const uint16_t *ep_rows) {
   const int k = p.k, vecs = p.hidden / 8;
   const bool with_shared = p.shared_id >= 0 && p.own.shared_mask;
   const bool ep = p.ep_world > 1;
   const int n_out = ep ? p.ep_M : p.T;
 #pragma unroll 1
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_out * vecs; i += gridDim.x * blockDim.x) {
+  for (int i = blockIdx.x + threadIdx.x * gridDim.x; i < n_out * vecs; i += gridDim.x * blockDim.x) {
     const int to = i / vecs, v = i - to * vecs;
     const int t = ep ? p.ep_rank * p.ep_M + to : to;
     const uint16_t *rows = (ep ? ep_rows + (size_t)to * (k + 1) * p.hidden
                                : p.slot_rows + (size_t)t * (k + 1) * p.hidden) + (size_t)v * 8;
+    uint4 r[kMoeMaxK];
+#pragma unroll
+    for (int s = 0; s < kMoeMaxK; ++s)
+      r[s] = s < k ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)s * p.hidden)) : make_uint4(0, 0, 0, 0);
+    const uint4 sh = with_shared ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)k * p.hidden))
+                                 : make_uint4(0, 0, 0, 0);
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-#pragma unroll 1
-    for (int s = 0; s < k; ++s) {
-      const uint4 r = __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)s * p.hidden));
-      const float w = slot_w[t * k + s];
-      const uint32_t q[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(bf16_to_f32(q[j] & 0xFFFFu), w));
-        acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(bf16_to_f32(q[j] >> 16), w));
+    for (int s = 0; s < kMoeMaxK; ++s) {
+      if (s < k) {
+        const float w = slot_w[t * k + s];
+        const uint32_t q[4] = {r[s].x, r[s].y, r[s].z, r[s].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(bf16_to_f32(q[j] & 0xFFFFu), w));
+          acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(bf16_to_f32(q[j] >> 16), w));
+        }
       }
     }
-    const uint4 sh = with_shared ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)k * p.hidden))
-                                 : make_uint4(0, 0, 0, 0);
     const uint32_t shw[4] = {sh.x, sh.y, sh.z, sh.w};
     uint32_t o[4];
 #pragma unroll
@@ -804,8 +812,10 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   mbar_fence_init();
   __syncthreads();            // the barriers are initialised; the selection scratch in the ring is dead
   // chunks requested so far (the same count in every thread); chunk j by warp j % 16
-  const int nchunk = (nt_gu * kb_gu + nt_dn * kb_dn + kDcChunk - 1) / kDcChunk;
-  int issued = nchunk < B ? nchunk : B;
+  // the gate/up chunks are requested first (they are needed first); the down
+  // chunks follow when the gate/up round ends
+  const int nchunk_gu = (nt_gu * kb_gu + kDcChunk - 1) / kDcChunk;
+  int issued = nchunk_gu < B ? nchunk_gu : B;
   if (lane == 0) {
 #pragma unroll 1
     for (int j = warp; j < issued; j += kDcWarps) dc_issue_chunk(st, j, smem + p.off_buf, bar0, B);
