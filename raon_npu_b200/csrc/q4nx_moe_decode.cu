@@ -310,6 +310,21 @@ static __device__ __noinline__ void dc_issue_chunk(const DcStream &st, int j, ui
   }
 }
 
+// Request the chunks whose slots are free once the stream's first ``done``
+// chunks are consumed (chunk j by lane 0 of warp j % 16).  Returns the new
+// count of requested chunks (the same in every thread).
+__device__ __forceinline__ int dc_refill(const DcStream &st, int issued, int done, uint8_t *buf, uint32_t bar0,
+                                         int B) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hi = done + B < st.nchunk ? done + B : st.nchunk;
+  if (lane == 0) {
+#pragma unroll 1
+    for (int j = issued + (warp - issued % kDcWarps + kDcWarps) % kDcWarps; j < hi; j += kDcWarps)
+      dc_issue_chunk(st, j, buf, bar0, B);
+  }
+  return hi > issued ? hi : issued;
+}
+
 __device__ __forceinline__ float dc_glu(float gate, float up, int kind, float gb, float vb) {
   return kind == RC_ACT_SITU ? act_situ(gate, up, gb, vb) : act_swiglu(gate, up);
 }
@@ -443,16 +458,7 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
     __syncthreads();
     // chunks whose units all lie before this round's end are consumed: their
     // slots take the next chunks of the stream (chunk j by warp j % 16)
-    if (!failed) {
-      const int done = (base + t1 * kb) / kDcChunk;
-      const int hi = done + B < st.nchunk ? done + B : st.nchunk;
-      if (lane == 0) {
-#pragma unroll 1
-        for (int jj = issued + (warp - issued % kDcWarps + kDcWarps) % kDcWarps; jj < hi; jj += kDcWarps)
-          dc_issue_chunk(st, jj, buf, bar0, B);
-      }
-      if (hi > issued) issued = hi;
-    }
+    if (!failed) issued = dc_refill(st, issued, (base + t1 * kb) / kDcChunk, buf, bar0, B);
   }
   return (issued << 1) | (failed ? 1 : 0);
 }
@@ -841,6 +847,9 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   int rv = dc_rounds<NTB>(p, smem, st, 0, stage, 1, g_mask, g_dst, 0, issued, failed);
   issued = rv >> 1;
   failed = (rv & 1) != 0;
+  // every gate/up unit is consumed (also in a CTA without gate/up tiles): the
+  // down chunks take the free slots
+  if (!failed) issued = dc_refill(st, issued, st.units0 / kDcChunk, smem + p.off_buf, bar0, B);
   dc_stamp(p, kTrGateUp);
   if (!failed && !dc_grid_barrier(p.bar, p.err, ok_s)) failed = true;
   dc_stamp(p, kTrActReady);
