@@ -804,26 +804,26 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
             eps[li].decode(xs[li], outs[li])
     torch.cuda.synchronize()
     ctx.sync()
-    graphs, graph_err = [], None
+
+    # The timed steps run as one CUDA graph of args.steps consecutive layer
+    # decodes (step s decodes layer s % n_layers), as a decode step runs its
+    # layers back to back; warm-up replays the same graph.
+    def steps_fn():
+        for s_ in range(args.steps):
+            eps[s_ % n_layers].decode(xs[s_ % n_layers], outs[s_ % n_layers])
+    graph, graph_err = None, None
     try:
-        for li in range(n_layers):
-            graphs.append(capture_graph(torch, lambda li=li: eps[li].decode(xs[li], outs[li])))
+        graph = capture_graph(torch, steps_fn)
     except Exception as e:                  # noqa: BLE001 - reported in the JSON line
-        graphs, graph_err = [], f"{type(e).__name__}: {e}"[:200]
-    ok = torch.tensor([1 if graphs else 0], dtype=torch.int32, device=dev)
+        graph, graph_err = None, f"{type(e).__name__}: {e}"[:200]
+    ok = torch.tensor([1 if graph is not None else 0], dtype=torch.int32, device=dev)
     if world > 1:
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     if not int(ok.item()):
-        graphs = []
-
-    def step(s):
-        li = s % n_layers
-        if graphs:
-            graphs[li].replay()
-        else:
-            eps[li].decode(xs[li], outs[li])
-    for s in range(args.warmup * n_layers):
-        step(s)
+        graph = None
+    run_steps = graph.replay if graph is not None else steps_fn
+    for _ in range(max(1, -(-args.warmup // args.steps))):
+        run_steps()
     torch.cuda.synchronize()
     ctx.sync()
     barrier()
@@ -836,14 +836,13 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for s in range(args.steps):
-        step(s)
+    run_steps()
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
     ms_max = _max_over_ranks(torch, dist, dev, world, e0.elapsed_time(e1) / args.steps)
-    del graphs
+    del graph
     ctx.sync()
 
     # Algorithmic bytes of each step on this rank: the packed weights of the
@@ -906,7 +905,8 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
                    "l2": "steps rotate over %d distinct layers; a layer's %.1f MB of experts return after "
                          "%.0f MB of other layers' (> L2 126 MB)" % (n_layers, touched / 1e6,
                                                                       (n_layers - 1) * touched / 1e6),
-                   "cuda_graph": bool(int(ok.item())), "graph_error": graph_err},
+                   "cuda_graph": bool(int(ok.item())), "graph_error": graph_err,
+                   "timing": "one CUDA graph of the K timed layer decodes, back to back"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": MEASURED_TRAFFIC["moe_layer_t1"] if world == 1 and M == 1 else None,

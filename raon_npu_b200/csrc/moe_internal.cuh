@@ -102,6 +102,7 @@ struct rc_moe {
   int fused;                  // decode through the single persistent kernel when the shape fits
   unsigned long long *fz_bar; // grid-barrier arrival count of the fused kernel (only grows)
   unsigned fz_epoch;          // ctx->timeout_epoch when fz_bar was last known consistent
+  int *dc_cols;               // [hidden/16] down tiles written per output column tile (zero between calls)
   rc::MoeEp *ep;              // peer-memory expert parallelism (null until rc_moe_ep_init)
   int prefill_kernel;         // RC_PREFILL_GEMV (register fragments) or RC_PREFILL_TCGEN05
   int down_fmt;               // kFormatQ4nx or kFormatBfp16 (RC_UPLOAD_DOWN_BFP16), one for every expert

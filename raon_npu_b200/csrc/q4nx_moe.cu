@@ -928,6 +928,7 @@ int rc_moe_destroy(rc_moe *m) {
   cudaFree(m->act);
   cudaFree(m->down_out);
   cudaFree(m->fz_bar);
+  cudaFree(m->dc_cols);
   ep_release(m);
   delete m;
   return RC_OK;

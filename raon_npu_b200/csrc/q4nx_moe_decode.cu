@@ -79,6 +79,7 @@ struct DcParams {
   int stage_blk;                     // act blocks (groups) the staging area holds
   int off_buf, off_stage, off_part, off_tab, off_sel, off_red, off_bar;
   unsigned long long *bar;           // grid-barrier arrival count (only grows)
+  int *cols;                         // [hidden/16] down tiles written per column tile (zero between calls)
   int *err;
   int ep_world, ep_rank, ep_M;
   uint8_t *const *ep_peer;
@@ -310,6 +311,51 @@ static __device__ __noinline__ void dc_issue_chunk(const DcStream &st, int j, ui
   }
 }
 
+// Eight columns of one token: ascending-ID f32 sum (product rounded, then
+// sum rounded) of the k slot rows at ``rows`` (stride ``hidden``) with the
+// weights ``w``, RTNE, then RTNE(routed + shared row k) when with_shared.
+__device__ __forceinline__ uint4 dc_combine8(const uint16_t *rows, int hidden, int k, const float *w,
+                                             bool with_shared) {
+  const uint4 sh = with_shared ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)k * hidden))
+                               : make_uint4(0, 0, 0, 0);
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  // rows in batches of eight, all of a batch requested before any is summed
+#pragma unroll 1
+  for (int s0 = 0; s0 < k; s0 += 8) {
+    uint4 r[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+      r[s] = s0 + s < k ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)(s0 + s) * hidden))
+                        : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      if (s0 + s < k) {
+        const float ws = w[s0 + s];
+        const uint32_t q[4] = {r[s].x, r[s].y, r[s].z, r[s].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(bf16_to_f32(q[j] & 0xFFFFu), ws));
+          acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(bf16_to_f32(q[j] >> 16), ws));
+        }
+      }
+    }
+  }
+  const uint32_t shw[4] = {sh.x, sh.y, sh.z, sh.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t lo = f32_to_bf16_rne(acc[2 * j]), hi = f32_to_bf16_rne(acc[2 * j + 1]);
+    if (with_shared) {
+      lo = f32_to_bf16_rne(bf16_to_f32(lo) + bf16_to_f32(shw[j] & 0xFFFFu));
+      hi = f32_to_bf16_rne(bf16_to_f32(hi) + bf16_to_f32(shw[j] >> 16));
+    }
+    o[j] = lo | (hi << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // Request the chunks whose slots are free once the stream's first ``done``
 // chunks are consumed (chunk j by lane 0 of warp j % 16).  Returns the new
 // count of requested chunks (the same in every thread).
@@ -339,10 +385,15 @@ __host__ __device__ __forceinline__ int dc_qn(int T, int tb) {
 // One phase's rounds (ph 0: gate/up with the GLU epilogue, 1: down).
 // ``issued``: chunks requested so far; returns (chunks requested << 1) | a
 // wait ran out.  ``p`` and ``st`` live in shared memory.
+// On one GPU the down phase also combines: the warp that writes the last
+// down tile of an output column tile (column counter ``p.cols``, one
+// arrival per group) sums that column tile of every token (``ng`` groups,
+// slot weights ``slot_w``) and clears the counter for the next call.
 template <int NTB>
 __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const DcStream &st, int ph,
-                                             const uint8_t *stage, int nblk, const uint32_t *g_mask,
-                                             const int *g_dst, int g_lo, int issued, bool failed) {
+                                         const uint8_t *stage, int nblk, const uint32_t *g_mask,
+                                         const int *g_dst, int g_lo, int issued, bool failed, int ng,
+                                         const float *slot_w) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, T = p.T;
   uint8_t *const *ep_peer_s = reinterpret_cast<uint8_t *const *>(smem + p.off_red + kDcRedBytes);
   uint8_t *buf = smem + p.off_buf;
@@ -451,6 +502,27 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
               y[0] = live ? f32_to_bf16_rne(acc.v[tb][e2]) : (uint16_t)0;
               y[8] = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : (uint16_t)0;
             }
+          }
+        }
+        if (ph == 1 && p.ep_world <= 1 && p.out) {
+          // the last writer of column tile ``tile`` combines it (threadfence
+          // reduction: stores, fence, count; the last counter sees them all)
+          __syncwarp();
+          int old = 0;
+          if (lane == 0) {
+            __threadfence();
+            old = atomicAdd(p.cols + tile, 1);
+          }
+          old = __shfl_sync(0xffffffffu, old, 0);
+          if (old == ng - 1) {
+            __threadfence();
+            const int t = lane >> 1, h = lane & 1;
+            if (t < T) {
+              const uint16_t *rows = p.slot_rows + (size_t)t * (p.k + 1) * p.hidden + tile * kUnitRows + h * 8;
+              *reinterpret_cast<uint4 *>(p.out + (size_t)t * p.hidden + tile * kUnitRows + h * 8) =
+                  dc_combine8(rows, p.hidden, p.k, slot_w + t * p.k, p.shared_id >= 0 && p.own.shared_mask);
+            }
+            if (lane == 0) p.cols[tile] = 0;
           }
         }
       }
@@ -655,39 +727,8 @@ static __device__ __noinline__ void dc_combine(const DcParams &p, const float *s
     const int t = ep ? p.ep_rank * p.ep_M + to : to;
     const uint16_t *rows = (ep ? ep_rows + (size_t)to * (k + 1) * p.hidden
                                : p.slot_rows + (size_t)t * (k + 1) * p.hidden) + (size_t)v * 8;
-    uint4 r[kMoeMaxK];
-#pragma unroll
-    for (int s = 0; s < kMoeMaxK; ++s)
-      r[s] = s < k ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)s * p.hidden)) : make_uint4(0, 0, 0, 0);
-    const uint4 sh = with_shared ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)k * p.hidden))
-                                 : make_uint4(0, 0, 0, 0);
-    float acc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-#pragma unroll
-    for (int s = 0; s < kMoeMaxK; ++s) {
-      if (s < k) {
-        const float w = slot_w[t * k + s];
-        const uint32_t q[4] = {r[s].x, r[s].y, r[s].z, r[s].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(bf16_to_f32(q[j] & 0xFFFFu), w));
-          acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(bf16_to_f32(q[j] >> 16), w));
-        }
-      }
-    }
-    const uint32_t shw[4] = {sh.x, sh.y, sh.z, sh.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t lo = f32_to_bf16_rne(acc[2 * j]), hi = f32_to_bf16_rne(acc[2 * j + 1]);
-      if (with_shared) {
-        lo = f32_to_bf16_rne(bf16_to_f32(lo) + bf16_to_f32(shw[j] & 0xFFFFu));
-        hi = f32_to_bf16_rne(bf16_to_f32(hi) + bf16_to_f32(shw[j] >> 16));
-      }
-      o[j] = lo | (hi << 16);
-    }
-    *reinterpret_cast<uint4 *>(p.out + (size_t)to * p.hidden + (size_t)v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4 *>(p.out + (size_t)to * p.hidden + (size_t)v * 8) =
+        dc_combine8(rows, p.hidden, k, slot_w + t * k, with_shared);
   }
 }
 
@@ -715,6 +756,16 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   uint4 wpre = make_uint4(0, 0, 0, 0);
   if ((int)blockIdx.x < E && warp < p.hidden / kUnitK)
     wpre = __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)blockIdx.x * p.hidden + warp * kUnitK + lane * 8));
+
+  // The shared expert's weights do not depend on the routing: each CTA asks
+  // L2 for its share of them now, so the stream finds them there.
+  if (tid == 0 && p.shared_id >= 0 && p.own.shared_mask && p.gu_tiles[E] != nullptr) {
+    const size_t gu_units = (size_t)gt_gu * kb_gu, dn_units = (size_t)gt_dn * kb_dn;
+    const size_t a0 = gu_units * blockIdx.x / gridDim.x, a1 = gu_units * (blockIdx.x + 1) / gridDim.x;
+    const size_t b0 = dn_units * blockIdx.x / gridDim.x, b1 = dn_units * (blockIdx.x + 1) / gridDim.x;
+    if (a1 > a0) bulk_prefetch_l2(p.gu_tiles[E] + a0 * kUnitBytes, (uint32_t)((a1 - a0) * kUnitBytes));
+    if (b1 > b0) bulk_prefetch_l2(p.dn_tiles[E] + b0 * kUnitBytes, (uint32_t)((b1 - b0) * kUnitBytes));
+  }
 
   // ---- expert parallelism: every rank's token rows into every rank's buffer
   unsigned long long ep_calls = 0;
@@ -844,7 +895,7 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
 
   // ------------------------------------------------------------ 5 gate/up
   bool failed = false;
-  int rv = dc_rounds<NTB>(p, smem, st, 0, stage, 1, g_mask, g_dst, 0, issued, failed);
+  int rv = dc_rounds<NTB>(p, smem, st, 0, stage, 1, g_mask, g_dst, 0, issued, failed, ng, slot_w);
   issued = rv >> 1;
   failed = (rv & 1) != 0;
   // every gate/up unit is consumed (also in a CTA without gate/up tiles): the
@@ -863,29 +914,33 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
       dc_stage(p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, p.inter_pad, 8 * NTB, nblk, T, kb_dn, stage, warp,
                kDcWarps);
     __syncthreads();
-    rv = dc_rounds<NTB>(p, smem, st, 1, stage, nblk > 0 ? nblk : 1, g_mask, g_dst, g_lo, issued, failed);
+    rv = dc_rounds<NTB>(p, smem, st, 1, stage, nblk > 0 ? nblk : 1, g_mask, g_dst, g_lo, issued, failed, ng,
+                        slot_w);
     issued = rv >> 1;
     failed = (rv & 1) != 0;
   }
   dc_stamp(p, kTrDown);
-  if (p.ep_world > 1 && tid == 0) __threadfence_system();   // this CTA's rows to peers, before the barrier
-  if (!failed && !dc_grid_barrier(p.bar, p.err, ok_s)) failed = true;
-  if (p.ep_world > 1 && !failed) {
-    // every rank's rows for this rank's tokens have been written once every
-    // rank has passed its own barrier and signalled
-    if (blockIdx.x == 0 && tid == 0) {
-      __threadfence_system();
-      for (int r = 0; r < p.ep_world; ++r)
-        red_add_release_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r]) + 1, 1ull);
+  if (p.ep_world > 1) {
+    // expert parallelism: every rank's rows for this rank's tokens have been
+    // written once every rank has passed its own barrier and signalled; then
+    // the grid combines this rank's tokens
+    if (tid == 0) __threadfence_system();   // this CTA's rows to peers, before the barrier
+    if (!failed && !dc_grid_barrier(p.bar, p.err, ok_s)) failed = true;
+    if (!failed) {
+      if (blockIdx.x == 0 && tid == 0) {
+        __threadfence_system();
+        for (int r = 0; r < p.ep_world; ++r)
+          red_add_release_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r]) + 1, 1ull);
+      }
+      if (!dc_wait_sys(p.ep_flags + 1, (ep_calls + 1) * p.ep_world, p.err, ok_s)) failed = true;
     }
-    if (!dc_wait_sys(p.ep_flags + 1, (ep_calls + 1) * p.ep_world, p.err, ok_s)) failed = true;
+    dc_stamp(p, kTrRows);
+    if (!failed && p.out)
+      dc_combine(p, slot_w, reinterpret_cast<const uint16_t *>(ep_peer_s[p.ep_rank] + p.ep_red_off));
+  } else {
+    // one GPU: the down phase combined each column tile as its last tile was written
+    dc_stamp(p, kTrRows);
   }
-  dc_stamp(p, kTrRows);
-
-  // ------------------------------------------------------------ 7 combine
-  if (!failed && p.out)
-    dc_combine(p, slot_w, p.ep_world > 1 ? reinterpret_cast<const uint16_t *>(ep_peer_s[p.ep_rank] + p.ep_red_off)
-                                         : nullptr);
   if (p.ep_world > 1 && !failed && blockIdx.x == 0 && tid == 0)
     *reinterpret_cast<volatile unsigned long long *>(p.ep_flags + 2) = ep_calls + 1;
   __syncthreads();
@@ -982,15 +1037,21 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
     return RC_ERR_INVALID;
   }
   rc_ctx *ctx = m->ctx;
+  const size_t cols_bytes = (size_t)(m->hidden / kUnitRows) * sizeof(int);
   if (!m->fz_bar) {
     RC_CUDA_TRY(cudaMalloc(&m->fz_bar, sizeof(unsigned long long)));
     RC_CUDA_TRY(cudaMemset(m->fz_bar, 0, sizeof(unsigned long long)));
     m->fz_epoch = ctx->timeout_epoch;
   }
+  if (!m->dc_cols) {
+    RC_CUDA_TRY(cudaMalloc(&m->dc_cols, cols_bytes));
+    RC_CUDA_TRY(cudaMemset(m->dc_cols, 0, cols_bytes));
+  }
   if (m->fz_epoch != ctx->timeout_epoch) {
-    // a bounded wait gave up since the last launch: the arrival count may be
-    // left over from that launch
+    // a bounded wait gave up since the last launch: the arrival count and
+    // the column counters may be left over from that launch
     RC_CUDA_TRY(cudaMemsetAsync(m->fz_bar, 0, sizeof(unsigned long long), s));
+    RC_CUDA_TRY(cudaMemsetAsync(m->dc_cols, 0, cols_bytes, s));
     m->fz_epoch = ctx->timeout_epoch;
   }
   DcParams p{};
@@ -1032,6 +1093,7 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
   p.off_red = L.off_red;
   p.off_bar = L.off_bar;
   p.bar = m->fz_bar;
+  p.cols = m->dc_cols;
   p.err = ctx->err;
   p.trace = m->trace;
   p.ep_world = 1;

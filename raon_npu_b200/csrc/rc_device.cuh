@@ -106,6 +106,12 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void *src, uin
 }
 
 // The same without a cache hint (weights that several CTAs re-read soon).
+// Prefetch ``bytes`` (a multiple of 16, 16-byte aligned) of global memory
+// into L2 without a destination in shared memory.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void bulk_copy_g2s_plain(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)
