@@ -589,11 +589,16 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
                                               uint32_t *mask_s) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int T = p.T, E = p.n_experts, k = p.k, n = T * E;
+  // keys in rows of E4 (E rounded up to 4; the padding keys are 0, below
+  // every router key, which are >= 1)
+  const int E4 = (E + 3) & ~3;
   uint32_t *key_s = reinterpret_cast<uint32_t *>(scratch);
-  float *sc_s = reinterpret_cast<float *>(key_s + n);
+  float *sc_s = reinterpret_cast<float *>(key_s + T * E4);
+#pragma unroll 1
+  for (int i = tid; i < T * (E4 - E); i += kDcThreads) key_s[(i / (E4 - E)) * E4 + E + i % (E4 - E)] = 0u;
 #pragma unroll 1
   for (int i = tid; i < n; i += kDcThreads) {
-    const int e = i - (i / E) * E;
+    const int t = i / E, e = i - t * E;
     const float l = __ldcg(p.logits + i);
     float sc, v;
     if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
@@ -604,32 +609,29 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
       v = sc;
     }
     sc_s[i] = sc;
-    key_s[i] = dc_route_key(v);
+    key_s[t * E4 + e] = dc_route_key(v);
   }
   __syncthreads();
-  // ranks: warp w takes the candidates (t, c) with c = w, w + 16, ...; the
-  // lanes hold token t's keys (lane l: experts l, l + 32, ...), each lane
-  // counts the keys ahead of the candidate, one warp sum gives its rank
+  // ranks: one thread per candidate (t, c) scans token t's keys, four at a
+  // time, counting those ahead of it (no cross-lane steps on the chain)
 #pragma unroll 1
-  for (int t = 0; t < T; ++t) {
-    const uint32_t *kr = key_s + t * E;
-    uint32_t kk[kMoeMaxExperts / 32];
-#pragma unroll
-    for (int m = 0; m < kMoeMaxExperts / 32; ++m) kk[m] = m * 32 + lane < E ? kr[m * 32 + lane] : 0u;
-#pragma unroll 2
-    for (int c = warp; c < E; c += kDcWarps) {
-      const uint32_t kc = kr[c];
-      int cnt = 0;
-#pragma unroll
-      for (int m = 0; m < kMoeMaxExperts / 32; ++m) {
-        const int e2 = m * 32 + lane;
-        cnt += (e2 < E && (kk[m] > kc || (kk[m] == kc && e2 < c))) ? 1 : 0;
-      }
-      const int rank = (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
-      if (rank < k && lane == 0) {
-        sel_e[t * k + rank] = c;
-        sel_sc[t * k + rank] = sc_s[t * E + c];
-      }
+  for (int i = tid; i < n; i += kDcThreads) {
+    const int t = i / E, c = i - t * E;
+    const uint32_t kc = key_s[t * E4 + c];
+    const uint4 *kr4 = reinterpret_cast<const uint4 *>(key_s + t * E4);
+    int rank = 0;
+#pragma unroll 4
+    for (int q = 0; q < E4 / 4; ++q) {
+      const uint4 kq = kr4[q];
+      const int e0 = 4 * q;
+      rank += (kq.x > kc || (kq.x == kc && e0 < c)) ? 1 : 0;
+      rank += (kq.y > kc || (kq.y == kc && e0 + 1 < c)) ? 1 : 0;
+      rank += (kq.z > kc || (kq.z == kc && e0 + 2 < c)) ? 1 : 0;
+      rank += (kq.w > kc || (kq.w == kc && e0 + 3 < c)) ? 1 : 0;
+    }
+    if (rank < k) {
+      sel_e[t * k + rank] = c;
+      sel_sc[t * k + rank] = sc_s[i];
     }
   }
   __syncthreads();
@@ -682,6 +684,27 @@ static __device__ __noinline__ void dc_groups(const DcParams &p, const int32_t *
                                               int *n_groups, const uint8_t **all_gu, const uint8_t **all_dn,
                                               const uint8_t **g_gu, const uint8_t **g_dn) {
   const int tid = threadIdx.x, lane = tid & 31, T = p.T, k = p.k, E = p.n_experts;
+  if (T == 1) {
+    // one token: its ascending slot list (routed experts, then the shared
+    // one) is the group list, the slot position the group's destination row
+    if (tid < 32) {
+      const int e = lane <= k ? slots[lane] : -1;
+      const bool mine = lane < k ? (e >= p.own.lo && e < p.own.hi) : (lane == k && e >= 0 && (p.own.shared_mask & 1u));
+      const uint32_t b = __ballot_sync(0xffffffffu, mine);
+      if (mine) {
+        const int gi = __popc(b & ((1u << lane) - 1u));
+        g_expert[gi] = e;
+        g_mask[gi] = 1u;
+        gidx_s[e] = gi;
+        g_dst[gi] = lane;
+        g_gu[gi] = all_gu[e];
+        g_dn[gi] = all_dn[e];
+      }
+      if (lane == 0) *n_groups = __popc(b);
+    }
+    __syncthreads();
+    return;
+  }
   if (tid < 32) {
     int base = 0;
 #pragma unroll 1
@@ -997,7 +1020,7 @@ static bool dc_layout(const rc_moe *m, int T, int k, const MoeOwned &own, DcLayo
     const size_t bytes = (size_t)B * kDcChunk * kUnitBytes + ((size_t)ru * pb + 15) / 16 * 16;
     if (bytes > rest) continue;
     // the selection scratch (T*E keys and scores) lives in the unit ring
-    if ((size_t)T * E * 8 > (size_t)B * kDcChunk * kUnitBytes) continue;
+    if ((size_t)T * (E + 4) * 8 > (size_t)B * kDcChunk * kUnitBytes) continue;
     size_t off = 0;
     const size_t o_buf = off;
     off += (size_t)B * kDcChunk * kUnitBytes;
