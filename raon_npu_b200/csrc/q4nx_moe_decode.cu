@@ -291,24 +291,22 @@ static __device__ __noinline__ void dc_issue_chunk(const DcStream &st, int j, ui
   const int slot = j % slots;
   const uint32_t bar = bar0 + 8 * slot;
   const int s0 = j * kDcChunk, s1 = s0 + kDcChunk < st.units ? s0 + kDcChunk : st.units;
-  int bytes = 0;
-#pragma unroll 1
-  for (int s = s0; s < s1;) {
-    int run;
-    const uint8_t *src = dc_unit_src(st, s, s1 - s, &run);
-    if (src) bytes += run * kUnitBytes;
-    s += run;
-  }
-  mbar_arrive_expect_tx(bar, bytes);
   const uint64_t pol = policy_evict_first();
   const uint32_t dst0 = smem_addr(buf) + slot * kDcChunk * kUnitBytes;
+  // each contiguous run's bytes join the phase's transaction count before its
+  // copy is issued; the single arrival comes last, so the phase cannot
+  // complete before every run is accounted for
 #pragma unroll 1
   for (int s = s0; s < s1;) {
     int run;
     const uint8_t *src = dc_unit_src(st, s, s1 - s, &run);
-    if (src) bulk_copy_g2s(dst0 + (s - s0) * kUnitBytes, src, run * kUnitBytes, bar, pol);
+    if (src) {
+      mbar_expect_tx(bar, run * kUnitBytes);
+      bulk_copy_g2s(dst0 + (s - s0) * kUnitBytes, src, run * kUnitBytes, bar, pol);
+    }
     s += run;
   }
+  mbar_arrive(bar);
 }
 
 // Eight columns of one token: ascending-ID f32 sum (product rounded, then
@@ -824,12 +822,14 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   int *gidx_s = reinterpret_cast<int *>(mask_s + (E + 1));                         // [E+1]
   int *n_groups_s = gidx_s + (E + 1);                                              // [4]
   int32_t *g_dst = n_groups_s + 4;                                                 // [E+1][T]
-#pragma unroll 1
-  for (int i = tid; i <= E; i += kDcThreads) {
-    all_gu[i] = p.gu_tiles[i];
-    all_dn[i] = p.dn_tiles[i];
-    bias_s[i] = i < E ? p.bias[i] : 0.f;
-    mask_s[i] = i == E ? p.own.shared_mask : 0u;
+  // the tables are requested now and stored after the logits, so their
+  // latency hides behind the router (E + 1 <= 512 entries, one per thread)
+  const uint8_t *tab_gu = nullptr, *tab_dn = nullptr;
+  float tab_bias = 0.f;
+  if (tid <= E) {
+    tab_gu = p.gu_tiles[tid];
+    tab_dn = p.dn_tiles[tid];
+    if (tid < E) tab_bias = p.bias[tid];
   }
   if (p.ep_world > 1) {
     if (!dc_wait_sys(p.ep_flags + 0, (ep_calls + 1) * p.ep_world, p.err, ok_s)) return;
@@ -848,6 +848,12 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   } else {
     dc_logits(p, reinterpret_cast<double *>(smem + p.off_red), wpre, nlog);
     dc_stage(p.x, p.hidden, 0, 1, T, kb_gu, stage, warp, kDcWarps);
+  }
+  if (tid <= E) {
+    all_gu[tid] = tab_gu;
+    all_dn[tid] = tab_dn;
+    bias_s[tid] = tab_bias;
+    mask_s[tid] = tid == E ? p.own.shared_mask : 0u;
   }
   dc_stamp(p, kTrLogits);
   if (!dc_grid_barrier(p.bar, p.err, ok_s)) return;
