@@ -54,12 +54,12 @@ HBM_FALLBACK_GBS = 6650.0
 
 # DRAM traffic of the timed work, from ncu captures of the same commands on a
 # B200 (dram__bytes_read.sum + dram__bytes_write.sum): the GEMV launches of
-# one sweep step; one config-3 decode layer at T = 1 (rc_moe_fused_kernel); the
+# one sweep step; one config-3 decode layer at T = 1 (rc_moe_decode_kernel); the
 # two grouped GEMVs of one 512-token prefill layer.  Single-GPU figures.
 MEASURED_TRAFFIC = {"gemv_step": 1033.4e6, "moe_layer_t1": 27.30e6, "prefill_gemms": 300.75e6}
 TRAFFIC_SOURCE = {
     "gemv_step": "profiles/gemv_sweep_launch_list.md (all rc_q4nx_gemv_kernel launches of one step)",
-    "moe_layer_t1": "profiles/moe_decode_fused_t1.md (one rc_moe_fused_kernel launch, T = 1)",
+    "moe_layer_t1": "profiles/moe_decode_fused_t1.md (one rc_moe_decode_kernel launch, T = 1)",
     "prefill_gemms": "profiles/moe_prefill_gemv_t512.md (the two grouped GEMV launches of a 512-token layer)",
 }
 
@@ -889,10 +889,10 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = moe_cpu_baseline(args.cpu_seconds)
     if world == 1 or transport == "p2p":
-        per_step, kdesc = 1, "rc_moe_fused_kernel: router, top-k, grouped gate/up and down GEMVs, combine" + (
+        per_step, kdesc = 1, "rc_moe_decode_kernel: router, top-k, grouped gate/up and down GEMVs, combine" + (
             "; token and expert rows exchanged over NVLink peer stores inside it" if world > 1 else "")
     else:
-        per_step, kdesc = 2, ("rc_moe_fused_kernel (local experts) + combine, NCCL all-gather and reduce-scatter "
+        per_step, kdesc = 2, ("rc_moe_decode_kernel (local experts) + combine, NCCL all-gather and reduce-scatter "
                               "around them")
     barrier()
     for ep in eps:

@@ -100,7 +100,7 @@ struct rc_moe {
   uint16_t *down_out;         // [16][kMax+1][hidden]
   rc::PfScratch *pf;          // prefill scratch, grown on demand (null until the first prefill)
   int fused;                  // decode through the single persistent kernel when the shape fits
-  unsigned long long *fz_bar; // grid-barrier arrival count of the fused kernel (only grows)
+  unsigned long long *fz_bar; // grid-barrier arrival count of the persistent decode kernel (only grows)
   unsigned fz_epoch;          // ctx->timeout_epoch when fz_bar was last known consistent
   int *dc_cols;               // [hidden/16] down tiles written per output column tile (zero between calls)
   rc::MoeEp *ep;              // peer-memory expert parallelism (null until rc_moe_ep_init)
@@ -133,22 +133,13 @@ namespace rc {
 void pf_free(rc_moe *m);   // releases m->pf (q4nx_prefill.cu)
 // Router for 16 < T <= 4096 tokens (q4nx_prefill.cu): ids / weights [T][k],
 // logits [T][E] (each optional).
-// Fused decode (q4nx_moe_fused.cu).
+// Persistent decode kernel (q4nx_moe_decode.cu).
 bool moe_fused_fits(const rc_moe *m, int T, int k, const MoeOwned &own);
-bool moe_fused_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own);
-int moe_fused_decode(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling, int act,
-                     float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign, uint16_t *out,
-                     int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s,
-                     const MoeEpArgs *ep = nullptr);
 bool moe_decode_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own);
 int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling,
                           int act, float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign,
                           uint16_t *out, int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s,
                           const MoeEpArgs *ep = nullptr);
-bool moe_persistent_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own);
-int moe_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling, int act,
-                   float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign, uint16_t *out,
-                   int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s, const MoeEpArgs *ep = nullptr);
 int pf_route_tokens(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, int renormalize, float scaling,
                     int32_t *ids_dev, float *w_dev, float *logits_dev, void *stream);
 }  // namespace rc

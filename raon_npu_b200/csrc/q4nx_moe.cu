@@ -969,8 +969,7 @@ int rc_moe_set_expert(rc_moe *m, int expert, const uint8_t *gate_up, size_t gate
 
 int rc_moe_set_fused(rc_moe *m, int enable) {
   RC_CHECK_ARG(m, "rc_moe_set_fused: NULL argument");
-  RC_CHECK_ARG(enable >= 0 && enable <= 2, "rc_moe_set_fused: enable must be 0, 1 or 2");
-  m->fused = enable;
+  m->fused = enable ? 1 : 0;
   return RC_OK;
 }
 
@@ -1128,7 +1127,7 @@ int rc_moe_decode(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, in
   const cudaStream_t s = pick_stream(m->ctx, stream);
   if ((reinterpret_cast<uintptr_t>(x_dev) & 15) == 0 && (reinterpret_cast<uintptr_t>(out_dev) & 15) == 0 &&
       moe_fused_fits(m, T, k, own))
-    return moe_persistent(m, x_dev, T, k, router, renormalize, scaling, act, gate_beta, value_beta, own,
+    return moe_decode_persistent(m, x_dev, T, k, router, renormalize, scaling, act, gate_beta, value_beta, own,
                             m->down_out, 0, out_dev, ids_dev, w_dev, nullptr, s);
   rc = moe_route(m, x_dev, T, k, router, renormalize, scaling, own, s);
   if (rc) return rc;
@@ -1165,7 +1164,7 @@ int rc_moe_decode_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int rout
   // ranks' slot rows can be summed in the exchange (x + 0 = x exactly).
   RC_CHECK_ARG((reinterpret_cast<uintptr_t>(slot_out_dev) & 15) == 0, "slot_out must be 16-byte aligned");
   if ((reinterpret_cast<uintptr_t>(x_dev) & 15) == 0 && moe_fused_fits(m, T, k, own))
-    return moe_persistent(m, x_dev, T, k, router, renormalize, scaling, act, gate_beta, value_beta, own,
+    return moe_decode_persistent(m, x_dev, T, k, router, renormalize, scaling, act, gate_beta, value_beta, own,
                             slot_out_dev, 1, nullptr, nullptr, nullptr, slot_w_dev, s);
   MoeScratch sc = m->s;
   sc.slot_w = slot_w_dev;
@@ -1289,7 +1288,7 @@ int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int re
   if (rc) return rc;
   RC_CHECK_ARG(m->down_fmt == kFormatQ4nx,
                "rc_moe_ep_decode: the persistent decode kernel takes q4nx down matrices, not bfp16ebs8");
-  RC_CHECK_ARG(moe_persistent_shape_ok(m, T, k, own),
+  RC_CHECK_ARG(moe_decode_shape_ok(m, T, k, own),
                "rc_moe_ep_decode: T=%d k=%d does not fit the persistent decode kernel", T, k);
   RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
   MoeEpArgs a;
@@ -1301,7 +1300,7 @@ int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int re
   a.tok_off = (uint32_t)ep_tok_off();
   a.red_off = (uint32_t)ep_red_off(ep->world, ep->M, m->hidden);
   a.x_own = x_dev;
-  return moe_persistent(m, reinterpret_cast<const uint16_t *>(ep->base + ep_tok_off()), T, k, router,
+  return moe_decode_persistent(m, reinterpret_cast<const uint16_t *>(ep->base + ep_tok_off()), T, k, router,
                           renormalize, scaling, act, gate_beta, value_beta, own, m->down_out, 0, out_dev, nullptr,
                           nullptr, nullptr, pick_stream(m->ctx, stream), &a);
 }

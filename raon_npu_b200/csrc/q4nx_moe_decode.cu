@@ -1165,21 +1165,10 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
   return RC_OK;
 }
 
-// The persistent decode path of a layer: this kernel (rc_moe_set_fused 1, the
-// default), or the earlier kernel of q4nx_moe_fused.cu (2).  Both give the
-// same bytes.
-bool moe_persistent_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own) {
-  return m->fused == 2 ? moe_fused_shape_ok(m, T, k, own) : moe_decode_shape_ok(m, T, k, own);
-}
-
-int moe_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling, int act,
-                   float gb, float vb, const MoeOwned &own, uint16_t *slot_rows, int zero_foreign, uint16_t *out,
-                   int32_t *ids_out, float *w_out, float *slot_w_out, cudaStream_t s, const MoeEpArgs *ep) {
-  if (m->fused == 2)
-    return moe_fused_decode(m, x, T, k, router, renorm, scaling, act, gb, vb, own, slot_rows, zero_foreign, out,
-                            ids_out, w_out, slot_w_out, s, ep);
-  return moe_decode_persistent(m, x, T, k, router, renorm, scaling, act, gb, vb, own, slot_rows, zero_foreign, out,
-                               ids_out, w_out, slot_w_out, s, ep);
+// Whether the persistent kernel takes this call: it is switched on
+// (rc_moe_set_fused) and the shape is one it can run.
+bool moe_fused_fits(const rc_moe *m, int T, int k, const MoeOwned &own) {
+  return m->fused && moe_decode_shape_ok(m, T, k, own);
 }
 
 }  // namespace rc

@@ -335,11 +335,10 @@ class MoeLayer:
                                              ctypes.c_void_p(None if b is None else b.ctypes.data)),
               "rc_moe_set_router")
 
-    def set_fused(self, enable) -> None:
-        """Decode through one persistent kernel (True / 1, the default) or
-        separate launches (False / 0); 2 selects the earlier persistent kernel.
-        All give the same bytes."""
-        check(self.ctx.lib.rc_moe_set_fused(self.handle, int(enable)), "rc_moe_set_fused")
+    def set_fused(self, enable: bool) -> None:
+        """Decode through one persistent kernel (default) or separate launches;
+        both give the same bytes."""
+        check(self.ctx.lib.rc_moe_set_fused(self.handle, int(bool(enable))), "rc_moe_set_fused")
 
     TRACE_PHASES = ("start", "tokens", "logits", "routed", "selected", "staged", "gate_up", "act_ready", "down",
                     "rows", "end")
