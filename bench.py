@@ -1050,10 +1050,12 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
         cpu = {"value": round(n_tok / secs, 2), "unit": "tokens/s", "cores": th["threads"], "kind": "port",
                "sample": f"{n_tok} of the layer's tokens through the oracle per token (biased softmax router, "
                          f"NumpyBackend.moe_experts restated + shared expert), f32 weights cached"}
+    exchange = getattr(eps[0], "last_prefill_exchange", None) if world > 1 else None
     for ep in eps:
         ep.layer.close()
     return {
         "metric": "MoE prefill layer tokens/s", "value": round(T / (ms_max * 1e-3), 1), "unit": "tokens/s",
+        "exchange_rank0": exchange,
         "ms_per_step": round(ms_max, 4), "scaling": "strong",
         "config": {"workload": "MoE prefill layer (BASELINE configs[3]): 512 tokens, Zipf(1.1) expert load",
                    "parallelism": f"ep{world}", "tokens_per_rank": M, "kernel": prefill_kernel_desc(world),
@@ -1077,7 +1079,8 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
 
 def prefill_kernel_desc(world: int) -> str:
     return ("router, plan, grouped gate/up + down GEMVs over 8-token blocks (register-fragment mma), combine"
-            + ("; NCCL all-gather + reduce-scatter" if world > 1 else ""))
+            + ("; the token rows of remote routes to their experts' owners and the expert rows back by NCCL "
+               "all-to-all (split sizes read on the host: eager launches)" if world > 1 else ""))
 
 
 # ------------------------------------------------------ full decode step --

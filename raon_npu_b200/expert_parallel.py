@@ -19,6 +19,11 @@ tokens:
 4. ``combine`` (ascending expert ID, f32, then the shared expert) of the own
    tokens.
 
+Prefill instead sends only the routed rows: every rank routes its own
+tokens, computes its own experts for them, and exchanges the token rows of
+remote routes with their experts' owners in an all-to-all, the owners
+returning the expert rows the same way (``prefill``).
+
 The result of every token is byte-identical to the single-GPU decode
 (``MoeLayer.decode``): each expert's rows come out of whole-tile GEMVs whose
 columns do not interact, the exchange is exact and the combine is the same
@@ -173,9 +178,27 @@ class ExpertParallelMoe:
                            with_shared=self.layer.has_shared)
 
     def prefill(self, x, out) -> None:
-        """Prefill of this rank's M tokens x [M, hidden] -> out [M, hidden]: the
-        same exchange as ``decode`` around the tensor-core grouped GEMM
-        (``MoeLayer.prefill_local`` / ``prefill_combine``)."""
+        """Prefill of this rank's M tokens x [M, hidden] -> out [M, hidden]
+        with an all-to-all exchange of only the routed rows:
+
+        1. route the own tokens (``route``) and compute, for them, the experts
+           this rank owns and the shared expert (``prefill_local``: slot rows
+           [M, k+1, hidden] in ascending expert ID, zeros for remote slots,
+           and the slot weights);
+        2. send the token row of every remote route (token, expert) to the
+           expert's owner, grouped by destination (``all_to_all_single``; the
+           split sizes travel first);
+        3. the owner computes each received row's one expert
+           (``prefill_experts`` with k = 1 and weight 1: the expert's bf16
+           output row, unchanged by the sum) and sends the rows back in the
+           order received;
+        4. the rows fill the remote slots; ``prefill_combine`` of the own
+           tokens.
+
+        Each expert row comes out of the same tile arithmetic as on one GPU
+        and the combine is the same kernel, so a token's bytes equal the
+        single-GPU prefill.  The split sizes are read on the host, so this
+        path is not captured in a CUDA graph."""
         import torch
         import torch.distributed as dist
         M, H = x.shape
@@ -183,24 +206,55 @@ class ExpertParallelMoe:
         if N == 1:
             self.layer.prefill(x, k, out, **self.kw)
             return
-        T = N * M
+        if x.is_cuda and torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the expert-parallel prefill sizes its exchange on the host; it cannot be captured")
         dev = x.device
-        if N > 1:
-            xg = self._buf("pxg", (T, H), torch.int16, dev)
-            dist.all_gather_into_tensor(_bf16(xg), _bf16(x), group=self.group)
-        else:
-            xg = x
-        slots = self._buf("pslots", (T, k + 1, H), torch.int16, dev)
-        sw = self._buf("psw", (T, k), torch.float32, dev)
-        shared = (self.rank * M, M) if self.layer.has_shared else (0, 0)
-        self.layer.prefill_local(xg, k, slots, sw, experts=self.experts, shared_tokens=shared, **self.kw)
-        if N > 1:
-            mine = self._buf("pmine", (M, k + 1, H), torch.int16, dev)
-            dist.reduce_scatter_tensor(_bf16(mine), _bf16(slots), op=dist.ReduceOp.SUM, group=self.group)
-        else:
-            mine = slots
-        self.layer.prefill_combine(mine, sw[self.rank * M:(self.rank + 1) * M], k, out, tokens=M,
-                                   with_shared=self.layer.has_shared)
+        E = self.layer.n_experts
+        per = E // N
+        kw = self.kw
+        ids = self._buf("pf_ids", (M, k), torch.int32, dev)
+        w = self._buf("pf_w", (M, k), torch.float32, dev)
+        self.layer.route(x, M, k, ids, w, router=kw["router"], renormalize=kw["renormalize"],
+                         scaling=kw["scaling"])
+        slots = self._buf("pf_slots", (M, k + 1, H), torch.int16, dev)
+        sw = self._buf("pf_sw", (M, k), torch.float32, dev)
+        shared = (0, M) if self.layer.has_shared else (0, 0)
+        self.layer.prefill_local(x, k, slots, sw, experts=self.experts, shared_tokens=shared, **kw)
+        # remote routes grouped by destination rank (stable: token-major within a destination)
+        ids64 = ids.to(torch.int64)
+        dest = (ids64 // per).reshape(-1)
+        pos = (ids64.unsqueeze(2) > ids64.unsqueeze(1)).sum(dim=2).reshape(-1)   # ascending-ID slot
+        route = torch.arange(M * k, device=dev)
+        remote = dest != self.rank
+        order = torch.argsort(dest * (M * k) + route)
+        order = order[remote[order]]
+        send_counts = torch.bincount(dest[order], minlength=N).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        send = send_counts.tolist()
+        recv = recv_counts.tolist()
+        tok = order // k
+        send_x = x[tok].contiguous()
+        send_e = ids64.reshape(-1)[order].to(torch.int32).contiguous()
+        n_recv = int(sum(recv))
+        recv_x = torch.empty((n_recv, H), dtype=x.dtype, device=dev)
+        recv_e = torch.empty((n_recv,), dtype=torch.int32, device=dev)
+        dist.all_to_all_single(_bf16(recv_x), _bf16(send_x), output_split_sizes=recv, input_split_sizes=send,
+                               group=self.group)
+        dist.all_to_all_single(recv_e, send_e, output_split_sizes=recv, input_split_sizes=send, group=self.group)
+        rows = torch.empty((n_recv, H), dtype=x.dtype, device=dev)
+        if n_recv:
+            ones = torch.ones((n_recv, 1), dtype=torch.float32, device=dev)
+            self.layer.prefill_experts(recv_x, recv_e.reshape(n_recv, 1), ones, 1, rows, act=kw["act"],
+                                       gate_beta=kw["gate_beta"], value_beta=kw["value_beta"], with_shared=False)
+        back = torch.empty_like(send_x)
+        dist.all_to_all_single(_bf16(back), _bf16(rows), output_split_sizes=send, input_split_sizes=recv,
+                               group=self.group)
+        if order.numel():
+            slots[tok, pos[order]] = back
+        self.last_prefill_exchange = {"rows_sent": int(order.numel()), "rows_received": n_recv,
+                                      "bytes_sent": 2 * H * (int(order.numel()) + n_recv)}
+        self.layer.prefill_combine(slots, sw, k, out, tokens=M, with_shared=self.layer.has_shared)
 
     def _host_call(self, x: np.ndarray, run, tag: str) -> np.ndarray:
         """x [M, hidden] bf16 bits on the host -> run(x_dev, out_dev) -> out on

@@ -72,6 +72,27 @@ class OracleLayer:
         slots.copy_(torch.from_numpy(rows.view(np.int16)))
         sw.copy_(torch.from_numpy(wts))
 
+    def route(self, x, tokens, k, ids, w, **_):
+        import torch
+        from oracle import backend as ob
+        xs = x.numpy().view(np.uint16)
+        res = [ob.route_softmax(xs[t], self.wr, k) for t in range(tokens)]
+        ids.copy_(torch.from_numpy(np.stack([r[0] for r in res]).astype(np.int32)))
+        w.copy_(torch.from_numpy(np.stack([r[1] for r in res])))
+
+    prefill_local = decode_local
+
+    def prefill_experts(self, x, ids, w, k, out, act, with_shared=False, **_):
+        import torch
+        from oracle import backend as ob
+        xs = x.numpy().view(np.uint16)
+        ii, ww = ids.numpy(), w.numpy()
+        res = np.stack([ob.moe_experts(self.experts, xs[t], ii[t], ww[t], act=act) for t in range(xs.shape[0])])
+        out.copy_(torch.from_numpy(res.view(np.int16)))
+
+    def prefill_combine(self, slots, sw, k, out, tokens, with_shared):
+        self.combine(slots, sw, k, out, tokens, with_shared)
+
     def combine(self, slots, sw, k, out, tokens, with_shared):
         import torch
         from oracle import backend as ob
@@ -122,6 +143,58 @@ def test_expert_parallel_two_ranks_match_single_process(tmp_path):
             ref, _, _, _ = ob.moe_decode_layer({e: experts[e] for e in range(E)}, experts[E], wr, x[t], K,
                                                act="swiglu")
             np.testing.assert_array_equal(out[t], ref)
+
+
+def _prefill_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+    from raon_npu_b200.expert_parallel import ExpertParallelMoe
+    from oracle import q4nx as q
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        experts, wr = _model()
+        per = E // world
+        owned = set(range(rank * per, (rank + 1) * per)) | {E}
+        ep = ExpertParallelMoe(OracleLayer(experts, wr, owned), K, act="swiglu")
+        rng = np.random.default_rng(300 + rank)
+        x = q.f32_to_bf16(rng.standard_normal((5, HIDDEN)).astype(np.float32))
+        out = torch.empty((5, HIDDEN), dtype=torch.int16)
+        ep.prefill(torch.from_numpy(x.view(np.int16)), out)
+        np.save(os.path.join(result_dir, f"px{rank}.npy"), x)
+        np.save(os.path.join(result_dir, f"pout{rank}.npy"), out.numpy().view(np.uint16))
+        np.save(os.path.join(result_dir, f"pex{rank}.npy"), np.array([ep.last_prefill_exchange], dtype=object),
+                allow_pickle=True)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_expert_parallel_prefill_all_to_all_matches_single_process(tmp_path):
+    """Prefill over two gloo ranks: only the rows of remote routes cross
+    (all-to-all there and back), and every rank's outputs equal the
+    single-process oracle layer byte for byte."""
+    import torch.multiprocessing as mp
+    from oracle import backend as ob
+    world = 2
+    mp.start_processes(_prefill_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    experts, wr = _model()
+    sent = 0
+    for rank in range(world):
+        x = np.load(tmp_path / f"px{rank}.npy")
+        out = np.load(tmp_path / f"pout{rank}.npy")
+        ex = np.load(tmp_path / f"pex{rank}.npy", allow_pickle=True)[0]
+        remote = 0
+        for t in range(x.shape[0]):
+            ref, ids, _, _ = ob.moe_decode_layer({e: experts[e] for e in range(E)}, experts[E], wr, x[t], K,
+                                                 act="swiglu")
+            np.testing.assert_array_equal(out[t], ref)
+            remote += int(sum(1 for e in ids if int(e) // (E // world) != rank))
+        assert ex["rows_sent"] == remote
+        sent += ex["rows_sent"]
+    assert sent == sum(np.load(tmp_path / f"pex{r}.npy", allow_pickle=True)[0]["rows_received"] for r in range(world))
 
 
 def test_single_process_owns_every_expert():
