@@ -1,4 +1,4 @@
-"""Expert-parallel MoE decode on 2+ GPUs of one box.
+"""Expert-parallel MoE decode (and prefill) on 2+ GPUs of one box.
 
 Each rank (one process per GPU) holds E/N routed experts and the shared
 expert and decodes its own tokens through ``ExpertParallelMoe``, over both
@@ -6,7 +6,8 @@ transports: ``"nccl"`` (all-gather, grouped expert GEMVs, reduce-scatter,
 combine) and ``"p2p"`` (one persistent kernel that exchanges token and expert
 rows through the ranks' peer-mapped buffers).  Every rank's output must
 equal, byte for byte, the single-GPU ``MoeLayer.decode`` of the same tokens
-with all experts loaded.  The p2p case also makes a peer wait run out on
+with all experts loaded; the prefill of 40 tokens per rank (all-to-all of
+the routed rows) must equal the single-GPU prefill.  The p2p case also makes a peer wait run out on
 purpose -- rank 1 skips one call, so rank 0's kernel waits for token rows
 that never come -- and checks that rank 0 gets the timeout status after the
 1 s bound and that the layer then refuses further exchange calls.  Skipped
@@ -83,6 +84,18 @@ def _worker(rank, world, port, out_dir, transport):
         host = ep.decode_host(x.cpu().numpy().view(np.uint16))
         res.append(bool(np.array_equal(host, ref.cpu().numpy().view(np.uint16))))
         ctx.sync()
+        if transport == "nccl":
+            # prefill: the routed rows of remote routes cross in an all-to-all
+            gen.manual_seed(700 + rank)
+            xp = torch.randn((40, H), generator=gen, device="cuda").to(torch.bfloat16).view(torch.int16).contiguous()
+            outp = torch.empty_like(xp)
+            ep.prefill(xp, outp)
+            refp = torch.empty_like(xp)
+            full.prefill(xp, K, refp, act="swiglu")
+            torch.cuda.synchronize()
+            res.append(bool(torch.equal(outp, refp)))
+            res.append(ep.last_prefill_exchange["rows_sent"] > 0)
+            ctx.sync()
         if transport == "p2p":
             res.append(ep._ep_M == M)           # the peer path really ran
             dist.barrier()
