@@ -463,7 +463,8 @@ class MoeLayer:
     def prefill(self, x_dev, k: int, out_dev, ids_dev=None, w_dev=None, router: str = "softmax",
                 renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
                 value_beta: float = 25.0, stream: int | None = None) -> None:
-        """The layer for T <= 4096 tokens on the tcgen05 grouped GEMM: x [T, hidden] -> out [T, hidden]."""
+        """The layer for T <= 4096 tokens on the prefill kernel chosen by
+        ``set_prefill_kernel``: x [T, hidden] -> out [T, hidden]."""
         check(self.ctx.lib.rc_moe_prefill(
             self.handle, ctypes.c_void_p(_ptr(x_dev)), _tokens(x_dev, self.hidden), int(k), ROUTER_CODES[router],
             int(bool(renormalize)), float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta),

@@ -185,3 +185,179 @@ def sample_inputs(vocab, seed, kind):
     order = np.argsort(-logits, kind="stable")
     seen = [int(order[0]), int(order[3]), int(order[17]), int(rng.integers(vocab)), int(rng.integers(vocab))]
     return logits, seen, seed + 1000
+
+
+# ------------------------------------------------------------- tiny model --
+# The reference's tiny three-layer model (host/test_host_small.py:103-133: RDA
+# + dense MLP, MLA + MoE, RDA + MoE; 8 experts, top-2, one shared expert, the
+# SiTU betas of its ``tiny_situ_model``), widened where the q4nx MoE kernels
+# need it: hidden 256 (a whole q4nx K block) instead of 64 and an expert
+# intermediate of 64 (the MoE layer's granularity) instead of 32.
+TINY_MODEL_CONFIG = dict(
+    vocab_size=256, hidden_size=256, intermediate_size=128, num_hidden_layers=3,
+    num_attention_heads=4, head_dim=16, num_experts=8, num_experts_per_token=2,
+    moe_intermediate_size=64, num_shared_experts=1, first_k_dense_replace=1,
+    q_lora_rank=32, kv_lora_rank=32, qk_nope_head_dim=16, qk_rope_head_dim=8, v_head_dim=16,
+    rda_decay_rank=16,
+    rda_config={"num_heads": 4, "head_dim": 16, "conv_kernel_size": 4, "full_rank_gate": True,
+                "gate_lower_bound": -5.0, "rda_layers": [1, 3], "mla_layers": [2]},
+    activation_situ_beta=2.0, activation_situ_linear_beta=9.0,
+    routed_scaling_factor=1.5, moe_renormalize=True,
+    pad_token_id=0, eos_token_id=[2], max_position_embeddings=64,
+)
+TINY_MODEL_SEED = 701
+TINY_MODEL_TOKENS = (1, 17, 42, 200, 7, 99)
+
+
+def _tiny_linear_shapes(c: dict) -> dict:
+    """name -> (out, in) of every matrix the model multiplies through
+    ``Backend.linear`` (host/raon.py:1108-1134,1166-1222,1295-1327,932)."""
+    C, H = c["hidden_size"], c["num_attention_heads"]
+    rda = c["rda_config"]
+    rp = rda["num_heads"] * rda["head_dim"]
+    rda_layers = {x - 1 for x in rda["rda_layers"]}
+    out = {}
+    for L in range(c["num_hidden_layers"]):
+        a = f"model.layers.{L}.self_attn"
+        if L in rda_layers:
+            for p in ("q", "k", "v", "g"):
+                out[f"{a}.{p}_proj.weight"] = (rp, C)
+            out[f"{a}.b_proj.weight"] = (rda["num_heads"], C)
+            out[f"{a}.rda_w_proj.weight"] = (rda["num_heads"], C)
+            out[f"{a}.f_a_proj.weight"] = (c["rda_decay_rank"], C)
+            out[f"{a}.f_b_proj.weight"] = (rp, c["rda_decay_rank"])
+            out[f"{a}.o_proj.weight"] = (C, rp)
+        else:
+            qd = c["qk_nope_head_dim"] + c["qk_rope_head_dim"]
+            out[f"{a}.q_a_proj.weight"] = (c["q_lora_rank"], C)
+            out[f"{a}.q_b_proj.weight"] = (H * qd, c["q_lora_rank"])
+            out[f"{a}.kv_a_proj_with_mqa.weight"] = (c["kv_lora_rank"] + c["qk_rope_head_dim"], C)
+            out[f"{a}.kv_b_proj.weight"] = (H * (c["qk_nope_head_dim"] + c["v_head_dim"]), c["kv_lora_rank"])
+            out[f"{a}.g_proj.weight"] = (H * c["v_head_dim"], C)
+            out[f"{a}.o_proj.weight"] = (C, H * c["v_head_dim"])
+        if L < c["first_k_dense_replace"]:
+            m, inter = f"model.layers.{L}.mlp", c["intermediate_size"]
+            out[f"{m}.gate_proj.weight"] = (inter, C)
+            out[f"{m}.up_proj.weight"] = (inter, C)
+            out[f"{m}.down_proj.weight"] = (C, inter)
+        # (the shared experts' gate/up/down are made with the routed experts)
+    out["lm_head.weight"] = (c["vocab_size"], C)
+    return out
+
+
+def _q4nx_padded(w: np.ndarray, q):
+    """Zero-pad to 128 rows / 256 columns (the exporter's GEMV alignment,
+    quant/q4nx.py:226-248), quantise and pack; returns (packed, padded n, padded
+    k, dequantised f32 weights of the unpadded [n, k])."""
+    n, k = w.shape
+    wp = np.pad(w, ((0, (-n) % 128), (0, (-k) % 256)))
+    packed, f32 = q4nx_weight(wp, q)
+    return packed, wp.shape[0], wp.shape[1], np.ascontiguousarray(f32[:n, :k])
+
+
+def tiny_model(q=None):
+    """Seeded weights of the tiny model in q4nx form.
+
+    Returns ``host`` (name -> array, the weights the reference's host model
+    and NumpyBackend read: the q4nx matrices as their dequantised f32 values,
+    the rest as f32, the embedding as bf16 bits), ``bundles`` (bundle ->
+    (packed, padded n, padded k)), ``linears`` (name -> (bundle, first row,
+    end row, unpadded k): a shared expert's gate and up are the two row halves
+    of its [gate; up] bundle, as the reference's exporter packs them),
+    ``experts`` (MoE layer -> expert -> (packed [gate; up], packed K-padded
+    down); the shared expert under id ``num_experts``, the same bytes as its
+    bundles) and ``router`` (MoE layer -> (bf16 bits [E, C], correction bias
+    f32 [E]))."""
+    if q is None:
+        import oracle.q4nx as q
+    c = TINY_MODEL_CONFIG
+    rng = np.random.default_rng(TINY_MODEL_SEED)
+    C, V, n_mhc = c["hidden_size"], c["vocab_size"], 4
+    E, I = c["num_experts"], c["moe_intermediate_size"]
+
+    def normal(shape, std):
+        return (rng.standard_normal(shape) * std).astype(np.float32)
+
+    host, bundles, linears, experts, router = {}, {}, {}, {}, {}
+    host["model.embed_tokens.weight"] = _bf16_bits(normal((V, C), 1.0))
+    host["model.norm.weight"] = 1.0 + normal((C,), 0.1)
+    for name, (n, k) in _tiny_linear_shapes(c).items():
+        packed, n_pad, k_pad, f32 = _q4nx_padded(normal((n, k), k ** -0.5), q)
+        bundles[name] = (packed, n_pad, k_pad)
+        linears[name] = (name, 0, n, k)
+        host[name] = f32
+    rda_layers = {x - 1 for x in c["rda_config"]["rda_layers"]}
+    rp, hd = 4 * 16, 16
+    for L in range(c["num_hidden_layers"]):
+        p = f"model.layers.{L}"
+        host[f"{p}.input_layernorm.weight"] = 1.0 + normal((C,), 0.1)
+        host[f"{p}.post_attention_layernorm.weight"] = 1.0 + normal((C,), 0.1)
+        for site in ("self_attn_raon_mhc", "mlp_raon_mhc"):
+            s = f"{p}.{site}"
+            std = 0.5 * (n_mhc * C) ** -0.5
+            host[f"{s}.phi_pre"] = normal((n_mhc, n_mhc * C), std)
+            host[f"{s}.phi_post"] = normal((n_mhc, n_mhc * C), std)
+            host[f"{s}.res.phi_z"] = normal(((n_mhc - 1) ** 2, n_mhc * C), std)
+            for a in ("alpha_pre", "alpha_post", "res.alpha_z"):
+                host[f"{s}.{a}"] = np.array([0.5], np.float32)
+            host[f"{s}.b_pre"] = normal((n_mhc,), 0.1)
+            host[f"{s}.b_post"] = normal((n_mhc,), 0.1)
+            host[f"{s}.res.b_z"] = normal(((n_mhc - 1) ** 2,), 0.1)
+            host[f"{s}.res.eta"] = np.array([0.0], np.float32)
+        a = f"{p}.self_attn"
+        if L in rda_layers:
+            for kind in ("q", "k", "v"):
+                host[f"{a}.{kind}_conv1d.weight"] = normal((rp, c["rda_config"]["conv_kernel_size"]), 0.5)
+            host[f"{a}.dt_bias"] = normal((rp,), 0.1)
+            host[f"{a}.A_log"] = np.log(rng.uniform(1.0, 4.0, 4)).astype(np.float32)
+            host[f"{a}.o_norm.weight"] = 1.0 + normal((hd,), 0.1)
+        else:
+            host[f"{a}.q_a_layernorm.weight"] = 1.0 + normal((c["q_lora_rank"],), 0.1)
+            host[f"{a}.kv_a_layernorm.weight"] = 1.0 + normal((c["kv_lora_rank"],), 0.1)
+        if L < c["first_k_dense_replace"]:
+            continue
+        m = f"{p}.moe"
+        bits = _bf16_bits(normal((E, C), C ** -0.5))
+        bias = normal((E,), 0.05)
+        router[L] = (bits, bias)
+        host[f"{m}.gate.weight"] = (bits.astype(np.uint32) << 16).view(np.float32)
+        host[f"{m}.gate.e_score_correction_bias"] = bias
+        experts[L] = {}
+        for e in range(E + 1):
+            pgu, fgu = q4nx_weight(normal((2 * I, C), C ** -0.5), q)
+            pdn, n_pad, k_pad, fdn = _q4nx_padded(normal((C, I), I ** -0.5), q)
+            experts[L][e] = (pgu, pdn)
+            ex = f"{m}.experts.{e}" if e < E else f"{m}.shared_experts"
+            host[f"{ex}.gate_proj.weight"] = np.ascontiguousarray(fgu[:I])
+            host[f"{ex}.up_proj.weight"] = np.ascontiguousarray(fgu[I:])
+            host[f"{ex}.down_proj.weight"] = fdn
+            if e == E:
+                bundles[f"{ex}.gate_up"] = (pgu, 2 * I, C)
+                bundles[f"{ex}.down_proj.weight"] = (pdn, n_pad, k_pad)
+                linears[f"{ex}.gate_proj.weight"] = (f"{ex}.gate_up", 0, I, C)
+                linears[f"{ex}.up_proj.weight"] = (f"{ex}.gate_up", I, 2 * I, C)
+                linears[f"{ex}.down_proj.weight"] = (f"{ex}.down_proj.weight", 0, C, I)
+    return {"host": host, "bundles": bundles, "linears": linears, "experts": experts, "router": router}
+
+
+def tiny_model_trace(npz) -> dict:
+    """The recorded ``RaonModel.step`` calls of ``tiny_model.npz`` as a list of
+    dicts (kind "linear": name, x, y; kind "moe": layer, x, y, top, w, betas,
+    layer_out), the per-step call ranges and the per-step logits."""
+    z = np.load(npz)
+    calls = []
+    moe = {int(i): j for j, i in enumerate(z["moe_call"])}
+    for i in range(len(z["name"])):
+        c = {"x": z["x_flat"][z["x_off"][i]:z["x_off"][i + 1]],
+             "y": z["y_flat"][z["y_off"][i]:z["y_off"][i + 1]]}
+        if i in moe:
+            j = moe[i]
+            c.update(kind="moe", layer=int(z["moe_layer"][j]), top=z["moe_top"][j], w=z["moe_w"][j],
+                     betas=tuple(float(b) for b in z["moe_betas"][j]), layer_out=z["moe_layer_out"][j])
+        else:
+            c.update(kind="linear", name=str(z["name"][i]))
+        calls.append(c)
+    starts = [int(s) for s in z["step_starts"]]
+    return {"calls": calls, "steps": list(zip(starts[:-1], starts[1:])),
+            "logits": [z[f"step{s}/logits"] for s in range(len(starts) - 1)],
+            "bundles_sha": str(z["bundles_sha"]), "experts_sha": str(z["experts_sha"])}

@@ -31,14 +31,16 @@ sys.path.insert(0, REF)
 from quant import q4nx as rq  # noqa: E402
 from host.backend import NumpyBackend  # noqa: E402
 from host.weights import Weights  # noqa: E402
-from host.raon import RaonModel  # noqa: E402
+from host.raon import RaonConfig, RaonModel  # noqa: E402
 from kernels.moe_grouped.planner import build_plan, scatter_b2  # noqa: E402
 from serve.engine import GenOptions, sample_token  # noqa: E402
 
 sys.path.insert(0, str(HERE.parent.parent))
 from tests.golden.cases import (  # noqa: E402
     QUANT_CASES, LINEAR_CASES, MOE_CASE, ROUTER_CASE, COMBINE_CASE, SAMPLE_CASES, BFP16_CASES,
+    TINY_MODEL_CONFIG, TINY_MODEL_TOKENS,
     quant_input, linear_inputs, moe_inputs, router_inputs, combine_inputs, sample_inputs, bfp16_input,
+    tiny_model,
 )
 
 
@@ -50,6 +52,7 @@ class _Tensors(Weights):
         self.selected_layers = None
         self.load_global = True
         self.skip_moe_experts = False
+        self._f32_cache = {}
 
 
 def sha(b: bytes) -> str:
@@ -186,7 +189,82 @@ def make_bfp16():
     np.savez_compressed(HERE / "bfp16.npz", **out)
 
 
+class _RecordingBackend(NumpyBackend):
+    """NumpyBackend that records the path calls the model makes: every
+    ``linear`` and ``moe_experts`` call with its inputs and output (the
+    experts' own linears inside ``moe_experts`` are not separate calls)."""
+
+    def __init__(self, weights):
+        super().__init__(weights)
+        self.calls = []
+        self._inside_moe = False
+
+    def linear(self, name, x):
+        y = super().linear(name, x)
+        if not self._inside_moe:
+            self.calls.append({"kind": "linear", "name": name, "x": np.array(x), "y": np.array(y)})
+        return y
+
+    def moe_experts(self, layer, x, top_ids, top_weights, gate_beta=4.0, value_beta=25.0, shared_gu=None):
+        self._inside_moe = True
+        try:
+            y = super().moe_experts(layer, x, top_ids, top_weights, gate_beta=gate_beta, value_beta=value_beta,
+                                    shared_gu=shared_gu)
+        finally:
+            self._inside_moe = False
+        self.calls.append({"kind": "moe", "layer": layer, "x": np.array(x), "y": np.array(y),
+                           "top": np.array(top_ids), "w": np.array(top_weights, np.float32),
+                           "betas": np.array([gate_beta, value_beta], np.float64)})
+        return y
+
+
+def make_tiny_model():
+    """``RaonModel.step`` (host/raon.py:856-933) over TINY_MODEL_TOKENS on the
+    tiny model's q4nx weights, NumpyBackend computing: every path call of every
+    step (inputs, outputs, the model's own sigmoid+bias routes), each MoE
+    layer's output (``_moe_token``: routed + shared, host/raon.py:1293-1330)
+    and the step's logits."""
+    m = tiny_model(rq)
+    cfg = RaonConfig.from_dict(dict(TINY_MODEL_CONFIG))
+    be = _RecordingBackend(_Tensors(m["host"]))
+    model = RaonModel(cfg, _Tensors(m["host"]), be)
+    moe_token = model._moe_token
+    layer_out = []
+
+    def recording_moe_token(layer_idx, hidden, shared_gate_up=None):
+        res = moe_token(layer_idx, hidden, shared_gate_up)
+        layer_out.append(np.array(res[0]))
+        return res
+    model._moe_token = recording_moe_token
+    out = {"bundles_sha": np.array(sha(b"".join(m["bundles"][n][0] for n in sorted(m["bundles"])))),
+           "experts_sha": np.array(sha(b"".join(m["experts"][L][e][i] for L in sorted(m["experts"])
+                                                for e in sorted(m["experts"][L]) for i in (0, 1))))}
+    starts = []
+    for s_i, tok in enumerate(TINY_MODEL_TOKENS):
+        starts.append(len(be.calls))
+        out[f"step{s_i}/logits"] = np.asarray(model.step(tok), np.float32)
+    starts.append(len(be.calls))
+    out["step_starts"] = np.array(starts, np.int32)
+    # one flat array of every call's input and one of its output, with offsets
+    xs = [c["x"].reshape(-1) for c in be.calls]
+    ys = [c["y"].reshape(-1) for c in be.calls]
+    out["x_flat"], out["y_flat"] = np.concatenate(xs), np.concatenate(ys)
+    out["x_off"] = np.cumsum([0] + [a.size for a in xs]).astype(np.int32)
+    out["y_off"] = np.cumsum([0] + [a.size for a in ys]).astype(np.int32)
+    out["name"] = np.array([c.get("name", "") for c in be.calls])
+    moe = [i for i, c in enumerate(be.calls) if c["kind"] == "moe"]
+    assert len(moe) == len(layer_out)
+    out["moe_call"] = np.array(moe, np.int32)
+    out["moe_layer"] = np.array([be.calls[i]["layer"] for i in moe], np.int32)
+    out["moe_top"] = np.stack([be.calls[i]["top"] for i in moe]).astype(np.int32)
+    out["moe_w"] = np.stack([be.calls[i]["w"] for i in moe])
+    out["moe_betas"] = np.stack([be.calls[i]["betas"] for i in moe])
+    out["moe_layer_out"] = np.stack(layer_out)
+    np.savez_compressed(HERE / "tiny_model.npz", **out)
+
+
 if __name__ == "__main__":
+    make_tiny_model()
     make_bfp16()
     make_sample()
     make_quant()
