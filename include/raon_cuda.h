@@ -173,7 +173,9 @@ int rc_moe_set_fused(rc_moe *m, int enable);
  * grid passed the logits, 4 top-k and group table built, 5 token rows
  * staged, 6 this CTA's gate/up tiles done, 7 the activations its down tiles
  * read are complete, 8 its down tiles done, 9 every expert row of the
- * combined tokens written, 10 combine done.  ``ctas`` >= the SM count;
+ * combined tokens written, 10 combine done, 11 the tokens' router keys in
+ * shared memory, 12 the top-k ranks found, 13 the activation rows its down
+ * tiles read staged.  ``ctas`` >= the SM count;
  * NULL switches the stamps off.  No counterpart in the reference. */
 int rc_moe_set_trace(rc_moe *m, unsigned long long *stamps_dev, int ctas);
 

@@ -125,6 +125,9 @@ enum TracePhase : int {
   kTrDown,           // this CTA's down tiles done
   kTrRows,           // every expert row of the combined tokens is written (grid / peers)
   kTrEnd,            // combine done
+  kTrKeys,           // selection: every router key of the tokens in shared memory
+  kTrRanked,         // selection: the top-k ranks found
+  kTrActStaged,      // down: the activation rows staged as mma fragments
   kTracePhases = 16
 };
 }  // namespace rc

@@ -610,6 +610,7 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
     key_s[t * E4 + e] = dc_route_key(v);
   }
   __syncthreads();
+  dc_stamp(p, kTrKeys);
   // ranks: one thread per candidate (t, c) scans token t's keys, four at a
   // time, counting those ahead of it (no cross-lane steps on the chain)
 #pragma unroll 1
@@ -633,6 +634,7 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
     }
   }
   __syncthreads();
+  dc_stamp(p, kTrRanked);
   if (warp < T) {
     // lane r < k holds the token's r-th best expert; the weights' sums run
     // over the ranks in order (shuffles), as a single thread would add them
@@ -943,6 +945,7 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
       dc_stage(p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, p.inter_pad, 8 * NTB, nblk, T, kb_dn, stage, warp,
                kDcWarps);
     __syncthreads();
+    dc_stamp(p, kTrActStaged);
     rv = dc_rounds<NTB>(p, smem, st, 1, stage, nblk > 0 ? nblk : 1, g_mask, g_dst, g_lo, issued, failed, ng,
                         slot_w);
     issued = rv >> 1;

@@ -17,22 +17,27 @@
 //   combine   per token, its slot rows in ascending ID (f32 multiply, then
 //             add, no FMA), RTNE, plus the shared row
 //
-// The grouped GEMM (one CTA per SM, 8 warps, persistent over work items
-// (64-token chunk, 128-row weight tile)):
+// The grouped GEMM (one CTA per SM, persistent over work items (64-row chunk
+// of one expert, 128-row weight tile), a k-block of 256 columns per step):
 //   A  weight tile: the q4nx codes of 128 rows x 256 columns arrive by bulk
 //      copy in the t16 upload layout and are written to shared memory as
 //      bf16 (128 + code) -- exact -- in the 128-byte-swizzled K-major layout
 //      the tensor core reads;
-//   B  the chunk's 64 token rows x 256 columns, fetched with cp.async (the
-//      gate/up stage gathers them from x through the plan), swizzled the
-//      same way; the per-32-column group sums S of the rows come with them;
+//   B  the chunk's 64 source rows x 256 columns: a gather pass first copies
+//      the token rows into permuted order (the down GEMM's act rows already
+//      are), so a chunk's rows are contiguous and arrive as four 64 x 64
+//      TMA boxes in the same swizzle; the rows' per-32-column group sums S
+//      (computed by that pass) arrive as a fifth box;
 //   D  one tcgen05.mma chain of K = 32 per quantisation group into its own
 //      tensor-memory accumulator (8 groups x 64 columns = 512 columns);
-//   promotion: the thread of weight row r (TMEM lane r; warps w and w+4 share
-//      the lanes and split the token columns) reads the 8 group accumulators
-//      with tcgen05.ld and adds scale * D + (min - 128 scale) * S in f32
-//      registers -- the same arithmetic as the decode GEMV and as the
+//   promotion: the thread of weight row r (TMEM lane r) reads the group
+//      accumulators with tcgen05.ld and adds scale * D + (min - 128 scale) * S
+//      in f32 registers -- the same arithmetic as the decode GEMV and as the
 //      reference NPU kernel's per-group scaling (grouped_mmul.cc:196-254).
+// Loads, expansion, MMAs and promotion run in different warps on mbarrier
+// rings (see rc_pf_tc_kernel).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <string.h>
 
 #include "moe_internal.cuh"
@@ -46,23 +51,14 @@ constexpr int kPfMaxTokens = 4096;
 constexpr int kPfRows = 128;         // weight rows per tile: MMA M, TMEM lanes
 constexpr int kPfCols = 64;          // token columns per work item: max MMA N
 constexpr int kPfBlk = 8;            // token rows per block of the register-fragment (mma.sync) path
-constexpr int kPfThreads = 256;
-constexpr int kPfWarps = kPfThreads / 32;
 constexpr int kPfTmemCols = 512;     // 8 group accumulators x 64 columns
 constexpr int kPfGroups = 8;         // 32-column quantisation groups per 256-column block
 
-// shared-memory map of the GEMM kernel (offsets from a 1024-byte aligned base)
-constexpr int kPfA = 0;                              // 4 sub-tiles x [128 rows x 128 B]
-constexpr int kPfASub = kPfRows * 128;               // 16 KB
-constexpr int kPfB = 4 * kPfASub;                    // 2 stages x 4 sub-tiles x [64 rows x 128 B]
-constexpr int kPfBSub = kPfCols * 128;               // 8 KB
-constexpr int kPfBStage = 4 * kPfBSub;
-constexpr int kPfU = kPfB + 2 * kPfBStage;           // 2 stages x 8 units of 2560 B
-constexpr int kPfUStage = 8 * kUnitBytes;
-constexpr int kPfS = kPfU + 2 * kPfUStage;           // group sums [8][64] f32
-constexpr int kPfBar = kPfS + kPfGroups * kPfCols * 4;   // 3 mbarriers + TMEM address
-constexpr int kPfSmem = kPfBar + 64;
-constexpr int kPfSmemAlloc = kPfSmem + 1024;         // room to align the base
+// operand tiles of the tensor-core kernel
+constexpr int kPfASub = kPfRows * 128;               // A: [128 rows x 128 B] per 64-column sub-tile
+constexpr int kPfBSub = kPfCols * 128;               // B: [64 rows x 128 B] per 64-column sub-tile
+constexpr int kPfBStage = 4 * kPfBSub;               // B of one 256-column k-block
+constexpr int kPfUStage = 8 * kUnitBytes;            // the 8 units of a 128-row tile's k-block
 constexpr int kPfPlanSmemMax = kGemvSmemLimit - 8 * 1024;   // dynamic part of the plan kernel (static: ~4.1 KB)
 
 struct PfScratch {
@@ -82,15 +78,12 @@ struct PfScratch {
   int32_t *blk_expert, *blk_row0, *blk_n;   // 8-row token blocks of the permuted rows
   uint32_t *xf;             // the blocks' staged activations (f16 fragments), for K up to max(hidden, inter_pad)
   void *xaux;               // and their aux words
+  uint16_t *x_perm;         // [P][hidden] token rows in permuted order (the gate/up GEMM's B rows)
+  float *ssum_x, *ssum_act; // group sums of x_perm / act rows: [P][hidden / 32], [P][inter_pad / 32]
+  CUtensorMap tm_x, tm_act, tm_sx, tm_sact;   // TMA maps of those four arrays (64-row boxes)
 };
 
 // ------------------------------------------------------------ small PTX --
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -382,6 +375,7 @@ __global__ void __launch_bounds__(1024) rc_pf_plan_kernel(PfPlanParams p) {
     if (lane == 0) {
       p.n_chunks[0] = cbase < p.chunk_cap ? cbase : p.chunk_cap;
       p.n_chunks[1] = bbase < p.blk_cap ? bbase : p.blk_cap;
+      p.n_chunks[2] = base;                       // permuted rows in all
     }
   }
   __syncthreads();
@@ -427,263 +421,442 @@ struct PfGemmParams {
   int kb;                               // K / 256
   int m_tiles;                          // weight rows / 128
   const int32_t *n_chunks, *chunk_expert, *chunk_row0, *chunk_n;
-  const uint16_t *src;                  // gate/up: x [T][ld_src]; down: act [P][ld_src]
-  int ld_src;
-  const int32_t *row_token;             // gate/up: permuted row -> token row of x; down: null
   uint16_t *y;                          // gate/up: act [P][ld_y]; down: down [P][ld_y]
   int ld_y;
-  int act;
   float gate_beta, value_beta;
   int *err;
 };
 
+// ------------------------------------------- warp-specialised grouped GEMM --
+// Warp roles, so that loads, code expansion, MMAs and promotion overlap:
+//   warp 0        producer (one thread): unit bulk copies into a 3-stage
+//                 ring; the chunk's rows and their group sums as TMA boxes
+//                 into a 2-stage ring
+//   warp 1        tensor memory owner; lane 0 issues the MMAs
+//   warps 2..5    expand a stage's codes into bf16 A tiles, a part at a
+//                 time
+//   warps 6..13   promotion: TMEM lane quarter (warp & 3), token half
+//                 ((warp - 6) >> 2); f32 accumulators in registers; the
+//                 item's epilogue
+// Tensor memory holds the 8 group accumulators of a k-block (8 x 64
+// columns); a k-block runs in kTcParts parts, and each part's accumulators
+// and A sub-tiles pass from expansion to MMAs to promotion on their own
+// barriers, so the parts of one step overlap.
+// Every wait is bounded and also watches a CTA-wide abort word, so a timeout
+// in one role unwinds all of them.
+constexpr int kTcWarps = 14;
+constexpr int kTcThreads = kTcWarps * 32;
+constexpr int kTcConvThreads = 128;            // warps 2..5
+constexpr int kTcPromoThreads = 256;           // warps 6..13
+constexpr int kTcUStages = 3;
+constexpr int kTcBStages = 2;
+constexpr int kTcParts = 2;                    // a k-block's MMAs / promotion in 2 parts of 4 groups
+constexpr int kTcGpp = kPfGroups / kTcParts;   // quantisation groups per part
+constexpr int kTcSubs = 4 / kTcParts;          // 64-column A sub-tiles per part
+constexpr int kTcTb = kTcGpp == 4 ? 8 : 16;    // token columns per TMEM read of a part's groups
+constexpr int kTcA = 0;                        // the A parts
+constexpr int kTcB = kTcA + 4 * kPfASub;       // kTcBStages x 4 sub-tiles x [64 rows x 128 B]
+constexpr int kTcS = kTcB + kTcBStages * kPfBStage;                    // kTcBStages x [64 rows][8 groups] f32
+constexpr int kTcU = kTcS + kTcBStages * kPfGroups * kPfCols * 4;      // kTcUStages x 8 units
+constexpr int kTcBar = kTcU + kTcUStages * kPfUStage;
+// barriers (8 bytes each): full_u[3] empty_u[3] full_b[2] empty_b[2] afull, amma, tfree [kTcParts] each
+constexpr int kTcNumBars = 2 * kTcUStages + 2 * kTcBStages + 3 * kTcParts;
+constexpr int kTcSmem = kTcBar + kTcNumBars * 8 + 16;
+constexpr int kTcSmemAlloc = kTcSmem + 1024;
+static_assert(kTcSmemAlloc <= kGemvSmemLimit, "warp-specialised GEMM shared memory");
+
+struct TcBars {
+  uint32_t full_u, empty_u, full_b, empty_b, afull, amma, tfree;
+};
+
+// Bounded wait that also gives up when another role has aborted.
+__device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity, const volatile int *abort_word) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_word) return false;
+    if (global_timer_ns() - t0 > 1000000000ull) return false;
+  }
+}
+
+// 2-D TMA tile load into this CTA's shared memory (no multicast), completing on ``bar``.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t addr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(addr));
+}
+
 template <int EPI>
-__global__ void __launch_bounds__(kPfThreads, 1) rc_pf_gemm_kernel(PfGemmParams p) {
+__global__ void __launch_bounds__(kTcThreads, 1)
+    rc_pf_tc_kernel(const __grid_constant__ PfGemmParams p, const __grid_constant__ CUtensorMap tm_b,
+                    const __grid_constant__ CUtensorMap tm_s) {
   extern __shared__ uint8_t pf_raw_smem[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(pf_raw_smem) + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int lq = warp & 3;            // TMEM lane quarter this warp may read
-  const int ch = warp >> 2;           // token-column half this warp promotes
-  uint8_t *sA = sm + kPfA;
-  float *sS = reinterpret_cast<float *>(sm + kPfS);
-  const uint32_t bar_u0 = smem_addr(sm + kPfBar), bar_mma = bar_u0 + 16;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kPfBar + 32);
+  const uint32_t bar0 = smem_addr(sm + kTcBar);
+  const uint32_t bar_p = bar0 + 16 * kTcUStages + 16 * kTcBStages;   // the per-part barriers
+  const TcBars bars{bar0, bar0 + 8 * kTcUStages, bar0 + 16 * kTcUStages, bar0 + 16 * kTcUStages + 8 * kTcBStages,
+                    bar_p, bar_p + 8 * kTcParts, bar_p + 16 * kTcParts};
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kTcBar + kTcNumBars * 8);
+  volatile int *abort_word = reinterpret_cast<volatile int *>(sm + kTcBar + kTcNumBars * 8 + 4);
 
-  if (warp == 0) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
                  "r"(kPfTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(bar_u0, 1);
-    mbar_init(bar_u0 + 8, 1);
-    mbar_init(bar_mma, 1);
+    *abort_word = 0;
+    for (int i = 0; i < kTcUStages; ++i) {
+      mbar_init(bars.full_u + 8 * i, 1);
+      mbar_init(bars.empty_u + 8 * i, kTcConvThreads + kTcPromoThreads);
+    }
+    for (int i = 0; i < kTcBStages; ++i) {
+      mbar_init(bars.full_b + 8 * i, 1);
+      mbar_init(bars.empty_b + 8 * i, 1 + kTcPromoThreads);
+    }
+    for (int q = 0; q < kTcParts; ++q) {
+      mbar_init(bars.afull + 8 * q, kTcConvThreads);
+      mbar_init(bars.amma + 8 * q, 1);
+      mbar_init(bars.tfree + 8 * q, kTcPromoThreads);
+    }
     mbar_fence_init();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint64_t pol = policy_evict_first();
   const int n_chunks = *p.n_chunks;
   const int n_items = n_chunks * p.m_tiles;
-  uint32_t ph_u[2] = {0u, 0u}, ph_mma = 0u;
+  const int kb = p.kb;
   bool failed = false;
-  const int r_row = 32 * lq + lane;                 // TMEM lane = weight row of the tile
-  const int u_row = r_row >> 4, rr = r_row & 15;
 
-  for (int item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
-    const int chunk = item % n_chunks, m = item / n_chunks;
-    const int e = p.chunk_expert[chunk], row0 = p.chunk_row0[chunk], n = p.chunk_n[chunk];
-    const int n16 = (n + 15) & ~15;
-    const uint8_t *wt = p.expert_tiles[e];
-    if (wt == nullptr) {
-      if (tid == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
-      continue;
-    }
-    // source rows of this thread's B chunks: token row warp + 8j, 16-byte column chunk `lane`
-    const uint16_t *srow[kPfCols / kPfWarps];
-#pragma unroll
-    for (int j = 0; j < kPfCols / kPfWarps; ++j) {
-      const int r = warp + kPfWarps * j;
-      srow[j] = nullptr;
-      if (r < n) {
-        const int prow = row0 + r;
-        const int srcr = EPI != kPfEpiDown ? p.row_token[prow] : prow;
-        srow[j] = p.src + (size_t)srcr * p.ld_src;
-      }
-    }
-    auto issue_units = [&](int kbi, int st) {
-      if (tid == 0) {
-        mbar_arrive_expect_tx(bar_u0 + 8 * st, kPfUStage);
-        for (int u = 0; u < 8; ++u)
-          bulk_copy_g2s(smem_addr(sm + kPfU + st * kPfUStage + u * kUnitBytes),
-                        wt + ((size_t)(8 * m + u) * p.kb + kbi) * kUnitBytes, kUnitBytes, bar_u0 + 8 * st, pol);
-      }
-    };
-    auto issue_b = [&](int kbi, int st) {
-      uint8_t *sB = sm + kPfB + st * kPfBStage;
-#pragma unroll
-      for (int j = 0; j < kPfCols / kPfWarps; ++j) {
-        const int r = warp + kPfWarps * j;
-        const uint32_t dst = smem_addr(sB + (lane >> 3) * kPfBSub + sw128_off(r, (lane & 7) * 8));
-        const uint16_t *src = srow[j] ? srow[j] + kbi * kUnitK + lane * 8 : p.src;
-        cp_async16(dst, src, srow[j] ? 16u : 0u);
-      }
-      cp_async_commit();
-    };
-
-    float acc[kPfCols / 2];
-#pragma unroll
-    for (int i = 0; i < kPfCols / 2; ++i) acc[i] = 0.f;
-    issue_units(0, 0);
-    issue_b(0, 0);
-    for (int kbi = 0; kbi < p.kb; ++kbi) {
-      const int st = kbi & 1;
-      if (kbi + 1 < p.kb) {
-        issue_units(kbi + 1, st ^ 1);
-        issue_b(kbi + 1, st ^ 1);
-        cp_async_wait_1();
-      } else {
-        cp_async_wait_all();
-      }
-      __syncthreads();                                // B(kbi) visible to all threads
-      {
-        // group sums of the B rows: (row idx & 63, group idx >> 6)
-        const uint8_t *sB = sm + kPfB + st * kPfBStage;
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int idx = tid + kPfThreads * i;
-          const int r = idx & 63, g = idx >> 6;
-          float part = 0.f;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int kc = g * 4 + c;
-            const uint4 v = *reinterpret_cast<const uint4 *>(sB + (kc >> 3) * kPfBSub + sw128_off(r, (kc & 7) * 8));
-            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) part += bf16_to_f32(w4[q] & 0xFFFFu) + bf16_to_f32(w4[q] >> 16);
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // One thread: per step the 8 weight units (bulk copies) and, as TMA tiles
+    // of the permuted rows, the chunk's 64 source rows (four 64-column
+    // swizzled boxes) and their group sums.
+    int u_filled = 0, b_filled = 0;   // steps whose unit / row stage was issued
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int step = 0;
+      for (int item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
+        const int chunk = item % n_chunks, m = item / n_chunks;
+        const int e = p.chunk_expert[chunk], row0 = p.chunk_row0[chunk];
+        const uint8_t *wt = p.expert_tiles[e];
+        for (int kbi = 0; kbi < kb; ++kbi, ++step) {
+          const int us = step % kTcUStages, bs = step % kTcBStages;
+          if (step >= kTcUStages && !tc_wait(bars.empty_u + 8 * us, ((step / kTcUStages) - 1) & 1, abort_word)) {
+            failed = true;
+            break;
           }
-          sS[g * kPfCols + r] = part;
+          // an expert that is not loaded: the stage completes without data
+          // (its outputs are garbage) and the call reports the error word
+          mbar_arrive_expect_tx(bars.full_u + 8 * us, wt != nullptr ? kPfUStage : 0u);
+          if (wt == nullptr) atomicCAS(p.err, 0, kErrWaitTimeout);
+          if (wt != nullptr)
+            for (int u = 0; u < 8; ++u)
+              bulk_copy_g2s(smem_addr(sm + kTcU + us * kPfUStage + u * kUnitBytes),
+                            wt + ((size_t)(8 * m + u) * kb + kbi) * kUnitBytes, kUnitBytes, bars.full_u + 8 * us,
+                            pol);
+          u_filled = step + 1;
+          if (step >= kTcBStages && !tc_wait(bars.empty_b + 8 * bs, ((step / kTcBStages) - 1) & 1, abort_word)) {
+            failed = true;
+            break;
+          }
+          const uint32_t fb = bars.full_b + 8 * bs;
+          mbar_arrive_expect_tx(fb, kPfBStage + kPfGroups * kPfCols * 4);
+          const uint32_t sB = smem_addr(sm + kTcB + bs * kPfBStage);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tma_load_2d(sB + j * kPfBSub, &tm_b, kbi * kUnitK + 64 * j, row0, fb);
+          tma_load_2d(smem_addr(sm + kTcS + bs * kPfGroups * kPfCols * 4), &tm_s, kbi * kPfGroups, row0, fb);
+          b_filled = step + 1;
         }
       }
-      const bool ok_u = mbar_wait_bounded(bar_u0 + 8 * st, ph_u[st]);
-      ph_u[st] ^= 1u;
-      if (__syncthreads_or(!ok_u)) {
-        failed = true;
-        break;
+      if (failed) *abort_word = 1;
+      // every copy issued lands before the shared memory goes away: wait for
+      // the last fill of each stage (these complete whatever the other roles do)
+      const int zero = 0;
+      for (int us = 0; us < kTcUStages; ++us) {
+        const int fills = (u_filled + kTcUStages - 1 - us) / kTcUStages;
+        if (fills > 0) tc_wait(bars.full_u + 8 * us, (fills - 1) & 1, &zero);
       }
-      {
-        // weight codes -> bf16 (128 + code): one quad of fragment words (lanes
-        // 4g..4g+3 of step s) holds 8 consecutive columns of rows g and g+8
-        // twice over, written as four 16-byte swizzled chunks
-        const uint8_t *U = sm + kPfU + st * kPfUStage;
+      for (int bs = 0; bs < kTcBStages; ++bs) {
+        const int fills = (b_filled + kTcBStages - 1 - bs) / kTcBStages;
+        if (fills > 0) tc_wait(bars.full_b + 8 * bs, (fills - 1) & 1, &zero);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    int step = 0;
+    uint32_t commits[kTcParts] = {};   // completions issued on amma[q]
+    for (int item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
+      const int chunk = item % n_chunks;
+      const int n16 = (p.chunk_n[chunk] + 15) & ~15;
+      const uint32_t idesc = umma_idesc_bf16(kPfRows, n16);
+      for (int kbi = 0; kbi < kb && !failed; ++kbi, ++step) {
+        const int bs = step % kTcBStages;
+        if (__any_sync(0xffffffffu, !tc_wait(bars.full_b + 8 * bs, (step / kTcBStages) & 1, abort_word))) {
+          failed = true;
+          break;
+        }
+        for (int q = 0; q < kTcParts; ++q) {
+          if (__any_sync(0xffffffffu, !tc_wait(bars.afull + 8 * q, step & 1, abort_word) ||
+                                          (step > 0 && !tc_wait(bars.tfree + 8 * q, (step - 1) & 1, abort_word)))) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint64_t da = umma_desc_sw128(smem_addr(sm + kTcA + q * kTcSubs * kPfASub));
+            const uint64_t db = umma_desc_sw128(smem_addr(sm + kTcB + bs * kPfBStage + q * kTcSubs * kPfBSub));
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int gi = tid + kPfThreads * j;
-          const int u = gi >> 7, rem = gi & 127, s = rem >> 3, g = rem & 7;
-          const uint8_t *base = U + u * kUnitBytes + ((s >> 2) * 32 + 4 * g) * 16 + (s & 3) * 4;
-          uint32_t w[4];
+            for (int gg = 0; gg < kTcGpp; ++gg) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) w[q] = *reinterpret_cast<const uint32_t *>(base + q * 16);
-          const int ra = 16 * u + g, rb = ra + 8;
-          uint8_t *A = sA + (s >> 2) * kPfASub;
-          const int kk = 16 * (s & 3);
-          *reinterpret_cast<uint4 *>(A + sw128_off(ra, kk)) =
-              make_uint4(codes_to_bf16x2<0>(w[0]), codes_to_bf16x2<0>(w[1]), codes_to_bf16x2<0>(w[2]),
-                         codes_to_bf16x2<0>(w[3]));
-          *reinterpret_cast<uint4 *>(A + sw128_off(ra, kk + 8)) =
-              make_uint4(codes_to_bf16x2<2>(w[0]), codes_to_bf16x2<2>(w[1]), codes_to_bf16x2<2>(w[2]),
-                         codes_to_bf16x2<2>(w[3]));
-          *reinterpret_cast<uint4 *>(A + sw128_off(rb, kk)) =
-              make_uint4(codes_to_bf16x2<1>(w[0]), codes_to_bf16x2<1>(w[1]), codes_to_bf16x2<1>(w[2]),
-                         codes_to_bf16x2<1>(w[3]));
-          *reinterpret_cast<uint4 *>(A + sw128_off(rb, kk + 8)) =
-              make_uint4(codes_to_bf16x2<3>(w[0]), codes_to_bf16x2<3>(w[1]), codes_to_bf16x2<3>(w[2]),
-                         codes_to_bf16x2<3>(w[3]));
+              for (int hh = 0; hh < 2; ++hh) {
+                const int kk = gg * 32 + hh * 16;      // column within the part: sub-tile kk / 64, column kk % 64
+                umma_bf16(tbase + (kTcGpp * q + gg) * kPfCols,
+                          da + (uint64_t)(((kk >> 6) * kPfASub + (kk & 63) * 2) >> 4),
+                          db + (uint64_t)(((kk >> 6) * kPfBSub + (kk & 63) * 2) >> 4), idesc, (uint32_t)hh);
+              }
+            }
+            umma_commit(bars.amma + 8 * q);
+            if (q == kTcParts - 1) umma_commit(bars.empty_b + 8 * bs);
+          }
+          __syncwarp();
+          ++commits[q];
         }
       }
-      // this thread's row parameters for the 8 groups
-      float sc[kPfGroups], mp[kPfGroups];
-      {
-        const uint8_t *P = sm + kPfU + st * kPfUStage + u_row * kUnitBytes + kUnitCodeBytes;
-#pragma unroll
-        for (int g = 0; g < kPfGroups; ++g) {
-          const uint32_t pw = *reinterpret_cast<const uint32_t *>(P + ((rr & 7) * 8 + g) * 8 + (rr >> 3) * 4);
-          sc[g] = bf16_lo_f32(pw);
-          mp[g] = fmaf(-128.f, sc[g], bf16_hi_f32(pw));
+    }
+    if (failed) *abort_word = 1;
+    // no MMA may still run when tensor memory is released (the abort word is
+    // not consulted here: these commits always complete)
+    const int zero = 0;
+    for (int q = 0; q < kTcParts; ++q)
+      if (commits[q] > 0) tc_wait(bars.amma + 8 * q, (commits[q] - 1) & 1, &zero);
+  } else if (warp < 6) {
+    // ----------------------------------------------------- code expansion
+    const int ct = tid - 64;
+    int step = 0;
+    for (int item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
+      for (int kbi = 0; kbi < kb && !failed; ++kbi, ++step) {
+        const int us = step % kTcUStages;
+        if (__any_sync(0xffffffffu, !tc_wait(bars.full_u + 8 * us, (step / kTcUStages) & 1, abort_word))) {
+          failed = true;
+          break;
         }
+        const uint8_t *U = sm + kTcU + us * kPfUStage;
+        for (int q = 0; q < kTcParts; ++q) {
+          // the MMAs that read this A part in the previous step are done
+          if (step > 0 && __any_sync(0xffffffffu, !tc_wait(bars.amma + 8 * q, (step - 1) & 1, abort_word))) {
+            failed = true;
+            break;
+          }
+          uint8_t *Ap = sm + kTcA + q * kTcSubs * kPfASub;
+          constexpr int kPer = 128 / kTcParts;                // items of a unit in one part
+#pragma unroll
+          for (int j = 0; j < 8 / kTcParts; ++j) {
+            const int gi = ct + kTcConvThreads * j;           // unit, k-step of the part, row group
+            const int u = gi / kPer, rem = gi % kPer, s = 4 * kTcSubs * q + (rem >> 3), g = rem & 7;
+            const uint8_t *base = U + u * kUnitBytes + ((s >> 2) * 32 + 4 * g) * 16 + (s & 3) * 4;
+            // the four words sit 16 B apart: lanes start at word (g >> 1) so that
+            // a warp's 32 loads fall in 32 different banks, then rotate back
+            const int rot = (g >> 1) & 3;
+            uint32_t v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const uint32_t *>(base + ((i + rot) & 3) * 16);
+            const bool r1 = rot & 1, r2 = rot & 2;
+            const uint32_t t0 = r1 ? v[3] : v[0], t1 = r1 ? v[0] : v[1], t2 = r1 ? v[1] : v[2], t3 = r1 ? v[2] : v[3];
+            const uint32_t w[4] = {r2 ? t2 : t0, r2 ? t3 : t1, r2 ? t0 : t2, r2 ? t1 : t3};
+            const int ra = 16 * u + g, rb = ra + 8;
+            const int kk = 16 * (s & 3);
+            uint8_t *As = Ap + ((s >> 2) - kTcSubs * q) * kPfASub;
+            *reinterpret_cast<uint4 *>(As + sw128_off(ra, kk)) =
+                make_uint4(codes_to_bf16x2<0>(w[0]), codes_to_bf16x2<0>(w[1]), codes_to_bf16x2<0>(w[2]),
+                           codes_to_bf16x2<0>(w[3]));
+            *reinterpret_cast<uint4 *>(As + sw128_off(ra, kk + 8)) =
+                make_uint4(codes_to_bf16x2<2>(w[0]), codes_to_bf16x2<2>(w[1]), codes_to_bf16x2<2>(w[2]),
+                           codes_to_bf16x2<2>(w[3]));
+            *reinterpret_cast<uint4 *>(As + sw128_off(rb, kk)) =
+                make_uint4(codes_to_bf16x2<1>(w[0]), codes_to_bf16x2<1>(w[1]), codes_to_bf16x2<1>(w[2]),
+                           codes_to_bf16x2<1>(w[3]));
+            *reinterpret_cast<uint4 *>(As + sw128_off(rb, kk + 8)) =
+                make_uint4(codes_to_bf16x2<3>(w[0]), codes_to_bf16x2<3>(w[1]), codes_to_bf16x2<3>(w[2]),
+                           codes_to_bf16x2<3>(w[3]));
+          }
+          fence_proxy_async();
+          mbar_arrive(bars.afull + 8 * q);
+        }
+        if (!failed) mbar_arrive(bars.empty_u + 8 * us);
       }
-      fence_proxy_async();
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      if (tid == 0) {
-        const uint8_t *sB = sm + kPfB + st * kPfBStage;
-        const uint32_t idesc = umma_idesc_bf16(kPfRows, n16);
-        // descriptors advance by (byte offset >> 4) in their start-address
-        // field (no carry: shared addresses stay below 256 KB).  One thread
-        // issues an MMA only every ~60 cycles, so the issue loop is kept to an
-        // add per operand.
-        const uint64_t da = umma_desc_sw128(smem_addr(sA)), db = umma_desc_sw128(smem_addr(sB));
+    }
+    if (failed) *abort_word = 1;
+  } else {
+    // ------------------------------------------------------------ promotion
+    const int lq = warp & 3, ch = (warp - 6) >> 2;
+    const int r_row = 32 * lq + lane;
+    const int u_row = r_row >> 4, rr = r_row & 15;
+    int step = 0;
+    for (int item = blockIdx.x; item < n_items && !failed; item += gridDim.x) {
+      const int chunk = item % n_chunks, m = item / n_chunks;
+      const int row0 = p.chunk_row0[chunk], n = p.chunk_n[chunk];
+      const int n16 = (n + 15) & ~15;
+      const bool active = 32 * ch < n16;
+      float2 acc[kPfCols / 4];
 #pragma unroll
-        for (int g = 0; g < kPfGroups; ++g) {
+      for (int i = 0; i < kPfCols / 4; ++i) acc[i] = make_float2(0.f, 0.f);
+      for (int kbi = 0; kbi < kb && !failed; ++kbi, ++step) {
+        const int us = step % kTcUStages, bs = step % kTcBStages;
+        if (__any_sync(0xffffffffu, !tc_wait(bars.full_u + 8 * us, (step / kTcUStages) & 1, abort_word))) {
+          failed = true;
+          break;
+        }
+        float sc[kPfGroups], mp[kPfGroups];
+        {
+          const uint8_t *P = sm + kTcU + us * kPfUStage + u_row * kUnitBytes + kUnitCodeBytes;
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int k0 = g * 32 + h * 16, sub = k0 >> 6, kk = k0 & 63;
-            umma_bf16(tbase + g * kPfCols, da + (uint64_t)((sub * kPfASub + kk * 2) >> 4),
-                      db + (uint64_t)((sub * kPfBSub + kk * 2) >> 4), idesc, (uint32_t)h);
+          for (int g = 0; g < kPfGroups; ++g) {
+            const uint32_t pw = *reinterpret_cast<const uint32_t *>(P + ((rr & 7) * 8 + g) * 8 + (rr >> 3) * 4);
+            sc[g] = bf16_lo_f32(pw);
+            mp[g] = fmaf(-128.f, sc[g], bf16_hi_f32(pw));
           }
         }
-        umma_commit(bar_mma);
-      }
-      const bool ok_m = mbar_wait_bounded(bar_mma, ph_mma);
-      ph_mma ^= 1u;
-      if (__syncthreads_or(!ok_m)) {
-        failed = true;
-        break;
-      }
-      tc_fence_after();
-      // promotion: acc += scale * D_g + (min - 128 scale) * S_g for this
-      // warp's 32 token columns
+        mbar_arrive(bars.empty_u + 8 * us);
+        // the stage's group sums (TMA writes, acquired through the stage's barrier)
+        if (__any_sync(0xffffffffu, !tc_wait(bars.full_b + 8 * bs, (step / kTcBStages) & 1, abort_word))) {
+          failed = true;
+          break;
+        }
+        const float *sS = reinterpret_cast<const float *>(sm + kTcS + bs * kPfGroups * kPfCols * 4);
 #pragma unroll
-      for (int g = 0; g < kPfGroups; ++g) {
-        const float sgl = sc[g], a3 = mp[g];
-        const float *Sg = sS + g * kPfCols + 32 * ch;
-        if (32 * ch < n16) {
-          // both 16-column halves in flight before one wait
-          uint32_t v[2][16];
-          const uint32_t ta = tbase + ((uint32_t)(32 * lq) << 16) + g * kPfCols + 32 * ch;
-          tmem_ld16(ta, v[0]);
-          if (32 * ch + 16 < n16) tmem_ld16(ta + 16, v[1]);
-          tmem_wait_ld();
+        for (int q = 0; q < kTcParts; ++q) {
+          if (failed || __any_sync(0xffffffffu, !tc_wait(bars.amma + 8 * q, step & 1, abort_word))) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          if (active) {
+            float2 a3[kTcGpp], sg[kTcGpp];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (32 * ch + 16 * h < n16) {
+            for (int gg = 0; gg < kTcGpp; ++gg) {
+              a3[gg] = make_float2(mp[kTcGpp * q + gg], mp[kTcGpp * q + gg]);
+              sg[gg] = make_float2(sc[kTcGpp * q + gg], sc[kTcGpp * q + gg]);
+            }
 #pragma unroll
-              for (int j = 0; j < 16; ++j)
-                acc[16 * h + j] = fmaf(sgl, __uint_as_float(v[h][j]), fmaf(a3, Sg[16 * h + j], acc[16 * h + j]));
+            for (int tb = 0; tb < 32 / kTcTb; ++tb) {
+              // kTcTb token columns of the part's group accumulators, one wait
+              uint32_t v[kTcGpp][kTcTb];
+#pragma unroll
+              for (int gg = 0; gg < kTcGpp; ++gg) {
+                const uint32_t ta = tbase + ((uint32_t)(32 * lq) << 16) + (kTcGpp * q + gg) * kPfCols + 32 * ch + kTcTb * tb;
+                if constexpr (kTcTb == 8) tmem_ld8(ta, *reinterpret_cast<uint32_t(*)[8]>(&v[gg][0]));
+                else tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(&v[gg][0]));
+              }
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < kTcTb / 2; ++j) {
+                const int t = 32 * ch + kTcTb * tb + 2 * j;
+                float s0[kTcGpp], s1[kTcGpp];
+                if constexpr (kTcGpp == 4) {
+                  const float4 x0 = *reinterpret_cast<const float4 *>(sS + t * kPfGroups + kTcGpp * q);
+                  const float4 x1 = *reinterpret_cast<const float4 *>(sS + (t + 1) * kPfGroups + kTcGpp * q);
+                  s0[0] = x0.x, s0[1] = x0.y, s0[2] = x0.z, s0[3] = x0.w;
+                  s1[0] = x1.x, s1[1] = x1.y, s1[2] = x1.z, s1[3] = x1.w;
+                } else {
+#pragma unroll
+                  for (int gg = 0; gg < kTcGpp; ++gg) {
+                    s0[gg] = sS[t * kPfGroups + kTcGpp * q + gg];
+                    s1[gg] = sS[(t + 1) * kPfGroups + kTcGpp * q + gg];
+                  }
+                }
+                float2 &ac = acc[(kTcTb / 2) * tb + j];
+#pragma unroll
+                for (int gg = 0; gg < kTcGpp; ++gg) {
+                  ac = __ffma2_rn(a3[gg], make_float2(s0[gg], s1[gg]), ac);
+                  ac = __ffma2_rn(sg[gg], make_float2(__uint_as_float(v[gg][2 * j]), __uint_as_float(v[gg][2 * j + 1])),
+                                  ac);
+                }
+              }
             }
           }
+          tc_fence_before();
+          mbar_arrive(bars.tfree + 8 * q);
+        }
+        if (!failed) mbar_arrive(bars.empty_b + 8 * bs);
+      }
+      if (failed) break;
+      // ---- epilogue: this warp's 32 token columns
+      float a[kPfCols / 2];
+#pragma unroll
+      for (int i = 0; i < kPfCols / 4; ++i) a[2 * i] = acc[i].x, a[2 * i + 1] = acc[i].y;
+      if (EPI != kPfEpiDown) {
+        const int col = 8 * (8 * m + u_row) + rr;       // rows rr < 8: gate, rr >= 8: up of the same column
+#pragma unroll
+        for (int t = 0; t < kPfCols / 2; ++t) {
+          const float up = __shfl_down_sync(0xffffffffu, a[t], 8);
+          const int tok = 32 * ch + t;
+          if (rr < 8 && tok < n) {
+            const float gate = bf16_round(a[t]);
+            const float u = bf16_round(up);
+            const float v = EPI == kPfEpiSitu ? act_situ(gate, u, p.gate_beta, p.value_beta) : act_swiglu(gate, u);
+            p.y[(size_t)(row0 + tok) * p.ld_y + col] = f32_to_bf16_rne(v);
+          }
+        }
+      } else {
+        const int col = kPfRows * m + r_row;
+#pragma unroll
+        for (int t = 0; t < kPfCols / 2; ++t) {
+          const int tok = 32 * ch + t;
+          if (tok < n) p.y[(size_t)(row0 + tok) * p.ld_y + col] = f32_to_bf16_rne(a[t]);
         }
       }
-      tc_fence_before();
-      __syncthreads();                                // TMEM, A and this stage's B/U free again
     }
-    if (failed) break;
-    // ---- epilogue: this warp's 32 token columns
-    if (EPI != kPfEpiDown) {
-      const int col = 8 * (8 * m + u_row) + rr;       // rows rr < 8: gate, rr >= 8: up of the same column
-#pragma unroll
-      for (int t = 0; t < kPfCols / 2; ++t) {
-        const float up = __shfl_down_sync(0xffffffffu, acc[t], 8);
-        const int tok = 32 * ch + t;
-        if (rr < 8 && tok < n) {
-          const float gate = bf16_round(acc[t]);
-          const float u = bf16_round(up);
-          const float v = EPI == kPfEpiSitu ? act_situ(gate, u, p.gate_beta, p.value_beta) : act_swiglu(gate, u);
-          p.y[(size_t)(row0 + tok) * p.ld_y + col] = f32_to_bf16_rne(v);
-        }
-      }
-    } else {
-      const int col = kPfRows * m + r_row;
-#pragma unroll
-      for (int t = 0; t < kPfCols / 2; ++t) {
-        const int tok = 32 * ch + t;
-        if (tok < n) p.y[(size_t)(row0 + tok) * p.ld_y + col] = f32_to_bf16_rne(acc[t]);
-      }
-    }
+    if (failed) *abort_word = 1;
   }
-  if (failed && tid == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
-  // let copies still in flight land before the shared memory is released
-  cp_async_wait_all();
-  if (failed && tid == 0) {
-    mbar_wait_bounded(bar_u0, ph_u[0]);
-    mbar_wait_bounded(bar_u0 + 8, ph_u[1]);
-  }
+  if (failed && lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kPfTmemCols));
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kPfTmemCols));
+}
+
+// Rows of the tensor-core GEMMs: for each of the *n_rows permuted rows r,
+// source row row_token[r] (or r itself when row_token is null) copied to
+// dst[r] (when dst is set), and its group sums s[r][g]: the group's four
+// 8-column chunks in turn, each chunk's four bf16 pairs added pairwise first.
+__global__ void rc_pf_rows_kernel(const uint16_t *src, int K, int ld, const int32_t *row_token, const int32_t *n_rows,
+                                  uint16_t *dst, float *s) {
+  const int groups = K / 32, total = *n_rows * groups;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int r = i / groups, g = i - r * groups;
+    const int sr = row_token ? row_token[r] : r;
+    const uint4 *p = reinterpret_cast<const uint4 *>(src + (size_t)sr * ld + 32 * g);
+    uint4 v[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] = __ldg(p + c);
+    if (dst) {
+      uint4 *d = reinterpret_cast<uint4 *>(dst + (size_t)r * K + 32 * g);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) d[c] = v[c];
+    }
+    float part = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t w4[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) part += bf16_to_f32(w4[q] & 0xFFFFu) + bf16_to_f32(w4[q] >> 16);
+    }
+    s[i] = part;
+  }
 }
 
 // ------------------------------------------------ register-fragment path --
@@ -931,6 +1104,36 @@ __global__ void rc_pf_identity_rows_kernel(int32_t *rows, int n) {
 }
 
 // ------------------------------------------------------------------ host --
+// A 2-D TMA map of a row-major [rows][cols] array with (box_cols x box_rows)
+// boxes; rows past the end read as zeros.  The encoder is the driver's,
+// reached through the runtime (no link against the driver library).
+static bool tma_map_2d(CUtensorMap *map, void *base, CUtensorMapDataType type, int esize, int cols, size_t rows,
+                       int box_cols, int box_rows, bool swizzle128, const char **why) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (encode == nullptr) {
+    cudaDriverEntryPointQueryResult q{};
+    void *fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr) {
+      *why = "cuTensorMapEncodeTiled is not available";
+      return false;
+    }
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const cuuint64_t dim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t stride[1] = {(cuuint64_t)cols * esize};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = encode(map, type, 2, base, dim, stride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *why = "cuTensorMapEncodeTiled rejected a map";
+    return false;
+  }
+  return true;
+}
+
 static void pf_release(PfScratch *s) {
   if (!s) return;
   cudaFree(s->logits);
@@ -953,6 +1156,9 @@ static void pf_release(PfScratch *s) {
   cudaFree(s->blk_n);
   cudaFree(s->xf);
   cudaFree(s->xaux);
+  cudaFree(s->x_perm);
+  cudaFree(s->ssum_x);
+  cudaFree(s->ssum_act);
   delete s;
 }
 
@@ -985,12 +1191,15 @@ static int pf_scratch(rc_moe *m, int T) {
   if (e == cudaSuccess) e = cudaMalloc(&s->row_token, P * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->cnt, (size_t)(E + 1) * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->off, (size_t)(E + 1) * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&s->n_chunks, 8);
+  if (e == cudaSuccess) e = cudaMalloc(&s->n_chunks, 16);
   if (e == cudaSuccess) e = cudaMalloc(&s->blk_expert, (size_t)s->blk_cap * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->blk_row0, (size_t)s->blk_cap * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->blk_n, (size_t)s->blk_cap * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->xf, xfrag_bytes(s->blk_cap, kmax));
   if (e == cudaSuccess) e = cudaMalloc(&s->xaux, xaux_bytes(s->blk_cap, kmax));
+  if (e == cudaSuccess) e = cudaMalloc(&s->x_perm, P * m->hidden * 2);
+  if (e == cudaSuccess) e = cudaMalloc(&s->ssum_x, P * (m->hidden / 32) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->ssum_act, P * (m->inter_pad / 32) * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->chunk_expert, (size_t)s->chunk_cap * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->chunk_row0, (size_t)s->chunk_cap * 4);
   if (e == cudaSuccess) e = cudaMalloc(&s->chunk_n, (size_t)s->chunk_cap * 4);
@@ -1002,24 +1211,43 @@ static int pf_scratch(rc_moe *m, int T) {
     set_error("MoE prefill scratch for %d tokens: %s", T, cudaGetErrorString(e));
     return RC_ERR_CUDA;
   }
+  const char *why = nullptr;
+  if (!tma_map_2d(&s->tm_x, s->x_perm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->hidden, P, 64, 64, true, &why) ||
+      !tma_map_2d(&s->tm_act, s->act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->inter_pad, P, 64, 64, true, &why) ||
+      !tma_map_2d(&s->tm_sx, s->ssum_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m->hidden / 32, P, kPfGroups, 64, false,
+                  &why) ||
+      !tma_map_2d(&s->tm_sact, s->ssum_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m->inter_pad / 32, P, kPfGroups, 64,
+                  false, &why)) {
+    pf_release(s);
+    set_error("MoE prefill tensor maps: %s", why);
+    return RC_ERR_CUDA;
+  }
   m->pf = s;
   return RC_OK;
 }
 
 template <int EPI>
-static cudaError_t pf_launch_gemm(const rc_ctx *ctx, const PfGemmParams &p, cudaStream_t s) {
+static cudaError_t pf_launch_tc(const rc_ctx *ctx, const PfGemmParams &p, const CUtensorMap &tm_b,
+                                const CUtensorMap &tm_s, cudaStream_t s) {
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(rc_pf_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemAlloc);
+    e = cudaFuncSetAttribute(rc_pf_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemAlloc);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured[dev] = true;
   }
   // No programmatic overlap: a CTA of the next kernel must never sit on an SM
   // waiting for this grid while holding what this grid needs (tensor memory).
-  rc_pf_gemm_kernel<EPI><<<ctx->sm_count, kPfThreads, kPfSmemAlloc, s>>>(p);
+  rc_pf_tc_kernel<EPI><<<ctx->sm_count, kTcThreads, kTcSmemAlloc, s>>>(p, tm_b, tm_s);
+  return cudaGetLastError();
+}
+
+// The permuted source rows of a tensor-core GEMM and their group sums.
+static cudaError_t pf_rows(const rc_ctx *ctx, const uint16_t *src, int K, int ld, const int32_t *row_token,
+                           const int32_t *n_rows, uint16_t *dst, float *ssum, cudaStream_t s) {
+  rc_pf_rows_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(src, K, ld, row_token, n_rows, dst, ssum);
   return cudaGetLastError();
 }
 
@@ -1157,29 +1385,26 @@ static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t
   g.chunk_expert = ps->chunk_expert;
   g.chunk_row0 = ps->chunk_row0;
   g.chunk_n = ps->chunk_n;
-  g.src = x;
-  g.ld_src = m->hidden;
-  g.row_token = ps->row_token;
   g.y = ps->act;
   g.ld_y = m->inter_pad;
-  g.act = r.act;
   g.gate_beta = r.gb;
   g.value_beta = r.vb;
   g.err = m->ctx->err;
+  // the chunks' token rows in permuted order, with their group sums
+  RC_CUDA_TRY(pf_rows(m->ctx, x, m->hidden, m->hidden, ps->row_token, ps->n_chunks + 2, ps->x_perm, ps->ssum_x, s));
   if (r.act == RC_ACT_SITU)
-    RC_CUDA_TRY(pf_launch_gemm<kPfEpiSitu>(m->ctx, g, s));
+    RC_CUDA_TRY(pf_launch_tc<kPfEpiSitu>(m->ctx, g, ps->tm_x, ps->tm_sx, s));
   else
-    RC_CUDA_TRY(pf_launch_gemm<kPfEpiSwiglu>(m->ctx, g, s));
+    RC_CUDA_TRY(pf_launch_tc<kPfEpiSwiglu>(m->ctx, g, ps->tm_x, ps->tm_sx, s));
   PfGemmParams d = g;
   d.expert_tiles = m->dn_tiles;
   d.kb = m->inter_pad / kUnitK;
   d.m_tiles = m->hidden / kPfRows;
-  d.src = ps->act;
-  d.ld_src = m->inter_pad;
-  d.row_token = nullptr;
   d.y = ps->down;
   d.ld_y = m->hidden;
-  RC_CUDA_TRY(pf_launch_gemm<kPfEpiDown>(m->ctx, d, s));
+  RC_CUDA_TRY(pf_rows(m->ctx, ps->act, m->inter_pad, m->inter_pad, nullptr, ps->n_chunks + 2, nullptr, ps->ssum_act,
+                      s));
+  RC_CUDA_TRY(pf_launch_tc<kPfEpiDown>(m->ctx, d, ps->tm_act, ps->tm_sact, s));
   return RC_OK;
 }
 
