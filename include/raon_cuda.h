@@ -175,7 +175,8 @@ int rc_moe_set_fused(rc_moe *m, int enable);
  * read are complete, 8 its down tiles done, 9 every expert row of the
  * combined tokens written, 10 combine done, 11 the tokens' router keys in
  * shared memory, 12 the top-k ranks found, 13 the activation rows its down
- * tiles read staged.  ``ctas`` >= the SM count;
+ * tiles read staged, 14 its first down round's units computed, 15 that
+ * round's tiles summed and written.  ``ctas`` >= the SM count;
  * NULL switches the stamps off.  No counterpart in the reference. */
 int rc_moe_set_trace(rc_moe *m, unsigned long long *stamps_dev, int ctas);
 

@@ -128,6 +128,8 @@ enum TracePhase : int {
   kTrKeys,           // selection: every router key of the tokens in shared memory
   kTrRanked,         // selection: the top-k ranks found
   kTrActStaged,      // down: the activation rows staged as mma fragments
+  kTrDownUnits,      // down: this CTA's units computed (first round)
+  kTrDownTiles,      // down: this CTA's tiles summed and written (first round)
   kTracePhases = 16
 };
 }  // namespace rc

@@ -77,6 +77,7 @@ struct DcParams {
   int chunk_slots;                   // B: chunk slots of the unit ring
   int round_units;                   // units a round may hold (partials)
   int stage_blk;                     // act blocks (groups) the staging area holds
+  int col_down;                      // down tiles column-major, whole columns per CTA, combined in the CTA
   int off_buf, off_stage, off_part, off_tab, off_sel, off_red, off_bar;
   unsigned long long *bar;           // grid-barrier arrival count (only grows)
   int *cols;                         // [hidden/16] down tiles written per column tile (zero between calls)
@@ -265,6 +266,7 @@ struct DcStream {
   int c0[2], nt[2], kb[2], gt[2];
   int units0, units;                 // gate/up units; all units
   int nchunk;                        // chunks of kDcChunk units
+  int col, ng;                       // down list column-major (tile = index / ng, group = index % ng)
 };
 
 // The global address and the contiguous extent (in units, <= n) of unit s.
@@ -272,12 +274,19 @@ __device__ __forceinline__ const uint8_t *dc_unit_src(const DcStream &st, int s,
   const int ph = s < st.units0 ? 0 : 1;
   const int u = ph ? s - st.units0 : s;
   const int kb = st.kb[ph];
-  const int tg = st.c0[ph] + u / kb;                      // tile in the group-major list
-  const int grp = tg / st.gt[ph], tile = tg - grp * st.gt[ph];
-  // units left in this group of this phase
-  const int grp_end_tile = (grp + 1) * st.gt[ph] < st.c0[ph] + st.nt[ph] ? (grp + 1) * st.gt[ph]
-                                                                           : st.c0[ph] + st.nt[ph];
-  const int left = (grp_end_tile - tg) * kb - (u % kb);
+  const int tg = st.c0[ph] + u / kb;                      // tile in the phase's list
+  int grp, tile, left;
+  if (ph == 1 && st.col) {
+    // column-major: consecutive list entries are different experts
+    tile = tg / st.ng, grp = tg - tile * st.ng;
+    left = kb - (u % kb);
+  } else {
+    grp = tg / st.gt[ph], tile = tg - grp * st.gt[ph];
+    // units left in this group of this phase
+    const int grp_end_tile = (grp + 1) * st.gt[ph] < st.c0[ph] + st.nt[ph] ? (grp + 1) * st.gt[ph]
+                                                                             : st.c0[ph] + st.nt[ph];
+    left = (grp_end_tile - tg) * kb - (u % kb);
+  }
   *run = left < n ? left : n;
   const uint8_t *b = st.g_ptr[ph][grp];
   return b ? b + ((size_t)tile * kb + u % kb) * kUnitBytes : nullptr;
@@ -312,10 +321,13 @@ static __device__ __noinline__ void dc_issue_chunk(const DcStream &st, int j, ui
 // Eight columns of one token: ascending-ID f32 sum (product rounded, then
 // sum rounded) of the k slot rows at ``rows`` (stride ``hidden``) with the
 // weights ``w``, RTNE, then RTNE(routed + shared row k) when with_shared.
+template <bool SHARED_MEM = false>
 __device__ __forceinline__ uint4 dc_combine8(const uint16_t *rows, int hidden, int k, const float *w,
                                              bool with_shared) {
-  const uint4 sh = with_shared ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)k * hidden))
-                               : make_uint4(0, 0, 0, 0);
+  auto ld = [](const uint16_t *a) {
+    return SHARED_MEM ? *reinterpret_cast<const uint4 *>(a) : __ldcg(reinterpret_cast<const uint4 *>(a));
+  };
+  const uint4 sh = with_shared ? ld(rows + (size_t)k * hidden) : make_uint4(0, 0, 0, 0);
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;
@@ -325,8 +337,7 @@ __device__ __forceinline__ uint4 dc_combine8(const uint16_t *rows, int hidden, i
     uint4 r[8];
 #pragma unroll
     for (int s = 0; s < 8; ++s)
-      r[s] = s0 + s < k ? __ldcg(reinterpret_cast<const uint4 *>(rows + (size_t)(s0 + s) * hidden))
-                        : make_uint4(0, 0, 0, 0);
+      r[s] = s0 + s < k ? ld(rows + (size_t)(s0 + s) * hidden) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
       if (s0 + s < k) {
@@ -416,7 +427,11 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
       // without divisions
       int u = t0 * kb + warp;
       int tile_r = u / kb, kbi = u - tile_r * kb;                // tile of the phase range
-      int tg = c0 + tile_r, grp = tg / gt, tin = tg - grp * gt;   // group and tile within it
+      // group and tile of the list entry; column-major lists step the group first
+      const bool col = ph == 1 && st.col;
+      const int inner_n = col ? ng : gt;
+      int tg = c0 + tile_r, outer = tg / inner_n, inner = tg - outer * inner_n;
+      int grp = col ? inner : outer;
       int sidx = base + u, j = sidx / kDcChunk, off = sidx - j * kDcChunk;
       int slot = j % B;
       uint32_t par = (uint32_t)(j / B) & 1u;
@@ -445,8 +460,9 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
         kbi += dk;
         int tstep = dt;
         if (kbi >= kb) kbi -= kb, ++tstep;
-        tin += tstep;
-        while (tin >= gt) tin -= gt, ++grp;
+        inner += tstep;
+        while (inner >= inner_n) inner -= inner_n, ++outer;
+        grp = col ? inner : outer;
         off += doff;
         int cstep = dj;
         if (off >= kDcChunk) off -= kDcChunk, ++cstep;
@@ -456,11 +472,14 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
     }
     // a wait that ran out in any warp stops the phase (CTA-uniform verdict)
     if (__syncthreads_or(wfail)) failed = true;
+    if (ph == 1 && t0 == 0) dc_stamp(p, kTrDownUnits);
     if (!failed) {
       // a tile is the sum of its units' results in k-block order
 #pragma unroll 1
       for (int ti = t0 + warp; ti < t1; ti += kDcWarps) {
-        const int tg = c0 + ti, grp = tg / gt, tile = tg - grp * gt;
+        const int tg = c0 + ti;
+        const bool col = ph == 1 && st.col;
+        const int grp = col ? tg % ng : tg / gt, tile = col ? tg / ng : tg - (tg / gt) * gt;
         const bool live = st.g_ptr[ph][grp] != nullptr;
         Acc<NTB> acc;
         acc_zero(acc);
@@ -488,7 +507,11 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
             } else {
               const int srow = g_dst[grp * T + t];     // slot row t*(k+1) + position
               uint16_t *y;
-              if (p.ep_world > 1) {
+              if (col) {
+                // this CTA holds every expert row of the column tile: rows
+                // [slot row][16 columns] in the (now free) staging area
+                y = reinterpret_cast<uint16_t *>(smem + p.off_stage) + (size_t)srow * kUnitRows + g;
+              } else if (p.ep_world > 1) {
                 // straight into the buffer of the token's owner
                 const int tt = srow / (p.k + 1), pos = srow - tt * (p.k + 1);
                 const int owner = tt / p.ep_M, tl = tt - owner * p.ep_M;
@@ -502,7 +525,7 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
             }
           }
         }
-        if (ph == 1 && p.ep_world <= 1 && p.out) {
+        if (ph == 1 && !col && p.ep_world <= 1 && p.out) {
           // the last writer of column tile ``tile`` combines it (threadfence
           // reduction: stores, fence, count; the last counter sees them all)
           __syncwarp();
@@ -526,6 +549,7 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
       }
     }
     __syncthreads();
+    if (ph == 1 && t0 == 0) dc_stamp(p, kTrDownTiles);
     // chunks whose units all lie before this round's end are consumed: their
     // slots take the next chunks of the stream (chunk j by warp j % 16)
     if (!failed) issued = dc_refill(st, issued, (base + t1 * kb) / kDcChunk, buf, bar0, B);
@@ -773,6 +797,11 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   const int gt_dn = p.hidden / kUnitRows, kb_dn = p.inter_pad / kUnitK;
   uint8_t *stage = smem + p.off_stage;
   dc_stamp(p, kTrStart);
+  // Chaining: the next launch in the stream may start its CTAs as this
+  // grid's CTAs leave their SMs (its prologue below reads only weights and
+  // tables); it waits for this grid before it touches anything this grid
+  // reads or writes.
+  pdl_launch_dependents();
 
   // the lane's router slice of this CTA's first expert, in flight while the
   // tables load and the token rows are staged
@@ -789,6 +818,10 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
     if (a1 > a0) bulk_prefetch_l2(p.gu_tiles[E] + a0 * kUnitBytes, (uint32_t)((a1 - a0) * kUnitBytes));
     if (b1 > b0) bulk_prefetch_l2(p.dn_tiles[E] + b0 * kUnitBytes, (uint32_t)((b1 - b0) * kUnitBytes));
   }
+
+  // the previous kernel in the stream (the producer of x, or the previous
+  // call sharing this layer's counters and scratch) is complete from here on
+  pdl_wait_prior();
 
   // ---- expert parallelism: every rank's token rows into every rank's buffer
   unsigned long long ep_calls = 0;
@@ -875,7 +908,8 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   const int ng = *n_groups_s;
   const int tot_gu = ng * gt_gu, tot_dn = ng * gt_dn;
   const int per_gu = (tot_gu + (int)gridDim.x - 1) / (int)gridDim.x;
-  const int per_dn = (tot_dn + (int)gridDim.x - 1) / (int)gridDim.x;
+  // column-major down: CTA c owns output column tile c of every group
+  const int per_dn = p.col_down ? ng : (tot_dn + (int)gridDim.x - 1) / (int)gridDim.x;
   const int c0_gu = blockIdx.x * per_gu, c0_dn = blockIdx.x * per_dn;
   const int nt_gu = c0_gu < tot_gu ? (c0_gu + per_gu < tot_gu ? per_gu : tot_gu - c0_gu) : 0;
   const int nt_dn = c0_dn < tot_dn ? (c0_dn + per_dn < tot_dn ? per_dn : tot_dn - c0_dn) : 0;
@@ -893,17 +927,18 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
     st.units0 = nt_gu * kb_gu;
     st.units = st.units0 + nt_dn * kb_dn;
     st.nchunk = (st.units + kDcChunk - 1) / kDcChunk;
+    st.col = p.col_down;
+    st.ng = ng;
   }
   const int B = p.chunk_slots;
   const uint32_t bar0 = smem_addr(smem + p.off_bar);
   if (tid < B) mbar_init(bar0 + 8 * tid, 1);
   mbar_fence_init();
   __syncthreads();            // the barriers are initialised; the selection scratch in the ring is dead
-  // chunks requested so far (the same count in every thread); chunk j by warp j % 16
-  // the gate/up chunks are requested first (they are needed first); the down
-  // chunks follow when the gate/up round ends
-  const int nchunk_gu = (nt_gu * kb_gu + kDcChunk - 1) / kDcChunk;
-  int issued = nchunk_gu < B ? nchunk_gu : B;
+  // chunks requested so far (the same count in every thread); chunk j by warp
+  // j % 16.  Every chunk the ring holds is requested now, the gate/up ones
+  // first in the stream; the rest follow as rounds free their slots.
+  int issued = st.nchunk < B ? st.nchunk : B;
   if (lane == 0) {
 #pragma unroll 1
     for (int j = warp; j < issued; j += kDcWarps) dc_issue_chunk(st, j, smem + p.off_buf, bar0, B);
@@ -938,8 +973,8 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
 
   // --------------------------------------------------------------- 6 down
   if (!failed) {
-    const int g_lo = c0_dn / gt_dn;
-    const int g_hi = nt_dn ? (c0_dn + nt_dn - 1) / gt_dn : g_lo - 1;
+    const int g_lo = p.col_down ? 0 : c0_dn / gt_dn;
+    const int g_hi = nt_dn ? (p.col_down ? ng - 1 : (c0_dn + nt_dn - 1) / gt_dn) : g_lo - 1;
     const int nblk = g_hi - g_lo + 1;
     if (nblk > 0)
       dc_stage(p.act + (size_t)g_lo * 8 * NTB * p.inter_pad, p.inter_pad, 8 * NTB, nblk, T, kb_dn, stage, warp,
@@ -950,6 +985,19 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
                         slot_w);
     issued = rv >> 1;
     failed = (rv & 1) != 0;
+    if (!failed && p.col_down && nt_dn > 0) {
+      // every expert row of column tile blockIdx.x is in this CTA: combine it
+      // for every token straight from shared memory
+      __syncthreads();
+      const uint16_t *rows_s = reinterpret_cast<const uint16_t *>(stage);
+      const bool with_shared = p.shared_id >= 0 && p.own.shared_mask;
+      if (tid < 2 * T) {
+        const int t = tid >> 1, h = tid & 1;
+        *reinterpret_cast<uint4 *>(p.out + (size_t)t * p.hidden + blockIdx.x * kUnitRows + h * 8) =
+            dc_combine8<true>(rows_s + (size_t)t * (k + 1) * kUnitRows + h * 8, kUnitRows, k, slot_w + t * k,
+                              with_shared);
+      }
+    }
   }
   dc_stamp(p, kTrDown);
   if (p.ep_world > 1) {
@@ -1003,13 +1051,22 @@ static int dc_max_groups(int T, int k, const MoeOwned &own) {
 // split between the unit ring (B chunk slots) and the round partials, a
 // round holding at most B - 1 chunks of units and at least one tile of
 // either phase.
-static bool dc_layout(const rc_moe *m, int T, int k, const MoeOwned &own, DcLayout *L) {
+// Column-major down (every group of one output column tile in one CTA,
+// combined there): on one GPU with an output, when the output column tiles
+// do not outnumber the CTAs and every group's activations of few tokens fit
+// a small staging area.  The layout must also hold a CTA's units in one round.
+static bool dc_col_down(const rc_moe *m, int T, int k, const MoeOwned &own) {
+  const int gt_dn = m->hidden / kUnitRows, kb_dn = m->inter_pad / kUnitK;
+  return gt_dn <= m->ctx->sm_count && dc_stage_bytes(dc_max_groups(T, k, own), T, kb_dn) <= 32 * 1024;
+}
+
+static bool dc_layout(const rc_moe *m, int T, int k, const MoeOwned &own, bool col, DcLayout *L) {
   const int ntb = T <= 8 ? 1 : 2, E = m->n_experts, grid = m->ctx->sm_count;
   const int hidden = m->hidden, inter_pad = m->inter_pad;
   const int kb_gu = hidden / kUnitK, kb_dn = inter_pad / kUnitK, gt_dn = hidden / kUnitRows;
   const int mg = dc_max_groups(T, k, own);
-  const int per_dn = (mg * gt_dn + grid - 1) / grid;
-  int blk = 1 + (per_dn + gt_dn - 2) / gt_dn;              // groups a CTA's down range can touch
+  const int per_dn = col ? mg : (mg * gt_dn + grid - 1) / grid;
+  int blk = col ? mg : 1 + (per_dn + gt_dn - 2) / gt_dn;   // groups a CTA's down range can touch
   if (blk > mg) blk = mg > 0 ? mg : 1;
   size_t stage = dc_stage_bytes(1, T, kb_gu);
   const size_t st_a = dc_stage_bytes(blk, T, kb_dn);
@@ -1023,9 +1080,10 @@ static bool dc_layout(const rc_moe *m, int T, int k, const MoeOwned &own, DcLayo
                        (red + 15) / 16 * 16 + (size_t)kDcMaxChunks * 8;
   if (fixed >= (size_t)kDcSmemLimit) return false;
   const size_t rest = (size_t)kDcSmemLimit - fixed;
+  if (col && (size_t)T * (k + 1) * kUnitRows * 2 > stage) return false;
   for (int B = kDcMaxChunks; B >= 2; --B) {
     const int ru = (B - 1) * kDcChunk;
-    if (ru < need) break;
+    if (ru < need || (col && ru < per_dn * kb_dn)) break;
     const size_t bytes = (size_t)B * kDcChunk * kUnitBytes + ((size_t)ru * pb + 15) / 16 * 16;
     if (bytes > rest) continue;
     // the selection scratch (T*E keys and scores) lives in the unit ring
@@ -1055,7 +1113,7 @@ static bool dc_layout(const rc_moe *m, int T, int k, const MoeOwned &own, DcLayo
 bool moe_decode_shape_ok(const rc_moe *m, int T, int k, const MoeOwned &own) {
   if (m->down_fmt != kFormatQ4nx) return false;   // q4nx unit arithmetic only
   DcLayout L;
-  return dc_layout(m, T, k, own, &L);
+  return dc_layout(m, T, k, own, false, &L);
 }
 
 int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router, int renorm, float scaling,
@@ -1064,7 +1122,9 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
                           const MoeEpArgs *ep) {
   const int ntb = T <= 8 ? 1 : 2;
   DcLayout L;
-  if (!dc_layout(m, T, k, own, &L)) {
+  const bool col = ep == nullptr && out != nullptr && !zero_foreign && dc_col_down(m, T, k, own) &&
+                   dc_layout(m, T, k, own, true, &L);
+  if (!col && !dc_layout(m, T, k, own, false, &L)) {
     set_error("MoE decode: no shared-memory layout for T=%d k=%d", T, k);
     return RC_ERR_INVALID;
   }
@@ -1117,6 +1177,7 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
   p.chunk_slots = L.chunk_slots;
   p.round_units = L.round_units;
   p.stage_blk = L.stage_blk;
+  p.col_down = col ? 1 : 0;
   p.off_buf = L.off_buf;
   p.off_stage = L.off_stage;
   p.off_part = L.off_part;
@@ -1156,11 +1217,13 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
   cfg.blockDim = dim3(kDcThreads);
   cfg.dynamicSmemBytes = L.smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;      // every CTA resident: the grid barriers are safe
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (ntb == 1)
     RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, rc_moe_decode_kernel<1>, p));
   else

@@ -341,7 +341,7 @@ class MoeLayer:
         check(self.ctx.lib.rc_moe_set_fused(self.handle, int(bool(enable))), "rc_moe_set_fused")
 
     TRACE_PHASES = ("start", "tokens", "logits", "routed", "selected", "staged", "gate_up", "act_ready", "down",
-                    "rows", "end", "keys", "ranked", "act_staged")
+                    "rows", "end", "keys", "ranked", "act_staged", "down_units", "down_tiles")
 
     def set_trace(self, stamps_dev, ctas: int = 0) -> None:
         """Phase stamps of the persistent decode kernel (``rc_moe_set_trace``):
