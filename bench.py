@@ -1078,7 +1078,8 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
 
 
 def prefill_kernel_desc(world: int) -> str:
-    return ("router, plan, grouped gate/up + down GEMVs over 8-token blocks (register-fragment mma), combine"
+    return ("router, plan, rows gathered into expert order, tcgen05 grouped gate/up + down GEMMs over 64-token "
+            "chunks (q4nx codes expanded to bf16 in shared memory, TMEM accumulators), combine"
             + ("; the token rows of remote routes to their experts' owners and the expert rows back by NCCL "
                "all-to-all (split sizes read on the host: eager launches)" if world > 1 else ""))
 

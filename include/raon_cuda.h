@@ -271,12 +271,15 @@ int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int re
 
 /* Which kernel runs the prefill experts' GEMMs (same routing, plan and
  * combine; results within the oracle tolerance of each other):
- * RC_PREFILL_GEMV (default) -- a grouped GEMV over 8-token blocks with the
- * decode GEMV's register-fragment (mma.sync) unit arithmetic;
- * RC_PREFILL_TCGEN05 -- the tcgen05 grouped GEMM over 64-token chunks.  With
- * per-32-column scales tcgen05 needs a separate accumulator per group, 16
- * MMA instructions per (128-row tile, 256-column block) whatever the tile's
- * token count, which the few tokens most experts get cannot amortise. */
+ * RC_PREFILL_TCGEN05 (default) -- the tcgen05 grouped GEMM over 64-token
+ * chunks (warp-specialised: TMA loads, bf16 expansion of the codes, MMAs
+ * into one tensor-memory accumulator per 32-column group, promotion);
+ * RC_PREFILL_GEMV -- a grouped GEMV over 8-token blocks with the decode
+ * GEMV's register-fragment (mma.sync) unit arithmetic: a token's bytes equal
+ * the decode path's, and it is the faster of the two below a few hundred
+ * tokens.  rc_moe_experts_grouped always uses RC_PREFILL_GEMV for T > 16,
+ * so its bytes do not depend on T.  Layers with bfp16ebs8 down matrices
+ * always use RC_PREFILL_GEMV. */
 #define RC_PREFILL_GEMV 0
 #define RC_PREFILL_TCGEN05 1
 int rc_moe_set_prefill_kernel(rc_moe *m, int kernel);

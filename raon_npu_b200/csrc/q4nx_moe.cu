@@ -851,6 +851,7 @@ int rc_moe_create(rc_ctx *ctx, int hidden, int inter, int n_experts, int has_sha
   m->n_experts = n_experts;
   m->has_shared = has_shared ? 1 : 0;
   m->fused = 1;
+  m->prefill_kernel = RC_PREFILL_TCGEN05;
   m->down_fmt = kFormatQ4nx;
   const int ne = n_experts + 1;
   m->gate_up = new rc_weight *[ne]();
@@ -1077,11 +1078,15 @@ int rc_moe_experts_grouped(rc_moe *m, const uint16_t *x_dev, int T, const int32_
                "shared_gu needs shared_out and a loaded shared expert");
   if (T > kMoeMaxTokens) {
     // Prefill-sized call: the routed experts of all T tokens in one pass of
-    // the prefill kernels (a token's bytes equal the decode path's), then the
-    // shared expert's down rows in 16-token chunks of the decode kernels with
-    // no routed expert in the computed range.
+    // the register-fragment prefill kernels (a token's bytes equal the
+    // decode path's, so the bytes do not depend on T), then the shared
+    // expert's down rows in 16-token chunks of the decode kernels with no
+    // routed expert in the computed range.
+    const int kernel = m->prefill_kernel;
+    m->prefill_kernel = RC_PREFILL_GEMV;
     int rc = rc_moe_prefill_experts(m, x_dev, T, ids_dev, w_dev, k, act, gate_beta, value_beta, 0, routed_out_dev,
                                     stream);
+    m->prefill_kernel = kernel;
     if (rc || !shared_gu_dev) return rc;
     RC_CHECK_ARG((reinterpret_cast<uintptr_t>(shared_gu_dev) & 15) == 0 && (m->inter * 4) % 16 == 0,
                  "shared_gu rows must be 16-byte aligned");

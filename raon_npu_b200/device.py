@@ -351,8 +351,9 @@ class MoeLayer:
               "rc_moe_set_trace")
 
     def set_prefill_kernel(self, kernel: str) -> None:
-        """"gemv" (default: register-fragment grouped GEMV over 8-token blocks) or
-        "tcgen05" (tensor-core grouped GEMM over 64-token chunks)."""
+        """"tcgen05" (default: tensor-core grouped GEMM over 64-token chunks) or
+        "gemv" (register-fragment grouped GEMV over 8-token blocks, the decode
+        path's bytes)."""
         codes = {"gemv": _lib.RC_PREFILL_GEMV, "tcgen05": _lib.RC_PREFILL_TCGEN05}
         if kernel not in codes:
             raise ValueError(f"unknown prefill kernel {kernel!r}")

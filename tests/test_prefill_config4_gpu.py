@@ -181,7 +181,7 @@ def test_config4_prefill_bfp16_down_every_token_matches_oracle(torch, ctx, c4):
 
 
 def test_config4_prefill_equals_decode_bytes(torch, ctx, c4):
-    """The default prefill kernel runs the decode GEMV's unit arithmetic on the
+    """The register-fragment prefill kernel runs the decode GEMV's unit arithmetic on the
     same per-token staging: at config 4's shape its bytes are the decode
     path's (16 tokens per decode call)."""
     layer = c4[0]
