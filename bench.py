@@ -55,12 +55,12 @@ HBM_FALLBACK_GBS = 6650.0
 # DRAM traffic of the timed work, from ncu captures of the same commands on a
 # B200 (dram__bytes_read.sum + dram__bytes_write.sum): the GEMV launches of
 # one sweep step; one config-3 decode layer at T = 1 (rc_moe_decode_kernel); the
-# two grouped GEMVs of one 512-token prefill layer.  Single-GPU figures.
-MEASURED_TRAFFIC = {"gemv_step": 1033.4e6, "moe_layer_t1": 27.16e6, "prefill_gemms": 300.75e6}
+# two grouped tcgen05 GEMMs of one 512-token prefill layer.  Single-GPU figures.
+MEASURED_TRAFFIC = {"gemv_step": 1033.4e6, "moe_layer_t1": 27.16e6, "prefill_gemms": 264.79e6}
 TRAFFIC_SOURCE = {
     "gemv_step": "profiles/gemv_sweep_launch_list.md (all rc_q4nx_gemv_kernel launches of one step)",
     "moe_layer_t1": "profiles/moe_decode_layer_t1.md (one rc_moe_decode_kernel launch, T = 1)",
-    "prefill_gemms": "profiles/moe_prefill_gemv_t512.md (the two grouped GEMV launches of a 512-token layer)",
+    "prefill_gemms": "profiles/moe_prefill_gemm_t512.md (the two rc_pf_tc_kernel launches of a 512-token layer)",
 }
 
 
