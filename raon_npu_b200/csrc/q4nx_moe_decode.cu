@@ -85,7 +85,8 @@ struct DcParams {
   int ep_world, ep_rank, ep_M;
   uint8_t *const *ep_peer;
   unsigned long long *ep_flags;
-  uint32_t ep_tok_off, ep_red_off;
+  uint32_t ep_tok_off, ep_red_off, ep_col_off;
+  unsigned long long ep_call;        // this call's number (calls done before it), set in the kernel
   const uint16_t *ep_x_own;
   unsigned long long *trace;         // phase stamps [grid][kTracePhases] (null: off)
 };
@@ -549,6 +550,25 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
       }
     }
     __syncthreads();
+    if (ph == 1 && p.ep_world > 1 && !failed && warp == 0) {
+      // expert parallelism: the CTA's rows of this round are written (remote
+      // stores included); per tile a lane makes them visible system-wide and
+      // counts the tile on its column; the rank's last tile of an output
+      // column tile flags that column to every rank (the rows' owners)
+#pragma unroll 1
+      for (int ti = t0 + lane; ti < t1; ti += 32) {
+        const int tg = c0 + ti, tile = tg - (tg / gt) * gt;
+        __threadfence_system();
+        if (atomicAdd(p.cols + tile, 1) == ng - 1) {
+          __threadfence_system();
+          p.cols[tile] = 0;
+          for (int r = 0; r < p.ep_world; ++r)
+            st_relaxed_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r] + p.ep_col_off) +
+                               (size_t)p.ep_rank * gt + tile,
+                           p.ep_call + 1);
+        }
+      }
+    }
     if (ph == 1 && t0 == 0) dc_stamp(p, kTrDownTiles);
     // chunks whose units all lie before this round's end are consumed: their
     // slots take the next chunks of the stream (chunk j by warp j % 16)
@@ -759,26 +779,6 @@ static __device__ __noinline__ void dc_groups(const DcParams &p, const int32_t *
   __syncthreads();
 }
 
-// ascending-ID f32 combine (product rounded, then sum rounded) of the slot
-// rows of token t, RTNE, then RTNE(routed + shared).  Item i (8 columns of
-// one token) goes to CTA i % grid, so every CTA takes a few; a thread
-// requests all k + 1 slot rows before it sums them.
-static __device__ __noinline__ void dc_combine(const DcParams &p, const float *slot_w, const uint16_t *ep_rows) {
-  const int k = p.k, vecs = p.hidden / 8;
-  const bool with_shared = p.shared_id >= 0 && p.own.shared_mask;
-  const bool ep = p.ep_world > 1;
-  const int n_out = ep ? p.ep_M : p.T;
-#pragma unroll 1
-  for (int i = blockIdx.x + threadIdx.x * gridDim.x; i < n_out * vecs; i += gridDim.x * blockDim.x) {
-    const int to = i / vecs, v = i - to * vecs;
-    const int t = ep ? p.ep_rank * p.ep_M + to : to;
-    const uint16_t *rows = (ep ? ep_rows + (size_t)to * (k + 1) * p.hidden
-                               : p.slot_rows + (size_t)t * (k + 1) * p.hidden) + (size_t)v * 8;
-    *reinterpret_cast<uint4 *>(p.out + (size_t)to * p.hidden + (size_t)v * 8) =
-        dc_combine8(rows, p.hidden, k, slot_w + t * k, with_shared);
-  }
-}
-
 // ------------------------------------------------------------- kernel ---
 template <int NTB>
 __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p_arg) {
@@ -827,6 +827,7 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   unsigned long long ep_calls = 0;
   if (p.ep_world > 1) {
     ep_calls = *reinterpret_cast<volatile unsigned long long *>(p.ep_flags + 2);
+    if (tid == 0) p.ep_call = ep_calls;      // read by the down epilogue (after several barriers)
     if (tid < p.ep_world) ep_peer_s[tid] = p.ep_peer[tid];
     __syncthreads();
     if (blockIdx.x == 0) {
@@ -1001,22 +1002,51 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   }
   dc_stamp(p, kTrDown);
   if (p.ep_world > 1) {
-    // expert parallelism: every rank's rows for this rank's tokens have been
-    // written once every rank has passed its own barrier and signalled; then
-    // the grid combines this rank's tokens
-    if (tid == 0) __threadfence_system();   // this CTA's rows to peers, before the barrier
-    if (!failed && !dc_grid_barrier(p.bar, p.err, ok_s)) failed = true;
-    if (!failed) {
-      if (blockIdx.x == 0 && tid == 0) {
-        __threadfence_system();
+    // expert parallelism: each column tile of this rank's tokens is combined
+    // once every rank has flagged its rows of that column (a rank that
+    // computed no group flags every column here)
+    const unsigned long long *colf = reinterpret_cast<const unsigned long long *>(ep_peer_s[p.ep_rank] +
+                                                                                  p.ep_col_off);
+    if (!failed && ng == 0 && tid == 0) {
+      __threadfence_system();
+      for (int c = blockIdx.x; c < gt_dn; c += gridDim.x)
         for (int r = 0; r < p.ep_world; ++r)
-          red_add_release_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r]) + 1, 1ull);
+          st_relaxed_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r] + p.ep_col_off) +
+                             (size_t)p.ep_rank * gt_dn + c,
+                         ep_calls + 1);
+    }
+    const bool with_shared = p.shared_id >= 0 && p.own.shared_mask;
+    const uint16_t *red = reinterpret_cast<const uint16_t *>(ep_peer_s[p.ep_rank] + p.ep_red_off);
+#pragma unroll 1
+    for (int c = blockIdx.x; c < gt_dn && !failed; c += gridDim.x) {
+      if (tid == 0) {
+        int ok = 1;
+        const uint64_t t0 = global_timer_ns();
+        for (int r = 0; r < p.ep_world && ok; ++r) {
+          while (ld_acquire_sys(colf + (size_t)r * gt_dn + c) < ep_calls + 1) {
+            if (global_timer_ns() - t0 > 1000000000ull) {
+              ok = 0;
+              atomicCAS(p.err, 0, kErrWaitTimeout);
+              break;
+            }
+          }
+        }
+        *ok_s = ok;
       }
-      if (!dc_wait_sys(p.ep_flags + 1, (ep_calls + 1) * p.ep_world, p.err, ok_s)) failed = true;
+      __syncthreads();
+      if (!*ok_s) {
+        failed = true;
+        break;
+      }
+      if (p.out && tid < 2 * p.ep_M) {
+        const int t = tid >> 1, h = tid & 1;
+        *reinterpret_cast<uint4 *>(p.out + (size_t)t * p.hidden + c * kUnitRows + h * 8) =
+            dc_combine8(red + (size_t)t * (k + 1) * p.hidden + c * kUnitRows + h * 8, p.hidden, k,
+                        slot_w + (p.ep_rank * p.ep_M + t) * k, with_shared);
+      }
+      __syncthreads();
     }
     dc_stamp(p, kTrRows);
-    if (!failed && p.out)
-      dc_combine(p, slot_w, reinterpret_cast<const uint16_t *>(ep_peer_s[p.ep_rank] + p.ep_red_off));
   } else {
     // one GPU: the down phase combined each column tile as its last tile was written
     dc_stamp(p, kTrRows);
@@ -1198,6 +1228,7 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
     p.ep_flags = ep->flags;
     p.ep_tok_off = ep->tok_off;
     p.ep_red_off = ep->red_off;
+    p.ep_col_off = ep->col_off;
     p.ep_x_own = ep->x_own;
   }
   static bool configured[64][2] = {};
