@@ -754,6 +754,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
 #pragma unroll
             for (int tb = 0; tb < 32 / kTcTb; ++tb) {
+              // token columns past the chunk's MMA width hold nothing to promote
+              if (kTcTb * tb >= n16 - 32 * ch) break;
               // kTcTb token columns of the part's group accumulators, one wait
               uint32_t v[kTcGpp][kTcTb];
 #pragma unroll
