@@ -1051,11 +1051,37 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
                "sample": f"{n_tok} of the layer's tokens through the oracle per token (biased softmax router, "
                          f"NumpyBackend.moe_experts restated + shared expert), f32 weights cached"}
     exchange = getattr(eps[0], "last_prefill_exchange", None) if world > 1 else None
+    # the all-to-all exchange (only routed rows travel; eager: its split sizes
+    # are read on the host), timed on the same layers for comparison
+    a2a = None
+    if world > 1:
+        for ep in eps:
+            ep.prefill_exchange = "a2a"
+        for s_ in range(max(2, args.warmup)):
+            eps[s_ % n_layers].prefill(xs[s_ % n_layers], outs[s_ % n_layers])
+        torch.cuda.synchronize()
+        barrier()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        n_a = max(2, min(args.steps, 10))
+        a0.record(stream)
+        for s_ in range(n_a):
+            eps[s_ % n_layers].prefill(xs[s_ % n_layers], outs[s_ % n_layers])
+        a1.record(stream)
+        torch.cuda.synchronize()
+        a_ms = _max_over_ranks(torch, dist, dev, world, a0.elapsed_time(a1) / n_a)
+        a2a = {"value": round(T / (a_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(a_ms, 4),
+               "exchange_rank0": getattr(eps[0], "last_prefill_exchange", None),
+               "how": "ExpertParallelMoe(prefill_exchange='a2a'): each rank routes its tokens, the token row of "
+                      "every route goes to its expert's owner (all_to_all_single, split sizes read on the host), "
+                      "one prefill pass over the received rows, the expert rows back; eager launches"}
+        for ep in eps:
+            ep.prefill_exchange = "gather"
     for ep in eps:
         ep.layer.close()
     return {
         "metric": "MoE prefill layer tokens/s", "value": round(T / (ms_max * 1e-3), 1), "unit": "tokens/s",
-        "exchange_rank0": exchange,
+        "exchange_rank0": exchange, "a2a": a2a,
         "ms_per_step": round(ms_max, 4), "scaling": "strong",
         "config": {"workload": "MoE prefill layer (BASELINE configs[3]): 512 tokens, Zipf(1.1) expert load",
                    "parallelism": f"ep{world}", "tokens_per_rank": M, "kernel": prefill_kernel_desc(world),
@@ -1080,8 +1106,8 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
 def prefill_kernel_desc(world: int) -> str:
     return ("router, plan, rows gathered into expert order, tcgen05 grouped gate/up + down GEMMs over 64-token "
             "chunks (q4nx codes expanded to bf16 in shared memory, TMEM accumulators), combine"
-            + ("; the token rows of remote routes to their experts' owners and the expert rows back by NCCL "
-               "all-to-all (split sizes read on the host: eager launches)" if world > 1 else ""))
+            + ("; expert-parallel: NCCL all-gather of the token rows, the rank's experts over all tokens, "
+               "reduce-scatter of the slot rows (one CUDA graph per layer)" if world > 1 else ""))
 
 
 # ------------------------------------------------------ full decode step --

@@ -297,7 +297,9 @@ int rc_moe_prefill(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, i
                    int32_t *ids_dev, float *w_dev, void *stream);
 
 /* rc_moe_prefill for caller-supplied routes ids / w [T][k] (distinct ids per
- * token; an id whose expert is not loaded sets the device error word). */
+ * token; an id whose expert is not loaded sets the device error word).  On a
+ * layer with a shared expert a route may also name it (id n_experts), like a
+ * routed expert -- the expert-parallel prefill's jobs do so. */
 int rc_moe_prefill_experts(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev,
                            const float *w_dev, int k, int act, float gate_beta, float value_beta,
                            int with_shared, uint16_t *out_dev, void *stream);

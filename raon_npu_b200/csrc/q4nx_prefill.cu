@@ -294,6 +294,7 @@ __global__ void rc_pf_slots_kernel(const int32_t *ids, const float *w, int T, in
 struct PfPlanParams {
   const int32_t *slot_expert;   // [T][k+1]
   int T, k, E1;                 // E1 = experts + 1 (index E = shared)
+  int max_id;                   // caller routes name experts < max_id (E, or E + 1: the shared one too)
   int lo, hi;                   // routed experts computed here
   int st0, st1;                 // tokens whose shared expert is computed here
   int32_t *slot_row, *row_token, *cnt, *off, *n_chunks, *chunk_expert, *chunk_row0, *chunk_n;
@@ -324,7 +325,7 @@ __global__ void __launch_bounds__(1024) rc_pf_plan_kernel(PfPlanParams p) {
   for (int i = tid; i < p.T * k1; i += blockDim.x) {
     const int t = i / k1, r = i - t * k1;
     const int e = p.slot_expert[i];
-    if (r < p.k && (e < 0 || e >= p.E1 - 1)) atomicCAS(p.err, 0, kErrBadExpert);   // caller id out of range
+    if (r < p.k && (e < 0 || e >= p.max_id)) atomicCAS(p.err, 0, kErrBadExpert);   // caller id out of range
     else if (computed(t, r, e)) atomicOr(mask + (size_t)e * nw + (t >> 5), 1u << (t & 31));
   }
   __syncthreads();
@@ -383,7 +384,7 @@ __global__ void __launch_bounds__(1024) rc_pf_plan_kernel(PfPlanParams p) {
     const int t = i / k1, r = i - t * k1;
     const int e = p.slot_expert[i];
     int row = -1;
-    if (!(r < p.k && (e < 0 || e >= p.E1 - 1)) && computed(t, r, e)) {
+    if (!(r < p.k && (e < 0 || e >= p.max_id)) && computed(t, r, e)) {
       const uint32_t m = mask[(size_t)e * nw + (t >> 5)];
       row = s_off[e] + (int)pre[(size_t)e * nw + (t >> 5)] + __popc(m & ((1u << (t & 31)) - 1u));
       p.row_token[row] = t;
@@ -1272,6 +1273,7 @@ struct PfRun {
   int T, k, act;
   float gb, vb;
   int lo, hi, st0, st1;        // computed experts / shared tokens
+  int max_id;                  // routed ids below this (n_experts; + 1 when caller routes may name the shared expert)
 };
 
 // gate/up + down on the register-fragment path (after the plan): stage the
@@ -1345,6 +1347,7 @@ static int pf_experts(rc_moe *m, const uint16_t *x, const PfRun &r, cudaStream_t
   pp.T = r.T;
   pp.k = r.k;
   pp.E1 = m->n_experts + 1;
+  pp.max_id = r.max_id;
   pp.lo = r.lo;
   pp.hi = r.hi;
   pp.st0 = r.st0;
@@ -1501,7 +1504,7 @@ int rc_moe_prefill(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, i
   if ((rc = pf_scratch(m, T))) return rc;
   const cudaStream_t s = pick_stream(m->ctx, stream);
   if ((rc = pf_route(m, x_dev, T, k, router, renormalize, scaling, s))) return rc;
-  PfRun r{T, k, act, gate_beta, value_beta, 0, m->n_experts, 0, m->has_shared ? T : 0};
+  PfRun r{T, k, act, gate_beta, value_beta, 0, m->n_experts, 0, m->has_shared ? T : 0, m->n_experts};
   if ((rc = pf_experts(m, x_dev, r, s))) return rc;
   rc_pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
                       s>>>(m->pf->down, m->pf->slot_row, m->pf->slot_w, k, m->has_shared, m->hidden, out_dev);
@@ -1527,7 +1530,9 @@ int rc_moe_prefill_experts(rc_moe *m, const uint16_t *x_dev, int T, const int32_
   RC_CUDA_TRY(cudaGetLastError());
   // every routed expert the caller names must be loaded: checked on the device
   // side by a null tile table entry (error word), so no host copy of the ids
-  PfRun r{T, k, act, gate_beta, value_beta, 0, m->n_experts, 0, with_shared ? T : 0};
+  // a caller's route may name the shared expert (id n_experts) like a routed one
+  const int max_id = m->n_experts + (m->has_shared ? 1 : 0);
+  PfRun r{T, k, act, gate_beta, value_beta, 0, max_id, 0, with_shared ? T : 0, max_id};
   if ((rc = pf_experts(m, x_dev, r, s))) return rc;
   rc_pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
                       s>>>(m->pf->down, m->pf->slot_row, m->pf->slot_w, k, with_shared, m->hidden, out_dev);
@@ -1552,7 +1557,7 @@ int rc_moe_prefill_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int rou
   if ((rc = pf_scratch(m, T))) return rc;
   const cudaStream_t s = pick_stream(m->ctx, stream);
   if ((rc = pf_route(m, x_dev, T, k, router, renormalize, scaling, s))) return rc;
-  PfRun r{T, k, act, gate_beta, value_beta, expert_lo, expert_hi, shared_t0, shared_t0 + shared_tn};
+  PfRun r{T, k, act, gate_beta, value_beta, expert_lo, expert_hi, shared_t0, shared_t0 + shared_tn, m->n_experts};
   if ((rc = pf_experts(m, x_dev, r, s))) return rc;
   rc_pf_slot_rows_kernel<<<T * (k + 1), 256, 0, s>>>(m->pf->down, m->pf->slot_row, m->hidden, slot_out_dev);
   RC_CUDA_TRY(cudaGetLastError());

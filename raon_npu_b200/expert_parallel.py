@@ -55,11 +55,17 @@ class ExpertParallelMoe:
     the same ``decode_local`` / ``combine`` interface and ``n_experts``,
     ``hidden``, ``has_shared`` attributes).  Only the experts this rank owns
     (``owns``) need to be loaded into it.
+
+    ``prefill_exchange``: "gather" (default: all-gather of the token rows,
+    this rank's experts over all tokens, reduce-scatter of the slot rows;
+    fixed sizes, so a prefill can be captured in a CUDA graph) or "a2a"
+    (only the routed rows travel, both ways; split sizes read on the host,
+    so the calls are eager).  Both give the single-GPU bytes.
     """
 
     def __init__(self, layer, k: int, group=None, act: str = "swiglu", router: str = "softmax",
                  renormalize: bool = True, scaling: float = 1.0, gate_beta: float = 4.0, value_beta: float = 25.0,
-                 transport: str = "auto"):
+                 transport: str = "auto", prefill_exchange: str = "gather"):
         import torch.distributed as dist
         self.layer = layer
         self.k = int(k)
@@ -76,6 +82,9 @@ class ExpertParallelMoe:
         self._bufs: dict = {}
         if transport not in ("auto", "p2p", "nccl"):
             raise ValueError(f"unknown transport {transport!r}")
+        if prefill_exchange not in ("gather", "a2a"):
+            raise ValueError(f"unknown prefill exchange {prefill_exchange!r}")
+        self.prefill_exchange = prefill_exchange
         self.transport = transport
         self._ep_M = None               # token count the peer buffers are set up for (p2p)
 
@@ -179,26 +188,64 @@ class ExpertParallelMoe:
 
     def prefill(self, x, out) -> None:
         """Prefill of this rank's M tokens x [M, hidden] -> out [M, hidden]
+        with the exchange ``prefill_exchange`` names."""
+        if self.world == 1:
+            self.layer.prefill(x, self.k, out, **self.kw)
+        elif self.prefill_exchange == "a2a":
+            self.prefill_a2a(x, out)
+        else:
+            self.prefill_gather(x, out)
+
+    def prefill_gather(self, x, out) -> None:
+        """All-gather of every rank's token rows; this rank's experts for every
+        token that chose them and the shared expert for its own tokens
+        (``prefill_local``: slot rows [T, k+1, hidden], zeros where another
+        rank owns the slot); reduce-scatter (sum) of the slot rows, exact as
+        each row is non-zero on one rank only; ``prefill_combine`` of the own
+        tokens.  Sizes are fixed, so it can be captured in a CUDA graph."""
+        import torch
+        import torch.distributed as dist
+        M, H = x.shape
+        N, k = self.world, self.k
+        T = N * M
+        dev = x.device
+        xg = self._buf("pxg", (T, H), torch.int16, dev)
+        dist.all_gather_into_tensor(_bf16(xg), _bf16(x), group=self.group)
+        slots = self._buf("pslots", (T, k + 1, H), torch.int16, dev)
+        sw = self._buf("psw", (T, k), torch.float32, dev)
+        shared = (self.rank * M, M) if self.layer.has_shared else (0, 0)
+        self.layer.prefill_local(xg, k, slots, sw, experts=self.experts, shared_tokens=shared, **self.kw)
+        mine = self._buf("pmine", (M, k + 1, H), torch.int16, dev)
+        dist.reduce_scatter_tensor(_bf16(mine), _bf16(slots), op=dist.ReduceOp.SUM, group=self.group)
+        self.last_prefill_exchange = {"rows_sent": (N - 1) * M * (k + 1) + (N - 1) * M,
+                                      "rows_received": (N - 1) * M * (k + 1) + (N - 1) * M,
+                                      "bytes_sent": 2 * H * ((N - 1) * M * (k + 1) + (N - 1) * M)}
+        self.layer.prefill_combine(mine, sw[self.rank * M:(self.rank + 1) * M], k, out, tokens=M,
+                                   with_shared=self.layer.has_shared)
+
+    def prefill_a2a(self, x, out) -> None:
+        """Prefill of this rank's M tokens x [M, hidden] -> out [M, hidden]
         with an all-to-all exchange of only the routed rows:
 
-        1. route the own tokens (``route``) and compute, for them, the experts
-           this rank owns and the shared expert (``prefill_local``: slot rows
-           [M, k+1, hidden] in ascending expert ID, zeros for remote slots,
-           and the slot weights);
-        2. send the token row of every remote route (token, expert) to the
-           expert's owner, grouped by destination (``all_to_all_single``; the
-           split sizes travel first);
-        3. the owner computes each received row's one expert
-           (``prefill_experts`` with k = 1 and weight 1: the expert's bf16
-           output row, unchanged by the sum) and sends the rows back in the
-           order received;
-        4. the rows fill the remote slots; ``prefill_combine`` of the own
-           tokens.
+        1. route the own tokens on the device (``route``);
+        2. every (token, route) becomes a job for the expert's owner, and
+           every token a job for the shared expert on this rank; the jobs'
+           token rows go to their owners grouped by destination
+           (``all_to_all_single``, this rank's own jobs included; the split
+           sizes travel first);
+        3. each rank runs all the jobs it received in one pass of the prefill
+           kernels (``prefill_experts`` with k = 1 and weight 1: the expert's
+           bf16 output row, unchanged by the sum), so every local expert's
+           weights are streamed once, and sends the rows back in the order
+           received;
+        4. the rows fill the slots [M, k+1, hidden] (ascending expert ID, the
+           shared expert last); ``prefill_combine`` of the own tokens.
 
         Each expert row comes out of the same tile arithmetic as on one GPU
-        and the combine is the same kernel, so a token's bytes equal the
-        single-GPU prefill.  The split sizes are read on the host, so this
-        path is not captured in a CUDA graph."""
+        (a token's row never depends on the other rows of a pass) and the
+        combine is the same kernel, so a token's bytes equal the single-GPU
+        prefill.  The split sizes are read on the host, so this path is not
+        captured in a CUDA graph."""
         import torch
         import torch.distributed as dist
         M, H = x.shape
@@ -212,30 +259,30 @@ class ExpertParallelMoe:
         E = self.layer.n_experts
         per = E // N
         kw = self.kw
+        has_shared = self.layer.has_shared
         ids = self._buf("pf_ids", (M, k), torch.int32, dev)
         w = self._buf("pf_w", (M, k), torch.float32, dev)
         self.layer.route(x, M, k, ids, w, router=kw["router"], renormalize=kw["renormalize"],
                          scaling=kw["scaling"])
-        slots = self._buf("pf_slots", (M, k + 1, H), torch.int16, dev)
-        sw = self._buf("pf_sw", (M, k), torch.float32, dev)
-        shared = (0, M) if self.layer.has_shared else (0, 0)
-        self.layer.prefill_local(x, k, slots, sw, experts=self.experts, shared_tokens=shared, **kw)
-        # remote routes grouped by destination rank (stable: token-major within a destination)
         ids64 = ids.to(torch.int64)
-        dest = (ids64 // per).reshape(-1)
-        pos = (ids64.unsqueeze(2) > ids64.unsqueeze(1)).sum(dim=2).reshape(-1)   # ascending-ID slot
-        route = torch.arange(M * k, device=dev)
-        remote = dest != self.rank
-        order = torch.argsort(dest * (M * k) + route)
-        order = order[remote[order]]
-        send_counts = torch.bincount(dest[order], minlength=N).to(torch.int64)
+        # ascending-ID slot of every route; the shared expert takes slot k
+        pos = (ids64.unsqueeze(2) > ids64.unsqueeze(1)).sum(dim=2)
+        slot_w = torch.zeros((M, k), dtype=torch.float32, device=dev)
+        slot_w.scatter_(1, pos, w)
+        kj = k + 1 if has_shared else k
+        job_e = torch.cat([ids64, torch.full((M, 1), E, dtype=torch.int64, device=dev)], 1) if has_shared else ids64
+        job_slot = torch.cat([pos, torch.full((M, 1), k, dtype=torch.int64, device=dev)], 1) if has_shared else pos
+        job_e, job_slot = job_e.reshape(-1), job_slot.reshape(-1)
+        dest = torch.where(job_e == E, torch.full_like(job_e, self.rank), job_e // per)
+        order = torch.argsort(dest * (M * kj) + torch.arange(M * kj, device=dev))   # by destination, token-major
+        send_counts = torch.bincount(dest, minlength=N).to(torch.int64)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         send = send_counts.tolist()
         recv = recv_counts.tolist()
-        tok = order // k
+        tok = order // kj
         send_x = x[tok].contiguous()
-        send_e = ids64.reshape(-1)[order].to(torch.int32).contiguous()
+        send_e = job_e[order].to(torch.int32).contiguous()
         n_recv = int(sum(recv))
         recv_x = torch.empty((n_recv, H), dtype=x.dtype, device=dev)
         recv_e = torch.empty((n_recv,), dtype=torch.int32, device=dev)
@@ -250,11 +297,12 @@ class ExpertParallelMoe:
         back = torch.empty_like(send_x)
         dist.all_to_all_single(_bf16(back), _bf16(rows), output_split_sizes=send, input_split_sizes=recv,
                                group=self.group)
-        if order.numel():
-            slots[tok, pos[order]] = back
-        self.last_prefill_exchange = {"rows_sent": int(order.numel()), "rows_received": n_recv,
-                                      "bytes_sent": 2 * H * (int(order.numel()) + n_recv)}
-        self.layer.prefill_combine(slots, sw, k, out, tokens=M, with_shared=self.layer.has_shared)
+        slots = self._buf("pf_slots", (M, k + 1, H), torch.int16, dev)
+        slots[tok, job_slot[order]] = back
+        own = send[self.rank]
+        self.last_prefill_exchange = {"rows_sent": int(order.numel()) - own, "rows_received": n_recv - recv[self.rank],
+                                      "bytes_sent": 2 * H * (int(order.numel()) - own + n_recv - recv[self.rank])}
+        self.layer.prefill_combine(slots, slot_w, k, out, tokens=M, with_shared=has_shared)
 
     def _host_call(self, x: np.ndarray, run, tag: str) -> np.ndarray:
         """x [M, hidden] bf16 bits on the host -> run(x_dev, out_dev) -> out on

@@ -145,7 +145,7 @@ def test_expert_parallel_two_ranks_match_single_process(tmp_path):
             np.testing.assert_array_equal(out[t], ref)
 
 
-def _prefill_worker(rank, world, port, result_dir):
+def _prefill_worker(rank, world, port, result_dir, exchange):
     import torch
     import torch.distributed as dist
     from raon_npu_b200.expert_parallel import ExpertParallelMoe
@@ -157,7 +157,7 @@ def _prefill_worker(rank, world, port, result_dir):
         experts, wr = _model()
         per = E // world
         owned = set(range(rank * per, (rank + 1) * per)) | {E}
-        ep = ExpertParallelMoe(OracleLayer(experts, wr, owned), K, act="swiglu")
+        ep = ExpertParallelMoe(OracleLayer(experts, wr, owned), K, act="swiglu", prefill_exchange=exchange)
         rng = np.random.default_rng(300 + rank)
         x = q.f32_to_bf16(rng.standard_normal((5, HIDDEN)).astype(np.float32))
         out = torch.empty((5, HIDDEN), dtype=torch.int16)
@@ -171,14 +171,15 @@ def _prefill_worker(rank, world, port, result_dir):
 
 
 @pytest.mark.timeout(300)
-def test_expert_parallel_prefill_all_to_all_matches_single_process(tmp_path):
-    """Prefill over two gloo ranks: only the rows of remote routes cross
-    (all-to-all there and back), and every rank's outputs equal the
-    single-process oracle layer byte for byte."""
+@pytest.mark.parametrize("exchange", ["a2a", "gather"])
+def test_expert_parallel_prefill_matches_single_process(tmp_path, exchange):
+    """Prefill over two gloo ranks, either exchange: every rank's outputs
+    equal the single-process oracle layer byte for byte; with "a2a" only the
+    rows of remote routes cross (there and back)."""
     import torch.multiprocessing as mp
     from oracle import backend as ob
     world = 2
-    mp.start_processes(_prefill_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+    mp.start_processes(_prefill_worker, args=(world, _free_port(), str(tmp_path), exchange), nprocs=world,
                        start_method="spawn")
     experts, wr = _model()
     sent = 0
@@ -192,7 +193,8 @@ def test_expert_parallel_prefill_all_to_all_matches_single_process(tmp_path):
                                                  act="swiglu")
             np.testing.assert_array_equal(out[t], ref)
             remote += int(sum(1 for e in ids if int(e) // (E // world) != rank))
-        assert ex["rows_sent"] == remote
+        if exchange == "a2a":
+            assert ex["rows_sent"] == remote
         sent += ex["rows_sent"]
     assert sent == sum(np.load(tmp_path / f"pex{r}.npy", allow_pickle=True)[0]["rows_received"] for r in range(world))
 

@@ -85,16 +85,20 @@ def _worker(rank, world, port, out_dir, transport):
         res.append(bool(np.array_equal(host, ref.cpu().numpy().view(np.uint16))))
         ctx.sync()
         if transport == "nccl":
-            # prefill: the routed rows of remote routes cross in an all-to-all
+            # prefill, both exchanges: the gathered tokens with the slot rows
+            # reduce-scattered, and the routed rows of remote routes in an
+            # all-to-all there and back
             gen.manual_seed(700 + rank)
             xp = torch.randn((40, H), generator=gen, device="cuda").to(torch.bfloat16).view(torch.int16).contiguous()
-            outp = torch.empty_like(xp)
-            ep.prefill(xp, outp)
             refp = torch.empty_like(xp)
             full.prefill(xp, K, refp, act="swiglu")
-            torch.cuda.synchronize()
-            res.append(bool(torch.equal(outp, refp)))
-            res.append(ep.last_prefill_exchange["rows_sent"] > 0)
+            for exchange in ("gather", "a2a"):
+                ep.prefill_exchange = exchange
+                outp = torch.empty_like(xp)
+                ep.prefill(xp, outp)
+                torch.cuda.synchronize()
+                res.append(bool(torch.equal(outp, refp)))
+                res.append(ep.last_prefill_exchange["rows_sent"] > 0)
             ctx.sync()
         if transport == "p2p":
             res.append(ep._ep_M == M)           # the peer path really ran
