@@ -147,8 +147,23 @@ __global__ void __launch_bounds__(256) rc_pf_logits_kernel(const uint16_t *x, in
 #pragma unroll
     for (int ei = 0; ei < kPfLogitExperts; ++ei) acc[ei] = 0.0;
     const uint4 *xr = reinterpret_cast<const uint4 *>(x + (size_t)t * hidden);
+    // the lane's slices of the token row, all requested before the sums
+    // (hidden <= 8 * 256 columns here; wider rows take the loop below)
+    constexpr int kPre = 8;
+    uint4 xpre[kPre];
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) xpre[i] = lane + 32 * i < v8 ? __ldg(xr + lane + 32 * i) : make_uint4(0, 0, 0, 0);
     for (int c = lane; c < v8; c += 32) {
-      const uint4 xa = __ldg(xr + c);
+      const int ci = (c - lane) / 32;
+      uint4 xa;
+      if (ci < kPre) {
+        xa = xpre[0];
+#pragma unroll
+        for (int i = 1; i < kPre; ++i)
+          if (ci == i) xa = xpre[i];
+      } else {
+        xa = __ldg(xr + c);
+      }
       const uint32_t xs[4] = {xa.x, xa.y, xa.z, xa.w};
       double xd[8];
 #pragma unroll
