@@ -913,7 +913,7 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
                      "traffic_source": TRAFFIC_SOURCE["moe_layer_t1"],
                      "per_rank_bytes_per_step": round(avg_rank_bytes), "kernel": kdesc},
         "e2e": {"value": round(world * M / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * M * H,
-                "d2h_bytes_per_step": 2 * M * H, "api": "ExpertParallelMoe.decode_host (synchronous)"},
+                "d2h_bytes_per_step": 2 * M * H, "api": "ExpertParallelMoe.decode_host -> rc_moe_decode_host / rc_moe_ep_decode_host (synchronous)"},
         "gpu_launches": per_step * args.steps,
         "clocks": clk,
         "cpu_baseline": cpu,
@@ -1096,7 +1096,7 @@ def run_moe_prefill(args, ctx, torch, dev, rank: int, world: int, local_rank: in
                      "tensor_peak_tflops": tflops_peak, "tensor_frac": round(tc_frac, 4),
                      "per_rank_bytes_per_step": round(avg_bytes), "per_rank_flops_per_step": round(avg_flops)},
         "e2e": {"value": round(T / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * M * H,
-                "d2h_bytes_per_step": 2 * M * H, "api": "ExpertParallelMoe.prefill_host (synchronous)"},
+                "d2h_bytes_per_step": 2 * M * H, "api": "ExpertParallelMoe.prefill_host (synchronous; rc_moe_prefill_host on one GPU)"},
         "gpu_launches": (8 if world == 1 else 9) * args.steps,
         "clocks": clk,
         "cpu_baseline": cpu,

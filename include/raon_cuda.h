@@ -224,6 +224,23 @@ int rc_moe_decode(rc_moe *m, const uint16_t *x_dev, int T, int k, int router, in
                   float scaling, int act, float gate_beta, float value_beta, uint16_t *out_dev,
                   int32_t *ids_dev, float *w_dev, void *stream);
 
+/* rc_moe_decode, rc_moe_prefill and rc_moe_ep_decode on host buffers (the
+ * entry a host runtime such as the reference's ``Backend`` binds): x_host
+ * [T][hidden] (rc_moe_ep_decode_host: [tokens_per_rank][hidden]) is copied in
+ * through pinned staging, the layer runs on ``stream`` (NULL: the context's),
+ * out_host (and ids_host / w_host [T][k] when given) are copied back, and one
+ * wait covers the results and the device error word.  Work the caller queued
+ * on other streams is not waited for. */
+int rc_moe_decode_host(rc_moe *m, const uint16_t *x_host, int T, int k, int router, int renormalize,
+                       float scaling, int act, float gate_beta, float value_beta, uint16_t *out_host,
+                       int32_t *ids_host, float *w_host, void *stream);
+int rc_moe_prefill_host(rc_moe *m, const uint16_t *x_host, int T, int k, int router, int renormalize,
+                        float scaling, int act, float gate_beta, float value_beta, uint16_t *out_host,
+                        int32_t *ids_host, float *w_host, void *stream);
+int rc_moe_ep_decode_host(rc_moe *m, const uint16_t *x_host, int k, int router, int renormalize,
+                          float scaling, int act, float gate_beta, float value_beta, uint16_t *out_host,
+                          void *stream);
+
 /* Expert-parallel halves of rc_moe_decode.  decode_local routes all T tokens,
  * runs the routed experts [expert_lo, expert_hi) for every token and the
  * shared expert for tokens [shared_t0, shared_t0 + shared_tn), and writes the

@@ -75,6 +75,9 @@ SIGNATURES = {
     "rc_moe_experts_host": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _F, _I, _P]),
     "rc_moe_experts_grouped": (_I, [_P, _P, _I, _P, _P, _I, _P, _I, _F, _F, _P, _P, _P]),
     "rc_moe_decode": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _P, _P, _P, _P]),
+    "rc_moe_decode_host": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _P, _P, _P, _P]),
+    "rc_moe_prefill_host": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _P, _P, _P, _P]),
+    "rc_moe_ep_decode_host": (_I, [_P, _P, _I, _I, _I, _F, _I, _F, _F, _P, _P]),
     "rc_moe_decode_local": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _I, _I, _I, _I, _P, _P, _P]),
     "rc_moe_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _P]),
     "rc_moe_prefill": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _P, _P, _P, _P]),

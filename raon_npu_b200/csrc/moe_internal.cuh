@@ -11,6 +11,7 @@ namespace rc {
 
 constexpr int kMoeMaxK = 16;               // routed experts per token
 constexpr int kMoeMaxTokens = 16;          // tokens per call: two 8-column mma blocks
+constexpr int kPfMaxTokens = 4096;         // tokens per prefill call
 constexpr int kMoeMaxExperts = 256;
 constexpr int kMoeWarps = 16;
 constexpr int kMoePartialBytes = 32 * 1024;   // per-CTA unit partials of one round

@@ -863,8 +863,7 @@ int rc_gemv_host(rc_ctx *ctx, const rc_weight *w, const void *x_host, int x_dtyp
   rc = rc_gemv(ctx, w, ctx->dev_x, x_dtype, w->k, T, ctx->dev_y, x_dtype, w->n, 0, w->n, bias_dev, nullptr);
   if (rc) return rc;
   RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, yb, cudaMemcpyDeviceToHost, ctx->stream));
-  RC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-  rc = check_error_word(ctx);
+  rc = finish_host_call(ctx, ctx->stream);
   if (rc) return rc;
   memcpy(y_host, ctx->pin_y, yb);
   return RC_OK;

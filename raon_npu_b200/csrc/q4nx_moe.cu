@@ -1062,8 +1062,7 @@ int rc_moe_experts_host(rc_moe *m, const uint16_t *x_host, int T, const int32_t 
                       static_cast<uint16_t *>(ctx->dev_y), nullptr);
   if (rc) return rc;
   RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, yb, cudaMemcpyDeviceToHost, ctx->stream));
-  RC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-  rc = check_error_word(ctx);
+  rc = finish_host_call(ctx, ctx->stream);
   if (rc) return rc;
   memcpy(out_host, ctx->pin_y, yb);
   return RC_OK;
@@ -1309,6 +1308,81 @@ int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int re
   return moe_decode_persistent(m, reinterpret_cast<const uint16_t *>(ep->base + ep_tok_off()), T, k, router,
                           renormalize, scaling, act, gate_beta, value_beta, own, m->down_out, 0, out_dev, nullptr,
                           nullptr, nullptr, pick_stream(m->ctx, stream), &a);
+}
+
+
+}  // extern "C"
+
+// A layer call on host buffers: the token rows are copied in from pinned
+// staging, ``run`` launches on the stream, the output rows (and the optional
+// ids / weights [T_out][k]) are copied back, and one wait covers the results
+// and the error word.
+template <class Run>
+static int moe_layer_host(rc_moe *m, const uint16_t *x_host, int T_in, int T_out, int k, uint16_t *out_host,
+                          int32_t *ids_host, float *w_host, void *stream, Run run) {
+  rc_ctx *ctx = m->ctx;
+  RC_CUDA_TRY(cudaSetDevice(ctx->device));
+  const cudaStream_t s = pick_stream(ctx, stream);
+  const size_t xb = (size_t)T_in * m->hidden * 2, yb = (size_t)T_out * m->hidden * 2;
+  const size_t rb = (size_t)T_out * k * 4;
+  const size_t off_ids = (yb + 15) / 16 * 16, off_w = off_ids + (rb + 15) / 16 * 16;
+  const size_t back = (ids_host || w_host) ? off_w + rb : yb;
+  int rc = ensure_host_staging(ctx, xb, back);
+  if (rc) return rc;
+  memcpy(ctx->pin_x, x_host, xb);
+  RC_CUDA_TRY(cudaMemcpyAsync(ctx->dev_x, ctx->pin_x, xb, cudaMemcpyHostToDevice, s));
+  uint8_t *dy = static_cast<uint8_t *>(ctx->dev_y);
+  rc = run(static_cast<const uint16_t *>(ctx->dev_x), reinterpret_cast<uint16_t *>(dy),
+           ids_host ? reinterpret_cast<int32_t *>(dy + off_ids) : nullptr,
+           w_host ? reinterpret_cast<float *>(dy + off_w) : nullptr, static_cast<void *>(s));
+  if (rc) return rc;
+  RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, back, cudaMemcpyDeviceToHost, s));
+  rc = finish_host_call(ctx, s);
+  if (rc) return rc;
+  const uint8_t *py = static_cast<const uint8_t *>(ctx->pin_y);
+  memcpy(out_host, py, yb);
+  if (ids_host) memcpy(ids_host, py + off_ids, rb);
+  if (w_host) memcpy(w_host, py + off_w, rb);
+  return RC_OK;
+}
+
+extern "C" {
+
+int rc_moe_decode_host(rc_moe *m, const uint16_t *x_host, int T, int k, int router, int renormalize, float scaling,
+                       int act, float gate_beta, float value_beta, uint16_t *out_host, int32_t *ids_host,
+                       float *w_host, void *stream) {
+  RC_CHECK_ARG(m && x_host && out_host, "rc_moe_decode_host: NULL argument");
+  RC_MOE_CHECK_TK("rc_moe_decode_host");
+  return moe_layer_host(m, x_host, T, T, k, out_host, ids_host, w_host, stream,
+                        [&](const uint16_t *x, uint16_t *y, int32_t *ids, float *w, void *st) {
+                          return rc_moe_decode(m, x, T, k, router, renormalize, scaling, act, gate_beta, value_beta,
+                                               y, ids, w, st);
+                        });
+}
+
+int rc_moe_prefill_host(rc_moe *m, const uint16_t *x_host, int T, int k, int router, int renormalize, float scaling,
+                        int act, float gate_beta, float value_beta, uint16_t *out_host, int32_t *ids_host,
+                        float *w_host, void *stream) {
+  RC_CHECK_ARG(m && x_host && out_host, "rc_moe_prefill_host: NULL argument");
+  RC_CHECK_ARG(T >= 1 && T <= kPfMaxTokens, "rc_moe_prefill_host: T=%d outside 1..%d", T, kPfMaxTokens);
+  RC_CHECK_ARG(k >= 1 && k <= kMoeMaxK, "rc_moe_prefill_host: k=%d outside 1..%d", k, kMoeMaxK);
+  return moe_layer_host(m, x_host, T, T, k, out_host, ids_host, w_host, stream,
+                        [&](const uint16_t *x, uint16_t *y, int32_t *ids, float *w, void *st) {
+                          return rc_moe_prefill(m, x, T, k, router, renormalize, scaling, act, gate_beta, value_beta,
+                                                y, ids, w, st);
+                        });
+}
+
+int rc_moe_ep_decode_host(rc_moe *m, const uint16_t *x_host, int k, int router, int renormalize, float scaling,
+                          int act, float gate_beta, float value_beta, uint16_t *out_host, void *stream) {
+  RC_CHECK_ARG(m && x_host && out_host, "rc_moe_ep_decode_host: NULL argument");
+  RC_CHECK_ARG(m->ep, "rc_moe_ep_decode_host: rc_moe_ep_init has not run");
+  const int M = m->ep->M;
+  return moe_layer_host(m, x_host, M, M, k, out_host, nullptr, nullptr, stream,
+                        [&](const uint16_t *x, uint16_t *y, int32_t *, float *, void *st) {
+                          return rc_moe_ep_decode(m, x, k, router, renormalize, scaling, act, gate_beta, value_beta,
+                                                  y, st);
+                        });
 }
 
 }  // extern "C"

@@ -47,7 +47,6 @@
 
 namespace rc {
 
-constexpr int kPfMaxTokens = 4096;
 constexpr int kPfRows = 128;         // weight rows per tile: MMA M, TMEM lanes
 constexpr int kPfCols = 64;          // token columns per work item: max MMA N
 constexpr int kPfBlk = 8;            // token rows per block of the register-fragment (mma.sync) path

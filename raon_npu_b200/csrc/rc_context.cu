@@ -72,10 +72,8 @@ static int grow_device(void **p, size_t *cap, size_t need) {
   return RC_OK;
 }
 
-// Report (and clear) the error word a kernel leaves when a bounded wait gives up.
-int check_error_word(rc_ctx *ctx) {
-  int word = 0;
-  RC_CUDA_TRY(cudaMemcpy(&word, ctx->err, sizeof(int), cudaMemcpyDeviceToHost));
+// The status of an error word read back from the device (cleared when set).
+static int report_error_word(rc_ctx *ctx, int word) {
   if (word) {
     RC_CUDA_TRY(cudaMemset(ctx->err, 0, sizeof(int)));
     if (word == 2) {
@@ -97,6 +95,21 @@ int check_error_word(rc_ctx *ctx) {
   return RC_OK;
 }
 
+// Report (and clear) the error word a kernel leaves when a bounded wait gives up.
+int check_error_word(rc_ctx *ctx) {
+  int word = 0;
+  RC_CUDA_TRY(cudaMemcpy(&word, ctx->err, sizeof(int), cudaMemcpyDeviceToHost));
+  return report_error_word(ctx, word);
+}
+
+// The end of a host-buffer entry point: the error word follows the results
+// back on stream s (pinned, asynchronous), so one wait covers both.
+int finish_host_call(rc_ctx *ctx, cudaStream_t s) {
+  RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_err, ctx->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  RC_CUDA_TRY(cudaStreamSynchronize(s));
+  return report_error_word(ctx, *ctx->pin_err);
+}
+
 int ensure_sample_scratch(rc_ctx *ctx, size_t bytes) {
   return grow_device(&ctx->sample_bits, &ctx->sample_bits_cap, bytes);
 }
@@ -105,6 +118,7 @@ int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb) {
   int rc;
   if ((rc = grow_pinned(&ctx->pin_x, &ctx->pin_x_cap, xb))) return rc;
   if ((rc = grow_pinned(&ctx->pin_y, &ctx->pin_y_cap, yb))) return rc;
+  if (!ctx->pin_err) RC_CUDA_TRY(cudaMallocHost(reinterpret_cast<void **>(&ctx->pin_err), sizeof(int)));
   if ((rc = grow_device(&ctx->dev_x, &ctx->dev_x_cap, xb))) return rc;
   if ((rc = grow_device(&ctx->dev_y, &ctx->dev_y_cap, yb))) return rc;
   return RC_OK;
@@ -175,6 +189,7 @@ int rc_destroy(rc_ctx *ctx) {
   cudaFree(ctx->sample_bits);
   if (ctx->pin_x) cudaFreeHost(ctx->pin_x);
   if (ctx->pin_y) cudaFreeHost(ctx->pin_y);
+  if (ctx->pin_err) cudaFreeHost(ctx->pin_err);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   free(ctx);
   return RC_OK;

@@ -106,8 +106,9 @@ struct rc_ctx {
   int *err;             // device error word
   unsigned timeout_epoch;   // bumped whenever a bounded device wait is found to have given up
   int *qflag;           // quantiser status word (non-finite input / overflow)
-  // Host staging for rc_gemv_host.
+  // Host staging of the host-buffer entry points (rc_*_host).
   void *pin_x, *pin_y;
+  int *pin_err;         // pinned copy of the error word
   size_t pin_x_cap, pin_y_cap;
   void *dev_x, *dev_y;
   size_t dev_x_cap, dev_y_cap;
@@ -121,6 +122,7 @@ int ensure_gemv_scratch(rc_ctx *ctx, int k, int n_tiles);
 int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb);
 int ensure_sample_scratch(rc_ctx *ctx, size_t bytes);
 int check_error_word(rc_ctx *ctx);
+int finish_host_call(rc_ctx *ctx, cudaStream_t s);
 // Grouped down projection of an MoE layer with bfp16ebs8 down matrices
 // (bfp16_gemv.cu).  Decode: the group tables of the q4nx MoE kernels.
 // Prefill (blk_row0 != null): 8-row blocks of the permuted rows, block b =

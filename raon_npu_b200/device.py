@@ -414,6 +414,38 @@ class MoeLayer:
             ctypes.c_void_p(_ptr(out_dev)), ctypes.c_void_p(_ptr(ids_dev)), ctypes.c_void_p(_ptr(w_dev)),
             ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_decode")
 
+    def _layer_host(self, fn: str, x: np.ndarray, k: int, routes: bool, stream: int | None, router: str,
+                    renormalize: bool, scaling: float, act: str, gate_beta: float, value_beta: float):
+        xh = np.ascontiguousarray(x, dtype=np.uint16)
+        if xh.shape[-1] != self.hidden or xh.ndim > 2:
+            raise ValueError(f"x must be [T, {self.hidden}] bf16 bits, got {xh.shape}")
+        T = 1 if xh.ndim == 1 else xh.shape[0]
+        out = np.empty(xh.shape, np.uint16)
+        ids = np.empty((T, k), np.int32) if routes else None
+        w = np.empty((T, k), np.float32) if routes else None
+        check(getattr(self.ctx.lib, fn)(
+            self.handle, ctypes.c_void_p(xh.ctypes.data), T, int(k), ROUTER_CODES[router], int(bool(renormalize)),
+            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(out.ctypes.data),
+            ctypes.c_void_p(ids.ctypes.data if routes else None), ctypes.c_void_p(w.ctypes.data if routes else None),
+            ctypes.c_void_p(_stream_for(stream))), fn)
+        return (out, ids, w) if routes else out
+
+    def decode_host(self, x: np.ndarray, k: int, routes: bool = False, stream: int | None = None,
+                    router: str = "softmax", renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu",
+                    gate_beta: float = 4.0, value_beta: float = 25.0):
+        """``decode`` on host arrays through one C call (pinned copies in and
+        out, one wait): x [T, hidden] bf16 bits -> out [T, hidden], and with
+        ``routes`` also the top-k ids / weights [T, k]."""
+        return self._layer_host("rc_moe_decode_host", x, k, routes, stream, router, renormalize, scaling, act,
+                                gate_beta, value_beta)
+
+    def prefill_host(self, x: np.ndarray, k: int, routes: bool = False, stream: int | None = None,
+                     router: str = "softmax", renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu",
+                     gate_beta: float = 4.0, value_beta: float = 25.0):
+        """``prefill`` on host arrays, as ``decode_host``."""
+        return self._layer_host("rc_moe_prefill_host", x, k, routes, stream, router, renormalize, scaling, act,
+                                gate_beta, value_beta)
+
     def decode_local(self, x_dev, k: int, slot_out_dev, slot_w_dev, experts: tuple[int, int] | None = None,
                      shared_tokens: tuple[int, int] | None = None, router: str = "softmax",
                      renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
@@ -460,6 +492,21 @@ class MoeLayer:
             self.handle, ctypes.c_void_p(_ptr(x_dev)), int(k), ROUTER_CODES[router], int(bool(renormalize)),
             float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(_ptr(out_dev)),
             ctypes.c_void_p(_stream_for(stream, x_dev, out_dev))), "rc_moe_ep_decode")
+
+    def ep_decode_host(self, x: np.ndarray, k: int, stream: int | None = None, router: str = "softmax",
+                       renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,
+                       value_beta: float = 25.0) -> np.ndarray:
+        """``ep_decode`` on host arrays through one C call: this rank's tokens
+        x [M, hidden] bf16 bits -> out [M, hidden]."""
+        xh = np.ascontiguousarray(x, dtype=np.uint16)
+        if xh.ndim != 2 or xh.shape[1] != self.hidden:
+            raise ValueError(f"x must be [M, {self.hidden}] bf16 bits, got {xh.shape}")
+        out = np.empty(xh.shape, np.uint16)
+        check(self.ctx.lib.rc_moe_ep_decode_host(
+            self.handle, ctypes.c_void_p(xh.ctypes.data), int(k), ROUTER_CODES[router], int(bool(renormalize)),
+            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(out.ctypes.data),
+            ctypes.c_void_p(_stream_for(stream))), "rc_moe_ep_decode_host")
+        return out
 
     def prefill(self, x_dev, k: int, out_dev, ids_dev=None, w_dev=None, router: str = "softmax",
                 renormalize: bool = True, scaling: float = 1.0, act: str = "swiglu", gate_beta: float = 4.0,

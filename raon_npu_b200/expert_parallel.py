@@ -19,10 +19,13 @@ tokens:
 4. ``combine`` (ascending expert ID, f32, then the shared expert) of the own
    tokens.
 
-Prefill instead sends only the routed rows: every rank routes its own
-tokens, computes its own experts for them, and exchanges the token rows of
-remote routes with their experts' owners in an all-to-all, the owners
-returning the expert rows the same way (``prefill``).
+Prefill (``prefill``) has two exchanges.  "gather" (the default) is the
+same four steps over the ranks' whole token sets: all-gather, this rank's
+experts over all tokens, reduce-scatter of the slot rows, combine -- fixed
+sizes, so a CUDA graph can hold it.  "a2a" sends only the routed rows: every
+rank routes its own tokens and exchanges the token rows of remote routes with
+their experts' owners in an all-to-all, the owners returning the expert rows
+the same way.
 
 The result of every token is byte-identical to the single-GPU decode
 (``MoeLayer.decode``): each expert's rows come out of whole-tile GEMVs whose
@@ -41,6 +44,8 @@ buffers are CUDA IPC mappings set up once per token count with one
 from __future__ import annotations
 
 import numpy as np
+
+from .device import CUDA_STREAM_LEGACY
 
 
 def _bf16(t):
@@ -328,11 +333,31 @@ class ExpertParallelMoe:
         torch.cuda.current_stream(dev).synchronize()
         return pin_out.numpy().copy().view(np.uint16)
 
+    @staticmethod
+    def _torch_stream() -> int:
+        """The current torch stream as the C ABI takes it (the legacy default
+        stream as cudaStreamLegacy), so host calls are ordered after the
+        device calls made through the tensors' streams."""
+        import torch
+        h = int(torch.cuda.current_stream().cuda_stream)
+        return h if h != 0 else CUDA_STREAM_LEGACY
+
     def decode_host(self, x: np.ndarray) -> np.ndarray:
         """Host entry point: x [M, hidden] bf16 bits -> out [M, hidden] (copies in
-        from pinned memory, decodes, copies out, waits)."""
-        return self._host_call(x, self.decode, "dec")
+        from pinned memory, decodes, copies out, waits).  One GPU and the
+        peer-memory exchange go through one C call each (the copies, the layer
+        and a single wait in native code); the NCCL exchange through torch."""
+        xs = np.ascontiguousarray(x, dtype=np.uint16)
+        if self.world == 1:
+            return self.layer.decode_host(xs, self.k, stream=self._torch_stream(), **self.kw)
+        if self._use_p2p(xs.shape[0]):
+            return self.layer.ep_decode_host(xs, self.k, stream=self._torch_stream(), **self.kw)
+        return self._host_call(xs, self.decode, "dec")
 
     def prefill_host(self, x: np.ndarray) -> np.ndarray:
-        """``prefill`` on host buffers, as ``decode_host``."""
-        return self._host_call(x, self.prefill, "pf")
+        """``prefill`` on host buffers, as ``decode_host`` (one C call on one
+        GPU; the collective exchanges through torch)."""
+        xs = np.ascontiguousarray(x, dtype=np.uint16)
+        if self.world == 1:
+            return self.layer.prefill_host(xs, self.k, stream=self._torch_stream(), **self.kw)
+        return self._host_call(xs, self.prefill, "pf")

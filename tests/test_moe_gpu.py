@@ -675,3 +675,41 @@ def test_fused_decode_edge_shapes(torch, ctx, hidden, inter, E, k, T):
     assert torch.equal(fw, sw)
     assert torch.equal(fo, so)
     layer.close()
+
+
+@pytest.mark.parametrize("T", [1, 5, 16, 40, 300])
+def test_host_entry_points_equal_device_calls(torch, ctx, T):
+    """rc_moe_decode_host / rc_moe_prefill_host (and ExpertParallelMoe's host
+    entry on one GPU) give the bytes, ids and weights of the device calls."""
+    from raon_npu_b200.expert_parallel import ExpertParallelMoe
+    E, k = 32, 8
+    layer, _, _ = _config3_layer(torch, ctx, n_experts=E, seed=98)
+    rng = np.random.default_rng(700 + T)
+    x = q.f32_to_bf16(rng.standard_normal((T, 2048)).astype(np.float32))
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    out = torch.empty((T, 2048), dtype=torch.int16, device="cuda")
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    entries = ([("decode", layer.decode, layer.decode_host)] if T <= 16 else []) + \
+        [("prefill", layer.prefill, layer.prefill_host)]
+    host_out = {}
+    for name, dev_call, host_call in entries:
+        dev_call(xd, k, out, ids, w, act="situ", router="sigmoid_bias", scaling=1.5)
+        torch.cuda.synchronize()
+        ctx.sync()
+        ho, hi, hw = host_call(x, k, routes=True, act="situ", router="sigmoid_bias", scaling=1.5)
+        np.testing.assert_array_equal(ho, out.cpu().numpy().view(np.uint16), err_msg=name)
+        np.testing.assert_array_equal(hi, ids.cpu().numpy(), err_msg=name)
+        np.testing.assert_array_equal(hw, w.cpu().numpy(), err_msg=name)
+        np.testing.assert_array_equal(host_call(x, k, act="situ", router="sigmoid_bias", scaling=1.5), ho,
+                                      err_msg=name)
+        host_out[name] = ho
+    ep = ExpertParallelMoe(layer, k, act="situ", router="sigmoid_bias", scaling=1.5)
+    if T <= 16:
+        np.testing.assert_array_equal(ep.decode_host(x), host_out["decode"])
+    np.testing.assert_array_equal(ep.prefill_host(x), host_out["prefill"])
+    with pytest.raises(ValueError):
+        layer.decode_host(np.zeros((17, 2048), np.uint16), k)
+    with pytest.raises(ValueError):
+        layer.decode_host(np.zeros((1, 1024), np.uint16), k)
+    layer.close()
