@@ -124,7 +124,11 @@ __host__ __device__ constexpr size_t dc_stage_bytes(int nblk, int tsl, int kb) {
 }
 
 // One warp per (block, slot, k-block) task; tasks w0, w0 + nw, ... of
-// nblk * Tsl * kb.  Row of (b, t): src + (b * row_blk + t) * ld.
+// nblk * Tsl * kb.  Row of (b, t): src + (b * row_blk + t) * ld.  A warp
+// requests the rows of up to kDcStageBatch tasks before it converts the
+// first, so their L2 latencies overlap.
+constexpr int kDcStageBatch = 3;
+
 static __device__ __noinline__ void dc_stage(const uint16_t *src, int ld, int row_blk, int nblk, int tsl, int kb,
                                              uint8_t *area, int w0, int nw) {
   const int lane = threadIdx.x & 31;
@@ -133,49 +137,62 @@ static __device__ __noinline__ void dc_stage(const uint16_t *src, int ld, int ro
   float *inv = reinterpret_cast<float *>(area + (size_t)nblk * tsl * kb * 576);
   const int ntask = nblk * tsl * kb;
 #pragma unroll 1
-  for (int i = w0; i < ntask; i += nw) {
-    const int b = i / (tsl * kb), r = i - b * tsl * kb, t = r / kb, kbi = r - t * kb;
-    const uint4 raw = __ldcg(reinterpret_cast<const uint4 *>(src + ((size_t)b * row_blk + t) * ld +
-                                                               kbi * kUnitK + lane * 8));
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    float v[8];
+  for (int i0 = w0; i0 < ntask; i0 += kDcStageBatch * nw) {
+    uint4 raws[kDcStageBatch];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[2 * j] = bf16_lo_f32(w[j]);
-      v[2 * j + 1] = bf16_hi_f32(w[j]);
+    for (int jb = 0; jb < kDcStageBatch; ++jb) {
+      const int i = i0 + jb * nw;
+      if (i < ntask) {
+        const int b = i / (tsl * kb), r = i - b * tsl * kb, t = r / kb, kbi = r - t * kb;
+        raws[jb] = __ldcg(reinterpret_cast<const uint4 *>(src + ((size_t)b * row_blk + t) * ld + kbi * kUnitK +
+                                                          lane * 8));
+      }
     }
-    const int s = block_shift(warp_absmax(v));
-    const float sc = pow2f(s);
-    uint32_t hw[4];
-    float part = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = v[2 * j] * sc, c = v[2 * j + 1] * sc;
-      const __half2 h = __floats2half2_rn(a, c);
-      hw[j] = *reinterpret_cast<const uint32_t *>(&h);
-      part += a;   // a bf16 value times 2^s is exact in f16: sum the exact values
-      part += c;
-    }
-    const size_t u = (size_t)b * kb + kbi;
-    const int st = lane >> 1, jj = lane & 1;
-    uint32_t *fw = frag + (((u * 4 + (st >> 2)) * tsl + t) * 4) * 8 + (st & 3) * 2 + jj;
+    for (int jb = 0; jb < kDcStageBatch; ++jb) {
+      const int i = i0 + jb * nw;
+      if (i >= ntask) break;
+      const int b = i / (tsl * kb), r = i - b * tsl * kb, t = r / kb, kbi = r - t * kb;
+      const uint32_t w[4] = {raws[jb].x, raws[jb].y, raws[jb].z, raws[jb].w};
+      float v[8];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) fw[q * 8] = hw[q];
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    if ((lane & 3) == 0) {
-      const int gi = lane >> 2;
-      const float sp = part * 5.9604644775390625e-08f;   // S' 2^-24 (exact)
-      const uint16_t s1 = f32_to_bf16_rne(sp);
-      const float r1 = sp - bf16_to_f32(s1);
-      const uint16_t s2 = f32_to_bf16_rne(r1);
-      uint16_t *bw = bmin16 + ((u * tsl + t) * 4 + (gi >> 1)) * 8 + (gi & 1);
-      bw[0] = s1;
-      bw[2] = s2;
-      bw[4] = f32_to_bf16_rne(r1 - bf16_to_f32(s2));
-      bw[6] = 0;
+      for (int j = 0; j < 4; ++j) {
+        v[2 * j] = bf16_lo_f32(w[j]);
+        v[2 * j + 1] = bf16_hi_f32(w[j]);
+      }
+      const int s = block_shift(warp_absmax(v));
+      const float sc = pow2f(s);
+      uint32_t hw[4];
+      float part = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = v[2 * j] * sc, c = v[2 * j + 1] * sc;
+        const __half2 h = __floats2half2_rn(a, c);
+        hw[j] = *reinterpret_cast<const uint32_t *>(&h);
+        part += a;   // a bf16 value times 2^s is exact in f16: sum the exact values
+        part += c;
+      }
+      const size_t u = (size_t)b * kb + kbi;
+      const int st = lane >> 1, jj = lane & 1;
+      uint32_t *fw = frag + (((u * 4 + (st >> 2)) * tsl + t) * 4) * 8 + (st & 3) * 2 + jj;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) fw[q * 8] = hw[q];
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      if ((lane & 3) == 0) {
+        const int gi = lane >> 2;
+        const float sp = part * 5.9604644775390625e-08f;   // S' 2^-24 (exact)
+        const uint16_t s1 = f32_to_bf16_rne(sp);
+        const float r1 = sp - bf16_to_f32(s1);
+        const uint16_t s2 = f32_to_bf16_rne(r1);
+        uint16_t *bw = bmin16 + ((u * tsl + t) * 4 + (gi >> 1)) * 8 + (gi & 1);
+        bw[0] = s1;
+        bw[2] = s2;
+        bw[4] = f32_to_bf16_rne(r1 - bf16_to_f32(s2));
+        bw[6] = 0;
+      }
+      if (lane == 0) inv[u * tsl + t] = pow2f(-s);
     }
-    if (lane == 0) inv[u * tsl + t] = pow2f(-s);
   }
 }
 
