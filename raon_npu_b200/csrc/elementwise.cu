@@ -1,9 +1,65 @@
 // Elementwise glue of a decode step: the residual add of the hidden stream,
-// plain or followed by an RMS normalisation.
+// plain or followed by an RMS normalisation; the staging copies of the
+// host-buffer entry points.
 #include "rc_device.cuh"
 #include "rc_internal.cuh"
 
 namespace rc {
+
+// ------------------------------------------------------- host staging --
+// The host-buffer entry points move their inputs and results between pinned
+// host memory (mapped into the device's address space) and device memory with
+// this kernel rather than with copy-engine transfers: chained to its
+// neighbours by programmatic dependent launch it starts within about a
+// microsecond of its predecessor, where a copy-engine transfer of a few KB
+// costs several.  The copy out also carries the context's error word.
+constexpr int kStageThreads = 256;
+
+__global__ void __launch_bounds__(kStageThreads) rc_stage_copy_kernel(const uint8_t *src, uint8_t *dst, size_t bytes,
+                                                                   const int *err_src, int *err_dst) {
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  const size_t n16 = bytes / 16, stride = (size_t)gridDim.x * blockDim.x;
+  const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (size_t i = i0; i < n16; i += stride)
+    reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(src)[i];
+  for (size_t i = n16 * 16 + i0; i < bytes; i += stride) dst[i] = src[i];
+  if (err_dst && i0 == 0) *err_dst = *reinterpret_cast<const volatile int *>(err_src);
+}
+
+static int stage_copy(rc_ctx *ctx, void *dst, const void *src, size_t bytes, bool with_err, cudaStream_t s) {
+  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) != 0) {
+    set_error("host staging: buffers must be 16-byte aligned");
+    return RC_ERR_INVALID;
+  }
+  long long blocks = (long long)((bytes / 16 + kStageThreads - 1) / kStageThreads);
+  if (blocks < 1) blocks = 1;
+  if (blocks > 4ll * ctx->sm_count) blocks = 4ll * ctx->sm_count;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(kStageThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  RC_CUDA_TRY(cudaLaunchKernelEx(&cfg, rc_stage_copy_kernel, static_cast<const uint8_t *>(src),
+                                 static_cast<uint8_t *>(dst), bytes, with_err ? ctx->err : nullptr,
+                                 with_err ? ctx->pin_err : nullptr));
+  return RC_OK;
+}
+
+int host_copy_in(rc_ctx *ctx, void *dev, const void *pinned, size_t bytes, cudaStream_t s) {
+  return stage_copy(ctx, dev, pinned, bytes, false, s);
+}
+
+int host_copy_out_and_wait(rc_ctx *ctx, void *pinned, const void *dev, size_t bytes, cudaStream_t s) {
+  int rc = stage_copy(ctx, pinned, dev, bytes, true, s);
+  if (rc) return rc;
+  RC_CUDA_TRY(cudaStreamSynchronize(s));
+  return report_error_word(ctx, *ctx->pin_err);
+}
 
 // out = RTNE(f32(a) + f32(b)), 8 bf16 per thread.
 __global__ void rc_add_bf16_kernel(const uint16_t *a, const uint16_t *b, uint16_t *out, long long n) {

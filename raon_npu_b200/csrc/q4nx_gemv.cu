@@ -859,12 +859,10 @@ int rc_gemv_host(rc_ctx *ctx, const rc_weight *w, const void *x_host, int x_dtyp
   int rc = ensure_host_staging(ctx, xb, yb);
   if (rc) return rc;
   memcpy(ctx->pin_x, x_host, xb);
-  RC_CUDA_TRY(cudaMemcpyAsync(ctx->dev_x, ctx->pin_x, xb, cudaMemcpyHostToDevice, ctx->stream));
+  if ((rc = host_copy_in(ctx, ctx->dev_x, ctx->pin_x, xb, ctx->stream))) return rc;
   rc = rc_gemv(ctx, w, ctx->dev_x, x_dtype, w->k, T, ctx->dev_y, x_dtype, w->n, 0, w->n, bias_dev, nullptr);
   if (rc) return rc;
-  RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, yb, cudaMemcpyDeviceToHost, ctx->stream));
-  rc = finish_host_call(ctx, ctx->stream);
-  if (rc) return rc;
+  if ((rc = host_copy_out_and_wait(ctx, ctx->pin_y, ctx->dev_y, yb, ctx->stream))) return rc;
   memcpy(y_host, ctx->pin_y, yb);
   return RC_OK;
 }

@@ -1056,14 +1056,12 @@ int rc_moe_experts_host(rc_moe *m, const uint16_t *x_host, int T, const int32_t 
   memcpy(px + off_ids, ids_host, id_bytes);
   memcpy(px + off_w, w_host, id_bytes);
   uint8_t *dx = static_cast<uint8_t *>(ctx->dev_x);
-  RC_CUDA_TRY(cudaMemcpyAsync(dx, px, xb, cudaMemcpyHostToDevice, ctx->stream));
+  if ((rc = host_copy_in(ctx, dx, px, xb, ctx->stream))) return rc;
   rc = rc_moe_experts(m, reinterpret_cast<const uint16_t *>(dx), T, reinterpret_cast<const int32_t *>(dx + off_ids),
                       reinterpret_cast<const float *>(dx + off_w), k, act, gate_beta, value_beta, with_shared,
                       static_cast<uint16_t *>(ctx->dev_y), nullptr);
   if (rc) return rc;
-  RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, yb, cudaMemcpyDeviceToHost, ctx->stream));
-  rc = finish_host_call(ctx, ctx->stream);
-  if (rc) return rc;
+  if ((rc = host_copy_out_and_wait(ctx, ctx->pin_y, ctx->dev_y, yb, ctx->stream))) return rc;
   memcpy(out_host, ctx->pin_y, yb);
   return RC_OK;
 }
@@ -1315,8 +1313,8 @@ int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int re
 
 // A layer call on host buffers: the token rows are copied in from pinned
 // staging, ``run`` launches on the stream, the output rows (and the optional
-// ids / weights [T_out][k]) are copied back, and one wait covers the results
-// and the error word.
+// ids / weights [T_out][k]) are copied back with the error word, and one wait
+// covers them (the copies are kernels: host_copy_in / host_copy_out_and_wait).
 template <class Run>
 static int moe_layer_host(rc_moe *m, const uint16_t *x_host, int T_in, int T_out, int k, uint16_t *out_host,
                           int32_t *ids_host, float *w_host, void *stream, Run run) {
@@ -1330,15 +1328,13 @@ static int moe_layer_host(rc_moe *m, const uint16_t *x_host, int T_in, int T_out
   int rc = ensure_host_staging(ctx, xb, back);
   if (rc) return rc;
   memcpy(ctx->pin_x, x_host, xb);
-  RC_CUDA_TRY(cudaMemcpyAsync(ctx->dev_x, ctx->pin_x, xb, cudaMemcpyHostToDevice, s));
+  if ((rc = host_copy_in(ctx, ctx->dev_x, ctx->pin_x, xb, s))) return rc;
   uint8_t *dy = static_cast<uint8_t *>(ctx->dev_y);
   rc = run(static_cast<const uint16_t *>(ctx->dev_x), reinterpret_cast<uint16_t *>(dy),
            ids_host ? reinterpret_cast<int32_t *>(dy + off_ids) : nullptr,
            w_host ? reinterpret_cast<float *>(dy + off_w) : nullptr, static_cast<void *>(s));
   if (rc) return rc;
-  RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, back, cudaMemcpyDeviceToHost, s));
-  rc = finish_host_call(ctx, s);
-  if (rc) return rc;
+  if ((rc = host_copy_out_and_wait(ctx, ctx->pin_y, ctx->dev_y, back, s))) return rc;
   const uint8_t *py = static_cast<const uint8_t *>(ctx->pin_y);
   memcpy(out_host, py, yb);
   if (ids_host) memcpy(ids_host, py + off_ids, rb);

@@ -73,7 +73,7 @@ static int grow_device(void **p, size_t *cap, size_t need) {
 }
 
 // The status of an error word read back from the device (cleared when set).
-static int report_error_word(rc_ctx *ctx, int word) {
+int report_error_word(rc_ctx *ctx, int word) {
   if (word) {
     RC_CUDA_TRY(cudaMemset(ctx->err, 0, sizeof(int)));
     if (word == 2) {
@@ -100,14 +100,6 @@ int check_error_word(rc_ctx *ctx) {
   int word = 0;
   RC_CUDA_TRY(cudaMemcpy(&word, ctx->err, sizeof(int), cudaMemcpyDeviceToHost));
   return report_error_word(ctx, word);
-}
-
-// The end of a host-buffer entry point: the error word follows the results
-// back on stream s (pinned, asynchronous), so one wait covers both.
-int finish_host_call(rc_ctx *ctx, cudaStream_t s) {
-  RC_CUDA_TRY(cudaMemcpyAsync(ctx->pin_err, ctx->err, sizeof(int), cudaMemcpyDeviceToHost, s));
-  RC_CUDA_TRY(cudaStreamSynchronize(s));
-  return report_error_word(ctx, *ctx->pin_err);
 }
 
 int ensure_sample_scratch(rc_ctx *ctx, size_t bytes) {

@@ -122,7 +122,12 @@ int ensure_gemv_scratch(rc_ctx *ctx, int k, int n_tiles);
 int ensure_host_staging(rc_ctx *ctx, size_t xb, size_t yb);
 int ensure_sample_scratch(rc_ctx *ctx, size_t bytes);
 int check_error_word(rc_ctx *ctx);
-int finish_host_call(rc_ctx *ctx, cudaStream_t s);
+int report_error_word(rc_ctx *ctx, int word);
+// Host staging of the host-buffer entry points (elementwise.cu): pinned host
+// memory <-> device memory by kernels on stream s; the copy out also brings
+// the error word back, then waits for s and reports it.
+int host_copy_in(rc_ctx *ctx, void *dev, const void *pinned, size_t bytes, cudaStream_t s);
+int host_copy_out_and_wait(rc_ctx *ctx, void *pinned, const void *dev, size_t bytes, cudaStream_t s);
 // Grouped down projection of an MoE layer with bfp16ebs8 down matrices
 // (bfp16_gemv.cu).  Decode: the group tables of the q4nx MoE kernels.
 // Prefill (blk_row0 != null): 8-row blocks of the permuted rows, block b =

@@ -23,6 +23,17 @@ def _ptr(t) -> int:
     return int(t.data_ptr())
 
 
+_char_from_buffer = ctypes.c_char.from_buffer
+
+
+def _np_addr(a: np.ndarray) -> int:
+    """Address of a C-contiguous host array's first byte (a writable array's
+    through the buffer protocol, which costs a fraction of ``a.ctypes``)."""
+    if a.flags.writeable and a.size:
+        return ctypes.addressof(_char_from_buffer(a))
+    return a.ctypes.data
+
+
 def _stream_for(stream, *tensors) -> int:
     """The stream to launch on: an explicit one, else the current torch stream of
     the first torch tensor argument (so launches are ordered after the torch
@@ -229,9 +240,8 @@ class Q4nxWeight:
         if x.ndim != 2 or x.shape[1] != self.k:
             raise ValueError(f"x must be [T, {self.k}], got {x.shape}")
         xc = np.ascontiguousarray(x)
-        check(self.ctx.lib.rc_gemv_host(self.ctx.handle, self.handle, ctypes.c_void_p(xc.ctypes.data), dt,
-                                        int(x.shape[0]), ctypes.c_void_p(out.ctypes.data),
-                                        ctypes.c_void_p(_ptr(bias_dev))), "rc_gemv_host")
+        check(self.ctx.lib.rc_gemv_host(self.ctx.handle, self.handle, _np_addr(xc), dt, int(x.shape[0]),
+                                        _np_addr(out), _ptr(bias_dev) or None), "rc_gemv_host")
         return out
 
 
@@ -424,10 +434,9 @@ class MoeLayer:
         ids = np.empty((T, k), np.int32) if routes else None
         w = np.empty((T, k), np.float32) if routes else None
         check(getattr(self.ctx.lib, fn)(
-            self.handle, ctypes.c_void_p(xh.ctypes.data), T, int(k), ROUTER_CODES[router], int(bool(renormalize)),
-            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(out.ctypes.data),
-            ctypes.c_void_p(ids.ctypes.data if routes else None), ctypes.c_void_p(w.ctypes.data if routes else None),
-            ctypes.c_void_p(_stream_for(stream))), fn)
+            self.handle, _np_addr(xh), T, int(k), ROUTER_CODES[router], int(bool(renormalize)), float(scaling),
+            ACT_CODES[act], float(gate_beta), float(value_beta), _np_addr(out), _np_addr(ids) if routes else None,
+            _np_addr(w) if routes else None, _stream_for(stream)), fn)
         return (out, ids, w) if routes else out
 
     def decode_host(self, x: np.ndarray, k: int, routes: bool = False, stream: int | None = None,
@@ -503,9 +512,9 @@ class MoeLayer:
             raise ValueError(f"x must be [M, {self.hidden}] bf16 bits, got {xh.shape}")
         out = np.empty(xh.shape, np.uint16)
         check(self.ctx.lib.rc_moe_ep_decode_host(
-            self.handle, ctypes.c_void_p(xh.ctypes.data), int(k), ROUTER_CODES[router], int(bool(renormalize)),
-            float(scaling), ACT_CODES[act], float(gate_beta), float(value_beta), ctypes.c_void_p(out.ctypes.data),
-            ctypes.c_void_p(_stream_for(stream))), "rc_moe_ep_decode_host")
+            self.handle, _np_addr(xh), int(k), ROUTER_CODES[router], int(bool(renormalize)), float(scaling),
+            ACT_CODES[act], float(gate_beta), float(value_beta), _np_addr(out), _stream_for(stream)),
+            "rc_moe_ep_decode_host")
         return out
 
     def prefill(self, x_dev, k: int, out_dev, ids_dev=None, w_dev=None, router: str = "softmax",
