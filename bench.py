@@ -744,23 +744,33 @@ def moe_ep_parity(ctx, torch, dev, rank: int, world: int, ep) -> dict:
             "reference": "rc_moe_decode of the same layer with all 129 experts on rank 0's GPU"}
 
 
-def moe_phase_trace(ctx, torch, dev, eps, xs, outs, calls: int) -> dict:
-    """Where a decode step's time goes: the decode kernel's global-timer phase
-    stamps (rc_moe_set_trace) over ``calls`` L2-cold steps (layers rotated as
-    in the timed loop).  Per phase: [median, max] over CTAs of the stamp, in
-    us after the earliest CTA started, averaged over the calls (this rank)."""
+def moe_phase_trace(ctx, torch, dev, eps, xs, outs, calls: int, barrier) -> dict:
+    """Where a decode step's time goes in the timed loop's steady state: the
+    decode kernel's global-timer phase stamps (rc_moe_set_trace) of the last
+    of ``calls`` L2-cold steps (layers rotated as in the timed loop) replayed
+    back to back in one CUDA graph, over a few replays.  Per phase: [median,
+    max] over CTAs of the stamp, in us after the earliest CTA started,
+    averaged over the replays (this rank)."""
     from raon_npu_b200.device import MoeLayer
     n = ctx.sm_count
     buf = torch.zeros(n * 16, dtype=torch.int64, device=dev)
     for ep in eps:
         ep.layer.set_trace(buf, n)
+
+    def seq():
+        for c in range(calls):
+            li = c % len(eps)
+            eps[li].decode(xs[li], outs[li])
+    seq()
+    torch.cuda.synchronize()
+    g = capture_graph(torch, seq)
     rows = []
-    for c in range(calls):
-        buf.zero_()
-        li = c % len(eps)
-        eps[li].decode(xs[li], outs[li])
+    for _ in range(3):
+        barrier()
+        g.replay()
         torch.cuda.synchronize()
         rows.append(buf.view(n, 16).cpu().numpy().astype(np.int64))
+    del g
     for ep in eps:
         ep.layer.set_trace(None, 0)
     ctx.sync()
@@ -883,7 +893,7 @@ def run_moe(args, ctx, torch, dev, rank: int, world: int, local_rank: int, barri
     phases = None
     if world == 1 or transport == "p2p":
         barrier()
-        phases = moe_phase_trace(ctx, torch, dev, eps, xs, outs, calls=2 * n_layers)
+        phases = moe_phase_trace(ctx, torch, dev, eps, xs, outs, calls=2 * n_layers, barrier=barrier)
     parity = moe_ep_parity(ctx, torch, dev, rank, world, eps[0]) if world > 1 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

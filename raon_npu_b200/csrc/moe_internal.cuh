@@ -46,12 +46,12 @@ struct PfScratch;   // prefill scratch (q4nx_prefill.cu)
 //   [0, kEpFlagBytes)  u64 counters: [0] token-row arrivals (every rank adds
 //                      1 per call), [2] calls done
 //   tok                [world*M][hidden] bf16: every rank's token rows
-//   red                [M][kMoeMaxK+1][hidden] bf16: the expert rows of this
+//   red                [M][k+1][hidden/16][8] u64: the expert rows of this
 //                      rank's tokens, each written by the rank that owns the
-//                      expert (slot k: the shared expert, written here)
-//   col                [kEpMaxRanks][hidden/16] u64: per source rank and
-//                      16-column output tile, the number of the last call
-//                      whose expert rows of that tile the source has written
+//                      expert (slot k: the shared expert, written here); word
+//                      g of (token, slot, 16-column tile) holds rows g and
+//                      g + 8 of the tile as bf16 (bits 0-31) and the number
+//                      of the call that wrote it (bits 32-63)
 constexpr int kEpMaxRanks = 8;
 constexpr size_t kEpFlagBytes = 256;
 struct MoeEp {
@@ -74,11 +74,8 @@ struct MoeEpBlob {
 static_assert(sizeof(MoeEpBlob) <= 128, "exchange blob exceeds RC_EP_HANDLE_BYTES");
 inline size_t ep_tok_off() { return kEpFlagBytes; }
 inline size_t ep_red_off(int world, int M, int hidden) { return kEpFlagBytes + (size_t)world * M * hidden * 2; }
-inline size_t ep_col_off(int world, int M, int hidden) {
-  return (ep_red_off(world, M, hidden) + (size_t)M * (kMoeMaxK + 1) * hidden * 2 + 15) / 16 * 16;
-}
 inline size_t ep_bytes(int world, int M, int hidden) {
-  return ep_col_off(world, M, hidden) + (size_t)kEpMaxRanks * (hidden / 16) * 8;
+  return ep_red_off(world, M, hidden) + (size_t)M * (kMoeMaxK + 1) * hidden * 4;
 }
 
 // What the fused kernel needs of an expert-parallel call (null: one GPU).
@@ -86,7 +83,7 @@ struct MoeEpArgs {
   int rank, world, M;
   uint8_t *const *peer_dev;
   unsigned long long *flags;
-  uint32_t tok_off, red_off, col_off;
+  uint32_t tok_off, red_off;
   const uint16_t *x_own;
 };
 

@@ -1301,7 +1301,6 @@ int rc_moe_ep_decode(rc_moe *m, const uint16_t *x_dev, int k, int router, int re
   a.flags = reinterpret_cast<unsigned long long *>(ep->base);
   a.tok_off = (uint32_t)ep_tok_off();
   a.red_off = (uint32_t)ep_red_off(ep->world, ep->M, m->hidden);
-  a.col_off = (uint32_t)ep_col_off(ep->world, ep->M, m->hidden);
   a.x_own = x_dev;
   return moe_decode_persistent(m, reinterpret_cast<const uint16_t *>(ep->base + ep_tok_off()), T, k, router,
                           renormalize, scaling, act, gate_beta, value_beta, own, m->down_out, 0, out_dev, nullptr,

@@ -85,7 +85,7 @@ struct DcParams {
   int ep_world, ep_rank, ep_M;
   uint8_t *const *ep_peer;
   unsigned long long *ep_flags;
-  uint32_t ep_tok_off, ep_red_off, ep_col_off;
+  uint32_t ep_tok_off, ep_red_off;
   unsigned long long ep_call;        // this call's number (calls done before it), set in the kernel
   const uint16_t *ep_x_own;
   unsigned long long *trace;         // phase stamps [grid][kTracePhases] (null: off)
@@ -524,22 +524,25 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
               p.act[((size_t)grp * 8 * NTB + t) * p.inter_pad + tile * 8 + g] = f32_to_bf16_rne(v);
             } else {
               const int srow = g_dst[grp * T + t];     // slot row t*(k+1) + position
-              uint16_t *y;
-              if (col) {
-                // this CTA holds every expert row of the column tile: rows
-                // [slot row][16 columns] in the (now free) staging area
-                y = reinterpret_cast<uint16_t *>(smem + p.off_stage) + (size_t)srow * kUnitRows + g;
-              } else if (p.ep_world > 1) {
-                // straight into the buffer of the token's owner
+              const uint32_t r0 = live ? f32_to_bf16_rne(acc.v[tb][e2]) : 0u;
+              const uint32_t r1 = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : 0u;
+              if (!col && p.ep_world > 1) {
+                // straight into the buffer of the token's owner: rows g and
+                // g + 8 of the tile and this call's number in one 8-byte
+                // store, so the owner needs no fence or flag to read them
                 const int tt = srow / (p.k + 1), pos = srow - tt * (p.k + 1);
                 const int owner = tt / p.ep_M, tl = tt - owner * p.ep_M;
-                y = reinterpret_cast<uint16_t *>(ep_peer_s[owner] + p.ep_red_off) +
-                    ((size_t)tl * (p.k + 1) + pos) * p.hidden + tile * kUnitRows + g;
+                unsigned long long *wd = reinterpret_cast<unsigned long long *>(ep_peer_s[owner] + p.ep_red_off) +
+                                         (((size_t)tl * (p.k + 1) + pos) * (p.hidden / kUnitRows) + tile) * 8 + g;
+                st_relaxed_sys(wd, ((unsigned long long)(uint32_t)(p.ep_call + 1) << 32) | r0 | (r1 << 16));
               } else {
-                y = p.slot_rows + (size_t)srow * p.hidden + tile * kUnitRows + g;
+                // col: this CTA holds every expert row of the column tile --
+                // rows [slot row][16 columns] in the (now free) staging area
+                uint16_t *y = col ? reinterpret_cast<uint16_t *>(smem + p.off_stage) + (size_t)srow * kUnitRows + g
+                                  : p.slot_rows + (size_t)srow * p.hidden + tile * kUnitRows + g;
+                y[0] = (uint16_t)r0;
+                y[8] = (uint16_t)r1;
               }
-              y[0] = live ? f32_to_bf16_rne(acc.v[tb][e2]) : (uint16_t)0;
-              y[8] = live ? f32_to_bf16_rne(acc.v[tb][2 + e2]) : (uint16_t)0;
             }
           }
         }
@@ -567,31 +570,58 @@ __device__ __forceinline__ int dc_rounds(const DcParams &p, uint8_t *smem, const
       }
     }
     __syncthreads();
-    if (ph == 1 && p.ep_world > 1 && !failed && warp == 0) {
-      // expert parallelism: the CTA's rows of this round are written (remote
-      // stores included); per tile a lane makes them visible system-wide and
-      // counts the tile on its column; the rank's last tile of an output
-      // column tile flags that column to every rank (the rows' owners)
-#pragma unroll 1
-      for (int ti = t0 + lane; ti < t1; ti += 32) {
-        const int tg = c0 + ti, tile = tg - (tg / gt) * gt;
-        __threadfence_system();
-        if (atomicAdd(p.cols + tile, 1) == ng - 1) {
-          __threadfence_system();
-          p.cols[tile] = 0;
-          for (int r = 0; r < p.ep_world; ++r)
-            st_relaxed_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r] + p.ep_col_off) +
-                               (size_t)p.ep_rank * gt + tile,
-                           p.ep_call + 1);
-        }
-      }
-    }
     if (ph == 1 && t0 == 0) dc_stamp(p, kTrDownTiles);
     // chunks whose units all lie before this round's end are consumed: their
     // slots take the next chunks of the stream (chunk j by warp j % 16)
     if (!failed) issued = dc_refill(st, issued, (base + t1 * kb) / kDcChunk, buf, bar0, B);
   }
   return (issued << 1) | (failed ? 1 : 0);
+}
+
+// The combine of rows g and g + 8 of one column tile for one token from the
+// expert-parallel exchange: word s*stride of ``w0`` (slot s) carries the two
+// rows' bf16 values (bits 0-15, 16-31) and the number of the call that wrote
+// them (bits 32-63).  Waits, until global time t0 + 1 s, for every slot's
+// word of call ``want``, then sums exactly as dc_combine8 (ascending slots,
+// f32 multiply then add, RTNE, plus the shared row); false on a timeout.
+__device__ __forceinline__ bool dc_combine_tagged(const unsigned long long *w0, size_t stride, int k,
+                                                  const float *w, bool with_shared, uint32_t want, uint64_t t0,
+                                                  uint16_t *out) {
+  const int ns = k + (with_shared ? 1 : 0);
+  unsigned long long v[kMoeMaxK + 1];
+  uint32_t pending = (ns >= 32 ? 0xFFFFFFFFu : (1u << ns) - 1u);
+  while (true) {
+#pragma unroll
+    for (int s = 0; s < kMoeMaxK + 1; ++s) {
+      if ((pending >> s) & 1u) {
+        v[s] = ld_relaxed_sys(w0 + (size_t)s * stride);
+        if ((uint32_t)(v[s] >> 32) == want) pending &= ~(1u << s);
+      }
+    }
+    if (!pending) break;
+    if (global_timer_ns() - t0 > 1000000000ull) return false;
+  }
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int s = 0; s < kMoeMaxK; ++s) {
+    if (s < k) {
+      const float ws = w[s];
+      a0 = __fadd_rn(a0, __fmul_rn(bf16_to_f32((uint32_t)v[s] & 0xFFFFu), ws));
+      a1 = __fadd_rn(a1, __fmul_rn(bf16_to_f32(((uint32_t)v[s] >> 16) & 0xFFFFu), ws));
+    }
+  }
+  uint32_t r0 = f32_to_bf16_rne(a0), r1 = f32_to_bf16_rne(a1);
+  if (with_shared) {
+    uint32_t sh = 0;
+#pragma unroll
+    for (int s = 0; s < kMoeMaxK + 1; ++s)
+      if (s == k) sh = (uint32_t)v[s];
+    r0 = f32_to_bf16_rne(bf16_to_f32(r0) + bf16_to_f32(sh & 0xFFFFu));
+    r1 = f32_to_bf16_rne(bf16_to_f32(r1) + bf16_to_f32(sh >> 16));
+  }
+  out[0] = (uint16_t)r0;
+  out[8] = (uint16_t)r1;
+  return true;
 }
 
 // ---------------------------------------------------------- routing -----
@@ -836,6 +866,9 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
     if (b1 > b0) bulk_prefetch_l2(p.dn_tiles[E] + b0 * kUnitBytes, (uint32_t)((b1 - b0) * kUnitBytes));
   }
 
+  // the peer buffer table is fixed when the exchange is set up: read it now
+  if (p.ep_world > 1 && tid < p.ep_world) ep_peer_s[tid] = p.ep_peer[tid];
+
   // the previous kernel in the stream (the producer of x, or the previous
   // call sharing this layer's counters and scratch) is complete from here on
   pdl_wait_prior();
@@ -843,24 +876,22 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   // ---- expert parallelism: every rank's token rows into every rank's buffer
   unsigned long long ep_calls = 0;
   if (p.ep_world > 1) {
+    __syncthreads();
+    // CTA r stores this rank's token rows into rank r's buffer and counts
+    // them there: the ranks are served in parallel, one releasing add each
+    // (the barrier orders the CTA's stores before thread 0's release)
+    const int n16 = p.ep_M * p.hidden / 8;
+    const uint4 *src = reinterpret_cast<const uint4 *>(p.ep_x_own);
+#pragma unroll 1
+    for (int r = blockIdx.x; r < p.ep_world; r += gridDim.x) {
+      uint4 *dst = reinterpret_cast<uint4 *>(ep_peer_s[r] + p.ep_tok_off) + (size_t)p.ep_rank * n16;
+      for (int i = tid; i < n16; i += blockDim.x) dst[i] = src[i];
+      __syncthreads();
+      if (tid == 0) red_add_release_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r]) + 0, 1ull);
+    }
+    // the calls made so far (the previous call of this layer wrote it)
     ep_calls = *reinterpret_cast<volatile unsigned long long *>(p.ep_flags + 2);
     if (tid == 0) p.ep_call = ep_calls;      // read by the down epilogue (after several barriers)
-    if (tid < p.ep_world) ep_peer_s[tid] = p.ep_peer[tid];
-    __syncthreads();
-    if (blockIdx.x == 0) {
-      const int n16 = p.ep_M * p.hidden / 8;
-      const uint4 *src = reinterpret_cast<const uint4 *>(p.ep_x_own);
-      for (int r = 0; r < p.ep_world; ++r) {
-        uint4 *dst = reinterpret_cast<uint4 *>(ep_peer_s[r] + p.ep_tok_off) + (size_t)p.ep_rank * n16;
-        for (int i = tid; i < n16; i += blockDim.x) dst[i] = src[i];
-      }
-      __syncthreads();
-      if (tid == 0) {
-        __threadfence_system();
-        for (int r = 0; r < p.ep_world; ++r)
-          red_add_release_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r]) + 0, 1ull);
-      }
-    }
   }
 
   // per-expert tables kept in shared memory for the whole kernel
@@ -1019,49 +1050,28 @@ __global__ void __launch_bounds__(kDcThreads, 1) rc_moe_decode_kernel(DcParams p
   }
   dc_stamp(p, kTrDown);
   if (p.ep_world > 1) {
-    // expert parallelism: each column tile of this rank's tokens is combined
-    // once every rank has flagged its rows of that column (a rank that
-    // computed no group flags every column here)
-    const unsigned long long *colf = reinterpret_cast<const unsigned long long *>(ep_peer_s[p.ep_rank] +
-                                                                                  p.ep_col_off);
-    if (!failed && ng == 0 && tid == 0) {
-      __threadfence_system();
-      for (int c = blockIdx.x; c < gt_dn; c += gridDim.x)
-        for (int r = 0; r < p.ep_world; ++r)
-          st_relaxed_sys(reinterpret_cast<unsigned long long *>(ep_peer_s[r] + p.ep_col_off) +
-                             (size_t)p.ep_rank * gt_dn + c,
-                         ep_calls + 1);
-    }
+    // expert parallelism: every expert row of this rank's tokens arrives
+    // tagged with the call's number; thread (t, g) of a column tile waits for
+    // rows g and g + 8 of every slot of token t, then combines them
     const bool with_shared = p.shared_id >= 0 && p.own.shared_mask;
-    const uint16_t *red = reinterpret_cast<const uint16_t *>(ep_peer_s[p.ep_rank] + p.ep_red_off);
+    const unsigned long long *red =
+        reinterpret_cast<const unsigned long long *>(ep_peer_s[p.ep_rank] + p.ep_red_off);
+    if (tid == 0) *ok_s = 1;
+    __syncthreads();
+    const uint64_t tw = global_timer_ns();
 #pragma unroll 1
     for (int c = blockIdx.x; c < gt_dn && !failed; c += gridDim.x) {
-      if (tid == 0) {
-        int ok = 1;
-        const uint64_t t0 = global_timer_ns();
-        for (int r = 0; r < p.ep_world && ok; ++r) {
-          while (ld_acquire_sys(colf + (size_t)r * gt_dn + c) < ep_calls + 1) {
-            if (global_timer_ns() - t0 > 1000000000ull) {
-              ok = 0;
-              atomicCAS(p.err, 0, kErrWaitTimeout);
-              break;
-            }
-          }
+      if (p.out && tid < 8 * p.ep_M) {
+        const int t = tid >> 3, g = tid & 7;
+        if (!dc_combine_tagged(red + ((size_t)t * (k + 1) * gt_dn + c) * 8 + g, (size_t)gt_dn * 8, k,
+                               slot_w + (p.ep_rank * p.ep_M + t) * k, with_shared, (uint32_t)(ep_calls + 1), tw,
+                               p.out + (size_t)t * p.hidden + c * kUnitRows + g)) {
+          atomicCAS(p.err, 0, kErrWaitTimeout);
+          *ok_s = 0;
         }
-        *ok_s = ok;
       }
       __syncthreads();
-      if (!*ok_s) {
-        failed = true;
-        break;
-      }
-      if (p.out && tid < 2 * p.ep_M) {
-        const int t = tid >> 1, h = tid & 1;
-        *reinterpret_cast<uint4 *>(p.out + (size_t)t * p.hidden + c * kUnitRows + h * 8) =
-            dc_combine8(red + (size_t)t * (k + 1) * p.hidden + c * kUnitRows + h * 8, p.hidden, k,
-                        slot_w + (p.ep_rank * p.ep_M + t) * k, with_shared);
-      }
-      __syncthreads();
+      if (!*ok_s) failed = true;
     }
     dc_stamp(p, kTrRows);
   } else {
@@ -1245,7 +1255,6 @@ int moe_decode_persistent(rc_moe *m, const uint16_t *x, int T, int k, int router
     p.ep_flags = ep->flags;
     p.ep_tok_off = ep->tok_off;
     p.ep_red_off = ep->red_off;
-    p.ep_col_off = ep->col_off;
     p.ep_x_own = ep->x_own;
   }
   static bool configured[64][2] = {};
