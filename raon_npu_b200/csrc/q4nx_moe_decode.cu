@@ -702,26 +702,34 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
   }
   __syncthreads();
   dc_stamp(p, kTrKeys);
-  // ranks: one thread per candidate (t, c) scans token t's keys, four at a
-  // time, counting those ahead of it (no cross-lane steps on the chain)
+  // top-k: warp t takes token t's best key k times over -- the largest key,
+  // the lowest expert index among equal ones (one warp max, one warp min),
+  // then removes it (0 ranks below every router key) -- so the ranks follow
+  // the strict order (key descending, index ascending)
 #pragma unroll 1
-  for (int i = tid; i < n; i += kDcThreads) {
-    const int t = i / E, c = i - t * E;
-    const uint32_t kc = key_s[t * E4 + c];
-    const uint4 *kr4 = reinterpret_cast<const uint4 *>(key_s + t * E4);
-    int rank = 0;
-#pragma unroll 4
-    for (int q = 0; q < E4 / 4; ++q) {
-      const uint4 kq = kr4[q];
-      const int e0 = 4 * q;
-      rank += (kq.x > kc || (kq.x == kc && e0 < c)) ? 1 : 0;
-      rank += (kq.y > kc || (kq.y == kc && e0 + 1 < c)) ? 1 : 0;
-      rank += (kq.z > kc || (kq.z == kc && e0 + 2 < c)) ? 1 : 0;
-      rank += (kq.w > kc || (kq.w == kc && e0 + 3 < c)) ? 1 : 0;
+  for (int t = warp; t < T; t += kDcWarps) {
+    uint32_t kv[kMoeMaxExperts / 32];
+#pragma unroll
+    for (int j = 0; j < kMoeMaxExperts / 32; ++j) {
+      const int e = lane + 32 * j;
+      kv[j] = e < E ? key_s[t * E4 + e] : 0u;
     }
-    if (rank < k) {
-      sel_e[t * k + rank] = c;
-      sel_sc[t * k + rank] = sc_s[i];
+#pragma unroll 1
+    for (int r = 0; r < k; ++r) {
+      uint32_t bk = 0u;
+      int bj = 0;
+#pragma unroll
+      for (int j = 0; j < kMoeMaxExperts / 32; ++j)
+        if (kv[j] > bk) bk = kv[j], bj = j;
+      const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+      const uint32_t mi = __reduce_min_sync(0xffffffffu, bk == mk ? (uint32_t)(lane + 32 * bj) : 0xFFFFFFFFu);
+#pragma unroll
+      for (int j = 0; j < kMoeMaxExperts / 32; ++j)
+        if ((uint32_t)(lane + 32 * j) == mi) kv[j] = 0u;
+      if (lane == 0) {
+        sel_e[t * k + r] = (int32_t)mi;
+        sel_sc[t * k + r] = sc_s[t * E + mi];
+      }
     }
   }
   __syncthreads();
