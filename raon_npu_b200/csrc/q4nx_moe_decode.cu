@@ -635,27 +635,91 @@ static __device__ __noinline__ void dc_logits(const DcParams &p, double *red, ui
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = p.T, E = p.n_experts, nslice = p.hidden / kUnitK;
   if (warp >= nlog) return;
+  if (T <= 4) {
+    // few tokens: one token at a time
+#pragma unroll 1
+    for (int e = blockIdx.x; e < E; e += gridDim.x) {
+#pragma unroll 1
+      for (int t = 0; t < T; ++t) {
+        double acc = 0.0;
+#pragma unroll 1
+        for (int sl = warp; sl < nslice; sl += nlog) {
+          const int col = sl * kUnitK + lane * 8;
+          const uint4 wv = (e == (int)blockIdx.x && sl == warp)
+                               ? wpre : __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
+          const uint4 xv = __ldcg(reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.hidden + col));
+          const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            acc = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), (double)bf16_to_f32(ww[j] & 0xFFFFu), acc);
+            acc = fma((double)bf16_to_f32(xw[j] >> 16), (double)bf16_to_f32(ww[j] >> 16), acc);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) red[warp * kMoeMaxTokens + t] = acc;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(nlog * 32) : "memory");
+      if (tid < T) {
+        double a = 0.0;
+#pragma unroll 1
+        for (int w = 0; w < nlog; ++w) a += red[w * kMoeMaxTokens + tid];
+        p.logits[(size_t)tid * E + e] = __double2float_rn(a);
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(nlog * 32) : "memory");
+    }
+    return;
+  }
+  // more tokens: every token's sum at once, the router slice read and widened once
 #pragma unroll 1
   for (int e = blockIdx.x; e < E; e += gridDim.x) {
-#pragma unroll 1
-    for (int t = 0; t < T; ++t) {
-      double acc = 0.0;
-#pragma unroll 1
-      for (int sl = warp; sl < nslice; sl += nlog) {
-        const int col = sl * kUnitK + lane * 8;
-        const uint4 wv = (e == (int)blockIdx.x && sl == warp)
-                             ? wpre : __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
-        const uint4 xv = __ldcg(reinterpret_cast<const uint4 *>(p.x + (size_t)t * p.hidden + col));
-        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    double acc[kMoeMaxTokens];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          acc = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), (double)bf16_to_f32(ww[j] & 0xFFFFu), acc);
-          acc = fma((double)bf16_to_f32(xw[j] >> 16), (double)bf16_to_f32(ww[j] >> 16), acc);
+    for (int t = 0; t < kMoeMaxTokens; ++t) acc[t] = 0.0;
+#pragma unroll 1
+    for (int sl = warp; sl < nslice; sl += nlog) {
+      const int col = sl * kUnitK + lane * 8;
+      const uint4 wv = (e == (int)blockIdx.x && sl == warp)
+                           ? wpre : __ldg(reinterpret_cast<const uint4 *>(p.wr + (size_t)e * p.hidden + col));
+      double wd[8];
+      // eight tokens' slices are requested before the router slice is widened
+#pragma unroll
+      for (int t0 = 0; t0 < kMoeMaxTokens; t0 += 8) {
+        if (t0 < T) {
+          uint4 xv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (t0 + i < T) xv[i] = __ldcg(reinterpret_cast<const uint4 *>(p.x + (size_t)(t0 + i) * p.hidden + col));
+          if (t0 == 0) {
+            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              wd[2 * j] = (double)bf16_to_f32(ww[j] & 0xFFFFu);
+              wd[2 * j + 1] = (double)bf16_to_f32(ww[j] >> 16);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (t0 + i < T) {
+              const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                acc[t0 + i] = fma((double)bf16_to_f32(xw[j] & 0xFFFFu), wd[2 * j], acc[t0 + i]);
+                acc[t0 + i] = fma((double)bf16_to_f32(xw[j] >> 16), wd[2 * j + 1], acc[t0 + i]);
+              }
+            }
+          }
         }
       }
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) red[warp * kMoeMaxTokens + t] = acc;
+    for (int t = 0; t < kMoeMaxTokens; ++t) {
+      if (t < T) {
+        double a = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) red[warp * kMoeMaxTokens + t] = a;
+      }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(nlog * 32) : "memory");
     if (tid < T) {
