@@ -10,9 +10,9 @@
 //   2 logits     CTA c computes the logits of experts c, c + grid, ...
 //                (f64 sums of exact bf16 products, rounded once to f32)
 //   -- grid barrier --
-//   3 selection  every CTA ranks the T x E router keys (larger first, NaN
-//                last, ties by lower index) by counting, takes the k best per
-//                token, the weights, the ascending-ID slot lists and the group
+//   3 selection  every CTA takes each token's k best router keys (larger
+//                first, NaN last, ties by lower index; one warp per token),
+//                the weights, the ascending-ID slot lists and the group
 //                table -- identical inputs, identical tables, no barrier
 //   4 stream     the CTA's share of the layer -- a contiguous range of
 //                (group, row tile) tiles of gate/up, then one of down -- is a
@@ -732,11 +732,11 @@ static __device__ __noinline__ void dc_logits(const DcParams &p, double *red, ui
   }
 }
 
-// Selection by the whole CTA: every (token, expert) pair counts the experts
-// ahead of it in router order (a larger key, or an equal key and a lower
-// index); the pairs ranked below k are the top-k, best first.  Then per token
-// (warp t, lane r < k) the weight, the ascending-ID slot position and the
-// expert's token mask.  ``scratch`` holds T*E keys and scores.
+// Selection by the whole CTA: the router keys of every (token, expert) pair,
+// then per token (warp t) the k best in router order (a larger key, or an
+// equal key and a lower index), best first; then per token (warp t, lane
+// r < k) the weight, the ascending-ID slot position and the expert's token
+// mask.  ``scratch`` holds T*E keys and scores.
 static __device__ __noinline__ void dc_select(const DcParams &p, const float *bias_s, uint8_t *scratch,
                                               int32_t *slots, float *slot_w, int32_t *sel_e, float *sel_sc,
                                               uint32_t *mask_s) {
