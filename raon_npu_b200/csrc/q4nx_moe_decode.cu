@@ -44,6 +44,7 @@ namespace rc {
 
 constexpr int kDcWarps = 16;
 constexpr int kDcThreads = kDcWarps * 32;
+static_assert(kMoeMaxTokens <= kDcWarps, "the selection takes one warp per token");
 constexpr int kDcChunk = 6;         // units per chunk
 constexpr int kDcMaxChunks = 32;    // chunk slots at most (shared memory decides)
 // dynamic shared memory of one CTA: the opt-in limit less the static copies
@@ -796,7 +797,8 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
       }
     }
   }
-  __syncthreads();
+  // warp t wrote token t's picks and reads them next (T <= 16 warps)
+  __syncwarp();
   dc_stamp(p, kTrRanked);
   if (warp < T) {
     // lane r < k holds the token's r-th best expert; the weights' sums run
@@ -805,10 +807,19 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
     const bool sel = r < k;
     const int e = sel ? sel_e[t * k + r] : 0x7FFFFFFF;
     const float sc = sel ? sel_sc[t * k + r] : 0.f;
-    float w, sum = 0.f;
+    // (every rank's value is fetched first, then added in rank order)
+    auto ranked_sum = [&](float v) {
+      float vs[kMoeMaxK], acc = 0.f;
+#pragma unroll
+      for (int r2 = 0; r2 < kMoeMaxK; ++r2) vs[r2] = __shfl_sync(0xffffffffu, v, r2);
+#pragma unroll
+      for (int r2 = 0; r2 < kMoeMaxK; ++r2)
+        if (r2 < k) acc += vs[r2];
+      return acc;
+    };
+    float w;
     if (p.mode == RC_ROUTER_SIGMOID_BIAS) {
-#pragma unroll 1
-      for (int r2 = 0; r2 < k; ++r2) sum += __shfl_sync(0xffffffffu, sc, r2);
+      const float sum = ranked_sum(sc);
       w = sc;
       if (p.renorm) w = w / (sum + 1e-20f);
       w = w * p.scaling;
@@ -816,13 +827,14 @@ static __device__ __noinline__ void dc_select(const DcParams &p, const float *bi
       // softmax over all experts renormalised over the top-k equals the
       // softmax of the selected scores (the full denominator cancels)
       const float ex = expf(sc - __shfl_sync(0xffffffffu, sc, 0));
-#pragma unroll 1
-      for (int r2 = 0; r2 < k; ++r2) sum += __shfl_sync(0xffffffffu, ex, r2);
-      w = ex / sum;
+      w = ex / ranked_sum(ex);
     }
     int pos = 0;
-#pragma unroll 1
-    for (int r2 = 0; r2 < k; ++r2) pos += __shfl_sync(0xffffffffu, e, r2) < e ? 1 : 0;
+#pragma unroll
+    for (int r2 = 0; r2 < kMoeMaxK; ++r2) {
+      const int e2 = __shfl_sync(0xffffffffu, e, r2);
+      pos += (r2 < k && e2 < e) ? 1 : 0;
+    }
     if (sel) {
       slots[t * (k + 1) + pos] = e;
       slot_w[t * k + pos] = w;
