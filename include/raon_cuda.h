@@ -331,6 +331,15 @@ int rc_moe_prefill_local(rc_moe *m, const uint16_t *x_dev, int T, int k, int rou
                          float scaling, int act, float gate_beta, float value_beta, int expert_lo,
                          int expert_hi, int shared_t0, int shared_tn, uint16_t *slot_out_dev,
                          float *slot_w_dev, void *stream);
+/* rc_moe_prefill_local for caller-supplied routes ids / w [T][k] (rank order,
+ * as rc_moe_route returns them): the expert-parallel prefill routes each
+ * rank's own tokens and exchanges the routes with the token rows, so no rank
+ * routes another's tokens.  With the prefill router's routes (rc_moe_route,
+ * T > 16) the slot rows and weights are those of rc_moe_prefill_local. */
+int rc_moe_prefill_local_routes(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev,
+                                const float *w_dev, int k, int act, float gate_beta, float value_beta,
+                                int expert_lo, int expert_hi, int shared_t0, int shared_tn,
+                                uint16_t *slot_out_dev, float *slot_w_dev, void *stream);
 int rc_moe_prefill_combine(rc_moe *m, const uint16_t *slot_out_dev, const float *slot_w_dev, int T,
                            int k, int with_shared, uint16_t *out_dev, void *stream);
 

@@ -83,6 +83,7 @@ SIGNATURES = {
     "rc_moe_prefill": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _P, _P, _P, _P]),
     "rc_moe_prefill_experts": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _F, _I, _P, _P]),
     "rc_moe_prefill_local": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _F, _F, _I, _I, _I, _I, _P, _P, _P]),
+    "rc_moe_prefill_local_routes": (_I, [_P, _P, _I, _P, _P, _I, _I, _F, _F, _I, _I, _I, _I, _P, _P, _P]),
     "rc_moe_prefill_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _P]),
     "rc_sample_tokens": (_I, [_P, _P, _I, _I, _I, _I, _D, _D, _D, _P, _P, _P, _P, _P]),
     "rc_add_bf16": (_I, [_P, _P, _P, _P, ctypes.c_longlong, _P]),

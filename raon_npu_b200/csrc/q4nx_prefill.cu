@@ -121,17 +121,19 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 // ---------------------------------------------------------------- router --
 // logits[t][e] = f32(sum_h f64(x[t][h]) * f64(wr[e][h])).  A CTA takes 8
-// experts x 32 tokens: the experts' router rows are staged in shared memory
-// once and reused by all 32 tokens; each warp takes 4 tokens, each lane 8
-// columns per 256-column step, one f64 accumulator per expert.
-constexpr int kPfLogitExperts = 8, kPfLogitTokens = 32;
+// experts x 8*tpw tokens: the experts' router rows are staged in shared
+// memory once and reused by all its tokens; each warp takes tpw tokens (4,
+// or fewer when T is small, so the grid still fills the SMs), each lane 8
+// columns per 256-column step, one f64 accumulator per expert.  A token's
+// sums do not depend on which warp takes it.
+constexpr int kPfLogitExperts = 8, kPfLogitMaxTpw = 4;
 
 __global__ void __launch_bounds__(256) rc_pf_logits_kernel(const uint16_t *x, int T, int hidden, const uint16_t *wr,
-                                                        int E, float *logits) {
+                                                        int E, float *logits, int tpw) {
   extern __shared__ __align__(16) uint8_t pf_logit_smem[];
   uint4 *w_s = reinterpret_cast<uint4 *>(pf_logit_smem);    // [8][hidden/8]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e0 = blockIdx.x * kPfLogitExperts, t0 = blockIdx.y * kPfLogitTokens;
+  const int e0 = blockIdx.x * kPfLogitExperts, t0 = blockIdx.y * 8 * tpw;
   const int v8 = hidden / 8;
   for (int i = threadIdx.x; i < kPfLogitExperts * v8; i += blockDim.x) {
     const int ei = i / v8, c = i - ei * v8;
@@ -139,8 +141,8 @@ __global__ void __launch_bounds__(256) rc_pf_logits_kernel(const uint16_t *x, in
                          : make_uint4(0, 0, 0, 0);
   }
   __syncthreads();
-  for (int tt = 0; tt < kPfLogitTokens / 8; ++tt) {
-    const int t = t0 + warp * (kPfLogitTokens / 8) + tt;
+  for (int tt = 0; tt < tpw; ++tt) {
+    const int t = t0 + warp * tpw + tt;
     if (t >= T) break;
     double acc[kPfLogitExperts];
 #pragma unroll
@@ -1440,8 +1442,12 @@ static int pf_route(rc_moe *m, const uint16_t *x, int T, int k, int router, int 
     if (dev < 64) configured[dev] = true;
   }
   RC_CHECK_ARG(lsm <= (size_t)kGemvSmemLimit, "hidden %d too large for the prefill router", m->hidden);
-  rc_pf_logits_kernel<<<dim3((E + kPfLogitExperts - 1) / kPfLogitExperts, (T + kPfLogitTokens - 1) / kPfLogitTokens),
-                     256, lsm, s>>>(x, T, m->hidden, m->router_w, E, ps->logits);
+  // tokens per warp: 4 unless the grid would then have fewer CTAs than SMs
+  const int gx = (E + kPfLogitExperts - 1) / kPfLogitExperts;
+  int tpw = kPfLogitMaxTpw;
+  while (tpw > 1 && (long long)gx * ((T + 8 * tpw - 1) / (8 * tpw)) < m->ctx->sm_count) tpw >>= 1;
+  rc_pf_logits_kernel<<<dim3(gx, (T + 8 * tpw - 1) / (8 * tpw)), 256, lsm, s>>>(x, T, m->hidden, m->router_w, E,
+                                                                           ps->logits, tpw);
   RC_CUDA_TRY(cudaGetLastError());
   PfSelectParams sp{};
   sp.logits = ps->logits;
@@ -1551,6 +1557,35 @@ int rc_moe_prefill_experts(rc_moe *m, const uint16_t *x_dev, int T, const int32_
   rc_pf_combine_kernel<<<dim3((m->hidden / 8 + kPfCombineThreads - 1) / kPfCombineThreads, T), kPfCombineThreads, 0,
                       s>>>(m->pf->down, m->pf->slot_row, m->pf->slot_w, k, with_shared, m->hidden, out_dev);
   RC_CUDA_TRY(cudaGetLastError());
+  return RC_OK;
+}
+
+int rc_moe_prefill_local_routes(rc_moe *m, const uint16_t *x_dev, int T, const int32_t *ids_dev,
+                                const float *w_dev, int k, int act, float gate_beta, float value_beta, int expert_lo,
+                                int expert_hi, int shared_t0, int shared_tn, uint16_t *slot_out_dev, float *slot_w_dev,
+                                void *stream) {
+  RC_CHECK_ARG(m && x_dev && ids_dev && w_dev && slot_out_dev && slot_w_dev,
+               "rc_moe_prefill_local_routes: NULL argument");
+  RC_CHECK_ARG((reinterpret_cast<uintptr_t>(slot_out_dev) & 15) == 0, "slot_out must be 16-byte aligned");
+  RC_CHECK_ARG(0 <= expert_lo && expert_lo <= expert_hi && expert_hi <= m->n_experts,
+               "expert range [%d, %d) outside 0..%d", expert_lo, expert_hi, m->n_experts);
+  RC_CHECK_ARG(shared_tn == 0 || (m->has_shared && shared_t0 >= 0 && shared_tn > 0 && shared_t0 + shared_tn <= T),
+               "shared token range [%d, +%d) invalid for T=%d", shared_t0, shared_tn, T);
+  int rc = pf_check(m, x_dev, T, k, act, expert_lo, expert_hi);
+  if (rc) return rc;
+  RC_CHECK_ARG(!shared_tn || m->gate_up[m->n_experts], "the shared expert is not loaded");
+  RC_CUDA_TRY(cudaSetDevice(m->ctx->device));
+  if ((rc = pf_scratch(m, T))) return rc;
+  const cudaStream_t s = pick_stream(m->ctx, stream);
+  // the caller's routes in ascending-ID slot order, as the router leaves them
+  rc_pf_slots_kernel<<<(T + 127) / 128, 128, 0, s>>>(ids_dev, w_dev, T, k, m->has_shared ? m->n_experts : -1,
+                                                 m->pf->slot_expert, m->pf->slot_w);
+  RC_CUDA_TRY(cudaGetLastError());
+  PfRun r{T, k, act, gate_beta, value_beta, expert_lo, expert_hi, shared_t0, shared_t0 + shared_tn, m->n_experts};
+  if ((rc = pf_experts(m, x_dev, r, s))) return rc;
+  rc_pf_slot_rows_kernel<<<T * (k + 1), 256, 0, s>>>(m->pf->down, m->pf->slot_row, m->hidden, slot_out_dev);
+  RC_CUDA_TRY(cudaGetLastError());
+  RC_CUDA_TRY(cudaMemcpyAsync(slot_w_dev, m->pf->slot_w, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, s));
   return RC_OK;
 }
 

@@ -550,6 +550,23 @@ class MoeLayer:
             int(shared_tokens[1]), ctypes.c_void_p(_ptr(slot_out_dev)), ctypes.c_void_p(_ptr(slot_w_dev)),
             ctypes.c_void_p(_stream_for(stream, x_dev, slot_out_dev))), "rc_moe_prefill_local")
 
+    def prefill_local_routes(self, x_dev, ids_dev, w_dev, k: int, slot_out_dev, slot_w_dev,
+                             experts: tuple[int, int] | None = None, shared_tokens: tuple[int, int] | None = None,
+                             act: str = "swiglu", gate_beta: float = 4.0, value_beta: float = 25.0,
+                             stream: int | None = None, **_router) -> None:
+        """``prefill_local`` for given routes ids / w [T, k] (rank order, as
+        ``route`` returns them); router options are accepted and ignored."""
+        T = _tokens(x_dev, self.hidden)
+        lo, hi = (0, self.n_experts) if experts is None else (int(experts[0]), int(experts[1]))
+        if shared_tokens is None:
+            shared_tokens = (0, T) if self.has_shared else (0, 0)
+        check(self.ctx.lib.rc_moe_prefill_local_routes(
+            self.handle, ctypes.c_void_p(_ptr(x_dev)), T, ctypes.c_void_p(_ptr(ids_dev)),
+            ctypes.c_void_p(_ptr(w_dev)), int(k), ACT_CODES[act], float(gate_beta), float(value_beta), lo, hi,
+            int(shared_tokens[0]), int(shared_tokens[1]), ctypes.c_void_p(_ptr(slot_out_dev)),
+            ctypes.c_void_p(_ptr(slot_w_dev)), ctypes.c_void_p(_stream_for(stream, x_dev, slot_out_dev))),
+            "rc_moe_prefill_local_routes")
+
     def prefill_combine(self, slot_out_dev, slot_w_dev, k: int, out_dev, tokens: int, with_shared: bool = True,
                         stream: int | None = None) -> None:
         check(self.ctx.lib.rc_moe_prefill_combine(

@@ -48,6 +48,11 @@ import numpy as np
 from .device import CUDA_STREAM_LEGACY
 
 
+# rc_moe_route runs the prefill router above this many tokens (the decode
+# router below it, whose f64 sums run in another order)
+_DECODE_ROUTER_MAX_TOKENS = 16
+
+
 def _bf16(t):
     import torch
     return t.view(torch.bfloat16)
@@ -202,12 +207,14 @@ class ExpertParallelMoe:
             self.prefill_gather(x, out)
 
     def prefill_gather(self, x, out) -> None:
-        """All-gather of every rank's token rows; this rank's experts for every
-        token that chose them and the shared expert for its own tokens
-        (``prefill_local``: slot rows [T, k+1, hidden], zeros where another
-        rank owns the slot); reduce-scatter (sum) of the slot rows, exact as
-        each row is non-zero on one rank only; ``prefill_combine`` of the own
-        tokens.  Sizes are fixed, so it can be captured in a CUDA graph."""
+        """All-gather of every rank's token rows (above 16 tokens per rank with
+        their routes: each rank routes only its own tokens); this rank's
+        experts for every token that chose them and the shared expert for its
+        own tokens (``prefill_local`` / ``prefill_local_routes``: slot rows
+        [T, k+1, hidden], zeros where another rank owns the slot);
+        reduce-scatter (sum) of the slot rows, exact as each row is non-zero
+        on one rank only; ``prefill_combine`` of the own tokens.  Sizes are
+        fixed, so it can be captured in a CUDA graph."""
         import torch
         import torch.distributed as dist
         M, H = x.shape
@@ -215,11 +222,34 @@ class ExpertParallelMoe:
         T = N * M
         dev = x.device
         xg = self._buf("pxg", (T, H), torch.int16, dev)
-        dist.all_gather_into_tensor(_bf16(xg), _bf16(x), group=self.group)
         slots = self._buf("pslots", (T, k + 1, H), torch.int16, dev)
         sw = self._buf("psw", (T, k), torch.float32, dev)
         shared = (self.rank * M, M) if self.layer.has_shared else (0, 0)
-        self.layer.prefill_local(xg, k, slots, sw, experts=self.experts, shared_tokens=shared, **self.kw)
+        if M > _DECODE_ROUTER_MAX_TOKENS and hasattr(self.layer, "prefill_local_routes"):
+            # each rank routes only its own tokens (the prefill router, so the
+            # routes are those a single GPU computes) and the routes travel
+            # with the token rows in one all-gather: row = [x | ids | w]
+            route_kw = {n: self.kw[n] for n in ("router", "renormalize", "scaling")}
+            ids = self._buf("pids", (M, k), torch.int32, dev)
+            wts = self._buf("pw", (M, k), torch.float32, dev)
+            self.layer.route(x, M, k, ids, wts, **route_kw)
+            W = H + 4 * k
+            pk = self._buf("ppk", (M, W), torch.int16, dev)
+            pk[:, :H].copy_(x)
+            pk[:, H:H + 2 * k].view(torch.int32).copy_(ids)
+            pk[:, H + 2 * k:].view(torch.float32).copy_(wts)
+            pkg = self._buf("ppkg", (T, W), torch.int16, dev)
+            dist.all_gather_into_tensor(_bf16(pkg), _bf16(pk), group=self.group)
+            xg.copy_(pkg[:, :H])
+            idsg = self._buf("pidsg", (T, k), torch.int32, dev)
+            wg = self._buf("pwg", (T, k), torch.float32, dev)
+            idsg.copy_(pkg[:, H:H + 2 * k].view(torch.int32))
+            wg.copy_(pkg[:, H + 2 * k:].view(torch.float32))
+            self.layer.prefill_local_routes(xg, idsg, wg, k, slots, sw, experts=self.experts, shared_tokens=shared,
+                                            **self.kw)
+        else:
+            dist.all_gather_into_tensor(_bf16(xg), _bf16(x), group=self.group)
+            self.layer.prefill_local(xg, k, slots, sw, experts=self.experts, shared_tokens=shared, **self.kw)
         mine = self._buf("pmine", (M, k + 1, H), torch.int16, dev)
         dist.reduce_scatter_tensor(_bf16(mine), _bf16(slots), op=dist.ReduceOp.SUM, group=self.group)
         self.last_prefill_exchange = {"rows_sent": (N - 1) * M * (k + 1) + (N - 1) * M,

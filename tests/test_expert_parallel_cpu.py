@@ -52,15 +52,25 @@ class OracleLayer:
         self.n_experts, self.hidden, self.has_shared = E, HIDDEN, True
 
     def decode_local(self, x, k, slots, sw, experts, shared_tokens, act, **_):
-        import torch
         from oracle import backend as ob
         xs = x.numpy().view(np.uint16)
+        routes = [ob.route_softmax(xs[t], self.wr, k)[:2] for t in range(xs.shape[0])]
+        self._local(xs, routes, k, slots, sw, experts, shared_tokens, act)
+
+    def prefill_local_routes(self, x, ids, w, k, slots, sw, experts, shared_tokens, act, **_):
+        xs = x.numpy().view(np.uint16)
+        routes = list(zip(ids.numpy(), w.numpy()))
+        self._local(xs, routes, k, slots, sw, experts, shared_tokens, act)
+
+    def _local(self, xs, routes, k, slots, sw, experts, shared_tokens, act):
+        import torch
+        from oracle import backend as ob
         lo, hi = experts
         t0, tn = shared_tokens
         rows = np.zeros((xs.shape[0], k + 1, self.hidden), np.uint16)
         wts = np.zeros((xs.shape[0], k), np.float32)
         for t in range(xs.shape[0]):
-            ids, w, _ = ob.route_softmax(xs[t], self.wr, k)
+            ids, w = routes[t]
             order = np.argsort(ids, kind="stable")
             for pos, r in enumerate(order):
                 e = int(ids[r])
@@ -145,7 +155,7 @@ def test_expert_parallel_two_ranks_match_single_process(tmp_path):
             np.testing.assert_array_equal(out[t], ref)
 
 
-def _prefill_worker(rank, world, port, result_dir, exchange):
+def _prefill_worker(rank, world, port, result_dir, exchange, M):
     import torch
     import torch.distributed as dist
     from raon_npu_b200.expert_parallel import ExpertParallelMoe
@@ -159,8 +169,8 @@ def _prefill_worker(rank, world, port, result_dir, exchange):
         owned = set(range(rank * per, (rank + 1) * per)) | {E}
         ep = ExpertParallelMoe(OracleLayer(experts, wr, owned), K, act="swiglu", prefill_exchange=exchange)
         rng = np.random.default_rng(300 + rank)
-        x = q.f32_to_bf16(rng.standard_normal((5, HIDDEN)).astype(np.float32))
-        out = torch.empty((5, HIDDEN), dtype=torch.int16)
+        x = q.f32_to_bf16(rng.standard_normal((M, HIDDEN)).astype(np.float32))
+        out = torch.empty((M, HIDDEN), dtype=torch.int16)
         ep.prefill(torch.from_numpy(x.view(np.int16)), out)
         np.save(os.path.join(result_dir, f"px{rank}.npy"), x)
         np.save(os.path.join(result_dir, f"pout{rank}.npy"), out.numpy().view(np.uint16))
@@ -171,15 +181,17 @@ def _prefill_worker(rank, world, port, result_dir, exchange):
 
 
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("exchange", ["a2a", "gather"])
-def test_expert_parallel_prefill_matches_single_process(tmp_path, exchange):
+@pytest.mark.parametrize("exchange,M", [("a2a", 5), ("gather", 5), ("gather", 20)])
+def test_expert_parallel_prefill_matches_single_process(tmp_path, exchange, M):
     """Prefill over two gloo ranks, either exchange: every rank's outputs
     equal the single-process oracle layer byte for byte; with "a2a" only the
-    rows of remote routes cross (there and back)."""
+    rows of remote routes cross (there and back); "gather" above 16 tokens
+    per rank routes each rank's own tokens and gathers the routes with the
+    rows."""
     import torch.multiprocessing as mp
     from oracle import backend as ob
     world = 2
-    mp.start_processes(_prefill_worker, args=(world, _free_port(), str(tmp_path), exchange), nprocs=world,
+    mp.start_processes(_prefill_worker, args=(world, _free_port(), str(tmp_path), exchange, M), nprocs=world,
                        start_method="spawn")
     experts, wr = _model()
     sent = 0

@@ -190,7 +190,9 @@ def test_prefill_caller_routes_reproduce_routed_call(torch, ctx, c4, kernel):
 
 def test_prefill_expert_parallel_ranks_reproduce_single_gpu_bytes(torch, ctx):
     """4 'ranks' each holding 8 of 32 experts and the shared one: summed slot
-    rows combined per rank's tokens give exactly the single-GPU bytes."""
+    rows combined per rank's tokens give exactly the single-GPU bytes.  With
+    routes each rank computed for its own 24 tokens only (the prefill router),
+    ``prefill_local_routes`` gives the same slot rows and weights."""
     E, R, T = 32, 4, 96
     full, wr, _ = _config3_layer(torch, ctx, n_experts=E, seed=103)
     per = E // R
@@ -204,11 +206,22 @@ def test_prefill_expert_parallel_ranks_reproduce_single_gpu_bytes(torch, ctx):
     total = torch.zeros((T, 9, 2048), dtype=torch.float32, device="cuda")
     sws = []
     M = T // R
+    ids = torch.empty((T, 8), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, 8), dtype=torch.float32, device="cuda")
+    for r, layer in enumerate(ranks):
+        layer.route(xd[r * M:(r + 1) * M], M, 8, ids[r * M:(r + 1) * M], wts[r * M:(r + 1) * M])
     for r, layer in enumerate(ranks):
         slots = torch.empty((T, 9, 2048), dtype=torch.int16, device="cuda")
         sw = torch.empty((T, 8), dtype=torch.float32, device="cuda")
         layer.prefill_local(xd, 8, slots, sw, experts=(r * per, (r + 1) * per), shared_tokens=(r * M, M),
                             act="swiglu")
+        slots2 = torch.full((T, 9, 2048), 0x7FC0, dtype=torch.int16, device="cuda")
+        sw2 = torch.full((T, 8), float("nan"), dtype=torch.float32, device="cuda")
+        layer.prefill_local_routes(xd, ids, wts, 8, slots2, sw2, experts=(r * per, (r + 1) * per),
+                                   shared_tokens=(r * M, M), act="swiglu")
+        torch.cuda.synchronize()
+        assert torch.equal(slots2, slots), r
+        assert torch.equal(sw2, sw), r
         total += slots.view(torch.bfloat16).float()
         sws.append(sw)
     torch.cuda.synchronize()
