@@ -141,36 +141,40 @@ __global__ void __launch_bounds__(256) rc_pf_logits_kernel(const uint16_t *x, in
                          : make_uint4(0, 0, 0, 0);
   }
   __syncthreads();
-  for (int tt = 0; tt < tpw; ++tt) {
-    const int t = t0 + warp * tpw + tt;
-    if (t >= T) break;
-    double acc[kPfLogitExperts];
+  // tokens in pairs: each router value is widened once for both tokens (the
+  // widening runs on the f64 pipe like the sums); a token's sums are the same
+  // chain of fused multiply-adds whether it is paired or not
+  for (int tt = 0; tt < tpw; tt += 2) {
+    const int ta = t0 + warp * tpw + tt;
+    if (ta >= T) break;
+    const bool two = tt + 1 < tpw && ta + 1 < T;
+    const int tb = two ? ta + 1 : ta;
+    double acc0[kPfLogitExperts], acc1[kPfLogitExperts];
 #pragma unroll
-    for (int ei = 0; ei < kPfLogitExperts; ++ei) acc[ei] = 0.0;
-    const uint4 *xr = reinterpret_cast<const uint4 *>(x + (size_t)t * hidden);
-    // the lane's slices of the token row, all requested before the sums
-    // (hidden <= 8 * 256 columns here; wider rows take the loop below)
-    constexpr int kPre = 8;
-    uint4 xpre[kPre];
-#pragma unroll
-    for (int i = 0; i < kPre; ++i) xpre[i] = lane + 32 * i < v8 ? __ldg(xr + lane + 32 * i) : make_uint4(0, 0, 0, 0);
+    for (int ei = 0; ei < kPfLogitExperts; ++ei) acc0[ei] = acc1[ei] = 0.0;
+    const uint4 *xra = reinterpret_cast<const uint4 *>(x + (size_t)ta * hidden);
+    const uint4 *xrb = reinterpret_cast<const uint4 *>(x + (size_t)tb * hidden);
+    // the next two slices of both rows are in flight while one is summed
+    uint4 na = lane < v8 ? __ldg(xra + lane) : make_uint4(0, 0, 0, 0);
+    uint4 nb = lane < v8 ? __ldg(xrb + lane) : make_uint4(0, 0, 0, 0);
+    uint4 na2 = lane + 32 < v8 ? __ldg(xra + lane + 32) : make_uint4(0, 0, 0, 0);
+    uint4 nb2 = lane + 32 < v8 ? __ldg(xrb + lane + 32) : make_uint4(0, 0, 0, 0);
     for (int c = lane; c < v8; c += 32) {
-      const int ci = (c - lane) / 32;
-      uint4 xa;
-      if (ci < kPre) {
-        xa = xpre[0];
-#pragma unroll
-        for (int i = 1; i < kPre; ++i)
-          if (ci == i) xa = xpre[i];
-      } else {
-        xa = __ldg(xr + c);
+      const uint4 xa = na, xb = nb;
+      na = na2;
+      nb = nb2;
+      if (c + 64 < v8) {
+        na2 = __ldg(xra + c + 64);
+        nb2 = __ldg(xrb + c + 64);
       }
-      const uint32_t xs[4] = {xa.x, xa.y, xa.z, xa.w};
-      double xd[8];
+      const uint32_t xsa[4] = {xa.x, xa.y, xa.z, xa.w}, xsb[4] = {xb.x, xb.y, xb.z, xb.w};
+      double xda[8], xdb[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        xd[2 * j] = (double)bf16_to_f32(xs[j] & 0xFFFFu);
-        xd[2 * j + 1] = (double)bf16_to_f32(xs[j] >> 16);
+        xda[2 * j] = (double)bf16_to_f32(xsa[j] & 0xFFFFu);
+        xda[2 * j + 1] = (double)bf16_to_f32(xsa[j] >> 16);
+        xdb[2 * j] = (double)bf16_to_f32(xsb[j] & 0xFFFFu);
+        xdb[2 * j + 1] = (double)bf16_to_f32(xsb[j] >> 16);
       }
 #pragma unroll
       for (int ei = 0; ei < kPfLogitExperts; ++ei) {
@@ -178,17 +182,26 @@ __global__ void __launch_bounds__(256) rc_pf_logits_kernel(const uint16_t *x, in
         const uint32_t ws[4] = {wa.x, wa.y, wa.z, wa.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          acc[ei] = fma(xd[2 * j], (double)bf16_to_f32(ws[j] & 0xFFFFu), acc[ei]);
-          acc[ei] = fma(xd[2 * j + 1], (double)bf16_to_f32(ws[j] >> 16), acc[ei]);
+          const double wl = (double)bf16_to_f32(ws[j] & 0xFFFFu), wh = (double)bf16_to_f32(ws[j] >> 16);
+          acc0[ei] = fma(xda[2 * j], wl, acc0[ei]);
+          acc0[ei] = fma(xda[2 * j + 1], wh, acc0[ei]);
+          acc1[ei] = fma(xdb[2 * j], wl, acc1[ei]);
+          acc1[ei] = fma(xdb[2 * j + 1], wh, acc1[ei]);
         }
       }
     }
 #pragma unroll
     for (int ei = 0; ei < kPfLogitExperts; ++ei) {
-      double a = acc[ei];
+      double a0 = acc0[ei], a1 = acc1[ei];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0 && e0 + ei < E) logits[(size_t)t * E + e0 + ei] = __double2float_rn(a);
+      for (int o = 16; o > 0; o >>= 1) {
+        a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+        a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+      }
+      if (lane == 0 && e0 + ei < E) {
+        logits[(size_t)ta * E + e0 + ei] = __double2float_rn(a0);
+        if (two) logits[(size_t)tb * E + e0 + ei] = __double2float_rn(a1);
+      }
     }
   }
 }
