@@ -123,9 +123,9 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // logits[t][e] = f32(sum_h f64(x[t][h]) * f64(wr[e][h])).  A CTA takes 8
 // experts x 8*tpw tokens: the experts' router rows are staged in shared
 // memory once and reused by all its tokens; each warp takes tpw tokens (4,
-// or fewer when T is small, so the grid still fills the SMs), each lane 8
-// columns per 256-column step, one f64 accumulator per expert.  A token's
-// sums do not depend on which warp takes it.
+// or 2 when T is small, so the grid still fills the SMs), two at a time,
+// each lane 8 columns per 256-column step, one f64 accumulator per (token,
+// expert).  A token's sums do not depend on which warp takes it.
 constexpr int kPfLogitExperts = 8, kPfLogitMaxTpw = 4;
 
 __global__ void __launch_bounds__(256) rc_pf_logits_kernel(const uint16_t *x, int T, int hidden, const uint16_t *wr,
@@ -1455,10 +1455,11 @@ static int pf_route(rc_moe *m, const uint16_t *x, int T, int k, int router, int 
     if (dev < 64) configured[dev] = true;
   }
   RC_CHECK_ARG(lsm <= (size_t)kGemvSmemLimit, "hidden %d too large for the prefill router", m->hidden);
-  // tokens per warp: 4 unless the grid would then have fewer CTAs than SMs
+  // tokens per warp: 4 unless the grid would then have fewer CTAs than SMs,
+  // and at least 2 (a warp's tokens go in pairs)
   const int gx = (E + kPfLogitExperts - 1) / kPfLogitExperts;
   int tpw = kPfLogitMaxTpw;
-  while (tpw > 1 && (long long)gx * ((T + 8 * tpw - 1) / (8 * tpw)) < m->ctx->sm_count) tpw >>= 1;
+  while (tpw > 2 && (long long)gx * ((T + 8 * tpw - 1) / (8 * tpw)) < m->ctx->sm_count) tpw >>= 1;
   rc_pf_logits_kernel<<<dim3(gx, (T + 8 * tpw - 1) / (8 * tpw)), 256, lsm, s>>>(x, T, m->hidden, m->router_w, E,
                                                                            ps->logits, tpw);
   RC_CUDA_TRY(cudaGetLastError());
